@@ -1,0 +1,273 @@
+"""Numerics of the sm_100a kernels against plain PyTorch fp32 references.
+
+Each CUDA kernel is compared with an fp32 restatement of the same op; shapes
+include tails (M, N, K not multiples of the tile) to exercise the TMA
+out-of-bounds fill and the epilogue masks.
+"""
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _lib():
+    import harp_b200
+
+    assert harp_b200.load_native(build_if_needed=True), "CUDA library must load on a GPU box"
+    torch.manual_seed(0)
+
+
+def _err():
+    return torch.zeros(4, dtype=torch.int32, device="cuda")
+
+
+def _check_err(err):
+    e = err.cpu().tolist()
+    assert e[0] == 0, f"device error word {e}"
+
+
+def _gemm(A, a_mn, B, b_mn, M, N, K, epi=0, bias=None, alpha=1.0, residual=None, gate=None, rpb=0, C=None,
+          force_simt=False):
+    out_dtype = torch.float32 if epi in (1, 3) else torch.bfloat16
+    if C is None:
+        C = torch.zeros(M, N, dtype=out_dtype, device="cuda")
+    err = _err()
+    torch.ops.harp.gemm(A, a_mn, B, b_mn, C, M, N, K, bias, epi, alpha, residual, gate, rpb, err, force_simt)
+    torch.cuda.synchronize()
+    _check_err(err)
+    return C
+
+
+def _ref(A, a_mn, B, b_mn):
+    a = A.float().t() if a_mn else A.float()
+    b = B.float() if b_mn else B.float().t()
+    return a @ b
+
+
+SHAPES = [(128, 256, 64), (256, 512, 256), (300, 200, 136), (1000, 1152, 1152), (64, 3456, 1152), (17, 40, 24),
+          (2176, 4608, 1152)]
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, False), (True, True)])
+def test_gemm_majors(M, N, K, a_mn, b_mn):
+    A = (torch.randn(K, M) if a_mn else torch.randn(M, K)).to(torch.bfloat16).cuda()
+    B = (torch.randn(K, N) if b_mn else torch.randn(N, K)).to(torch.bfloat16).cuda()
+    C = _gemm(A, a_mn, B, b_mn, M, N, K)
+    ref = _ref(A, a_mn, B, b_mn)
+    tol = 2e-2 * math.sqrt(K) + 1e-2
+    assert (C.float() - ref).abs().max().item() < tol, (C.float() - ref).abs().max().item()
+
+
+def test_gemm_epilogues():
+    M, N, K, B_ = 512, 384, 192, 4
+    A = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+    W = torch.randn(N, K, device="cuda").to(torch.bfloat16)
+    bias = torch.randn(N, device="cuda").to(torch.bfloat16)
+    ref = A.float() @ W.float().t() + bias.float()
+    c = _gemm(A, False, W, False, M, N, K, epi=0, bias=bias)
+    assert (c.float() - ref).abs().max() < 0.5
+    c32 = _gemm(A, False, W, False, M, N, K, epi=1, bias=bias)
+    assert (c32 - ref).abs().max() < 0.05
+    acc = torch.randn(M, N, device="cuda")
+    acc0 = acc.clone()
+    _gemm(A, False, W, False, M, N, K, epi=3, bias=bias, C=acc)
+    assert (acc - (acc0 + ref)).abs().max() < 0.05
+    res = torch.randn(M, N, device="cuda").to(torch.bfloat16)
+    gate = torch.randn(B_, N, device="cuda").to(torch.bfloat16)
+    out = _gemm(A, False, W, False, M, N, K, epi=4, bias=bias, residual=res, gate=gate, rpb=M // B_)
+    gref = res.float() + gate.float().repeat_interleave(M // B_, 0) * ref
+    assert (out.float() - gref).abs().max() < 1.0
+
+
+def test_gemm_simt_fallback_matches():
+    M, N, K = 100, 72, 40
+    A = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+    W = torch.randn(N, K, device="cuda").to(torch.bfloat16)
+    c1 = _gemm(A, False, W, False, M, N, K, force_simt=True)
+    ref = A.float() @ W.float().t()
+    assert (c1.float() - ref).abs().max() < 0.2
+
+
+def _rms_ref(x, w, scale, shift, rpb, eps):
+    xf = x.float()
+    y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
+    if w is not None:
+        y = y * w.float()
+    if scale is not None:
+        y = y * (1 + scale.float().repeat_interleave(rpb, 0))
+    if shift is not None:
+        y = y + shift.float().repeat_interleave(rpb, 0)
+    return y
+
+
+@pytest.mark.parametrize("use_w,use_mod", [(True, False), (False, True), (True, True)])
+def test_rmsnorm_mod_fwd_bwd(use_w, use_mod):
+    Bn, S, D, eps = 3, 96, 1152, 1e-6
+    R = Bn * S
+    x = torch.randn(R, D, device="cuda").to(torch.bfloat16)
+    w = (torch.rand(D, device="cuda") + 0.5).to(torch.bfloat16) if use_w else None
+    mod = torch.randn(Bn, 2 * D, device="cuda").to(torch.bfloat16) * 0.5 if use_mod else None
+    scale = mod[:, :D] if use_mod else None
+    shift = mod[:, D:] if use_mod else None
+    y = torch.empty_like(x)
+    rstd = torch.empty(R, device="cuda")
+    torch.ops.harp.rmsnorm_mod_fwd(x, w, scale, shift, S, eps, y, rstd, False)
+    ref = _rms_ref(x, w, scale, shift, S, eps)
+    assert (y.float() - ref).abs().max() < 0.08
+    # backward
+    dy = torch.randn(R, D, device="cuda").to(torch.bfloat16)
+    rpb = torch.ops.harp.rows_per_block(S)
+    nblk = R // rpb
+    pw = torch.empty(nblk, D, device="cuda") if use_w else None
+    ps = torch.empty(nblk, D, device="cuda") if use_mod else None
+    pb = torch.empty(nblk, D, device="cuda") if use_mod else None
+    dx = torch.empty_like(x)
+    torch.ops.harp.rmsnorm_mod_bwd(x, rstd, dy, w, scale, S, None, dx, pw, ps, pb, rpb)
+    xr = x.float().requires_grad_()
+    wr = w.float().requires_grad_() if use_w else None
+    scr = scale.float().requires_grad_() if use_mod else None
+    shr = shift.float().requires_grad_() if use_mod else None
+    yr = _rms_ref(xr, wr, scr, shr, S, eps)
+    yr.backward(dy.float())
+    assert (dx.float() - xr.grad).abs().max() < 0.1
+    if use_w:
+        gw = torch.empty(1, D, device="cuda")
+        torch.ops.harp.reduce_partials(pw, nblk, gw, False)
+        assert torch.allclose(gw[0], wr.grad, atol=0.5, rtol=2e-2)
+    if use_mod:
+        gs = torch.empty(Bn, D, device="cuda")
+        gb = torch.empty(Bn, D, device="cuda")
+        torch.ops.harp.reduce_partials(ps, S // rpb, gs, False)
+        torch.ops.harp.reduce_partials(pb, S // rpb, gb, False)
+        assert torch.allclose(gs, scr.grad, atol=0.5, rtol=2e-2)
+        assert torch.allclose(gb, shr.grad, atol=0.5, rtol=2e-2)
+
+
+def _rope_ref(x, cos, sin):
+    x0, x1 = x[..., 0::2], x[..., 1::2]
+    o0 = x0 * cos - x1 * sin
+    o1 = x0 * sin + x1 * cos
+    return torch.stack([o0, o1], -1).flatten(-2)
+
+
+@pytest.mark.parametrize("Dh", [64, 72, 128])
+def test_qknorm_rope(Dh):
+    R, H, eps = 200, 4, 1e-5
+    qkv = torch.randn(R, 3 * H * Dh, device="cuda").to(torch.bfloat16)
+    wq = (torch.rand(Dh, device="cuda") + 0.5).to(torch.bfloat16)
+    wk = (torch.rand(Dh, device="cuda") + 0.5).to(torch.bfloat16)
+    ang = torch.rand(R, Dh // 2, device="cuda") * 6.0
+    freqs = torch.stack([ang.cos(), ang.sin()], -1).contiguous()
+    qo = torch.empty(R, H * Dh, device="cuda", dtype=torch.bfloat16)
+    ko = torch.empty_like(qo)
+    rq = torch.empty(R * H, device="cuda")
+    rk = torch.empty(R * H, device="cuda")
+    torch.ops.harp.qknorm_rope_fwd(qkv, H, Dh, wq, wk, freqs, R, eps, True, qo, ko, rq, rk)
+
+    def ref(xpart, w):
+        xr = xpart.view(R, H, Dh)
+        n = xr * torch.rsqrt(xr.pow(2).mean(-1, keepdim=True) + eps) * w
+        return _rope_ref(n, ang.cos()[:, None], ang.sin()[:, None]).reshape(R, H * Dh)
+
+    q_in = qkv[:, : H * Dh].float().requires_grad_()
+    k_in = qkv[:, H * Dh : 2 * H * Dh].float().requires_grad_()
+    wqr = wq.float().requires_grad_()
+    wkr = wk.float().requires_grad_()
+    qr, kr = ref(q_in, wqr), ref(k_in, wkr)
+    assert (qo.float() - qr).abs().max() < 0.05
+    assert (ko.float() - kr).abs().max() < 0.05
+    dq = torch.randn_like(qo)
+    dk = torch.randn_like(ko)
+    dqkv = torch.zeros_like(qkv)
+    ipb = 64
+    nblk = (R * H + ipb - 1) // ipb
+    pwq = torch.empty(nblk, Dh, device="cuda")
+    pwk = torch.empty(nblk, Dh, device="cuda")
+    torch.ops.harp.qknorm_rope_bwd(dq, dk, qkv, rq, rk, H, Dh, wq, wk, freqs, R, True, dqkv, pwq, pwk, ipb)
+    (qr * dq.float()).sum().add((kr * dk.float()).sum()).backward()
+    assert (dqkv[:, : H * Dh].float() - q_in.grad).abs().max() < 0.05
+    assert (dqkv[:, H * Dh : 2 * H * Dh].float() - k_in.grad).abs().max() < 0.05
+    gwq = torch.empty(1, Dh, device="cuda")
+    torch.ops.harp.reduce_partials(pwq, nblk, gwq, False)
+    assert torch.allclose(gwq[0], wqr.grad, atol=0.3, rtol=2e-2)
+
+
+def test_swiglu_and_gate_bwd():
+    R, F = 256, 512
+    gu = torch.randn(R, 2 * F, device="cuda").to(torch.bfloat16)
+    h = torch.empty(R, F, device="cuda", dtype=torch.bfloat16)
+    torch.ops.harp.swiglu_fwd(gu, h)
+    g, u = gu.float()[:, :F].requires_grad_(), gu.float()[:, F:].requires_grad_()
+    hr = torch.nn.functional.silu(g) * u
+    assert (h.float() - hr).abs().max() < 0.05
+    dh = torch.randn_like(h)
+    dgu = torch.empty_like(gu)
+    torch.ops.harp.swiglu_bwd(dh, gu, dgu)
+    hr.backward(dh.float())
+    assert (dgu[:, :F].float() - g.grad).abs().max() < 0.05
+    assert (dgu[:, F:].float() - u.grad).abs().max() < 0.05
+    # gated residual backward
+    Bn, S, D = 2, 128, 384
+    dy = torch.randn(Bn * S, D, device="cuda").to(torch.bfloat16)
+    a = torch.randn(Bn * S, D, device="cuda").to(torch.bfloat16)
+    gate = torch.randn(Bn, D, device="cuda").to(torch.bfloat16)
+    rpb = torch.ops.harp.rows_per_block(S)
+    nblk = Bn * S // rpb
+    da = torch.empty_like(dy)
+    pg = torch.empty(nblk, D, device="cuda")
+    pb = torch.empty(nblk, D, device="cuda")
+    torch.ops.harp.gate_bwd(dy, a, gate, S, da, pg, pb, rpb)
+    ref_da = dy.float() * gate.float().repeat_interleave(S, 0)
+    assert (da.float() - ref_da).abs().max() < 0.05
+    gg = torch.empty(Bn, D, device="cuda")
+    torch.ops.harp.reduce_partials(pg, S // rpb, gg, False)
+    ref_g = (dy.float() * a.float()).view(Bn, S, D).sum(1)
+    assert torch.allclose(gg, ref_g, atol=0.3, rtol=1e-2)
+
+
+def test_adamw_flat_matches_torch():
+    n = 10007
+    p0 = torch.randn(n, device="cuda")
+    g = torch.randn(n, device="cuda")
+    master, m, v = p0.clone(), torch.zeros(n, device="cuda"), torch.zeros(n, device="cuda")
+    pref = p0.clone().requires_grad_()
+    opt = torch.optim.AdamW([pref], lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01)
+    for step in range(1, 4):
+        torch.ops.harp.adamw_flat(master, m, v, g, None, 1e-3, 0.9, 0.999, 1e-8, 0.01, step, 1.0)
+        pref.grad = g.clone()
+        opt.step()
+    assert torch.allclose(master, pref.detach(), atol=1e-6, rtol=1e-5)
+
+
+def test_philox_uniform_range_and_determinism():
+    a = torch.empty(100003, device="cuda")
+    b = torch.empty(100003, device="cuda")
+    torch.ops.harp.philox_uniform(a, 7, 0, -2.0, 3.0)
+    torch.ops.harp.philox_uniform(b, 7, 0, -2.0, 3.0)
+    assert torch.equal(a, b)
+    assert a.min() >= -2.0 and a.max() < 3.0
+    assert abs(a.mean().item() - 0.5) < 0.05
+
+
+def test_compat_linear_ops():
+    x = torch.randn(4, 37, 256, device="cuda").to(torch.bfloat16)
+    w = torch.randn(320, 256, device="cuda").to(torch.bfloat16)
+    b = torch.randn(320, device="cuda").to(torch.bfloat16)
+    out = torch.empty(4, 37, 320, device="cuda", dtype=torch.bfloat16)
+    torch.ops.xhpops.kp_linear_forward(x, w, b, out)
+    ref = x.float() @ w.float().t() + b.float()
+    assert (out.float() - ref).abs().max() < 0.5
+    g = torch.randn_like(out)
+    gi = torch.empty_like(x)
+    gw = torch.empty_like(w)
+    gb = torch.empty_like(b)
+    torch.ops.xhpops.kp_linear_backward(g, x, w, gi, gw, gb)
+    torch.cuda.synchronize()
+    gf = g.float().view(-1, 320)
+    assert (gi.float().view(-1, 256) - gf @ w.float()).abs().max() < 0.5
+    assert (gw.float() - gf.t() @ x.float().view(-1, 256)).abs().max() < 2.0
+    assert (gb.float() - gf.sum(0)).abs().max() < 0.5
