@@ -1,2 +1,796 @@
-// placeholder, replaced by the flash-attention kernels
+// Flash attention forward / backward on tcgen05 + TMEM (sm_100a), the compute
+// core of ring attention.
+//
+// Reference: gemm/ring_attention/ring_attn.cpp:2412-2575 (forward: per-head SME
+// GEMMs over the full T_local x T_local score matrix, bf16 running max) and
+// :2577-2829 (backward: Q-rotating, KV-stationary, dQ partial slots).  Here:
+//   * scores never leave the SM: S = Q K^T accumulates in TMEM, the softmax
+//     warps read it with tcgen05.ld, write P (bf16) back over S, and the MMA
+//     O += P V takes P straight from TMEM (A operand in tensor memory);
+//   * the row max / log-sum-exp are fp32 (the reference keeps m_i in bf16);
+//   * keys are tiled (128 per tile) so memory is O(T*D), not O(T^2);
+//   * K/V may be a gathered sequence made of `chunk` pieces that arrive from
+//     peer GPUs: before loading a key tile the TMA warp waits (bounded) for the
+//     readiness flag of every chunk it touches, and tiles are visited starting
+//     at this rank's own chunk, so compute starts while peer chunks land.
+//
+// Operand layout.  Every Q/K/V/dO tile is loaded by TMA as 8-element (16-byte)
+// column strips: strip c of a 128-row tile lives at smem offset c*2048 and row r
+// at +16*r.  That is the no-swizzle canonical core-matrix layout, valid for the
+// tensor core both as a K-major operand (head dim = reduction) and as an
+// MN-major operand (head dim = output columns), so one tile serves S = Q K^T,
+// O = P V and all five backward products.  head_dim is zero-padded to a
+// multiple of 16 by loading strips past the end of the head (TMA fills zeros).
+#include "common.cuh"
+#include "gemm_sm100.h"
+
 #include <ATen/ATen.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAException.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/library.h>
+
+namespace harp {
+namespace {
+
+using bf16 = __nv_bfloat16;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O only when the max grows by > 2^8
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+__device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity) {
+  const unsigned long long t0 = globaltimer_ns();
+  while (!mbar_try_wait(bar, parity))
+    if (globaltimer_ns() - t0 > 1000000000ull) return false;
+  return true;
+}
+__device__ __forceinline__ uint64_t kmajor_desc(uint32_t tile_addr, int ks) {
+  // K-major (head dim is the reduction): next 8-row group at +128 B,
+  // next 8-element strip at +2048 B; a 16-wide k-step spans two strips.
+  return make_sdesc(tile_addr + ks * 4096, 2048, 128, kLayoutNone);
+}
+__device__ __forceinline__ uint64_t mnmajor_desc(uint32_t tile_addr, int ks) {
+  // MN-major (head dim / query index is the output dim, tile rows are the
+  // reduction): next 8 reduction rows at +128 B, next 8 output columns at
+  // +2048 B; a 16-row k-step advances 256 B.
+  return make_sdesc(tile_addr + ks * 256, 128, 2048, kLayoutNone);
+}
+
+// ===========================================================================
+// Forward
+// ===========================================================================
+struct FwdArgs {
+  int B, Sq, Skv, H, Dh;
+  float scale_log2;
+  bf16* O;
+  long ldo;
+  float* lse;  // natural-log LSE, index (b*Sq + s)*H + h
+  const unsigned int* ready;  // per-chunk readiness flags (nullptr: all local)
+  int chunk_len;
+  int start_tile;
+  unsigned int epoch;
+  unsigned long long timeout_ns;
+  int* err;
+};
+
+template <int NCH>
+struct FwdCfg {
+  static constexpr int DPAD = NCH * 8;
+  static constexpr int TILE = NCH * 2048;
+  static constexpr int STAGES = (NCH <= 10) ? 3 : 2;
+  static constexpr int SMEM = 2 * TILE + STAGES * 2 * TILE + 1024 + 512;
+};
+constexpr int kFwdThreads = 384;  // w0 TMA, w1 MMA, w2-3 spare, w4-7 softmax tile 0, w8-11 softmax tile 1
+
+template <int NCH>
+__global__ void __launch_bounds__(kFwdThreads, 1)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const FwdArgs a) {
+  using C = FwdCfg<NCH>;
+  constexpr int ST = C::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sK = sQ + 2 * C::TILE;
+  uint8_t* sV = sK + ST * C::TILE;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + ST * C::TILE);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;
+  uint64_t* k_empty = k_full + ST;
+  uint64_t* v_full = k_empty + ST;
+  uint64_t* v_empty = v_full + ST;
+  uint64_t* s_full = v_empty + ST;  // [2]
+  uint64_t* p_full = s_full + 2;    // [2]
+  uint64_t* o_final = p_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_final + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int nqp = (a.Sq + 255) / 256;
+  const int bh = blockIdx.x / nqp, qp = blockIdx.x % nqp;
+  const int b = bh / a.H, h = bh % a.H;
+  const int q0 = qp * 256;
+  const int ntile = (q0 + 128 < a.Sq) ? 2 : 1;
+  const int nkv = (a.Skv + 127) / 128;
+  int* err = a.err;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&p_full[t], 4);
+    }
+    mbar_init(o_final, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      int issued_k[4] = {0, 0, 0, 0}, issued_v[4] = {0, 0, 0, 0};
+      bool ok = true;
+      mbar_arrive_expect_tx(q_full, ntile * C::TILE);
+      for (int t = 0; t < ntile; ++t)
+#pragma unroll
+        for (int c = 0; c < NCH; ++c) tma_load_4d(sQ + t * C::TILE + c * 2048, &tmQ, q_full, c * 8, h, q0 + 128 * t, b);
+      for (int jj = 0; jj < nkv && ok; ++jj) {
+        const int j = (a.start_tile + jj) % nkv;
+        const int key0 = j * 128;
+        if (a.ready != nullptr) {
+          const int kend = min(key0 + 128, a.Skv) - 1;
+          for (int c = key0 / a.chunk_len; c <= kend / a.chunk_len && ok; ++c)
+            ok = wait_flag_geq(a.ready + c, a.epoch, a.timeout_ns, err, 20);
+          if (!ok) break;
+          fence_proxy_async_global();
+        }
+        const int st = jj % ST;
+        const uint32_t ph = (jj / ST) & 1;
+        if (!mbar_wait(&k_empty[st], ph ^ 1, err, 21)) { ok = false; break; }
+        mbar_arrive_expect_tx(&k_full[st], C::TILE);
+#pragma unroll
+        for (int c = 0; c < NCH; ++c) tma_load_4d(sK + st * C::TILE + c * 2048, &tmK, &k_full[st], c * 8, h, key0, b);
+        issued_k[st]++;
+        if (!mbar_wait(&v_empty[st], ph ^ 1, err, 22)) { ok = false; break; }
+        mbar_arrive_expect_tx(&v_full[st], C::TILE);
+#pragma unroll
+        for (int c = 0; c < NCH; ++c) tma_load_4d(sV + st * C::TILE + c * 2048, &tmV, &v_full[st], c * 8, h, key0, b);
+        issued_v[st]++;
+      }
+      mbar_wait_drain(q_full, 0);
+      for (int s = 0; s < ST; ++s) {
+        if (issued_k[s]) mbar_wait_drain(&k_full[s], (issued_k[s] - 1) & 1);
+        if (issued_v[s]) mbar_wait_drain(&v_full[s], (issued_v[s] - 1) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idS = make_idesc_bf16(128, 128, false, false);
+      constexpr uint32_t idO = make_idesc_bf16(128, C::DPAD, false, true);
+      auto issue_S = [&](int t, int st) {
+        const uint32_t qa = smem_u32(sQ + t * C::TILE), ka = smem_u32(sK + st * C::TILE);
+#pragma unroll
+        for (int ks = 0; ks < NCH / 2; ++ks)
+          mma_ss(tmem + t * 128, kmajor_desc(qa, ks), kmajor_desc(ka, ks), idS, ks > 0 ? 1u : 0u);
+      };
+      bool ok = mbar_wait(q_full, 0, err, 30);
+      if (ok) ok = mbar_wait(&k_full[0], 0, err, 31);
+      if (ok) {
+        tc_fence_after();
+        for (int t = 0; t < ntile; ++t) {
+          issue_S(t, 0);
+          mma_commit(&s_full[t]);
+        }
+        mma_commit(&k_empty[0]);
+      }
+      for (int jj = 0; jj < nkv && ok; ++jj) {
+        const int st = jj % ST;
+        const uint32_t ph = (jj / ST) & 1;
+        if (!mbar_wait(&v_full[st], ph, err, 32)) { ok = false; break; }
+        const bool has_next = jj + 1 < nkv;
+        const int st2 = (jj + 1) % ST;
+        const uint32_t ph2 = ((jj + 1) / ST) & 1;
+        const uint32_t va = smem_u32(sV + st * C::TILE);
+        for (int t = 0; t < ntile; ++t) {
+          if (!mbar_wait(&p_full[t], jj & 1, err, 33)) { ok = false; break; }
+          tc_fence_after();
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks)
+            mma_ts(tmem + 256 + t * 128, tmem + t * 128 + ks * 8, mnmajor_desc(va, ks), idO,
+                   (jj > 0 || ks > 0) ? 1u : 0u);
+          if (has_next) {
+            if (t == 0) {
+              if (!mbar_wait(&k_full[st2], ph2, err, 34)) { ok = false; break; }
+              tc_fence_after();
+            }
+            issue_S(t, st2);
+            mma_commit(&s_full[t]);
+          }
+        }
+        if (!ok) break;
+        if (has_next) mma_commit(&k_empty[st2]);
+        mma_commit(&v_empty[st]);
+      }
+      mma_commit(o_final);
+      mbar_wait_drain(o_final, 0);
+    }
+  } else if (warp >= 4) {
+    const int t = (warp - 4) / 4;
+    const int quarter = warp & 3;
+    if (t < ntile) {
+      const int rloc = quarter * 32 + lane;
+      const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+      const uint32_t tS = tmem + lane_off + t * 128;
+      const uint32_t tO = tmem + lane_off + 256 + t * 128;
+      float m = -INFINITY, l = 0.f;
+      bool ok = true;
+      for (int jj = 0; jj < nkv; ++jj) {
+        const int j = (a.start_tile + jj) % nkv;
+        const int nvalid = min(128, a.Skv - j * 128);
+        if (!mbar_wait(&s_full[t], jj & 1, err, 40)) { ok = false; break; }
+        tc_fence_after();
+        float mx = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t v[32];
+          tmem_ld32(tS + c * 32, v);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (c * 32 + i < nvalid) mx = fmaxf(mx, __uint_as_float(v[i]));
+        }
+        const float m_new = fmaxf(m, mx * a.scale_log2);
+        const bool need = m_new > m + kRescaleThreshold;
+        if (__any_sync(0xffffffffu, need)) {
+          if (jj > 0) {
+            const float alpha = exp2f(m - m_new);
+            l *= alpha;
+#pragma unroll
+            for (int c = 0; c < C::DPAD; c += 16) {
+              uint32_t v[16];
+              tmem_ld16(tO + c, v);
+              tmem_wait_ld();
+#pragma unroll
+              for (int i = 0; i < 16; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
+              tmem_st16(tO + c, v);
+            }
+          }
+          m = m_new;
+        }
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t v[32];
+          tmem_ld32(tS + c * 32, v);
+          tmem_wait_ld();
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int k = c * 32 + 2 * i;
+            const float p0 = (k < nvalid) ? exp2f(__uint_as_float(v[2 * i]) * a.scale_log2 - m) : 0.f;
+            const float p1 = (k + 1 < nvalid) ? exp2f(__uint_as_float(v[2 * i + 1]) * a.scale_log2 - m) : 0.f;
+            l += p0 + p1;
+            pk[i] = pack_bf16x2(p0, p1);
+          }
+          tmem_st16(tS + c * 16, pk);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[t]);
+      }
+      if (ok) ok = mbar_wait(o_final, 0, err, 41);
+      tc_fence_after();
+      const int s = q0 + t * 128 + rloc;
+      const float inv_l = (l > 0.f) ? 1.f / l : 0.f;
+      bf16* orow = a.O + (long)(b * a.Sq + s) * a.ldo + h * a.Dh;
+#pragma unroll
+      for (int c = 0; c < C::DPAD; c += 16) {
+        uint32_t v[16];
+        tmem_ld16(tO + c, v);
+        tmem_wait_ld();
+        if (s < a.Sq && ok) {
+#pragma unroll
+          for (int g = 0; g < 2; ++g) {
+            const int d = c + 8 * g;
+            if (d < a.Dh) {
+              uint4 pk;
+              pk.x = pack_bf16x2(__uint_as_float(v[8 * g + 0]) * inv_l, __uint_as_float(v[8 * g + 1]) * inv_l);
+              pk.y = pack_bf16x2(__uint_as_float(v[8 * g + 2]) * inv_l, __uint_as_float(v[8 * g + 3]) * inv_l);
+              pk.z = pack_bf16x2(__uint_as_float(v[8 * g + 4]) * inv_l, __uint_as_float(v[8 * g + 5]) * inv_l);
+              pk.w = pack_bf16x2(__uint_as_float(v[8 * g + 6]) * inv_l, __uint_as_float(v[8 * g + 7]) * inv_l);
+              *reinterpret_cast<uint4*>(orow + d) = pk;
+            }
+          }
+        }
+      }
+      if (s < a.Sq && ok) a.lse[(long)(b * a.Sq + s) * a.H + h] = (m + log2f(l)) * kLn2;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ===========================================================================
+// Backward (KV-stationary): one CTA per (b, h, 128-key tile); loops over query
+// tiles.  S^T = K Q^T and dP^T = V dO^T land in TMEM with keys as rows; the
+// dS warps turn them into P^T, dS^T (bf16, back into TMEM, and dS into smem);
+// dV += P^T dO and dK += dS^T Q accumulate in TMEM across the loop; the dQ
+// contribution dS K is read out by the dQ warps and added into an fp32 buffer.
+// ===========================================================================
+struct BwdArgs {
+  int B, Sq, Skv, H, Dh;
+  float scale_log2, scale;
+  const float* lse;
+  const float* delta;
+  float* dq_acc;  // [(b*Sq+s)*H + h][Dh]
+  bf16* dK;
+  long lddk;
+  bf16* dV;
+  long lddv;
+  int* err;
+};
+
+template <int NCH>
+struct BwdCfg {
+  static constexpr int DPAD = NCH * 8;
+  static constexpr int TILE = NCH * 2048;
+  static constexpr int STAGES = 2;
+  static constexpr int DS_BYTES = 128 * 128 * 2;
+  static constexpr int SMEM = 2 * TILE + STAGES * 2 * TILE + DS_BYTES + 1024 + 512;
+  static constexpr int DV_COL = 256;
+  static constexpr int DK_COL = 256 + DPAD;
+  static constexpr bool DQ_SEPARATE = (3 * DPAD <= 256);
+  static constexpr int DQ_COL = DQ_SEPARATE ? 256 + 2 * DPAD : 0;
+};
+constexpr int kBwdThreads = 320;  // w0 TMA, w1 MMA, w2-5 dS warps, w6-9 dQ warps
+
+template <int NCH>
+__global__ void __launch_bounds__(kBwdThreads, 1)
+    attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
+                    const BwdArgs a) {
+  using C = BwdCfg<NCH>;
+  constexpr int ST = C::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sK = smem;
+  uint8_t* sV = sK + C::TILE;
+  uint8_t* sQ = sV + C::TILE;         // [ST]
+  uint8_t* sdO = sQ + ST * C::TILE;   // [ST]
+  uint8_t* sdS = sdO + ST * C::TILE;  // 128x128 bf16, MN-major strips over queries
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sdS + C::DS_BYTES);
+  uint64_t* kv_full = bars;
+  uint64_t* qdo_full = bars + 1;       // [ST]
+  uint64_t* qdo_empty = qdo_full + ST;  // [ST]
+  uint64_t* s_full = qdo_empty + ST;
+  uint64_t* p_full = s_full + 1;
+  uint64_t* dq_full = p_full + 1;
+  uint64_t* dq_free = dq_full + 1;
+  uint64_t* fin = dq_free + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fin + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int nkt = (a.Skv + 127) / 128;
+  const int bh = blockIdx.x / nkt, kt = blockIdx.x % nkt;
+  const int b = bh / a.H, h = bh % a.H;
+  const int k0 = kt * 128;
+  const int nq = (a.Sq + 127) / 128;
+  int* err = a.err;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(&qdo_full[s], 1);
+      mbar_init(&qdo_empty[s], 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(p_full, 4);
+    mbar_init(dq_full, 1);
+    mbar_init(dq_free, 4);
+    mbar_init(fin, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS = tmem, tdP = tmem + 128, tdV = tmem + C::DV_COL, tdK = tmem + C::DK_COL,
+                 tdQ = tmem + C::DQ_COL;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      tma_prefetch_desc(&tmdO);
+      int issued[2] = {0, 0};
+      bool ok = true;
+      mbar_arrive_expect_tx(kv_full, 2 * C::TILE);
+#pragma unroll
+      for (int c = 0; c < NCH; ++c) {
+        tma_load_4d(sK + c * 2048, &tmK, kv_full, c * 8, h, k0, b);
+        tma_load_4d(sV + c * 2048, &tmV, kv_full, c * 8, h, k0, b);
+      }
+      for (int i = 0; i < nq && ok; ++i) {
+        const int st = i % ST;
+        const uint32_t ph = (i / ST) & 1;
+        if (!mbar_wait(&qdo_empty[st], ph ^ 1, err, 50)) { ok = false; break; }
+        mbar_arrive_expect_tx(&qdo_full[st], 2 * C::TILE);
+#pragma unroll
+        for (int c = 0; c < NCH; ++c) {
+          tma_load_4d(sQ + st * C::TILE + c * 2048, &tmQ, &qdo_full[st], c * 8, h, i * 128, b);
+          tma_load_4d(sdO + st * C::TILE + c * 2048, &tmdO, &qdo_full[st], c * 8, h, i * 128, b);
+        }
+        issued[st]++;
+      }
+      mbar_wait_drain(kv_full, 0);
+      for (int s = 0; s < ST; ++s)
+        if (issued[s]) mbar_wait_drain(&qdo_full[s], (issued[s] - 1) & 1);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idS = make_idesc_bf16(128, 128, false, false);
+      constexpr uint32_t idO = make_idesc_bf16(128, C::DPAD, false, true);
+      constexpr uint32_t idQ = make_idesc_bf16(128, C::DPAD, true, true);
+      const uint32_t ka = smem_u32(sK), va = smem_u32(sV), dsa = smem_u32(sdS);
+      bool ok = mbar_wait(kv_full, 0, err, 60);
+      for (int i = 0; i < nq && ok; ++i) {
+        const int st = i % ST;
+        const uint32_t ph = (i / ST) & 1;
+        if (!mbar_wait(&qdo_full[st], ph, err, 61)) { ok = false; break; }
+        if (!C::DQ_SEPARATE && i > 0) {
+          if (!mbar_wait(dq_free, (i - 1) & 1, err, 62)) { ok = false; break; }
+        }
+        tc_fence_after();
+        const uint32_t qa = smem_u32(sQ + st * C::TILE), doa = smem_u32(sdO + st * C::TILE);
+#pragma unroll
+        for (int ks = 0; ks < NCH / 2; ++ks)
+          mma_ss(tS, kmajor_desc(ka, ks), kmajor_desc(qa, ks), idS, ks > 0 ? 1u : 0u);
+#pragma unroll
+        for (int ks = 0; ks < NCH / 2; ++ks)
+          mma_ss(tdP, kmajor_desc(va, ks), kmajor_desc(doa, ks), idS, ks > 0 ? 1u : 0u);
+        mma_commit(s_full);
+        if (!mbar_wait(p_full, i & 1, err, 63)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks)
+          mma_ts(tdV, tS + ks * 8, mnmajor_desc(doa, ks), idO, (i > 0 || ks > 0) ? 1u : 0u);
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks)
+          mma_ts(tdK, tdP + ks * 8, mnmajor_desc(qa, ks), idO, (i > 0 || ks > 0) ? 1u : 0u);
+        if (C::DQ_SEPARATE && i > 0) {
+          if (!mbar_wait(dq_free, (i - 1) & 1, err, 64)) { ok = false; break; }
+          tc_fence_after();
+        }
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks)
+          mma_ss(tdQ, mnmajor_desc(dsa, ks), mnmajor_desc(ka, ks), idQ, ks > 0 ? 1u : 0u);
+        mma_commit(dq_full);
+        mma_commit(&qdo_empty[st]);
+      }
+      mma_commit(fin);
+      mbar_wait_drain(fin, 0);
+    }
+  } else if (warp >= 2 && warp < 6) {
+    // ---------------- dS warps: thread = key row ----------------
+    const int quarter = warp & 3;
+    const int kr = quarter * 32 + lane;
+    const int key = k0 + kr;
+    const bool key_ok = key < a.Skv;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    bool ok = true;
+    for (int i = 0; i < nq; ++i) {
+      if (!mbar_wait(s_full, i & 1, err, 70)) { ok = false; break; }
+      tc_fence_after();
+      const int q0 = i * 128;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t s[32], dp[32];
+        tmem_ld32(tS + lane_off + c * 32, s);
+        tmem_ld32(tdP + lane_off + c * 32, dp);
+        tmem_wait_ld();
+        const int qi = q0 + c * 32 + lane;
+        const long qidx = (long)(b * a.Sq + qi) * a.H + h;
+        const float L = (qi < a.Sq) ? a.lse[qidx] * kLog2e : INFINITY;
+        const float Dl = (qi < a.Sq) ? a.delta[qidx] : 0.f;
+        uint32_t pp[16], dd[16];
+#pragma unroll
+        for (int k2 = 0; k2 < 16; ++k2) {
+          const float L0 = __shfl_sync(0xffffffffu, L, 2 * k2), L1 = __shfl_sync(0xffffffffu, L, 2 * k2 + 1);
+          const float D0 = __shfl_sync(0xffffffffu, Dl, 2 * k2), D1 = __shfl_sync(0xffffffffu, Dl, 2 * k2 + 1);
+          const float p0 = key_ok ? exp2f(__uint_as_float(s[2 * k2]) * a.scale_log2 - L0) : 0.f;
+          const float p1 = key_ok ? exp2f(__uint_as_float(s[2 * k2 + 1]) * a.scale_log2 - L1) : 0.f;
+          const float ds0 = p0 * (__uint_as_float(dp[2 * k2]) - D0);
+          const float ds1 = p1 * (__uint_as_float(dp[2 * k2 + 1]) - D1);
+          pp[k2] = pack_bf16x2(p0, p1);
+          dd[k2] = pack_bf16x2(ds0, ds1);
+        }
+        tmem_st16(tS + lane_off + c * 16, pp);
+        tmem_st16(tdP + lane_off + c * 16, dd);
+#pragma unroll
+        for (int g = 0; g < 4; ++g)
+          *reinterpret_cast<uint4*>(sdS + (c * 4 + g) * 2048 + kr * 16) =
+              make_uint4(dd[4 * g], dd[4 * g + 1], dd[4 * g + 2], dd[4 * g + 3]);
+      }
+      tmem_wait_st();
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+    }
+    if (ok) ok = mbar_wait(fin, 0, err, 71);
+    tc_fence_after();
+    bf16* vrow = a.dV + (long)(b * a.Skv + key) * a.lddv + h * a.Dh;
+#pragma unroll
+    for (int c = 0; c < C::DPAD; c += 16) {
+      uint32_t v[16];
+      tmem_ld16(tdV + lane_off + c, v);
+      tmem_wait_ld();
+      if (key_ok && ok) {
+#pragma unroll
+        for (int g = 0; g < 2; ++g) {
+          const int d = c + 8 * g;
+          if (d < a.Dh) {
+            uint4 pk;
+            pk.x = pack_bf16x2(__uint_as_float(v[8 * g + 0]), __uint_as_float(v[8 * g + 1]));
+            pk.y = pack_bf16x2(__uint_as_float(v[8 * g + 2]), __uint_as_float(v[8 * g + 3]));
+            pk.z = pack_bf16x2(__uint_as_float(v[8 * g + 4]), __uint_as_float(v[8 * g + 5]));
+            pk.w = pack_bf16x2(__uint_as_float(v[8 * g + 6]), __uint_as_float(v[8 * g + 7]));
+            *reinterpret_cast<uint4*>(vrow + d) = pk;
+          }
+        }
+      }
+    }
+  } else if (warp >= 6) {
+    // ---------------- dQ warps: thread = query row of the dQ partial ----------------
+    const int quarter = warp & 3;
+    const int qr = quarter * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    bool ok = true;
+    for (int i = 0; i < nq; ++i) {
+      if (!mbar_wait(dq_full, i & 1, err, 80)) { ok = false; break; }
+      tc_fence_after();
+      const int q = i * 128 + qr;
+      float* dst = a.dq_acc + ((long)(b * a.Sq + q) * a.H + h) * a.Dh;
+#pragma unroll
+      for (int c = 0; c < C::DPAD; c += 16) {
+        uint32_t v[16];
+        tmem_ld16(tdQ + lane_off + c, v);
+        tmem_wait_ld();
+        if (q < a.Sq) {
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            const int d = c + 4 * g;
+            if (d < a.Dh)
+              atomicAdd(reinterpret_cast<float4*>(dst + d),
+                        make_float4(__uint_as_float(v[4 * g]), __uint_as_float(v[4 * g + 1]),
+                                    __uint_as_float(v[4 * g + 2]), __uint_as_float(v[4 * g + 3])));
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dq_free);
+    }
+    if (ok) ok = mbar_wait(fin, 0, err, 81);
+    tc_fence_after();
+    const int key = k0 + qr;
+    bf16* krow = a.dK + (long)(b * a.Skv + key) * a.lddk + h * a.Dh;
+#pragma unroll
+    for (int c = 0; c < C::DPAD; c += 16) {
+      uint32_t v[16];
+      tmem_ld16(tdK + lane_off + c, v);
+      tmem_wait_ld();
+      if (key < a.Skv && ok) {
+#pragma unroll
+        for (int g = 0; g < 2; ++g) {
+          const int d = c + 8 * g;
+          if (d < a.Dh) {
+            uint4 pk;
+            pk.x = pack_bf16x2(__uint_as_float(v[8 * g + 0]) * a.scale, __uint_as_float(v[8 * g + 1]) * a.scale);
+            pk.y = pack_bf16x2(__uint_as_float(v[8 * g + 2]) * a.scale, __uint_as_float(v[8 * g + 3]) * a.scale);
+            pk.z = pack_bf16x2(__uint_as_float(v[8 * g + 4]) * a.scale, __uint_as_float(v[8 * g + 5]) * a.scale);
+            pk.w = pack_bf16x2(__uint_as_float(v[8 * g + 6]) * a.scale, __uint_as_float(v[8 * g + 7]) * a.scale);
+            *reinterpret_cast<uint4*>(krow + d) = pk;
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// dQ = scale * dq_acc  (fp32 [R*H, Dh] -> bf16 [R, ld] token-major)
+__global__ void dq_finalize_kernel(const float* __restrict__ acc, int R, int H, int Dh, float scale,
+                                   bf16* __restrict__ out, long ldo) {
+  const long i = ((long)blockIdx.x * blockDim.x + threadIdx.x) * 4;
+  const long total = (long)R * H * Dh;
+  if (i >= total) return;
+  const float4 v = *reinterpret_cast<const float4*>(acc + i);
+  const long row = i / ((long)H * Dh);
+  const long col = i % ((long)H * Dh);
+  bf16* o = out + row * ldo + col;
+  *reinterpret_cast<uint2*>(o) = make_uint2(pack_bf16x2(v.x * scale, v.y * scale), pack_bf16x2(v.z * scale, v.w * scale));
+}
+
+int nch_for(int Dh) {
+  const int dpad = ((Dh + 15) / 16) * 16;
+  if (dpad <= 64) return 8;
+  if (dpad <= 80) return 10;
+  if (dpad <= 96) return 12;
+  TORCH_CHECK(dpad <= 128, "harp attention: head_dim > 128 not supported (got ", Dh, ")");
+  return 16;
+}
+
+template <int NCH>
+void launch_fwd(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const FwdArgs& args,
+                cudaStream_t stream) {
+  using C = FwdCfg<NCH>;
+  static bool configured = false;
+  if (!configured) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_kernel<NCH>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    configured = true;
+  }
+  const int nqp = (args.Sq + 255) / 256;
+  const int grid = args.B * args.H * nqp;
+  attn_fwd_kernel<NCH><<<grid, kFwdThreads, C::SMEM, stream>>>(mq, mk, mv, args);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  count_launch();
+}
+
+template <int NCH>
+void launch_bwd(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mdo,
+                const BwdArgs& args, cudaStream_t stream) {
+  using C = BwdCfg<NCH>;
+  static bool configured = false;
+  if (!configured) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_kernel<NCH>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    configured = true;
+  }
+  const int nkt = (args.Skv + 127) / 128;
+  const int grid = args.B * args.H * nkt;
+  attn_bwd_kernel<NCH><<<grid, kBwdThreads, C::SMEM, stream>>>(mq, mk, mv, mdo, args);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  count_launch();
+}
+
+}  // namespace
+
+// q: [B*Sq, >= H*Dh] token-major (row stride q.stride(0)); k, v: [B*Skv, ...];
+// o: [B*Sq, ...]; lse: fp32 [B*Sq*H].  `ready` (optional) holds one flag per
+// `chunk_len` keys; key tiles are visited from `start_tile` and each waits for
+// its chunks' flags to reach `epoch`.
+void attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, int64_t B, int64_t Sq, int64_t Skv,
+              int64_t H, int64_t Dh, double scale, at::Tensor& o, at::Tensor& lse,
+              const c10::optional<at::Tensor>& ready, int64_t chunk_len, int64_t start_tile, int64_t epoch,
+              double timeout_s, at::Tensor& err) {
+  TORCH_CHECK(q.is_cuda() && k.is_cuda() && v.is_cuda() && o.is_cuda(), "attn_fwd: CUDA tensors");
+  TORCH_CHECK(q.scalar_type() == at::kBFloat16 && k.scalar_type() == at::kBFloat16 &&
+                  v.scalar_type() == at::kBFloat16 && o.scalar_type() == at::kBFloat16,
+              "attn_fwd: bf16");
+  TORCH_CHECK(q.stride(-1) == 1 && k.stride(-1) == 1 && v.stride(-1) == 1 && o.stride(-1) == 1, "attn_fwd: inner stride");
+  TORCH_CHECK(lse.scalar_type() == at::kFloat && lse.numel() >= B * Sq * H, "attn_fwd: lse");
+  if (B * Sq == 0) return;
+  TORCH_CHECK(Skv > 0, "attn_fwd: empty key sequence");
+  const at::cuda::CUDAGuard guard(q.device());
+  const int nch = nch_for((int)Dh);
+  CUtensorMap mq = make_strip_map(q.data_ptr(), B, Sq, q.stride(0), H, Dh, 128);
+  CUtensorMap mk = make_strip_map(k.data_ptr(), B, Skv, k.stride(0), H, Dh, 128);
+  CUtensorMap mv = make_strip_map(v.data_ptr(), B, Skv, v.stride(0), H, Dh, 128);
+  FwdArgs args;
+  args.B = B; args.Sq = Sq; args.Skv = Skv; args.H = H; args.Dh = Dh;
+  args.scale_log2 = (float)(scale * 1.4426950408889634);
+  args.O = reinterpret_cast<bf16*>(o.data_ptr());
+  args.ldo = o.stride(0);
+  args.lse = lse.data_ptr<float>();
+  args.ready = ready.has_value() ? reinterpret_cast<const unsigned int*>(ready->data_ptr<int>()) : nullptr;
+  args.chunk_len = chunk_len > 0 ? (int)chunk_len : (int)Skv;
+  args.start_tile = (int)start_tile;
+  args.epoch = (unsigned int)epoch;
+  args.timeout_ns = (unsigned long long)(timeout_s * 1e9);
+  args.err = err.data_ptr<int>();
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  switch (nch) {
+    case 8: launch_fwd<8>(mq, mk, mv, args, stream); break;
+    case 10: launch_fwd<10>(mq, mk, mv, args, stream); break;
+    case 12: launch_fwd<12>(mq, mk, mv, args, stream); break;
+    default: launch_fwd<16>(mq, mk, mv, args, stream); break;
+  }
+}
+
+// Backward.  delta = rowsum(dO * O) fp32 [B*Sq*H]; dq_acc fp32 [B*Sq*H*Dh],
+// zeroed by the caller; dk/dv written (bf16, token-major).
+void attn_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& dout,
+              const at::Tensor& lse, const at::Tensor& delta, int64_t B, int64_t Sq, int64_t Skv, int64_t H,
+              int64_t Dh, double scale, at::Tensor& dq_acc, at::Tensor& dk, at::Tensor& dv, at::Tensor& err) {
+  TORCH_CHECK(dq_acc.scalar_type() == at::kFloat && dq_acc.is_contiguous(), "attn_bwd: dq_acc fp32 contiguous");
+  TORCH_CHECK(dk.stride(-1) == 1 && dv.stride(-1) == 1 && dout.stride(-1) == 1, "attn_bwd: inner stride");
+  if (B * Skv == 0) return;
+  const at::cuda::CUDAGuard guard(q.device());
+  const int nch = nch_for((int)Dh);
+  CUtensorMap mq = make_strip_map(q.data_ptr(), B, Sq, q.stride(0), H, Dh, 128);
+  CUtensorMap mk = make_strip_map(k.data_ptr(), B, Skv, k.stride(0), H, Dh, 128);
+  CUtensorMap mv = make_strip_map(v.data_ptr(), B, Skv, v.stride(0), H, Dh, 128);
+  CUtensorMap mdo = make_strip_map(dout.data_ptr(), B, Sq, dout.stride(0), H, Dh, 128);
+  BwdArgs args;
+  args.B = B; args.Sq = Sq; args.Skv = Skv; args.H = H; args.Dh = Dh;
+  args.scale_log2 = (float)(scale * 1.4426950408889634);
+  args.scale = (float)scale;
+  args.lse = lse.data_ptr<float>();
+  args.delta = delta.data_ptr<float>();
+  args.dq_acc = dq_acc.data_ptr<float>();
+  args.dK = reinterpret_cast<bf16*>(dk.data_ptr());
+  args.lddk = dk.stride(0);
+  args.dV = reinterpret_cast<bf16*>(dv.data_ptr());
+  args.lddv = dv.stride(0);
+  args.err = err.data_ptr<int>();
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  switch (nch) {
+    case 8: launch_bwd<8>(mq, mk, mv, mdo, args, stream); break;
+    case 10: launch_bwd<10>(mq, mk, mv, mdo, args, stream); break;
+    case 12: launch_bwd<12>(mq, mk, mv, mdo, args, stream); break;
+    default: launch_bwd<16>(mq, mk, mv, mdo, args, stream); break;
+  }
+}
+
+void dq_finalize(const at::Tensor& acc, int64_t H, int64_t Dh, double scale, at::Tensor& out) {
+  const long total = acc.numel();
+  if (total == 0) return;
+  TORCH_CHECK(Dh % 4 == 0 && acc.is_contiguous(), "dq_finalize");
+  const int R = total / (H * Dh);
+  const at::cuda::CUDAGuard guard(acc.device());
+  dq_finalize_kernel<<<(total / 4 + 255) / 256, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      acc.data_ptr<float>(), R, (int)H, (int)Dh, (float)scale, reinterpret_cast<bf16*>(out.data_ptr()), out.stride(0));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  count_launch();
+}
+
+}  // namespace harp
+
+TORCH_LIBRARY_FRAGMENT(harp, m) {
+  m.def("attn_fwd(Tensor q, Tensor k, Tensor v, int B, int Sq, int Skv, int H, int Dh, float scale, Tensor(a!) o, "
+        "Tensor(b!) lse, Tensor? ready, int chunk_len, int start_tile, int epoch, float timeout_s, Tensor(c!) err) -> ()");
+  m.def("attn_bwd(Tensor q, Tensor k, Tensor v, Tensor dout, Tensor lse, Tensor delta, int B, int Sq, int Skv, "
+        "int H, int Dh, float scale, Tensor(a!) dq_acc, Tensor(b!) dk, Tensor(c!) dv, Tensor(d!) err) -> ()");
+  m.def("dq_finalize(Tensor acc, int H, int Dh, float scale, Tensor(a!) out) -> ()");
+}
+TORCH_LIBRARY_IMPL(harp, CUDA, m) {
+  m.impl("attn_fwd", &harp::attn_fwd);
+  m.impl("attn_bwd", &harp::attn_bwd);
+  m.impl("dq_finalize", &harp::dq_finalize);
+}

@@ -24,7 +24,6 @@
 #include <ATen/ATen.h>
 #include <c10/cuda/CUDAException.h>
 
-#include <mutex>
 
 namespace harp {
 
@@ -47,6 +46,8 @@ struct GemmArgs {
   int rows_per_batch;
   int epi;
   float alpha;
+  void* C2;  // kEpiGatedResidualSave: pre-gate value (acc + bias), bf16
+  long ldc2;
   int* err;
 };
 
@@ -93,9 +94,31 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int m, int n, 
   switch (a.epi) {
     case kEpiStoreBf16:
     case kEpiAccumBf16:
-    case kEpiGatedResidual: {
+    case kEpiGatedResidual:
+    case kEpiGatedResidualSave: {
       __nv_bfloat16* crow = reinterpret_cast<__nv_bfloat16*>(a.C) + (long)m * a.ldc + n;
-      if (a.epi == kEpiGatedResidual) {
+      if (a.epi == kEpiGatedResidualSave) {
+        __nv_bfloat16* c2 = reinterpret_cast<__nv_bfloat16*>(a.C2) + (long)m * a.ldc2 + n;
+        if (full && ((reinterpret_cast<uintptr_t>(c2) & 15) == 0)) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint4 pk;
+            pk.x = pack_bf16x2(x[8 * q + 0], x[8 * q + 1]);
+            pk.y = pack_bf16x2(x[8 * q + 2], x[8 * q + 3]);
+            pk.z = pack_bf16x2(x[8 * q + 4], x[8 * q + 5]);
+            pk.w = pack_bf16x2(x[8 * q + 6], x[8 * q + 7]);
+            *reinterpret_cast<uint4*>(c2 + 8 * q) = pk;
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (n + j < a.N) c2[j] = __float2bfloat16(x[j]);
+        }
+        // the residual path uses the bf16-rounded value, like an unfused gate * a
+#pragma unroll
+        for (int j = 0; j < 32; ++j) x[j] = __bfloat162float(__float2bfloat16(x[j]));
+      }
+      if (a.epi == kEpiGatedResidual || a.epi == kEpiGatedResidualSave) {
         const __nv_bfloat16* rrow = a.residual + (long)m * a.ldr + n;
         const __nv_bfloat16* g = a.gate + (long)(m / a.rows_per_batch) * a.gate_ld + n;
 #pragma unroll
@@ -356,7 +379,13 @@ __global__ void gemm_bf16_simt(const __nv_bfloat16* __restrict__ A, long sam, lo
       case kEpiAccumF32:
         reinterpret_cast<float*>(args.C)[m * args.ldc + n] += x;
         break;
-      case kEpiGatedResidual: {
+      case kEpiGatedResidual:
+      case kEpiGatedResidualSave: {
+        if (args.epi == kEpiGatedResidualSave) {
+          const __nv_bfloat16 xb = __float2bfloat16(x);
+          reinterpret_cast<__nv_bfloat16*>(args.C2)[m * args.ldc2 + n] = xb;
+          x = __bfloat162float(xb);
+        }
         const float r = __bfloat162float(args.residual[m * args.ldr + n]);
         const float g = __bfloat162float(args.gate[(m / args.rows_per_batch) * args.gate_ld + n]);
         reinterpret_cast<__nv_bfloat16*>(args.C)[m * args.ldc + n] = __float2bfloat16(r + g * x);
@@ -369,24 +398,6 @@ __global__ void gemm_bf16_simt(const __nv_bfloat16* __restrict__ A, long sam, lo
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn get_encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    cudaError_t e = cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q);
-    TORCH_CHECK(e == cudaSuccess && q == cudaDriverEntryPointSuccess && p != nullptr,
-                "harp_b200: cuTensorMapEncodeTiled entry point unavailable");
-    fn = reinterpret_cast<EncodeTiledFn>(p);
-  });
-  return fn;
-}
-
 // 2D bf16 map over a row-major [rows, cols] matrix with row stride `ld`
 // (elements); box = box_cols x box_rows, 128B swizzle.
 CUtensorMap make_map_2d(const void* base, long rows, long cols, long ld, int box_cols, int box_rows) {
@@ -401,16 +412,6 @@ CUtensorMap make_map_2d(const void* base, long rows, long cols, long ld, int box
   TORCH_CHECK(r == CUDA_SUCCESS, "harp_b200: cuTensorMapEncodeTiled failed (", (int)r, ") rows=", rows,
               " cols=", cols, " ld=", ld);
   return m;
-}
-
-int num_sms() {
-  static int n = -1;
-  if (n < 0) {
-    int dev;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-  }
-  return n;
 }
 
 template <int BN, bool A_MN, bool B_MN>
@@ -441,17 +442,19 @@ void dispatch_major(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorM
 // Pick the N tile that wastes the least work in the last column band and in
 // the last wave of the persistent grid.
 int pick_bn(int M, int N) {
-  const int cands[3] = {256, 192, 128};
-  int best = 256;
-  double best_cost = 1e30;
+  // Wider tiles reuse each A tile across more columns (less L2->SMEM traffic per
+  // FLOP), so take BN=256 unless its last wave / last column band wastes
+  // noticeably more work than a narrower tile.
   const int sms = num_sms();
-  for (int bn : cands) {
+  auto cost = [&](int bn) {
     const long tiles = (long)((M + BM - 1) / BM) * ((N + bn - 1) / bn);
     const long waves = (tiles + sms - 1) / sms;
-    // cost ~ waves * tile work (proportional to bn)
-    const double cost = (double)waves * bn;
-    if (cost < best_cost - 1e-9) { best_cost = cost; best = bn; }
-  }
+    const double eff = bn == 256 ? 1.0 : (bn == 192 ? 0.93 : 0.80);
+    return (double)waves * bn / eff;
+  };
+  int best = 256;
+  for (int bn : {192, 128})
+    if (cost(bn) < cost(best) * 0.97) best = bn;
   return best;
 }
 
@@ -468,7 +471,8 @@ static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 // (row stride lda), else [M, K].  B: if b_mn, B is stored [K, N], else [N, K].
 void gemm(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, at::Tensor& C, int M, int N, int K,
           const c10::optional<at::Tensor>& bias, int epi, double alpha, const c10::optional<at::Tensor>& residual,
-          const c10::optional<at::Tensor>& gate, int rows_per_batch, at::Tensor& err, bool force_simt) {
+          const c10::optional<at::Tensor>& gate, int rows_per_batch, at::Tensor& err, bool force_simt,
+          const c10::optional<at::Tensor>& C2) {
   TORCH_CHECK(A.is_cuda() && B.is_cuda() && C.is_cuda(), "harp gemm: CUDA tensors required");
   TORCH_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16, "harp gemm: bf16 operands");
   TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && C.dim() == 2, "harp gemm: 2-D operands");
@@ -489,7 +493,14 @@ void gemm(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, at::Te
   args.bias = bias.has_value() ? reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr()) : nullptr;
   args.residual = nullptr; args.ldr = 0; args.gate = nullptr; args.gate_ld = 0;
   args.rows_per_batch = rows_per_batch > 0 ? rows_per_batch : M;
-  if (epi == kEpiGatedResidual) {
+  args.C2 = nullptr;
+  args.ldc2 = 0;
+  if (epi == kEpiGatedResidualSave) {
+    TORCH_CHECK(C2.has_value() && C2->scalar_type() == at::kBFloat16 && C2->stride(1) == 1, "harp gemm: C2");
+    args.C2 = C2->data_ptr();
+    args.ldc2 = C2->stride(0);
+  }
+  if (epi == kEpiGatedResidual || epi == kEpiGatedResidualSave) {
     TORCH_CHECK(residual.has_value() && gate.has_value(), "harp gemm: gated residual needs residual and gate");
     args.residual = reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr());
     args.ldr = residual->stride(0);

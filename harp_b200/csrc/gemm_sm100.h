@@ -4,6 +4,7 @@
 #include <c10/util/Optional.h>
 
 #include <atomic>
+#include <cuda.h>
 
 namespace harp {
 
@@ -14,16 +15,29 @@ enum GemmEpi : int {
   kEpiAccumBf16 = 2,      // C += alpha*acc (+bias)                     bf16
   kEpiAccumF32 = 3,       // C += alpha*acc (+bias)                     fp32
   kEpiGatedResidual = 4,  // C = R + gate[row/rows_per_batch] * (alpha*acc + bias)   bf16
+  kEpiGatedResidualSave = 5,  // as 4, and C2 = alpha*acc + bias (the pre-gate value)  bf16
 };
 
 void gemm(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, at::Tensor& C, int M, int N, int K,
           const c10::optional<at::Tensor>& bias, int epi, double alpha, const c10::optional<at::Tensor>& residual,
-          const c10::optional<at::Tensor>& gate, int rows_per_batch, at::Tensor& err, bool force_simt);
+          const c10::optional<at::Tensor>& gate, int rows_per_batch, at::Tensor& err, bool force_simt,
+          const c10::optional<at::Tensor>& C2 = c10::nullopt);
 
 // Count of harp kernel launches issued by this process (for the bench's
 // `gpu_launches` field).  Every launcher in the library calls count_launch().
 void count_launch();
 long long launch_count();
 void reset_launch_count();
+
+// Shared host helpers (runtime.cpp).
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn get_encode_fn();
+int num_sms();
+// 4-D bf16 "strip" map over a token-major [B, S, ld] activation holding H heads
+// of Dh elements per token: dims {Dh, H, S, B}; the box is 8 elements x 1 head
+// x `box_rows` tokens x 1 batch, i.e. one 16-byte column strip of a tile.
+CUtensorMap make_strip_map(const void* base, long B, long S, long ld, long H, long Dh, int box_rows);
 
 }  // namespace harp

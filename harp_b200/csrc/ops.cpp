@@ -69,9 +69,9 @@ at::Tensor& compat_err(const at::Device& dev) {
 void gemm_op(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, at::Tensor C, int64_t M, int64_t N,
              int64_t K, const c10::optional<at::Tensor>& bias, int64_t epi, double alpha,
              const c10::optional<at::Tensor>& residual, const c10::optional<at::Tensor>& gate, int64_t rows_per_batch,
-             at::Tensor err, bool force_simt) {
+             at::Tensor err, bool force_simt, const c10::optional<at::Tensor>& C2) {
   gemm(A, a_mn, B, b_mn, C, (int)M, (int)N, (int)K, bias, (int)epi, alpha, residual, gate, (int)rows_per_batch, err,
-       force_simt);
+       force_simt, C2);
 }
 
 // ---- xhpops (reference linear ops) ----
@@ -193,7 +193,8 @@ int64_t rows_per_block_op(int64_t rpb) { return rows_per_block_for((int)rpb); }
 
 TORCH_LIBRARY(harp, m) {
   m.def("gemm(Tensor A, bool a_mn, Tensor B, bool b_mn, Tensor(a!) C, int M, int N, int K, Tensor? bias, int epi, "
-        "float alpha, Tensor? residual, Tensor? gate, int rows_per_batch, Tensor(b!) err, bool force_simt) -> ()");
+        "float alpha, Tensor? residual, Tensor? gate, int rows_per_batch, Tensor(b!) err, bool force_simt, "
+        "Tensor(c!)? C2=None) -> ()");
   m.def("rmsnorm_mod_fwd(Tensor x, Tensor? w, Tensor? scale, Tensor? shift, int rows_per_batch, float eps, "
         "Tensor(a!) y, Tensor(b!) rstd, bool save_rms) -> ()");
   m.def("rmsnorm_mod_bwd(Tensor x, Tensor rstd, Tensor dy, Tensor? w, Tensor? scale, int rows_per_batch, "

@@ -1,2 +1,52 @@
-// placeholder, replaced by the host runtime
+// Host-side helpers shared by the kernels: the cuTensorMapEncodeTiled entry
+// point (resolved through the runtime, so nothing links libcuda directly), SM
+// count, and the tensor-map builders the tcgen05 kernels use.
 #include <ATen/ATen.h>
+#include <cuda_runtime.h>
+
+#include <mutex>
+
+#include "gemm_sm100.h"
+
+namespace harp {
+
+EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q);
+    TORCH_CHECK(e == cudaSuccess && q == cudaDriverEntryPointSuccess && p != nullptr,
+                "harp_b200: cuTensorMapEncodeTiled entry point unavailable");
+    fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+int num_sms() {
+  static int n[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (n[dev] == 0) cudaDeviceGetAttribute(&n[dev], cudaDevAttrMultiProcessorCount, dev);
+  return n[dev];
+}
+
+CUtensorMap make_strip_map(const void* base, long B, long S, long ld, long H, long Dh, int box_rows) {
+  TORCH_CHECK(Dh % 8 == 0, "harp attention: head_dim must be a multiple of 8 (got ", Dh, ")");
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(base) & 15) == 0, "harp attention: base not 16-byte aligned");
+  TORCH_CHECK((ld * 2) % 16 == 0, "harp attention: row stride must be a multiple of 16 bytes");
+  CUtensorMap m;
+  cuuint64_t dims[4] = {(cuuint64_t)Dh, (cuuint64_t)H, (cuuint64_t)S, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)Dh * 2, (cuuint64_t)ld * 2, (cuuint64_t)S * ld * 2};
+  cuuint32_t box[4] = {8, 1, (cuuint32_t)box_rows, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = get_encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box,
+                               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "harp attention: cuTensorMapEncodeTiled failed (", (int)r, ") B=", B, " S=", S,
+              " ld=", ld, " H=", H, " Dh=", Dh);
+  return m;
+}
+
+}  // namespace harp

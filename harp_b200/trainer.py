@@ -1,0 +1,251 @@
+"""Training engine: flat parameter/gradient buffers, ZeRO-1 sharded AdamW,
+gradient sync, and the step API used by train.py, bench.py and smoke().
+
+Mapping to the reference:
+  * The reference shares one copy of weights and gradients per die through
+    POSIX shm, sums SP gradients into it (accumulate_sp/accumulate.cpp), then
+    either all-reduces over DP (COMM_MODE 0) or reduce-scatters over the RS
+    group, steps AdamW on row chunks and all-gathers the chunks back
+    (COMM_MODE 1; managers/weight_manager.py:127-208).
+  * Here every rank owns a replica of the bf16 weights in ONE flat buffer
+    (parameters are views into it) and a flat bf16 gradient buffer.  After
+    backward, gradients are summed over every rank (SP and DP alike) by a
+    reduce-scatter of the flat buffer, each rank runs AdamW (fp32 master, m, v)
+    on its 1/world shard, and the updated bf16 shards are all-gathered.  That is
+    the reference's COMM_MODE 1 with rs_size = world, done on the whole buffer.
+  * comm="nvl" routes the reduce-scatter / AdamW / all-gather through the
+    NVLink kernels of harp_b200.parallel.nvlink (one fused kernel per bucket).
+"""
+from __future__ import annotations
+
+import math
+import os
+from dataclasses import dataclass
+from typing import Dict, List, Optional
+
+import torch
+import torch.distributed as dist
+
+from .models.dit import DiT, flow_matching_loss_local
+from .ops import functional as Fn
+from .parallel import collectives as C
+from .parallel.sequence import SPContext
+from .runtime import errors
+
+
+@dataclass
+class TrainConfig:
+    lr: float = 1e-4
+    beta1: float = 0.9
+    beta2: float = 0.999
+    eps: float = 1e-8
+    weight_decay: float = 0.0
+    grad_scale: float = 1.0
+    comm: str = "auto"  # "auto" | "torch" | "nvl"
+    align: int = 256  # elements; every parameter starts on a 512-byte boundary
+
+
+class FlatParams:
+    """Packs every parameter of `model` into one contiguous buffer (and one for
+    gradients).  Parameters become views; registration order is kept, so
+    adjacently registered weights (e.g. SwiGLU w1, w3) stay adjacent."""
+
+    def __init__(self, model: torch.nn.Module, device, dtype=torch.bfloat16, align: int = 256, world: int = 1):
+        self.params: List[torch.nn.Parameter] = []
+        self.names: List[str] = []
+        offs = []
+        off = 0
+        seen = set()
+        prev_end = None
+        for name, p in model.named_parameters():
+            if id(p) in seen:
+                continue
+            seen.add(id(p))
+            # keep tightly-packed neighbours contiguous (w1 directly followed by w3)
+            if not (name.endswith("w3.weight") and prev_end is not None):
+                off = (off + align - 1) // align * align
+            offs.append(off)
+            self.params.append(p)
+            self.names.append(name)
+            off += p.numel()
+            prev_end = off
+        quantum = align * max(1, world)
+        self.numel = (off + quantum - 1) // quantum * quantum
+        self.offsets = offs
+        self.flat = torch.zeros(self.numel, device=device, dtype=dtype)
+        self.grad = torch.zeros(self.numel, device=device, dtype=dtype)
+        for p, o in zip(self.params, offs):
+            n = p.numel()
+            self.flat[o:o + n].copy_(p.data.reshape(-1).to(device=device, dtype=dtype))
+            p.data = self.flat[o:o + n].view(p.shape)
+        self.attach_grads()
+
+    def attach_grads(self):
+        for p, o in zip(self.params, self.offsets):
+            p.grad = self.grad[o:o + p.numel()].view(p.shape)
+
+    def zero_grad(self):
+        self.grad.zero_()
+        # autograd may have replaced a grad view (e.g. after a None grad); re-attach
+        for p, o in zip(self.params, self.offsets):
+            g = p.grad
+            if g is None or g.data_ptr() != self.grad[o:].data_ptr():
+                p.grad = self.grad[o:o + p.numel()].view(p.shape)
+
+    def state_dict_views(self) -> Dict[str, torch.Tensor]:
+        return {n: p.data for n, p in zip(self.names, self.params)}
+
+
+class ShardedAdamW:
+    """AdamW with fp32 master weights and moments for this rank's 1/world
+    slice of the flat parameter buffer."""
+
+    def __init__(self, flat: FlatParams, cfg: TrainConfig, group=None):
+        self.flat, self.cfg, self.group = flat, cfg, group
+        self.world = C.world(group)
+        self.rank = C.rank(group)
+        n = flat.numel // self.world
+        self.shard_numel = n
+        lo = self.rank * n
+        self.master = flat.flat[lo:lo + n].float().clone()
+        self.m = torch.zeros_like(self.master)
+        self.v = torch.zeros_like(self.master)
+        self.grad_shard = torch.empty(n, device=flat.flat.device, dtype=flat.grad.dtype)
+        self.step_count = 0
+        self.lr = cfg.lr
+
+    def param_shard(self) -> torch.Tensor:
+        n = self.shard_numel
+        return self.flat.flat[self.rank * n:(self.rank + 1) * n]
+
+    def step(self, grad_shard: Optional[torch.Tensor] = None):
+        self.step_count += 1
+        g = grad_shard if grad_shard is not None else self.grad_shard
+        Fn.adamw_flat(self.master, self.m, self.v, g, self.param_shard(), self.lr, self.cfg.beta1, self.cfg.beta2,
+                      self.cfg.eps, self.cfg.weight_decay, self.step_count, self.cfg.grad_scale)
+
+    def state_dict(self):
+        return {"step": self.step_count, "lr": self.lr, "master": self.master.cpu(), "exp_avg": self.m.cpu(),
+                "exp_avg_sq": self.v.cpu(), "rank": self.rank, "world": self.world,
+                "shard_numel": self.shard_numel}
+
+    def load_state_dict(self, sd):
+        assert sd["world"] == self.world and sd["shard_numel"] == self.shard_numel, "optimizer shard layout mismatch"
+        self.step_count = sd["step"]
+        self.lr = sd["lr"]
+        self.master.copy_(sd["master"])
+        self.m.copy_(sd["exp_avg"])
+        self.v.copy_(sd["exp_avg_sq"])
+        self.param_shard().copy_(self.master.to(self.param_shard().dtype))
+
+
+@dataclass
+class ParallelState:
+    world_size: int = 1
+    rank: int = 0
+    sp_size: int = 1
+    dp_size: int = 1
+    world_group: object = None
+    sp_group: object = None
+    dp_group: object = None
+
+    @staticmethod
+    def build(sp_size: Optional[int] = None) -> "ParallelState":
+        if not (dist.is_available() and dist.is_initialized()):
+            return ParallelState()
+        W, r = dist.get_world_size(), dist.get_rank()
+        sp = sp_size or W
+        assert W % sp == 0, f"world {W} not divisible by sp {sp}"
+        dp = W // sp
+        sp_group = dp_group = None
+        # SP groups: consecutive ranks (the reference's sp_ranks[i // sp]); DP: same local index
+        for g in range(dp):
+            ranks = list(range(g * sp, (g + 1) * sp))
+            pg = dist.new_group(ranks) if sp < W else dist.group.WORLD
+            if r in ranks:
+                sp_group = pg
+        for l in range(sp):
+            ranks = list(range(l, W, sp))
+            pg = dist.new_group(ranks) if dp > 1 else None
+            if r in ranks:
+                dp_group = pg
+        return ParallelState(W, r, sp, dp, dist.group.WORLD, sp_group, dp_group)
+
+
+class Trainer:
+    """One training step = forward (sequence-parallel), backward, gradient sync,
+    sharded AdamW, parameter all-gather.  ``step()`` is the public end-to-end
+    call: it takes a (pinned) host batch, copies it to the GPU, trains, and
+    returns the loss as a Python float."""
+
+    def __init__(self, model: DiT, par: ParallelState, cfg: TrainConfig, device, sp_backend: str = "auto"):
+        self.model, self.par, self.cfg, self.device = model, par, cfg, device
+        self.flat = FlatParams(model, device, align=cfg.align, world=par.world_size)
+        self.opt = ShardedAdamW(self.flat, cfg, par.world_group)
+        backend = sp_backend
+        comm = None
+        if par.sp_size > 1:
+            if backend == "auto":
+                backend = "nvl" if (torch.device(device).type == "cuda" and _nvl_available()) else "torch"
+            if backend == "nvl":
+                from .parallel.nvlink import NVLinkComm
+
+                comm = NVLinkComm.get(par.sp_group, device)
+        self.sp = SPContext.from_group(par.sp_group, backend=backend, comm=comm) if par.sp_size > 1 else SPContext()
+        self.grad_comm = None
+        if par.world_size > 1 and cfg.comm == "nvl":
+            from .parallel.nvlink import NVLinkComm
+
+            self.grad_comm = NVLinkComm.get(par.world_group, device)
+        self.global_step = 0
+
+    # -- device-resident step (inputs already on the GPU) -------------------
+    def train_step(self, latent, noise, text, sigmas) -> torch.Tensor:
+        self.flat.zero_grad()
+        loss = flow_matching_loss_local(self.model, latent, noise, text, sigmas, self.sp)
+        if self.par.dp_size > 1:
+            loss = loss / self.par.dp_size
+        loss.backward()
+        self.sync_and_step()
+        self.global_step += 1
+        lsum = loss.detach().float().reshape(1)
+        if self.par.world_size > 1:
+            C.all_reduce_sum_(lsum, self.par.world_group)
+            # each SP group holds one sample set: undo the dp split and sum of SP partials
+        return lsum
+
+    def sync_and_step(self):
+        if self.par.world_size == 1:
+            self.opt.step(self.flat.grad)
+            return
+        if self.grad_comm is not None:
+            self.grad_comm.rs_adamw_ag(self.flat, self.opt)
+            return
+        C.reduce_scatter_flat(self.flat.grad, self.opt.grad_shard, self.par.world_group)
+        self.opt.step()
+        C.all_gather_flat(self.opt.param_shard(), self.flat.flat, self.par.world_group)
+
+    # -- public end-to-end step ------------------------------------------------
+    def step(self, batch: Dict[str, torch.Tensor]) -> float:
+        """batch: host tensors 'latent' [B,C,H,W], 'noise' [B,C,H,W], 'text' [B,L,Dt], 'sigmas' [B]
+        (pinned for asynchronous copies).  Returns the loss (global mean)."""
+        dev = self.device
+        latent = batch["latent"].to(dev, non_blocking=True)
+        noise = batch["noise"].to(dev, non_blocking=True)
+        text = batch["text"].to(dev, non_blocking=True)
+        sigmas = batch["sigmas"].to(dev, non_blocking=True)
+        loss = self.train_step(latent, noise, text, sigmas)
+        return float(loss.item())
+
+    def check_errors(self):
+        if torch.device(self.device).type == "cuda":
+            errors.check(torch.device(self.device))
+
+
+def _nvl_available() -> bool:
+    try:
+        from .parallel import nvlink  # noqa: F401
+
+        return nvlink.available()
+    except Exception:
+        return False
