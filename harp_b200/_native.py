@@ -31,6 +31,7 @@ SOURCES = [
     "attention_sm100.cu",
     "comm.cu",
     "runtime.cpp",
+    "noalloc_rmsnorm.cu",
 ]
 CUDA_FLAGS = [
     "-gencode",
