@@ -38,12 +38,39 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O only when the max grows by > 2^8
 
+// 2^x on the MUFU (hardware ex2 instruction; flushes denormal results to 0,
+// 2^-inf = 0).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 __device__ __forceinline__ void fence_proxy_async_global() {
   asm volatile("fence.proxy.async.global;" ::: "memory");
 }
+// Untiled bulk copy global -> shared (both 16-byte aligned, size % 16 == 0),
+// completing on `bar` (transaction bytes).
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+// dst(global, via map) += src(smem) for one box; bulk-group completion.
+__device__ __forceinline__ void tma_reduce_add_4d(const CUtensorMap* map, const void* src, int c0, int c1, int c2,
+                                                  int c3) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.4d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity) {
   const unsigned long long t0 = globaltimer_ns();
   while (!mbar_try_wait(bar, parity))
@@ -70,7 +97,8 @@ struct FwdArgs {
   float scale_log2;
   bf16* O;
   long ldo;
-  float* lse;  // natural-log LSE, index (b*Sq + s)*H + h
+  float* lse;  // natural-log LSE, [B, H, lse_ld] (lse_ld >= Sq rounded up to 128)
+  int lse_ld;
   const unsigned int* ready;  // per-chunk readiness flags (nullptr: all local)
   int chunk_len;
   int start_tile;
@@ -84,7 +112,7 @@ struct FwdCfg {
   static constexpr int DPAD = NCH * 8;
   static constexpr int TILE = NCH * 2048;
   static constexpr int STAGES = (NCH <= 10) ? 3 : 2;
-  static constexpr int SMEM = 2 * TILE + STAGES * 2 * TILE + 1024 + 512;
+  static constexpr int SMEM = 2 * TILE + STAGES * 2 * TILE + 128 + 256;  // 128-B alignment slack + barriers
 };
 constexpr int kFwdThreads = 384;  // w0 TMA, w1 MMA, w2-3 spare, w4-7 softmax tile 0, w8-11 softmax tile 1
 
@@ -95,7 +123,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   using C = FwdCfg<NCH>;
   constexpr int ST = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
   uint8_t* sQ = smem;
   uint8_t* sK = sQ + 2 * C::TILE;
   uint8_t* sV = sK + ST * C::TILE;
@@ -249,21 +277,33 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         const int nvalid = min(128, a.Skv - j * 128);
         if (!mbar_wait(&s_full[t], jj & 1, err, 40)) { ok = false; break; }
         tc_fence_after();
-        float mx = -INFINITY;
+        const bool full_tile = (nvalid == 128);  // only the last key tile of a sequence is partial
+        float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint32_t v[32];
           tmem_ld32(tS + c * 32, v);
           tmem_wait_ld();
+          if (full_tile) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (c * 32 + i < nvalid) mx = fmaxf(mx, __uint_as_float(v[i]));
+            for (int i = 0; i < 32; i += 4) {
+              mx0 = fmaxf(mx0, __uint_as_float(v[i]));
+              mx1 = fmaxf(mx1, __uint_as_float(v[i + 1]));
+              mx2 = fmaxf(mx2, __uint_as_float(v[i + 2]));
+              mx3 = fmaxf(mx3, __uint_as_float(v[i + 3]));
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (c * 32 + i < nvalid) mx0 = fmaxf(mx0, __uint_as_float(v[i]));
+          }
         }
+        const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
         const float m_new = fmaxf(m, mx * a.scale_log2);
         const bool need = m_new > m + kRescaleThreshold;
         if (__any_sync(0xffffffffu, need)) {
           if (jj > 0) {
-            const float alpha = exp2f(m - m_new);
+            const float alpha = ex2_approx(m - m_new);
             l *= alpha;
 #pragma unroll
             for (int c = 0; c < C::DPAD; c += 16) {
@@ -277,6 +317,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           }
           m = m_new;
         }
+        // p = 2^(s*scale*log2e - m): one packed FMA per pair, MUFU ex2, packed sum.
+        const float2 scl = make_float2(a.scale_log2, a.scale_log2);
+        const float2 negm = make_float2(-m, -m);
+        float2 lacc = make_float2(0.f, 0.f);
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint32_t v[32];
@@ -285,14 +329,19 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           uint32_t pk[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            const int k = c * 32 + 2 * i;
-            const float p0 = (k < nvalid) ? exp2f(__uint_as_float(v[2 * i]) * a.scale_log2 - m) : 0.f;
-            const float p1 = (k + 1 < nvalid) ? exp2f(__uint_as_float(v[2 * i + 1]) * a.scale_log2 - m) : 0.f;
-            l += p0 + p1;
-            pk[i] = pack_bf16x2(p0, p1);
+            float2 x = __ffma2_rn(make_float2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1])), scl, negm);
+            if (!full_tile) {
+              const int k = c * 32 + 2 * i;
+              if (k >= nvalid) x.x = -INFINITY;
+              if (k + 1 >= nvalid) x.y = -INFINITY;
+            }
+            const float2 p = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+            lacc = __fadd2_rn(lacc, p);
+            pk[i] = pack_bf16x2(p.x, p.y);
           }
           tmem_st16(tS + c * 16, pk);
         }
+        l += lacc.x + lacc.y;
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
@@ -323,7 +372,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           }
         }
       }
-      if (s < a.Sq && ok) a.lse[(long)(b * a.Sq + s) * a.H + h] = (m + log2f(l)) * kLn2;
+      if (s < a.Sq && ok) a.lse[(long)(b * a.H + h) * a.lse_ld + s] = (m + log2f(l)) * kLn2;
     }
   }
 
@@ -345,8 +394,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 struct BwdArgs {
   int B, Sq, Skv, H, Dh;
   float scale_log2, scale;
-  const float* lse;
-  const float* delta;
+  const float* lse;    // [B, H, lse_ld] natural log; +inf past Sq
+  const float* delta;  // [B, H, lse_ld]; 0 past Sq
+  int lse_ld;
   float* dq_acc;  // [(b*Sq+s)*H + h][Dh]
   bf16* dK;
   long lddk;
@@ -361,7 +411,10 @@ struct BwdCfg {
   static constexpr int TILE = NCH * 2048;
   static constexpr int STAGES = 2;
   static constexpr int DS_BYTES = 128 * 128 * 2;
-  static constexpr int SMEM = 2 * TILE + STAGES * 2 * TILE + DS_BYTES + 1024 + 512;
+  static constexpr int LD_BYTES = 256 * 4;  // per stage: 128 lse + 128 delta
+  static constexpr int SMEM = 2 * TILE + STAGES * 2 * TILE + DS_BYTES + STAGES * LD_BYTES + 128 + 256;
+  static_assert(SMEM <= 232448, "exceeds the 227 KB per-CTA shared memory limit");
+  static_assert(2 * TILE >= 128 * DPAD * 4, "dQ staging (128 x Dh fp32) must fit in one Q/dO stage");
   static constexpr int DV_COL = 256;
   static constexpr int DK_COL = 256 + DPAD;
   static constexpr bool DQ_SEPARATE = (3 * DPAD <= 256);
@@ -373,17 +426,20 @@ template <int NCH>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
-                    const BwdArgs a) {
+                    const __grid_constant__ CUtensorMap tmdQ, const BwdArgs a) {
   using C = BwdCfg<NCH>;
   constexpr int ST = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
   uint8_t* sK = smem;
   uint8_t* sV = sK + C::TILE;
-  uint8_t* sQ = sV + C::TILE;         // [ST]
-  uint8_t* sdO = sQ + ST * C::TILE;   // [ST]
-  uint8_t* sdS = sdO + ST * C::TILE;  // 128x128 bf16, MN-major strips over queries
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sdS + C::DS_BYTES);
+  // stage st holds Q_i at sQD + 2*st*TILE and dO_i right after it; once the
+  // iteration's MMAs are done the dQ warps reuse those 2 tiles to stage the
+  // fp32 dQ partial for the TMA reduce-add.
+  uint8_t* sQD = sV + C::TILE;
+  uint8_t* sdS = sQD + 2 * ST * C::TILE;  // 128x128 bf16, MN-major strips over queries
+  float* sLD = reinterpret_cast<float*>(sdS + C::DS_BYTES);  // [ST][lse 128 | delta 128]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sdS + C::DS_BYTES + ST * C::LD_BYTES);
   uint64_t* kv_full = bars;
   uint64_t* qdo_full = bars + 1;       // [ST]
   uint64_t* qdo_empty = qdo_full + ST;  // [ST]
@@ -392,7 +448,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint64_t* dq_full = p_full + 1;
   uint64_t* dq_free = dq_full + 1;
   uint64_t* fin = dq_free + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fin + 1);
+  uint64_t* dqs_bar = fin + 1;  // dQ warps -> TMA issuer: staging written
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(dqs_bar + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int nkt = (a.Skv + 127) / 128;
@@ -413,6 +470,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     mbar_init(dq_full, 1);
     mbar_init(dq_free, 4);
     mbar_init(fin, 1);
+    mbar_init(dqs_bar, 4);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -444,11 +502,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const int st = i % ST;
         const uint32_t ph = (i / ST) & 1;
         if (!mbar_wait(&qdo_empty[st], ph ^ 1, err, 50)) { ok = false; break; }
-        mbar_arrive_expect_tx(&qdo_full[st], 2 * C::TILE);
+        mbar_arrive_expect_tx(&qdo_full[st], 2 * C::TILE + C::LD_BYTES);
+        const long lrow = (long)(b * a.H + h) * a.lse_ld + i * 128;
+        bulk_load(sLD + st * 256, a.lse + lrow, 512, &qdo_full[st]);
+        bulk_load(sLD + st * 256 + 128, a.delta + lrow, 512, &qdo_full[st]);
 #pragma unroll
         for (int c = 0; c < NCH; ++c) {
-          tma_load_4d(sQ + st * C::TILE + c * 2048, &tmQ, &qdo_full[st], c * 8, h, i * 128, b);
-          tma_load_4d(sdO + st * C::TILE + c * 2048, &tmdO, &qdo_full[st], c * 8, h, i * 128, b);
+          tma_load_4d(sQD + 2 * st * C::TILE + c * 2048, &tmQ, &qdo_full[st], c * 8, h, i * 128, b);
+          tma_load_4d(sQD + (2 * st + 1) * C::TILE + c * 2048, &tmdO, &qdo_full[st], c * 8, h, i * 128, b);
         }
         issued[st]++;
       }
@@ -471,7 +532,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           if (!mbar_wait(dq_free, (i - 1) & 1, err, 62)) { ok = false; break; }
         }
         tc_fence_after();
-        const uint32_t qa = smem_u32(sQ + st * C::TILE), doa = smem_u32(sdO + st * C::TILE);
+        const uint32_t qa = smem_u32(sQD + 2 * st * C::TILE), doa = smem_u32(sQD + (2 * st + 1) * C::TILE);
 #pragma unroll
         for (int ks = 0; ks < NCH / 2; ++ks)
           mma_ss(tS, kmajor_desc(ka, ks), kmajor_desc(qa, ks), idS, ks > 0 ? 1u : 0u);
@@ -494,8 +555,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks)
           mma_ss(tdQ, mnmajor_desc(dsa, ks), mnmajor_desc(ka, ks), idQ, ks > 0 ? 1u : 0u);
-        mma_commit(dq_full);
-        mma_commit(&qdo_empty[st]);
+        mma_commit(dq_full);  // also frees Q_i/dO_i: the dQ warps hand the stage back
       }
       mma_commit(fin);
       mbar_wait_drain(fin, 0);
@@ -511,28 +571,37 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     for (int i = 0; i < nq; ++i) {
       if (!mbar_wait(s_full, i & 1, err, 70)) { ok = false; break; }
       tc_fence_after();
-      const int q0 = i * 128;
+      const float* sL = sLD + (i % ST) * 256;  // lse of the 128 queries of tile i (+inf past Sq)
+      const float* sDl = sL + 128;              // delta (0 past Sq)
+      const float2 scl = make_float2(a.scale_log2, a.scale_log2);
+      const float2 kmask = make_float2(key_ok ? 1.f : 0.f, key_ok ? 1.f : 0.f);
+      const float2 nl2e = make_float2(-kLog2e, -kLog2e);
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         uint32_t s[32], dp[32];
         tmem_ld32(tS + lane_off + c * 32, s);
         tmem_ld32(tdP + lane_off + c * 32, dp);
         tmem_wait_ld();
-        const int qi = q0 + c * 32 + lane;
-        const long qidx = (long)(b * a.Sq + qi) * a.H + h;
-        const float L = (qi < a.Sq) ? a.lse[qidx] * kLog2e : INFINITY;
-        const float Dl = (qi < a.Sq) ? a.delta[qidx] : 0.f;
         uint32_t pp[16], dd[16];
 #pragma unroll
-        for (int k2 = 0; k2 < 16; ++k2) {
-          const float L0 = __shfl_sync(0xffffffffu, L, 2 * k2), L1 = __shfl_sync(0xffffffffu, L, 2 * k2 + 1);
-          const float D0 = __shfl_sync(0xffffffffu, Dl, 2 * k2), D1 = __shfl_sync(0xffffffffu, Dl, 2 * k2 + 1);
-          const float p0 = key_ok ? exp2f(__uint_as_float(s[2 * k2]) * a.scale_log2 - L0) : 0.f;
-          const float p1 = key_ok ? exp2f(__uint_as_float(s[2 * k2 + 1]) * a.scale_log2 - L1) : 0.f;
-          const float ds0 = p0 * (__uint_as_float(dp[2 * k2]) - D0);
-          const float ds1 = p1 * (__uint_as_float(dp[2 * k2 + 1]) - D1);
-          pp[k2] = pack_bf16x2(p0, p1);
-          dd[k2] = pack_bf16x2(ds0, ds1);
+        for (int k4 = 0; k4 < 8; ++k4) {
+          const float4 L4 = *reinterpret_cast<const float4*>(sL + c * 32 + 4 * k4);  // smem broadcast
+          const float4 D4 = *reinterpret_cast<const float4*>(sDl + c * 32 + 4 * k4);
+#pragma unroll
+          for (int h2 = 0; h2 < 2; ++h2) {
+            const int k2 = 2 * k4 + h2;
+            const float2 Lp = h2 ? make_float2(L4.z, L4.w) : make_float2(L4.x, L4.y);
+            const float2 Dp = h2 ? make_float2(D4.z, D4.w) : make_float2(D4.x, D4.y);
+            // x = s*scale*log2e - lse*log2e
+            const float2 x = __ffma2_rn(make_float2(__uint_as_float(s[2 * k2]), __uint_as_float(s[2 * k2 + 1])), scl,
+                                        __fmul2_rn(Lp, nl2e));
+            const float2 p = __fmul2_rn(make_float2(ex2_approx(x.x), ex2_approx(x.y)), kmask);
+            const float2 ds = __fmul2_rn(
+                p, __fadd2_rn(make_float2(__uint_as_float(dp[2 * k2]), __uint_as_float(dp[2 * k2 + 1])),
+                              make_float2(-Dp.x, -Dp.y)));
+            pp[k2] = pack_bf16x2(p.x, p.y);
+            dd[k2] = pack_bf16x2(ds.x, ds.y);
+          }
         }
         tmem_st16(tS + lane_off + c * 16, pp);
         tmem_st16(tdP + lane_off + c * 16, dd);
@@ -579,28 +648,41 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     for (int i = 0; i < nq; ++i) {
       if (!mbar_wait(dq_full, i & 1, err, 80)) { ok = false; break; }
       tc_fence_after();
-      const int q = i * 128 + qr;
-      float* dst = a.dq_acc + ((long)(b * a.Sq + q) * a.H + h) * a.Dh;
+      const int st = i % ST;
+      float* stage = reinterpret_cast<float*>(sQD + 2 * st * C::TILE);  // [128][Dh] fp32 staging
+      float* srow = stage + qr * a.Dh;
 #pragma unroll
       for (int c = 0; c < C::DPAD; c += 16) {
         uint32_t v[16];
         tmem_ld16(tdQ + lane_off + c, v);
         tmem_wait_ld();
-        if (q < a.Sq) {
 #pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            const int d = c + 4 * g;
-            if (d < a.Dh)
-              atomicAdd(reinterpret_cast<float4*>(dst + d),
-                        make_float4(__uint_as_float(v[4 * g]), __uint_as_float(v[4 * g + 1]),
-                                    __uint_as_float(v[4 * g + 2]), __uint_as_float(v[4 * g + 3])));
-          }
+        for (int g = 0; g < 4; ++g) {
+          const int d = c + 4 * g;
+          if (d < a.Dh)
+            *reinterpret_cast<float4*>(srow + d) =
+                make_float4(__uint_as_float(v[4 * g]), __uint_as_float(v[4 * g + 1]), __uint_as_float(v[4 * g + 2]),
+                            __uint_as_float(v[4 * g + 3]));
         }
       }
       tc_fence_before();
+      fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(dq_free);
+      if (lane == 0) {
+        mbar_arrive(dq_free);
+        mbar_arrive(dqs_bar);
+      }
+      if (warp == 6 && lane == 0) {
+        // one thread: when all 4 dQ warps staged their rows, reduce-add the
+        // [128 x Dh] tile into dq_acc (rows past Sq are clipped by TMA), then
+        // give the stage back to the TMA producer.
+        if (!mbar_wait(dqs_bar, i & 1, err, 82)) { ok = false; break; }
+        tma_reduce_add_4d(&tmdQ, stage, 0, h, i * 128, b);
+        bulk_wait_read_all();
+        mbar_arrive(&qdo_empty[st]);
+      }
     }
+    if (warp == 6 && lane == 0) bulk_wait_all();
     if (ok) ok = mbar_wait(fin, 0, err, 81);
     tc_fence_after();
     const int key = k0 + qr;
@@ -675,7 +757,7 @@ void launch_fwd(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap&
 
 template <int NCH>
 void launch_bwd(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mdo,
-                const BwdArgs& args, cudaStream_t stream) {
+                const CUtensorMap& mdq, const BwdArgs& args, cudaStream_t stream) {
   using C = BwdCfg<NCH>;
   static bool configured = false;
   if (!configured) {
@@ -684,7 +766,7 @@ void launch_bwd(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap&
   }
   const int nkt = (args.Skv + 127) / 128;
   const int grid = args.B * args.H * nkt;
-  attn_bwd_kernel<NCH><<<grid, kBwdThreads, C::SMEM, stream>>>(mq, mk, mv, mdo, args);
+  attn_bwd_kernel<NCH><<<grid, kBwdThreads, C::SMEM, stream>>>(mq, mk, mv, mdo, mdq, args);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   count_launch();
 }
@@ -704,7 +786,8 @@ void attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, int
                   v.scalar_type() == at::kBFloat16 && o.scalar_type() == at::kBFloat16,
               "attn_fwd: bf16");
   TORCH_CHECK(q.stride(-1) == 1 && k.stride(-1) == 1 && v.stride(-1) == 1 && o.stride(-1) == 1, "attn_fwd: inner stride");
-  TORCH_CHECK(lse.scalar_type() == at::kFloat && lse.numel() >= B * Sq * H, "attn_fwd: lse");
+  const long lse_ld = ((Sq + 127) / 128) * 128;
+  TORCH_CHECK(lse.scalar_type() == at::kFloat && lse.numel() >= B * H * lse_ld, "attn_fwd: lse [B, H, roundup(Sq,128)]");
   if (B * Sq == 0) return;
   TORCH_CHECK(Skv > 0, "attn_fwd: empty key sequence");
   const at::cuda::CUDAGuard guard(q.device());
@@ -718,6 +801,7 @@ void attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, int
   args.O = reinterpret_cast<bf16*>(o.data_ptr());
   args.ldo = o.stride(0);
   args.lse = lse.data_ptr<float>();
+  args.lse_ld = (int)lse_ld;
   args.ready = ready.has_value() ? reinterpret_cast<const unsigned int*>(ready->data_ptr<int>()) : nullptr;
   args.chunk_len = chunk_len > 0 ? (int)chunk_len : (int)Skv;
   args.start_tile = (int)start_tile;
@@ -739,6 +823,11 @@ void attn_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, con
               const at::Tensor& lse, const at::Tensor& delta, int64_t B, int64_t Sq, int64_t Skv, int64_t H,
               int64_t Dh, double scale, at::Tensor& dq_acc, at::Tensor& dk, at::Tensor& dv, at::Tensor& err) {
   TORCH_CHECK(dq_acc.scalar_type() == at::kFloat && dq_acc.is_contiguous(), "attn_bwd: dq_acc fp32 contiguous");
+  const long lse_ld = ((Sq + 127) / 128) * 128;
+  TORCH_CHECK(lse.numel() >= B * H * lse_ld && delta.numel() >= B * H * lse_ld, "attn_bwd: lse/delta layout");
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(lse.data_ptr()) & 15) == 0 &&
+                  (reinterpret_cast<uintptr_t>(delta.data_ptr()) & 15) == 0,
+              "attn_bwd: lse/delta alignment");
   TORCH_CHECK(dk.stride(-1) == 1 && dv.stride(-1) == 1 && dout.stride(-1) == 1, "attn_bwd: inner stride");
   if (B * Skv == 0) return;
   const at::cuda::CUDAGuard guard(q.device());
@@ -747,12 +836,14 @@ void attn_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, con
   CUtensorMap mk = make_strip_map(k.data_ptr(), B, Skv, k.stride(0), H, Dh, 128);
   CUtensorMap mv = make_strip_map(v.data_ptr(), B, Skv, v.stride(0), H, Dh, 128);
   CUtensorMap mdo = make_strip_map(dout.data_ptr(), B, Sq, dout.stride(0), H, Dh, 128);
+  CUtensorMap mdq = make_f32_rows_map(dq_acc.data_ptr(), B, Sq, H, Dh, 128);
   BwdArgs args;
   args.B = B; args.Sq = Sq; args.Skv = Skv; args.H = H; args.Dh = Dh;
   args.scale_log2 = (float)(scale * 1.4426950408889634);
   args.scale = (float)scale;
   args.lse = lse.data_ptr<float>();
   args.delta = delta.data_ptr<float>();
+  args.lse_ld = (int)lse_ld;
   args.dq_acc = dq_acc.data_ptr<float>();
   args.dK = reinterpret_cast<bf16*>(dk.data_ptr());
   args.lddk = dk.stride(0);
@@ -761,10 +852,10 @@ void attn_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, con
   args.err = err.data_ptr<int>();
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
   switch (nch) {
-    case 8: launch_bwd<8>(mq, mk, mv, mdo, args, stream); break;
-    case 10: launch_bwd<10>(mq, mk, mv, mdo, args, stream); break;
-    case 12: launch_bwd<12>(mq, mk, mv, mdo, args, stream); break;
-    default: launch_bwd<16>(mq, mk, mv, mdo, args, stream); break;
+    case 8: launch_bwd<8>(mq, mk, mv, mdo, mdq, args, stream); break;
+    case 10: launch_bwd<10>(mq, mk, mv, mdo, mdq, args, stream); break;
+    case 12: launch_bwd<12>(mq, mk, mv, mdo, mdq, args, stream); break;
+    default: launch_bwd<16>(mq, mk, mv, mdo, mdq, args, stream); break;
   }
 }
 

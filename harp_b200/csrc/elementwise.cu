@@ -708,9 +708,10 @@ __global__ void philox_uniform_kernel(void* out, int is_bf16, long n, unsigned l
   }
 }
 
-// Row-wise dot for attention backward: Dst[r, h] = sum_d dO[r,h,d]*O[r,h,d].
+// Row-wise dot for attention backward: delta[b, h, s] = sum_d dO[r,h,d]*O[r,h,d]
+// with r = b*S + s; output row stride `ld` (>= S) per (b, h).
 __global__ void rowdot_kernel(const bf16* __restrict__ a, long lda, const bf16* __restrict__ b, long ldb, int R,
-                              int H, int Dh, float* __restrict__ out) {
+                              int H, int Dh, int S, long ld, float* __restrict__ out) {
   const long item = (long)blockIdx.x * blockDim.x + threadIdx.x;
   if (item >= (long)R * H) return;
   const int row = (int)(item / H), h = (int)(item % H);
@@ -724,7 +725,8 @@ __global__ void rowdot_kernel(const bf16* __restrict__ a, long lda, const bf16* 
 #pragma unroll
     for (int j = 0; j < 8; ++j) s += fa[j] * fb[j];
   }
-  out[item] = s;
+  const int bb = row / S, ss = row % S;
+  out[((long)bb * H + h) * ld + ss] = s;
 }
 
 int pick_rpb(int rows_per_batch) {
@@ -1004,14 +1006,16 @@ void philox_uniform(at::Tensor& out, int64_t seed, int64_t offset, double lo, do
   count_launch();
 }
 
-void rowdot(const at::Tensor& a, const at::Tensor& b, int64_t H, int64_t Dh, at::Tensor& out) {
+void rowdot(const at::Tensor& a, const at::Tensor& b, int64_t H, int64_t Dh, int64_t S, at::Tensor& out) {
   const int R = a.size(0);
   if (R == 0) return;
   TORCH_CHECK(Dh % 8 == 0, "rowdot: Dh % 8");
+  const long ld = ((S + 127) / 128) * 128;
+  TORCH_CHECK(out.numel() >= (R / S) * H * ld, "rowdot: out layout [B, H, roundup(S,128)]");
   const at::cuda::CUDAGuard g(a.device());
   const long items = (long)R * H;
   rowdot_kernel<<<(items + 255) / 256, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-      bp(a), a.stride(0), bp(b), b.stride(0), R, H, Dh, out.data_ptr<float>());
+      bp(a), a.stride(0), bp(b), b.stride(0), R, H, Dh, (int)S, ld, out.data_ptr<float>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   count_launch();
 }

@@ -54,7 +54,7 @@ void adamw_flat(at::Tensor& master, at::Tensor& m, at::Tensor& v, const at::Tens
 void adamw_list(at::TensorList params, at::TensorList grads, at::TensorList exp_avgs, at::TensorList exp_avg_sqs,
                 double lr, double beta1, double beta2, double eps, double wd, int64_t step);
 void philox_uniform(at::Tensor& out, int64_t seed, int64_t offset, double lo, double hi);
-void rowdot(const at::Tensor& a, const at::Tensor& b, int64_t H, int64_t Dh, at::Tensor& out);
+void rowdot(const at::Tensor& a, const at::Tensor& b, int64_t H, int64_t Dh, int64_t S, at::Tensor& out);
 
 namespace {
 
@@ -218,7 +218,7 @@ TORCH_LIBRARY(harp, m) {
   m.def("adamw_flat(Tensor(a!) master, Tensor(b!) m, Tensor(c!) v, Tensor grad, Tensor(d!)? param, float lr, "
         "float beta1, float beta2, float eps, float wd, int step, float grad_scale) -> ()");
   m.def("philox_uniform(Tensor(a!) out, int seed, int offset, float lo, float hi) -> ()");
-  m.def("rowdot(Tensor a, Tensor b, int H, int Dh, Tensor(a!) out) -> ()");
+  m.def("rowdot(Tensor a, Tensor b, int H, int Dh, int S, Tensor(a!) out) -> ()");
   m.def("launch_count() -> int");
   m.def("reset_launch_count() -> ()");
   m.def("rows_per_block(int rows_per_batch) -> int");

@@ -49,4 +49,19 @@ CUtensorMap make_strip_map(const void* base, long B, long S, long ld, long H, lo
   return m;
 }
 
+CUtensorMap make_f32_rows_map(const void* base, long B, long S, long H, long Dh, int box_rows) {
+  TORCH_CHECK(Dh % 4 == 0 && Dh <= 256, "harp: fp32 row map needs Dh % 4 == 0 and Dh <= 256");
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(base) & 15) == 0, "harp: fp32 row map base alignment");
+  CUtensorMap m;
+  cuuint64_t dims[4] = {(cuuint64_t)Dh, (cuuint64_t)H, (cuuint64_t)S, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)Dh * 4, (cuuint64_t)H * Dh * 4, (cuuint64_t)S * H * Dh * 4};
+  cuuint32_t box[4] = {(cuuint32_t)Dh, 1, (cuuint32_t)box_rows, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = get_encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<void*>(base), dims, strides, box,
+                               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "harp: cuTensorMapEncodeTiled (fp32 rows) failed (", (int)r, ")");
+  return m;
+}
+
 }  // namespace harp

@@ -383,13 +383,22 @@ def gate_bwd(dy, a, gate, rows_per_batch, want_bias=True):
     return da.to(dy.dtype), dgate, dbias
 
 
-def rowdot(a: torch.Tensor, b: torch.Tensor, H: int, Dh: int) -> torch.Tensor:
+def lse_ld(S: int) -> int:
+    """Row stride of the per-(batch, head) LSE / delta buffers: S rounded up to a key tile."""
+    return (S + 127) // 128 * 128
+
+
+def rowdot(a: torch.Tensor, b: torch.Tensor, H: int, Dh: int, S: int) -> torch.Tensor:
+    """delta[b, h, s] = sum_d a[b*S+s, h, d] * b[b*S+s, h, d]; layout [B, H, lse_ld(S)] (0 past S)."""
     R = a.shape[0]
-    out = torch.empty(R * H, device=a.device)
+    B = R // S
+    ld = lse_ld(S)
+    out = torch.zeros(B * H * ld, device=a.device)
     if _cuda(a):
-        torch.ops.harp.rowdot(a, b, H, Dh, out)
+        torch.ops.harp.rowdot(a, b, H, Dh, S, out)
         return out
-    out.copy_((a.float().view(R, H, Dh) * b.float().view(R, H, Dh)).sum(-1).view(-1))
+    d = (a.float().view(B, S, H, Dh) * b.float().view(B, S, H, Dh)).sum(-1).permute(0, 2, 1)
+    out.view(B, H, ld)[:, :, :S].copy_(d)
     return out
 
 
@@ -415,10 +424,11 @@ def silu_bwd(dy: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
 # ---------------------------------------------------------------------------
 def attn_fwd(q, k, v, B, Sq, Skv, H, Dh, scale=None, ready=None, chunk_len=0, start_tile=0, epoch=0,
              timeout_s=10.0, out=None):
-    """q [B*Sq, >=H*Dh], k/v [B*Skv, >=H*Dh] token-major. Returns (o [B*Sq, H*Dh], lse fp32 [B*Sq*H])."""
+    """q [B*Sq, >=H*Dh], k/v [B*Skv, >=H*Dh] token-major.  Returns (o [B*Sq, H*Dh],
+    lse fp32 [B, H, lse_ld(Sq)] natural log, +inf past Sq)."""
     scale = scale if scale is not None else 1.0 / math.sqrt(Dh)
     o = out if out is not None else torch.empty(B * Sq, H * Dh, device=q.device, dtype=q.dtype)
-    lse = torch.empty(B * Sq * H, device=q.device)
+    lse = torch.full((B * H * lse_ld(Sq),), float("inf"), device=q.device)
     if _cuda(q):
         torch.ops.harp.attn_fwd(q, k, v, B, Sq, Skv, H, Dh, scale, o, lse, ready, chunk_len, start_tile, epoch,
                                 timeout_s, errors.word(q.device))
@@ -431,7 +441,7 @@ def attn_fwd(q, k, v, B, Sq, Skv, H, Dh, scale=None, ready=None, chunk_len=0, st
     p = torch.exp(s - l[..., None])
     of = torch.einsum("bhqk,bkhd->bqhd", p, vf)
     o.copy_(of.reshape(B * Sq, H * Dh).to(o.dtype))
-    lse.copy_(l.permute(0, 2, 1).reshape(-1))
+    lse.view(B, H, -1)[:, :, :Sq].copy_(l)
     return o, lse
 
 
@@ -442,7 +452,7 @@ def attn_bwd(q, k, v, o, do, lse, B, Sq, Skv, H, Dh, scale=None, dk_out=None, dv
     dv = dv_out if dv_out is not None else torch.empty(B * Skv, H * Dh, device=q.device, dtype=q.dtype)
     dq = dq_out if dq_out is not None else torch.empty(B * Sq, H * Dh, device=q.device, dtype=q.dtype)
     if _cuda(q):
-        delta = rowdot(do, o, H, Dh)
+        delta = rowdot(do, o, H, Dh, Sq)
         dq_acc = torch.zeros(B * Sq * H * Dh, device=q.device)
         torch.ops.harp.attn_bwd(q, k, v, do, lse, delta, B, Sq, Skv, H, Dh, scale, dq_acc, dk, dv,
                                 errors.word(q.device))
@@ -453,7 +463,7 @@ def attn_bwd(q, k, v, o, do, lse, B, Sq, Skv, H, Dh, scale=None, dk_out=None, dv
     vf = v[:, : H * Dh].float().view(B, Skv, H, Dh)
     dof = do.float().view(B, Sq, H, Dh)
     s = torch.einsum("bqhd,bkhd->bhqk", qf, kf) * scale
-    p = torch.exp(s - lse.view(B, Sq, H).permute(0, 2, 1)[..., None])
+    p = torch.exp(s - lse.view(B, H, -1)[:, :, :Sq, None])
     dvf = torch.einsum("bhqk,bqhd->bkhd", p, dof)
     dp = torch.einsum("bqhd,bkhd->bhqk", dof, vf)
     delta = (dof * o.float().view(B, Sq, H, Dh)).sum(-1).permute(0, 2, 1)[..., None]
