@@ -175,15 +175,26 @@ __global__ void rmsnorm_mod_bwd_kernel(const bf16* __restrict__ x, long ldx, con
 
 // out[g, d] (+)= sum_{j in group g} partial[j, d]; groups of `per_group`
 // consecutive partial rows.  out fp32 or bf16 with row stride ldo.
+// Block = 32 columns x 8 warps: lane = column, warp w sums rows w, w+8, ...
+// (coalesced 128-byte row segments), then warp 0 adds the 8 warp sums in a
+// fixed order (deterministic).
 __global__ void reduce_partials_kernel(const float* __restrict__ part, int nrows, int per_group, int D,
                                        void* __restrict__ out, long ldo, int out_bf16, int accumulate) {
-  const int d = blockIdx.x * blockDim.x + threadIdx.x;
+  __shared__ float ws[8][33];
+  const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
+  const int d = blockIdx.x * 32 + lane;
   const int g = blockIdx.y;
-  if (d >= D) return;
-  float s = 0.f;
   const int j0 = g * per_group;
   const int j1 = min(nrows, j0 + per_group);
-  for (int j = j0; j < j1; ++j) s += part[(long)j * D + d];
+  float s = 0.f;
+  if (d < D)
+    for (int j = j0 + warp; j < j1; j += 8) s += part[(long)j * D + d];
+  ws[warp][lane] = s;
+  __syncthreads();
+  if (warp != 0 || d >= D) return;
+  s = 0.f;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) s += ws[w][lane];
   if (out_bf16) {
     bf16* o = reinterpret_cast<bf16*>(out) + (long)g * ldo + d;
     if (accumulate) s += __bfloat162float(*o);
@@ -276,8 +287,8 @@ __global__ void qknorm_rope_fwd_kernel(const bf16* __restrict__ qkv, long ld, in
 // (row, head) items, 8 warps.
 __device__ __forceinline__ void norm_rope_bwd_one(const bf16* __restrict__ x, const bf16* __restrict__ dy,
                                                   const bf16* __restrict__ w, const float2* __restrict__ fr, int Dh,
-                                                  float rs, int do_norm, bf16* __restrict__ dx, float* sacc,
-                                                  int lane) {
+                                                  float rs, int do_norm, bf16* __restrict__ dx, float2 (&wacc)[4],
+                                                  bool want_w, int lane) {
   const int P = Dh / 2;
   float2 xv[4], gv[4], wv[4];
   float dot = 0.f;
@@ -316,9 +327,9 @@ __device__ __forceinline__ void norm_rope_bwd_one(const bf16* __restrict__ x, co
       const float d0 = rs * (gv[i].x * wv[i].x - xh0 * mu);
       const float d1 = rs * (gv[i].y * wv[i].y - xh1 * mu);
       *reinterpret_cast<uint32_t*>(dx + 2 * p) = pack_bf16x2(d0, d1);
-      if (sacc) {
-        atomicAdd(&sacc[2 * p], gv[i].x * xh0);
-        atomicAdd(&sacc[2 * p + 1], gv[i].y * xh1);
+      if (want_w) {  // per-lane accumulation of d(w) for the pairs this lane owns
+        wacc[i].x += gv[i].x * xh0;
+        wacc[i].y += gv[i].y * xh1;
       }
     }
   }
@@ -331,12 +342,15 @@ __global__ void qknorm_rope_bwd_kernel(const bf16* __restrict__ dq, const bf16* 
                                        const float2* __restrict__ freqs, int freq_rows, int do_norm,
                                        int items_per_block, bf16* __restrict__ dqkv, long lddx,
                                        float* __restrict__ pwq, float* __restrict__ pwk) {
-  extern __shared__ float sacc[];  // [2*Dh]
+  extern __shared__ float sacc[];  // [nwarps][2*Dh]: per-warp d(wq), d(wk) partials
   const int lane = threadIdx.x % 32, warp = threadIdx.x / 32, nw = blockDim.x / 32;
   const bool want_w = (pwq != nullptr) && do_norm;
-  if (want_w)
-    for (int i = threadIdx.x; i < 2 * Dh; i += blockDim.x) sacc[i] = 0.f;
-  __syncthreads();
+  float2 accq[4], acck[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    accq[i] = make_float2(0.f, 0.f);
+    acck[i] = make_float2(0.f, 0.f);
+  }
   const long base = (long)blockIdx.x * items_per_block;
   for (int it = warp; it < items_per_block; it += nw) {
     const long item = base + it;
@@ -348,16 +362,29 @@ __global__ void qknorm_rope_bwd_kernel(const bf16* __restrict__ dq, const bf16* 
     bf16* dxq = dqkv + (long)row * lddx + h * Dh;
     bf16* dxk = dxq + (long)H * Dh;
     norm_rope_bwd_one(xq, dq + (long)row * lddo + h * Dh, wq, fr, Dh, do_norm ? rstd_q[item] : 1.f, do_norm, dxq,
-                      want_w ? sacc : nullptr, lane);
+                      accq, want_w, lane);
     norm_rope_bwd_one(xk, dk + (long)row * lddo + h * Dh, wk, fr, Dh, do_norm ? rstd_k[item] : 1.f, do_norm, dxk,
-                      want_w ? sacc + Dh : nullptr, lane);
+                      acck, want_w, lane);
+  }
+  if (!want_w) return;
+  float* mine = sacc + warp * 2 * Dh;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int p = lane + 32 * i;
+    if (p < Dh / 2) {
+      mine[2 * p] = accq[i].x;
+      mine[2 * p + 1] = accq[i].y;
+      mine[Dh + 2 * p] = acck[i].x;
+      mine[Dh + 2 * p + 1] = acck[i].y;
+    }
   }
   __syncthreads();
-  if (want_w)
-    for (int i = threadIdx.x; i < Dh; i += blockDim.x) {
-      pwq[(long)blockIdx.x * Dh + i] = sacc[i];
-      pwk[(long)blockIdx.x * Dh + i] = sacc[Dh + i];
-    }
+  for (int i = threadIdx.x; i < 2 * Dh; i += blockDim.x) {
+    float v = 0.f;
+    for (int w = 0; w < nw; ++w) v += sacc[w * 2 * Dh + i];  // fixed order: deterministic
+    if (i < Dh) pwq[(long)blockIdx.x * Dh + i] = v;
+    else pwk[(long)blockIdx.x * Dh + i - Dh] = v;
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -790,7 +817,7 @@ void reduce_partials(const at::Tensor& part, int64_t per_group, at::Tensor& out,
   const int groups = out.size(0);
   if (nrows == 0) return;
   const at::cuda::CUDAGuard g(part.device());
-  dim3 grid((D + 255) / 256, groups);
+  dim3 grid((D + 31) / 32, groups);
   reduce_partials_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       part.data_ptr<float>(), nrows, (int)per_group, D, out.data_ptr(), out.stride(0),
       out.scalar_type() == at::kBFloat16 ? 1 : 0, accumulate ? 1 : 0);
@@ -830,7 +857,7 @@ void qknorm_rope_bwd(const at::Tensor& dq, const at::Tensor& dk, const at::Tenso
   const at::cuda::CUDAGuard g(qkv.device());
   const long items = (long)R * H;
   const long grid = (items + items_per_block - 1) / items_per_block;
-  qknorm_rope_bwd_kernel<<<grid, 256, 2 * Dh * sizeof(float), at::cuda::getCurrentCUDAStream()>>>(
+  qknorm_rope_bwd_kernel<<<grid, 256, 8 * 2 * Dh * sizeof(float), at::cuda::getCurrentCUDAStream()>>>(
       bp(dq), bp(dk), dq.stride(0), bp(qkv), qkv.stride(0),
       rstd_q.has_value() ? rstd_q->data_ptr<float>() : nullptr, rstd_k.has_value() ? rstd_k->data_ptr<float>() : nullptr,
       R, H, Dh, bp(wq), bp(wk),

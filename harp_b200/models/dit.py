@@ -237,10 +237,14 @@ class DiTBlockFunction(torch.autograd.Function):
         # ---- MLP branch: x2 = x1 + g2 * (hh W2^T + b2)
         da2, dg2, db2 = Fn.gate_bwd(dy, a2, g2, S, want_bias=True)
         dmod[:, 5 * D:6 * D] = dg2
-        dhh, dw2, _ = Fn.linear_bwd(da2, hh, w2, need_bias=False)
+        dhh, dw2, _ = Fn.linear_bwd(da2, hh, w2, need_bias=False, dw_out=_direct(w2))
         dgu = Fn.swiglu_bwd(dhh, gu)
         w13 = _w13(w1, w3)
-        dh2, dw13, _ = Fn.linear_bwd(dgu, h2, w13, need_bias=False)
+        g1d, g3d = _direct(w1), _direct(w3)
+        dw13_out = _w13(g1d, g3d) if (g1d is not None and g3d is not None) else None
+        if dw13_out is not None and dw13_out.data_ptr() != g1d.data_ptr():
+            dw13_out = None  # the two slots are not adjacent: write to a temporary instead
+        dh2, dw13, _ = Fn.linear_bwd(dgu, h2, w13, need_bias=False, dw_out=dw13_out)
         dx1, _, dsc2, dsh2 = Fn.rmsnorm_mod_bwd(x1, rstd2, dh2, None, sc2, S, dres=dy, want_mod=True)
         dmod[:, 3 * D:4 * D] = dsh2
         dmod[:, 4 * D:5 * D] = dsc2
@@ -248,28 +252,50 @@ class DiTBlockFunction(torch.autograd.Function):
         # ---- attention branch: x1 = x + g1 * (o Wo^T + bo)
         da1, dg1, dbo = Fn.gate_bwd(dx1, a1, g1, S, want_bias=True)
         dmod[:, 2 * D:3 * D] = dg1
-        do, dwo, _ = Fn.linear_bwd(da1, o, proj_w, need_bias=False)
+        do, dwo, _ = Fn.linear_bwd(da1, o, proj_w, need_bias=False, dw_out=_direct(proj_w))
         dqkv = torch.empty(R, 3 * D, device=dy.device, dtype=dy.dtype)
         dq, dk = sp_attention_backward(ctx.attn_saved, q, k, qkv[:, 2 * D:], o, do, B, S, H, Dh, sp,
                                        dv_out=dqkv[:, 2 * D:])
         dwq, dwk = Fn.qknorm_rope_bwd(dq, dk, qkv, rq, rk, H, Dh, qn_w, kn_w, freqs, cfg.qk_norm, dqkv,
                                       want_dw=cfg.qk_norm)
-        dh1, dwqkv, dbqkv = Fn.linear_bwd(dqkv, h1, qkv_w, need_bias=True)
+        dh1, dwqkv, dbqkv = Fn.linear_bwd(dqkv, h1, qkv_w, need_bias=True, dw_out=_direct(qkv_w))
         dx, _, dsc1, dsh1 = Fn.rmsnorm_mod_bwd(x2d, rstd1, dh1, None, sc1, S, dres=dx1, want_mod=True)
         dmod[:, 0:D] = dsh1
         dmod[:, D:2 * D] = dsc1
 
         # ---- adaLN: mod = silu(c) W^T + b
         dmod_b = dmod.to(torch.bfloat16)
-        dada_w = Fn.gemm(dmod_b, c_silu, a_mn=True, b_mn=True)  # [6D, Dc]
-        dada_b = dmod.sum(0).to(torch.bfloat16)
+        dada_w = Fn.gemm(dmod_b, c_silu, a_mn=True, b_mn=True, out=_direct(ada_w))  # [6D, Dc]
+        dada_b = dmod.sum(0)
         dc_silu = Fn.gemm(dmod_b, ada_w, b_mn=True)  # [B, Dc]
 
-        grads = [dada_w, dada_b, dwqkv, dbqkv]
+        grads = [_emit(ada_w, dada_w), _emit(ada_b, dada_b), _emit(qkv_w, dwqkv), _emit(qkv_b, dbqkv)]
         if cfg.qk_norm:
-            grads += [dwq.to(qn_w.dtype), dwk.to(kn_w.dtype)]
-        grads += [dwo, dbo.to(proj_b.dtype), dw13[:F_], dw13[F_:], dw2, db2.to(w2_b.dtype)]
+            grads += [_emit(qn_w, dwq), _emit(kn_w, dwk)]
+        grads += [_emit(proj_w, dwo), _emit(proj_b, dbo), _emit(w1, dw13[:F_]), _emit(w3, dw13[F_:]),
+                  _emit(w2, dw2), _emit(w2_b, db2)]
         return (dx.view(B, S, D), dc_silu, None, None, None, *grads)
+
+
+def _direct(p: torch.Tensor) -> Optional[torch.Tensor]:
+    """The gradient slot of `p` when the trainer enabled direct gradient writes
+    (p.grad is then a view into the flat gradient buffer, zeroed every step).
+    The fused block uses each of its parameters exactly once per step, so its
+    weight-gradient GEMMs can store straight into that slot."""
+    if getattr(p, "_harp_direct_grad", False) and p.grad is not None:
+        return p.grad
+    return None
+
+
+def _emit(p: torch.Tensor, g: torch.Tensor):
+    """What backward returns for parameter `p`: None when the gradient went
+    (or now goes) straight into p's slot, else the gradient in p's dtype."""
+    tgt = _direct(p)
+    if tgt is None:
+        return g.to(p.dtype)
+    if g.data_ptr() != tgt.data_ptr():
+        tgt.copy_(g.view_as(tgt))
+    return None
 
 
 # ---------------------------------------------------------------------------

@@ -83,6 +83,8 @@ class FlatParams:
     def attach_grads(self):
         for p, o in zip(self.params, self.offsets):
             p.grad = self.grad[o:o + p.numel()].view(p.shape)
+            # fused blocks may store their weight gradients straight into this slot
+            p._harp_direct_grad = True
 
     def zero_grad(self):
         self.grad.zero_()
