@@ -335,7 +335,7 @@ __device__ __forceinline__ void norm_rope_bwd_one(const bf16* __restrict__ x, co
   }
 }
 
-__global__ void qknorm_rope_bwd_kernel(const bf16* __restrict__ dq, const bf16* __restrict__ dk, long lddo,
+__global__ void qknorm_rope_bwd_kernel(const bf16* __restrict__ dq, const bf16* __restrict__ dk, long lddq, long lddk,
                                        const bf16* __restrict__ qkv, long ld, const float* __restrict__ rstd_q,
                                        const float* __restrict__ rstd_k, int R, int H, int Dh,
                                        const bf16* __restrict__ wq, const bf16* __restrict__ wk,
@@ -361,9 +361,9 @@ __global__ void qknorm_rope_bwd_kernel(const bf16* __restrict__ dq, const bf16* 
     const bf16* xk = xq + (long)H * Dh;
     bf16* dxq = dqkv + (long)row * lddx + h * Dh;
     bf16* dxk = dxq + (long)H * Dh;
-    norm_rope_bwd_one(xq, dq + (long)row * lddo + h * Dh, wq, fr, Dh, do_norm ? rstd_q[item] : 1.f, do_norm, dxq,
+    norm_rope_bwd_one(xq, dq + (long)row * lddq + h * Dh, wq, fr, Dh, do_norm ? rstd_q[item] : 1.f, do_norm, dxq,
                       accq, want_w, lane);
-    norm_rope_bwd_one(xk, dk + (long)row * lddo + h * Dh, wk, fr, Dh, do_norm ? rstd_k[item] : 1.f, do_norm, dxk,
+    norm_rope_bwd_one(xk, dk + (long)row * lddk + h * Dh, wk, fr, Dh, do_norm ? rstd_k[item] : 1.f, do_norm, dxk,
                       acck, want_w, lane);
   }
   if (!want_w) return;
@@ -853,12 +853,12 @@ void qknorm_rope_bwd(const at::Tensor& dq, const at::Tensor& dk, const at::Tenso
                      const c10::optional<at::Tensor>& pwq, const c10::optional<at::Tensor>& pwk, int64_t items_per_block) {
   const int R = qkv.size(0);
   if (R == 0) return;
-  TORCH_CHECK(dq.stride(0) == dk.stride(0), "qknorm_rope_bwd: dq/dk stride");
+  TORCH_CHECK(dq.stride(1) == 1 && dk.stride(1) == 1, "qknorm_rope_bwd: dq/dk inner stride");
   const at::cuda::CUDAGuard g(qkv.device());
   const long items = (long)R * H;
   const long grid = (items + items_per_block - 1) / items_per_block;
   qknorm_rope_bwd_kernel<<<grid, 256, 8 * 2 * Dh * sizeof(float), at::cuda::getCurrentCUDAStream()>>>(
-      bp(dq), bp(dk), dq.stride(0), bp(qkv), qkv.stride(0),
+      bp(dq), bp(dk), dq.stride(0), dk.stride(0), bp(qkv), qkv.stride(0),
       rstd_q.has_value() ? rstd_q->data_ptr<float>() : nullptr, rstd_k.has_value() ? rstd_k->data_ptr<float>() : nullptr,
       R, H, Dh, bp(wq), bp(wk),
       freqs.has_value() ? reinterpret_cast<const float2*>(freqs->data_ptr<float>()) : nullptr, (int)freq_rows,

@@ -1,0 +1,235 @@
+"""NVLink peer-memory communicator ("nvl" backend).
+
+The B200 replacement for the reference's HMPI process group plus die-shared
+memory (hmpi/ProcessGroupHMPI.cpp, gemm/ring_attention/ring_attn.cpp:1344-2410,
+accumulate_sp/accumulate.cpp).  One process per GPU; torch.distributed carries
+only the set-up (exchange of CUDA IPC handles); every data transfer is a
+harp kernel that reads or writes peer memory over NVLink.
+
+Synchronisation uses monotonically increasing epochs per purpose: a rank
+publishes "my buffer for epoch e is ready" by storing e into its slot of every
+peer's flag array (release, system scope); consumers wait until the slot is
+>= e (acquire, bounded by a timeout that raises HarpDeviceError instead of
+hanging).  Because epochs only grow, flags are never reset.  No kernel waits
+for another kernel of the same GPU: every wait is for a flag that a peer GPU
+writes.
+
+Purposes and buffers:
+  KV      per-layer symmetric K|V buffers; a layer's gather waits for each
+          peer's KV flag and pulls its chunk into the local gathered buffer.
+  DKV     two symmetric dK|dV buffers used alternately by consecutive
+          backward layers; the pull reduce-scatter of layer i waits for the
+          peers' DKV flags; DKV_ACK tells the writer that everyone finished
+          pulling, before the buffer is written again two layers later.
+  GRAD / PARAM  the fused gradient reduce-scatter + AdamW + parameter push
+          waits for every peer's GRAD flag; PARAM tells peers the new
+          parameters have landed, which the next step waits for.
+"""
+from __future__ import annotations
+
+import os
+from typing import Dict, List, Optional
+
+import torch
+import torch.distributed as dist
+
+from .. import _native
+from ..runtime import errors
+from . import collectives as C
+
+# flag slot layout (int32 per slot, world <= 8)
+_KV, _DKV, _DKV_ACK0, _DKV_ACK1, _GRAD, _PARAM, _BARRIER = 0, 8, 16, 24, 32, 40, 48
+_NFLAGS = 64
+DEFAULT_TIMEOUT_S = float(os.environ.get("HARP_COMM_TIMEOUT_S", "120"))
+
+
+def available() -> bool:
+    if os.environ.get("HARP_COMM", "").lower() == "torch":
+        return False
+    return torch.cuda.is_available() and _native.available() and hasattr(torch.ops, "harp_comm")
+
+
+class SymBuffer:
+    """One symmetric segment: allocated on every rank of `group` (a collective
+    call: same size and order everywhere) and mapped into every peer."""
+
+    def __init__(self, group, nbytes: int, device: torch.device):
+        self.nbytes = (nbytes + 4095) // 4096 * 4096
+        self.device = device
+        dev = device.index
+        ptr, handle = torch.ops.harp_comm.ipc_alloc(self.nbytes, dev)
+        world, rank = C.world(group), C.rank(group)
+        handles: List[Optional[list]] = [None] * world
+        dist.all_gather_object(handles, handle.tolist(), group=group)
+        self.bases: List[int] = []
+        self._opened: List[int] = []
+        for r in range(world):
+            if r == rank:
+                self.bases.append(ptr)
+            else:
+                p = torch.ops.harp_comm.ipc_open(torch.tensor(handles[r], dtype=torch.uint8), dev)
+                self.bases.append(p)
+                self._opened.append(p)
+        self._own = ptr
+        self.local = torch.ops.harp_comm.view(ptr, self.nbytes, torch.uint8, dev)
+
+    def tensor(self, numel: int, dtype: torch.dtype, offset: int = 0) -> torch.Tensor:
+        esz = torch.empty((), dtype=dtype).element_size()
+        assert offset % esz == 0 and offset + numel * esz <= self.nbytes
+        return self.local[offset:offset + numel * esz].view(dtype)
+
+    def release(self):
+        for p in self._opened:
+            torch.ops.harp_comm.ipc_release(p)
+        torch.ops.harp_comm.ipc_release(self._own)
+        self._opened = []
+
+
+class NVLinkComm:
+    _instances: Dict[tuple, "NVLinkComm"] = {}
+
+    @classmethod
+    def get(cls, group, device) -> "NVLinkComm":
+        key = (id(group), str(device))
+        inst = cls._instances.get(key)
+        if inst is None:
+            inst = cls(group, torch.device(device))
+            cls._instances[key] = inst
+        return inst
+
+    @classmethod
+    def close_all(cls):
+        for inst in list(cls._instances.values()):
+            inst.close()
+        cls._instances.clear()
+
+    def __init__(self, group, device: torch.device, timeout_s: float = DEFAULT_TIMEOUT_S):
+        _native.require()
+        self.group, self.device = group, device
+        self.world, self.rank = C.world(group), C.rank(group)
+        assert self.world <= 8, "harp NVLink comm: one node, at most 8 GPUs"
+        self.timeout_s = timeout_s
+        self.flags_buf = SymBuffer(group, _NFLAGS * 4, device)
+        self.flags = self.flags_buf.tensor(_NFLAGS, torch.int32)
+        self.flag_bases = self.flags_buf.bases
+        self.epoch = {"kv": 0, "dkv": 0, "grad": 0, "barrier": 0}
+        self._kv_bufs: List[SymBuffer] = []
+        self._kv_idx = 0
+        self._dkv_bufs: List[SymBuffer] = []
+        self._dkv_idx = 0
+        self._dkv_last_epoch = [0, 0]
+        self._flat: Optional[Dict[str, SymBuffer]] = None
+        torch.cuda.synchronize(device)
+        C.all_reduce_sum_(torch.zeros(1, device=device), group)  # everyone mapped before first use
+
+    # -- basics ---------------------------------------------------------------
+    @property
+    def err(self) -> torch.Tensor:
+        return errors.word(self.device)
+
+    def signal(self, base: int, value: int):
+        """Store `value` into slot base+rank of every rank's flag array (self included)."""
+        torch.ops.harp_comm.signal([b + 4 * base for b in self.flag_bases], self.rank, value, -1)
+
+    def wait_all(self, base: int, value: int):
+        """Wait (on the current stream) until every rank's slot base+c >= value."""
+        torch.ops.harp_comm.wait(self.flags, base, self.world, value, self.timeout_s, self.err)
+
+    def barrier(self):
+        self.epoch["barrier"] += 1
+        e = self.epoch["barrier"]
+        self.signal(_BARRIER, e)
+        self.wait_all(_BARRIER, e)
+
+    def begin_step(self):
+        self._kv_idx = 0
+        self._dkv_idx = 0
+
+    # -- sequence-parallel K/V exchange (forward) -------------------------------
+    def kv_exchange(self, k: torch.Tensor, v: torch.Tensor, B: int, S: int, HD: int):
+        """k, v: local [B*S, HD] views.  Returns (kv_full [B*W*S, 2HD], None, 0):
+        rows (b*W + c)*S .. +S of kv_full hold rank c's K|V of sample b."""
+        i = self._kv_idx
+        self._kv_idx += 1
+        nbytes = B * S * 2 * HD * 2
+        while len(self._kv_bufs) <= i:
+            self._kv_bufs.append(SymBuffer(self.group, nbytes, self.device))
+        buf = self._kv_bufs[i]
+        assert buf.nbytes >= nbytes, "K/V exchange buffer shape changed between steps"
+        kv_out = buf.tensor(B * S * 2 * HD, torch.bfloat16).view(B * S, 2 * HD)
+        kv_out[:, :HD].copy_(k)
+        kv_out[:, HD:].copy_(v)
+        self.epoch["kv"] += 1
+        e = self.epoch["kv"]
+        self.signal(_KV, e)
+        W = self.world
+        kv_full = torch.empty(B * W * S, 2 * HD, device=k.device, dtype=torch.bfloat16)
+        row = 2 * HD * 2  # bytes per token row
+        # each (source c, sample b) is one contiguous segment of S rows
+        torch.ops.harp_comm.gather(buf.bases, 0, S * row, kv_full, 0, S * row, W * S * row, S * row, B, self.rank,
+                                   self.flags, _KV, e, self.timeout_s, self.err)
+        return kv_full, None, 0
+
+    # -- sequence-parallel dK/dV reduce-scatter (backward) ----------------------
+    def dkv_buffer(self, rows: int, cols: int, dtype) -> torch.Tensor:
+        slot = self._dkv_idx % 2
+        nbytes = rows * cols * 2
+        while len(self._dkv_bufs) < 2:
+            self._dkv_bufs.append(SymBuffer(self.group, nbytes, self.device))
+        assert self._dkv_bufs[slot].nbytes >= nbytes
+        # everyone must have finished pulling what this buffer held two layers ago
+        last = self._dkv_last_epoch[slot]
+        if last > 0:
+            self.wait_all(_DKV_ACK0 if slot == 0 else _DKV_ACK1, last)
+        return self._dkv_bufs[slot].tensor(rows * cols, torch.bfloat16).view(rows, cols)
+
+    def dkv_reduce_scatter(self, dkv_full: torch.Tensor, B: int, S: int, HD: int) -> torch.Tensor:
+        slot = self._dkv_idx % 2
+        self._dkv_idx += 1
+        buf = self._dkv_bufs[slot]
+        self.epoch["dkv"] += 1
+        e = self.epoch["dkv"]
+        self.signal(_DKV, e)
+        W = self.world
+        out = torch.empty(B * S, 2 * HD, device=dkv_full.device, dtype=torch.bfloat16)
+        # my chunk of sample b in every peer's dkv_full: rows (b*W + rank)*S .. +S
+        seg = S * 2 * HD
+        torch.ops.harp_comm.reduce_scatter(buf.bases, self.rank * seg, W * seg, out, seg, seg, B, self.rank,
+                                           self.flags, _DKV, e, self.timeout_s, self.err)
+        self._dkv_last_epoch[slot] = e
+        self.signal(_DKV_ACK0 if slot == 0 else _DKV_ACK1, e)
+        return out
+
+    # -- gradients: fused reduce-scatter + AdamW + parameter push ---------------
+    def allocate_flat(self, numel: int):
+        """Symmetric flat parameter and gradient buffers (bf16)."""
+        if self._flat is None:
+            self._flat = {"param": SymBuffer(self.group, numel * 2, self.device),
+                          "grad": SymBuffer(self.group, numel * 2, self.device)}
+        return (self._flat["param"].tensor(numel, torch.bfloat16), self._flat["grad"].tensor(numel, torch.bfloat16))
+
+    def wait_params(self):
+        """Before touching parameters or gradients of a new step: every peer has
+        pushed its updated shard (and therefore finished reading our gradients)."""
+        if self.epoch["grad"] > 0:
+            self.wait_all(_PARAM, self.epoch["grad"])
+
+    def rs_adamw_ag(self, flat, opt):
+        assert self._flat is not None, "flat buffers must come from allocate_flat()"
+        self.epoch["grad"] += 1
+        e = self.epoch["grad"]
+        self.signal(_GRAD, e)
+        opt.step_count += 1
+        cfg = opt.cfg
+        n = opt.shard_numel
+        torch.ops.harp_comm.rs_adamw_ag(self._flat["grad"].bases, self._flat["param"].bases, self.rank * n, n,
+                                        opt.master, opt.m, opt.v, opt.lr, cfg.beta1, cfg.beta2, cfg.eps,
+                                        cfg.weight_decay, opt.step_count, cfg.grad_scale, self.rank, self.flags,
+                                        _GRAD, e, self.timeout_s, self.err)
+        self.signal(_PARAM, e)
+
+    def close(self):
+        torch.cuda.synchronize(self.device)
+        for b in self._kv_bufs + self._dkv_bufs + list((self._flat or {}).values()) + [self.flags_buf]:
+            b.release()
+        self._kv_bufs, self._dkv_bufs, self._flat = [], [], None

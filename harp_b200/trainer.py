@@ -50,7 +50,8 @@ class FlatParams:
     gradients).  Parameters become views; registration order is kept, so
     adjacently registered weights (e.g. SwiGLU w1, w3) stay adjacent."""
 
-    def __init__(self, model: torch.nn.Module, device, dtype=torch.bfloat16, align: int = 256, world: int = 1):
+    def __init__(self, model: torch.nn.Module, device, dtype=torch.bfloat16, align: int = 256, world: int = 1,
+                 alloc=None):
         self.params: List[torch.nn.Parameter] = []
         self.names: List[str] = []
         offs = []
@@ -72,8 +73,14 @@ class FlatParams:
         quantum = align * max(1, world)
         self.numel = (off + quantum - 1) // quantum * quantum
         self.offsets = offs
-        self.flat = torch.zeros(self.numel, device=device, dtype=dtype)
-        self.grad = torch.zeros(self.numel, device=device, dtype=dtype)
+        if alloc is not None:
+            # e.g. symmetric (peer-mapped) buffers of the NVLink communicator
+            self.flat, self.grad = alloc(self.numel)
+            self.flat.zero_()
+            self.grad.zero_()
+        else:
+            self.flat = torch.zeros(self.numel, device=device, dtype=dtype)
+            self.grad = torch.zeros(self.numel, device=device, dtype=dtype)
         for p, o in zip(self.params, offs):
             n = p.numel()
             self.flat[o:o + n].copy_(p.data.reshape(-1).to(device=device, dtype=dtype))
@@ -182,27 +189,36 @@ class Trainer:
 
     def __init__(self, model: DiT, par: ParallelState, cfg: TrainConfig, device, sp_backend: str = "auto"):
         self.model, self.par, self.cfg, self.device = model, par, cfg, device
-        self.flat = FlatParams(model, device, align=cfg.align, world=par.world_size)
+        on_gpu = torch.device(device).type == "cuda"
+        self.grad_comm = None
+        if par.world_size > 1 and on_gpu and (cfg.comm == "nvl" or (cfg.comm == "auto" and _nvl_available())):
+            from .parallel.nvlink import NVLinkComm
+
+            self.grad_comm = NVLinkComm.get(par.world_group, device)
+        alloc = self.grad_comm.allocate_flat if self.grad_comm is not None else None
+        self.flat = FlatParams(model, device, align=cfg.align, world=par.world_size, alloc=alloc)
         self.opt = ShardedAdamW(self.flat, cfg, par.world_group)
         backend = sp_backend
         comm = None
         if par.sp_size > 1:
             if backend == "auto":
-                backend = "nvl" if (torch.device(device).type == "cuda" and _nvl_available()) else "torch"
+                backend = "nvl" if (on_gpu and _nvl_available()) else "torch"
             if backend == "nvl":
                 from .parallel.nvlink import NVLinkComm
 
                 comm = NVLinkComm.get(par.sp_group, device)
+        self.sp_comm = comm
         self.sp = SPContext.from_group(par.sp_group, backend=backend, comm=comm) if par.sp_size > 1 else SPContext()
-        self.grad_comm = None
-        if par.world_size > 1 and cfg.comm == "nvl":
-            from .parallel.nvlink import NVLinkComm
-
-            self.grad_comm = NVLinkComm.get(par.world_group, device)
         self.global_step = 0
 
     # -- device-resident step (inputs already on the GPU) -------------------
     def train_step(self, latent, noise, text, sigmas) -> torch.Tensor:
+        for comm in {id(c): c for c in (self.sp_comm, self.grad_comm) if c is not None}.values():
+            comm.begin_step()
+        if self.grad_comm is not None:
+            # peers' parameter shards of the previous step have landed and they
+            # are done reading our gradient buffer: safe to zero it and run
+            self.grad_comm.wait_params()
         self.flat.zero_grad()
         loss = flow_matching_loss_local(self.model, latent, noise, text, sigmas, self.sp)
         if self.par.dp_size > 1:
