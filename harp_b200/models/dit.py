@@ -36,6 +36,7 @@ import torch
 import torch.nn as nn
 
 from ..ops import functional as Fn
+from ..ops.modules import LinearFunction, SiLUFunction
 from ..parallel.sequence import SPContext, sp_attention_backward, sp_attention_forward
 
 
@@ -323,42 +324,6 @@ class TimestepEmbedder(nn.Module):
         h = LinearFunction.apply(f, self.mlp[0].weight, self.mlp[0].bias)
         h = SiLUFunction.apply(h)
         return LinearFunction.apply(h, self.mlp[2].weight, self.mlp[2].bias)
-
-
-class LinearFunction(torch.autograd.Function):
-    """y = x W^T + b on the harp GEMM (any leading dims)."""
-
-    @staticmethod
-    def forward(ctx, x, w, b):
-        shp = x.shape
-        x2 = x.reshape(-1, shp[-1])
-        if not x2.is_contiguous():
-            x2 = x2.contiguous()
-        y = Fn.gemm(x2, w, bias=b)
-        ctx.save_for_backward(x2, w)
-        ctx.has_b = b is not None
-        ctx.shp = shp
-        return y.view(*shp[:-1], w.shape[0])
-
-    @staticmethod
-    def backward(ctx, dy):
-        x2, w = ctx.saved_tensors
-        dy2 = dy.reshape(-1, dy.shape[-1]).contiguous()
-        dx, dw, db = Fn.linear_bwd(dy2, x2, w, need_bias=ctx.has_b)
-        return dx.view(ctx.shp), dw, (db.to(w.dtype) if db is not None else None)
-
-
-class SiLUFunction(torch.autograd.Function):
-    @staticmethod
-    def forward(ctx, x):
-        x = x.contiguous()
-        ctx.save_for_backward(x)
-        return Fn.silu(x)
-
-    @staticmethod
-    def backward(ctx, dy):
-        (x,) = ctx.saved_tensors
-        return Fn.silu_bwd(dy.contiguous(), x)
 
 
 class FinalLayerFunction(torch.autograd.Function):

@@ -1,0 +1,502 @@
+"""Z-Image DiT: the reference's model family, same module tree and state_dict
+keys, running on the harp kernels.
+
+Reference sources (layout and math):
+  src/models/z_image/standalone_transformer.py
+      RMSNorm :123-156, TimestepEmbedder :159-194, ZAttention :198-276,
+      FeedForward :279-290, ZImageTransformerBlock :294-355, FinalLayer :358-372,
+      RopeEmbedder :375-414, ZImageTransformer2DModel :417-755
+  src/models/z_image/hl_model.py    Z_Transformer (SP wrapper, cond branch,
+                                    metadata embedders) :37-453
+  src/models/z_image/module/block.py, module/attn.py    Z_SingleBlock,
+                                    Z_JointBlock, Z_Attention
+State-dict layout of Z_Transformer (kept exactly):
+  {noise_refiner,context_refiner,layers,cond_refiner_1,cond_refiner_2}.<i>.attention.attn.
+      {to_q,to_k,to_v,to_out.0}.weight, {norm_q,norm_k}.weight
+  ....z_block.{attention_norm1,attention_norm2,ffn_norm1,ffn_norm2}.weight,
+      z_block.feed_forward.{w1,w2,w3}.weight, z_block.adaLN_modulation.0.{weight,bias}
+  cond_embedder_{1,2}.{weight,bias}, cond_pad_token, meta_embeddings.<i>.mlp.{0,2}.*
+  z_transformer.{all_x_embedder.2-1, all_final_layer.2-1.*, t_embedder.mlp.*,
+      cap_embedder.{0,1}.*, x_pad_token, cap_pad_token}
+
+Differences from the reference, on purpose:
+  * residual math of the blocks follows the base model (x + gate*norm2(f(...)));
+    HARP's block.py drops the MLP residual (block.py:44-49) - set
+    `harp_block_compat=True` to reproduce that.
+  * samples in a batch must have the same token count (the reference ignores
+    attention masks in its ring attention too, attn.py:91-99).
+  * under sequence parallelism every embedder and the final layer run on the
+    tokens a rank holds (never replicated), so summing parameter gradients
+    over all ranks is exact; the reference instead replicates them and keeps
+    only the owner's gradient (grad_manager.py:53-61).
+"""
+from __future__ import annotations
+
+import copy
+import json
+import math
+import os
+from typing import Dict, List, Optional, Sequence, Tuple
+
+import torch
+import torch.nn as nn
+
+from ..ops import functional as Fn
+from ..ops.modules import (LinearFunction, MySiLU, MyTanh, QKNormRopeFunction, kpLinear, kpRMSNorm, sp_attention)
+from ..parallel.sequence import SPContext
+
+ADALN_EMBED_DIM = 256
+SEQ_MULTI_OF = 32
+
+
+def Linear(i, o, bias=True):
+    return kpLinear(i, o, bias=bias, dtype=torch.float32)
+
+
+def RMSNorm(dim, eps=1e-5):
+    return kpRMSNorm(dim, eps=eps)
+
+
+class TimestepEmbedder(nn.Module):
+    def __init__(self, out_size, mid_size=None, frequency_embedding_size=256):
+        super().__init__()
+        mid_size = mid_size or out_size
+        self.mlp = nn.Sequential(Linear(frequency_embedding_size, mid_size), nn.SiLU(), Linear(mid_size, out_size))
+        self.frequency_embedding_size = frequency_embedding_size
+
+    @staticmethod
+    def timestep_embedding(t, dim, max_period=10000):
+        half = dim // 2
+        freqs = torch.exp(-math.log(max_period) * torch.arange(half, dtype=torch.float32, device=t.device) / half)
+        args = t[:, None].float() * freqs[None]
+        emb = torch.cat([torch.cos(args), torch.sin(args)], -1)
+        if dim % 2:
+            emb = torch.cat([emb, torch.zeros_like(emb[:, :1])], -1)
+        return emb
+
+    def forward(self, t):
+        f = self.timestep_embedding(t, self.frequency_embedding_size).to(self.mlp[0].weight.dtype)
+        h = self.mlp[0](f)
+        h = MySiLU.apply(h)
+        return self.mlp[2](h)
+
+
+class ZAttention(nn.Module):
+    def __init__(self, query_dim, heads, dim_head, qk_norm="rms_norm", eps=1e-5):
+        super().__init__()
+        inner = heads * dim_head
+        self.heads, self.dim_head = heads, dim_head
+        self.to_q = Linear(query_dim, inner, bias=False)
+        self.to_k = Linear(query_dim, inner, bias=False)
+        self.to_v = Linear(query_dim, inner, bias=False)
+        self.to_out = nn.ModuleList([Linear(inner, query_dim, bias=False), nn.Identity()])
+        self.norm_q = RMSNorm(dim_head, eps) if qk_norm else None
+        self.norm_k = RMSNorm(dim_head, eps) if qk_norm else None
+
+    def forward(self, x, freqs, sp: SPContext):
+        """x [B, S, D]; freqs fp32 [B*S, Dh/2, 2] (per token row)."""
+        H, Dh = self.heads, self.dim_head
+        q, k, v = self.to_q(x), self.to_k(x), self.to_v(x)
+        wq = self.norm_q.weight if self.norm_q is not None else None
+        wk = self.norm_k.weight if self.norm_k is not None else None
+        eps = self.norm_q.eps if self.norm_q is not None else 1e-5
+        q, k = QKNormRopeFunction.apply(q, k, wq, wk, freqs, H, Dh, eps, self.norm_q is not None)
+        o = sp_attention(q, k, v.contiguous(), H, Dh, sp)
+        return self.to_out[0](o)
+
+
+class FeedForward(nn.Module):
+    def __init__(self, dim, hidden_dim):
+        super().__init__()
+        self.w1 = Linear(dim, hidden_dim, bias=False)
+        self.w2 = Linear(hidden_dim, dim, bias=False)
+        self.w3 = Linear(dim, hidden_dim, bias=False)
+
+    def _forward_silu_gating(self, x1, x3):
+        return MySiLU.apply(x1) * x3
+
+    def forward(self, x):
+        return self.w2(self._forward_silu_gating(self.w1(x), self.w3(x)))
+
+
+class ZImageTransformerBlock(nn.Module):
+    def __init__(self, layer_id, dim, n_heads, n_kv_heads, norm_eps, qk_norm, modulation=True):
+        super().__init__()
+        self.dim, self.layer_id = dim, layer_id
+        self.head_dim = dim // n_heads
+        self.attention = ZAttention(dim, n_heads, dim // n_heads, "rms_norm" if qk_norm else None, eps=1e-5)
+        self.feed_forward = FeedForward(dim, int(dim / 3 * 8))
+        self.attention_norm1 = RMSNorm(dim, norm_eps)
+        self.ffn_norm1 = RMSNorm(dim, norm_eps)
+        self.attention_norm2 = RMSNorm(dim, norm_eps)
+        self.ffn_norm2 = RMSNorm(dim, norm_eps)
+        self.modulation = modulation
+        if modulation:
+            self.adaLN_modulation = nn.Sequential(Linear(min(dim, ADALN_EMBED_DIM), 4 * dim, bias=True))
+
+    def forward(self, x, freqs, adaln_input=None, sp: Optional[SPContext] = None, attention=None, compat=False):
+        sp = sp or SPContext()
+        attn = attention if attention is not None else self.attention
+        if self.modulation:
+            mod = self.adaLN_modulation(adaln_input).unsqueeze(1)
+            scale_msa, gate_msa, scale_mlp, gate_mlp = mod.chunk(4, dim=2)
+            gate_msa, gate_mlp = MyTanh.apply(gate_msa.contiguous()), MyTanh.apply(gate_mlp.contiguous())
+            scale_msa, scale_mlp = 1.0 + scale_msa, 1.0 + scale_mlp
+            a = attn(self.attention_norm1(x) * scale_msa, freqs, sp)
+            x = x + gate_msa * self.attention_norm2(a)
+            if compat:  # HARP block.py:44-49 (MLP residual dropped)
+                h = self.feed_forward(self.ffn_norm1(x) * scale_mlp)
+                return self.ffn_norm2(h) * gate_mlp + h
+            return x + gate_mlp * self.ffn_norm2(self.feed_forward(self.ffn_norm1(x) * scale_mlp))
+        a = attn(self.attention_norm1(x), freqs, sp)
+        x = x + self.attention_norm2(a)
+        if compat:
+            h = self.feed_forward(self.ffn_norm1(x))
+            return h + self.ffn_norm2(h)
+        return x + self.ffn_norm2(self.feed_forward(self.ffn_norm1(x)))
+
+
+class FinalLayer(nn.Module):
+    def __init__(self, hidden_size, out_channels):
+        super().__init__()
+        self.norm_final = nn.LayerNorm(hidden_size, elementwise_affine=False, eps=1e-6)
+        self.linear = Linear(hidden_size, out_channels, bias=True)
+        self.adaLN_modulation = nn.Sequential(nn.SiLU(), Linear(min(hidden_size, ADALN_EMBED_DIM), hidden_size))
+
+    def forward(self, x, c):
+        scale = 1.0 + self.adaLN_modulation[1](MySiLU.apply(c.contiguous()))
+        y = torch.nn.functional.layer_norm(x.float(), (x.shape[-1],), eps=1e-6).to(x.dtype) * scale.unsqueeze(1)
+        return self.linear(y)
+
+
+class RopeEmbedder:
+    """3-axis rotary tables: axis a of head_dim slice axes_dims[a] uses
+    frequencies theta^(-2i/d_a) at integer positions; returns fp32 (cos, sin)."""
+
+    def __init__(self, theta=256.0, axes_dims=(16, 56, 56), axes_lens=(64, 128, 128)):
+        self.theta, self.axes_dims, self.axes_lens = theta, tuple(axes_dims), tuple(axes_lens)
+
+    def __call__(self, ids: torch.Tensor) -> torch.Tensor:
+        parts = []
+        for a, d in enumerate(self.axes_dims):
+            inv = 1.0 / (self.theta ** (torch.arange(0, d, 2, dtype=torch.float64, device=ids.device) / d))
+            parts.append(ids[:, a].double()[:, None] * inv[None])
+        ang = torch.cat(parts, -1)
+        return torch.stack([ang.cos(), ang.sin()], -1).float()
+
+    def complex(self, ids):
+        f = self(ids)
+        return torch.complex(f[..., 0], f[..., 1])
+
+
+class ConfigMixin:
+    config_name = "config.json"
+
+    @classmethod
+    def load_config(cls, path, subfolder=None, revision=None):
+        p = os.path.expanduser(path)
+        if subfolder:
+            p = os.path.join(p, subfolder)
+        if os.path.isdir(p):
+            p = os.path.join(p, cls.config_name)
+        with open(p) as fh:
+            return json.load(fh)
+
+    @classmethod
+    def from_config(cls, config):
+        import inspect
+
+        keys = set(inspect.signature(cls.__init__).parameters) - {"self"}
+        return cls(**{k: v for k, v in dict(config).items() if k in keys})
+
+    def save_config(self, directory):
+        os.makedirs(directory, exist_ok=True)
+        with open(os.path.join(directory, self.config_name), "w") as fh:
+            json.dump(dict(self.config), fh, indent=2, sort_keys=True)
+
+
+def _grid(size, start, device):
+    axes = [torch.arange(s0, s0 + n, dtype=torch.int32, device=device) for s0, n in zip(start, size)]
+    return torch.stack(torch.meshgrid(axes, indexing="ij"), -1)
+
+
+class ZImageTransformer2DModel(nn.Module, ConfigMixin):
+    def __init__(self, all_patch_size=(2,), all_f_patch_size=(1,), in_channels=16, dim=3840, n_layers=30,
+                 n_refiner_layers=2, n_heads=30, n_kv_heads=30, norm_eps=1e-5, qk_norm=True, cap_feat_dim=2560,
+                 rope_theta=256.0, t_scale=1000.0, axes_dims=(32, 48, 48), axes_lens=(1024, 512, 512)):
+        super().__init__()
+        self.in_channels = self.out_channels = in_channels
+        self.all_patch_size, self.all_f_patch_size = tuple(all_patch_size), tuple(all_f_patch_size)
+        self.dim, self.n_heads, self.t_scale = dim, n_heads, t_scale
+        self.config = dict(all_patch_size=list(all_patch_size), all_f_patch_size=list(all_f_patch_size),
+                           in_channels=in_channels, dim=dim, n_layers=n_layers, n_refiner_layers=n_refiner_layers,
+                           n_heads=n_heads, n_kv_heads=n_kv_heads, norm_eps=norm_eps, qk_norm=qk_norm,
+                           cap_feat_dim=cap_feat_dim, rope_theta=rope_theta, t_scale=t_scale,
+                           axes_dims=list(axes_dims), axes_lens=list(axes_lens))
+        xe, fl = {}, {}
+        for p, f in zip(self.all_patch_size, self.all_f_patch_size):
+            xe[f"{p}-{f}"] = Linear(f * p * p * in_channels, dim, bias=True)
+            fl[f"{p}-{f}"] = FinalLayer(dim, p * p * f * in_channels)
+        self.all_x_embedder = nn.ModuleDict(xe)
+        self.all_final_layer = nn.ModuleDict(fl)
+        self.noise_refiner = nn.ModuleList([ZImageTransformerBlock(1000 + i, dim, n_heads, n_kv_heads, norm_eps,
+                                                                   qk_norm, True) for i in range(n_refiner_layers)])
+        self.context_refiner = nn.ModuleList([ZImageTransformerBlock(i, dim, n_heads, n_kv_heads, norm_eps, qk_norm,
+                                                                     False) for i in range(n_refiner_layers)])
+        self.t_embedder = TimestepEmbedder(min(dim, ADALN_EMBED_DIM), mid_size=1024)
+        self.cap_embedder = nn.Sequential(RMSNorm(cap_feat_dim, norm_eps), Linear(cap_feat_dim, dim, bias=True))
+        self.x_pad_token = nn.Parameter(torch.zeros(1, dim))
+        self.cap_pad_token = nn.Parameter(torch.zeros(1, dim))
+        self.layers = nn.ModuleList([ZImageTransformerBlock(i, dim, n_heads, n_kv_heads, norm_eps, qk_norm)
+                                     for i in range(n_layers)])
+        assert dim // n_heads == sum(axes_dims)
+        self.rope_embedder = RopeEmbedder(rope_theta, axes_dims, axes_lens)
+
+    # -- patchify (standalone_transformer.py:535-640), equal-size samples --
+    def patchify(self, images: List[torch.Tensor], patch_size: int, f_patch_size: int):
+        out, sizes = [], []
+        for img in images:
+            C, F_, H, W = img.shape
+            pF, pH, pW = f_patch_size, patch_size, patch_size
+            sizes.append((F_, H, W))
+            t = img.view(C, F_ // pF, pF, H // pH, pH, W // pW, pW).permute(1, 3, 5, 2, 4, 6, 0)
+            out.append(t.reshape((F_ // pF) * (H // pH) * (W // pW), pF * pH * pW * C))
+        return out, sizes
+
+    def unpatchify(self, x: torch.Tensor, size, patch_size, f_patch_size):
+        F_, H, W = size
+        pF, pH = f_patch_size, patch_size
+        n = (F_ // pF) * (H // pH) * (W // pH)
+        return (x[:n].view(F_ // pF, H // pH, W // pH, pF, pH, pH, self.out_channels)
+                .permute(6, 0, 3, 1, 4, 2, 5).reshape(self.out_channels, F_, H, W))
+
+    def positions(self, cap_len: int, grid: Tuple[int, int, int], device) -> Tuple[torch.Tensor, torch.Tensor]:
+        cap_pad = (-cap_len) % SEQ_MULTI_OF
+        cap_ids = _grid((cap_len + cap_pad, 1, 1), (1, 0, 0), device).flatten(0, 2)
+        img_ids = _grid(grid, (cap_len + cap_pad + 1, 0, 0), device).flatten(0, 2)
+        return img_ids, cap_ids
+
+    def forward(self, x: List[torch.Tensor], t, cap_feats: List[torch.Tensor], patch_size=2, f_patch_size=1,
+                return_dict=True, sp: Optional[SPContext] = None):
+        """Single-rank reference forward (standalone_transformer.py:673-755) on
+        equal-size samples whose caption length is a multiple of 32."""
+        sp = sp or SPContext()
+        B = len(x)
+        dev = x[0].device
+        c = self.t_embedder(t * self.t_scale)
+        imgs, sizes = self.patchify(x, patch_size, f_patch_size)
+        xs = self.all_x_embedder[f"{patch_size}-{f_patch_size}"](torch.stack(imgs))
+        caps = self.cap_embedder(torch.stack(list(cap_feats)).to(xs.dtype))
+        F_, H, W = sizes[0]
+        grid = (F_ // f_patch_size, H // patch_size, W // patch_size)
+        img_ids, cap_ids = self.positions(caps.shape[1], grid, dev)
+        f_img = self.rope_embedder(img_ids).repeat(B, 1, 1)
+        f_cap = self.rope_embedder(cap_ids).repeat(B, 1, 1)
+        adaln = c.to(xs.dtype)
+        for layer in self.noise_refiner:
+            xs = layer(xs, f_img, adaln, sp)
+        for layer in self.context_refiner:
+            caps = layer(caps, f_cap)
+        uni = torch.cat([xs, caps], 1)
+        f_uni = torch.cat([self.rope_embedder(img_ids), self.rope_embedder(cap_ids)], 0).repeat(B, 1, 1)
+        for layer in self.layers:
+            uni = layer(uni, f_uni, adaln, sp)
+        out = self.all_final_layer[f"{patch_size}-{f_patch_size}"](uni, adaln)
+        res = [self.unpatchify(out[i], sizes[i], patch_size, f_patch_size) for i in range(B)]
+        return (res,) if not return_dict else {"sample": res}
+
+
+# ---------------------------------------------------------------------------
+# HARP SP wrapper (hl_model.py) with its block/attention wrappers
+# ---------------------------------------------------------------------------
+class Z_Attention(nn.Module):
+    """module/attn.py:51-105: holds the pretrained ZAttention as `attn`."""
+
+    def __init__(self, pretrained_attn: ZAttention, sp_size: int = 1):
+        super().__init__()
+        self.attn = pretrained_attn
+        self.sp_size = sp_size
+
+    def forward(self, x, freqs, sp):
+        return self.attn(x, freqs, sp)
+
+
+class Z_SingleBlock(nn.Module):
+    """module/block.py:10-60: the base block as `z_block`, its attention re-routed."""
+
+    def __init__(self, pretrained_block: ZImageTransformerBlock, sp_size: int = 1, compat: bool = False):
+        super().__init__()
+        self.attention = Z_Attention(pretrained_block.attention, sp_size)
+        pretrained_block.attention = None
+        self.z_block = pretrained_block
+        self.compat = compat
+
+    def forward(self, hidden_states, attn_mask=None, RoPE_embeds=None, adaln_input=None, sp=None):
+        return self.z_block(hidden_states, RoPE_embeds, adaln_input, sp, attention=self.attention, compat=self.compat)
+
+
+Z_JointBlock = Z_SingleBlock
+
+
+class Z_Transformer(nn.Module):
+    """Sequence-parallel Z-Image with HARP's condition-image branch and metadata
+    embedders (hl_model.py:37-109).  forward() takes the reference's arguments
+    and returns the prediction for the image tokens this rank holds, plus the
+    range of image positions they cover (use loss_local for training)."""
+
+    def __init__(self, z_transformer: ZImageTransformer2DModel, num_metadata: int = 0, in_channels=None,
+                 use_cond: bool = False, sp_group_model=None, sp_size=None, cond_channels: int = 192,
+                 harp_block_compat: bool = False):
+        super().__init__()
+        self.sp_group_model = sp_group_model
+        self.out_channels = self.in_channels = in_channels or z_transformer.in_channels
+        c = harp_block_compat
+        if use_cond:
+            self.cond_refiner_1 = nn.ModuleList([Z_SingleBlock(b, sp_size or 1, c)
+                                                 for b in copy.deepcopy(z_transformer.noise_refiner)])
+            self.cond_refiner_2 = nn.ModuleList([Z_SingleBlock(b, sp_size or 1, c)
+                                                 for b in copy.deepcopy(z_transformer.noise_refiner)])
+            self.cond_embedder_1 = Linear(2 * 2 * cond_channels, z_transformer.dim)
+            self.cond_embedder_2 = Linear(2 * 2 * cond_channels, z_transformer.dim)
+            self.cond_pad_token = nn.Parameter(z_transformer.x_pad_token.detach().clone())
+        self.use_cond = use_cond
+        self.noise_refiner = nn.ModuleList([Z_SingleBlock(b, sp_size or 1, c) for b in z_transformer.noise_refiner])
+        z_transformer.noise_refiner = None
+        self.context_refiner = nn.ModuleList([Z_SingleBlock(b, sp_size or 1, c)
+                                              for b in z_transformer.context_refiner])
+        z_transformer.context_refiner = None
+        self.layers = nn.ModuleList([Z_JointBlock(b, sp_size or 1, c) for b in z_transformer.layers])
+        z_transformer.layers = None
+        self.z_transformer = z_transformer
+        self.n_metadata = num_metadata
+        self.meta_embeddings = (nn.ModuleList([TimestepEmbedder(min(z_transformer.dim, ADALN_EMBED_DIM),
+                                                                mid_size=1024) for _ in range(num_metadata)])
+                                if num_metadata > 0 else None)
+
+    @property
+    def config(self):
+        return self.z_transformer.config
+
+    def _cond_tokens(self, cond: torch.Tensor, patch_size: int):
+        C, H, W = cond.shape
+        t = cond.view(C, H // patch_size, patch_size, W // patch_size, patch_size).permute(1, 3, 2, 4, 0)
+        return t.reshape((H // patch_size) * (W // patch_size), patch_size * patch_size * C)
+
+    def forward_local(self, x: List[torch.Tensor], t, text_embedding: List[torch.Tensor], patch_size=2,
+                      f_patch_size=1, metadata=None, cond_list=None, sp: Optional[SPContext] = None):
+        """Returns (pred [B, n_local_img, p*p*C], img_lo, img_hi)."""
+        sp = sp or SPContext()
+        zt = self.z_transformer
+        B = len(x)
+        dev = x[0].device
+        c = zt.t_embedder(t * zt.t_scale)
+        if metadata is not None and self.meta_embeddings is not None:
+            for i, emb in enumerate(self.meta_embeddings):
+                c = c + emb(metadata[:, i])
+        imgs, sizes = zt.patchify(x, patch_size, f_patch_size)
+        img = torch.stack(imgs)  # [B, N, pdim]
+        cap = torch.stack(list(text_embedding))
+        F_, H, W = sizes[0]
+        grid = (F_ // f_patch_size, H // patch_size, W // patch_size)
+        N, L = img.shape[1], cap.shape[1]
+        img_ids, cap_ids = zt.positions(L, grid, dev)
+        L_pad = cap_ids.shape[0]
+        if L_pad != L:
+            cap = torch.cat([cap, cap[:, -1:].expand(B, L_pad - L, cap.shape[2])], 1)
+        adaln = c.to(torch.bfloat16 if img.dtype == torch.bfloat16 else img.dtype)
+        xs = _local(img, sp)
+        xs = zt.all_x_embedder[f"{patch_size}-{f_patch_size}"](xs)
+        lo_i, hi_i = _range(N, sp)
+        f_img = zt.rope_embedder(img_ids[lo_i:hi_i]).repeat(B, 1, 1)
+        for layer in self.noise_refiner:
+            xs = layer(xs, None, f_img, adaln, sp)
+        caps = zt.cap_embedder(_local(cap, sp).to(xs.dtype))
+        lo_c, hi_c = _range(L_pad, sp)
+        f_cap = zt.rope_embedder(cap_ids[lo_c:hi_c]).repeat(B, 1, 1)
+        if L_pad != L:
+            padm = torch.arange(lo_c, hi_c, device=dev) >= L
+            caps = torch.where(padm[None, :, None], zt.cap_pad_token.to(caps.dtype), caps)
+        for layer in self.context_refiner:
+            caps = layer(caps, None, f_cap, None, sp)
+        streams = [(xs, N), (caps, L_pad)]
+        ids = [img_ids, cap_ids]
+        if self.use_cond and cond_list is not None:
+            for j, cl in enumerate(cond_list):
+                ctoks = torch.stack([self._cond_tokens(cc, patch_size) for cc in cl])
+                Nc = ctoks.shape[1]
+                cids = _grid((1, H // patch_size, W // patch_size), (L_pad + 2 + j, 0, 0), dev).flatten(0, 2)
+                emb = getattr(self, f"cond_embedder_{j + 1}")
+                cs = emb(_local(ctoks.to(xs.dtype), sp))
+                lo_k, hi_k = _range(Nc, sp)
+                f_c = zt.rope_embedder(cids[lo_k:hi_k]).repeat(B, 1, 1)
+                for layer in getattr(self, f"cond_refiner_{j + 1}"):
+                    cs = layer(cs, None, f_c, adaln, sp)
+                streams.append((cs, Nc))
+                ids.append(cids)
+        # unified sequence [img ; text ; cond...]: gather each stream, concatenate, take this rank's chunk
+        full = [_gather_seq(s, sp) for s, _ in streams]
+        uni_full = torch.cat(full, 1)
+        uni = _local(uni_full, sp)
+        all_ids = torch.cat(ids, 0)
+        lo_u, hi_u = _range(all_ids.shape[0], sp)
+        f_uni = zt.rope_embedder(all_ids[lo_u:hi_u]).repeat(B, 1, 1)
+        for layer in self.layers:
+            uni = layer(uni, None, f_uni, adaln, sp)
+        out = zt.all_final_layer[f"{patch_size}-{f_patch_size}"](uni, adaln)
+        img_lo, img_hi = min(lo_u, N), min(hi_u, N)
+        return out[:, : max(0, img_hi - img_lo)], img_lo, img_hi
+
+    def forward(self, x, t, text_embedding, patch_size=2, f_patch_size=1, return_dict=True, metadata=None,
+                cond_list=None, sp: Optional[SPContext] = None):
+        pred, lo, hi = self.forward_local(x, t, text_embedding, patch_size, f_patch_size, metadata, cond_list, sp)
+        return (pred, lo, hi) if not return_dict else {"sample": pred, "range": (lo, hi)}
+
+
+def _range(n: int, sp: SPContext) -> Tuple[int, int]:
+    assert n % sp.size == 0, f"sequence length {n} not divisible by sp={sp.size}"
+    k = n // sp.size
+    return sp.rank * k, (sp.rank + 1) * k
+
+
+def _local(x: torch.Tensor, sp: SPContext) -> torch.Tensor:
+    if sp.size == 1:
+        return x
+    lo, hi = _range(x.shape[1], sp)
+    return x[:, lo:hi]
+
+
+def _gather_seq(x: torch.Tensor, sp: SPContext) -> torch.Tensor:
+    if sp.size == 1:
+        return x
+    from ..managers.shard_manager import SequenceAllGather
+
+    return SequenceAllGather.apply(x.contiguous(), sp.group)
+
+
+def zimage_loss_local(model: Z_Transformer, latent, noise, text, sigmas, sp: SPContext, metadata=None, cond=None,
+                      weighting=None):
+    """Flow-matching loss on this rank's image tokens, normalized by the global
+    element count (summing over SP ranks gives the global mean)."""
+    B = latent.shape[0]
+    s = sigmas.view(B, 1, 1, 1).to(latent.dtype)
+    x_t = (1.0 - s) * latent + s * noise
+    target = latent - noise  # the reference's target (train.py:496)
+    zt = model.z_transformer
+    pred, lo, hi = model.forward_local(list(x_t.unsqueeze(2).unbind(0)), (1000 - sigmas * 1000) / 1000,
+                                       list(text.unbind(0)), metadata=metadata, cond_list=cond, sp=sp)
+    tgt, _ = zt.patchify(list(target.unsqueeze(2).unbind(0)), 2, 1)
+    tgt = torch.stack(tgt)
+    if hi <= lo:
+        return pred.float().sum() * 0.0
+    sq = (pred.float() - tgt[:, lo:hi].float()).pow(2)
+    if weighting is not None:
+        sq = sq * weighting.view(B, 1, 1).float()
+    return sq.sum() / tgt.numel()
+
+
+PRESETS = {
+    "zimage-6b": dict(dim=3840, n_layers=30, n_refiner_layers=2, n_heads=30, cap_feat_dim=2560,
+                      axes_dims=(32, 48, 48), axes_lens=(1024, 512, 512)),
+    "zimage-tiny": dict(dim=256, n_layers=2, n_refiner_layers=1, n_heads=4, cap_feat_dim=64,
+                        axes_dims=(16, 24, 24), axes_lens=(256, 64, 64)),
+}

@@ -187,8 +187,12 @@ class Trainer:
     call: it takes a (pinned) host batch, copies it to the GPU, trains, and
     returns the loss as a Python float."""
 
-    def __init__(self, model: DiT, par: ParallelState, cfg: TrainConfig, device, sp_backend: str = "auto"):
+    def __init__(self, model, par: ParallelState, cfg: TrainConfig, device, sp_backend: str = "auto",
+                 loss_fn=None):
+        """loss_fn(model, latent, noise, text, sigmas, sp, **extra) -> this rank's share
+        of the global loss; defaults to the DiT flow-matching loss."""
         self.model, self.par, self.cfg, self.device = model, par, cfg, device
+        self.loss_fn = loss_fn or flow_matching_loss_local
         on_gpu = torch.device(device).type == "cuda"
         self.grad_comm = None
         if par.world_size > 1 and on_gpu and (cfg.comm == "nvl" or (cfg.comm == "auto" and _nvl_available())):
@@ -212,7 +216,7 @@ class Trainer:
         self.global_step = 0
 
     # -- device-resident step (inputs already on the GPU) -------------------
-    def train_step(self, latent, noise, text, sigmas) -> torch.Tensor:
+    def train_step(self, latent, noise, text, sigmas, **extra) -> torch.Tensor:
         for comm in {id(c): c for c in (self.sp_comm, self.grad_comm) if c is not None}.values():
             comm.begin_step()
         if self.grad_comm is not None:
@@ -220,7 +224,7 @@ class Trainer:
             # are done reading our gradient buffer: safe to zero it and run
             self.grad_comm.wait_params()
         self.flat.zero_grad()
-        loss = flow_matching_loss_local(self.model, latent, noise, text, sigmas, self.sp)
+        loss = self.loss_fn(self.model, latent, noise, text, sigmas, self.sp, **extra)
         if self.par.dp_size > 1:
             loss = loss / self.par.dp_size
         loss.backward()
@@ -252,12 +256,21 @@ class Trainer:
         noise = batch["noise"].to(dev, non_blocking=True)
         text = batch["text"].to(dev, non_blocking=True)
         sigmas = batch["sigmas"].to(dev, non_blocking=True)
-        loss = self.train_step(latent, noise, text, sigmas)
+        extra = {k: _to_dev(v, dev) for k, v in batch.items() if k not in ("latent", "noise", "text", "sigmas")}
+        loss = self.train_step(latent, noise, text, sigmas, **extra)
         return float(loss.item())
 
     def check_errors(self):
         if torch.device(self.device).type == "cuda":
             errors.check(torch.device(self.device))
+
+
+def _to_dev(v, dev):
+    if isinstance(v, torch.Tensor):
+        return v.to(dev, non_blocking=True)
+    if isinstance(v, (list, tuple)):
+        return type(v)(_to_dev(x, dev) for x in v)
+    return v
 
 
 def _nvl_available() -> bool:

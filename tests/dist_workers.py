@@ -1,0 +1,190 @@
+"""Rank bodies for the multi-process tests (gloo on CPU).  Each worker writes
+its results to <out>/rank<r>.pt; the test process compares them."""
+from __future__ import annotations
+
+import datetime
+import os
+import sys
+import time
+
+import torch
+import torch.distributed as dist
+
+
+def _init(rank, world, port, timeout_s=60):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=timeout_s))
+    torch.manual_seed(1234)
+
+
+def entry(rank, world, port, name, out, args):
+    _init(rank, world, port, timeout_s=args.get("pg_timeout", 60) if isinstance(args, dict) else 60)
+    try:
+        res = globals()[name](rank, world, out, args)
+        torch.save(res, os.path.join(out, f"rank{rank}.pt"))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------
+def sp_attention(rank, world, out, args):
+    from harp_b200.ops.modules import sp_attention as spa
+    from harp_b200.parallel.sequence import SPContext
+
+    B, S, H, Dh = 2, 32, 2, 16
+    g = torch.Generator().manual_seed(0)
+    q, k, v = (torch.randn(B, S, H * Dh, generator=g).bfloat16() for _ in range(3))
+    do = torch.randn(B, S, H * Dh, generator=g).bfloat16()
+    sp = SPContext.from_group(dist.group.WORLD, backend="torch")
+    n = S // world
+    sl = slice(rank * n, (rank + 1) * n)
+    ql, kl, vl = (t[:, sl].clone().requires_grad_(True) for t in (q, k, v))
+    o = spa(ql, kl, vl, H, Dh, sp)
+    o.backward(do[:, sl])
+    return {"o": o.detach(), "dq": ql.grad, "dk": kl.grad, "dv": vl.grad, "sl": (sl.start, sl.stop),
+            "q": q, "k": k, "v": v, "do": do}
+
+
+def trainer_run(rank, world, out, args):
+    from harp_b200.models.dit import DiT, PRESETS
+    from harp_b200.trainer import ParallelState, TrainConfig, Trainer
+
+    sp_size = args["sp"]
+    model = DiT(PRESETS["tiny"])
+    model.initialize_weights(0)
+    model = model.to(torch.bfloat16)
+    par = ParallelState.build(sp_size)
+    tr = Trainer(model, par, TrainConfig(lr=1e-3, weight_decay=0.01), "cpu")
+    batch = torch.load(args["batch"])
+    dp_rank = rank // sp_size
+    per = batch["latent"].shape[0] // par.dp_size
+    sel = slice(dp_rank * per, (dp_rank + 1) * per)
+    losses = []
+    for step in range(args["steps"]):
+        b = {k: v[sel] for k, v in batch.items()}
+        losses.append(tr.step(b))
+    return {"losses": losses, "flat": tr.flat.flat.clone(), "sd": {k: v.clone() for k, v in model.state_dict().items()}}
+
+
+def managers(rank, world, out, args):
+    from harp_b200.managers.grad_manager import AsyncGradSyncManager
+    from harp_b200.managers.shard_manager import SequenceAllGather, SequenceScatter, SPBroadcast
+    from harp_b200.managers.weight_manager import (AsyncParamAllGatherManager, build_balanced_param_groups,
+                                                   build_chunk_param, set_opt_hook)
+
+    res = {}
+    grp = dist.group.WORLD
+    # sequence scatter / all-gather / broadcast
+    x = torch.arange(2 * 8 * 3, dtype=torch.float32).view(2, 8, 3).requires_grad_(True)
+    loc = SequenceScatter.apply(x, grp)
+    res["scatter"] = loc.detach().clone()
+    (loc * (rank + 1)).sum().backward()
+    res["scatter_grad"] = x.grad.clone()
+    y = torch.full((1, 2, 2), float(rank)).requires_grad_(True)
+    full = SequenceAllGather.apply(y, grp)
+    res["gather"] = full.detach().clone()
+    (full * torch.arange(4.0).view(1, 4, 1)).sum().backward()
+    res["gather_grad"] = y.grad.clone()
+    z = torch.ones(3, requires_grad=True)
+    (SPBroadcast.apply(z, grp) * (rank + 1)).sum().backward()
+    res["bcast_grad"] = z.grad.clone()
+
+    # balanced ownership + row chunks + background all-gather
+    torch.manual_seed(5)
+    model = torch.nn.Sequential(torch.nn.Linear(8, 8), torch.nn.LayerNorm(8), torch.nn.Linear(8, 4))
+    mine, prank = build_balanced_param_groups(model, world, rank, block_size=100)
+    res["owners"] = [prank[id(p)] for p in model.parameters()]
+    for p in model.parameters():
+        p.shared_grad = torch.zeros_like(p)
+        p.state = torch.zeros((), dtype=torch.uint8)
+    chunks = build_chunk_param(list(model.parameters()), model, world, rank)
+    res["chunk_rows"] = [(getattr(c, "chunk_begin", 0), getattr(c, "chunk_end", c.shape[0] if c.ndim else 0))
+                         for c in chunks]
+    before = [p.detach().clone() for p in model.parameters()]
+    hooks = set_opt_hook(model, timeout_s=30)
+    mgr = AsyncParamAllGatherManager(grp, world)
+    for p in model.parameters():
+        if hasattr(p, "chunk_part"):
+            p.chunk_part.data.add_(float(rank + 1))  # "optimizer step" on this rank's rows
+            mgr.push(p)
+    mgr.wait_all()
+    model(torch.ones(1, 8))  # pre-hooks see every gathered parameter ready
+    for h in hooks:
+        h.remove()
+    mgr.shutdown()
+    res["gathered_delta"] = [(p.detach() - b) for p, b in zip(model.parameters(), before)]
+
+    # gradient sync, three communication modes.  The RS group (rows of a
+    # parameter) and the DP group (replicas) are orthogonal: mode 0 uses a
+    # DP group of both ranks; modes 1/2 an RS group of both ranks and a DP group
+    # of one.
+    solo = [dist.new_group([r]) for r in range(world)][rank]
+    for mode in (0, 1, 2):
+        torch.manual_seed(9)
+        m2 = torch.nn.Sequential(torch.nn.Linear(4, 4), torch.nn.Linear(4, 4))
+        for p in m2.parameters():
+            p.shared_grad = torch.zeros_like(p)
+        params = list(m2.parameters())
+        if mode:
+            build_chunk_param(params, m2, world, rank)
+        gm = AsyncGradSyncManager(m2, rank, 0, {id(p): rank for p in params}, set(params), sp_group=None,
+                                  dp_group=grp if mode == 0 else solo, rs_group=grp, comm_mode=mode,
+                                  replicated=lambda n: True)
+        (m2(torch.full((2, 4), float(rank + 1))).sum()).backward()
+        gm.wait_for_completion()
+        gm.shutdown()
+        res[f"grad_mode{mode}"] = [((p.chunk_part.grad.clone(), p.chunk_part.chunk_begin) if mode and
+                                    hasattr(p, "chunk_part") else (p.shared_grad.clone(), 0)) for p in params]
+    return res
+
+
+def checkpoint(rank, world, out, args):
+    from harp_b200.models.dit import DiT, PRESETS
+    from harp_b200.trainer import ParallelState, TrainConfig, Trainer
+    from harp_b200.utils.checkpoint import latest_checkpoint, load_checkpoint, save_checkpoint
+    from harp_b200.utils.diffusion import LRSchedule
+
+    model = DiT(PRESETS["tiny"])
+    model.initialize_weights(0)
+    model = model.to(torch.bfloat16)
+    tr = Trainer(model, ParallelState.build(world), TrainConfig(lr=1e-3), "cpu")
+    lrs = LRSchedule("linear", 1e-3, num_warmup_steps=1, num_training_steps=10)
+    batch = torch.load(args["batch"])
+    tr.step(batch)
+    lrs.step()
+    save_checkpoint(args["dir"], 1, tr, lrs)
+    snap = (tr.flat.flat.clone(), tr.opt.master.clone(), tr.opt.m.clone(), tr.opt.v.clone(), lrs.lr())
+    tr.step(batch)  # move everything away from the snapshot
+    lrs.step()
+    path = latest_checkpoint(args["dir"])
+    step = load_checkpoint(path, tr, lrs)
+    now = (tr.flat.flat.clone(), tr.opt.master.clone(), tr.opt.m.clone(), tr.opt.v.clone(), lrs.lr())
+    l2 = tr.step(batch)
+    return {"step": step, "snap": snap, "now": now, "loss_after_resume": l2, "path": path}
+
+
+def rank_exit(rank, world, out, args):
+    """Rank 1 leaves between steps (nothing of its own in flight); rank 0 must
+    see its next collective fail inside the process-group timeout."""
+    from harp_b200.utils.fault import FaultInjector, Heartbeat
+
+    os.environ["HARP_FAULT_RANK"] = "1"
+    f = FaultInjector("exit@step:2", rank=rank)
+    hb = Heartbeat(dist.distributed_c10d._get_default_store(), rank, world, period_s=0.05)
+    t = torch.ones(4)
+    for step in range(4):
+        f.fire("step", step)
+        t0 = time.time()
+        try:
+            dist.all_reduce(t)
+        except Exception as e:  # noqa: BLE001 - any transport error counts as detection
+            time.sleep(0.5)
+            stale = hb.stale(0.2)
+            time.sleep(0.5)
+            stale = hb.stale(0.2)
+            hb.stop()
+            return {"failed_at": step, "elapsed": time.time() - t0, "error": type(e).__name__, "stale": stale}
+    hb.stop()
+    return {"failed_at": None}

@@ -1,0 +1,202 @@
+"""Host-side utilities: scheduler and loss weighting, learning-rate schedules,
+the .npz data format, logging / timing, fault injection, heartbeat, the wait
+and copy engines (reference test strategy: each helper checked in isolation
+against closed-form values)."""
+import json
+import math
+import os
+import threading
+import time
+
+import numpy as np
+import pytest
+import torch
+
+from harp_b200.managers import mem_manager as MM
+from harp_b200.managers import ring_attn_manager as RA
+from harp_b200.utils import data as DA
+from harp_b200.utils import diffusion as DF
+from harp_b200.utils import fault as FT
+from harp_b200.utils import observability as OB
+
+
+def test_flow_match_scheduler_shift_and_lookup(tmp_path):
+    s = DF.FlowMatchEulerDiscreteScheduler(num_train_timesteps=1000, shift=3.0)
+    t = torch.linspace(1000, 1, 1000) / 1000
+    ref = 3.0 * t / (1 + 2.0 * t)
+    torch.testing.assert_close(s.sigmas, ref)
+    torch.testing.assert_close(s.timesteps, ref * 1000)
+    idx = torch.tensor([0, 10, 999])
+    torch.testing.assert_close(s.sigmas_for(s.timesteps[idx]), s.sigmas[idx])
+    s.save_config(str(tmp_path / "scheduler"))
+    s2 = DF.FlowMatchEulerDiscreteScheduler.from_pretrained(str(tmp_path), subfolder="scheduler")
+    assert s2.config.shift == 3.0
+    torch.testing.assert_close(s2.sigmas, s.sigmas)
+    # missing config directory: defaults (the reference loads diffusers' defaults)
+    assert DF.FlowMatchEulerDiscreteScheduler.from_pretrained(str(tmp_path / "nope")).config.shift == 1.0
+
+
+def test_timestep_density_and_weighting():
+    g = torch.Generator().manual_seed(0)
+    for scheme in ("logit_normal", "mode", "none", "sigma_sqrt", "cosmap"):
+        u = DF.compute_density_for_timestep_sampling(scheme, 4096, 0.0, 1.0, 1.29, generator=g)
+        assert u.shape == (4096,) and (u >= 0).all() and (u <= 1).all(), scheme
+    u = DF.compute_density_for_timestep_sampling("logit_normal", 20000, 0.0, 1.0, generator=g)
+    assert abs(u.mean().item() - 0.5) < 0.01  # sigmoid of a symmetric normal
+    sig = torch.tensor([0.25, 0.5, 1.0])
+    torch.testing.assert_close(DF.compute_loss_weighting_for_sd3("sigma_sqrt", sig), sig ** -2.0)
+    torch.testing.assert_close(DF.compute_loss_weighting_for_sd3("cosmap", sig),
+                               2 / (math.pi * (1 - 2 * sig + 2 * sig ** 2)))
+    torch.testing.assert_close(DF.compute_loss_weighting_for_sd3("logit_normal", sig), torch.ones(3))
+
+
+@pytest.mark.parametrize("name", ["constant", "constant_with_warmup", "linear", "cosine", "cosine_with_restarts",
+                                  "polynomial"])
+def test_lr_schedules_closed_form(name):
+    W, T, base = 10, 100, 1e-3
+    sch = DF.LRSchedule(name, base, num_warmup_steps=W, num_training_steps=T)
+    lrs = []
+    for _ in range(T):
+        lrs.append(sch.lr())
+        sch.step()
+    if name != "constant":
+        assert lrs[0] == 0.0 and abs(lrs[5] - base * 0.5) < 1e-12
+    if name == "linear":
+        assert abs(lrs[55] - base * (T - 55) / (T - W)) < 1e-12
+    if name == "cosine":
+        assert abs(lrs[55] - base * 0.5 * (1 + math.cos(math.pi * 45 / 90))) < 1e-12
+    # state round trip
+    sd = sch.state_dict()
+    sch2 = DF.LRSchedule(name, base, num_warmup_steps=W, num_training_steps=T)
+    sch2.load_state_dict(sd)
+    assert sch2.lr() == sch.lr()
+
+
+def test_piecewise_constant_rules():
+    sch = DF.LRSchedule("piecewise_constant", 1.0, step_rules="1:10,0.1:20,0.01")
+    got = []
+    for _ in range(30):
+        got.append(sch.lr())
+        sch.step()
+    assert got[0] == 1.0 and got[10] == pytest.approx(0.1) and got[25] == pytest.approx(0.01)
+
+
+def test_npz_dataset_roundtrip_and_collate(tmp_path):
+    idx = DA.write_npz_samples(str(tmp_path), 3, latent_channels=4, latent_size=8, text_len=5, text_dim=6,
+                               num_metadata=4, cond_channels=3)
+    ds = DA.NpzDataset(idx)
+    assert len(ds) == 3 and ds.num_metadata == 4
+    it = ds[1]
+    assert it["latent_image"].shape == (4, 8, 8) and it["prompt_embeds"].shape == (5, 6)
+    # a path whose directories do not exist is found by name next to the index
+    with open(idx) as fh:
+        names = json.load(fh)
+    with open(idx, "w") as fh:
+        json.dump(["HARP/data/" + n for n in names], fh)
+    ds2 = DA.NpzDataset(str(tmp_path))
+    np.testing.assert_array_equal(ds2[1]["latent_image"], it["latent_image"])
+    b = DA.collate([ds[0], ds[1]])
+    assert b["latent_image"].shape == (2, 4, 8, 8)
+    assert isinstance(b["prompt_embeds"], list) and len(b["prompt_embeds"]) == 2
+    assert b["norm_metadata"].shape == (2, 4)
+    assert isinstance(b["cond"], list) and b["cond"][0].shape == (2, 3, 8, 8)
+    assert DA.custom_collate_fn is DA.collate and DA.TiffDataset is DA.NpzDataset
+
+
+def test_synthetic_data_is_deterministic():
+    a = DA.SyntheticDiTData(4, 4, 8, 5, 6, num_metadata=2, cond_channels=3, seed=7)
+    b = DA.SyntheticDiTData(4, 4, 8, 5, 6, num_metadata=2, cond_channels=3, seed=7)
+    for k in a[2]:
+        np.testing.assert_array_equal(a[2][k], b[2][k])
+    assert not np.array_equal(a[1]["latent_image"], a[2]["latent_image"])
+
+
+def test_logger_phase_timer_and_jsonl(tmp_path):
+    log = OB.setup_logger(str(tmp_path / "train.log"), True)
+    log.info("hello")
+    for h in log.handlers:
+        h.flush()
+    assert "hello" in (tmp_path / "train.log").read_text()
+    t = OB.PhaseTimer()
+    with t.phase("a"):
+        time.sleep(0.01)
+    with t.phase("a"):
+        pass
+    rep = t.report()
+    assert rep["a"] >= 9.0
+    w = OB.JsonlWriter(str(tmp_path / "m" / "metrics.jsonl"))
+    w.write({"x": 1})
+    w.write({"x": 2})
+    lines = (tmp_path / "m" / "metrics.jsonl").read_text().splitlines()
+    assert [json.loads(l)["x"] for l in lines] == [1, 2]
+    with OB.nvtx("noop"):
+        pass
+
+
+def test_fault_injector_kinds(monkeypatch):
+    f = FT.FaultInjector("raise@step:3,delay_ms@signal:20,drop@grad_sync", rank=0)
+    assert f.fire("step", 2)
+    with pytest.raises(FT.HarpInjectedFault):
+        f.fire("step", 3)
+    t0 = time.time()
+    assert f.fire("signal")
+    assert time.time() - t0 >= 0.015
+    assert f.fire("grad_sync") is False  # dropped once
+    assert f.fire("grad_sync") is True
+    monkeypatch.setenv("HARP_FAULT_RANK", "1")
+    g = FT.FaultInjector("raise@step", rank=0)
+    assert g.fire("step", 0)  # only rank 1 is faulty
+
+
+def test_heartbeat_detects_stopped_rank():
+    store = torch.distributed.HashStore()
+    hb0 = FT.Heartbeat(store, 0, 2, period_s=0.05)
+    hb1 = FT.Heartbeat(store, 1, 2, period_s=0.05)
+    time.sleep(0.2)
+    assert hb0.stale(0.15) == []
+    hb1.stop()
+    hb0.stale(0.15)
+    time.sleep(0.4)
+    assert hb0.stale(0.15) == [1]
+    hb0.stop()
+
+
+def test_wait_engine_completion_and_failure():
+    eng = RA.CPUWaitEngine()
+    try:
+        class Req:
+            def __init__(self, ok):
+                self.ok = ok
+
+            def wait(self):
+                time.sleep(0.01)
+                if not self.ok:
+                    raise RuntimeError("peer gone")
+
+        w = eng.submit(Req(True))
+        assert w.wait(timeout=5) and w.is_completed()
+        bad = eng.submit(Req(False))
+        with pytest.raises(RuntimeError):
+            bad.wait(timeout=5)
+    finally:
+        eng.shutdown()
+
+
+def test_memory_tiers_and_copy_engine_on_cpu():
+    with MM.use_hbm_allocator(False):
+        assert not MM.on_hbm()
+        with MM.use_hbm_allocator(True):
+            assert MM.on_hbm()
+        assert not MM.on_hbm()
+    x = MM.empty(4, 4, dtype=torch.float32, device="cpu")
+    assert x.shape == (4, 4)
+    eng = MM.CopyEngine.get_instance()
+    src = torch.randn(16)
+    w = eng.submit(src, to_host=True)
+    torch.testing.assert_close(w.wait(), src)
+    off = MM.HBMToDDROffloader()
+    with torch.autograd.graph.saved_tensors_hooks(off.pack_hook, off.unpack_hook):
+        a = torch.randn(8, requires_grad=True)
+        (a * a).sum().backward()
+    torch.testing.assert_close(a.grad, 2 * a.detach())
+    eng.shutdown()
