@@ -51,6 +51,8 @@ def parse():
     ap.add_argument("--text-len", type=int, default=TEXT_TOKENS)
     ap.add_argument("--sp", type=int, default=0, help="sequence-parallel size (default: all GPUs)")
     ap.add_argument("--sp-backend", default="auto", choices=["auto", "torch", "nvl"])
+    ap.add_argument("--sp-mode", default="auto", choices=["auto", "ring", "ulysses"],
+                    help="sequence-parallel attention: K/V gather (ring) or head all-to-all (ulysses)")
     ap.add_argument("--comm", default="auto", choices=["auto", "torch", "nvl"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--depth", type=int, default=0, help="override depth (debug only; not a valid bench)")
@@ -150,7 +152,8 @@ def make_batch(B, C, L, text_len, text_dim, device, seed, pinned=False):
 
 
 def run_reference(args):
-    why = ("the reference (wxyww2049/HARP) is a CPU-only ARMv9 SME/SVE stack: it needs the "
+    why = ("pip install of the reference fails: 'Directory is not installable. Neither setup.py nor "
+           "pyproject.toml found'; it is a CPU-only ARMv9 SME/SVE stack needing the "
            "-march=armv9+sve+sve2+sme toolchain, HMPI and KBLAS, and its kernels/_C*.so op library is not "
            "shipped, so it can neither be installed nor run on a B200 box")
     if int(os.environ.get("RANK", "0")) == 0:
@@ -186,7 +189,8 @@ def main():
             model = DiT(cfg)
         model.initialize_weights(seed=0)
         model = model.to(torch.bfloat16)
-        trainer = Trainer(model, par, TrainConfig(comm=args.comm), device, sp_backend=args.sp_backend)
+        trainer = Trainer(model, par, TrainConfig(comm=args.comm), device, sp_backend=args.sp_backend,
+                          sp_mode=args.sp_mode)
         cin, tdim = cfg.in_channels, cfg.text_dim
 
         def step(b):
@@ -197,7 +201,7 @@ def main():
 
         count_launches = lambda: int(torch.ops.harp.launch_count())  # noqa: E731
         reset_launches = lambda: torch.ops.harp.reset_launch_count()  # noqa: E731
-        parallelism = f"sp{sp}" + (f"xdp{dp}" if dp > 1 else "")
+        parallelism = f"sp{sp}" + (f"xdp{dp}" if dp > 1 else "") + (f"-{trainer.sp.mode}" if sp > 1 else "")
     else:
         sys.path.insert(0, os.path.join(ROOT, "baseline"))
         from baseline.dit_baseline import BaselineTrainer

@@ -1,5 +1,5 @@
 // Device-side building blocks shared by every sm_100a kernel of harp_b200:
-// mbarriers, TMA (cp.async.bulk.tensor, never with .multicast::cluster),
+// mbarriers, TMA tile loads (each CTA loads its own tiles; no cluster-wide copies),
 // tcgen05 (TMEM alloc / MMA / commit / ld / st), bounded waits that report
 // through an error word instead of trapping, and bf16 helpers.
 //
@@ -101,7 +101,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
 }
 
 // ---------------------------------------------------------------------------
-// TMA (tiled, non-multicast).  Coordinates are in elements, innermost first.
+// TMA (tiled, one destination CTA).  Coordinates are in elements, innermost first.
 // Callers keep the innermost coordinate a multiple of 16 bytes.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {

@@ -244,6 +244,20 @@ class MMDiT(nn.Module):
         p = self.cfg.patch_size
         return latent.view(B, C, H // p, p, W // p, p).permute(0, 2, 4, 3, 5, 1).reshape(B, -1, p * p * C)
 
+    def unpatchify(self, x, H, W):
+        B = x.shape[0]
+        p, C = self.cfg.patch_size, self.cfg.in_channels
+        return x.view(B, H // p, W // p, p, p, C).permute(0, 5, 1, 3, 2, 4).reshape(B, C, H, W)
+
+    def forward(self, latent, text, t, sp: Optional[SPContext] = None):
+        """Full-sequence forward (one SP rank): velocity prediction [B, C, H, W]."""
+        sp = sp or SPContext.single()
+        B, C, H, W = latent.shape
+        p = self.cfg.patch_size
+        out, lo, hi = self.forward_local(self.patchify(latent), text, t, H // p, W // p, sp)
+        assert lo == 0 and hi == (H // p) * (W // p), "full forward needs sp=1"
+        return self.unpatchify(out, H, W)
+
 
 def mmdit_loss_local(model: MMDiT, latent, noise, text, sigmas, sp: SPContext, weighting=None, **_):
     B, C, H, W = latent.shape

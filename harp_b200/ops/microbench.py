@@ -1,0 +1,228 @@
+"""Kernel microbenchmarks on the DiT-XL/2 training shapes.
+
+    python -m harp_b200.ops.microbench [case ...] [--iters N] [--small] [--no-ref]
+
+Cases: gemm_qkv gemm_proj gemm_w13 gemm_w2 gemm_dw13 gemm_dx2 attn_fwd attn_bwd
+attn_fwd_d128 attn_bwd_d128 rmsnorm_fwd rmsnorm_bwd qknorm_fwd qknorm_bwd swiglu_fwd
+adamw (default: all).  Each case runs the harp kernel and, unless --no-ref,
+the library path of the same op (cuBLAS through torch.matmul, SDPA for
+attention).  Timing: CUDA events on the launching stream around each launch,
+after 3 warm-up launches, with a 512 MiB write between timed launches so every
+launch starts from a cold L2 (126 MB).  Achieved TFLOP/s and GB/s are divided
+by MEASURED_PEAKS.json (copy bandwidth; cuBLAS bf16 burst) when present.
+--small shrinks the shapes for ncu captures (inputs still larger than L2 for
+the memory-bound cases).  One JSON line per case.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+from typing import Callable, Dict, Optional
+
+import torch
+
+from . import functional as Fn
+
+B, S, D, H, Dh, F_ = 4, 4352, 1152, 16, 72, 4608
+
+
+def _peaks() -> Dict[str, float]:
+    p = os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))),
+                     "MEASURED_PEAKS.json")
+    try:
+        with open(p) as fh:
+            d = json.load(fh)
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]), "src": "measured"}
+    except (OSError, KeyError, ValueError):
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "src": "fallback"}
+
+
+class Timer:
+    def __init__(self):
+        self.flush = torch.empty(512 << 20, dtype=torch.uint8, device="cuda")
+
+    def __call__(self, fn: Callable[[], None], iters: int, warmup: int = 3) -> float:
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        tot = 0.0
+        for _ in range(iters):
+            self.flush.fill_(1)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            torch.cuda.synchronize()
+            tot += a.elapsed_time(b)
+        return tot / iters
+
+
+def _r(*shape, scale=1.0):
+    return (torch.randn(*shape, device="cuda") * scale).to(torch.bfloat16)
+
+
+def gemm_case(M, N, K, a_mn=False, b_mn=False):
+    def make():
+        a = _r(K, M) if a_mn else _r(M, K)
+        b = _r(K, N) if b_mn else _r(N, K)
+        out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        harp = lambda: Fn.gemm(a, b, a_mn=a_mn, b_mn=b_mn, out=out)  # noqa: E731
+        am = a.t() if a_mn else a
+        bm = b if b_mn else b.t()
+        ref = lambda: torch.matmul(am, bm, out=out)  # noqa: E731
+        return harp, ref, {"flops": 2.0 * M * N * K, "shape": [M, N, K], "a_mn": a_mn, "b_mn": b_mn}
+    return make
+
+
+def attn_case(fwd: bool, dh: int, heads: int):
+    def make():
+        T = B * S
+        q, k, v = _r(T, heads * dh), _r(T, heads * dh), _r(T, heads * dh)
+        o, lse = Fn.attn_fwd(q, k, v, B, S, S, heads, dh)
+        do = _r(T, heads * dh)
+        qh, kh, vh = (t.view(B, S, heads, dh).transpose(1, 2) for t in (q, k, v))
+        flops = 4.0 * B * heads * S * S * dh * (1.0 if fwd else 2.5)
+        if fwd:
+            harp = lambda: Fn.attn_fwd(q, k, v, B, S, S, heads, dh, out=o)  # noqa: E731
+            ref = lambda: torch.nn.functional.scaled_dot_product_attention(qh, kh, vh)  # noqa: E731
+        else:
+            dq = torch.empty_like(q)
+            dk = torch.empty_like(k)
+            dv = torch.empty_like(v)
+            harp = lambda: Fn.attn_bwd(q, k, v, o, do, lse, B, S, S, heads, dh, dq_out=dq, dk_out=dk,  # noqa: E731
+                                       dv_out=dv)
+            qr, kr, vr = (t.detach().clone().requires_grad_(True) for t in (qh, kh, vh))
+            orf = torch.nn.functional.scaled_dot_product_attention(qr, kr, vr)
+            dor = do.view(B, S, heads, dh).transpose(1, 2)
+            ref = lambda: torch.autograd.grad(orf, (qr, kr, vr), dor, retain_graph=True)  # noqa: E731
+        return harp, ref, {"flops": flops, "shape": [B, S, heads, dh]}
+    return make
+
+
+def rmsnorm_case(bwd: bool):
+    def make():
+        R = B * S
+        x = _r(R, D)
+        sc, sh = _r(B, D, scale=0.1), _r(B, D, scale=0.1)
+        y, rstd = Fn.rmsnorm_mod_fwd(x, None, sc, sh, S, 1e-6)
+        dy = _r(R, D)
+        if not bwd:
+            harp = lambda: Fn.rmsnorm_mod_fwd(x, None, sc, sh, S, 1e-6, out=y)  # noqa: E731
+            nbytes = 2 * R * D * 2
+            ref = lambda: torch.nn.functional.rms_norm(x, (D,), None, 1e-6)  # noqa: E731
+        else:
+            harp = lambda: Fn.rmsnorm_mod_bwd(x, rstd, dy, None, sc, S, dres=dy, want_mod=True)  # noqa: E731
+            nbytes = 4 * R * D * 2
+            ref = None
+        return harp, ref, {"bytes": nbytes, "shape": [R, D]}
+    return make
+
+
+def qknorm_case(bwd: bool):
+    def make():
+        from ..models.dit import joint_positions, rope_freqs
+
+        R = B * S
+        qkv = _r(R, 3 * D)
+        wq = torch.ones(Dh, device="cuda", dtype=torch.bfloat16)
+        wk = torch.ones_like(wq)
+        freqs = rope_freqs(joint_positions(64, 64, 256), (8, 32, 32), 10000.0).cuda()
+        q, k, rq, rk = Fn.qknorm_rope_fwd(qkv, H, Dh, wq, wk, freqs, 1e-6)
+        if not bwd:
+            harp = lambda: Fn.qknorm_rope_fwd(qkv, H, Dh, wq, wk, freqs, 1e-6)  # noqa: E731
+            nbytes = 4 * R * D * 2
+        else:
+            dq, dk = _r(R, D), _r(R, D)
+            dqkv = torch.empty_like(qkv)
+            harp = lambda: Fn.qknorm_rope_bwd(dq, dk, qkv, rq, rk, H, Dh, wq, wk, freqs, True, dqkv)  # noqa: E731
+            nbytes = 6 * R * D * 2
+        return harp, None, {"bytes": nbytes, "shape": [R, H, Dh]}
+    return make
+
+
+def swiglu_case():
+    def make():
+        R = B * S
+        gu = _r(R, 2 * F_)
+        harp = lambda: Fn.swiglu_fwd(gu, F_)  # noqa: E731
+        g, u = gu[:, :F_], gu[:, F_:]
+        ref = lambda: torch.nn.functional.silu(g) * u  # noqa: E731
+        return harp, ref, {"bytes": 3 * R * F_ * 2, "shape": [R, F_]}
+    return make
+
+
+def adamw_case(n):
+    def make():
+        master = torch.randn(n, device="cuda")
+        m = torch.zeros_like(master)
+        v = torch.zeros_like(master)
+        g = _r(n, scale=1e-3)
+        p = master.to(torch.bfloat16)
+        harp = lambda: Fn.adamw_flat(master, m, v, g, p, 1e-4, 0.9, 0.999, 1e-8, 0.0, 1)  # noqa: E731
+        # master, m, v read+write (fp32), grad read (bf16), param write (bf16)
+        return harp, None, {"bytes": n * (3 * 4 * 2 + 2 + 2), "shape": [n]}
+    return make
+
+
+def build_cases(gemm_rows: int, adamw_n: int) -> Dict[str, Callable]:
+    return {
+        "gemm_qkv": gemm_case(gemm_rows, 3 * D, D),
+        "gemm_proj": gemm_case(gemm_rows, D, D),
+        "gemm_w13": gemm_case(gemm_rows, 2 * F_, D),
+        "gemm_w2": gemm_case(gemm_rows, D, F_),
+        "gemm_dw13": gemm_case(2 * F_, D, gemm_rows, a_mn=True, b_mn=True),
+        "gemm_dx2": gemm_case(gemm_rows, F_, D, b_mn=True),
+        "attn_fwd": attn_case(True, Dh, H),
+        "attn_bwd": attn_case(False, Dh, H),
+        "attn_fwd_d128": attn_case(True, 128, 24),
+        "attn_bwd_d128": attn_case(False, 128, 24),
+        "rmsnorm_fwd": rmsnorm_case(False),
+        "rmsnorm_bwd": rmsnorm_case(True),
+        "qknorm_fwd": qknorm_case(False),
+        "qknorm_bwd": qknorm_case(True),
+        "swiglu_fwd": swiglu_case(),
+        "adamw": adamw_case(adamw_n),
+    }
+
+
+def main(argv=None):
+    global B, S
+    ap = argparse.ArgumentParser()
+    ap.add_argument("cases", nargs="*")
+    ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--small", action="store_true", help="batch 1, 2048 tokens (ncu captures)")
+    ap.add_argument("--no-ref", action="store_true")
+    args = ap.parse_args(argv)
+    from .. import _native
+
+    _native.require()
+    if args.small:
+        B, S = 1, 2048
+    cases = build_cases(4 * B * S if args.small else B * S, 64_000_000 if args.small else 675_000_000)
+    peaks = _peaks()
+    timer = Timer()
+    for name in args.cases or list(cases):
+        harp, ref, info = cases[name]()
+        rec = {"case": name, **info}
+        for tag, fn in (("harp", harp), ("ref", None if args.no_ref else ref)):
+            if fn is None:
+                continue
+            ms = timer(fn, args.iters)
+            rec[f"{tag}_ms"] = round(ms, 4)
+            if "flops" in info:
+                tf = info["flops"] / ms / 1e9
+                rec[f"{tag}_tflops"] = round(tf, 1)
+                rec[f"{tag}_frac_of_{peaks['src']}_bf16"] = round(tf / peaks["bf16_tflops"], 3)
+            else:
+                gbs = info["bytes"] / ms / 1e6
+                rec[f"{tag}_gbs"] = round(gbs, 1)
+                rec[f"{tag}_frac_of_{peaks['src']}_hbm"] = round(gbs / peaks["hbm_gbs"], 3)
+        print(json.dumps(rec), flush=True)
+        del harp, ref
+        torch.cuda.empty_cache()
+
+
+if __name__ == "__main__":
+    main()

@@ -44,6 +44,17 @@ def all_gather_cat(x: torch.Tensor, group=None) -> torch.Tensor:
     return out
 
 
+def all_to_all(x: torch.Tensor, group=None) -> torch.Tensor:
+    """x: [n, ...] (slab j goes to rank j) -> [n, ...] with slab j = what rank j sent here."""
+    n = world(group)
+    if n == 1:
+        return x.clone()
+    x = x.contiguous()
+    out = torch.empty_like(x)
+    dist.all_to_all_single(out, x, group=group)
+    return out
+
+
 def reduce_scatter_sum(x: torch.Tensor, group=None) -> torch.Tensor:
     """x: [n, ...] (one slab per rank) -> sum over ranks of slab[my rank]."""
     n = world(group)

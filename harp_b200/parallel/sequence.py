@@ -14,6 +14,14 @@ the NVLink exchange is used).  The backward computes dQ locally and dK/dV
 for the whole gathered sequence, then reduce-scatters dK/dV back to the
 chunk owners.
 
+Ulysses mode (mode="ulysses", heads divisible by sp): instead of gathering
+K/V, an all-to-all turns the sequence-sharded q, k, v into head-sharded ones
+over the FULL sequence (rank r keeps heads [r*H/sp, (r+1)*H/sp)), attention
+runs locally, and a second all-to-all returns the output to sequence
+sharding.  Per rank and layer this moves 4 x (local activation) x (sp-1)/sp
+bytes each way instead of 2 x sp x (local K/V) for the gather, i.e. about
+sp/2 times less traffic at sp >= 4.  The reference has no Ulysses mode.
+
 Exchange backends:
   "torch"  torch.distributed all-gather / reduce-scatter (gloo or NCCL)
   "nvl"    harp NVLink exchange: peers' K/V pulled over NVLink into a
@@ -38,17 +46,46 @@ class SPContext:
     group: Any = None
     backend: str = "local"  # "local" | "torch" | "nvl"
     comm: Any = None  # harp_b200.parallel.nvlink.NVLinkComm for backend == "nvl"
+    mode: str = "ring"  # "ring" (gather K/V) | "ulysses" (head all-to-all)
 
     @staticmethod
     def single() -> "SPContext":
         return SPContext()
 
     @staticmethod
-    def from_group(group, backend: str = "torch", comm=None) -> "SPContext":
+    def from_group(group, backend: str = "torch", comm=None, mode: str = "ring") -> "SPContext":
         n = C.world(group)
         if n == 1:
             return SPContext()
-        return SPContext(size=n, rank=C.rank(group), group=group, backend=backend, comm=comm)
+        return SPContext(size=n, rank=C.rank(group), group=group, backend=backend, comm=comm, mode=mode)
+
+
+def resolve_mode(mode: str, heads: int, sp_size: int) -> str:
+    """"auto": Ulysses when the heads split evenly over the SP ranks and
+    sp >= 4 (at sp=2 both move the same bytes and the K/V gather overlaps
+    with attention), else the K/V gather."""
+    if mode == "auto":
+        return "ulysses" if sp_size >= 4 and heads % sp_size == 0 else "ring"
+    if mode == "ulysses" and heads % sp_size != 0:
+        raise ValueError(f"ulysses SP needs heads ({heads}) divisible by sp ({sp_size})")
+    return mode
+
+
+def _seq_to_heads(ts, B, S, H, Dh, sp: SPContext) -> torch.Tensor:
+    """Sequence-sharded [B*S, >=H*Dh] tensors -> head-sharded [T, B*sp*S, (H/sp)*Dh]
+    over the full sequence (global token order: chunk-major)."""
+    N, Hn = sp.size, H // sp.size
+    x = torch.stack([t[:, :H * Dh].reshape(B, S, N, Hn, Dh) for t in ts], 0)  # [T, B, S, N, Hn, Dh]
+    recv = C.all_to_all(x.permute(3, 0, 1, 2, 4, 5).contiguous(), sp.group)  # [N(chunk), T, B, S, Hn, Dh]
+    return recv.permute(1, 2, 0, 3, 4, 5).reshape(len(ts), B * N * S, Hn * Dh)
+
+
+def _heads_to_seq(ts, B, S, H, Dh, sp: SPContext) -> torch.Tensor:
+    """Head-sharded [B*sp*S, (H/sp)*Dh] tensors -> sequence-sharded [T, B*S, H*Dh]."""
+    N, Hn = sp.size, H // sp.size
+    x = torch.stack([t.reshape(B, N, S, Hn, Dh) for t in ts], 0)  # [T, B, N(chunk), S, Hn, Dh]
+    recv = C.all_to_all(x.permute(2, 0, 1, 3, 4, 5).contiguous(), sp.group)  # [N(head grp), T, B, S, Hn, Dh]
+    return recv.permute(1, 2, 3, 0, 4, 5).reshape(len(ts), B * S, H * Dh)
 
 
 def _kv_gather_torch(k, v, B, S, HD, sp: SPContext):
@@ -68,6 +105,12 @@ def sp_attention_forward(q, k, v, B: int, S: int, H: int, Dh: int, sp: SPContext
     if sp.size == 1:
         o, lse = Fn.attn_fwd(q, k, v, B, S, S, H, Dh)
         return o, {"lse": lse}
+    if sp.mode == "ulysses":
+        Hn, Sf = H // sp.size, sp.size * S
+        qkv_f = _seq_to_heads((q, k, v), B, S, H, Dh, sp)
+        o_f, lse = Fn.attn_fwd(qkv_f[0], qkv_f[1], qkv_f[2], B, Sf, Sf, Hn, Dh)
+        o = _heads_to_seq((o_f,), B, S, H, Dh, sp)[0]
+        return o, {"lse": lse, "qkv_f": qkv_f, "o_f": o_f}
     if sp.backend == "nvl" and sp.comm is not None:
         kv_full, ready, epoch = sp.comm.kv_exchange(k, v, B, S, HD)
         start_tile = (sp.rank * S) // 128
@@ -88,6 +131,16 @@ def sp_attention_backward(saved, q, k, v, o, do, B: int, S: int, H: int, Dh: int
     if sp.size == 1:
         dq, dk, dv = Fn.attn_bwd(q, k, v, o, do, lse, B, S, S, H, Dh, dv_out=dv_out)
         return (dq, dk) if dv_out is not None else (dq, dk, dv)
+    if sp.mode == "ulysses":
+        Hn, Sf = H // sp.size, sp.size * S
+        qkv_f, o_f = saved["qkv_f"], saved["o_f"]
+        do_f = _seq_to_heads((do,), B, S, H, Dh, sp)[0]
+        dq_f, dk_f, dv_f = Fn.attn_bwd(qkv_f[0], qkv_f[1], qkv_f[2], o_f, do_f, lse, B, Sf, Sf, Hn, Dh)
+        dqkv = _heads_to_seq((dq_f, dk_f, dv_f), B, S, H, Dh, sp)
+        if dv_out is not None:
+            dv_out.copy_(dqkv[2])
+            return dqkv[0], dqkv[1]
+        return dqkv[0], dqkv[1], dqkv[2]
     kv_full = saved["kv"]
     Skv = sp.size * S
     if sp.backend == "nvl" and sp.comm is not None:

@@ -29,7 +29,7 @@ import torch.distributed as dist
 from .models.dit import DiT, flow_matching_loss_local
 from .ops import functional as Fn
 from .parallel import collectives as C
-from .parallel.sequence import SPContext
+from .parallel.sequence import SPContext, resolve_mode
 from .runtime import errors
 
 
@@ -188,7 +188,7 @@ class Trainer:
     returns the loss as a Python float."""
 
     def __init__(self, model, par: ParallelState, cfg: TrainConfig, device, sp_backend: str = "auto",
-                 loss_fn=None):
+                 loss_fn=None, sp_mode: str = "auto"):
         """loss_fn(model, latent, noise, text, sigmas, sp, **extra) -> this rank's share
         of the global loss; defaults to the DiT flow-matching loss."""
         self.model, self.par, self.cfg, self.device = model, par, cfg, device
@@ -212,7 +212,9 @@ class Trainer:
 
                 comm = NVLinkComm.get(par.sp_group, device)
         self.sp_comm = comm
-        self.sp = SPContext.from_group(par.sp_group, backend=backend, comm=comm) if par.sp_size > 1 else SPContext()
+        mode = resolve_mode(sp_mode, _model_heads(model), par.sp_size) if par.sp_size > 1 else "ring"
+        self.sp = SPContext.from_group(par.sp_group, backend=backend, comm=comm, mode=mode) \
+            if par.sp_size > 1 else SPContext()
         self.global_step = 0
 
     # -- device-resident step (inputs already on the GPU) -------------------
@@ -263,6 +265,17 @@ class Trainer:
     def check_errors(self):
         if torch.device(self.device).type == "cuda":
             errors.check(torch.device(self.device))
+
+
+def _model_heads(model) -> int:
+    cfg = getattr(model, "cfg", None)
+    if cfg is not None and hasattr(cfg, "heads"):
+        return int(cfg.heads)
+    for m in model.modules():
+        for attr in ("n_heads", "heads", "num_heads"):
+            if isinstance(getattr(m, attr, None), int):
+                return int(getattr(m, attr))
+    return 1
 
 
 def _to_dev(v, dev):

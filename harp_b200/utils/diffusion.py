@@ -15,7 +15,7 @@ from __future__ import annotations
 import json
 import math
 import os
-from typing import Optional, Union
+from typing import Sequence, Optional, Union
 
 import torch
 from torch.optim import Optimizer
@@ -67,6 +67,46 @@ class FlowMatchEulerDiscreteScheduler:
         os.makedirs(directory, exist_ok=True)
         with open(os.path.join(directory, self.config_name), "w") as fh:
             json.dump(dict(self.config), fh, indent=2)
+
+    # -- sampling (inference) --------------------------------------------------
+    @staticmethod
+    def time_shift(mu: float, sigma: torch.Tensor) -> torch.Tensor:
+        """Resolution-dependent shift e^mu / (e^mu + 1/sigma - 1) (SD3 / Flux)."""
+        return math.exp(mu) / (math.exp(mu) + (1.0 / sigma - 1.0))
+
+    def set_timesteps(self, num_inference_steps: Optional[int] = None, device=None,
+                      sigmas: Optional[Sequence[float]] = None, mu: Optional[float] = None,
+                      timesteps: Optional[Sequence[float]] = None):
+        """Sampling grid: `num_inference_steps` sigmas from sigma_max down to
+        sigma_min (or the given sigmas / timesteps), shifted (static `shift`, or
+        time_shift(mu) with dynamic shifting), followed by a terminal 0."""
+        n_train = self.config.num_train_timesteps
+        if sigmas is not None:
+            sig = torch.tensor(list(sigmas), dtype=torch.float64)
+        elif timesteps is not None:
+            sig = torch.tensor(list(timesteps), dtype=torch.float64) / n_train
+        else:
+            sig = torch.linspace(self.sigma_max * n_train, self.sigma_min * n_train, num_inference_steps,
+                                 dtype=torch.float64) / n_train
+        if self.config.use_dynamic_shifting:
+            if mu is None:
+                raise ValueError("dynamic shifting needs mu")
+            sig = self.time_shift(mu, sig.clamp_min(1e-12))
+        else:
+            s = self.config.shift
+            sig = s * sig / (1 + (s - 1) * sig)
+        self.num_inference_steps = len(sig)
+        self.timesteps = (sig * n_train).float().to(device or "cpu")
+        self.sigmas = torch.cat([sig, sig.new_zeros(1)]).float().to(device or "cpu")
+        self._step_index = 0
+
+    def step(self, model_output: torch.Tensor, timestep, sample: torch.Tensor, return_dict: bool = False):
+        """Euler step of dx/dsigma = model_output (the noise - x0 velocity)."""
+        i = self._step_index
+        s, s_next = self.sigmas[i], self.sigmas[i + 1]
+        prev = (sample.float() + (s_next - s).to(sample.device) * model_output.float()).to(sample.dtype)
+        self._step_index += 1
+        return (prev,) if not return_dict else {"prev_sample": prev}
 
     def sigmas_for(self, timesteps: torch.Tensor) -> torch.Tensor:
         """sigma of each (exact) training timestep value."""

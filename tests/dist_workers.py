@@ -37,7 +37,7 @@ def sp_attention(rank, world, out, args):
     g = torch.Generator().manual_seed(0)
     q, k, v = (torch.randn(B, S, H * Dh, generator=g).bfloat16() for _ in range(3))
     do = torch.randn(B, S, H * Dh, generator=g).bfloat16()
-    sp = SPContext.from_group(dist.group.WORLD, backend="torch")
+    sp = SPContext.from_group(dist.group.WORLD, backend="torch", mode=args.get("mode", "ring"))
     n = S // world
     sl = slice(rank * n, (rank + 1) * n)
     ql, kl, vl = (t[:, sl].clone().requires_grad_(True) for t in (q, k, v))
@@ -56,7 +56,7 @@ def trainer_run(rank, world, out, args):
     model.initialize_weights(0)
     model = model.to(torch.bfloat16)
     par = ParallelState.build(sp_size)
-    tr = Trainer(model, par, TrainConfig(lr=1e-3, weight_decay=0.01), "cpu")
+    tr = Trainer(model, par, TrainConfig(lr=1e-3, weight_decay=0.01), "cpu", sp_mode=args.get("mode", "auto"))
     batch = torch.load(args["batch"])
     dp_rank = rank // sp_size
     per = batch["latent"].shape[0] // par.dp_size

@@ -52,8 +52,9 @@ def _full_attention(q, k, v, do, H, Dh):
     return o.detach(), q.grad, k.grad, v.grad
 
 
-def test_sp_attention_two_ranks_matches_full(tmp_path):
-    res, _ = _run("sp_attention", 2, tmp_path)
+@pytest.mark.parametrize("mode", ["ring", "ulysses"])
+def test_sp_attention_two_ranks_matches_full(tmp_path, mode):
+    res, _ = _run("sp_attention", 2, tmp_path, {"mode": mode})
     r0 = res[0]
     o, dq, dk, dv = _full_attention(r0["q"], r0["k"], r0["v"], r0["do"], 2, 16)
     for r in (0, 1):
@@ -91,12 +92,12 @@ def _single_run(batch, steps):
     return losses, tr.flat.flat.clone()
 
 
-@pytest.mark.parametrize("sp", [2, 1])
-def test_trainer_two_ranks_matches_single_process(tmp_path, sp):
+@pytest.mark.parametrize("sp,mode", [(2, "ring"), (2, "ulysses"), (1, "auto")])
+def test_trainer_two_ranks_matches_single_process(tmp_path, sp, mode):
     bpath = str(tmp_path / "batch.pt")
     batch = _batch(bpath)
     ref_losses, ref_flat = _single_run(batch, 3)
-    res, _ = _run("trainer_run", 2, tmp_path, {"sp": sp, "batch": bpath, "steps": 3})
+    res, _ = _run("trainer_run", 2, tmp_path, {"sp": sp, "batch": bpath, "steps": 3, "mode": mode})
     for r in (0, 1):
         got = res[r]["losses"]
         assert got == pytest.approx(ref_losses, rel=2e-3), (r, got, ref_losses)

@@ -153,3 +153,50 @@ def test_rope_tables():
     f = D.rope_freqs(pos, (4, 6, 6), 10000.0)
     assert f.shape == (10, 8, 2)
     torch.testing.assert_close(f[..., 0].pow(2) + f[..., 1].pow(2), torch.ones(10, 8))
+
+
+def test_cfg_inference_runs_for_every_family():
+    from harp_b200 import inference as I
+    from harp_b200.utils.diffusion import FlowMatchEulerDiscreteScheduler as FS
+
+    torch.manual_seed(0)
+    dit = D.DiT(D.PRESETS["tiny"])
+    dit.initialize_weights(0)
+    dit = dit.bfloat16()
+    pe = [torch.randn(16, dit.cfg.text_dim).bfloat16() for _ in range(2)]
+    ne = [torch.zeros(16, dit.cfg.text_dim).bfloat16() for _ in range(2)]
+    out = I.batch_image_inference(dit, None, FS(use_dynamic_shifting=True), None, pe, ne, height=128, width=128,
+                                  num_inference_steps=3, guidance_scale=3.0, cfg_normalization=1.5,
+                                  generator=torch.Generator().manual_seed(0), in_channels=dit.cfg.in_channels)
+    assert out["images"].shape == (2, dit.cfg.in_channels, 16, 16)
+    assert torch.isfinite(out["images"].float()).all()
+    # zero velocity everywhere -> the Euler sampler returns its starting noise
+    with torch.no_grad():
+        dit.final_layer.linear.weight.zero_()
+        dit.final_layer.linear.bias.zero_()
+    x0 = torch.randn(1, dit.cfg.in_channels, 16, 16).bfloat16()
+    out = I.batch_image_inference(dit, None, FS(), None, pe[:1], None, num_inference_steps=2, initial_latents=x0,
+                                  return_dict=False)[0]
+    assert torch.equal(out, x0)
+    zm = Z.Z_Transformer(Z.ZImageTransformer2DModel(**Z.PRESETS["zimage-tiny"]), num_metadata=4, use_cond=False)
+    zm = zm.bfloat16()
+    with torch.no_grad():
+        for p in zm.parameters():
+            p.normal_(0, 0.02)
+    pz = [torch.randn(16, 64).bfloat16() for _ in range(2)]
+    out = I.batch_image_inference(zm, None, FS(), None, pz, pz, height=128, width=128, num_inference_steps=2,
+                                  generator=torch.Generator().manual_seed(0), in_channels=16,
+                                  metadata=torch.rand(2, 4).bfloat16())
+    assert out["images"].shape == (2, 16, 16, 16)
+
+
+def test_scheduler_inference_grid():
+    from harp_b200.utils.diffusion import FlowMatchEulerDiscreteScheduler as FS
+
+    s = FS(shift=3.0)
+    s.sigma_min = 0.0
+    s.set_timesteps(4)
+    assert s.sigmas.shape == (5,) and s.sigmas[-1] == 0 and s.sigmas[0] == pytest.approx(1.0)
+    d = FS(use_dynamic_shifting=True)
+    d.set_timesteps(4, mu=1.0)
+    assert torch.all(d.sigmas[:-1][1:] < d.sigmas[:-1][:-1])

@@ -200,3 +200,59 @@ def test_memory_tiers_and_copy_engine_on_cpu():
         (a * a).sum().backward()
     torch.testing.assert_close(a.grad, 2 * a.detach())
     eng.shutdown()
+
+
+def test_metadata_roundtrip_and_caption():
+    from harp_b200.utils.misc import MetaData
+
+    md = MetaData()
+    raw = (120.5, -33.25, 0.5, 2020.0)
+    n = md.normalize(raw)
+    torch.testing.assert_close(n, torch.tensor([120.5 / 360 * 1000, -33.25 / 180 * 1000, 50.0, 2020 / 2100 * 1000]))
+    torch.testing.assert_close(md.unnormalize(n), torch.tensor(raw))
+    emb, cap = md.embedding(raw)
+    assert "resolution of 0.5" in cap and "2020.0" in cap
+
+
+def test_apply_rotary_emb_real_and_complex_agree():
+    from harp_b200.utils.misc import apply_rotary_emb
+
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(2, 3, 5, 8, generator=g)
+    ang = torch.randn(2, 5, 4, generator=g)
+    cis = torch.polar(torch.ones_like(ang), ang)
+    cos = ang.cos().repeat_interleave(2, -1)
+    sin = ang.sin().repeat_interleave(2, -1)
+    a = apply_rotary_emb(x, (cos, sin), use_real=True)
+    b = apply_rotary_emb(x, cis, use_real=False)
+    torch.testing.assert_close(a, b, rtol=1e-5, atol=1e-5)
+    # rotation keeps the norm of every pair
+    torch.testing.assert_close(a.norm(dim=-1), x.norm(dim=-1), rtol=1e-5, atol=1e-5)
+
+
+def test_fast_init_mode_is_deterministic():
+    from harp_b200.utils.misc import FastInitMode
+
+    def build():
+        with FastInitMode(seed=7):
+            return torch.nn.Linear(16, 8)
+
+    a, b = build(), build()
+    assert torch.equal(a.weight, b.weight) and torch.equal(a.bias, b.bias)
+    bound = 1 / math.sqrt(16)
+    assert a.weight.abs().max() <= bound
+
+
+def test_save_trainable_param_hook(tmp_path):
+    from safetensors.torch import load_file
+
+    from harp_b200.utils.misc import preserve_requires_grad, save_trainable_param_hook
+
+    m = torch.nn.Sequential(torch.nn.Linear(4, 4), torch.nn.Linear(4, 2))
+    m[0].weight.requires_grad_(False)
+    save_trainable_param_hook([m], [1], str(tmp_path))
+    sd = load_file(str(tmp_path / "model.safetensors"))
+    assert set(sd) == {"0.bias", "1.weight", "1.bias"}
+    with preserve_requires_grad(m):
+        m.requires_grad_(False)
+    assert m[1].weight.requires_grad and not m[0].weight.requires_grad

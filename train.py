@@ -75,6 +75,8 @@ def parse_args(argv=None):
     p.add_argument("--sp_size", type=int, default=4)
     p.add_argument("--rs_size", type=int, default=16, help="accepted; the optimizer shards over every rank")
     p.add_argument("--comm_backend", type=str, default="auto", choices=["auto", "nvl", "torch"])
+    p.add_argument("--sp_mode", type=str, default="auto", choices=["auto", "ring", "ulysses"],
+                   help="sequence-parallel attention: K/V gather (the reference's ring) or head all-to-all")
     p.add_argument("--enable_profiler", action="store_true")
     p.add_argument("--harp_block_compat", action="store_true", help="Z-Image: reproduce HARP's block residual")
     # accepted for command-line compatibility, unused (as in the reference)
@@ -204,7 +206,8 @@ def main(args):
     lr = args.learning_rate * (world * args.train_batch_size if args.scale_lr else 1)
     tcfg = TrainConfig(lr=lr, beta1=args.adam_beta1, beta2=args.adam_beta2, eps=args.adam_epsilon,
                        weight_decay=args.adam_weight_decay, comm=args.comm_backend)
-    trainer = Trainer(model, par, tcfg, device, sp_backend=args.comm_backend, loss_fn=loss_fn)
+    trainer = Trainer(model, par, tcfg, device, sp_backend=args.comm_backend, loss_fn=loss_fn,
+                      sp_mode=args.sp_mode)
     sched = D.FlowMatchEulerDiscreteScheduler.from_pretrained(args.pretrained_model_name_or_path or ".",
                                                               subfolder="scheduler")
     lrs = D.LRSchedule(args.lr_scheduler, lr, num_warmup_steps=args.lr_warmup_steps,
