@@ -32,6 +32,8 @@ SOURCES = [
     "comm.cu",
     "runtime.cpp",
     "noalloc_rmsnorm.cu",
+    "alloc.cpp",
+    "ulysses.cu",
 ]
 CUDA_FLAGS = [
     "-gencode",

@@ -103,6 +103,8 @@ struct FwdArgs {
   int chunk_len;
   int start_tile;
   unsigned int epoch;
+  int wait_q;  // queries arrive by chunk too (same flags): wait before loading a Q tile
+  int q_rot;   // query-pair index rotation (start with the pairs whose chunk is local)
   unsigned long long timeout_ns;
   int* err;
 };
@@ -140,7 +142,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int nqp = (a.Sq + 255) / 256;
-  const int bh = blockIdx.x / nqp, qp = blockIdx.x % nqp;
+  // Queries that arrive by chunk: query-pair-major order starting at q_rot, so
+  // the first wave works on pairs that are already here.  Else (b, h)-major,
+  // which keeps one (b, h)'s keys shared by neighbouring CTAs in L2.
+  const int nbh = a.B * a.H;
+  const int bh = a.wait_q ? (int)(blockIdx.x % nbh) : (int)(blockIdx.x / nqp);
+  const int qp = a.wait_q ? (int)((blockIdx.x / nbh + a.q_rot) % nqp) : (int)(blockIdx.x % nqp);
   const int b = bh / a.H, h = bh % a.H;
   const int q0 = qp * 256;
   const int ntile = (q0 + 128 < a.Sq) ? 2 : 1;
@@ -178,6 +185,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       tma_prefetch_desc(&tmV);
       int issued_k[4] = {0, 0, 0, 0}, issued_v[4] = {0, 0, 0, 0};
       bool ok = true;
+      if (a.ready != nullptr && a.wait_q) {
+        const int qend = min(q0 + 128 * ntile, a.Sq) - 1;
+        for (int c = q0 / a.chunk_len; c <= qend / a.chunk_len && ok; ++c)
+          ok = wait_flag_geq(a.ready + c, a.epoch, a.timeout_ns, err, 19);
+        fence_proxy_async_global();
+      }
       mbar_arrive_expect_tx(q_full, ntile * C::TILE);
       for (int t = 0; t < ntile; ++t)
 #pragma unroll
@@ -780,7 +793,7 @@ void launch_bwd(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap&
 void attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, int64_t B, int64_t Sq, int64_t Skv,
               int64_t H, int64_t Dh, double scale, at::Tensor& o, at::Tensor& lse,
               const c10::optional<at::Tensor>& ready, int64_t chunk_len, int64_t start_tile, int64_t epoch,
-              double timeout_s, at::Tensor& err) {
+              double timeout_s, at::Tensor& err, int64_t q_rot, bool wait_q) {
   TORCH_CHECK(q.is_cuda() && k.is_cuda() && v.is_cuda() && o.is_cuda(), "attn_fwd: CUDA tensors");
   TORCH_CHECK(q.scalar_type() == at::kBFloat16 && k.scalar_type() == at::kBFloat16 &&
                   v.scalar_type() == at::kBFloat16 && o.scalar_type() == at::kBFloat16,
@@ -806,6 +819,8 @@ void attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, int
   args.chunk_len = chunk_len > 0 ? (int)chunk_len : (int)Skv;
   args.start_tile = (int)start_tile;
   args.epoch = (unsigned int)epoch;
+  args.wait_q = (wait_q && args.ready != nullptr) ? 1 : 0;
+  args.q_rot = (int)(q_rot % ((Sq + 255) / 256));
   args.timeout_ns = (unsigned long long)(timeout_s * 1e9);
   args.err = err.data_ptr<int>();
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
@@ -875,7 +890,8 @@ void dq_finalize(const at::Tensor& acc, int64_t H, int64_t Dh, double scale, at:
 
 TORCH_LIBRARY_FRAGMENT(harp, m) {
   m.def("attn_fwd(Tensor q, Tensor k, Tensor v, int B, int Sq, int Skv, int H, int Dh, float scale, Tensor(a!) o, "
-        "Tensor(b!) lse, Tensor? ready, int chunk_len, int start_tile, int epoch, float timeout_s, Tensor(c!) err) -> ()");
+        "Tensor(b!) lse, Tensor? ready, int chunk_len, int start_tile, int epoch, float timeout_s, Tensor(c!) err, "
+        "int q_rot=0, bool wait_q=False) -> ()");
   m.def("attn_bwd(Tensor q, Tensor k, Tensor v, Tensor dout, Tensor lse, Tensor delta, int B, int Sq, int Skv, "
         "int H, int Dh, float scale, Tensor(a!) dq_acc, Tensor(b!) dk, Tensor(c!) dv, Tensor(d!) err) -> ()");
   m.def("dq_finalize(Tensor acc, int H, int Dh, float scale, Tensor(a!) out) -> ()");

@@ -21,6 +21,7 @@
 //     every peer's parameter buffer with 16-byte stores.
 #include "common.cuh"
 #include "gemm_sm100.h"
+#include "peer.cuh"
 
 #include <ATen/ATen.h>
 #include <ATen/cuda/CUDAContext.h>
@@ -36,7 +37,6 @@ namespace comm {
 namespace {
 
 using bf16 = __nv_bfloat16;
-constexpr int kMaxPeers = 8;
 
 struct Segment {
   void* ptr = nullptr;
@@ -50,9 +50,6 @@ std::unordered_map<int64_t, Segment> g_segments;
 // ---------------------------------------------------------------------------
 // kernels
 // ---------------------------------------------------------------------------
-struct PeerTable {
-  uint64_t base[kMaxPeers];  // segment base address of each rank (own included)
-};
 
 // flags[slot] on every peer (except `skip`) <- value, release at system scope.
 __global__ void signal_kernel(PeerTable flags, int world, int slot, unsigned int value, int skip) {
@@ -207,18 +204,6 @@ __global__ void rs_adamw_ag_kernel(PeerTable grads, PeerTable params, long long 
   __threadfence_system();
 }
 
-PeerTable make_table(const std::vector<int64_t>& ptrs, long long offset) {
-  TORCH_CHECK(ptrs.size() <= kMaxPeers, "harp_comm: at most ", kMaxPeers, " ranks per group");
-  PeerTable t;
-  for (int i = 0; i < kMaxPeers; ++i) t.base[i] = 0;
-  for (size_t i = 0; i < ptrs.size(); ++i) t.base[i] = (uint64_t)ptrs[i] + offset;
-  return t;
-}
-
-int grid_for(long long work, int threads) {
-  const long long want = (work + threads - 1) / threads;
-  return (int)std::max<long long>(1, std::min<long long>(want, (long long)num_sms() * 4));
-}
 
 }  // namespace
 

@@ -13,6 +13,7 @@
 // backward produces d(scale), d(shift) and d(w) as deterministic per-block
 // partial sums reduced by `reduce_partials`; QK-RMSNorm and RoPE are one pass.
 #include "common.cuh"
+#include "norm_rope.cuh"
 #include "gemm_sm100.h"
 
 #include <ATen/ATen.h>
@@ -38,11 +39,6 @@ __device__ __forceinline__ void store8(bf16* p, const float (&f)[8]) {
   v.z = pack_bf16x2(f[4], f[5]);
   v.w = pack_bf16x2(f[6], f[7]);
   *reinterpret_cast<uint4*>(p) = v;
-}
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
 }
 __device__ __forceinline__ float sigmoidf_(float x) { return 1.f / (1.f + __expf(-x)); }
 
@@ -211,45 +207,6 @@ __global__ void reduce_partials_kernel(const float* __restrict__ part, int nrows
 // qkv: [R, ld] with q at col 0, k at col H*Dh.  freqs: float2 (cos, sin)
 // [freq_rows, Dh/2]; row r uses freqs[r % freq_rows].  One warp per (row, head).
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void norm_rope_one(const bf16* __restrict__ src, const bf16* __restrict__ w,
-                                              const float2* __restrict__ fr, int Dh, float eps, bf16* __restrict__ dst,
-                                              float* rstd_out, int lane) {
-  const int P = Dh / 2;
-  float2 v[4];
-  float ss = 0.f;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int p = lane + 32 * i;
-    if (p < P) {
-      v[i] = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(src + 2 * p));
-      ss += v[i].x * v[i].x + v[i].y * v[i].y;
-    }
-  }
-  ss = warp_sum(ss);
-  const float rs = rsqrtf(ss / Dh + eps);
-  if (lane == 0 && rstd_out) *rstd_out = rs;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int p = lane + 32 * i;
-    if (p < P) {
-      float a = v[i].x * rs, b = v[i].y * rs;
-      if (w) {
-        float2 wf = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(w + 2 * p));
-        a *= wf.x;
-        b *= wf.y;
-      }
-      if (fr) {
-        const float2 cs = fr[p];
-        const float o0 = a * cs.x - b * cs.y;
-        const float o1 = a * cs.y + b * cs.x;
-        a = o0;
-        b = o1;
-      }
-      *reinterpret_cast<uint32_t*>(dst + 2 * p) = pack_bf16x2(a, b);
-    }
-  }
-}
-
 __global__ void qknorm_rope_fwd_kernel(const bf16* __restrict__ qkv, long ld, int R, int H, int Dh,
                                        const bf16* __restrict__ wq, const bf16* __restrict__ wk,
                                        const float2* __restrict__ freqs, int freq_rows, float eps, int do_norm,

@@ -33,22 +33,46 @@ def on_hbm() -> bool:
     return getattr(_tls, "hbm", True)
 
 
+def _native_ready() -> bool:
+    if not torch.cuda.is_available():
+        return False
+    from .. import _native
+
+    return _native.available()
+
+
 @contextmanager
 def use_hbm_allocator(state: bool = True):
+    """state=False: cuda tensors created inside the block live in pinned,
+    device-mapped host memory (the native allocator's host tier); True: the
+    default device memory.  The flag is per thread, as the reference's."""
     prev = on_hbm()
     _tls.hbm = state
     try:
-        yield
+        if not state and _native_ready():
+            from ..runtime import alloc
+
+            with alloc.use_tier("host"):
+                yield
+        else:
+            yield
     finally:
         _tls.hbm = prev
 
 
 def empty(*shape, dtype=torch.bfloat16, device=None) -> torch.Tensor:
-    """Allocate in the tier selected by use_hbm_allocator (device or pinned host)."""
+    """Allocate in the tier selected by use_hbm_allocator: device memory, or a
+    cuda tensor in pinned host memory (host tier of the native allocator; a
+    pinned CPU tensor when the library is not loaded)."""
     dev = torch.device(device) if device is not None else (
         torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else torch.device("cpu"))
     if on_hbm() or dev.type != "cuda":
         return torch.empty(*shape, dtype=dtype, device=dev)
+    if _native_ready():
+        from ..runtime import alloc
+
+        with alloc.use_tier("host", dev.index):
+            return torch.empty(*shape, dtype=dtype, device=dev)
     return torch.empty(*shape, dtype=dtype, pin_memory=True)
 
 

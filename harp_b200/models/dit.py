@@ -37,7 +37,7 @@ import torch.nn as nn
 
 from ..ops import functional as Fn
 from ..ops.modules import LinearFunction, SiLUFunction
-from ..parallel.sequence import SPContext, sp_attention_backward, sp_attention_forward
+from ..parallel.sequence import SPContext, qkv_attention_backward, qkv_attention_forward
 
 
 # ---------------------------------------------------------------------------
@@ -200,9 +200,8 @@ class DiTBlockFunction(torch.autograd.Function):
         sh1, sc1, g1, sh2, sc2, g2 = (mod[:, i * D:(i + 1) * D] for i in range(6))
         h1, rstd1 = Fn.rmsnorm_mod_fwd(x2d, None, sc1, sh1, S, cfg.norm_eps)
         qkv = Fn.gemm(h1, qkv_w, bias=qkv_b)  # [R, 3D]
-        q, k, rq, rk = Fn.qknorm_rope_fwd(qkv, H, Dh, qn_w, kn_w, freqs, 1e-6, do_norm=cfg.qk_norm)
-        v = qkv[:, 2 * D:]
-        o, attn_saved = sp_attention_forward(q, k, v, B, S, H, Dh, sp)
+        o, rq, rk, q, k, attn_saved = qkv_attention_forward(qkv, B, S, H, Dh, qn_w, kn_w, freqs, 1e-6, cfg.qk_norm,
+                                                            sp)
         a1 = torch.empty(R, D, device=x.device, dtype=x.dtype)
         x1 = Fn.gemm(o, proj_w, bias=proj_b, epi=Fn.EPI_GATED_RESIDUAL_SAVE, residual=x2d, gate=g1,
                      rows_per_batch=S, out2=a1)
@@ -254,11 +253,8 @@ class DiTBlockFunction(torch.autograd.Function):
         da1, dg1, dbo = Fn.gate_bwd(dx1, a1, g1, S, want_bias=True)
         dmod[:, 2 * D:3 * D] = dg1
         do, dwo, _ = Fn.linear_bwd(da1, o, proj_w, need_bias=False, dw_out=_direct(proj_w))
-        dqkv = torch.empty(R, 3 * D, device=dy.device, dtype=dy.dtype)
-        dq, dk = sp_attention_backward(ctx.attn_saved, q, k, qkv[:, 2 * D:], o, do, B, S, H, Dh, sp,
-                                       dv_out=dqkv[:, 2 * D:])
-        dwq, dwk = Fn.qknorm_rope_bwd(dq, dk, qkv, rq, rk, H, Dh, qn_w, kn_w, freqs, cfg.qk_norm, dqkv,
-                                      want_dw=cfg.qk_norm)
+        dqkv, dwq, dwk = qkv_attention_backward(ctx.attn_saved, qkv, q, k, o, do, rq, rk, qn_w, kn_w, freqs,
+                                                cfg.qk_norm, B, S, H, Dh, sp)
         dh1, dwqkv, dbqkv = Fn.linear_bwd(dqkv, h1, qkv_w, need_bias=True, dw_out=_direct(qkv_w))
         dx, _, dsc1, dsh1 = Fn.rmsnorm_mod_bwd(x2d, rstd1, dh1, None, sc1, S, dres=dx1, want_mod=True)
         dmod[:, 0:D] = dsh1

@@ -423,15 +423,17 @@ def silu_bwd(dy: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
 # attention (local; ring variants live in harp_b200.parallel.ring_attention)
 # ---------------------------------------------------------------------------
 def attn_fwd(q, k, v, B, Sq, Skv, H, Dh, scale=None, ready=None, chunk_len=0, start_tile=0, epoch=0,
-             timeout_s=10.0, out=None):
+             timeout_s=10.0, out=None, q_rot=0, wait_q=False):
     """q [B*Sq, >=H*Dh], k/v [B*Skv, >=H*Dh] token-major.  Returns (o [B*Sq, H*Dh],
-    lse fp32 [B, H, lse_ld(Sq)] natural log, +inf past Sq)."""
+    lse fp32 [B, H, lse_ld(Sq)] natural log, +inf past Sq).  With `ready`, key
+    (and, with wait_q, query) rows of chunk c = row // chunk_len are used only
+    once ready[c] >= epoch; q_rot rotates the order of the 256-query pairs."""
     scale = scale if scale is not None else 1.0 / math.sqrt(Dh)
     o = out if out is not None else torch.empty(B * Sq, H * Dh, device=q.device, dtype=q.dtype)
     lse = torch.full((B * H * lse_ld(Sq),), float("inf"), device=q.device)
     if _cuda(q):
         torch.ops.harp.attn_fwd(q, k, v, B, Sq, Skv, H, Dh, scale, o, lse, ready, chunk_len, start_tile, epoch,
-                                timeout_s, errors.word(q.device))
+                                timeout_s, errors.word(q.device), q_rot, wait_q)
         return o, lse
     qf = q[:, : H * Dh].float().view(B, Sq, H, Dh)
     kf = k[:, : H * Dh].float().view(B, Skv, H, Dh)

@@ -24,6 +24,12 @@ Purposes and buffers:
   GRAD / PARAM  the fused gradient reduce-scatter + AdamW + parameter push
           waits for every peer's GRAD flag; PARAM tells peers the new
           parameters have landed, which the next step waits for.
+  UQKV / UO / UDO / UDQ  Ulysses exchanges, one set of symmetric buffers
+          per layer (q|k|v head-sharded over the full sequence, the
+          sequence-sharded attention output, dO head-sharded, dq|dk|dv
+          sequence-sharded).  Each buffer is written once per step by its
+          senders; the next step's writes come after every rank's gradients
+          and parameters were exchanged, so no buffer needs an ack.
 """
 from __future__ import annotations
 
@@ -34,12 +40,14 @@ import torch
 import torch.distributed as dist
 
 from .. import _native
+from ..ops import functional as Fn
 from ..runtime import errors
 from . import collectives as C
 
 # flag slot layout (int32 per slot, world <= 8)
 _KV, _DKV, _DKV_ACK0, _DKV_ACK1, _GRAD, _PARAM, _BARRIER = 0, 8, 16, 24, 32, 40, 48
-_NFLAGS = 64
+_UQKV, _UO, _UDO, _UDQ = 56, 64, 72, 80
+_NFLAGS = 96
 DEFAULT_TIMEOUT_S = float(os.environ.get("HARP_COMM_TIMEOUT_S", "120"))
 
 
@@ -112,7 +120,9 @@ class NVLinkComm:
         self.flags_buf = SymBuffer(group, _NFLAGS * 4, device)
         self.flags = self.flags_buf.tensor(_NFLAGS, torch.int32)
         self.flag_bases = self.flags_buf.bases
-        self.epoch = {"kv": 0, "dkv": 0, "grad": 0, "barrier": 0}
+        self.epoch = {"kv": 0, "dkv": 0, "grad": 0, "barrier": 0, "uq": 0, "uo": 0, "udo": 0, "udq": 0}
+        self._uly: List[Dict[str, SymBuffer]] = []
+        self._uly_idx = 0
         self._kv_bufs: List[SymBuffer] = []
         self._kv_idx = 0
         self._dkv_bufs: List[SymBuffer] = []
@@ -144,6 +154,7 @@ class NVLinkComm:
     def begin_step(self):
         self._kv_idx = 0
         self._dkv_idx = 0
+        self._uly_idx = 0
 
     # -- sequence-parallel K/V exchange (forward) -------------------------------
     def kv_exchange(self, k: torch.Tensor, v: torch.Tensor, B: int, S: int, HD: int):
@@ -200,6 +211,72 @@ class NVLinkComm:
         self.signal(_DKV_ACK0 if slot == 0 else _DKV_ACK1, e)
         return out
 
+    # -- Ulysses: head all-to-all fused with QK-norm/RoPE and attention --------
+    def _uly_layer(self, i: int, B: int, S: int, H: int, Dh: int) -> Dict[str, SymBuffer]:
+        W = self.world
+        HD, HnDh = H * Dh, (H // W) * Dh
+        need = {"qkvf": 3 * B * W * S * HnDh * 2, "o": B * S * HD * 2, "dof": B * W * S * HnDh * 2,
+                "dqkv": B * S * 3 * HD * 2}
+        while len(self._uly) <= i:
+            self._uly.append({k: SymBuffer(self.group, n, self.device) for k, n in need.items()})
+        bufs = self._uly[i]
+        assert all(bufs[k].nbytes >= n for k, n in need.items()), "Ulysses buffer shape changed between steps"
+        return bufs
+
+    def uly_forward(self, qkv: torch.Tensor, B: int, S: int, H: int, Dh: int, wq, wk, freqs, eps: float,
+                    do_norm: bool):
+        """qkv: this rank's pre-norm q|k|v rows [B*S, >=3*H*Dh].  QK-norm + RoPE
+        are applied while q, k, v are written head-sharded into their owners'
+        buffers; attention over the full sequence starts on the local chunk and
+        takes every other chunk as its flag arrives; the output is written back
+        sequence-sharded.  Returns (o [B*S, H*Dh], rstd_q, rstd_k, saved)."""
+        i = self._uly_idx
+        self._uly_idx += 1
+        W, r = self.world, self.rank
+        Hn, Sf, HD = H // W, W * S, H * Dh
+        part = B * Sf * Hn * Dh
+        bufs = self._uly_layer(i, B, S, H, Dh)
+        rq = torch.empty(B * S * H, device=qkv.device, dtype=torch.float32) if do_norm else None
+        rk = torch.empty_like(rq) if do_norm else None
+        self.epoch["uq"] += 1
+        e = self.epoch["uq"]
+        torch.ops.harp_comm.uly_dispatch_qkv(qkv, S, H, Dh, r, bufs["qkvf"].bases, part, wq, wk, freqs,
+                                             freqs.shape[0] if freqs is not None else 1, eps, do_norm, rq, rk)
+        self.signal(_UQKV, e)
+        qkvf = bufs["qkvf"].tensor(3 * part, torch.bfloat16).view(3, B * Sf, Hn * Dh)
+        o_f, lse = Fn.attn_fwd(qkvf[0], qkvf[1], qkvf[2], B, Sf, Sf, Hn, Dh, ready=self.flags[_UQKV:_UQKV + W],
+                               chunk_len=S, start_tile=(r * S) // 128, epoch=e, timeout_s=self.timeout_s,
+                               q_rot=(r * S) // 256, wait_q=True)
+        self.epoch["uo"] += 1
+        eo = self.epoch["uo"]
+        torch.ops.harp_comm.uly_remap([o_f], 1, B, S, r, H, Dh, bufs["o"].bases, 0, HD, 0)
+        self.signal(_UO, eo)
+        self.wait_all(_UO, eo)
+        o = bufs["o"].tensor(B * S * HD, torch.bfloat16).view(B * S, HD)
+        return o, rq, rk, {"i": i, "qkvf": qkvf, "o_f": o_f, "lse": lse}
+
+    def uly_backward(self, saved, do: torch.Tensor, B: int, S: int, H: int, Dh: int) -> torch.Tensor:
+        """do: dL/d(attention output) of this rank's rows [B*S, H*Dh].  Returns
+        [B*S, 3*H*Dh]: dL/dq, dL/dk (after RoPE) and dL/dv of this rank's rows,
+        in a buffer the caller may overwrite in place."""
+        W, r = self.world, self.rank
+        Hn, Sf, HD = H // W, W * S, H * Dh
+        bufs = self._uly[saved["i"]]
+        self.epoch["udo"] += 1
+        e = self.epoch["udo"]
+        torch.ops.harp_comm.uly_remap([do], 0, B, S, r, H, Dh, bufs["dof"].bases, 0, 0, 0)
+        self.signal(_UDO, e)
+        self.wait_all(_UDO, e)
+        dof = bufs["dof"].tensor(B * Sf * Hn * Dh, torch.bfloat16).view(B * Sf, Hn * Dh)
+        qkvf = saved["qkvf"]
+        dq_f, dk_f, dv_f = Fn.attn_bwd(qkvf[0], qkvf[1], qkvf[2], saved["o_f"], dof, saved["lse"], B, Sf, Sf, Hn, Dh)
+        self.epoch["udq"] += 1
+        e2 = self.epoch["udq"]
+        torch.ops.harp_comm.uly_remap([dq_f, dk_f, dv_f], 1, B, S, r, H, Dh, bufs["dqkv"].bases, 0, 3 * HD, HD)
+        self.signal(_UDQ, e2)
+        self.wait_all(_UDQ, e2)
+        return bufs["dqkv"].tensor(B * S * 3 * HD, torch.bfloat16).view(B * S, 3 * HD)
+
     # -- gradients: fused reduce-scatter + AdamW + parameter push ---------------
     def allocate_flat(self, numel: int):
         """Symmetric flat parameter and gradient buffers (bf16)."""
@@ -230,6 +307,7 @@ class NVLinkComm:
 
     def close(self):
         torch.cuda.synchronize(self.device)
-        for b in self._kv_bufs + self._dkv_bufs + list((self._flat or {}).values()) + [self.flags_buf]:
+        uly = [b for layer in self._uly for b in layer.values()]
+        for b in self._kv_bufs + self._dkv_bufs + uly + list((self._flat or {}).values()) + [self.flags_buf]:
             b.release()
-        self._kv_bufs, self._dkv_bufs, self._flat = [], [], None
+        self._kv_bufs, self._dkv_bufs, self._flat, self._uly = [], [], None, []

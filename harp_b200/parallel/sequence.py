@@ -61,11 +61,11 @@ class SPContext:
 
 
 def resolve_mode(mode: str, heads: int, sp_size: int) -> str:
-    """"auto": Ulysses when the heads split evenly over the SP ranks and
-    sp >= 4 (at sp=2 both move the same bytes and the K/V gather overlaps
-    with attention), else the K/V gather."""
+    """"auto": Ulysses when the heads split evenly over the SP ranks (it moves
+    2x fewer bytes than the K/V gather at sp=4 and 4x fewer at sp=8, and its
+    fused NVLink form measured faster from sp=2 on), else the K/V gather."""
     if mode == "auto":
-        return "ulysses" if sp_size >= 4 and heads % sp_size == 0 else "ring"
+        return "ulysses" if sp_size > 1 and heads % sp_size == 0 else "ring"
     if mode == "ulysses" and heads % sp_size != 0:
         raise ValueError(f"ulysses SP needs heads ({heads}) divisible by sp ({sp_size})")
     return mode
@@ -158,3 +158,42 @@ def sp_attention_backward(saved, q, k, v, o, do, B: int, S: int, H: int, Dh: int
         dv_out.copy_(dkv[:, HD:])
         return dq, dk
     return dq, dk, dkv[:, HD:]
+
+
+def ulysses_nvl(sp: SPContext) -> bool:
+    """The fused NVLink Ulysses path (head all-to-all inside harp kernels)."""
+    return sp.size > 1 and sp.mode == "ulysses" and sp.backend == "nvl" and sp.comm is not None
+
+
+def qkv_attention_forward(qkv, B: int, S: int, H: int, Dh: int, wq, wk, freqs, eps: float, do_norm: bool,
+                          sp: SPContext):
+    """QK-norm + RoPE of the pre-norm q|k|v rows, then sequence-parallel
+    attention.  Returns (o [B*S, H*Dh], rstd_q, rstd_k, q, k, saved); q and k
+    (post-norm, this rank's rows) are None on the fused Ulysses path, whose
+    exchange applies the norm on the way."""
+    HD = H * Dh
+    if ulysses_nvl(sp):
+        o, rq, rk, saved = sp.comm.uly_forward(qkv, B, S, H, Dh, wq, wk, freqs, eps, do_norm)
+        return o, rq, rk, None, None, saved
+    q, k, rq, rk = Fn.qknorm_rope_fwd(qkv, H, Dh, wq, wk, freqs, eps, do_norm=do_norm)
+    o, saved = sp_attention_forward(q, k, qkv[:, 2 * HD:], B, S, H, Dh, sp)
+    return o, rq, rk, q, k, saved
+
+
+def qkv_attention_backward(saved, qkv, q, k, o, do, rq, rk, wq, wk, freqs, do_norm: bool, B: int, S: int, H: int,
+                           Dh: int, sp: SPContext, dqkv: Optional[torch.Tensor] = None):
+    """Backward of qkv_attention_forward: returns (d qkv_pre [B*S, 3*H*Dh],
+    dwq, dwk) (norm-weight gradients fp32, or None)."""
+    HD = H * Dh
+    if ulysses_nvl(sp):
+        g = sp.comm.uly_backward(saved, do, B, S, H, Dh)
+        # d(post-RoPE q, k) -> d(pre-norm q, k) in place (one warp per row and head
+        # reads its gradient before writing the result); dv is already final
+        dwq, dwk = Fn.qknorm_rope_bwd(g[:, :HD], g[:, HD:2 * HD], qkv, rq, rk, H, Dh, wq, wk, freqs, do_norm, g,
+                                      want_dw=do_norm)
+        return g, dwq, dwk
+    if dqkv is None:
+        dqkv = torch.empty(B * S, 3 * HD, device=qkv.device, dtype=qkv.dtype)
+    dq, dk = sp_attention_backward(saved, q, k, qkv[:, 2 * HD:], o, do, B, S, H, Dh, sp, dv_out=dqkv[:, 2 * HD:])
+    dwq, dwk = Fn.qknorm_rope_bwd(dq, dk, qkv, rq, rk, H, Dh, wq, wk, freqs, do_norm, dqkv, want_dw=do_norm)
+    return dqkv, dwq, dwk

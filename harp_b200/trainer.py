@@ -157,16 +157,24 @@ class ParallelState:
     world_group: object = None
     sp_group: object = None
     dp_group: object = None
+    rs_size: int = 1
+    rs_group: object = None
 
     @staticmethod
-    def build(sp_size: Optional[int] = None) -> "ParallelState":
+    def build(sp_size: Optional[int] = None, rs_size: Optional[int] = None) -> "ParallelState":
+        """Groups as the reference's train.py:155-166,234-272: SP groups of
+        consecutive ranks (i // sp); DP groups of equal SP index (i % sp); RS
+        groups of rs = min(rs_size, world / sp) ranks with equal SP index inside
+        blocks of sp * rs ranks (i // (sp * rs) * sp + i % sp)."""
         if not (dist.is_available() and dist.is_initialized()):
             return ParallelState()
         W, r = dist.get_world_size(), dist.get_rank()
         sp = sp_size or W
         assert W % sp == 0, f"world {W} not divisible by sp {sp}"
         dp = W // sp
-        sp_group = dp_group = None
+        rs = max(1, min(rs_size or 1, dp))
+        assert dp % rs == 0, f"dp {dp} not divisible by rs {rs}"
+        sp_group = dp_group = rs_group = None
         # SP groups: consecutive ranks (the reference's sp_ranks[i // sp]); DP: same local index
         for g in range(dp):
             ranks = list(range(g * sp, (g + 1) * sp))
@@ -178,7 +186,14 @@ class ParallelState:
             pg = dist.new_group(ranks) if dp > 1 else None
             if r in ranks:
                 dp_group = pg
-        return ParallelState(W, r, sp, dp, dist.group.WORLD, sp_group, dp_group)
+        if rs > 1:
+            for blk in range(W // (sp * rs)):
+                for l in range(sp):
+                    ranks = [blk * sp * rs + j * sp + l for j in range(rs)]
+                    pg = dist.new_group(ranks)
+                    if r in ranks:
+                        rs_group = pg
+        return ParallelState(W, r, sp, dp, dist.group.WORLD, sp_group, dp_group, rs, rs_group)
 
 
 class Trainer:

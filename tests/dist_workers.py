@@ -188,3 +188,11 @@ def rank_exit(rank, world, out, args):
             return {"failed_at": step, "elapsed": time.time() - t0, "error": type(e).__name__, "stale": stale}
     hb.stop()
     return {"failed_at": None}
+
+
+def groups(rank, world, out, args):
+    from harp_b200.trainer import ParallelState
+
+    par = ParallelState.build(args["sp"], args["rs"])
+    get = lambda g: dist.get_process_group_ranks(g) if g is not None else None  # noqa: E731
+    return {"sp": get(par.sp_group), "dp": get(par.dp_group), "rs": get(par.rs_group), "rs_size": par.rs_size}

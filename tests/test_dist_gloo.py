@@ -158,3 +158,13 @@ def test_rank_that_leaves_is_detected(tmp_path):
     assert d["failed_at"] == 2, d
     assert d["elapsed"] < 30
     assert d["stale"] == [1], d
+
+
+def test_group_topology_four_ranks(tmp_path):
+    res, _ = _run("groups", 4, tmp_path, {"sp": 2, "rs": 2})
+    # SP groups of consecutive ranks, DP groups of equal SP index, RS groups of
+    # equal SP index inside blocks of sp*rs ranks
+    assert [res[r]["sp"] for r in range(4)] == [[0, 1], [0, 1], [2, 3], [2, 3]]
+    assert [res[r]["dp"] for r in range(4)] == [[0, 2], [1, 3], [0, 2], [1, 3]]
+    assert [res[r]["rs"] for r in range(4)] == [[0, 2], [1, 3], [0, 2], [1, 3]]
+    assert res[0]["rs_size"] == 2

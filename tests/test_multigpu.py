@@ -1,0 +1,87 @@
+"""Two-GPU tests: sequence-parallel training through the NVLink kernels
+(fused Ulysses and K/V gather) against one GPU, and the bounded flag wait."""
+import multiprocessing as mp
+import os
+import socket
+
+import pytest
+import torch
+
+import mgpu_workers as W
+
+pytestmark = [pytest.mark.gpu, pytest.mark.multigpu, pytest.mark.timeout(900)]
+
+
+def _need(n):
+    if not torch.cuda.is_available() or torch.cuda.device_count() < n:
+        pytest.skip(f"needs {n} GPUs")
+
+
+def _port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _run(name, world, tmp_path, args):
+    ctx = mp.get_context("spawn")
+    port = _port()
+    procs = [ctx.Process(target=W.entry, args=(r, world, port, name, str(tmp_path), args)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(600)
+    codes = [p.exitcode for p in procs]
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert codes == [0] * world, codes
+    return {r: torch.load(os.path.join(str(tmp_path), f"rank{r}.pt"), weights_only=False) for r in range(world)}
+
+
+def _batch(path, n=2):
+    from harp_b200.models.dit import PRESETS
+
+    cfg = PRESETS["small"]
+    g = torch.Generator().manual_seed(7)
+    b = {"latent": torch.randn(n, cfg.in_channels, 32, 32, generator=g).bfloat16(),
+         "noise": torch.randn(n, cfg.in_channels, 32, 32, generator=g).bfloat16(),
+         "text": torch.randn(n, 64, cfg.text_dim, generator=g).bfloat16(),
+         "sigmas": torch.rand(n, generator=g)}
+    torch.save(b, path)
+    return b
+
+
+def _single(batch, steps):
+    from harp_b200.models.dit import DiT, PRESETS
+    from harp_b200.trainer import ParallelState, TrainConfig, Trainer
+
+    model = DiT(PRESETS["small"])
+    model.initialize_weights(0)
+    model = model.to(torch.bfloat16)
+    tr = Trainer(model, ParallelState(), TrainConfig(lr=1e-3), torch.device("cuda", 0))
+    losses = [tr.step({k: v.pin_memory() for k, v in batch.items()}) for _ in range(steps)]
+    return losses, tr.flat.flat.cpu()
+
+
+@pytest.mark.parametrize("mode,backend,comm", [("ulysses", "nvl", "nvl"), ("ring", "nvl", "nvl"),
+                                               ("ulysses", "torch", "torch")])
+def test_sp2_training_matches_one_gpu(tmp_path, mode, backend, comm):
+    _need(2)
+    bpath = str(tmp_path / "batch.pt")
+    batch = _batch(bpath)
+    ref_losses, ref_flat = _single(batch, 3)
+    res = _run("train", 2, tmp_path, {"batch": bpath, "steps": 3, "mode": mode, "backend": backend, "comm": comm})
+    for r in (0, 1):
+        assert res[r]["mode"] == mode and res[r]["backend"] == backend
+        assert res[r]["losses"] == pytest.approx(ref_losses, rel=1e-2), (res[r]["losses"], ref_losses)
+        torch.testing.assert_close(res[r]["flat"].float(), ref_flat.float(), rtol=2 ** -6, atol=2 * 3 * 1e-3)
+    assert torch.equal(res[0]["flat"], res[1]["flat"])
+
+
+def test_never_signalled_flag_times_out_cleanly(tmp_path):
+    _need(2)
+    res = _run("flag_timeout", 2, tmp_path, {})
+    for r in (0, 1):
+        assert res[r]["err"][0] == 2 and res[r]["err"][1] >= 100, res[r]  # peer timeout at a wait site
+        assert res[r]["x"] == 8.0

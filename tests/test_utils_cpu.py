@@ -256,3 +256,16 @@ def test_save_trainable_param_hook(tmp_path):
     with preserve_requires_grad(m):
         m.requires_grad_(False)
     assert m[1].weight.requires_grad and not m[0].weight.requires_grad
+
+
+def test_launch_rankfile_cpu_sets_and_command(tmp_path):
+    from harp_b200 import launch as L
+
+    lines = L.generate_rankfile(["node10", "node2", "node2"], ranks_per_node=2, cores_per_node=8)
+    assert lines == ["rank 0=node2 gpu=0 cpus=0-3", "rank 1=node2 gpu=1 cpus=4-7",
+                     "rank 2=node10 gpu=0 cpus=0-3", "rank 3=node10 gpu=1 cpus=4-7"]
+    # two GPUs per NUMA node: each rank gets half of its node's cores
+    aff = {0: [0, 1, 2, 3], 1: [0, 1, 2, 3], 2: [4, 5, 6, 7], 3: [4, 5, 6, 7]}
+    assert L.cpu_sets(4, affinity=aff) == [[0, 1], [2, 3], [4, 5], [6, 7]]
+    cmd = L.torchrun_cmd(["train.py", "--x"], 8)
+    assert "--master-addr=127.0.0.1" in cmd and cmd[-2:] == ["train.py", "--x"]

@@ -73,7 +73,7 @@ def parse_args(argv=None):
     p.add_argument("--max_grad_norm", default=1.0, type=float, help="accepted; not applied (as in the reference)")
     p.add_argument("--log_interval", type=int, default=1)
     p.add_argument("--sp_size", type=int, default=4)
-    p.add_argument("--rs_size", type=int, default=16, help="accepted; the optimizer shards over every rank")
+    p.add_argument("--rs_size", type=int, default=16, help="RS group size (rows of a parameter; the managers API); the trainer shards its optimizer over every rank")
     p.add_argument("--comm_backend", type=str, default="auto", choices=["auto", "nvl", "torch"])
     p.add_argument("--sp_mode", type=str, default="auto", choices=["auto", "ring", "ulysses"],
                    help="sequence-parallel attention: K/V gather (the reference's ring) or head all-to-all")
@@ -176,6 +176,10 @@ def main(args):
     from harp_b200.utils.observability import JsonlWriter, PhaseTimer, make_profiler, setup_logger
 
     rank, world, local = discover_ranks()
+    if os.environ.get("HARP_BIND_CPUS") == "1":
+        from harp_b200.launch import bind_process
+
+        bind_process(local)
     use_cuda = torch.cuda.is_available()
     device = torch.device("cuda", local) if use_cuda else torch.device("cpu")
     if use_cuda:
@@ -189,7 +193,7 @@ def main(args):
         kw = {"device_id": device} if use_cuda else {}
         dist.init_process_group(backend, timeout=datetime.timedelta(minutes=10), **kw)
     sp_size = min(args.sp_size, world) if world > 1 else 1
-    par = ParallelState.build(sp_size)
+    par = ParallelState.build(sp_size, args.rs_size)
     is_main = rank == 0
     args.work_dir = os.path.join(args.work_dir, args.run_timestamp) if not args.resume_from_checkpoint else \
         args.work_dir
