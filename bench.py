@@ -9,6 +9,7 @@ Scaling is weak: every GPU always holds 4 samples' worth of tokens
 are the same at every N.  Weights are random (Philox), data synthetic.
 
   python bench.py --gpus N --steps K --warmup W [--impl harp|baseline|reference]
+  python bench.py --op ring-attn --seq 65536 [--sp-mode ulysses|ring] ...   (attention op sweep)
 
 N > 1 is launched by torchrun (RANK / LOCAL_RANK / WORLD_SIZE from the env).
 Rank 0 prints one JSON line.  `value` is device-timed (CUDA events on the
@@ -46,9 +47,11 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="harp", choices=["harp", "baseline", "reference"])
     ap.add_argument("--model", default="dit-xl-2")
-    ap.add_argument("--batch-per-gpu", type=int, default=4)
-    ap.add_argument("--latent", type=int, default=128)
-    ap.add_argument("--text-len", type=int, default=TEXT_TOKENS)
+    ap.add_argument("--batch-per-gpu", type=int, default=4,
+                    help="dit-*: samples per GPU (weak scaling: each SP group holds batch-per-gpu * sp samples)")
+    ap.add_argument("--batch", type=int, default=1, help="mmdit-*/flux-*: samples per SP group (strong scaling)")
+    ap.add_argument("--latent", type=int, default=0, help="latent side (default: 128, mmdit-2b 256)")
+    ap.add_argument("--text-len", type=int, default=0, help="text tokens (default: 256, flux-12b 512)")
     ap.add_argument("--sp", type=int, default=0, help="sequence-parallel size (default: all GPUs)")
     ap.add_argument("--sp-backend", default="auto", choices=["auto", "torch", "nvl"])
     ap.add_argument("--sp-mode", default="auto", choices=["auto", "ring", "ulysses"],
@@ -56,6 +59,9 @@ def parse():
     ap.add_argument("--comm", default="auto", choices=["auto", "torch", "nvl"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--depth", type=int, default=0, help="override depth (debug only; not a valid bench)")
+    ap.add_argument("--op", default="train", choices=["train", "ring-attn"],
+                    help="ring-attn: sequence-parallel attention fwd+bwd of Q/K/V [1, 24, seq, 128]")
+    ap.add_argument("--seq", type=int, default=16384, help="ring-attn: total sequence length (split over ranks)")
     return ap.parse_args()
 
 
@@ -161,36 +167,166 @@ def run_reference(args):
     return 0
 
 
+def run_ring_attn(args):
+    """Sequence-parallel attention forward + backward, Q/K/V [1, 24, S, 128]
+    bf16 non-causal, S split evenly over the N ranks (BASELINE.json op sweep).
+    harp: fused NVLink Ulysses (head all-to-all inside harp kernels, attention
+    consuming chunks as they land) or the NVLink K/V gather ("ring"); baseline:
+    NCCL all-gather of K/V + SDPA forward/backward + NCCL reduce-scatter of
+    dK/dV.  TFLOP/s of the whole job = 4*S^2*H*D*(1 + 2.5) / time."""
+    rank, ws, local = setup_dist(args.gpus)
+    device = torch.device("cuda", local)
+    B, H, D, S = 1, 24, 128, args.seq
+    assert S % ws == 0
+    Sl = S // ws
+    g = torch.Generator(device=device).manual_seed(17 + rank)
+    q, k, v, do = (torch.randn(B * Sl, H * D, device=device, generator=g).to(torch.bfloat16) for _ in range(4))
+    mode = "-"
+    if args.impl == "harp":
+        import harp_b200
+        from harp_b200.parallel import sequence as SQ
+
+        assert harp_b200.load_native(build_if_needed=False), "harp CUDA library not built"
+        comm = None
+        if ws > 1:
+            from harp_b200.parallel.nvlink import NVLinkComm
+
+            comm = NVLinkComm.get(dist.group.WORLD, device)
+        mode = SQ.resolve_mode(args.sp_mode, H, ws) if ws > 1 else "local"
+        sp = SQ.SPContext.from_group(dist.group.WORLD if ws > 1 else None, backend="nvl", comm=comm, mode=mode) \
+            if ws > 1 else SQ.SPContext()
+        qkv = torch.cat([q, k, v], 1)
+
+        def step():
+            if comm is not None:
+                comm.begin_step()
+                comm.barrier()  # every rank is done with the previous step's buffers
+            if SQ.ulysses_nvl(sp):
+                o, _, _, saved = comm.uly_forward(qkv, B, Sl, H, D, None, None, None, 0.0, False)
+                comm.uly_backward(saved, do, B, Sl, H, D)
+            else:
+                o, saved = SQ.sp_attention_forward(q, k, v, B, Sl, H, D, sp)
+                SQ.sp_attention_backward(saved, q, k, v, o, do, B, Sl, H, D, sp)
+    else:
+        import torch.nn.functional as F
+
+        def step():
+            kv = torch.cat([k, v], 1)
+            if ws > 1:
+                full = torch.empty(ws * B * Sl, 2 * H * D, device=device, dtype=kv.dtype)
+                dist.all_gather_into_tensor(full, kv)
+            else:
+                full = kv
+            kf = full[:, :H * D].reshape(B, S, H, D).transpose(1, 2).detach().requires_grad_(True)
+            vf = full[:, H * D:].reshape(B, S, H, D).transpose(1, 2).detach().requires_grad_(True)
+            qf = q.view(B, Sl, H, D).transpose(1, 2).detach().requires_grad_(True)
+            o = F.scaled_dot_product_attention(qf, kf, vf)
+            o.backward(do.view(B, Sl, H, D).transpose(1, 2))
+            dkv = torch.cat([kf.grad.transpose(1, 2).reshape(B * S, H * D),
+                             vf.grad.transpose(1, 2).reshape(B * S, H * D)], 1)
+            if ws > 1:
+                mine = torch.empty(B * Sl, 2 * H * D, device=device, dtype=dkv.dtype)
+                dist.reduce_scatter_tensor(mine, dkv)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if ws > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(args.steps):
+        step()
+    ev1.record()
+    torch.cuda.synchronize()
+    if ws > 1:
+        dist.barrier()
+    ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps, ws)
+    if args.impl == "harp":
+        from harp_b200.runtime import errors
+
+        errors.check(device)
+    flops = 4.0 * B * H * S * S * D * 3.5
+    if rank == 0:
+        print(json.dumps({
+            "metric": "ring-attn fwd+bwd TFLOPS (whole job, max over ranks)", "value": flops / ms / 1e9,
+            "unit": "TFLOP/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic N(0,1) Q/K/V/dO", "impl": args.impl,
+            "config": {"op": "sequence-parallel attention fwd+bwd", "q_shape": [B, H, S, D], "seq_total": S,
+                       "seq_per_rank": Sl, "causal": False, "mode": mode,
+                       "l2": "Q/K/V/dO per rank %.0f MB; K/V of all ranks %.0f MB" %
+                             (4 * B * Sl * H * D * 2 / 1e6, 2 * B * S * H * D * 2 / 1e6)},
+        }), flush=True)
+    if ws > 1:
+        if args.impl == "harp":
+            from harp_b200.parallel.nvlink import NVLinkComm
+
+            torch.cuda.synchronize()
+            NVLinkComm.close_all()
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
+    if args.op == "ring-attn":
+        return run_ring_attn(args)
+    family = "dit" if args.model.startswith("dit") or args.model in ("tiny", "small") else "mmdit"
+    args.latent = args.latent or (256 if args.model == "mmdit-2b" else 128)
+    args.text_len = args.text_len or (512 if args.model == "flux-12b" else TEXT_TOKENS)
+    img_tokens = (args.latent // 2) ** 2
+    if args.impl == "baseline" and family != "dit":
+        print(json.dumps({"impl": "baseline", "unavailable": "the NCCL+cuBLAS/SDPA baseline implements the DiT "
+                          "configuration only"}))
+        return 0
     rank, ws, local = setup_dist(args.gpus)
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     sp = args.sp or ws
-    B = args.batch_per_gpu * sp  # per SP group; each GPU holds B * S / sp tokens = 4 samples' worth
+    # dit: weak scaling, each GPU holds batch_per_gpu samples' worth of tokens;
+    # mmdit/flux: a fixed batch per SP group split over its ranks (strong scaling)
+    B = args.batch_per_gpu * sp if family == "dit" else args.batch
     dp = ws // sp
     global_batch = B * dp
 
     if args.impl == "harp":
         import harp_b200
-        from harp_b200.models.dit import DiT, PRESETS
         from harp_b200.trainer import ParallelState, TrainConfig, Trainer
 
         assert harp_b200.load_native(build_if_needed=False), "harp CUDA library not built (run __graft_entry__.build())"
-        cfg = PRESETS[args.model]
-        if args.depth:
-            import dataclasses
-
-            cfg = dataclasses.replace(cfg, depth=args.depth)
         par = ParallelState.build(sp)
-        with torch.device(device):
-            model = DiT(cfg)
+        if family == "dit":
+            from harp_b200.models.dit import DiT, PRESETS
+
+            cfg = PRESETS[args.model]
+            if args.depth:
+                import dataclasses
+
+                cfg = dataclasses.replace(cfg, depth=args.depth)
+            with torch.device(device):
+                model = DiT(cfg)
+            loss_fn = None
+        else:
+            from harp_b200.models import mmdit as M
+
+            cfg = M.PRESETS[args.model]
+            if args.depth:
+                import dataclasses
+
+                cfg = dataclasses.replace(cfg, depth_double=min(cfg.depth_double, args.depth),
+                                          depth_single=min(cfg.depth_single, args.depth))
+            with torch.device(device):
+                model = M.MMDiT(cfg)
+            loss_fn = M.mmdit_loss_local
         model.initialize_weights(seed=0)
         model = model.to(torch.bfloat16)
         trainer = Trainer(model, par, TrainConfig(comm=args.comm), device, sp_backend=args.sp_backend,
-                          sp_mode=args.sp_mode)
+                          sp_mode=args.sp_mode, loss_fn=loss_fn)
         cin, tdim = cfg.in_channels, cfg.text_dim
 
         def step(b):
@@ -250,7 +386,7 @@ def main():
     ms = max_over_ranks(ms, ws)
     if args.impl == "harp":
         trainer.check_errors()
-    value = global_batch * IMG_TOKENS / (ms / 1000.0)
+    value = global_batch * img_tokens / (ms / 1000.0)
 
     e2e = None
     if not args.no_e2e:
@@ -266,7 +402,7 @@ def main():
         el = time.perf_counter() - t0
         el = max_over_ranks(el, ws)
         h2d = sum(v.numel() * v.element_size() for v in host_batch.values())
-        e2e = {"value": global_batch * IMG_TOKENS / (el / args.steps), "unit": "image-tokens/s",
+        e2e = {"value": global_batch * img_tokens / (el / args.steps), "unit": "image-tokens/s",
                "ms_per_step": 1000.0 * el / args.steps, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
                "api": "Trainer.step" if args.impl == "harp" else "BaselineTrainer.step", "last_loss": last}
 
@@ -280,7 +416,7 @@ def main():
             "warmup": args.warmup,
             "ms_per_step": ms,
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": "weak" if family == "dit" else "strong",
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic (random latents/text embeddings of the named shapes, random-init weights)",
@@ -288,13 +424,15 @@ def main():
             "config": {
                 "model": args.model if not args.depth else f"{args.model}(depth={args.depth}, NOT VALID)",
                 "global_batch": global_batch,
-                "per_gpu_batch": args.batch_per_gpu,
-                "seq_len": IMG_TOKENS + args.text_len,
-                "image_tokens": IMG_TOKENS,
+                "per_gpu_batch": args.batch_per_gpu if family == "dit" else global_batch / ws,
+                "seq_len": img_tokens + args.text_len,
+                "image_tokens": img_tokens,
                 "text_tokens": args.text_len,
                 "latent": [16, args.latent, args.latent],
                 "parallelism": parallelism,
-                "l2": "inputs larger than L2 (weights 1.7 GB, activations > 10 GB per step)",
+                "l2": "inputs larger than L2 (weights %.1f GB, activations > 10 GB per step)" %
+                      (sum(p.numel() for p in trainer.model.parameters()) * 2 / 1e9 if args.impl == "harp"
+                       else 1.35),
             },
             "loss": float(loss.reshape(-1)[0].item()),
             "gpu_launches": launches,

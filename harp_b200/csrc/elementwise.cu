@@ -174,23 +174,37 @@ __global__ void rmsnorm_mod_bwd_kernel(const bf16* __restrict__ x, long ldx, con
 // Block = 32 columns x 8 warps: lane = column, warp w sums rows w, w+8, ...
 // (coalesced 128-byte row segments), then warp 0 adds the 8 warp sums in a
 // fixed order (deterministic).
-__global__ void reduce_partials_kernel(const float* __restrict__ part, int nrows, int per_group, int D,
-                                       void* __restrict__ out, long ldo, int out_bf16, int accumulate) {
-  __shared__ float ws[8][33];
+// out[g, d] (+)= sum over rows j of group g of part[j, d].  32 columns per
+// block, NW warps striding over the group's rows with four independent partial
+// sums each (more loads in flight); every sum is combined in a fixed order, so
+// the result is deterministic.
+template <int NW>
+__global__ void __launch_bounds__(NW * 32) reduce_partials_kernel(const float* __restrict__ part, int nrows,
+                                                                 int per_group, int D, void* __restrict__ out,
+                                                                 long ldo, int out_bf16, int accumulate) {
+  __shared__ float ws[NW][33];
   const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
   const int d = blockIdx.x * 32 + lane;
   const int g = blockIdx.y;
   const int j0 = g * per_group;
   const int j1 = min(nrows, j0 + per_group);
-  float s = 0.f;
-  if (d < D)
-    for (int j = j0 + warp; j < j1; j += 8) s += part[(long)j * D + d];
-  ws[warp][lane] = s;
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+  if (d < D) {
+    int j = j0 + warp;
+    for (; j + 3 * NW < j1; j += 4 * NW) {
+      s0 += part[(long)j * D + d];
+      s1 += part[(long)(j + NW) * D + d];
+      s2 += part[(long)(j + 2 * NW) * D + d];
+      s3 += part[(long)(j + 3 * NW) * D + d];
+    }
+    for (; j < j1; j += NW) s0 += part[(long)j * D + d];
+  }
+  ws[warp][lane] = (s0 + s1) + (s2 + s3);
   __syncthreads();
   if (warp != 0 || d >= D) return;
-  s = 0.f;
+  float s = 0.f;
 #pragma unroll
-  for (int w = 0; w < 8; ++w) s += ws[w][lane];
+  for (int w = 0; w < NW; ++w) s += ws[w][lane];
   if (out_bf16) {
     bf16* o = reinterpret_cast<bf16*>(out) + (long)g * ldo + d;
     if (accumulate) s += __bfloat162float(*o);
@@ -342,6 +356,112 @@ __global__ void qknorm_rope_bwd_kernel(const bf16* __restrict__ dq, const bf16* 
     if (i < Dh) pwq[(long)blockIdx.x * Dh + i] = v;
     else pwk[(long)blockIdx.x * Dh + i - Dh] = v;
   }
+}
+
+// Vectorized backward: one thread per (row, head) of q (blockIdx.y == 0) or k
+// (blockIdx.y == 1), 16-byte loads, two passes over the head (the second hits
+// L1).  Block b owns items [b*ipb, (b+1)*ipb); its threads stride over them and
+// accumulate d(w) in registers, reduced once per block into pw[b].
+template <int DH>
+__global__ void __launch_bounds__(128) qknorm_rope_bwd_vec_kernel(
+    const bf16* __restrict__ dq, const bf16* __restrict__ dk, long lddq, long lddk, const bf16* __restrict__ qkv,
+    long ld, const float* __restrict__ rstd_q, const float* __restrict__ rstd_k, int R, int H,
+    const bf16* __restrict__ wq, const bf16* __restrict__ wk, const float2* __restrict__ freqs, int freq_rows,
+    int do_norm, long ipb, bf16* __restrict__ dqkv, long lddx, float* __restrict__ pwq, float* __restrict__ pwk) {
+  constexpr int NV = DH / 8;
+  const bool isk = blockIdx.y != 0;
+  const bf16* gbase = isk ? dk : dq;
+  const long ldg = isk ? lddk : lddq;
+  const bf16* xbase = qkv + (isk ? (long)H * DH : 0);
+  const float* rstd = isk ? rstd_k : rstd_q;
+  const bf16* w = isk ? wk : wq;
+  bf16* dxbase = dqkv + (isk ? (long)H * DH : 0);
+  float* pw = isk ? pwk : pwq;
+  const bool want_w = pw != nullptr && do_norm;
+  __shared__ float sw[DH];
+  __shared__ float sred[4][DH];
+  for (int i = threadIdx.x; i < DH; i += blockDim.x) sw[i] = (w && do_norm) ? __bfloat162float(w[i]) : 1.f;
+  __syncthreads();
+  float acc[DH];
+#pragma unroll
+  for (int i = 0; i < DH; ++i) acc[i] = 0.f;
+  const long items = (long)R * H;
+  const long lo = (long)blockIdx.x * ipb, hi = min(lo + ipb, items);
+  for (long item = lo + threadIdx.x; item < hi; item += blockDim.x) {
+    const int row = (int)(item / H), h = (int)(item % H);
+    const bf16* gp = gbase + (long)row * ldg + h * DH;
+    const bf16* xp = xbase + (long)row * ld + h * DH;
+    const float4* fp = freqs ? reinterpret_cast<const float4*>(freqs + (long)(row % freq_rows) * (DH / 2)) : nullptr;
+    const float rs = do_norm ? rstd[item] : 1.f;
+    float dot = 0.f;
+    if (do_norm) {
+#pragma unroll
+      for (int v = 0; v < NV; ++v) {
+        const uint4 g4 = *reinterpret_cast<const uint4*>(gp + 8 * v);
+        const uint4 x4 = *reinterpret_cast<const uint4*>(xp + 8 * v);
+        const uint32_t gw[4] = {g4.x, g4.y, g4.z, g4.w}, xw[4] = {x4.x, x4.y, x4.z, x4.w};
+        float4 fa = make_float4(1.f, 0.f, 1.f, 0.f), fb = fa;
+        if (fp) {
+          fa = fp[2 * v];
+          fb = fp[2 * v + 1];
+        }
+        const float cs[8] = {fa.x, fa.y, fa.z, fa.w, fb.x, fb.y, fb.z, fb.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 g = unpack_bf16x2(gw[j]), x = unpack_bf16x2(xw[j]);
+          const float c = cs[2 * j], sn = cs[2 * j + 1];
+          const float g0 = g.x * c + g.y * sn, g1 = -g.x * sn + g.y * c;  // inverse rotation
+          dot += g0 * sw[8 * v + 2 * j] * x.x + g1 * sw[8 * v + 2 * j + 1] * x.y;
+        }
+      }
+      dot *= rs;
+    }
+    const float mu = dot / DH;
+    bf16* dxp = dxbase + (long)row * lddx + h * DH;
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      const uint4 g4 = *reinterpret_cast<const uint4*>(gp + 8 * v);
+      const uint32_t gw[4] = {g4.x, g4.y, g4.z, g4.w};
+      uint32_t xw[4] = {0u, 0u, 0u, 0u};
+      if (do_norm) {
+        const uint4 x4 = *reinterpret_cast<const uint4*>(xp + 8 * v);
+        xw[0] = x4.x; xw[1] = x4.y; xw[2] = x4.z; xw[3] = x4.w;
+      }
+      float4 fa = make_float4(1.f, 0.f, 1.f, 0.f), fb = fa;
+      if (fp) {
+        fa = fp[2 * v];
+        fb = fp[2 * v + 1];
+      }
+      const float cs[8] = {fa.x, fa.y, fa.z, fa.w, fb.x, fb.y, fb.z, fb.w};
+      uint32_t ow[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 g = unpack_bf16x2(gw[j]);
+        const float c = cs[2 * j], sn = cs[2 * j + 1];
+        const float g0 = g.x * c + g.y * sn, g1 = -g.x * sn + g.y * c;
+        if (do_norm) {
+          const float2 x = unpack_bf16x2(xw[j]);
+          const float xh0 = x.x * rs, xh1 = x.y * rs;
+          ow[j] = pack_bf16x2(rs * (g0 * sw[8 * v + 2 * j] - xh0 * mu), rs * (g1 * sw[8 * v + 2 * j + 1] - xh1 * mu));
+          acc[8 * v + 2 * j] += g0 * xh0;
+          acc[8 * v + 2 * j + 1] += g1 * xh1;
+        } else {
+          ow[j] = pack_bf16x2(g0, g1);
+        }
+      }
+      *reinterpret_cast<uint4*>(dxp + 8 * v) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+    }
+  }
+  if (!want_w) return;
+  const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
+#pragma unroll
+  for (int i = 0; i < DH; ++i) {
+    const float t = warp_sum(acc[i]);
+    if (lane == 0) sred[warp][i] = t;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < DH; i += blockDim.x)
+    pw[(long)blockIdx.x * DH + i] = sred[0][i] + sred[1][i] + sred[2][i] + sred[3][i];  // fixed order
 }
 
 // ---------------------------------------------------------------------------
@@ -610,6 +730,51 @@ __global__ void adamw_flat_kernel(float* __restrict__ master, float* __restrict_
     if (param) param[i] = __float2bfloat16(p);
   }
 }
+// Vector form: 8 elements per thread and iteration (fp32 states as 2 x 16-byte
+// loads each, bf16 grad / param as one 16-byte access).  n % 8 == 0 and every
+// pointer 16-byte aligned.
+__global__ void __launch_bounds__(256) adamw_flat_vec_kernel(float* __restrict__ master, float* __restrict__ m,
+                                                             float* __restrict__ v,
+                                                             const bf16* __restrict__ grad_bf16,
+                                                             const float* __restrict__ grad_f32,
+                                                             bf16* __restrict__ param, long n8, AdamHyper h) {
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (long)gridDim.x * blockDim.x) {
+    float4* mp = reinterpret_cast<float4*>(master) + 2 * i;
+    float4* mmp = reinterpret_cast<float4*>(m) + 2 * i;
+    float4* vp = reinterpret_cast<float4*>(v) + 2 * i;
+    const float4 pa = mp[0], pb = mp[1], ma = mmp[0], mb = mmp[1], va = vp[0], vb = vp[1];
+    float g[8];
+    if (grad_f32) {
+      const float4 ga = reinterpret_cast<const float4*>(grad_f32)[2 * i];
+      const float4 gb = reinterpret_cast<const float4*>(grad_f32)[2 * i + 1];
+      g[0] = ga.x; g[1] = ga.y; g[2] = ga.z; g[3] = ga.w; g[4] = gb.x; g[5] = gb.y; g[6] = gb.z; g[7] = gb.w;
+    } else {
+      const uint4 gw = reinterpret_cast<const uint4*>(grad_bf16)[i];
+      const uint32_t w4[4] = {gw.x, gw.y, gw.z, gw.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = unpack_bf16x2(w4[j]);
+        g[2 * j] = f.x;
+        g[2 * j + 1] = f.y;
+      }
+    }
+    float p[8] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
+    float mm[8] = {ma.x, ma.y, ma.z, ma.w, mb.x, mb.y, mb.z, mb.w};
+    float vv[8] = {va.x, va.y, va.z, va.w, vb.x, vb.y, vb.z, vb.w};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) adam_elem(p[j], mm[j], vv[j], g[j], h);
+    mp[0] = make_float4(p[0], p[1], p[2], p[3]);
+    mp[1] = make_float4(p[4], p[5], p[6], p[7]);
+    mmp[0] = make_float4(mm[0], mm[1], mm[2], mm[3]);
+    mmp[1] = make_float4(mm[4], mm[5], mm[6], mm[7]);
+    vp[0] = make_float4(vv[0], vv[1], vv[2], vv[3]);
+    vp[1] = make_float4(vv[4], vv[5], vv[6], vv[7]);
+    if (param)
+      reinterpret_cast<uint4*>(param)[i] = make_uint4(pack_bf16x2(p[0], p[1]), pack_bf16x2(p[2], p[3]),
+                                                      pack_bf16x2(p[4], p[5]), pack_bf16x2(p[6], p[7]));
+  }
+}
+
 // Tensor-list variant (foreach): pointer tables in device memory.  Params may
 // be bf16 (is_bf16=1, no master) or fp32; states fp32 or same dtype as param.
 struct AdamListEntry {
@@ -775,9 +940,15 @@ void reduce_partials(const at::Tensor& part, int64_t per_group, at::Tensor& out,
   if (nrows == 0) return;
   const at::cuda::CUDAGuard g(part.device());
   dim3 grid((D + 31) / 32, groups);
-  reduce_partials_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-      part.data_ptr<float>(), nrows, (int)per_group, D, out.data_ptr(), out.stride(0),
-      out.scalar_type() == at::kBFloat16 ? 1 : 0, accumulate ? 1 : 0);
+  const int ob = out.scalar_type() == at::kBFloat16 ? 1 : 0, acc = accumulate ? 1 : 0;
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  // tall groups on few column blocks need more warps per block to keep loads in flight
+  if ((long)per_group >= 256 && (long)grid.x * grid.y < (long)num_sms())
+    reduce_partials_kernel<32><<<grid, 1024, 0, st>>>(part.data_ptr<float>(), nrows, (int)per_group, D,
+                                                      out.data_ptr(), out.stride(0), ob, acc);
+  else
+    reduce_partials_kernel<8><<<grid, 256, 0, st>>>(part.data_ptr<float>(), nrows, (int)per_group, D,
+                                                    out.data_ptr(), out.stride(0), ob, acc);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   count_launch();
 }
@@ -814,6 +985,35 @@ void qknorm_rope_bwd(const at::Tensor& dq, const at::Tensor& dk, const at::Tenso
   const at::cuda::CUDAGuard g(qkv.device());
   const long items = (long)R * H;
   const long grid = (items + items_per_block - 1) / items_per_block;
+  const bool vec_ok = (Dh == 64 || Dh == 72 || Dh == 80 || Dh == 96 || Dh == 128) && dq.stride(0) % 8 == 0 &&
+                      dk.stride(0) % 8 == 0 && qkv.stride(0) % 8 == 0 && dqkv.stride(0) % 8 == 0 &&
+                      reinterpret_cast<uintptr_t>(dq.data_ptr()) % 16 == 0 &&
+                      reinterpret_cast<uintptr_t>(dk.data_ptr()) % 16 == 0 &&
+                      reinterpret_cast<uintptr_t>(qkv.data_ptr()) % 16 == 0 &&
+                      reinterpret_cast<uintptr_t>(dqkv.data_ptr()) % 16 == 0 &&
+                      (!freqs.has_value() || reinterpret_cast<uintptr_t>(freqs->data_ptr()) % 16 == 0);
+  if (vec_ok) {
+    const dim3 vgrid((unsigned)grid, 2);
+#define HARP_QKB(DHV)                                                                                              \
+  qknorm_rope_bwd_vec_kernel<DHV><<<vgrid, 128, 0, at::cuda::getCurrentCUDAStream()>>>(                          \
+      bp(dq), bp(dk), dq.stride(0), dk.stride(0), bp(qkv), qkv.stride(0),                                          \
+      rstd_q.has_value() ? rstd_q->data_ptr<float>() : nullptr,                                                    \
+      rstd_k.has_value() ? rstd_k->data_ptr<float>() : nullptr, R, (int)H, bp(wq), bp(wk),                         \
+      freqs.has_value() ? reinterpret_cast<const float2*>(freqs->data_ptr<float>()) : nullptr, (int)freq_rows,     \
+      do_norm ? 1 : 0, (long)items_per_block, bpm(dqkv), dqkv.stride(0),                                           \
+      pwq.has_value() ? pwq->data_ptr<float>() : nullptr, pwk.has_value() ? pwk->data_ptr<float>() : nullptr)
+    switch (Dh) {
+      case 64: HARP_QKB(64); break;
+      case 72: HARP_QKB(72); break;
+      case 80: HARP_QKB(80); break;
+      case 96: HARP_QKB(96); break;
+      default: HARP_QKB(128); break;
+    }
+#undef HARP_QKB
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    count_launch();
+    return;
+  }
   qknorm_rope_bwd_kernel<<<grid, 256, 8 * 2 * Dh * sizeof(float), at::cuda::getCurrentCUDAStream()>>>(
       bp(dq), bp(dk), dq.stride(0), dk.stride(0), bp(qkv), qkv.stride(0),
       rstd_q.has_value() ? rstd_q->data_ptr<float>() : nullptr, rstd_k.has_value() ? rstd_k->data_ptr<float>() : nullptr,
@@ -936,6 +1136,19 @@ void adamw_flat(at::Tensor& master, at::Tensor& m, at::Tensor& v, const at::Tens
   h.bc2_sqrt = std::sqrt(1.0 - std::pow(beta2, (double)step));
   h.grad_scale = grad_scale;
   const bool gf32 = grad.scalar_type() == at::kFloat;
+  auto al = [](const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; };
+  if (n % 8 == 0 && al(master.data_ptr()) && al(m.data_ptr()) && al(v.data_ptr()) && al(grad.data_ptr()) &&
+      (!param.has_value() || al(param->data_ptr()))) {
+    const long n8 = n / 8;
+    const int vgrid = (int)std::min<long>((n8 + 255) / 256, (long)num_sms() * 8);
+    adamw_flat_vec_kernel<<<vgrid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+        master.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), gf32 ? nullptr : bp(grad),
+        gf32 ? grad.data_ptr<float>() : nullptr,
+        param.has_value() ? reinterpret_cast<bf16*>(param->data_ptr()) : nullptr, n8, h);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    count_launch();
+    return;
+  }
   const int grid = (int)std::min<long>((n + 255) / 256, 148 * 16);
   adamw_flat_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       master.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), gf32 ? nullptr : bp(grad),

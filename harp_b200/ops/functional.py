@@ -296,12 +296,23 @@ def qknorm_rope_fwd(qkv: torch.Tensor, H: int, Dh: int, wq, wk, freqs: Optional[
     return qo, ko, rq, rk
 
 
+_SMS = {}
+
+
+def _num_sms(device) -> int:
+    idx = torch.device(device).index or 0
+    if idx not in _SMS:
+        _SMS[idx] = torch.cuda.get_device_properties(idx).multi_processor_count
+    return _SMS[idx]
+
+
 def qknorm_rope_bwd(dq, dk, qkv, rq, rk, H, Dh, wq, wk, freqs, do_norm, dqkv, want_dw=True):
     """Writes d(q_pre), d(k_pre) into dqkv[:, :2*H*Dh]; returns (dwq, dwk) fp32 or None."""
     R = qkv.shape[0]
     frows = freqs.shape[0] if freqs is not None else 1
     if _cuda(qkv):
-        ipb = 64
+        # about 4 blocks per SM, each thread striding over ~ipb/128 (row, head) items
+        ipb = max(128, -(-R * H // (4 * _num_sms(qkv.device))))
         nblk = (R * H + ipb - 1) // ipb
         want = want_dw and do_norm and wq is not None
         pwq = torch.empty(nblk, Dh, device=qkv.device) if want else None

@@ -243,6 +243,31 @@ def test_adamw_flat_matches_torch():
     assert torch.allclose(master, pref.detach(), atol=1e-6, rtol=1e-5)
 
 
+@pytest.mark.parametrize("gdtype", [torch.float32, torch.bfloat16])
+def test_adamw_flat_vector_path_matches_scalar_path(gdtype):
+    """n % 8 == 0 with aligned buffers takes the 16-byte vector kernel; it must
+    agree with the element-wise kernel to a few ulp (same per-element math, the
+    compiler may contract multiply-adds differently)."""
+    n = 8 * 12531
+    p0 = torch.randn(n, device="cuda")
+    g = torch.randn(n, device="cuda").to(gdtype)
+    states = []
+    for length in (n, n + 1):  # n + 1: element-wise kernel on a buffer that is not a multiple of 8
+        master = torch.zeros(length, device="cuda")
+        master[:n] = p0
+        m, v = torch.zeros_like(master), torch.zeros_like(master)
+        gg = torch.zeros(length, device="cuda", dtype=gdtype)
+        gg[:n] = g
+        param = torch.empty(length, device="cuda", dtype=torch.bfloat16)
+        for step in range(1, 4):
+            torch.ops.harp.adamw_flat(master, m, v, gg, param, 1e-3, 0.9, 0.999, 1e-8, 0.01, step, 0.5)
+        states.append((master[:n].clone(), m[:n].clone(), v[:n].clone(), param[:n].clone()))
+    for a, b in zip(states[0][:3], states[1][:3]):
+        torch.testing.assert_close(a, b, rtol=4e-6, atol=1e-7)
+    torch.testing.assert_close(states[0][3].float(), states[1][3].float(), rtol=2 ** -7, atol=0.0)
+    torch.testing.assert_close(states[0][3], states[0][0].to(torch.bfloat16))
+
+
 def test_philox_uniform_range_and_determinism():
     a = torch.empty(100003, device="cuda")
     b = torch.empty(100003, device="cuda")
@@ -271,3 +296,43 @@ def test_compat_linear_ops():
     assert (gi.float().view(-1, 256) - gf @ w.float()).abs().max() < 0.5
     assert (gw.float() - gf.t() @ x.float().view(-1, 256)).abs().max() < 2.0
     assert (gb.float() - gf.sum(0)).abs().max() < 0.5
+
+
+@pytest.mark.parametrize("Dh,strided", [(72, False), (128, False), (64, True), (48, False)])
+def test_qknorm_rope_bwd_paths_match_autograd(Dh, strided):
+    """The functional wrapper: vectorized kernel for head_dim 64/72/80/96/128 with
+    16-byte aligned rows (strided dq/dk views of a wider buffer included), the
+    warp-per-item kernel otherwise; in-place use (dq aliasing the output) too."""
+    from harp_b200.ops import functional as Fn
+
+    R, H, eps = 300, 4, 1e-6
+    HD = H * Dh
+    qkv = torch.randn(R, 3 * HD, device="cuda").to(torch.bfloat16)
+    wq = (torch.rand(Dh, device="cuda") + 0.5).to(torch.bfloat16)
+    wk = (torch.rand(Dh, device="cuda") + 0.5).to(torch.bfloat16)
+    ang = torch.rand(R, Dh // 2, device="cuda") * 6.0
+    freqs = torch.stack([ang.cos(), ang.sin()], -1).contiguous()
+    q, k, rq, rk = Fn.qknorm_rope_fwd(qkv, H, Dh, wq, wk, freqs, eps)
+    if strided:
+        g = torch.randn(R, 3 * HD, device="cuda").to(torch.bfloat16)
+        dq, dk = g[:, :HD], g[:, HD:2 * HD]
+        out = g  # in place: the gradient buffer is the output buffer
+    else:
+        dq, dk = torch.randn_like(q), torch.randn_like(k)
+        out = torch.zeros_like(qkv)
+    dq_ref, dk_ref = dq.float().clone(), dk.float().clone()
+    dwq, dwk = Fn.qknorm_rope_bwd(dq, dk, qkv, rq, rk, H, Dh, wq, wk, freqs, True, out)
+
+    def ref(xpart, w):
+        xr = xpart.view(R, H, Dh)
+        n = xr * torch.rsqrt(xr.pow(2).mean(-1, keepdim=True) + eps) * w
+        return _rope_ref(n, ang.cos()[:, None], ang.sin()[:, None]).reshape(R, HD)
+
+    q_in = qkv[:, :HD].float().requires_grad_()
+    k_in = qkv[:, HD:2 * HD].float().requires_grad_()
+    wqr, wkr = wq.float().requires_grad_(), wk.float().requires_grad_()
+    (ref(q_in, wqr) * dq_ref).sum().add((ref(k_in, wkr) * dk_ref).sum()).backward()
+    assert (out[:, :HD].float() - q_in.grad).abs().max() < 0.05
+    assert (out[:, HD:2 * HD].float() - k_in.grad).abs().max() < 0.05
+    torch.testing.assert_close(dwq, wqr.grad, atol=0.3, rtol=2e-2)
+    torch.testing.assert_close(dwk, wkr.grad, atol=0.3, rtol=2e-2)

@@ -200,3 +200,23 @@ def test_scheduler_inference_grid():
     d = FS(use_dynamic_shifting=True)
     d.set_timesteps(4, mu=1.0)
     assert torch.all(d.sigmas[:-1][1:] < d.sigmas[:-1][:-1])
+
+
+def test_ring_attention_ops_match_sdpa():
+    from harp_b200.ops import ring_ops
+
+    ring_ops.set_sp_context(None)
+    g = torch.Generator().manual_seed(3)
+    B, T, H, D = 1, 24, 2, 16
+    q, k, v = (torch.randn(B, T, H, D, generator=g).bfloat16().transpose(1, 2).requires_grad_(True) for _ in range(3))
+    out = ring_ops.CPURingAttention.apply(q, k, v, 1)
+    do = torch.randn_like(out)
+    out.backward(do)
+    qr, kr, vr = (t.detach().float().requires_grad_(True) for t in (q, k, v))
+    ref = F.scaled_dot_product_attention(qr, kr, vr)
+    ref.backward(do.float())
+    torch.testing.assert_close(out.float(), ref, rtol=2e-2, atol=2e-2)
+    for a, b in ((q, qr), (k, kr), (v, vr)):
+        torch.testing.assert_close(a.grad.float(), b.grad, rtol=5e-2, atol=5e-2)
+    with pytest.raises(RuntimeError):
+        ring_ops.CPURingAttention.apply(q, k, v, 2)
