@@ -71,12 +71,30 @@ __device__ __forceinline__ void tma_reduce_add_4d(const CUtensorMap* map, const 
 }
 __device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// every bulk group but the most recent one has finished reading its source
+__device__ __forceinline__ void bulk_wait_read_one_pending() {
+  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
 __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity) {
   const unsigned long long t0 = globaltimer_ns();
   while (!mbar_try_wait(bar, parity))
     if (globaltimer_ns() - t0 > 1000000000ull) return false;
   return true;
 }
+// One 128-row strip-major tile (NCH strips of 8 elements): a single 5-D TMA
+// when the map is the (8, row, strip, head, batch) form, else one 4-D TMA per
+// strip.  Either way NCH * 2048 bytes arrive on `bar`.
+template <int NCH>
+__device__ __forceinline__ void load_strip_tile(uint8_t* dst, const CUtensorMap* map, uint64_t* bar, int row0, int h,
+                                                int b, int one_shot) {
+  if (one_shot) {
+    tma_load_5d(dst, map, bar, 0, row0, 0, h, b);
+  } else {
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) tma_load_4d(dst + c * 2048, map, bar, c * 8, h, row0, b);
+  }
+}
+
 __device__ __forceinline__ uint64_t kmajor_desc(uint32_t tile_addr, int ks) {
   // K-major (head dim is the reduction): next 8-row group at +128 B,
   // next 8-element strip at +2048 B; a 16-wide k-step spans two strips.
@@ -103,6 +121,7 @@ struct FwdArgs {
   int chunk_len;
   int start_tile;
   unsigned int epoch;
+  int strip5;  // tensor maps are the one-instruction 5-D strip form
   int wait_q;  // queries arrive by chunk too (same flags): wait before loading a Q tile
   int q_rot;   // query-pair index rotation (start with the pairs whose chunk is local)
   unsigned long long timeout_ns;
@@ -192,9 +211,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         fence_proxy_async_global();
       }
       mbar_arrive_expect_tx(q_full, ntile * C::TILE);
-      for (int t = 0; t < ntile; ++t)
-#pragma unroll
-        for (int c = 0; c < NCH; ++c) tma_load_4d(sQ + t * C::TILE + c * 2048, &tmQ, q_full, c * 8, h, q0 + 128 * t, b);
+      for (int t = 0; t < ntile; ++t) load_strip_tile<NCH>(sQ + t * C::TILE, &tmQ, q_full, q0 + 128 * t, h, b, a.strip5);
       for (int jj = 0; jj < nkv && ok; ++jj) {
         const int j = (a.start_tile + jj) % nkv;
         const int key0 = j * 128;
@@ -209,13 +226,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         const uint32_t ph = (jj / ST) & 1;
         if (!mbar_wait(&k_empty[st], ph ^ 1, err, 21)) { ok = false; break; }
         mbar_arrive_expect_tx(&k_full[st], C::TILE);
-#pragma unroll
-        for (int c = 0; c < NCH; ++c) tma_load_4d(sK + st * C::TILE + c * 2048, &tmK, &k_full[st], c * 8, h, key0, b);
+        load_strip_tile<NCH>(sK + st * C::TILE, &tmK, &k_full[st], key0, h, b, a.strip5);
         issued_k[st]++;
         if (!mbar_wait(&v_empty[st], ph ^ 1, err, 22)) { ok = false; break; }
         mbar_arrive_expect_tx(&v_full[st], C::TILE);
-#pragma unroll
-        for (int c = 0; c < NCH; ++c) tma_load_4d(sV + st * C::TILE + c * 2048, &tmV, &v_full[st], c * 8, h, key0, b);
+        load_strip_tile<NCH>(sV + st * C::TILE, &tmV, &v_full[st], key0, h, b, a.strip5);
         issued_v[st]++;
       }
       mbar_wait_drain(q_full, 0);
@@ -410,22 +425,37 @@ struct BwdArgs {
   const float* lse;    // [B, H, lse_ld] natural log; +inf past Sq
   const float* delta;  // [B, H, lse_ld]; 0 past Sq
   int lse_ld;
-  float* dq_acc;  // [(b*Sq+s)*H + h][Dh]
+  float* dq_acc;  // [b][h][s][Dh]: one contiguous slab per (batch, head)
   bf16* dK;
   long lddk;
   bf16* dV;
   long lddv;
   int* err;
+  int probe;  // record phase timestamps of CTA 0 into g_bwd_probe (HARP_ATTN_PROBE=1)
+  int strip5;  // tensor maps are the one-instruction 5-D strip form
+  int skip_dq;  // HARP_ATTN_DEBUG_SKIP_DQ=1: leave dQ out (timing experiments; dQ is then wrong)
 };
+
+// Phase timeline of one CTA of the backward kernels: 64 query tiles x 16
+// slots of %globaltimer values, read back with attn_bwd_probe().
+__device__ unsigned long long g_bwd_probe[64 * 16];
+#define BWD_PROBE(i, slot)                                                                              \
+  do {                                                                                                  \
+    if (a.probe && blockIdx.x == 0 && (i) < 64) g_bwd_probe[(i) * 16 + (slot)] = globaltimer_ns();    \
+  } while (0)
 
 template <int NCH>
 struct BwdCfg {
   static constexpr int DPAD = NCH * 8;
   static constexpr int TILE = NCH * 2048;
-  static constexpr int STAGES = 2;
   static constexpr int DS_BYTES = 128 * 128 * 2;
   static constexpr int LD_BYTES = 256 * 4;  // per stage: 128 lse + 128 delta
-  static constexpr int SMEM = 2 * TILE + STAGES * 2 * TILE + DS_BYTES + STAGES * LD_BYTES + 128 + 256;
+  static constexpr int smem_for(int st) { return 2 * TILE + st * 2 * TILE + DS_BYTES + st * LD_BYTES + 128 + 256; }
+  // Q/dO(+lse/delta) stages: a stage is refilled only after the dQ partial that
+  // is staged in it has been read by its TMA reduce, so a third stage keeps the
+  // loads two tiles ahead wherever shared memory allows it.
+  static constexpr int STAGES = smem_for(3) <= 232448 ? 3 : 2;
+  static constexpr int SMEM = smem_for(STAGES);
   static_assert(SMEM <= 232448, "exceeds the 227 KB per-CTA shared memory limit");
   static_assert(2 * TILE >= 128 * DPAD * 4, "dQ staging (128 x Dh fp32) must fit in one Q/dO stage");
   static constexpr int DV_COL = 256;
@@ -503,27 +533,22 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
       tma_prefetch_desc(&tmdO);
-      int issued[2] = {0, 0};
+      int issued[4] = {0, 0, 0, 0};
       bool ok = true;
       mbar_arrive_expect_tx(kv_full, 2 * C::TILE);
-#pragma unroll
-      for (int c = 0; c < NCH; ++c) {
-        tma_load_4d(sK + c * 2048, &tmK, kv_full, c * 8, h, k0, b);
-        tma_load_4d(sV + c * 2048, &tmV, kv_full, c * 8, h, k0, b);
-      }
+      load_strip_tile<NCH>(sK, &tmK, kv_full, k0, h, b, a.strip5);
+      load_strip_tile<NCH>(sV, &tmV, kv_full, k0, h, b, a.strip5);
       for (int i = 0; i < nq && ok; ++i) {
         const int st = i % ST;
         const uint32_t ph = (i / ST) & 1;
         if (!mbar_wait(&qdo_empty[st], ph ^ 1, err, 50)) { ok = false; break; }
+        BWD_PROBE(i, 10);
         mbar_arrive_expect_tx(&qdo_full[st], 2 * C::TILE + C::LD_BYTES);
         const long lrow = (long)(b * a.H + h) * a.lse_ld + i * 128;
         bulk_load(sLD + st * 256, a.lse + lrow, 512, &qdo_full[st]);
         bulk_load(sLD + st * 256 + 128, a.delta + lrow, 512, &qdo_full[st]);
-#pragma unroll
-        for (int c = 0; c < NCH; ++c) {
-          tma_load_4d(sQD + 2 * st * C::TILE + c * 2048, &tmQ, &qdo_full[st], c * 8, h, i * 128, b);
-          tma_load_4d(sQD + (2 * st + 1) * C::TILE + c * 2048, &tmdO, &qdo_full[st], c * 8, h, i * 128, b);
-        }
+        load_strip_tile<NCH>(sQD + 2 * st * C::TILE, &tmQ, &qdo_full[st], i * 128, h, b, a.strip5);
+        load_strip_tile<NCH>(sQD + (2 * st + 1) * C::TILE, &tmdO, &qdo_full[st], i * 128, h, b, a.strip5);
         issued[st]++;
       }
       mbar_wait_drain(kv_full, 0);
@@ -553,7 +578,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         for (int ks = 0; ks < NCH / 2; ++ks)
           mma_ss(tdP, kmajor_desc(va, ks), kmajor_desc(doa, ks), idS, ks > 0 ? 1u : 0u);
         mma_commit(s_full);
+        BWD_PROBE(i, 0);
         if (!mbar_wait(p_full, i & 1, err, 63)) { ok = false; break; }
+        BWD_PROBE(i, 1);
         tc_fence_after();
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks)
@@ -569,6 +596,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         for (int ks = 0; ks < 8; ++ks)
           mma_ss(tdQ, mnmajor_desc(dsa, ks), mnmajor_desc(ka, ks), idQ, ks > 0 ? 1u : 0u);
         mma_commit(dq_full);  // also frees Q_i/dO_i: the dQ warps hand the stage back
+        BWD_PROBE(i, 3);
       }
       mma_commit(fin);
       mbar_wait_drain(fin, 0);
@@ -583,6 +611,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     bool ok = true;
     for (int i = 0; i < nq; ++i) {
       if (!mbar_wait(s_full, i & 1, err, 70)) { ok = false; break; }
+      if (warp == 2 && lane == 0) BWD_PROBE(i, 4);
       tc_fence_after();
       const float* sL = sLD + (i % ST) * 256;  // lse of the 128 queries of tile i (+inf past Sq)
       const float* sDl = sL + 128;              // delta (0 past Sq)
@@ -627,6 +656,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
+      if (warp == 2 && lane == 0) BWD_PROBE(i, 5);
       if (lane == 0) mbar_arrive(p_full);
     }
     if (ok) ok = mbar_wait(fin, 0, err, 71);
@@ -660,6 +690,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     bool ok = true;
     for (int i = 0; i < nq; ++i) {
       if (!mbar_wait(dq_full, i & 1, err, 80)) { ok = false; break; }
+      if (warp == 6 && lane == 0) BWD_PROBE(i, 6);
       tc_fence_after();
       const int st = i % ST;
       float* stage = reinterpret_cast<float*>(sQD + 2 * st * C::TILE);  // [128][Dh] fp32 staging
@@ -690,8 +721,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         // [128 x Dh] tile into dq_acc (rows past Sq are clipped by TMA), then
         // give the stage back to the TMA producer.
         if (!mbar_wait(dqs_bar, i & 1, err, 82)) { ok = false; break; }
+        BWD_PROBE(i, 7);
         tma_reduce_add_4d(&tmdQ, stage, 0, h, i * 128, b);
         bulk_wait_read_all();
+        BWD_PROBE(i, 9);
         mbar_arrive(&qdo_empty[st]);
       }
     }
@@ -730,16 +763,335 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   }
 }
 
-// dQ = scale * dq_acc  (fp32 [R*H, Dh] -> bf16 [R, ld] token-major)
-__global__ void dq_finalize_kernel(const float* __restrict__ acc, int R, int H, int Dh, float scale,
+// ===========================================================================
+// Backward, overlapped schedule (head_dim <= 80, where dQ has TMEM columns of
+// its own).  Same data flow as attn_bwd_kernel, but every 128-query tile is
+// handled as two 64-query halves:
+//   * S^T / dP^T of each half are committed separately; the dS warps (w2-5)
+//     turn half 0 into P^T / dS^T while the dQ warps (w6-9) take half 1, so
+//     twice as many threads share the softmax-gradient work;
+//   * the MMA warp issues dV/dK for a half as soon as that half is ready, and
+//     issues the next tile's S/dP for half 0 ahead of this tile's dQ = dS K, so
+//     the tensor pipe keeps working while the warps compute.
+// Orderings that replace the single-tile barriers:
+//   - the next tile's S/dP overwrite TMEM columns whose previous readers (the
+//     half warps' loads, this tile's dV/dK MMAs) finished or were issued
+//     earlier on the in-order tensor pipe;
+//   - dS of tile i+1 is stored to shared memory only after dQ(i) (which reads
+//     it) completed: half-0 warps wait on dq_full(i) first, half-1 warps have
+//     already waited on it to read dQ(i) out;
+//   - dQ(i+1) overwrites the dQ columns only after p_full1(i+1), which the
+//     half-1 warps signal after their dQ(i) readout.
+// ===========================================================================
+template <int NCH>
+__global__ void __launch_bounds__(kBwdThreads, 1)
+    attn_bwd_ov_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                       const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
+                       const __grid_constant__ CUtensorMap tmdQ, const BwdArgs a) {
+  using C = BwdCfg<NCH>;
+  static_assert(C::DQ_SEPARATE, "overlapped backward needs dQ columns of its own");
+  constexpr int ST = C::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+  uint8_t* sK = smem;
+  uint8_t* sV = sK + C::TILE;
+  uint8_t* sQD = sV + C::TILE;
+  uint8_t* sdS = sQD + 2 * ST * C::TILE;
+  float* sLD = reinterpret_cast<float*>(sdS + C::DS_BYTES);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sdS + C::DS_BYTES + ST * C::LD_BYTES);
+  uint64_t* kv_full = bars;
+  uint64_t* qdo_full = bars + 1;        // [ST]
+  uint64_t* qdo_empty = qdo_full + ST;  // [ST]
+  uint64_t* s_full = qdo_empty + ST;    // [2] per half
+  uint64_t* p_full = s_full + 2;        // [2] per half, 4 arrivals each
+  uint64_t* dq_full = p_full + 2;
+  uint64_t* fin = dq_full + 1;
+  uint64_t* dqs_bar = fin + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(dqs_bar + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int nkt = (a.Skv + 127) / 128;
+  const int bh = blockIdx.x / nkt, kt = blockIdx.x % nkt;
+  const int b = bh / a.H, h = bh % a.H;
+  const int k0 = kt * 128;
+  const int nq = (a.Sq + 127) / 128;
+  int* err = a.err;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(&qdo_full[s], 1);
+      mbar_init(&qdo_empty[s], 1);
+    }
+    for (int hf = 0; hf < 2; ++hf) {
+      mbar_init(&s_full[hf], 1);
+      mbar_init(&p_full[hf], 4);
+    }
+    mbar_init(dq_full, 1);
+    mbar_init(fin, 1);
+    mbar_init(dqs_bar, 4);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS = tmem, tdP = tmem + 128, tdV = tmem + C::DV_COL, tdK = tmem + C::DK_COL,
+                 tdQ = tmem + C::DQ_COL;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      tma_prefetch_desc(&tmdO);
+      int issued[4] = {0, 0, 0, 0};
+      bool ok = true;
+      mbar_arrive_expect_tx(kv_full, 2 * C::TILE);
+      load_strip_tile<NCH>(sK, &tmK, kv_full, k0, h, b, a.strip5);
+      load_strip_tile<NCH>(sV, &tmV, kv_full, k0, h, b, a.strip5);
+      for (int i = 0; i < nq && ok; ++i) {
+        const int st = i % ST;
+        const uint32_t ph = (i / ST) & 1;
+        if (!mbar_wait(&qdo_empty[st], ph ^ 1, err, 50)) { ok = false; break; }
+        BWD_PROBE(i, 10);
+        mbar_arrive_expect_tx(&qdo_full[st], 2 * C::TILE + C::LD_BYTES);
+        const long lrow = (long)(b * a.H + h) * a.lse_ld + i * 128;
+        bulk_load(sLD + st * 256, a.lse + lrow, 512, &qdo_full[st]);
+        bulk_load(sLD + st * 256 + 128, a.delta + lrow, 512, &qdo_full[st]);
+        load_strip_tile<NCH>(sQD + 2 * st * C::TILE, &tmQ, &qdo_full[st], i * 128, h, b, a.strip5);
+        load_strip_tile<NCH>(sQD + (2 * st + 1) * C::TILE, &tmdO, &qdo_full[st], i * 128, h, b, a.strip5);
+        issued[st]++;
+      }
+      mbar_wait_drain(kv_full, 0);
+      for (int s = 0; s < ST; ++s)
+        if (issued[s]) mbar_wait_drain(&qdo_full[s], (issued[s] - 1) & 1);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idS = make_idesc_bf16(128, 64, false, false);
+      constexpr uint32_t idO = make_idesc_bf16(128, C::DPAD, false, true);
+      constexpr uint32_t idQ = make_idesc_bf16(128, C::DPAD, true, true);
+      const uint32_t ka = smem_u32(sK), va = smem_u32(sV), dsa = smem_u32(sdS);
+      // S^T, dP^T of query half hf of tile i (keys as TMEM lanes, 64 query columns)
+      auto issue_sdp = [&](int i, int hf) {
+        const int st = i % ST;
+        const uint32_t qa = smem_u32(sQD + 2 * st * C::TILE) + hf * 1024;
+        const uint32_t doa = smem_u32(sQD + (2 * st + 1) * C::TILE) + hf * 1024;
+#pragma unroll
+        for (int ks = 0; ks < NCH / 2; ++ks)
+          mma_ss(tS + 64 * hf, kmajor_desc(ka, ks), kmajor_desc(qa, ks), idS, ks > 0 ? 1u : 0u);
+#pragma unroll
+        for (int ks = 0; ks < NCH / 2; ++ks)
+          mma_ss(tdP + 64 * hf, kmajor_desc(va, ks), kmajor_desc(doa, ks), idS, ks > 0 ? 1u : 0u);
+        mma_commit(&s_full[hf]);
+      };
+      // dV += P^T dO and dK += dS^T Q over the 64 queries of half hf (packed
+      // bf16 P^T / dS^T at columns 64*hf .. 64*hf + 31)
+      auto issue_dvdk = [&](int i, int hf) {
+        const int st = i % ST;
+        const uint32_t qa = smem_u32(sQD + 2 * st * C::TILE), doa = smem_u32(sQD + (2 * st + 1) * C::TILE);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const int ks = 4 * hf + kk;
+          mma_ts(tdV, tS + 64 * hf + kk * 8, mnmajor_desc(doa, ks), idO, (i > 0 || ks > 0) ? 1u : 0u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const int ks = 4 * hf + kk;
+          mma_ts(tdK, tdP + 64 * hf + kk * 8, mnmajor_desc(qa, ks), idO, (i > 0 || ks > 0) ? 1u : 0u);
+        }
+      };
+      bool ok = mbar_wait(kv_full, 0, err, 60) && mbar_wait(&qdo_full[0], 0, err, 61);
+      if (ok) {
+        tc_fence_after();
+        issue_sdp(0, 0);
+        issue_sdp(0, 1);
+      }
+      for (int i = 0; i < nq && ok; ++i) {
+        BWD_PROBE(i, 0);
+        if (!mbar_wait(&p_full[0], i & 1, err, 63)) { ok = false; break; }
+        BWD_PROBE(i, 1);
+        tc_fence_after();
+        issue_dvdk(i, 0);
+        if (!mbar_wait(&p_full[1], i & 1, err, 64)) { ok = false; break; }
+        BWD_PROBE(i, 2);
+        tc_fence_after();
+        issue_dvdk(i, 1);
+        const bool more = i + 1 < nq;
+        if (more) {
+          if (!mbar_wait(&qdo_full[(i + 1) % ST], ((i + 1) / ST) & 1, err, 65)) { ok = false; break; }
+          tc_fence_after();
+          issue_sdp(i + 1, 0);
+        }
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks)
+          mma_ss(tdQ, mnmajor_desc(dsa, ks), mnmajor_desc(ka, ks), idQ, ks > 0 ? 1u : 0u);
+        mma_commit(dq_full);
+        BWD_PROBE(i, 3);
+        if (more) issue_sdp(i + 1, 1);
+      }
+      mma_commit(fin);
+      mbar_wait_drain(fin, 0);
+    }
+  } else {
+    // ---------------- w2-5: half 0 (queries 0-63); w6-9: half 1 (64-127) ----------------
+    const int hf = warp >= 6 ? 1 : 0;
+    const int quarter = warp & 3;
+    const int kr = quarter * 32 + lane;
+    const int key = k0 + kr;
+    const bool key_ok = key < a.Skv;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    bool ok = true;
+    for (int i = 0; i < nq && ok; ++i) {
+      if (!mbar_wait(&s_full[hf], i & 1, err, 70 + hf)) { ok = false; break; }
+      if ((warp == 2 || warp == 6) && lane == 0) BWD_PROBE(i, hf ? 6 : 4);
+      tc_fence_after();
+      const int st = i % ST;
+      const float* sL = sLD + st * 256;  // lse of the tile's 128 queries (+inf past Sq)
+      const float* sDl = sL + 128;        // delta (0 past Sq)
+      const float2 scl = make_float2(a.scale_log2, a.scale_log2);
+      const float2 kmask = make_float2(key_ok ? 1.f : 0.f, key_ok ? 1.f : 0.f);
+      const float2 nl2e = make_float2(-kLog2e, -kLog2e);
+#pragma unroll 1
+      for (int cc = 0; cc < 2; ++cc) {
+        const int c = 2 * hf + cc;  // 32-query chunk of the tile
+        uint32_t s[32], dp[32];
+        tmem_ld32(tS + lane_off + c * 32, s);
+        tmem_ld32(tdP + lane_off + c * 32, dp);
+        tmem_wait_ld();
+        uint32_t pp[16], dd[16];
+#pragma unroll
+        for (int k4 = 0; k4 < 8; ++k4) {
+          const float4 L4 = *reinterpret_cast<const float4*>(sL + c * 32 + 4 * k4);
+          const float4 D4 = *reinterpret_cast<const float4*>(sDl + c * 32 + 4 * k4);
+#pragma unroll
+          for (int h2 = 0; h2 < 2; ++h2) {
+            const int k2 = 2 * k4 + h2;
+            const float2 Lp = h2 ? make_float2(L4.z, L4.w) : make_float2(L4.x, L4.y);
+            const float2 Dp = h2 ? make_float2(D4.z, D4.w) : make_float2(D4.x, D4.y);
+            const float2 x = __ffma2_rn(make_float2(__uint_as_float(s[2 * k2]), __uint_as_float(s[2 * k2 + 1])), scl,
+                                        __fmul2_rn(Lp, nl2e));
+            const float2 p = __fmul2_rn(make_float2(ex2_approx(x.x), ex2_approx(x.y)), kmask);
+            const float2 ds = __fmul2_rn(
+                p, __fadd2_rn(make_float2(__uint_as_float(dp[2 * k2]), __uint_as_float(dp[2 * k2 + 1])),
+                              make_float2(-Dp.x, -Dp.y)));
+            pp[k2] = pack_bf16x2(p.x, p.y);
+            dd[k2] = pack_bf16x2(ds.x, ds.y);
+          }
+        }
+        // packed bf16 P^T / dS^T of this half start at column 64*hf
+        tmem_st16(tS + lane_off + 64 * hf + cc * 16, pp);
+        tmem_st16(tdP + lane_off + 64 * hf + cc * 16, dd);
+        if (cc == 0 && hf == 0 && i > 0) {
+          // dQ(i-1) reads the dS tile in shared memory: it must be done first
+          if (!mbar_wait(dq_full, (i - 1) & 1, err, 72)) { ok = false; break; }
+        }
+#pragma unroll
+        for (int g = 0; g < 4; ++g)
+          *reinterpret_cast<uint4*>(sdS + (c * 4 + g) * 2048 + kr * 16) =
+              make_uint4(dd[4 * g], dd[4 * g + 1], dd[4 * g + 2], dd[4 * g + 3]);
+      }
+      if (!ok) break;
+      tmem_wait_st();
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if ((warp == 2 || warp == 6) && lane == 0) BWD_PROBE(i, hf ? 7 : 5);
+      if (lane == 0) mbar_arrive(&p_full[hf]);
+      if (hf == 1) {
+        // read dQ(i) out of TMEM into the tile's Q/dO stage (fp32 staging) and
+        // reduce-add it into dq_acc with one TMA; then give the stage back
+        if (!mbar_wait(dq_full, i & 1, err, 80)) { ok = false; break; }
+        if (warp == 6 && lane == 0) BWD_PROBE(i, 8);
+        tc_fence_after();
+        const int qr = kr;
+        float* stage = reinterpret_cast<float*>(sQD + 2 * st * C::TILE);
+        float* srow = stage + qr * a.Dh;
+        {
+          uint32_t v[C::DPAD];  // all dQ columns of this row, one TMEM wait
+#pragma unroll
+          for (int c = 0; c < C::DPAD; c += 16)
+            tmem_ld16(tdQ + lane_off + c, *reinterpret_cast<uint32_t(*)[16]>(v + c));
+          tmem_wait_ld();
+#pragma unroll
+          for (int d = 0; d < C::DPAD; d += 4)
+            if (d < a.Dh)
+              *reinterpret_cast<float4*>(srow + d) = make_float4(__uint_as_float(v[d]), __uint_as_float(v[d + 1]),
+                                                                 __uint_as_float(v[d + 2]), __uint_as_float(v[d + 3]));
+        }
+        tc_fence_before();
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(dqs_bar);
+        if (warp == 6 && lane == 0) {
+          // issue the reduce-add of this tile and move on; the stage of the
+          // previous tile goes back to the producer once its reduce has read it
+          if (!mbar_wait(dqs_bar, i & 1, err, 82)) { ok = false; break; }
+          if (!a.skip_dq) tma_reduce_add_4d(&tmdQ, stage, 0, h, i * 128, b);
+          if (i > 0) {
+            bulk_wait_read_one_pending();
+            mbar_arrive(&qdo_empty[(i - 1) % ST]);
+          }
+          BWD_PROBE(i, 9);
+        }
+      }
+    }
+    if (warp == 6 && lane == 0) bulk_wait_all();
+    if (ok) ok = mbar_wait(fin, 0, err, 81);
+    tc_fence_after();
+    // half-0 warps write dV, half-1 warps write dK (scaled) for their key rows
+    const float mul = hf ? a.scale : 1.f;
+    const uint32_t tsrc = hf ? tdK : tdV;
+    bf16* orow = hf ? a.dK + (long)(b * a.Skv + key) * a.lddk + h * a.Dh
+                    : a.dV + (long)(b * a.Skv + key) * a.lddv + h * a.Dh;
+#pragma unroll
+    for (int c = 0; c < C::DPAD; c += 16) {
+      uint32_t v[16];
+      tmem_ld16(tsrc + lane_off + c, v);
+      tmem_wait_ld();
+      if (key_ok && ok) {
+#pragma unroll
+        for (int g = 0; g < 2; ++g) {
+          const int d = c + 8 * g;
+          if (d < a.Dh) {
+            uint4 pk;
+            pk.x = pack_bf16x2(__uint_as_float(v[8 * g + 0]) * mul, __uint_as_float(v[8 * g + 1]) * mul);
+            pk.y = pack_bf16x2(__uint_as_float(v[8 * g + 2]) * mul, __uint_as_float(v[8 * g + 3]) * mul);
+            pk.z = pack_bf16x2(__uint_as_float(v[8 * g + 4]) * mul, __uint_as_float(v[8 * g + 5]) * mul);
+            pk.w = pack_bf16x2(__uint_as_float(v[8 * g + 6]) * mul, __uint_as_float(v[8 * g + 7]) * mul);
+            *reinterpret_cast<uint4*>(orow + d) = pk;
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// dQ = scale * dq_acc  (fp32 [B][H][Sq][Dh] -> bf16 [B*Sq, ld] token-major)
+__global__ void dq_finalize_kernel(const float* __restrict__ acc, int B, int Sq, int H, int Dh, float scale,
                                    bf16* __restrict__ out, long ldo) {
   const long i = ((long)blockIdx.x * blockDim.x + threadIdx.x) * 4;
-  const long total = (long)R * H * Dh;
+  const long total = (long)B * H * Sq * Dh;
   if (i >= total) return;
   const float4 v = *reinterpret_cast<const float4*>(acc + i);
-  const long row = i / ((long)H * Dh);
-  const long col = i % ((long)H * Dh);
-  bf16* o = out + row * ldo + col;
+  const int d = (int)(i % Dh);
+  const long r = i / Dh;  // (b*H + h)*Sq + s
+  const int s = (int)(r % Sq);
+  const long bh = r / Sq;
+  const int h = (int)(bh % H), b = (int)(bh / H);
+  bf16* o = out + ((long)b * Sq + s) * ldo + (long)h * Dh + d;
   *reinterpret_cast<uint2*>(o) = make_uint2(pack_bf16x2(v.x * scale, v.y * scale), pack_bf16x2(v.z * scale, v.w * scale));
 }
 
@@ -768,18 +1120,45 @@ void launch_fwd(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap&
   count_launch();
 }
 
+// HARP_ATTN_STRIP5=0 loads strip tiles with one 4-D TMA per strip (comparisons).
+bool strip5_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("HARP_ATTN_STRIP5");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+// HARP_ATTN_BWD_OVERLAP=1 selects the half-tile overlapped schedule.  Measured
+// on B200 (DiT-XL/2 shapes) it is slower than the single-tile schedule: the
+// P/dS work is bound by the SM's exp and FMA throughput, so splitting it over
+// twice the warps does not shorten it, and the dQ read-out lands on the
+// critical path.  Kept for further work on the schedule.
+bool bwd_overlap_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("HARP_ATTN_BWD_OVERLAP");
+    return e && e[0] == '1';
+  }();
+  return on;
+}
+
 template <int NCH>
 void launch_bwd(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mdo,
                 const CUtensorMap& mdq, const BwdArgs& args, cudaStream_t stream) {
   using C = BwdCfg<NCH>;
-  static bool configured = false;
-  if (!configured) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_kernel<NCH>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
-    configured = true;
+  auto* kern = attn_bwd_kernel<NCH>;
+  if constexpr (C::DQ_SEPARATE) {
+    if (bwd_overlap_enabled()) kern = attn_bwd_ov_kernel<NCH>;
+  }
+  static bool configured[2] = {false, false};
+  const int which = kern == attn_bwd_kernel<NCH> ? 0 : 1;
+  if (!configured[which]) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    configured[which] = true;
   }
   const int nkt = (args.Skv + 127) / 128;
   const int grid = args.B * args.H * nkt;
-  attn_bwd_kernel<NCH><<<grid, kBwdThreads, C::SMEM, stream>>>(mq, mk, mv, mdo, mdq, args);
+  kern<<<grid, kBwdThreads, C::SMEM, stream>>>(mq, mk, mv, mdo, mdq, args);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   count_launch();
 }
@@ -805,10 +1184,17 @@ void attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, int
   TORCH_CHECK(Skv > 0, "attn_fwd: empty key sequence");
   const at::cuda::CUDAGuard guard(q.device());
   const int nch = nch_for((int)Dh);
-  CUtensorMap mq = make_strip_map(q.data_ptr(), B, Sq, q.stride(0), H, Dh, 128);
-  CUtensorMap mk = make_strip_map(k.data_ptr(), B, Skv, k.stride(0), H, Dh, 128);
-  CUtensorMap mv = make_strip_map(v.data_ptr(), B, Skv, v.stride(0), H, Dh, 128);
+  CUtensorMap mq, mk, mv;
+  const bool s5 = strip5_enabled() && make_strip5_map(&mq, q.data_ptr(), B, Sq, q.stride(0), H, Dh, 128, nch) &&
+                  make_strip5_map(&mk, k.data_ptr(), B, Skv, k.stride(0), H, Dh, 128, nch) &&
+                  make_strip5_map(&mv, v.data_ptr(), B, Skv, v.stride(0), H, Dh, 128, nch);
+  if (!s5) {
+    mq = make_strip_map(q.data_ptr(), B, Sq, q.stride(0), H, Dh, 128);
+    mk = make_strip_map(k.data_ptr(), B, Skv, k.stride(0), H, Dh, 128);
+    mv = make_strip_map(v.data_ptr(), B, Skv, v.stride(0), H, Dh, 128);
+  }
   FwdArgs args;
+  args.strip5 = s5 ? 1 : 0;
   args.B = B; args.Sq = Sq; args.Skv = Skv; args.H = H; args.Dh = Dh;
   args.scale_log2 = (float)(scale * 1.4426950408889634);
   args.O = reinterpret_cast<bf16*>(o.data_ptr());
@@ -847,11 +1233,18 @@ void attn_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, con
   if (B * Skv == 0) return;
   const at::cuda::CUDAGuard guard(q.device());
   const int nch = nch_for((int)Dh);
-  CUtensorMap mq = make_strip_map(q.data_ptr(), B, Sq, q.stride(0), H, Dh, 128);
-  CUtensorMap mk = make_strip_map(k.data_ptr(), B, Skv, k.stride(0), H, Dh, 128);
-  CUtensorMap mv = make_strip_map(v.data_ptr(), B, Skv, v.stride(0), H, Dh, 128);
-  CUtensorMap mdo = make_strip_map(dout.data_ptr(), B, Sq, dout.stride(0), H, Dh, 128);
-  CUtensorMap mdq = make_f32_rows_map(dq_acc.data_ptr(), B, Sq, H, Dh, 128);
+  CUtensorMap mq, mk, mv, mdo;
+  const bool s5 = strip5_enabled() && make_strip5_map(&mq, q.data_ptr(), B, Sq, q.stride(0), H, Dh, 128, nch) &&
+                  make_strip5_map(&mk, k.data_ptr(), B, Skv, k.stride(0), H, Dh, 128, nch) &&
+                  make_strip5_map(&mv, v.data_ptr(), B, Skv, v.stride(0), H, Dh, 128, nch) &&
+                  make_strip5_map(&mdo, dout.data_ptr(), B, Sq, dout.stride(0), H, Dh, 128, nch);
+  if (!s5) {
+    mq = make_strip_map(q.data_ptr(), B, Sq, q.stride(0), H, Dh, 128);
+    mk = make_strip_map(k.data_ptr(), B, Skv, k.stride(0), H, Dh, 128);
+    mv = make_strip_map(v.data_ptr(), B, Skv, v.stride(0), H, Dh, 128);
+    mdo = make_strip_map(dout.data_ptr(), B, Sq, dout.stride(0), H, Dh, 128);
+  }
+  CUtensorMap mdq = make_f32_bhsd_map(dq_acc.data_ptr(), B, Sq, H, Dh, 128);
   BwdArgs args;
   args.B = B; args.Sq = Sq; args.Skv = Skv; args.H = H; args.Dh = Dh;
   args.scale_log2 = (float)(scale * 1.4426950408889634);
@@ -865,6 +1258,17 @@ void attn_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, con
   args.dV = reinterpret_cast<bf16*>(dv.data_ptr());
   args.lddv = dv.stride(0);
   args.err = err.data_ptr<int>();
+  static const bool probe = [] {
+    const char* e = std::getenv("HARP_ATTN_PROBE");
+    return e && e[0] == '1';
+  }();
+  args.probe = probe ? 1 : 0;
+  args.strip5 = s5 ? 1 : 0;
+  static const bool skip_dq = [] {
+    const char* e = std::getenv("HARP_ATTN_DEBUG_SKIP_DQ");
+    return e && e[0] == '1';
+  }();
+  args.skip_dq = skip_dq ? 1 : 0;
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
   switch (nch) {
     case 8: launch_bwd<8>(mq, mk, mv, mdo, mdq, args, stream); break;
@@ -874,14 +1278,26 @@ void attn_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, con
   }
 }
 
-void dq_finalize(const at::Tensor& acc, int64_t H, int64_t Dh, double scale, at::Tensor& out) {
+// Timeline of CTA 0 of the last backward launch with HARP_ATTN_PROBE=1: int64
+// [64 tiles, 16 slots] of %globaltimer nanoseconds (0 = slot not reached).
+at::Tensor attn_bwd_probe() {
+  auto out = at::zeros({64, 16}, at::TensorOptions().dtype(at::kLong));
+  C10_CUDA_CHECK(cudaMemcpyFromSymbol(out.data_ptr(), g_bwd_probe, sizeof(unsigned long long) * 64 * 16));
+  static const unsigned long long zeros[64 * 16] = {};
+  C10_CUDA_CHECK(cudaMemcpyToSymbol(g_bwd_probe, zeros, sizeof(zeros)));
+  return out;
+}
+
+void dq_finalize(const at::Tensor& acc, int64_t H, int64_t Dh, double scale, at::Tensor& out, int64_t Sq) {
   const long total = acc.numel();
   if (total == 0) return;
-  TORCH_CHECK(Dh % 4 == 0 && acc.is_contiguous(), "dq_finalize");
-  const int R = total / (H * Dh);
+  TORCH_CHECK(Dh % 4 == 0 && acc.is_contiguous() && Sq > 0 && total % (H * Dh * Sq) == 0,
+              "dq_finalize: acc fp32 [B, H, Sq, Dh]");
+  const int B = (int)(total / (H * Dh * Sq));
   const at::cuda::CUDAGuard guard(acc.device());
   dq_finalize_kernel<<<(total / 4 + 255) / 256, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-      acc.data_ptr<float>(), R, (int)H, (int)Dh, (float)scale, reinterpret_cast<bf16*>(out.data_ptr()), out.stride(0));
+      acc.data_ptr<float>(), B, (int)Sq, (int)H, (int)Dh, (float)scale, reinterpret_cast<bf16*>(out.data_ptr()),
+      out.stride(0));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   count_launch();
 }
@@ -894,10 +1310,12 @@ TORCH_LIBRARY_FRAGMENT(harp, m) {
         "int q_rot=0, bool wait_q=False) -> ()");
   m.def("attn_bwd(Tensor q, Tensor k, Tensor v, Tensor dout, Tensor lse, Tensor delta, int B, int Sq, int Skv, "
         "int H, int Dh, float scale, Tensor(a!) dq_acc, Tensor(b!) dk, Tensor(c!) dv, Tensor(d!) err) -> ()");
-  m.def("dq_finalize(Tensor acc, int H, int Dh, float scale, Tensor(a!) out) -> ()");
+  m.def("dq_finalize(Tensor acc, int H, int Dh, float scale, Tensor(a!) out, int Sq) -> ()");
+  m.def("attn_bwd_probe() -> Tensor");
 }
 TORCH_LIBRARY_IMPL(harp, CUDA, m) {
   m.impl("attn_fwd", &harp::attn_fwd);
   m.impl("attn_bwd", &harp::attn_bwd);
   m.impl("dq_finalize", &harp::dq_finalize);
 }
+TORCH_LIBRARY_IMPL(harp, CompositeExplicitAutograd, m) { m.impl("attn_bwd_probe", &harp::attn_bwd_probe); }

@@ -39,7 +39,10 @@ int num_sms();
 // of Dh elements per token: dims {Dh, H, S, B}; the box is 8 elements x 1 head
 // x `box_rows` tokens x 1 batch, i.e. one 16-byte column strip of a tile.
 CUtensorMap make_strip_map(const void* base, long B, long S, long ld, long H, long Dh, int box_rows);
+bool make_strip5_map(CUtensorMap* m, const void* base, long B, long S, long ld, long H, long Dh, int box_rows,
+                     int nstrips);
 // 4-D fp32 map over a dense [B, S, H, Dh] buffer; box = Dh x 1 x box_rows x 1.
 CUtensorMap make_f32_rows_map(const void* base, long B, long S, long H, long Dh, int box_rows);
+CUtensorMap make_f32_bhsd_map(const void* base, long B, long S, long H, long Dh, int box_rows);
 
 }  // namespace harp

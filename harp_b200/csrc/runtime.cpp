@@ -49,6 +49,41 @@ CUtensorMap make_strip_map(const void* base, long B, long S, long ld, long H, lo
   return m;
 }
 
+// Strip-major tile with one TMA instruction: dims ordered (8 elements, row,
+// 8-element strip, head, batch) so that a box {8, rows, nstrips, 1, 1} lands in
+// shared memory as [strip][row][8] (strip c at c * rows * 16 bytes, row r at
+// r * 16).  Strips at or past Dh / 8 are outside the tensor and read as zero.
+// Returns false (map untouched) when the driver does not accept the layout.
+bool make_strip5_map(CUtensorMap* m, const void* base, long B, long S, long ld, long H, long Dh, int box_rows,
+                     int nstrips) {
+  if (Dh % 8 != 0 || (reinterpret_cast<uintptr_t>(base) & 15) != 0 || (ld * 2) % 16 != 0) return false;
+  cuuint64_t dims[5] = {8, (cuuint64_t)S, (cuuint64_t)(Dh / 8), (cuuint64_t)H, (cuuint64_t)B};
+  cuuint64_t strides[4] = {(cuuint64_t)ld * 2, 16, (cuuint64_t)Dh * 2, (cuuint64_t)S * ld * 2};
+  cuuint32_t box[5] = {8, (cuuint32_t)box_rows, (cuuint32_t)nstrips, 1, 1};
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  CUresult r = get_encode_fn()(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, const_cast<void*>(base), dims, strides, box,
+                               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// fp32 [B][H][S][Dh] (one contiguous [S, Dh] slab per batch and head), as the
+// 4-D box {Dh, 1, rows, 1} over dims (Dh, H, S, B).
+CUtensorMap make_f32_bhsd_map(const void* base, long B, long S, long H, long Dh, int box_rows) {
+  TORCH_CHECK(Dh % 4 == 0 && Dh <= 256, "harp: fp32 map needs Dh % 4 == 0 and Dh <= 256");
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(base) & 15) == 0, "harp: fp32 map base alignment");
+  CUtensorMap m;
+  cuuint64_t dims[4] = {(cuuint64_t)Dh, (cuuint64_t)H, (cuuint64_t)S, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)S * Dh * 4, (cuuint64_t)Dh * 4, (cuuint64_t)H * S * Dh * 4};
+  cuuint32_t box[4] = {(cuuint32_t)Dh, 1, (cuuint32_t)box_rows, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = get_encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<void*>(base), dims, strides, box,
+                               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "harp: cuTensorMapEncodeTiled (fp32 bhsd) failed (", (int)r, ")");
+  return m;
+}
+
 CUtensorMap make_f32_rows_map(const void* base, long B, long S, long H, long Dh, int box_rows) {
   TORCH_CHECK(Dh % 4 == 0 && Dh <= 256, "harp: fp32 row map needs Dh % 4 == 0 and Dh <= 256");
   TORCH_CHECK((reinterpret_cast<uintptr_t>(base) & 15) == 0, "harp: fp32 row map base alignment");

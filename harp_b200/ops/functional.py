@@ -466,10 +466,10 @@ def attn_bwd(q, k, v, o, do, lse, B, Sq, Skv, H, Dh, scale=None, dk_out=None, dv
     dq = dq_out if dq_out is not None else torch.empty(B * Sq, H * Dh, device=q.device, dtype=q.dtype)
     if _cuda(q):
         delta = rowdot(do, o, H, Dh, Sq)
-        dq_acc = torch.zeros(B * Sq * H * Dh, device=q.device)
+        dq_acc = torch.zeros(B * H * Sq * Dh, device=q.device)  # [B, H, Sq, Dh]
         torch.ops.harp.attn_bwd(q, k, v, do, lse, delta, B, Sq, Skv, H, Dh, scale, dq_acc, dk, dv,
                                 errors.word(q.device))
-        torch.ops.harp.dq_finalize(dq_acc, H, Dh, scale, dq)
+        torch.ops.harp.dq_finalize(dq_acc, H, Dh, scale, dq, Sq)
         return dq, dk, dv
     qf = q[:, : H * Dh].float().view(B, Sq, H, Dh)
     kf = k[:, : H * Dh].float().view(B, Skv, H, Dh)

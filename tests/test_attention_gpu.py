@@ -91,7 +91,7 @@ def test_attn_fwd_ready_timeout_reports_error():
 
 
 @pytest.mark.parametrize("Dh", [64, 72, 128])
-@pytest.mark.parametrize("B,Sq,Skv,H", [(1, 128, 128, 1), (2, 300, 300, 2), (1, 200, 330, 2)])
+@pytest.mark.parametrize("B,Sq,Skv,H", [(1, 128, 128, 1), (2, 300, 300, 2), (1, 200, 330, 2), (1, 1100, 700, 2)])
 def test_attn_bwd(B, Sq, Skv, H, Dh):
     q, k, v = _make(B, Sq, Skv, H, Dh)
     o, lse = _fwd(q, k, v, B, Sq, Skv, H, Dh)
@@ -99,13 +99,13 @@ def test_attn_bwd(B, Sq, Skv, H, Dh):
     do = torch.randn(B * Sq, H * Dh, device="cuda").to(torch.bfloat16)
     delta = torch.zeros(B * H * _ld(Sq), device="cuda")
     torch.ops.harp.rowdot(do, o, H, Dh, Sq, delta)
-    dq_acc = torch.zeros(B * Sq * H * Dh, device="cuda")
+    dq_acc = torch.zeros(B * H * Sq * Dh, device="cuda")  # [B, H, Sq, Dh]
     dk = torch.empty(B * Skv, H * Dh, device="cuda", dtype=torch.bfloat16)
     dv = torch.empty_like(dk)
     err = torch.zeros(4, dtype=torch.int32, device="cuda")
     torch.ops.harp.attn_bwd(q, k, v, do, lse, delta, B, Sq, Skv, H, Dh, scale, dq_acc, dk, dv, err)
     dq = torch.empty(B * Sq, H * Dh, device="cuda", dtype=torch.bfloat16)
-    torch.ops.harp.dq_finalize(dq_acc, H, Dh, scale, dq)
+    torch.ops.harp.dq_finalize(dq_acc, H, Dh, scale, dq, Sq)
     torch.cuda.synchronize()
     assert err.cpu()[0].item() == 0, err.cpu().tolist()
     qr = q.float().view(B, Sq, H, Dh).requires_grad_()
