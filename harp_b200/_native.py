@@ -146,3 +146,69 @@ def require() -> None:
             "harp_b200: CUDA kernels are required on GPU tensors but the library is not loaded: "
             f"{_load_error!r}"
         )
+
+
+# ---------------------------------------------------------------------------
+# the harp_nvl torch.distributed backend: a separate Python extension module
+# (it needs pybind11 and the c10d headers; the op library above does not)
+# ---------------------------------------------------------------------------
+C10D_NAME = "harp_b200_c10d"
+C10D_SOURCES = ["c10d_nvl.cpp", "c10d_nvl_kernels.cu"]
+_c10d_mod = None
+
+
+def c10d_so_path() -> str:
+    return os.path.join(BUILD_DIR, C10D_NAME + ".so")
+
+
+def _c10d_hash() -> str:
+    h = hashlib.sha256()
+    for s in C10D_SOURCES + ["c10d_nvl_kernels.h", "common.cuh"]:
+        with open(os.path.join(CSRC, s), "rb") as fh:
+            h.update(s.encode())
+            h.update(fh.read())
+    h.update(" ".join(CUDA_FLAGS + CXX_FLAGS).encode())
+    h.update(torch.__version__.encode())
+    return h.hexdigest()
+
+
+def build_c10d(verbose: bool = False):
+    """Compile the harp_nvl backend module for sm_100a and import it."""
+    global _c10d_mod
+    from torch.utils.cpp_extension import load as _load
+
+    os.makedirs(BUILD_DIR, exist_ok=True)
+    with _lock:
+        _c10d_mod = _load(name=C10D_NAME, sources=[os.path.join(CSRC, s) for s in C10D_SOURCES],
+                          extra_cflags=CXX_FLAGS, extra_cuda_cflags=CUDA_FLAGS, extra_include_paths=[CSRC],
+                          build_directory=BUILD_DIR, is_python_module=True, verbose=verbose)
+        with open(os.path.join(BUILD_DIR, C10D_NAME + ".stamp"), "w") as fh:
+            fh.write(_c10d_hash())
+    return _c10d_mod
+
+
+def load_c10d(build_if_needed: bool = True):
+    """The harp_nvl backend module (prebuilt in-tree, else compiled now)."""
+    global _c10d_mod
+    if _c10d_mod is not None:
+        return _c10d_mod
+    try:
+        with open(os.path.join(BUILD_DIR, C10D_NAME + ".stamp")) as fh:
+            fresh = fh.read().strip() == _c10d_hash() and os.path.exists(c10d_so_path())
+    except OSError:
+        fresh = False
+    if fresh:
+        import importlib.machinery
+        import importlib.util
+
+        import torch.distributed  # noqa: F401  (registers the c10d Python types the module returns)
+
+        loader = importlib.machinery.ExtensionFileLoader(C10D_NAME, c10d_so_path())
+        spec = importlib.util.spec_from_file_location(C10D_NAME, c10d_so_path(), loader=loader)
+        mod = importlib.util.module_from_spec(spec)
+        loader.exec_module(mod)
+        _c10d_mod = mod
+        return mod
+    if not build_if_needed:
+        raise RuntimeError("harp_nvl backend module not built (run harp_b200._native.build_c10d())")
+    return build_c10d()

@@ -60,3 +60,49 @@ def flag_timeout(rank, world, out, args):
     errors.word(dev).zero_()
     dist.barrier()
     return {"err": e, "x": x}
+
+
+def c10d_backend(rank, world, out, args):
+    """Every collective of the harp_nvl backend against values computed locally."""
+    from harp_b200.parallel import c10d_backend as CB
+
+    CB.register()
+    g = dist.new_group(backend=CB.NAME)
+    dev = torch.device("cuda", rank)
+    res = {}
+    for dtype in (torch.float32, torch.bfloat16):
+        for n in (1000, 3_000_001):  # one-shot and two-phase all-reduce (odd length included)
+            x = torch.arange(n, device=dev, dtype=torch.float32).to(dtype) * (rank + 1)
+            dist.all_reduce(x, group=g)
+            ref = torch.arange(n, device=dev, dtype=torch.float32).to(dtype).float() * sum(r + 1 for r in range(world))
+            res[f"ar_{dtype}_{n}"] = (x.float() - ref).abs().max().item() / max(1.0, ref.abs().max().item())
+    m = torch.tensor([float(rank)], device=dev)
+    dist.all_reduce(m, op=dist.ReduceOp.MAX, group=g)
+    res["max"] = m.item()
+    x = torch.full((1025,), float(rank), device=dev)
+    full = torch.empty(world * 1025, device=dev)
+    dist.all_gather_into_tensor(full, x, group=g)
+    res["ag"] = bool(torch.equal(full, torch.arange(world, device=dev).float().repeat_interleave(1025)))
+    lst = [torch.empty(3, device=dev) for _ in range(world)]
+    dist.all_gather(lst, torch.full((3,), rank + 0.5, device=dev), group=g)
+    res["ag_list"] = [t.tolist() for t in lst]
+    inp = torch.arange(world * 8, device=dev, dtype=torch.float32) + rank
+    o = torch.empty(8, device=dev)
+    dist.reduce_scatter_tensor(o, inp, group=g)
+    res["rs"] = bool(torch.equal(o, (torch.arange(world * 8, device=dev).float() * world
+                                     + sum(range(world)))[rank * 8:(rank + 1) * 8]))
+    b = torch.full((77,), float(rank), device=dev)
+    dist.broadcast(b, src=world - 1, group=g)
+    res["bcast"] = bool(torch.all(b == world - 1))
+    a_in = torch.arange(world * 4, device=dev, dtype=torch.float32) + 100 * rank
+    a_out = torch.empty_like(a_in)
+    dist.all_to_all_single(a_out, a_in, group=g)
+    exp = torch.cat([torch.arange(rank * 4, rank * 4 + 4, device=dev).float() + 100 * r for r in range(world)])
+    res["a2a"] = bool(torch.equal(a_out, exp))
+    dist.barrier(group=g)
+    w = dist.all_reduce(torch.ones(4, device=dev), group=g, async_op=True)
+    w.wait()
+    torch.cuda.synchronize()
+    res["async"] = True
+    dist.destroy_process_group(g)
+    return res

@@ -220,3 +220,21 @@ def test_ring_attention_ops_match_sdpa():
         torch.testing.assert_close(a.grad.float(), b.grad, rtol=5e-2, atol=5e-2)
     with pytest.raises(RuntimeError):
         ring_ops.CPURingAttention.apply(q, k, v, 2)
+
+
+def test_timestep_embeddings_closed_form():
+    from harp_b200.models import embedding as E
+
+    t = torch.tensor([0.0, 1.0, 250.5])
+    e = E.get_timestep_embedding(t, 9, flip_sin_to_cos=True, downscale_freq_shift=0)
+    half = 4
+    f = torch.exp(-math.log(10000) * torch.arange(half) / half)
+    torch.testing.assert_close(e[:, :half], torch.cos(t[:, None] * f))
+    torch.testing.assert_close(e[:, half:2 * half], torch.sin(t[:, None] * f))
+    assert e.shape == (3, 9) and torch.all(e[:, -1] == 0)
+    torch.testing.assert_close(E.Timesteps(8, False, 1)(t), E.get_timestep_embedding(t, 8))
+    te = E.TimestepEmbedding(8, 16, out_dim=4, cond_proj_dim=3)
+    assert te(torch.randn(2, 8), torch.randn(2, 3)).shape == (2, 4)
+    emb = E.TimestepEmbedder(32, frequency_embedding_size=16)
+    assert {n for n, _ in emb.named_parameters()} == {"mlp.0.weight", "mlp.0.bias", "mlp.2.weight", "mlp.2.bias"}
+    assert emb(t).shape == (3, 32)

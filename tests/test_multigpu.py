@@ -85,3 +85,16 @@ def test_never_signalled_flag_times_out_cleanly(tmp_path):
     for r in (0, 1):
         assert res[r]["err"][0] == 2 and res[r]["err"][1] >= 100, res[r]  # peer timeout at a wait site
         assert res[r]["x"] == 8.0
+
+
+def test_harp_nvl_c10d_backend_collectives(tmp_path):
+    _need(2)
+    res = _run("c10d_backend", 2, tmp_path, {})
+    for r in (0, 1):
+        d = res[r]
+        for k, v in d.items():
+            if k.startswith("ar_"):
+                assert v < 1e-2, (r, k, v)
+        assert d["max"] == 1.0
+        assert d["ag"] and d["rs"] and d["bcast"] and d["a2a"] and d["async"], d
+        assert d["ag_list"] == [[0.5] * 3, [1.5] * 3]
