@@ -276,13 +276,16 @@ def main():
         return run_reference(args)
     if args.op == "ring-attn":
         return run_ring_attn(args)
-    family = "dit" if args.model.startswith("dit") or args.model in ("tiny", "small") else "mmdit"
+    from harp_b200.models.dit import PRESETS as _DIT_PRESETS
+
+    family = "dit" if args.model in _DIT_PRESETS else "mmdit"
+    weak = args.model.startswith("dit") or args.model in ("tiny", "small")
     args.latent = args.latent or (256 if args.model == "mmdit-2b" else 128)
     args.text_len = args.text_len or (512 if args.model == "flux-12b" else TEXT_TOKENS)
     img_tokens = (args.latent // 2) ** 2
-    if args.impl == "baseline" and family != "dit":
-        print(json.dumps({"impl": "baseline", "unavailable": "the NCCL+cuBLAS/SDPA baseline implements the DiT "
-                          "configuration only"}))
+    if args.impl == "baseline" and not weak:
+        print(json.dumps({"impl": "baseline", "unavailable": "the NCCL+cuBLAS/SDPA baseline implements the "
+                          "DiT-XL/2 configuration only"}))
         return 0
     rank, ws, local = setup_dist(args.gpus)
     device = torch.device("cuda", local)
@@ -290,7 +293,7 @@ def main():
     sp = args.sp or ws
     # dit: weak scaling, each GPU holds batch_per_gpu samples' worth of tokens;
     # mmdit/flux: a fixed batch per SP group split over its ranks (strong scaling)
-    B = args.batch_per_gpu * sp if family == "dit" else args.batch
+    B = args.batch_per_gpu * sp if weak else args.batch
     dp = ws // sp
     global_batch = B * dp
 
@@ -416,7 +419,7 @@ def main():
             "warmup": args.warmup,
             "ms_per_step": ms,
             "higher_is_better": True,
-            "scaling": "weak" if family == "dit" else "strong",
+            "scaling": "weak" if weak else "strong",
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic (random latents/text embeddings of the named shapes, random-init weights)",
@@ -424,7 +427,7 @@ def main():
             "config": {
                 "model": args.model if not args.depth else f"{args.model}(depth={args.depth}, NOT VALID)",
                 "global_batch": global_batch,
-                "per_gpu_batch": args.batch_per_gpu if family == "dit" else global_batch / ws,
+                "per_gpu_batch": args.batch_per_gpu if weak else global_batch / ws,
                 "seq_len": img_tokens + args.text_len,
                 "image_tokens": img_tokens,
                 "text_tokens": args.text_len,

@@ -79,6 +79,10 @@ class DiTConfig:
 PRESETS = {
     # DiT-XL/2 at 1024px (latent 128x128, 4096 image tokens + 256 text tokens)
     "dit-xl-2": DiTConfig(hidden=1152, depth=28, heads=16, mlp_ratio=4.0, text_dim=1152, axes_dims=(24, 24, 24)),
+    # ~2.3B joint-attention DiT (Lumina-style: image and text tokens share every
+    # block's weights), 24 blocks, hidden 2304, 18 heads x 128, SwiGLU 6144
+    "mmdit-2b": DiTConfig(hidden=2304, depth=24, heads=18, mlp_ratio=8.0 / 3.0, text_dim=2304,
+                          axes_dims=(32, 48, 48)),
     # tiny DiT for CPU/gloo plumbing tests
     "tiny": DiTConfig(in_channels=4, hidden=384, depth=6, heads=6, mlp_ratio=4.0, text_dim=384,
                       axes_dims=(16, 24, 24)),

@@ -1,9 +1,10 @@
 """MMDiT / Flux-style DiT: double-stream joint blocks (+ single-stream blocks).
 
-Benchmark configurations: a ~2B MMDiT (24 joint blocks,
-hidden 2304, 18 heads x 128, 16384 image + 256 text tokens, SP 8) and a ~12B
-Flux-like model (19 double-stream + 38 single-stream blocks, hidden 3072,
-24 heads x 128, 4096 image + 512 text tokens of dim 4096).  The reference has
+Presets: an SD3-style ~2.5B double-stream MMDiT and a ~12B Flux-like model
+(19 double-stream + 38 single-stream blocks, hidden 3072, 24 heads x 128,
+4096 image + 512 text tokens of dim 4096 in the benchmark configuration).  The
+~2B joint-block benchmark model (hidden 2304, 24 blocks sharing weights between
+image and text tokens) is the DiT family's "mmdit-2b" preset.  The reference has
 only the Z-Image single-stream model; these families reuse the same op layer
 (harp GEMM, RMSNorm, QK-norm+RoPE, sequence-parallel attention, SwiGLU).
 
@@ -60,8 +61,13 @@ class MMDiTConfig:
 
 
 PRESETS = {
-    "mmdit-2b": MMDiTConfig(hidden=2304, heads=18, depth_double=24, depth_single=0, text_dim=2304),
-    "flux-12b": MMDiTConfig(hidden=3072, heads=24, depth_double=19, depth_single=38, text_dim=4096),
+    # SD3-style double-stream MMDiT, ~2.5B: 24 joint blocks, hidden 1536, 24 heads x 64
+    "sd3-2b": MMDiTConfig(hidden=1536, heads=24, depth_double=24, depth_single=0, text_dim=4096,
+                          axes_dims=(16, 24, 24)),
+    # Flux-like, ~11.8B: 19 double + 38 single blocks, hidden 3072, 24 heads x 128;
+    # SwiGLU hidden 8/3 D has the parameter count of a GELU MLP of 4 D
+    "flux-12b": MMDiTConfig(hidden=3072, heads=24, depth_double=19, depth_single=38, text_dim=4096,
+                            mlp_ratio=8.0 / 3.0),
     "mmdit-tiny": MMDiTConfig(hidden=256, heads=2, depth_double=2, depth_single=0, text_dim=128,
                               axes_dims=(32, 48, 48)),
     "flux-tiny": MMDiTConfig(hidden=256, heads=2, depth_double=1, depth_single=2, text_dim=128,

@@ -41,7 +41,8 @@ def parse_args(argv=None):
     p.add_argument("--pretrained_model_name_or_path", type=str, default="",
                    help="directory with transformer/config.json and scheduler/scheduler_config.json")
     p.add_argument("--model", type=str, default="dit-xl-2",
-                   help="dit-xl-2 | tiny | small | zimage-6b | zimage-tiny | mmdit-2b | mmdit-tiny | flux-12b | flux-tiny")
+                   help="dit-xl-2 | mmdit-2b | tiny | small (joint DiT) | zimage-6b | zimage-tiny | sd3-2b | mmdit-tiny | "
+             "flux-12b | flux-tiny (double-stream)")
     p.add_argument("--work_dir", type=str, default="work_dir")
     p.add_argument("--sub_work_dir", type=str, default="")
     p.add_argument("--data_root", type=str, default="", help="index.json of .npz samples (empty: synthetic)")
@@ -125,9 +126,9 @@ def build_model(args, device, sp_group, dtype=torch.bfloat16):
                                        weighting=weighting)
 
         return model, loss_fn, shapes
-    if name.startswith("mmdit") or name.startswith("flux"):
-        from harp_b200.models import mmdit as M
+    from harp_b200.models import mmdit as M
 
+    if name in M.PRESETS:
         cfg = M.PRESETS[name]
         with torch.device(device):
             model = M.MMDiT(cfg)
