@@ -49,7 +49,18 @@ struct GemmArgs {
   void* C2;  // kEpiGatedResidualSave: pre-gate value (acc + bias), bf16
   long ldc2;
   int* err;
+  int probe;  // accumulate per-role wait cycles into g_gemm_probe (HARP_GEMM_PROBE=1)
 };
+
+// Per-role cycle counters of the CTA-pair kernel, summed over CTAs and read
+// back with gemm_probe(): 0 MMA wait full, 1 MMA wait tempty, 2 producer wait
+// empty, 3 epilogue wait tfull, 4 epilogue TMEM load, 5 epilogue stores,
+// 6 MMA-thread lifetime, 7 tiles.
+__device__ unsigned long long g_gemm_probe[16];
+#define GEMM_PROBE_ADD(a, slot, v) \
+  do {                               \
+    if ((a).probe) atomicAdd(&g_gemm_probe[slot], (unsigned long long)(v)); \
+  } while (0)
 
 template <int BN>
 struct Cfg {
@@ -333,6 +344,292 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
+// CTA-pair variant (cta_group::2).  A cluster of two CTAs on neighbouring SMs
+// computes a 256 x BN tile: each CTA stages its own 128 rows of A and its own
+// BN/2 rows of B (no operand is read twice from L2), the leader CTA issues
+// M=256 tcgen05.mma that read both CTAs' shared memory and write both CTAs'
+// tensor memory (each holds its 128 accumulator rows x BN), and each CTA's
+// epilogue stores its own rows.  Per CTA and k-block this moves 32 KB instead
+// of the 48 KB of the 128 x 256 single-CTA tile, which is what keeps the
+// tensor pipe fed.  Synchronisation across the pair:
+//   full[s]   leader only: both CTAs' TMA loads complete on it (the loads name
+//             the leader's barrier); the leader's producer sets the byte count
+//   empty[s]  both CTAs: the leader's MMA commit arrives on its own and on the
+//             peer's copy, so both producers see the stage free
+//   tfull[a]  both CTAs: accumulator a of the tile is ready
+//   tempty[a] leader only: 4 epilogue warps of each CTA arrive (8 in total)
+// Every wait is bounded; errors fall through to the end, where both CTAs meet
+// at the cluster barrier before the paired TMEM is released.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t peer_addr(uint32_t local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  __syncwarp();
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t bar_cluster, int c0,
+                                                 int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+      "[%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(c0), "r"(c1)
+      : "memory");
+}
+__device__ __forceinline__ void mma_ss_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+}
+// arrive on the barrier at this shared::cluster address once the pair's MMAs issued so far are done
+__device__ __forceinline__ void mma_commit_pair(uint32_t bar_cluster) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_cluster)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst, int ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)),
+               "r"(ncols));
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::);
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, int ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols));
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
+
+// Each pipeline stage holds a K depth of 128 (two 128-byte swizzle atoms per
+// operand row), so one stage is eight M=256 MMAs and one commit.  Commits of
+// pair MMAs are not free: with four MMAs per commit the tensor pipe idles for
+// roughly a quarter of the time, with eight it loses well under a tenth.
+constexpr int BKP = 128;
+template <int BN>
+struct Cfg2 {
+  static constexpr int A_HALF = 128 * 64 * 2;       // 128 rows x one 64-wide K atom
+  static constexpr int B_HALF = (BN / 2) * 64 * 2;  // BN/2 rows x one K atom
+  static constexpr int A_BYTES = A_HALF * (BKP / 64);
+  static constexpr int B_BYTES = B_HALF * (BKP / 64);
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (227 * 1024 - 2048) / STAGE_BYTES;
+  static constexpr int TMEM_COLS = (2 * BN <= 256) ? 256 : 512;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+  static_assert(STAGES >= 3 && STAGES <= 8, "pair GEMM stage count");
+  static_assert(SMEM_BYTES <= 232448, "pair GEMM stages exceed 227 KB of shared memory");
+};
+
+template <int BN, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_bf16_tcgen05_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                           const GemmArgs args) {
+  using C_ = Cfg2<BN>;
+  static_assert(!B_MN || BN % 128 == 0, "MN-major B half tiles are whole 64-column atoms");
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smem_a = smem;
+  uint8_t* smem_b = smem + C_::STAGES * C_::A_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C_::STAGES * C_::STAGE_BYTES);
+  uint64_t* full_bar = bars;                         // [STAGES] (leader's are used)
+  uint64_t* empty_bar = bars + C_::STAGES;           // [STAGES]
+  uint64_t* tfull_bar = bars + 2 * C_::STAGES;       // [2]
+  uint64_t* tempty_bar = bars + 2 * C_::STAGES + 2;  // [2] (leader's are used)
+  uint64_t* drain_bar = bars + 2 * C_::STAGES + 4;   // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * C_::STAGES + 5);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const uint32_t rank = cluster_rank();  // 0 = leader
+  const int num_m = (args.M + 255) / 256;
+  const int num_n = (args.N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n;
+  const int num_kb = (args.K + BKP - 1) / BKP;
+  const int pair = blockIdx.x / 2, npairs = gridDim.x / 2;
+  int* err = args.err;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C_::STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull_bar[i], 1);
+      mbar_init(&tempty_bar[i], 8);
+    }
+    mbar_init(drain_bar, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, C_::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // both CTAs' barriers exist and the paired TMEM is allocated
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer (both CTAs) ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued[C_::STAGES] = {};
+      bool ok = true;
+      const uint32_t fb0 = peer_addr(smem_u32(&full_bar[0]), 0);  // the leader's barriers
+      for (int t = pair; t < num_tiles && ok; t += npairs) {
+        int mt, nt;
+        tile_coords(t, num_m, num_n, mt, nt);
+        const int m0 = mt * 256 + (int)rank * 128, n0 = nt * BN + (int)rank * (BN / 2);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          const long long w0 = clock64();
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1, err, 11)) { ok = false; break; }
+          GEMM_PROBE_ADD(args, rank == 0 ? 2 : 8, clock64() - w0);
+          const uint32_t fb = fb0 + stage * 8;
+          if (rank == 0) mbar_arrive_expect_tx(&full_bar[stage], 2 * C_::STAGE_BYTES);
+#pragma unroll
+          for (int h = 0; h < BKP / 64; ++h) {
+            uint8_t* sa = smem_a + stage * C_::A_BYTES + h * C_::A_HALF;
+            uint8_t* sb = smem_b + stage * C_::B_BYTES + h * C_::B_HALF;
+            const int k0 = kb * BKP + h * 64;
+            if (!A_MN) {
+              tma_load_2d_pair(sa, &tmA, fb, k0, m0);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 2; ++j) tma_load_2d_pair(sa + j * 8192, &tmA, fb, m0 + 64 * j, k0);
+            }
+            if (!B_MN) {
+              tma_load_2d_pair(sb, &tmB, fb, k0, n0);
+            } else {
+#pragma unroll
+              for (int j = 0; j < BN / 128; ++j) tma_load_2d_pair(sb + j * 8192, &tmB, fb, n0 + 64 * j, k0);
+            }
+          }
+          issued[stage]++;
+          if (++stage == C_::STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+      // this CTA's copies land before it can pass the final cluster barrier:
+      // the stage's empty barrier turns once the leader consumed it
+      for (int s = 0; s < C_::STAGES; ++s)
+        if (issued[s] > 0) mbar_wait_drain(&empty_bar[s], (uint32_t)((issued[s] - 1) & 1));
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (leader CTA) ----------------
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = make_idesc_bf16(256, BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      const long long life0 = clock64();
+      long long wfull = 0, wtempty = 0;
+      for (int t = pair; t < num_tiles && ok; t += npairs, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        long long w0 = clock64();
+        if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1, err, 12)) { ok = false; break; }
+        wtempty += clock64() - w0;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          w0 = clock64();
+          if (!mbar_wait(&full_bar[stage], phase, err, 13)) { ok = false; break; }
+          wfull += clock64() - w0;
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem_a + stage * C_::A_BYTES);
+          const uint32_t sb = smem_u32(smem_b + stage * C_::B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BKP / 16; ++kk) {
+            const int h = kk / 4, r = kk % 4;
+            const uint32_t ah = sa + h * C_::A_HALF, bh = sb + h * C_::B_HALF;
+            uint64_t adesc, bdesc;
+            if (!A_MN) adesc = make_sdesc(ah + r * 32, 16, 1024, kLayoutSw128);
+            else       adesc = make_sdesc(ah + r * 2048, 8192, 1024, kLayoutSw128);
+            if (!B_MN) bdesc = make_sdesc(bh + r * 32, 16, 1024, kLayoutSw128);
+            else       bdesc = make_sdesc(bh + r * 2048, 8192, 1024, kLayoutSw128);
+            mma_ss_pair(d_tmem, adesc, bdesc, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          }
+          const uint32_t eb = smem_u32(&empty_bar[stage]);
+          mma_commit_pair(eb);
+          mma_commit_pair(peer_addr(eb, 1));
+          if (++stage == C_::STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        const uint32_t tf = smem_u32(&tfull_bar[acc]);
+        mma_commit_pair(tf);
+        mma_commit_pair(peer_addr(tf, 1));
+      }
+      const uint32_t db = smem_u32(drain_bar);
+      mma_commit_pair(db);
+      mma_commit_pair(peer_addr(db, 1));
+      GEMM_PROBE_ADD(args, 0, wfull);
+      GEMM_PROBE_ADD(args, 1, wtempty);
+      GEMM_PROBE_ADD(args, 6, clock64() - life0);
+      GEMM_PROBE_ADD(args, 7, local);
+    }
+    // both CTAs: the pair's MMAs are done before the paired TMEM goes away
+    if (lane == 0) mbar_wait_drain(drain_bar, 0);
+  } else {
+    // ---------------- epilogue (warps 2..5, both CTAs) ----------------
+    const int quarter = warp & 3;
+    int local = 0;
+    const uint32_t te_leader[2] = {peer_addr(smem_u32(&tempty_bar[0]), 0), peer_addr(smem_u32(&tempty_bar[1]), 0)};
+    for (int t = pair; t < num_tiles; t += npairs, ++local) {
+      int mt, nt;
+      tile_coords(t, num_m, num_n, mt, nt);
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      const long long w0 = clock64();
+      if (!mbar_wait(&tfull_bar[acc], acc_phase, err, 14)) break;
+      tc_fence_after();
+      long long w1 = clock64(), tld = 0, tst = 0;
+      if (lane == 0) GEMM_PROBE_ADD(args, 3, w1 - w0);
+      const int m = mt * 256 + (int)rank * 128 + quarter * 32 + lane;
+      const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        const int n = nt * BN + c * 32;
+        uint32_t v[32];
+        tmem_ld32(tbase + c * 32, v);
+        tmem_wait_ld();
+        const long long w2 = clock64();
+        tld += w2 - w1;
+        if (n < args.N) epilogue_chunk<BN>(args, m, n, v);
+        w1 = clock64();
+        tst += w1 - w2;
+      }
+      if (lane == 0) {
+        GEMM_PROBE_ADD(args, 4, tld);
+        GEMM_PROBE_ADD(args, 5, tst);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(te_leader[acc]);
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync_all();  // neither CTA frees its half of the pair's TMEM while the other still works
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, C_::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // CUDA-core fallback for operands TMA cannot address (row strides that are not
 // a multiple of 16 bytes, or unaligned bases).  Same epilogues.
 // ---------------------------------------------------------------------------
@@ -430,6 +727,72 @@ void launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& arg
   count_launch();
 }
 
+// CTA-pair launch: clusters of two, one cluster per tile in flight, as many
+// clusters as the device keeps resident at once (GPC shapes can leave SMs
+// without a partner, so this is not simply SMs / 2).
+template <int BN, bool A_MN, bool B_MN>
+void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args, cudaStream_t stream) {
+  using C_ = Cfg2<BN>;
+  auto kern = gemm_bf16_tcgen05_pair<BN, A_MN, B_MN>;
+  static int max_clusters = 0;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = C_::SMEM_BYTES;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (max_clusters == 0) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C_::SMEM_BYTES));
+    cfg.gridDim = dim3(2 * (num_sms() / 2));
+    int n = 0;
+    C10_CUDA_CHECK(cudaOccupancyMaxActiveClusters(&n, kern, &cfg));
+    max_clusters = std::max(1, n);
+  }
+  const int tiles = ((args.M + 255) / 256) * ((args.N + BN - 1) / BN);
+  cfg.gridDim = dim3(2 * std::min(tiles, max_clusters));
+  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, args));
+  count_launch();
+}
+
+// An MN-major B half tile is whole 64-column swizzle atoms, so BN=192 (96
+// columns per CTA) pairs only with K-major B.
+template <int BN>
+void dispatch_pair(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args,
+                   cudaStream_t s) {
+  if constexpr (BN % 128 == 0) {
+    if (b_mn) {
+      if (a_mn) launch_pair<BN, true, true>(ta, tb, args, s);
+      else launch_pair<BN, false, true>(ta, tb, args, s);
+      return;
+    }
+  } else {
+    TORCH_CHECK(!b_mn, "harp gemm: CTA-pair tile width ", BN, " needs K-major B");
+  }
+  if (a_mn) launch_pair<BN, true, false>(ta, tb, args, s);
+  else launch_pair<BN, false, false>(ta, tb, args, s);
+}
+
+// Pair tile width: the one of 256 / 192 / 128 that wastes the least work in
+// the last column band and the last wave of clusters.
+int pick_bn_pair(int M, int N, bool b_mn) {
+  const int sms2 = num_sms() / 2;
+  auto cost = [&](int bn) {
+    const long tiles = (long)((M + 255) / 256) * ((N + bn - 1) / bn);
+    const long waves = (tiles + sms2 - 1) / sms2;
+    // narrower tiles move more operand bytes per FLOP (the feed is the limit)
+    return (double)waves * bn / (bn == 256 ? 1.0 : (bn == 192 ? 0.87 : 0.67));
+  };
+  int best = 256;
+  for (int bn : {192, 128})
+    if ((bn != 192 || !b_mn) && cost(bn) < cost(best) * 0.97) best = bn;
+  return best;
+}
+
 template <int BN>
 void dispatch_major(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args,
                     cudaStream_t s) {
@@ -461,6 +824,22 @@ int pick_bn(int M, int N) {
 }  // namespace
 
 static std::atomic<long long> g_launches{0};
+// 1: large GEMMs run on CTA pairs (cta_group::2); 0: single-CTA tiles only.
+static std::atomic<int> g_pair_mode{-1};
+static int pair_mode() {
+  int m = g_pair_mode.load(std::memory_order_relaxed);
+  if (m < 0) {
+    const char* e = std::getenv("HARP_GEMM_PAIR");
+    m = (e != nullptr && e[0] != '\0') ? (std::atoi(e) != 0 ? 1 : 0) : 1;
+    g_pair_mode.store(m);
+  }
+  return m;
+}
+int set_gemm_pair_mode(int mode) {
+  const int prev = pair_mode();
+  if (mode >= 0) g_pair_mode.store(mode != 0 ? 1 : 0);
+  return prev;
+}
 void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 long long launch_count() { return g_launches.load(); }
 void reset_launch_count() { g_launches.store(0); }
@@ -510,6 +889,12 @@ void gemm(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, at::Te
   args.epi = epi;
   args.alpha = (float)alpha;
   args.err = err.data_ptr<int>();
+  static const bool probe = [] {
+    const char* e = std::getenv("HARP_GEMM_PROBE");
+    return e != nullptr && e[0] == '1';
+  }();
+  args.probe = probe ? 1 : 0;
+
 
   if (K == 0) {
     // Degenerate: treat as zero accumulator.  Route through SIMT (K loop is empty).
@@ -527,6 +912,20 @@ void gemm(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, at::Te
     count_launch();
     return;
   }
+  if (pair_mode() && M >= 512 && N >= 256) {
+    // CTA pair: each CTA's TMA box is its own 128 rows of A and BN/2 rows of B
+    const int bn = pick_bn_pair(M, N, b_mn);
+    CUtensorMap ta = a_mn ? make_map_2d(A.data_ptr(), K, M, A.stride(0), 64, 64)
+                          : make_map_2d(A.data_ptr(), M, K, A.stride(0), 64, 128);
+    CUtensorMap tb = b_mn ? make_map_2d(B.data_ptr(), K, N, B.stride(0), 64, 64)
+                          : make_map_2d(B.data_ptr(), N, K, B.stride(0), 64, bn / 2);
+    switch (bn) {
+      case 256: dispatch_pair<256>(a_mn, b_mn, ta, tb, args, stream); break;
+      case 192: dispatch_pair<192>(a_mn, b_mn, ta, tb, args, stream); break;
+      default: dispatch_pair<128>(a_mn, b_mn, ta, tb, args, stream); break;
+    }
+    return;
+  }
   const int bn = pick_bn(M, N);
   CUtensorMap ta = a_mn ? make_map_2d(A.data_ptr(), K, M, A.stride(0), 64, 64)
                         : make_map_2d(A.data_ptr(), M, K, A.stride(0), 64, BM);
@@ -537,6 +936,14 @@ void gemm(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, at::Te
     case 192: dispatch_major<192>(a_mn, b_mn, ta, tb, args, stream); break;
     default: dispatch_major<128>(a_mn, b_mn, ta, tb, args, stream); break;
   }
+}
+
+at::Tensor gemm_probe() {
+  auto out = at::empty({16}, at::TensorOptions().dtype(at::kLong));
+  C10_CUDA_CHECK(cudaMemcpyFromSymbol(out.data_ptr(), g_gemm_probe, sizeof(unsigned long long) * 16));
+  const unsigned long long zeros[16] = {};
+  C10_CUDA_CHECK(cudaMemcpyToSymbol(g_gemm_probe, zeros, sizeof(zeros)));
+  return out;
 }
 
 }  // namespace harp

@@ -28,6 +28,11 @@ void gemm(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, at::Te
 void count_launch();
 long long launch_count();
 void reset_launch_count();
+// select CTA-pair tiles for large GEMMs (mode 1), single-CTA only (0), or
+// just query (-1); returns the previous mode
+int set_gemm_pair_mode(int mode);
+// per-role cycle counters of the CTA-pair kernel (HARP_GEMM_PROBE=1); read and reset
+at::Tensor gemm_probe();
 
 // Shared host helpers (runtime.cpp).
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,

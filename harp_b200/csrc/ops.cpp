@@ -186,6 +186,7 @@ void foreach_adamw_wd(at::TensorList params, at::TensorList grads, at::TensorLis
 
 int64_t launch_count_op() { return launch_count(); }
 void reset_launch_count_op() { reset_launch_count(); }
+int64_t gemm_pair_mode_op(int64_t mode) { return set_gemm_pair_mode((int)mode); }
 int64_t rows_per_block_op(int64_t rpb) { return rows_per_block_for((int)rpb); }
 
 }  // namespace
@@ -222,6 +223,8 @@ TORCH_LIBRARY(harp, m) {
   m.def("launch_count() -> int");
   m.def("reset_launch_count() -> ()");
   m.def("rows_per_block(int rows_per_batch) -> int");
+  m.def("gemm_pair_mode(int mode) -> int");
+  m.def("gemm_probe() -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(harp, CUDA, m) {
@@ -247,6 +250,8 @@ TORCH_LIBRARY_IMPL(harp, CompositeExplicitAutograd, m) {
   m.impl("launch_count", &harp::launch_count_op);
   m.impl("reset_launch_count", &harp::reset_launch_count_op);
   m.impl("rows_per_block", &harp::rows_per_block_op);
+  m.impl("gemm_pair_mode", &harp::gemm_pair_mode_op);
+  m.impl("gemm_probe", &harp::gemm_probe);
 }
 
 TORCH_LIBRARY(xhpops, m) {

@@ -194,6 +194,8 @@ def main(argv=None):
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--small", action="store_true", help="batch 1, 2048 tokens (ncu captures)")
     ap.add_argument("--no-ref", action="store_true")
+    ap.add_argument("--gemm-single", action="store_true",
+                    help="also time GEMM cases with CTA-pair tiles switched off (harp1)")
     args = ap.parse_args(argv)
     from .. import _native
 
@@ -206,10 +208,17 @@ def main(argv=None):
     for name in args.cases or list(cases):
         harp, ref, info = cases[name]()
         rec = {"case": name, **info}
-        for tag, fn in (("harp", harp), ("ref", None if args.no_ref else ref)):
+        single = args.gemm_single and name.startswith("gemm")
+        for tag, fn in (("harp", harp), ("harp1", harp if single else None),
+                        ("ref", None if args.no_ref else ref)):
             if fn is None:
                 continue
-            ms = timer(fn, args.iters)
+            prev = torch.ops.harp.gemm_pair_mode(0) if tag == "harp1" else None
+            try:
+                ms = timer(fn, args.iters)
+            finally:
+                if prev is not None:
+                    torch.ops.harp.gemm_pair_mode(prev)
             rec[f"{tag}_ms"] = round(ms, 4)
             if "flops" in info:
                 tf = info["flops"] / ms / 1e9

@@ -62,6 +62,40 @@ def test_gemm_majors(M, N, K, a_mn, b_mn):
     assert (C.float() - ref).abs().max().item() < tol, (C.float() - ref).abs().max().item()
 
 
+PAIR_SHAPES = [(512, 256, 64), (600, 300, 200), (1000, 1152, 1152), (2176, 4608, 1152), (4352, 1152, 4608),
+               (768, 640, 72)]
+
+
+@pytest.mark.parametrize("M,N,K", PAIR_SHAPES)
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, False), (True, True)])
+def test_gemm_cta_pair_matches_single(M, N, K, a_mn, b_mn):
+    """The CTA-pair (cta_group::2) kernel and the single-CTA kernel against fp32."""
+    A = (torch.randn(K, M) if a_mn else torch.randn(M, K)).to(torch.bfloat16).cuda()
+    B = (torch.randn(K, N) if b_mn else torch.randn(N, K)).to(torch.bfloat16).cuda()
+    ref = _ref(A, a_mn, B, b_mn)
+    tol = 2e-2 * math.sqrt(K) + 1e-2
+    prev = torch.ops.harp.gemm_pair_mode(1)
+    try:
+        c_pair = _gemm(A, a_mn, B, b_mn, M, N, K, epi=1)
+        torch.ops.harp.gemm_pair_mode(0)
+        c_one = _gemm(A, a_mn, B, b_mn, M, N, K, epi=1)
+    finally:
+        torch.ops.harp.gemm_pair_mode(prev)
+    assert (c_pair - ref).abs().max().item() < tol
+    assert (c_one - ref).abs().max().item() < tol
+    # same products summed in the same k order: fp32 results agree closely
+    assert (c_pair - c_one).abs().max().item() < 1e-3 * math.sqrt(K)
+
+
+@pytest.mark.parametrize("pair", [0, 1])
+def test_gemm_epilogues_modes(pair):
+    prev = torch.ops.harp.gemm_pair_mode(pair)
+    try:
+        test_gemm_epilogues()
+    finally:
+        torch.ops.harp.gemm_pair_mode(prev)
+
+
 def test_gemm_epilogues():
     M, N, K, B_ = 512, 384, 192, 4
     A = torch.randn(M, K, device="cuda").to(torch.bfloat16)
