@@ -463,10 +463,17 @@ struct BwdCfg {
   static constexpr bool DQ_SEPARATE = (3 * DPAD <= 256);
   static constexpr int DQ_COL = DQ_SEPARATE ? 256 + 2 * DPAD : 0;
 };
-constexpr int kBwdThreads = 320;  // w0 TMA, w1 MMA, w2-5 dS warps, w6-9 dQ warps
+constexpr int kBwdThreads = 320;  // overlapped schedule: w0 TMA, w1 MMA, w2-5 / w6-9 half-tile warps
+// Single-tile schedule: w0 TMA, w1 MMA, w2-5 dS warps (key columns 0-63), w6-9
+// dQ warps, w10-13 dS warps (columns 64-127).  Two dS warps per SM sub-partition
+// hide each other's TMEM-load and exp latencies.
+constexpr int kBwdThreads1 = 448;
+// TMEM column of the packed bf16 P^T / dS^T for queries [32c, 32c + 32):
+// chunks 0-1 (warps 2-5) at 0-31, chunks 2-3 (warps 10-13) at 64-95.
+__device__ __forceinline__ constexpr uint32_t pcol(int c) { return c * 16 + (c >= 2 ? 32 : 0); }
 
 template <int NCH>
-__global__ void __launch_bounds__(kBwdThreads, 1)
+__global__ void __launch_bounds__(kBwdThreads1, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
                     const __grid_constant__ CUtensorMap tmdQ, const BwdArgs a) {
@@ -509,7 +516,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       mbar_init(&qdo_empty[s], 1);
     }
     mbar_init(s_full, 1);
-    mbar_init(p_full, 4);
+    mbar_init(p_full, 8);
     mbar_init(dq_full, 1);
     mbar_init(dq_free, 4);
     mbar_init(fin, 1);
@@ -584,10 +591,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         tc_fence_after();
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks)
-          mma_ts(tdV, tS + ks * 8, mnmajor_desc(doa, ks), idO, (i > 0 || ks > 0) ? 1u : 0u);
+          mma_ts(tdV, tS + pcol(ks / 2) + (ks & 1) * 8, mnmajor_desc(doa, ks), idO, (i > 0 || ks > 0) ? 1u : 0u);
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks)
-          mma_ts(tdK, tdP + ks * 8, mnmajor_desc(qa, ks), idO, (i > 0 || ks > 0) ? 1u : 0u);
+          mma_ts(tdK, tdP + pcol(ks / 2) + (ks & 1) * 8, mnmajor_desc(qa, ks), idO, (i > 0 || ks > 0) ? 1u : 0u);
         if (C::DQ_SEPARATE && i > 0) {
           if (!mbar_wait(dq_free, (i - 1) & 1, err, 64)) { ok = false; break; }
           tc_fence_after();
@@ -601,9 +608,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       mma_commit(fin);
       mbar_wait_drain(fin, 0);
     }
-  } else if (warp >= 2 && warp < 6) {
-    // ---------------- dS warps: thread = key row ----------------
+  } else if ((warp >= 2 && warp < 6) || warp >= 10) {
+    // ---------------- dS warps: thread = key row, half of the query columns ----------------
     const int quarter = warp & 3;
+    const int c_begin = warp >= 10 ? 2 : 0;  // 32-column chunks [c_begin, c_begin + 2)
     const int kr = quarter * 32 + lane;
     const int key = k0 + kr;
     const bool key_ok = key < a.Skv;
@@ -619,7 +627,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const float2 kmask = make_float2(key_ok ? 1.f : 0.f, key_ok ? 1.f : 0.f);
       const float2 nl2e = make_float2(-kLog2e, -kLog2e);
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
+      for (int c = c_begin; c < c_begin + 2; ++c) {
         uint32_t s[32], dp[32];
         tmem_ld32(tS + lane_off + c * 32, s);
         tmem_ld32(tdP + lane_off + c * 32, dp);
@@ -645,8 +653,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             dd[k2] = pack_bf16x2(ds.x, ds.y);
           }
         }
-        tmem_st16(tS + lane_off + c * 16, pp);
-        tmem_st16(tdP + lane_off + c * 16, dd);
+        // P^T / dS^T (bf16 pairs) of queries [32c, 32c+32) go to columns
+        // pcol(c): the warp's own columns that it has already read, so the two
+        // warps of a lane quarter never overwrite scores the other still reads
+        tmem_st16(tS + lane_off + pcol(c), pp);
+        tmem_st16(tdP + lane_off + pcol(c), dd);
 #pragma unroll
         for (int g = 0; g < 4; ++g)
           *reinterpret_cast<uint4*>(sdS + (c * 4 + g) * 2048 + kr * 16) =
@@ -659,30 +670,32 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       if (warp == 2 && lane == 0) BWD_PROBE(i, 5);
       if (lane == 0) mbar_arrive(p_full);
     }
-    if (ok) ok = mbar_wait(fin, 0, err, 71);
-    tc_fence_after();
-    bf16* vrow = a.dV + (long)(b * a.Skv + key) * a.lddv + h * a.Dh;
+    if (warp < 10) {  // dV is stored by warps 2-5
+      if (ok) ok = mbar_wait(fin, 0, err, 71);
+      tc_fence_after();
+      bf16* vrow = a.dV + (long)(b * a.Skv + key) * a.lddv + h * a.Dh;
 #pragma unroll
-    for (int c = 0; c < C::DPAD; c += 16) {
-      uint32_t v[16];
-      tmem_ld16(tdV + lane_off + c, v);
-      tmem_wait_ld();
-      if (key_ok && ok) {
+      for (int c = 0; c < C::DPAD; c += 16) {
+        uint32_t v[16];
+        tmem_ld16(tdV + lane_off + c, v);
+        tmem_wait_ld();
+        if (key_ok && ok) {
 #pragma unroll
-        for (int g = 0; g < 2; ++g) {
-          const int d = c + 8 * g;
-          if (d < a.Dh) {
-            uint4 pk;
-            pk.x = pack_bf16x2(__uint_as_float(v[8 * g + 0]), __uint_as_float(v[8 * g + 1]));
-            pk.y = pack_bf16x2(__uint_as_float(v[8 * g + 2]), __uint_as_float(v[8 * g + 3]));
-            pk.z = pack_bf16x2(__uint_as_float(v[8 * g + 4]), __uint_as_float(v[8 * g + 5]));
-            pk.w = pack_bf16x2(__uint_as_float(v[8 * g + 6]), __uint_as_float(v[8 * g + 7]));
-            *reinterpret_cast<uint4*>(vrow + d) = pk;
+          for (int g = 0; g < 2; ++g) {
+            const int d = c + 8 * g;
+            if (d < a.Dh) {
+              uint4 pk;
+              pk.x = pack_bf16x2(__uint_as_float(v[8 * g + 0]), __uint_as_float(v[8 * g + 1]));
+              pk.y = pack_bf16x2(__uint_as_float(v[8 * g + 2]), __uint_as_float(v[8 * g + 3]));
+              pk.z = pack_bf16x2(__uint_as_float(v[8 * g + 4]), __uint_as_float(v[8 * g + 5]));
+              pk.w = pack_bf16x2(__uint_as_float(v[8 * g + 6]), __uint_as_float(v[8 * g + 7]));
+              *reinterpret_cast<uint4*>(vrow + d) = pk;
+            }
           }
         }
       }
     }
-  } else if (warp >= 6) {
+  } else if (warp >= 6 && warp < 10) {
     // ---------------- dQ warps: thread = query row of the dQ partial ----------------
     const int quarter = warp & 3;
     const int qr = quarter * 32 + lane;
@@ -1158,7 +1171,7 @@ void launch_bwd(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap&
   }
   const int nkt = (args.Skv + 127) / 128;
   const int grid = args.B * args.H * nkt;
-  kern<<<grid, kBwdThreads, C::SMEM, stream>>>(mq, mk, mv, mdo, mdq, args);
+  kern<<<grid, which == 0 ? kBwdThreads1 : kBwdThreads, C::SMEM, stream>>>(mq, mk, mv, mdo, mdq, args);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   count_launch();
 }
