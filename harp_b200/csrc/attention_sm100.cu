@@ -45,6 +45,27 @@ __device__ __forceinline__ float ex2_approx(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+// 2^x for a pair on the FMA pipe, so that part of a softmax tile's
+// exponentials runs beside the MUFU instead of queueing on it.  Method: Cody
+// and Waite style range reduction x = j + f with j = round(x) (the 1.5 * 2^23
+// shifter makes the FP add round to an integer), f in [-1/2, 1/2]; 2^f by a
+// cubic fitted here to 2^f on that interval (iteratively reweighted least
+// squares on the relative error, max relative error 7.5e-5, far below the
+// bf16 rounding of P); 2^j by adding j to the exponent field.  x is clamped to
+// >= -125 so the exponent add cannot wrap (2^-125 stands in for 0).
+__device__ __forceinline__ float2 ex2_poly2(float2 x) {
+  constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
+  x.x = fmaxf(x.x, -125.0f);
+  x.y = fmaxf(x.y, -125.0f);
+  const float2 t = __fadd2_rn(x, make_float2(kShift, kShift));
+  const float2 j = __fadd2_rn(t, make_float2(-kShift, -kShift));
+  const float2 f = __fadd2_rn(x, make_float2(-j.x, -j.y));
+  float2 p = __ffma2_rn(make_float2(0.05517132f, 0.05517132f), f, make_float2(0.24261054f, 0.24261054f));
+  p = __ffma2_rn(p, f, make_float2(0.69326099f, 0.69326099f));
+  p = __ffma2_rn(p, f, make_float2(0.99992811f, 0.99992811f));
+  return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(t.x) << 23)),
+                     __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23)));
+}
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -110,6 +131,12 @@ __device__ __forceinline__ uint64_t mnmajor_desc(uint32_t tile_addr, int ks) {
 // ===========================================================================
 // Forward
 // ===========================================================================
+__device__ unsigned long long g_bwd_probe[64 * 16];
+#define FWD_PROBE(i, slot)                                                                              \
+  do {                                                                                                  \
+    if (a.probe && blockIdx.x == 0 && (i) < 64) g_bwd_probe[(i) * 16 + (slot)] = globaltimer_ns();    \
+  } while (0)
+
 struct FwdArgs {
   int B, Sq, Skv, H, Dh;
   float scale_log2;
@@ -124,6 +151,8 @@ struct FwdArgs {
   int strip5;  // tensor maps are the one-instruction 5-D strip form
   int wait_q;  // queries arrive by chunk too (same flags): wait before loading a Q tile
   int q_rot;   // query-pair index rotation (start with the pairs whose chunk is local)
+  int probe;   // record key-tile step timestamps of CTA 0 (HARP_ATTN_PROBE=1)
+  int npoly;   // of every 16 exponential pairs of a row chunk, the first npoly run on the FMA pipe
   unsigned long long timeout_ns;
   int* err;
 };
@@ -137,7 +166,7 @@ struct FwdCfg {
 };
 constexpr int kFwdThreads = 384;  // w0 TMA, w1 MMA, w2-3 spare, w4-7 softmax tile 0, w8-11 softmax tile 1
 
-template <int NCH>
+template <int NCH, int NPOLY>
 __global__ void __launch_bounds__(kFwdThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const FwdArgs a) {
@@ -269,6 +298,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         const uint32_t va = smem_u32(sV + st * C::TILE);
         for (int t = 0; t < ntile; ++t) {
           if (!mbar_wait(&p_full[t], jj & 1, err, 33)) { ok = false; break; }
+          FWD_PROBE(jj, t);
           tc_fence_after();
 #pragma unroll
           for (int ks = 0; ks < 8; ++ks)
@@ -281,6 +311,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             }
             issue_S(t, st2);
             mma_commit(&s_full[t]);
+            FWD_PROBE(jj, 2 + t);
           }
         }
         if (!ok) break;
@@ -304,6 +335,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         const int j = (a.start_tile + jj) % nkv;
         const int nvalid = min(128, a.Skv - j * 128);
         if (!mbar_wait(&s_full[t], jj & 1, err, 40)) { ok = false; break; }
+        if (quarter == 0 && lane == 0) FWD_PROBE(jj, 4 + 3 * t);
         tc_fence_after();
         const bool full_tile = (nvalid == 128);  // only the last key tile of a sequence is partial
         float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
@@ -327,6 +359,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           }
         }
         const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
+        if (quarter == 0 && lane == 0) FWD_PROBE(jj, 5 + 3 * t);
         const float m_new = fmaxf(m, mx * a.scale_log2);
         const bool need = m_new > m + kRescaleThreshold;
         if (__any_sync(0xffffffffu, need)) {
@@ -363,7 +396,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
               if (k >= nvalid) x.x = -INFINITY;
               if (k + 1 >= nvalid) x.y = -INFINITY;
             }
-            const float2 p = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+            const float2 p = (i < NPOLY) ? ex2_poly2(x) : make_float2(ex2_approx(x.x), ex2_approx(x.y));
             lacc = __fadd2_rn(lacc, p);
             pk[i] = pack_bf16x2(p.x, p.y);
           }
@@ -374,6 +407,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[t]);
+        if (quarter == 0 && lane == 0) FWD_PROBE(jj, 6 + 3 * t);
       }
       if (ok) ok = mbar_wait(o_final, 0, err, 41);
       tc_fence_after();
@@ -436,9 +470,9 @@ struct BwdArgs {
   int skip_dq;  // HARP_ATTN_DEBUG_SKIP_DQ=1: leave dQ out (timing experiments; dQ is then wrong)
 };
 
-// Phase timeline of one CTA of the backward kernels: 64 query tiles x 16
-// slots of %globaltimer values, read back with attn_bwd_probe().
-__device__ unsigned long long g_bwd_probe[64 * 16];
+// Phase timeline of CTA 0 of the backward kernels: 64 query tiles x 16 slots
+// of %globaltimer values, read back with attn_bwd_probe() (the forward kernel
+// records its key-tile steps into the same buffer).
 #define BWD_PROBE(i, slot)                                                                              \
   do {                                                                                                  \
     if (a.probe && blockIdx.x == 0 && (i) < 64) g_bwd_probe[(i) * 16 + (slot)] = globaltimer_ns();    \
@@ -743,6 +777,386 @@ __global__ void __launch_bounds__(kBwdThreads1, 1)
     }
     if (warp == 6 && lane == 0) bulk_wait_all();
     if (ok) ok = mbar_wait(fin, 0, err, 81);
+    tc_fence_after();
+    const int key = k0 + qr;
+    bf16* krow = a.dK + (long)(b * a.Skv + key) * a.lddk + h * a.Dh;
+#pragma unroll
+    for (int c = 0; c < C::DPAD; c += 16) {
+      uint32_t v[16];
+      tmem_ld16(tdK + lane_off + c, v);
+      tmem_wait_ld();
+      if (key < a.Skv && ok) {
+#pragma unroll
+        for (int g = 0; g < 2; ++g) {
+          const int d = c + 8 * g;
+          if (d < a.Dh) {
+            uint4 pk;
+            pk.x = pack_bf16x2(__uint_as_float(v[8 * g + 0]) * a.scale, __uint_as_float(v[8 * g + 1]) * a.scale);
+            pk.y = pack_bf16x2(__uint_as_float(v[8 * g + 2]) * a.scale, __uint_as_float(v[8 * g + 3]) * a.scale);
+            pk.z = pack_bf16x2(__uint_as_float(v[8 * g + 4]) * a.scale, __uint_as_float(v[8 * g + 5]) * a.scale);
+            pk.w = pack_bf16x2(__uint_as_float(v[8 * g + 6]) * a.scale, __uint_as_float(v[8 * g + 7]) * a.scale);
+            *reinterpret_cast<uint4*>(krow + d) = pk;
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ===========================================================================
+// Backward, pipelined schedule (head_dim <= 80).  Same products as
+// attn_bwd_kernel, but P^T and dS go to shared memory rather than back into
+// TMEM, and the dS warps hand the S/dP columns back as soon as they hold the
+// scores in registers.  The MMA warp therefore issues S/dP of query tile i+1
+// before dV/dK/dQ of tile i, and the tensor pipe computes the next scores
+// while the dS warps turn this tile's scores into P and dS:
+//   s_full  MMA -> dS warps   S(i), dP(i) are in TMEM
+//   s_free  dS warps -> MMA   S(i), dP(i) are in registers; columns reusable
+//   p_full  dS warps -> MMA   P^T(i), dS(i) are in shared memory
+//   p_free  MMA -> dS warps   dV/dK/dQ(i) have read them
+//   dq_full / dq_free         dQ(i) in TMEM / read out by the dQ warps
+// The Q/dO stage of tile i goes back to the TMA warp when dV(i) and dK(i) are
+// done; dQ partials are staged in a buffer of their own for the TMA reduce.
+// ===========================================================================
+template <int NCH>
+struct BwdPipeCfg {
+  static constexpr int DPAD = NCH * 8;
+  static constexpr int TILE = NCH * 2048;
+  static constexpr int PS_BYTES = 128 * 128 * 2;  // one 128 x 128 bf16 operand (P^T or dS)
+  // Every operand here needs 16-byte alignment only (no-swizzle layouts), which
+  // dynamic shared memory always has, so there is no alignment slack; 128
+  // bytes hold the 15 barriers and the TMEM address.
+  static constexpr int LD_BYTES = 2 * 256 * 4;     // lse | delta of a query tile, double-buffered
+  static constexpr int smem_for(int st) { return 2 * TILE + st * 2 * TILE + 2 * PS_BYTES + LD_BYTES + 128; }
+  static constexpr int STAGES = smem_for(3) <= 232448 ? 3 : 2;
+  static constexpr int SMEM = smem_for(STAGES);
+  static_assert(SMEM <= 232448, "exceeds the 227 KB per-CTA shared memory limit");
+  static_assert(3 * DPAD <= 256, "dV, dK and dQ need columns of their own beside S and dP");
+  static_assert(2 * TILE >= 128 * DPAD * 4, "dQ staging (128 x Dh fp32) must fit in one Q/dO stage");
+  static constexpr int DV_COL = 256;
+  static constexpr int DK_COL = 256 + DPAD;
+  static constexpr int DQ_COL = 256 + 2 * DPAD;
+};
+// Four warpgroups: WG0 = w0 TMA, w1 MMA (w2-3 idle); WG1 = w4-7 and WG2 = w8-11
+// dS warps (query columns 0-63 / 64-127); WG3 = w12-15 dQ warps.  The dS warps
+// hold a tile's S and dP for 64 columns in registers, so registers move to
+// them with setmaxnreg: 80 + 168 + 168 + 96 = 512 = 4 x 128, the launch's
+// per-thread budget for 512 threads.
+constexpr int kBwdPipeThreads = 512;
+constexpr int kPipeRegsCtl = 80, kPipeRegsDs = 168, kPipeRegsDq = 96;
+static_assert(kPipeRegsCtl + 2 * kPipeRegsDs + kPipeRegsDq == 4 * (65536 / kBwdPipeThreads),
+              "warpgroup register split must add up to the launch budget");
+
+template <int NCH>
+__global__ void __launch_bounds__(kBwdPipeThreads, 1)
+    attn_bwd_pipe_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                         const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
+                         const __grid_constant__ CUtensorMap tmdQ, const BwdArgs a) {
+  using C = BwdPipeCfg<NCH>;
+  constexpr int ST = C::STAGES;
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  uint8_t* sK = smem_raw;
+  uint8_t* sV = sK + C::TILE;
+  // stage st: Q at 2*st*TILE, dO right after; once dV/dK of the tile are done
+  // the dQ warps reuse the stage to stage the fp32 dQ partial for the reduce
+  uint8_t* sQD = sV + C::TILE;
+  uint8_t* sP = sQD + 2 * ST * C::TILE;  // P^T: keys x queries, 8-query strips
+  uint8_t* sdS = sP + C::PS_BYTES;       // dS, same layout
+  float* sLD = reinterpret_cast<float*>(sdS + C::PS_BYTES);  // [2][lse 128 | delta 128]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(sLD) + C::LD_BYTES);
+  uint64_t* kv_full = bars;
+  uint64_t* qdo_full = bars + 1;        // [ST]
+  uint64_t* qdo_empty = qdo_full + ST;  // [ST]
+  uint64_t* s_full = qdo_empty + ST;
+  uint64_t* s_free = s_full + 1;
+  uint64_t* p_full = s_free + 1;
+  uint64_t* p_free = p_full + 1;
+  uint64_t* dq_full = p_free + 1;
+  uint64_t* dq_free = dq_full + 1;
+  uint64_t* dqs_bar = dq_free + 1;
+  uint64_t* fin = dqs_bar + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fin + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int nkt = (a.Skv + 127) / 128;
+  const int bh = blockIdx.x / nkt, kt = blockIdx.x % nkt;
+  const int b = bh / a.H, h = bh % a.H;
+  const int k0 = kt * 128;
+  const int nq = (a.Sq + 127) / 128;
+  int* err = a.err;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(&qdo_full[s], 1);
+      mbar_init(&qdo_empty[s], 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(s_free, 8);
+    mbar_init(p_full, 8);
+    mbar_init(p_free, 1);
+    mbar_init(dq_full, 1);
+    mbar_init(dq_free, 4);
+    mbar_init(dqs_bar, 4);
+    mbar_init(fin, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS = tmem, tdP = tmem + 128, tdV = tmem + C::DV_COL, tdK = tmem + C::DK_COL,
+                 tdQ = tmem + C::DQ_COL;
+  const int wg = warp / 4;
+
+  // each role's code sits inside the branch that sets its register budget
+  if (wg == 0) {
+   asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kPipeRegsCtl));
+   if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      tma_prefetch_desc(&tmdO);
+      int issued[4] = {0, 0, 0, 0};
+      bool ok = true;
+      mbar_arrive_expect_tx(kv_full, 2 * C::TILE);
+      load_strip_tile<NCH>(sK, &tmK, kv_full, k0, h, b, a.strip5);
+      load_strip_tile<NCH>(sV, &tmV, kv_full, k0, h, b, a.strip5);
+      for (int i = 0; i < nq && ok; ++i) {
+        const int st = i % ST;
+        const uint32_t ph = (i / ST) & 1;
+        if (!mbar_wait(&qdo_empty[st], ph ^ 1, err, 150)) { ok = false; break; }
+        BWD_PROBE(i, 10);
+        mbar_arrive_expect_tx(&qdo_full[st], 2 * C::TILE);
+        load_strip_tile<NCH>(sQD + 2 * st * C::TILE, &tmQ, &qdo_full[st], i * 128, h, b, a.strip5);
+        load_strip_tile<NCH>(sQD + (2 * st + 1) * C::TILE, &tmdO, &qdo_full[st], i * 128, h, b, a.strip5);
+        issued[st]++;
+      }
+      mbar_wait_drain(kv_full, 0);
+      for (int s = 0; s < ST; ++s)
+        if (issued[s]) mbar_wait_drain(&qdo_full[s], (issued[s] - 1) & 1);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idS = make_idesc_bf16(128, 128, false, false);
+      constexpr uint32_t idO = make_idesc_bf16(128, C::DPAD, false, true);
+      constexpr uint32_t idQ = make_idesc_bf16(128, C::DPAD, true, true);
+      const uint32_t ka = smem_u32(sK), va = smem_u32(sV), pa = smem_u32(sP), dsa = smem_u32(sdS);
+      // dV(j) += P^T(j) dO(j), dK(j) += dS^T(j) Q(j), dQ(j) = dS(j) K
+      auto rest = [&](int j) -> bool {
+        const int stj = j % ST;
+        if (!mbar_wait(p_full, j & 1, err, 163)) return false;
+        BWD_PROBE(j, 1);
+        tc_fence_after();
+        const uint32_t qa = smem_u32(sQD + 2 * stj * C::TILE), doa = smem_u32(sQD + (2 * stj + 1) * C::TILE);
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks)
+          mma_ss(tdV, kmajor_desc(pa, ks), mnmajor_desc(doa, ks), idO, (j > 0 || ks > 0) ? 1u : 0u);
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks)
+          mma_ss(tdK, kmajor_desc(dsa, ks), mnmajor_desc(qa, ks), idO, (j > 0 || ks > 0) ? 1u : 0u);
+        if (j > 0) {
+          if (!mbar_wait(dq_free, (j - 1) & 1, err, 164)) return false;
+          tc_fence_after();
+        }
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks)
+          mma_ss(tdQ, mnmajor_desc(dsa, ks), mnmajor_desc(ka, ks), idQ, ks > 0 ? 1u : 0u);
+        mma_commit(p_free);
+        mma_commit(dq_full);
+        BWD_PROBE(j, 3);
+        return true;
+      };
+      bool ok = mbar_wait(kv_full, 0, err, 160);
+      for (int i = 0; i < nq && ok; ++i) {
+        const int st = i % ST;
+        const uint32_t ph = (i / ST) & 1;
+        if (!mbar_wait(&qdo_full[st], ph, err, 161)) { ok = false; break; }
+        if (i > 0 && !mbar_wait(s_free, (i - 1) & 1, err, 162)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t qa = smem_u32(sQD + 2 * st * C::TILE), doa = smem_u32(sQD + (2 * st + 1) * C::TILE);
+#pragma unroll
+        for (int ks = 0; ks < NCH / 2; ++ks)
+          mma_ss(tS, kmajor_desc(ka, ks), kmajor_desc(qa, ks), idS, ks > 0 ? 1u : 0u);
+#pragma unroll
+        for (int ks = 0; ks < NCH / 2; ++ks)
+          mma_ss(tdP, kmajor_desc(va, ks), kmajor_desc(doa, ks), idS, ks > 0 ? 1u : 0u);
+        mma_commit(s_full);
+        BWD_PROBE(i, 0);
+        if (i > 0) ok = rest(i - 1);
+      }
+      if (ok && nq > 0) ok = rest(nq - 1);
+      mma_commit(fin);
+      mbar_wait_drain(fin, 0);
+    }
+   }
+  } else if (wg == 1 || wg == 2) {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kPipeRegsDs));
+    // ---------------- dS warps: thread = key row, 64 of the 128 query columns ----------------
+    const int quarter = warp & 3;
+    const int c_begin = wg == 2 ? 2 : 0;
+    const int kr = quarter * 32 + lane;
+    const int key = k0 + kr;
+    const bool key_ok = key < a.Skv;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const float2 scl = make_float2(a.scale_log2, a.scale_log2);
+    const float2 kmask = make_float2(key_ok ? 1.f : 0.f, key_ok ? 1.f : 0.f);
+    const float2 nl2e = make_float2(-kLog2e, -kLog2e);
+    bool ok = true;
+    const int ldt = (wg - 1) * 128 + kr;  // 0..255 over the eight dS warps
+    const float* ld_src = (ldt < 128 ? a.lse : a.delta) + (long)(b * a.H + h) * a.lse_ld + (ldt & 127);
+    // All eight dS warps run every iteration (errors only make the bounded
+    // waits return at once), so the named barrier always sees 256 threads.
+    for (int i = 0; i < nq; ++i) {
+      // lse / delta of the tile's 128 queries (+inf / 0 past Sq) into the
+      // buffer of this tile's parity; the barrier also means every dS warp is
+      // done with tile i-2, the buffer's previous user
+      float* ldb = sLD + (i & 1) * 256;
+      ldb[ldt] = __ldg(ld_src + i * 128);
+      asm volatile("bar.sync 2, 256;" ::: "memory");
+      if (!mbar_wait(s_full, i & 1, err, 170)) ok = false;
+      if (warp == 4 && lane == 0) BWD_PROBE(i, 4);
+      tc_fence_after();
+      uint32_t s[2][32], dp[2][32];
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        tmem_ld32(tS + lane_off + (c_begin + cc) * 32, s[cc]);
+        tmem_ld32(tdP + lane_off + (c_begin + cc) * 32, dp[cc]);
+      }
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(s_free);  // the MMA warp may overwrite S / dP now
+      const float* sL = ldb;
+      const float* sDl = ldb + 128;
+      uint32_t pp[2][16], dd[2][16];
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        const int c = c_begin + cc;
+#pragma unroll
+        for (int k4 = 0; k4 < 8; ++k4) {
+          const float4 L4 = *reinterpret_cast<const float4*>(sL + c * 32 + 4 * k4);  // smem broadcast
+          const float4 D4 = *reinterpret_cast<const float4*>(sDl + c * 32 + 4 * k4);
+#pragma unroll
+          for (int h2 = 0; h2 < 2; ++h2) {
+            const int k2 = 2 * k4 + h2;
+            const float2 Lp = h2 ? make_float2(L4.z, L4.w) : make_float2(L4.x, L4.y);
+            const float2 Dp = h2 ? make_float2(D4.z, D4.w) : make_float2(D4.x, D4.y);
+            const float2 x = __ffma2_rn(make_float2(__uint_as_float(s[cc][2 * k2]), __uint_as_float(s[cc][2 * k2 + 1])),
+                                        scl, __fmul2_rn(Lp, nl2e));
+            const float2 p = __fmul2_rn(make_float2(ex2_approx(x.x), ex2_approx(x.y)), kmask);
+            const float2 ds = __fmul2_rn(
+                p, __fadd2_rn(make_float2(__uint_as_float(dp[cc][2 * k2]), __uint_as_float(dp[cc][2 * k2 + 1])),
+                              make_float2(-Dp.x, -Dp.y)));
+            pp[cc][k2] = pack_bf16x2(p.x, p.y);
+            dd[cc][k2] = pack_bf16x2(ds.x, ds.y);
+          }
+        }
+      }
+      // the previous tile's dV/dK/dQ must be done reading P^T / dS
+      if (i > 0 && !mbar_wait(p_free, (i - 1) & 1, err, 171)) ok = false;
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        const int c = c_begin + cc;
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          *reinterpret_cast<uint4*>(sP + (c * 4 + g) * 2048 + kr * 16) =
+              make_uint4(pp[cc][4 * g], pp[cc][4 * g + 1], pp[cc][4 * g + 2], pp[cc][4 * g + 3]);
+          *reinterpret_cast<uint4*>(sdS + (c * 4 + g) * 2048 + kr * 16) =
+              make_uint4(dd[cc][4 * g], dd[cc][4 * g + 1], dd[cc][4 * g + 2], dd[cc][4 * g + 3]);
+        }
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (warp == 4 && lane == 0) BWD_PROBE(i, 5);
+      if (lane == 0) mbar_arrive(p_full);
+    }
+    if (wg == 1) {  // dV is stored by warpgroup 1
+      if (ok) ok = mbar_wait(fin, 0, err, 172);
+      tc_fence_after();
+      bf16* vrow = a.dV + (long)(b * a.Skv + key) * a.lddv + h * a.Dh;
+#pragma unroll
+      for (int c = 0; c < C::DPAD; c += 16) {
+        uint32_t v[16];
+        tmem_ld16(tdV + lane_off + c, v);
+        tmem_wait_ld();
+        if (key_ok && ok) {
+#pragma unroll
+          for (int g = 0; g < 2; ++g) {
+            const int d = c + 8 * g;
+            if (d < a.Dh) {
+              uint4 pk;
+              pk.x = pack_bf16x2(__uint_as_float(v[8 * g + 0]), __uint_as_float(v[8 * g + 1]));
+              pk.y = pack_bf16x2(__uint_as_float(v[8 * g + 2]), __uint_as_float(v[8 * g + 3]));
+              pk.z = pack_bf16x2(__uint_as_float(v[8 * g + 4]), __uint_as_float(v[8 * g + 5]));
+              pk.w = pack_bf16x2(__uint_as_float(v[8 * g + 6]), __uint_as_float(v[8 * g + 7]));
+              *reinterpret_cast<uint4*>(vrow + d) = pk;
+            }
+          }
+        }
+      }
+    }
+  } else {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kPipeRegsDq));
+    // ---------------- dQ warps (12-15): thread = query row of the dQ partial ----------------
+    const int quarter = warp & 3;
+    const int qr = quarter * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    bool ok = true;
+    // after an error the bounded waits return at once and the loop runs out
+    for (int i = 0; i < nq; ++i) {
+      if (!mbar_wait(dq_full, i & 1, err, 180)) ok = false;
+      if (warp == 12 && lane == 0) BWD_PROBE(i, 6);
+      tc_fence_after();
+      const int st = i % ST;
+      float* stage = reinterpret_cast<float*>(sQD + 2 * st * C::TILE);  // [128][Dh] fp32
+      float* srow = stage + qr * a.Dh;
+#pragma unroll
+      for (int c = 0; c < C::DPAD; c += 16) {
+        uint32_t v[16];
+        tmem_ld16(tdQ + lane_off + c, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          const int d = c + 4 * g;
+          if (d < a.Dh)
+            *reinterpret_cast<float4*>(srow + d) =
+                make_float4(__uint_as_float(v[4 * g]), __uint_as_float(v[4 * g + 1]), __uint_as_float(v[4 * g + 2]),
+                            __uint_as_float(v[4 * g + 3]));
+        }
+      }
+      tc_fence_before();
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(dq_free);
+        mbar_arrive(dqs_bar);
+      }
+      if (warp == 12 && lane == 0) {
+        if (!mbar_wait(dqs_bar, i & 1, err, 182)) ok = false;
+        if (ok) {
+          BWD_PROBE(i, 7);
+          if (!a.skip_dq) tma_reduce_add_4d(&tmdQ, stage, 0, h, i * 128, b);
+          bulk_wait_read_all();
+          BWD_PROBE(i, 9);
+        }
+        mbar_arrive(&qdo_empty[st]);  // the stage goes back to the TMA warp
+      }
+    }
+    if (warp == 12 && lane == 0) bulk_wait_all();
+    if (ok) ok = mbar_wait(fin, 0, err, 181);
     tc_fence_after();
     const int key = k0 + qr;
     bf16* krow = a.dK + (long)(b * a.Skv + key) * a.lddk + h * a.Dh;
@@ -1121,14 +1535,18 @@ template <int NCH>
 void launch_fwd(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const FwdArgs& args,
                 cudaStream_t stream) {
   using C = FwdCfg<NCH>;
+  auto* kern = args.npoly >= 8 ? attn_fwd_kernel<NCH, 8> : (args.npoly >= 4 ? attn_fwd_kernel<NCH, 4>
+                                                                            : attn_fwd_kernel<NCH, 0>);
   static bool configured = false;
   if (!configured) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_kernel<NCH>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    C10_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_kernel<NCH, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    C10_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_kernel<NCH, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    C10_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_kernel<NCH, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     configured = true;
   }
   const int nqp = (args.Sq + 255) / 256;
   const int grid = args.B * args.H * nqp;
-  attn_fwd_kernel<NCH><<<grid, kFwdThreads, C::SMEM, stream>>>(mq, mk, mv, args);
+  kern<<<grid, kFwdThreads, C::SMEM, stream>>>(mq, mk, mv, args);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   count_launch();
 }
@@ -1155,9 +1573,44 @@ bool bwd_overlap_enabled() {
   return on;
 }
 
+// HARP_ATTN_BWD_PIPE=0 keeps head dims <= 80 on the single-tile schedule
+// (comparisons); by default they take the pipelined one.
+bool bwd_pipe_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("HARP_ATTN_BWD_PIPE");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 template <int NCH>
 void launch_bwd(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mdo,
                 const CUtensorMap& mdq, const BwdArgs& args, cudaStream_t stream) {
+  if constexpr (3 * NCH * 8 <= 256) {
+    using P = BwdPipeCfg<NCH>;
+    // The setmaxnreg split assumes the kernel launches with exactly 128
+    // registers per thread (512 x 128 = the register file); with any other
+    // count the increase could never be granted, so such a build keeps the
+    // single-tile schedule.
+    static const bool pipe_ok = [] {
+      C10_CUDA_CHECK(
+          cudaFuncSetAttribute(attn_bwd_pipe_kernel<NCH>, cudaFuncAttributeMaxDynamicSharedMemorySize, P::SMEM));
+      cudaFuncAttributes fa;
+      C10_CUDA_CHECK(cudaFuncGetAttributes(&fa, attn_bwd_pipe_kernel<NCH>));
+      const bool ok = fa.numRegs * kBwdPipeThreads == 65536;
+      if (!ok)
+        TORCH_WARN_ONCE("harp attention: pipelined backward built with ", fa.numRegs,
+                        " registers per thread; using the single-tile schedule");
+      return ok;
+    }();
+    if (bwd_pipe_enabled() && !bwd_overlap_enabled() && pipe_ok) {
+      const int grid = args.B * args.H * ((args.Skv + 127) / 128);
+      attn_bwd_pipe_kernel<NCH><<<grid, kBwdPipeThreads, P::SMEM, stream>>>(mq, mk, mv, mdo, mdq, args);
+      C10_CUDA_KERNEL_LAUNCH_CHECK();
+      count_launch();
+      return;
+    }
+  }
   using C = BwdCfg<NCH>;
   auto* kern = attn_bwd_kernel<NCH>;
   if constexpr (C::DQ_SEPARATE) {
@@ -1208,6 +1661,16 @@ void attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, int
   }
   FwdArgs args;
   args.strip5 = s5 ? 1 : 0;
+  static const bool probe = [] {
+    const char* e = std::getenv("HARP_ATTN_PROBE");
+    return e != nullptr && e[0] == '1';
+  }();
+  args.probe = probe ? 1 : 0;
+  static const int npoly = [] {
+    const char* e = std::getenv("HARP_ATTN_POLY");
+    return e != nullptr ? std::max(0, std::min(16, std::atoi(e))) : 0;
+  }();
+  args.npoly = npoly;
   args.B = B; args.Sq = Sq; args.Skv = Skv; args.H = H; args.Dh = Dh;
   args.scale_log2 = (float)(scale * 1.4426950408889634);
   args.O = reinterpret_cast<bf16*>(o.data_ptr());
@@ -1301,6 +1764,33 @@ at::Tensor attn_bwd_probe() {
   return out;
 }
 
+namespace {
+__global__ void exp2_poly_kernel(const float* __restrict__ x, float* __restrict__ y, long n) {
+  const long i = 2 * ((long)blockIdx.x * blockDim.x + threadIdx.x);
+  if (i + 1 < n) {
+    const float2 r = ex2_poly2(make_float2(x[i], x[i + 1]));
+    y[i] = r.x;
+    y[i + 1] = r.y;
+  } else if (i < n) {
+    y[i] = ex2_poly2(make_float2(x[i], 0.f)).x;
+  }
+}
+}  // namespace
+
+// The softmax's FMA-pipe 2^x applied elementwise (numerics tests of the polynomial).
+at::Tensor exp2_poly(const at::Tensor& x) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kFloat && x.is_contiguous(), "exp2_poly: contiguous fp32 CUDA");
+  auto y = at::empty_like(x);
+  const long n = x.numel();
+  if (n == 0) return y;
+  const at::cuda::CUDAGuard guard(x.device());
+  const long pairs = (n + 1) / 2;
+  exp2_poly_kernel<<<(unsigned)((pairs + 255) / 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      x.data_ptr<float>(), y.data_ptr<float>(), n);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return y;
+}
+
 void dq_finalize(const at::Tensor& acc, int64_t H, int64_t Dh, double scale, at::Tensor& out, int64_t Sq) {
   const long total = acc.numel();
   if (total == 0) return;
@@ -1325,10 +1815,12 @@ TORCH_LIBRARY_FRAGMENT(harp, m) {
         "int H, int Dh, float scale, Tensor(a!) dq_acc, Tensor(b!) dk, Tensor(c!) dv, Tensor(d!) err) -> ()");
   m.def("dq_finalize(Tensor acc, int H, int Dh, float scale, Tensor(a!) out, int Sq) -> ()");
   m.def("attn_bwd_probe() -> Tensor");
+  m.def("exp2_poly(Tensor x) -> Tensor");
 }
 TORCH_LIBRARY_IMPL(harp, CUDA, m) {
   m.impl("attn_fwd", &harp::attn_fwd);
   m.impl("attn_bwd", &harp::attn_bwd);
   m.impl("dq_finalize", &harp::dq_finalize);
+  m.impl("exp2_poly", &harp::exp2_poly);
 }
 TORCH_LIBRARY_IMPL(harp, CompositeExplicitAutograd, m) { m.impl("attn_bwd_probe", &harp::attn_bwd_probe); }

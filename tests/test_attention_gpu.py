@@ -118,3 +118,44 @@ def test_attn_bwd(B, Sq, Skv, H, Dh):
         e = (g - ref).abs().max().item()
         tol = 3e-2 * max(1.0, ref.abs().max().item())
         assert e < tol, (name, e, tol)
+
+
+def test_exp2_poly_error_bound():
+    """The FMA-pipe 2^x of the softmax against fp32 exp2: relative error below
+    1e-4 over the range the softmax produces (clamped at -125)."""
+    x = torch.cat([torch.linspace(-125.0, 8.0, 1_000_001, device="cuda"),
+                   torch.rand(1_000_000, device="cuda") * -30.0])
+    y = torch.ops.harp.exp2_poly(x)
+    ref = torch.exp2(x.double())
+    rel = ((y.double() - ref) / ref).abs().max().item()
+    assert rel < 1e-4, rel
+    z = torch.ops.harp.exp2_poly(torch.tensor([-float("inf"), -1000.0, 0.0], device="cuda"))
+    assert z[0].item() < 1e-37 and z[1].item() < 1e-37 and z[2].item() == pytest.approx(1.0, rel=1e-4)
+
+
+@pytest.mark.parametrize("npoly", ["6", "16"])
+def test_attn_fwd_poly_exp(npoly):
+    """Forward attention with part (or all) of the softmax exponentials on the
+    polynomial: same result as the fp32 reference within bf16 tolerance."""
+    import subprocess
+    import sys
+
+    code = (
+        "import torch, harp_b200\n"
+        "from harp_b200.ops import functional as Fn\n"
+        "harp_b200.load_native(build_if_needed=False)\n"
+        "torch.manual_seed(0)\n"
+        "B, S, H, Dh = 2, 700, 3, 72\n"
+        "q, k, v = (torch.randn(B*S, H*Dh, device='cuda').bfloat16() for _ in range(3))\n"
+        "o, lse = Fn.attn_fwd(q, k, v, B, S, S, H, Dh)\n"
+        "qf, kf, vf = (t.float().view(B, S, H, Dh).transpose(1, 2) for t in (q, k, v))\n"
+        "ref = torch.softmax(qf @ kf.transpose(-1, -2) / Dh**0.5, -1) @ vf\n"
+        "err = (o.float().view(B, S, H, Dh).transpose(1, 2) - ref).abs().max().item()\n"
+        "assert err < 2e-2, err\n"
+        "print('ok', err)\n"
+    )
+    import os
+
+    env = dict(os.environ, HARP_ATTN_POLY=npoly)
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and "ok" in r.stdout, r.stdout + r.stderr
