@@ -102,29 +102,40 @@ __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity) 
     if (globaltimer_ns() - t0 > 1000000000ull) return false;
   return true;
 }
-// One 128-row strip-major tile (NCH strips of 8 elements): a single 5-D TMA
-// when the map is the (8, row, strip, head, batch) form, else one 4-D TMA per
-// strip.  Either way NCH * 2048 bytes arrive on `bar`.
+// One 128-row operand tile (Q, K, V or dO of one head) in 32-byte swizzled
+// atoms: atom a holds head-dim elements [16a, 16a + 16) of all 128 rows, 32
+// bytes per row, at dst + a * 4096.  One 4-D TMA per atom (NCH / 2 of them);
+// elements past the head dim are outside the tensor and read as zero.  Rows
+// of 32 bytes move twice the data per TMA row of 8-element strips.
 template <int NCH>
-__device__ __forceinline__ void load_strip_tile(uint8_t* dst, const CUtensorMap* map, uint64_t* bar, int row0, int h,
-                                                int b, int one_shot) {
-  if (one_shot) {
-    tma_load_5d(dst, map, bar, 0, row0, 0, h, b);
-  } else {
+__device__ __forceinline__ void load_sw32_tile(uint8_t* dst, const CUtensorMap* map, uint64_t* bar, int row0, int h,
+                                               int b) {
 #pragma unroll
-    for (int c = 0; c < NCH; ++c) tma_load_4d(dst + c * 2048, map, bar, c * 8, h, row0, b);
-  }
+  for (int at = 0; at < NCH / 2; ++at) tma_load_4d(dst + at * 4096, map, bar, at * 16, h, row0, b);
+}
+// The 32-byte swizzled tile as a K-major operand (head dim is the reduction):
+// k-step ks is atom ks; 8-row groups 256 B apart.
+__device__ __forceinline__ uint64_t kmajor_sw32(uint32_t tile_addr, int ks) {
+  return make_sdesc(tile_addr + ks * 4096, 16, 256, kLayoutSw32);
+}
+// ... and as an MN-major operand (tile rows are the reduction, head dim the
+// output columns): a 16-row k-step advances 512 B, 8-row groups 256 B apart,
+// the next 16 output columns one atom (4096 B) further.
+__device__ __forceinline__ uint64_t mnmajor_sw32(uint32_t tile_addr, int ks) {
+  return make_sdesc(tile_addr + ks * 512, 4096, 256, kLayoutSw32);
 }
 
+// Operands the warps write themselves (P^T, dS) use the unswizzled
+// core-matrix layout of 8-element strips: strip c of a 128-row tile at c * 2048,
+// row r at + 16 r.
 __device__ __forceinline__ uint64_t kmajor_desc(uint32_t tile_addr, int ks) {
-  // K-major (head dim is the reduction): next 8-row group at +128 B,
-  // next 8-element strip at +2048 B; a 16-wide k-step spans two strips.
+  // K-major: next 8-row group at +128 B, next 8-element strip at +2048 B; a
+  // 16-wide k-step spans two strips.
   return make_sdesc(tile_addr + ks * 4096, 2048, 128, kLayoutNone);
 }
 __device__ __forceinline__ uint64_t mnmajor_desc(uint32_t tile_addr, int ks) {
-  // MN-major (head dim / query index is the output dim, tile rows are the
-  // reduction): next 8 reduction rows at +128 B, next 8 output columns at
-  // +2048 B; a 16-row k-step advances 256 B.
+  // MN-major (tile rows are the reduction): next 8 reduction rows at +128 B,
+  // next 8 output columns at +2048 B; a 16-row k-step advances 256 B.
   return make_sdesc(tile_addr + ks * 256, 128, 2048, kLayoutNone);
 }
 
@@ -148,7 +159,6 @@ struct FwdArgs {
   int chunk_len;
   int start_tile;
   unsigned int epoch;
-  int strip5;  // tensor maps are the one-instruction 5-D strip form
   int wait_q;  // queries arrive by chunk too (same flags): wait before loading a Q tile
   int q_rot;   // query-pair index rotation (start with the pairs whose chunk is local)
   int probe;   // record key-tile step timestamps of CTA 0 (HARP_ATTN_PROBE=1)
@@ -162,7 +172,7 @@ struct FwdCfg {
   static constexpr int DPAD = NCH * 8;
   static constexpr int TILE = NCH * 2048;
   static constexpr int STAGES = (NCH <= 10) ? 3 : 2;
-  static constexpr int SMEM = 2 * TILE + STAGES * 2 * TILE + 128 + 256;  // 128-B alignment slack + barriers
+  static constexpr int SMEM = 2 * TILE + STAGES * 2 * TILE + 256 + 256;  // 256-B alignment slack + barriers
 };
 constexpr int kFwdThreads = 384;  // w0 TMA, w1 MMA, w2-3 spare, w4-7 softmax tile 0, w8-11 softmax tile 1
 
@@ -173,7 +183,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   using C = FwdCfg<NCH>;
   constexpr int ST = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 255) & ~uintptr_t(255));
   uint8_t* sQ = smem;
   uint8_t* sK = sQ + 2 * C::TILE;
   uint8_t* sV = sK + ST * C::TILE;
@@ -240,7 +250,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         fence_proxy_async_global();
       }
       mbar_arrive_expect_tx(q_full, ntile * C::TILE);
-      for (int t = 0; t < ntile; ++t) load_strip_tile<NCH>(sQ + t * C::TILE, &tmQ, q_full, q0 + 128 * t, h, b, a.strip5);
+      for (int t = 0; t < ntile; ++t) load_sw32_tile<NCH>(sQ + t * C::TILE, &tmQ, q_full, q0 + 128 * t, h, b);
       for (int jj = 0; jj < nkv && ok; ++jj) {
         const int j = (a.start_tile + jj) % nkv;
         const int key0 = j * 128;
@@ -255,11 +265,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         const uint32_t ph = (jj / ST) & 1;
         if (!mbar_wait(&k_empty[st], ph ^ 1, err, 21)) { ok = false; break; }
         mbar_arrive_expect_tx(&k_full[st], C::TILE);
-        load_strip_tile<NCH>(sK + st * C::TILE, &tmK, &k_full[st], key0, h, b, a.strip5);
+        load_sw32_tile<NCH>(sK + st * C::TILE, &tmK, &k_full[st], key0, h, b);
         issued_k[st]++;
         if (!mbar_wait(&v_empty[st], ph ^ 1, err, 22)) { ok = false; break; }
         mbar_arrive_expect_tx(&v_full[st], C::TILE);
-        load_strip_tile<NCH>(sV + st * C::TILE, &tmV, &v_full[st], key0, h, b, a.strip5);
+        load_sw32_tile<NCH>(sV + st * C::TILE, &tmV, &v_full[st], key0, h, b);
         issued_v[st]++;
       }
       mbar_wait_drain(q_full, 0);
@@ -276,7 +286,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         const uint32_t qa = smem_u32(sQ + t * C::TILE), ka = smem_u32(sK + st * C::TILE);
 #pragma unroll
         for (int ks = 0; ks < NCH / 2; ++ks)
-          mma_ss(tmem + t * 128, kmajor_desc(qa, ks), kmajor_desc(ka, ks), idS, ks > 0 ? 1u : 0u);
+          mma_ss(tmem + t * 128, kmajor_sw32(qa, ks), kmajor_sw32(ka, ks), idS, ks > 0 ? 1u : 0u);
       };
       bool ok = mbar_wait(q_full, 0, err, 30);
       if (ok) ok = mbar_wait(&k_full[0], 0, err, 31);
@@ -302,7 +312,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           tc_fence_after();
 #pragma unroll
           for (int ks = 0; ks < 8; ++ks)
-            mma_ts(tmem + 256 + t * 128, tmem + t * 128 + ks * 8, mnmajor_desc(va, ks), idO,
+            mma_ts(tmem + 256 + t * 128, tmem + t * 128 + ks * 8, mnmajor_sw32(va, ks), idO,
                    (jj > 0 || ks > 0) ? 1u : 0u);
           if (has_next) {
             if (t == 0) {
@@ -466,7 +476,6 @@ struct BwdArgs {
   long lddv;
   int* err;
   int probe;  // record phase timestamps of CTA 0 into g_bwd_probe (HARP_ATTN_PROBE=1)
-  int strip5;  // tensor maps are the one-instruction 5-D strip form
   int skip_dq;  // HARP_ATTN_DEBUG_SKIP_DQ=1: leave dQ out (timing experiments; dQ is then wrong)
 };
 
@@ -484,7 +493,7 @@ struct BwdCfg {
   static constexpr int TILE = NCH * 2048;
   static constexpr int DS_BYTES = 128 * 128 * 2;
   static constexpr int LD_BYTES = 256 * 4;  // per stage: 128 lse + 128 delta
-  static constexpr int smem_for(int st) { return 2 * TILE + st * 2 * TILE + DS_BYTES + st * LD_BYTES + 128 + 256; }
+  static constexpr int smem_for(int st) { return 2 * TILE + st * 2 * TILE + DS_BYTES + st * LD_BYTES + 256 + 256; }
   // Q/dO(+lse/delta) stages: a stage is refilled only after the dQ partial that
   // is staged in it has been read by its TMA reduce, so a third stage keeps the
   // loads two tiles ahead wherever shared memory allows it.
@@ -514,7 +523,7 @@ __global__ void __launch_bounds__(kBwdThreads1, 1)
   using C = BwdCfg<NCH>;
   constexpr int ST = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 255) & ~uintptr_t(255));
   uint8_t* sK = smem;
   uint8_t* sV = sK + C::TILE;
   // stage st holds Q_i at sQD + 2*st*TILE and dO_i right after it; once the
@@ -577,8 +586,8 @@ __global__ void __launch_bounds__(kBwdThreads1, 1)
       int issued[4] = {0, 0, 0, 0};
       bool ok = true;
       mbar_arrive_expect_tx(kv_full, 2 * C::TILE);
-      load_strip_tile<NCH>(sK, &tmK, kv_full, k0, h, b, a.strip5);
-      load_strip_tile<NCH>(sV, &tmV, kv_full, k0, h, b, a.strip5);
+      load_sw32_tile<NCH>(sK, &tmK, kv_full, k0, h, b);
+      load_sw32_tile<NCH>(sV, &tmV, kv_full, k0, h, b);
       for (int i = 0; i < nq && ok; ++i) {
         const int st = i % ST;
         const uint32_t ph = (i / ST) & 1;
@@ -588,8 +597,8 @@ __global__ void __launch_bounds__(kBwdThreads1, 1)
         const long lrow = (long)(b * a.H + h) * a.lse_ld + i * 128;
         bulk_load(sLD + st * 256, a.lse + lrow, 512, &qdo_full[st]);
         bulk_load(sLD + st * 256 + 128, a.delta + lrow, 512, &qdo_full[st]);
-        load_strip_tile<NCH>(sQD + 2 * st * C::TILE, &tmQ, &qdo_full[st], i * 128, h, b, a.strip5);
-        load_strip_tile<NCH>(sQD + (2 * st + 1) * C::TILE, &tmdO, &qdo_full[st], i * 128, h, b, a.strip5);
+        load_sw32_tile<NCH>(sQD + 2 * st * C::TILE, &tmQ, &qdo_full[st], i * 128, h, b);
+        load_sw32_tile<NCH>(sQD + (2 * st + 1) * C::TILE, &tmdO, &qdo_full[st], i * 128, h, b);
         issued[st]++;
       }
       mbar_wait_drain(kv_full, 0);
@@ -614,10 +623,10 @@ __global__ void __launch_bounds__(kBwdThreads1, 1)
         const uint32_t qa = smem_u32(sQD + 2 * st * C::TILE), doa = smem_u32(sQD + (2 * st + 1) * C::TILE);
 #pragma unroll
         for (int ks = 0; ks < NCH / 2; ++ks)
-          mma_ss(tS, kmajor_desc(ka, ks), kmajor_desc(qa, ks), idS, ks > 0 ? 1u : 0u);
+          mma_ss(tS, kmajor_sw32(ka, ks), kmajor_sw32(qa, ks), idS, ks > 0 ? 1u : 0u);
 #pragma unroll
         for (int ks = 0; ks < NCH / 2; ++ks)
-          mma_ss(tdP, kmajor_desc(va, ks), kmajor_desc(doa, ks), idS, ks > 0 ? 1u : 0u);
+          mma_ss(tdP, kmajor_sw32(va, ks), kmajor_sw32(doa, ks), idS, ks > 0 ? 1u : 0u);
         mma_commit(s_full);
         BWD_PROBE(i, 0);
         if (!mbar_wait(p_full, i & 1, err, 63)) { ok = false; break; }
@@ -625,17 +634,17 @@ __global__ void __launch_bounds__(kBwdThreads1, 1)
         tc_fence_after();
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks)
-          mma_ts(tdV, tS + pcol(ks / 2) + (ks & 1) * 8, mnmajor_desc(doa, ks), idO, (i > 0 || ks > 0) ? 1u : 0u);
+          mma_ts(tdV, tS + pcol(ks / 2) + (ks & 1) * 8, mnmajor_sw32(doa, ks), idO, (i > 0 || ks > 0) ? 1u : 0u);
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks)
-          mma_ts(tdK, tdP + pcol(ks / 2) + (ks & 1) * 8, mnmajor_desc(qa, ks), idO, (i > 0 || ks > 0) ? 1u : 0u);
+          mma_ts(tdK, tdP + pcol(ks / 2) + (ks & 1) * 8, mnmajor_sw32(qa, ks), idO, (i > 0 || ks > 0) ? 1u : 0u);
         if (C::DQ_SEPARATE && i > 0) {
           if (!mbar_wait(dq_free, (i - 1) & 1, err, 64)) { ok = false; break; }
           tc_fence_after();
         }
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks)
-          mma_ss(tdQ, mnmajor_desc(dsa, ks), mnmajor_desc(ka, ks), idQ, ks > 0 ? 1u : 0u);
+          mma_ss(tdQ, mnmajor_desc(dsa, ks), mnmajor_sw32(ka, ks), idQ, ks > 0 ? 1u : 0u);
         mma_commit(dq_full);  // also frees Q_i/dO_i: the dQ warps hand the stage back
         BWD_PROBE(i, 3);
       }
@@ -830,11 +839,10 @@ struct BwdPipeCfg {
   static constexpr int DPAD = NCH * 8;
   static constexpr int TILE = NCH * 2048;
   static constexpr int PS_BYTES = 128 * 128 * 2;  // one 128 x 128 bf16 operand (P^T or dS)
-  // Every operand here needs 16-byte alignment only (no-swizzle layouts), which
-  // dynamic shared memory always has, so there is no alignment slack; 128
-  // bytes hold the 15 barriers and the TMEM address.
   static constexpr int LD_BYTES = 2 * 256 * 4;     // lse | delta of a query tile, double-buffered
-  static constexpr int smem_for(int st) { return 2 * TILE + st * 2 * TILE + 2 * PS_BYTES + LD_BYTES + 128; }
+  // 256 bytes of slack align the swizzled tiles (the 32-byte swizzle repeats
+  // every 256 B); 128 bytes hold the 15 barriers and the TMEM address.
+  static constexpr int smem_for(int st) { return 2 * TILE + st * 2 * TILE + 2 * PS_BYTES + LD_BYTES + 256 + 128; }
   static constexpr int STAGES = smem_for(3) <= 232448 ? 3 : 2;
   static constexpr int SMEM = smem_for(STAGES);
   static_assert(SMEM <= 232448, "exceeds the 227 KB per-CTA shared memory limit");
@@ -847,10 +855,10 @@ struct BwdPipeCfg {
 // Four warpgroups: WG0 = w0 TMA, w1 MMA (w2-3 idle); WG1 = w4-7 and WG2 = w8-11
 // dS warps (query columns 0-63 / 64-127); WG3 = w12-15 dQ warps.  The dS warps
 // hold a tile's S and dP for 64 columns in registers, so registers move to
-// them with setmaxnreg: 80 + 168 + 168 + 96 = 512 = 4 x 128, the launch's
+// them with setmaxnreg: 88 + 168 + 168 + 88 = 512 = 4 x 128, the launch's
 // per-thread budget for 512 threads.
 constexpr int kBwdPipeThreads = 512;
-constexpr int kPipeRegsCtl = 80, kPipeRegsDs = 168, kPipeRegsDq = 96;
+constexpr int kPipeRegsCtl = 88, kPipeRegsDs = 168, kPipeRegsDq = 88;
 static_assert(kPipeRegsCtl + 2 * kPipeRegsDs + kPipeRegsDq == 4 * (65536 / kBwdPipeThreads),
               "warpgroup register split must add up to the launch budget");
 
@@ -861,8 +869,8 @@ __global__ void __launch_bounds__(kBwdPipeThreads, 1)
                          const __grid_constant__ CUtensorMap tmdQ, const BwdArgs a) {
   using C = BwdPipeCfg<NCH>;
   constexpr int ST = C::STAGES;
-  extern __shared__ __align__(16) uint8_t smem_raw[];
-  uint8_t* sK = smem_raw;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sK = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 255) & ~uintptr_t(255));
   uint8_t* sV = sK + C::TILE;
   // stage st: Q at 2*st*TILE, dO right after; once dV/dK of the tile are done
   // the dQ warps reuse the stage to stage the fp32 dQ partial for the reduce
@@ -932,16 +940,16 @@ __global__ void __launch_bounds__(kBwdPipeThreads, 1)
       int issued[4] = {0, 0, 0, 0};
       bool ok = true;
       mbar_arrive_expect_tx(kv_full, 2 * C::TILE);
-      load_strip_tile<NCH>(sK, &tmK, kv_full, k0, h, b, a.strip5);
-      load_strip_tile<NCH>(sV, &tmV, kv_full, k0, h, b, a.strip5);
+      load_sw32_tile<NCH>(sK, &tmK, kv_full, k0, h, b);
+      load_sw32_tile<NCH>(sV, &tmV, kv_full, k0, h, b);
       for (int i = 0; i < nq && ok; ++i) {
         const int st = i % ST;
         const uint32_t ph = (i / ST) & 1;
         if (!mbar_wait(&qdo_empty[st], ph ^ 1, err, 150)) { ok = false; break; }
         BWD_PROBE(i, 10);
         mbar_arrive_expect_tx(&qdo_full[st], 2 * C::TILE);
-        load_strip_tile<NCH>(sQD + 2 * st * C::TILE, &tmQ, &qdo_full[st], i * 128, h, b, a.strip5);
-        load_strip_tile<NCH>(sQD + (2 * st + 1) * C::TILE, &tmdO, &qdo_full[st], i * 128, h, b, a.strip5);
+        load_sw32_tile<NCH>(sQD + 2 * st * C::TILE, &tmQ, &qdo_full[st], i * 128, h, b);
+        load_sw32_tile<NCH>(sQD + (2 * st + 1) * C::TILE, &tmdO, &qdo_full[st], i * 128, h, b);
         issued[st]++;
       }
       mbar_wait_drain(kv_full, 0);
@@ -963,17 +971,17 @@ __global__ void __launch_bounds__(kBwdPipeThreads, 1)
         const uint32_t qa = smem_u32(sQD + 2 * stj * C::TILE), doa = smem_u32(sQD + (2 * stj + 1) * C::TILE);
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks)
-          mma_ss(tdV, kmajor_desc(pa, ks), mnmajor_desc(doa, ks), idO, (j > 0 || ks > 0) ? 1u : 0u);
+          mma_ss(tdV, kmajor_desc(pa, ks), mnmajor_sw32(doa, ks), idO, (j > 0 || ks > 0) ? 1u : 0u);
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks)
-          mma_ss(tdK, kmajor_desc(dsa, ks), mnmajor_desc(qa, ks), idO, (j > 0 || ks > 0) ? 1u : 0u);
+          mma_ss(tdK, kmajor_desc(dsa, ks), mnmajor_sw32(qa, ks), idO, (j > 0 || ks > 0) ? 1u : 0u);
         if (j > 0) {
           if (!mbar_wait(dq_free, (j - 1) & 1, err, 164)) return false;
           tc_fence_after();
         }
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks)
-          mma_ss(tdQ, mnmajor_desc(dsa, ks), mnmajor_desc(ka, ks), idQ, ks > 0 ? 1u : 0u);
+          mma_ss(tdQ, mnmajor_desc(dsa, ks), mnmajor_sw32(ka, ks), idQ, ks > 0 ? 1u : 0u);
         mma_commit(p_free);
         mma_commit(dq_full);
         BWD_PROBE(j, 3);
@@ -989,10 +997,10 @@ __global__ void __launch_bounds__(kBwdPipeThreads, 1)
         const uint32_t qa = smem_u32(sQD + 2 * st * C::TILE), doa = smem_u32(sQD + (2 * st + 1) * C::TILE);
 #pragma unroll
         for (int ks = 0; ks < NCH / 2; ++ks)
-          mma_ss(tS, kmajor_desc(ka, ks), kmajor_desc(qa, ks), idS, ks > 0 ? 1u : 0u);
+          mma_ss(tS, kmajor_sw32(ka, ks), kmajor_sw32(qa, ks), idS, ks > 0 ? 1u : 0u);
 #pragma unroll
         for (int ks = 0; ks < NCH / 2; ++ks)
-          mma_ss(tdP, kmajor_desc(va, ks), kmajor_desc(doa, ks), idS, ks > 0 ? 1u : 0u);
+          mma_ss(tdP, kmajor_sw32(va, ks), kmajor_sw32(doa, ks), idS, ks > 0 ? 1u : 0u);
         mma_commit(s_full);
         BWD_PROBE(i, 0);
         if (i > 0) ok = rest(i - 1);
@@ -1019,12 +1027,15 @@ __global__ void __launch_bounds__(kBwdPipeThreads, 1)
     const float* ld_src = (ldt < 128 ? a.lse : a.delta) + (long)(b * a.H + h) * a.lse_ld + (ldt & 127);
     // All eight dS warps run every iteration (errors only make the bounded
     // waits return at once), so the named barrier always sees 256 threads.
+    // lse / delta of a tile's 128 queries (+inf / 0 past Sq) go to the buffer
+    // of the tile's parity: tile 0's now, tile i+1's (loaded during tile i) at
+    // the end of tile i.  The barrier at the top of tile i makes the writes
+    // visible and means every dS warp is done with tile i-2, the buffer's
+    // previous user.
+    sLD[ldt] = __ldg(ld_src);
     for (int i = 0; i < nq; ++i) {
-      // lse / delta of the tile's 128 queries (+inf / 0 past Sq) into the
-      // buffer of this tile's parity; the barrier also means every dS warp is
-      // done with tile i-2, the buffer's previous user
-      float* ldb = sLD + (i & 1) * 256;
-      ldb[ldt] = __ldg(ld_src + i * 128);
+      const float ld_next = (i + 1 < nq) ? __ldg(ld_src + (i + 1) * 128) : 0.f;
+      const float* ldb = sLD + (i & 1) * 256;
       asm volatile("bar.sync 2, 256;" ::: "memory");
       if (!mbar_wait(s_full, i & 1, err, 170)) ok = false;
       if (warp == 4 && lane == 0) BWD_PROBE(i, 4);
@@ -1039,6 +1050,8 @@ __global__ void __launch_bounds__(kBwdPipeThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(s_free);  // the MMA warp may overwrite S / dP now
+      if (warp == 4 && lane == 0) BWD_PROBE(i, 11);
+      const long long c_start = clock64();
       const float* sL = ldb;
       const float* sDl = ldb + 128;
       uint32_t pp[2][16], dd[2][16];
@@ -1065,8 +1078,11 @@ __global__ void __launch_bounds__(kBwdPipeThreads, 1)
           }
         }
       }
+      if (warp == 4 && lane == 0) BWD_PROBE(i, 12);
+      if (a.probe && blockIdx.x == 0 && warp == 4 && lane == 0 && i < 64) g_bwd_probe[i * 16 + 14] = clock64() - c_start;
       // the previous tile's dV/dK/dQ must be done reading P^T / dS
       if (i > 0 && !mbar_wait(p_free, (i - 1) & 1, err, 171)) ok = false;
+      if (warp == 4 && lane == 0) BWD_PROBE(i, 13);
 #pragma unroll
       for (int cc = 0; cc < 2; ++cc) {
         const int c = c_begin + cc;
@@ -1082,6 +1098,7 @@ __global__ void __launch_bounds__(kBwdPipeThreads, 1)
       __syncwarp();
       if (warp == 4 && lane == 0) BWD_PROBE(i, 5);
       if (lane == 0) mbar_arrive(p_full);
+      sLD[((i + 1) & 1) * 256 + ldt] = ld_next;
     }
     if (wg == 1) {  // dV is stored by warpgroup 1
       if (ok) ok = mbar_wait(fin, 0, err, 172);
@@ -1190,322 +1207,6 @@ __global__ void __launch_bounds__(kBwdPipeThreads, 1)
   }
 }
 
-// ===========================================================================
-// Backward, overlapped schedule (head_dim <= 80, where dQ has TMEM columns of
-// its own).  Same data flow as attn_bwd_kernel, but every 128-query tile is
-// handled as two 64-query halves:
-//   * S^T / dP^T of each half are committed separately; the dS warps (w2-5)
-//     turn half 0 into P^T / dS^T while the dQ warps (w6-9) take half 1, so
-//     twice as many threads share the softmax-gradient work;
-//   * the MMA warp issues dV/dK for a half as soon as that half is ready, and
-//     issues the next tile's S/dP for half 0 ahead of this tile's dQ = dS K, so
-//     the tensor pipe keeps working while the warps compute.
-// Orderings that replace the single-tile barriers:
-//   - the next tile's S/dP overwrite TMEM columns whose previous readers (the
-//     half warps' loads, this tile's dV/dK MMAs) finished or were issued
-//     earlier on the in-order tensor pipe;
-//   - dS of tile i+1 is stored to shared memory only after dQ(i) (which reads
-//     it) completed: half-0 warps wait on dq_full(i) first, half-1 warps have
-//     already waited on it to read dQ(i) out;
-//   - dQ(i+1) overwrites the dQ columns only after p_full1(i+1), which the
-//     half-1 warps signal after their dQ(i) readout.
-// ===========================================================================
-template <int NCH>
-__global__ void __launch_bounds__(kBwdThreads, 1)
-    attn_bwd_ov_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                       const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
-                       const __grid_constant__ CUtensorMap tmdQ, const BwdArgs a) {
-  using C = BwdCfg<NCH>;
-  static_assert(C::DQ_SEPARATE, "overlapped backward needs dQ columns of its own");
-  constexpr int ST = C::STAGES;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
-  uint8_t* sK = smem;
-  uint8_t* sV = sK + C::TILE;
-  uint8_t* sQD = sV + C::TILE;
-  uint8_t* sdS = sQD + 2 * ST * C::TILE;
-  float* sLD = reinterpret_cast<float*>(sdS + C::DS_BYTES);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sdS + C::DS_BYTES + ST * C::LD_BYTES);
-  uint64_t* kv_full = bars;
-  uint64_t* qdo_full = bars + 1;        // [ST]
-  uint64_t* qdo_empty = qdo_full + ST;  // [ST]
-  uint64_t* s_full = qdo_empty + ST;    // [2] per half
-  uint64_t* p_full = s_full + 2;        // [2] per half, 4 arrivals each
-  uint64_t* dq_full = p_full + 2;
-  uint64_t* fin = dq_full + 1;
-  uint64_t* dqs_bar = fin + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(dqs_bar + 1);
-
-  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int nkt = (a.Skv + 127) / 128;
-  const int bh = blockIdx.x / nkt, kt = blockIdx.x % nkt;
-  const int b = bh / a.H, h = bh % a.H;
-  const int k0 = kt * 128;
-  const int nq = (a.Sq + 127) / 128;
-  int* err = a.err;
-
-  if (threadIdx.x == 0) {
-    mbar_init(kv_full, 1);
-    for (int s = 0; s < ST; ++s) {
-      mbar_init(&qdo_full[s], 1);
-      mbar_init(&qdo_empty[s], 1);
-    }
-    for (int hf = 0; hf < 2; ++hf) {
-      mbar_init(&s_full[hf], 1);
-      mbar_init(&p_full[hf], 4);
-    }
-    mbar_init(dq_full, 1);
-    mbar_init(fin, 1);
-    mbar_init(dqs_bar, 4);
-    fence_mbar_init();
-  }
-  if (warp == 1) {
-    tmem_alloc(tmem_slot, 512);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  const uint32_t tS = tmem, tdP = tmem + 128, tdV = tmem + C::DV_COL, tdK = tmem + C::DK_COL,
-                 tdQ = tmem + C::DQ_COL;
-
-  if (warp == 0) {
-    if (lane == 0) {
-      tma_prefetch_desc(&tmQ);
-      tma_prefetch_desc(&tmK);
-      tma_prefetch_desc(&tmV);
-      tma_prefetch_desc(&tmdO);
-      int issued[4] = {0, 0, 0, 0};
-      bool ok = true;
-      mbar_arrive_expect_tx(kv_full, 2 * C::TILE);
-      load_strip_tile<NCH>(sK, &tmK, kv_full, k0, h, b, a.strip5);
-      load_strip_tile<NCH>(sV, &tmV, kv_full, k0, h, b, a.strip5);
-      for (int i = 0; i < nq && ok; ++i) {
-        const int st = i % ST;
-        const uint32_t ph = (i / ST) & 1;
-        if (!mbar_wait(&qdo_empty[st], ph ^ 1, err, 50)) { ok = false; break; }
-        BWD_PROBE(i, 10);
-        mbar_arrive_expect_tx(&qdo_full[st], 2 * C::TILE + C::LD_BYTES);
-        const long lrow = (long)(b * a.H + h) * a.lse_ld + i * 128;
-        bulk_load(sLD + st * 256, a.lse + lrow, 512, &qdo_full[st]);
-        bulk_load(sLD + st * 256 + 128, a.delta + lrow, 512, &qdo_full[st]);
-        load_strip_tile<NCH>(sQD + 2 * st * C::TILE, &tmQ, &qdo_full[st], i * 128, h, b, a.strip5);
-        load_strip_tile<NCH>(sQD + (2 * st + 1) * C::TILE, &tmdO, &qdo_full[st], i * 128, h, b, a.strip5);
-        issued[st]++;
-      }
-      mbar_wait_drain(kv_full, 0);
-      for (int s = 0; s < ST; ++s)
-        if (issued[s]) mbar_wait_drain(&qdo_full[s], (issued[s] - 1) & 1);
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {
-      constexpr uint32_t idS = make_idesc_bf16(128, 64, false, false);
-      constexpr uint32_t idO = make_idesc_bf16(128, C::DPAD, false, true);
-      constexpr uint32_t idQ = make_idesc_bf16(128, C::DPAD, true, true);
-      const uint32_t ka = smem_u32(sK), va = smem_u32(sV), dsa = smem_u32(sdS);
-      // S^T, dP^T of query half hf of tile i (keys as TMEM lanes, 64 query columns)
-      auto issue_sdp = [&](int i, int hf) {
-        const int st = i % ST;
-        const uint32_t qa = smem_u32(sQD + 2 * st * C::TILE) + hf * 1024;
-        const uint32_t doa = smem_u32(sQD + (2 * st + 1) * C::TILE) + hf * 1024;
-#pragma unroll
-        for (int ks = 0; ks < NCH / 2; ++ks)
-          mma_ss(tS + 64 * hf, kmajor_desc(ka, ks), kmajor_desc(qa, ks), idS, ks > 0 ? 1u : 0u);
-#pragma unroll
-        for (int ks = 0; ks < NCH / 2; ++ks)
-          mma_ss(tdP + 64 * hf, kmajor_desc(va, ks), kmajor_desc(doa, ks), idS, ks > 0 ? 1u : 0u);
-        mma_commit(&s_full[hf]);
-      };
-      // dV += P^T dO and dK += dS^T Q over the 64 queries of half hf (packed
-      // bf16 P^T / dS^T at columns 64*hf .. 64*hf + 31)
-      auto issue_dvdk = [&](int i, int hf) {
-        const int st = i % ST;
-        const uint32_t qa = smem_u32(sQD + 2 * st * C::TILE), doa = smem_u32(sQD + (2 * st + 1) * C::TILE);
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          const int ks = 4 * hf + kk;
-          mma_ts(tdV, tS + 64 * hf + kk * 8, mnmajor_desc(doa, ks), idO, (i > 0 || ks > 0) ? 1u : 0u);
-        }
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          const int ks = 4 * hf + kk;
-          mma_ts(tdK, tdP + 64 * hf + kk * 8, mnmajor_desc(qa, ks), idO, (i > 0 || ks > 0) ? 1u : 0u);
-        }
-      };
-      bool ok = mbar_wait(kv_full, 0, err, 60) && mbar_wait(&qdo_full[0], 0, err, 61);
-      if (ok) {
-        tc_fence_after();
-        issue_sdp(0, 0);
-        issue_sdp(0, 1);
-      }
-      for (int i = 0; i < nq && ok; ++i) {
-        BWD_PROBE(i, 0);
-        if (!mbar_wait(&p_full[0], i & 1, err, 63)) { ok = false; break; }
-        BWD_PROBE(i, 1);
-        tc_fence_after();
-        issue_dvdk(i, 0);
-        if (!mbar_wait(&p_full[1], i & 1, err, 64)) { ok = false; break; }
-        BWD_PROBE(i, 2);
-        tc_fence_after();
-        issue_dvdk(i, 1);
-        const bool more = i + 1 < nq;
-        if (more) {
-          if (!mbar_wait(&qdo_full[(i + 1) % ST], ((i + 1) / ST) & 1, err, 65)) { ok = false; break; }
-          tc_fence_after();
-          issue_sdp(i + 1, 0);
-        }
-#pragma unroll
-        for (int ks = 0; ks < 8; ++ks)
-          mma_ss(tdQ, mnmajor_desc(dsa, ks), mnmajor_desc(ka, ks), idQ, ks > 0 ? 1u : 0u);
-        mma_commit(dq_full);
-        BWD_PROBE(i, 3);
-        if (more) issue_sdp(i + 1, 1);
-      }
-      mma_commit(fin);
-      mbar_wait_drain(fin, 0);
-    }
-  } else {
-    // ---------------- w2-5: half 0 (queries 0-63); w6-9: half 1 (64-127) ----------------
-    const int hf = warp >= 6 ? 1 : 0;
-    const int quarter = warp & 3;
-    const int kr = quarter * 32 + lane;
-    const int key = k0 + kr;
-    const bool key_ok = key < a.Skv;
-    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    bool ok = true;
-    for (int i = 0; i < nq && ok; ++i) {
-      if (!mbar_wait(&s_full[hf], i & 1, err, 70 + hf)) { ok = false; break; }
-      if ((warp == 2 || warp == 6) && lane == 0) BWD_PROBE(i, hf ? 6 : 4);
-      tc_fence_after();
-      const int st = i % ST;
-      const float* sL = sLD + st * 256;  // lse of the tile's 128 queries (+inf past Sq)
-      const float* sDl = sL + 128;        // delta (0 past Sq)
-      const float2 scl = make_float2(a.scale_log2, a.scale_log2);
-      const float2 kmask = make_float2(key_ok ? 1.f : 0.f, key_ok ? 1.f : 0.f);
-      const float2 nl2e = make_float2(-kLog2e, -kLog2e);
-#pragma unroll 1
-      for (int cc = 0; cc < 2; ++cc) {
-        const int c = 2 * hf + cc;  // 32-query chunk of the tile
-        uint32_t s[32], dp[32];
-        tmem_ld32(tS + lane_off + c * 32, s);
-        tmem_ld32(tdP + lane_off + c * 32, dp);
-        tmem_wait_ld();
-        uint32_t pp[16], dd[16];
-#pragma unroll
-        for (int k4 = 0; k4 < 8; ++k4) {
-          const float4 L4 = *reinterpret_cast<const float4*>(sL + c * 32 + 4 * k4);
-          const float4 D4 = *reinterpret_cast<const float4*>(sDl + c * 32 + 4 * k4);
-#pragma unroll
-          for (int h2 = 0; h2 < 2; ++h2) {
-            const int k2 = 2 * k4 + h2;
-            const float2 Lp = h2 ? make_float2(L4.z, L4.w) : make_float2(L4.x, L4.y);
-            const float2 Dp = h2 ? make_float2(D4.z, D4.w) : make_float2(D4.x, D4.y);
-            const float2 x = __ffma2_rn(make_float2(__uint_as_float(s[2 * k2]), __uint_as_float(s[2 * k2 + 1])), scl,
-                                        __fmul2_rn(Lp, nl2e));
-            const float2 p = __fmul2_rn(make_float2(ex2_approx(x.x), ex2_approx(x.y)), kmask);
-            const float2 ds = __fmul2_rn(
-                p, __fadd2_rn(make_float2(__uint_as_float(dp[2 * k2]), __uint_as_float(dp[2 * k2 + 1])),
-                              make_float2(-Dp.x, -Dp.y)));
-            pp[k2] = pack_bf16x2(p.x, p.y);
-            dd[k2] = pack_bf16x2(ds.x, ds.y);
-          }
-        }
-        // packed bf16 P^T / dS^T of this half start at column 64*hf
-        tmem_st16(tS + lane_off + 64 * hf + cc * 16, pp);
-        tmem_st16(tdP + lane_off + 64 * hf + cc * 16, dd);
-        if (cc == 0 && hf == 0 && i > 0) {
-          // dQ(i-1) reads the dS tile in shared memory: it must be done first
-          if (!mbar_wait(dq_full, (i - 1) & 1, err, 72)) { ok = false; break; }
-        }
-#pragma unroll
-        for (int g = 0; g < 4; ++g)
-          *reinterpret_cast<uint4*>(sdS + (c * 4 + g) * 2048 + kr * 16) =
-              make_uint4(dd[4 * g], dd[4 * g + 1], dd[4 * g + 2], dd[4 * g + 3]);
-      }
-      if (!ok) break;
-      tmem_wait_st();
-      fence_proxy_async_smem();
-      tc_fence_before();
-      __syncwarp();
-      if ((warp == 2 || warp == 6) && lane == 0) BWD_PROBE(i, hf ? 7 : 5);
-      if (lane == 0) mbar_arrive(&p_full[hf]);
-      if (hf == 1) {
-        // read dQ(i) out of TMEM into the tile's Q/dO stage (fp32 staging) and
-        // reduce-add it into dq_acc with one TMA; then give the stage back
-        if (!mbar_wait(dq_full, i & 1, err, 80)) { ok = false; break; }
-        if (warp == 6 && lane == 0) BWD_PROBE(i, 8);
-        tc_fence_after();
-        const int qr = kr;
-        float* stage = reinterpret_cast<float*>(sQD + 2 * st * C::TILE);
-        float* srow = stage + qr * a.Dh;
-        {
-          uint32_t v[C::DPAD];  // all dQ columns of this row, one TMEM wait
-#pragma unroll
-          for (int c = 0; c < C::DPAD; c += 16)
-            tmem_ld16(tdQ + lane_off + c, *reinterpret_cast<uint32_t(*)[16]>(v + c));
-          tmem_wait_ld();
-#pragma unroll
-          for (int d = 0; d < C::DPAD; d += 4)
-            if (d < a.Dh)
-              *reinterpret_cast<float4*>(srow + d) = make_float4(__uint_as_float(v[d]), __uint_as_float(v[d + 1]),
-                                                                 __uint_as_float(v[d + 2]), __uint_as_float(v[d + 3]));
-        }
-        tc_fence_before();
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(dqs_bar);
-        if (warp == 6 && lane == 0) {
-          // issue the reduce-add of this tile and move on; the stage of the
-          // previous tile goes back to the producer once its reduce has read it
-          if (!mbar_wait(dqs_bar, i & 1, err, 82)) { ok = false; break; }
-          if (!a.skip_dq) tma_reduce_add_4d(&tmdQ, stage, 0, h, i * 128, b);
-          if (i > 0) {
-            bulk_wait_read_one_pending();
-            mbar_arrive(&qdo_empty[(i - 1) % ST]);
-          }
-          BWD_PROBE(i, 9);
-        }
-      }
-    }
-    if (warp == 6 && lane == 0) bulk_wait_all();
-    if (ok) ok = mbar_wait(fin, 0, err, 81);
-    tc_fence_after();
-    // half-0 warps write dV, half-1 warps write dK (scaled) for their key rows
-    const float mul = hf ? a.scale : 1.f;
-    const uint32_t tsrc = hf ? tdK : tdV;
-    bf16* orow = hf ? a.dK + (long)(b * a.Skv + key) * a.lddk + h * a.Dh
-                    : a.dV + (long)(b * a.Skv + key) * a.lddv + h * a.Dh;
-#pragma unroll
-    for (int c = 0; c < C::DPAD; c += 16) {
-      uint32_t v[16];
-      tmem_ld16(tsrc + lane_off + c, v);
-      tmem_wait_ld();
-      if (key_ok && ok) {
-#pragma unroll
-        for (int g = 0; g < 2; ++g) {
-          const int d = c + 8 * g;
-          if (d < a.Dh) {
-            uint4 pk;
-            pk.x = pack_bf16x2(__uint_as_float(v[8 * g + 0]) * mul, __uint_as_float(v[8 * g + 1]) * mul);
-            pk.y = pack_bf16x2(__uint_as_float(v[8 * g + 2]) * mul, __uint_as_float(v[8 * g + 3]) * mul);
-            pk.z = pack_bf16x2(__uint_as_float(v[8 * g + 4]) * mul, __uint_as_float(v[8 * g + 5]) * mul);
-            pk.w = pack_bf16x2(__uint_as_float(v[8 * g + 6]) * mul, __uint_as_float(v[8 * g + 7]) * mul);
-            *reinterpret_cast<uint4*>(orow + d) = pk;
-          }
-        }
-      }
-    }
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc(tmem, 512);
-  }
-}
-
 // dQ = scale * dq_acc  (fp32 [B][H][Sq][Dh] -> bf16 [B*Sq, ld] token-major)
 __global__ void dq_finalize_kernel(const float* __restrict__ acc, int B, int Sq, int H, int Dh, float scale,
                                    bf16* __restrict__ out, long ldo) {
@@ -1551,28 +1252,6 @@ void launch_fwd(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap&
   count_launch();
 }
 
-// HARP_ATTN_STRIP5=0 loads strip tiles with one 4-D TMA per strip (comparisons).
-bool strip5_enabled() {
-  static const bool on = [] {
-    const char* e = std::getenv("HARP_ATTN_STRIP5");
-    return !(e && e[0] == '0');
-  }();
-  return on;
-}
-
-// HARP_ATTN_BWD_OVERLAP=1 selects the half-tile overlapped schedule.  Measured
-// on B200 (DiT-XL/2 shapes) it is slower than the single-tile schedule: the
-// P/dS work is bound by the SM's exp and FMA throughput, so splitting it over
-// twice the warps does not shorten it, and the dQ read-out lands on the
-// critical path.  Kept for further work on the schedule.
-bool bwd_overlap_enabled() {
-  static const bool on = [] {
-    const char* e = std::getenv("HARP_ATTN_BWD_OVERLAP");
-    return e && e[0] == '1';
-  }();
-  return on;
-}
-
 // HARP_ATTN_BWD_PIPE=0 keeps head dims <= 80 on the single-tile schedule
 // (comparisons); by default they take the pipelined one.
 bool bwd_pipe_enabled() {
@@ -1603,7 +1282,7 @@ void launch_bwd(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap&
                         " registers per thread; using the single-tile schedule");
       return ok;
     }();
-    if (bwd_pipe_enabled() && !bwd_overlap_enabled() && pipe_ok) {
+    if (bwd_pipe_enabled() && pipe_ok) {
       const int grid = args.B * args.H * ((args.Skv + 127) / 128);
       attn_bwd_pipe_kernel<NCH><<<grid, kBwdPipeThreads, P::SMEM, stream>>>(mq, mk, mv, mdo, mdq, args);
       C10_CUDA_KERNEL_LAUNCH_CHECK();
@@ -1613,18 +1292,14 @@ void launch_bwd(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap&
   }
   using C = BwdCfg<NCH>;
   auto* kern = attn_bwd_kernel<NCH>;
-  if constexpr (C::DQ_SEPARATE) {
-    if (bwd_overlap_enabled()) kern = attn_bwd_ov_kernel<NCH>;
-  }
-  static bool configured[2] = {false, false};
-  const int which = kern == attn_bwd_kernel<NCH> ? 0 : 1;
-  if (!configured[which]) {
+  static bool configured = false;
+  if (!configured) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
-    configured[which] = true;
+    configured = true;
   }
   const int nkt = (args.Skv + 127) / 128;
   const int grid = args.B * args.H * nkt;
-  kern<<<grid, which == 0 ? kBwdThreads1 : kBwdThreads, C::SMEM, stream>>>(mq, mk, mv, mdo, mdq, args);
+  kern<<<grid, kBwdThreads1, C::SMEM, stream>>>(mq, mk, mv, mdo, mdq, args);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   count_launch();
 }
@@ -1651,16 +1326,10 @@ void attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, int
   const at::cuda::CUDAGuard guard(q.device());
   const int nch = nch_for((int)Dh);
   CUtensorMap mq, mk, mv;
-  const bool s5 = strip5_enabled() && make_strip5_map(&mq, q.data_ptr(), B, Sq, q.stride(0), H, Dh, 128, nch) &&
-                  make_strip5_map(&mk, k.data_ptr(), B, Skv, k.stride(0), H, Dh, 128, nch) &&
-                  make_strip5_map(&mv, v.data_ptr(), B, Skv, v.stride(0), H, Dh, 128, nch);
-  if (!s5) {
-    mq = make_strip_map(q.data_ptr(), B, Sq, q.stride(0), H, Dh, 128);
-    mk = make_strip_map(k.data_ptr(), B, Skv, k.stride(0), H, Dh, 128);
-    mv = make_strip_map(v.data_ptr(), B, Skv, v.stride(0), H, Dh, 128);
-  }
+  mq = make_sw32_map(q.data_ptr(), B, Sq, q.stride(0), H, Dh, 128);
+  mk = make_sw32_map(k.data_ptr(), B, Skv, k.stride(0), H, Dh, 128);
+  mv = make_sw32_map(v.data_ptr(), B, Skv, v.stride(0), H, Dh, 128);
   FwdArgs args;
-  args.strip5 = s5 ? 1 : 0;
   static const bool probe = [] {
     const char* e = std::getenv("HARP_ATTN_PROBE");
     return e != nullptr && e[0] == '1';
@@ -1710,16 +1379,10 @@ void attn_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, con
   const at::cuda::CUDAGuard guard(q.device());
   const int nch = nch_for((int)Dh);
   CUtensorMap mq, mk, mv, mdo;
-  const bool s5 = strip5_enabled() && make_strip5_map(&mq, q.data_ptr(), B, Sq, q.stride(0), H, Dh, 128, nch) &&
-                  make_strip5_map(&mk, k.data_ptr(), B, Skv, k.stride(0), H, Dh, 128, nch) &&
-                  make_strip5_map(&mv, v.data_ptr(), B, Skv, v.stride(0), H, Dh, 128, nch) &&
-                  make_strip5_map(&mdo, dout.data_ptr(), B, Sq, dout.stride(0), H, Dh, 128, nch);
-  if (!s5) {
-    mq = make_strip_map(q.data_ptr(), B, Sq, q.stride(0), H, Dh, 128);
-    mk = make_strip_map(k.data_ptr(), B, Skv, k.stride(0), H, Dh, 128);
-    mv = make_strip_map(v.data_ptr(), B, Skv, v.stride(0), H, Dh, 128);
-    mdo = make_strip_map(dout.data_ptr(), B, Sq, dout.stride(0), H, Dh, 128);
-  }
+  mq = make_sw32_map(q.data_ptr(), B, Sq, q.stride(0), H, Dh, 128);
+  mk = make_sw32_map(k.data_ptr(), B, Skv, k.stride(0), H, Dh, 128);
+  mv = make_sw32_map(v.data_ptr(), B, Skv, v.stride(0), H, Dh, 128);
+  mdo = make_sw32_map(dout.data_ptr(), B, Sq, dout.stride(0), H, Dh, 128);
   CUtensorMap mdq = make_f32_bhsd_map(dq_acc.data_ptr(), B, Sq, H, Dh, 128);
   BwdArgs args;
   args.B = B; args.Sq = Sq; args.Skv = Skv; args.H = H; args.Dh = Dh;
@@ -1739,7 +1402,6 @@ void attn_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, con
     return e && e[0] == '1';
   }();
   args.probe = probe ? 1 : 0;
-  args.strip5 = s5 ? 1 : 0;
   static const bool skip_dq = [] {
     const char* e = std::getenv("HARP_ATTN_DEBUG_SKIP_DQ");
     return e && e[0] == '1';

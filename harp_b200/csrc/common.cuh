@@ -231,10 +231,13 @@ __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8])
 //  bits [32,46) stride-dimension byte offset >> 4
 //  bits [46,48) version (1 on sm100)
 //  bits [49,52) base offset, bit 52 lbo mode
-//  bits [61,64) layout: 0 none (interleaved core matrices), 2 = 128B swizzle
+//  bits [61,64) layout: 0 none (interleaved core matrices), 2 / 4 / 6 = 128 / 64 /
+//               32-byte swizzle
 // ---------------------------------------------------------------------------
 constexpr uint64_t kLayoutNone = 0;
 constexpr uint64_t kLayoutSw128 = 2;
+constexpr uint64_t kLayoutSw64 = 4;
+constexpr uint64_t kLayoutSw32 = 6;
 
 __device__ __forceinline__ uint64_t make_sdesc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes,
                                                uint64_t layout) {

@@ -40,12 +40,10 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 EncodeTiledFn get_encode_fn();
 int num_sms();
-// 4-D bf16 "strip" map over a token-major [B, S, ld] activation holding H heads
-// of Dh elements per token: dims {Dh, H, S, B}; the box is 8 elements x 1 head
-// x `box_rows` tokens x 1 batch, i.e. one 16-byte column strip of a tile.
-CUtensorMap make_strip_map(const void* base, long B, long S, long ld, long H, long Dh, int box_rows);
-bool make_strip5_map(CUtensorMap* m, const void* base, long B, long S, long ld, long H, long Dh, int box_rows,
-                     int nstrips);
+// 4-D bf16 map over a token-major [B, S, ld] activation holding H heads of Dh
+// elements per token: dims {Dh, H, S, B}; the box is 16 elements x 1 head x
+// `box_rows` tokens x 1 batch with 32-byte swizzle (one atom of a tile).
+CUtensorMap make_sw32_map(const void* base, long B, long S, long ld, long H, long Dh, int box_rows);
 // 4-D fp32 map over a dense [B, S, H, Dh] buffer; box = Dh x 1 x box_rows x 1.
 CUtensorMap make_f32_rows_map(const void* base, long B, long S, long H, long Dh, int box_rows);
 CUtensorMap make_f32_bhsd_map(const void* base, long B, long S, long H, long Dh, int box_rows);

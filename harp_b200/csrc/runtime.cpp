@@ -32,39 +32,25 @@ int num_sms() {
   return n[dev];
 }
 
-CUtensorMap make_strip_map(const void* base, long B, long S, long ld, long H, long Dh, int box_rows) {
+// Attention operand tile in 32-byte swizzled atoms: 4-D view (Dh, H, S, B) of
+// a token-major [B*S, >= H*Dh] bf16 tensor (row stride ld elements), box
+// {16, 1, rows, 1}: one atom of 16 head-dim elements x `rows` tokens, 32 bytes
+// per row.  Elements at or past Dh are outside the tensor and read as zero.
+CUtensorMap make_sw32_map(const void* base, long B, long S, long ld, long H, long Dh, int box_rows) {
   TORCH_CHECK(Dh % 8 == 0, "harp attention: head_dim must be a multiple of 8 (got ", Dh, ")");
   TORCH_CHECK((reinterpret_cast<uintptr_t>(base) & 15) == 0, "harp attention: base not 16-byte aligned");
   TORCH_CHECK((ld * 2) % 16 == 0, "harp attention: row stride must be a multiple of 16 bytes");
   CUtensorMap m;
   cuuint64_t dims[4] = {(cuuint64_t)Dh, (cuuint64_t)H, (cuuint64_t)S, (cuuint64_t)B};
   cuuint64_t strides[3] = {(cuuint64_t)Dh * 2, (cuuint64_t)ld * 2, (cuuint64_t)S * ld * 2};
-  cuuint32_t box[4] = {8, 1, (cuuint32_t)box_rows, 1};
+  cuuint32_t box[4] = {16, 1, (cuuint32_t)box_rows, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = get_encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box,
-                               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_32B,
                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   TORCH_CHECK(r == CUDA_SUCCESS, "harp attention: cuTensorMapEncodeTiled failed (", (int)r, ") B=", B, " S=", S,
               " ld=", ld, " H=", H, " Dh=", Dh);
   return m;
-}
-
-// Strip-major tile with one TMA instruction: dims ordered (8 elements, row,
-// 8-element strip, head, batch) so that a box {8, rows, nstrips, 1, 1} lands in
-// shared memory as [strip][row][8] (strip c at c * rows * 16 bytes, row r at
-// r * 16).  Strips at or past Dh / 8 are outside the tensor and read as zero.
-// Returns false (map untouched) when the driver does not accept the layout.
-bool make_strip5_map(CUtensorMap* m, const void* base, long B, long S, long ld, long H, long Dh, int box_rows,
-                     int nstrips) {
-  if (Dh % 8 != 0 || (reinterpret_cast<uintptr_t>(base) & 15) != 0 || (ld * 2) % 16 != 0) return false;
-  cuuint64_t dims[5] = {8, (cuuint64_t)S, (cuuint64_t)(Dh / 8), (cuuint64_t)H, (cuuint64_t)B};
-  cuuint64_t strides[4] = {(cuuint64_t)ld * 2, 16, (cuuint64_t)Dh * 2, (cuuint64_t)S * ld * 2};
-  cuuint32_t box[5] = {8, (cuuint32_t)box_rows, (cuuint32_t)nstrips, 1, 1};
-  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
-  CUresult r = get_encode_fn()(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, const_cast<void*>(base), dims, strides, box,
-                               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS;
 }
 
 // fp32 [B][H][S][Dh] (one contiguous [S, Dh] slab per batch and head), as the
