@@ -894,8 +894,6 @@ void gemm(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, at::Te
     return e != nullptr && e[0] == '1';
   }();
   args.probe = probe ? 1 : 0;
-
-
   if (K == 0) {
     // Degenerate: treat as zero accumulator.  Route through SIMT (K loop is empty).
     force_simt = true;
