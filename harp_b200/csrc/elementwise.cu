@@ -106,6 +106,7 @@ __global__ void rmsnorm_mod_bwd_kernel(const bf16* __restrict__ x, long ldx, con
       const bf16* xr = x + (long)row * ldx;
       const bf16* gr = dy + (long)row * lddy;
       const float rs = rstd[row];
+#pragma unroll 2
       for (int c = lane * 8; c < D; c += 256) {
         float xf[8], gf[8], wf[8], sc[8];
         load8(xr + c, xf);
@@ -133,9 +134,11 @@ __global__ void rmsnorm_mod_bwd_kernel(const bf16* __restrict__ x, long ldx, con
     float aw[8], as_[8], ab[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) { aw[j] = 0.f; as_[j] = 0.f; ab[j] = 0.f; }
-    for (int rr = 0; rr < RPB; ++rr) {
+    // fixed trip count so that several rows' loads are in flight at once
+    const int nr = min(RPB, R - r0);
+#pragma unroll 4
+    for (int rr = 0; rr < nr; ++rr) {
       const int row = r0 + rr;
-      if (row >= R) break;
       const float rs = rstd[row];
       const float mu = srow[rr];
       float xf[8], gf[8], o[8];
@@ -518,9 +521,11 @@ __global__ void gate_bwd_kernel(const bf16* __restrict__ dy, long lddy, const bf
     float ag[8], ab[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) { ag[j] = 0.f; ab[j] = 0.f; }
-    for (int rr = 0; rr < RPB; ++rr) {
+    // fixed trip count so that several rows' loads are in flight at once
+    const int nr = min(RPB, R - r0);
+#pragma unroll 4
+    for (int rr = 0; rr < nr; ++rr) {
       const int row = r0 + rr;
-      if (row >= R) break;
       float d[8], av[8], o[8];
       load8(dy + (long)row * lddy + c, d);
       if (pg) load8(a + (long)row * lda + c, av);
@@ -547,9 +552,11 @@ __global__ void colsum_partial_kernel(const bf16* __restrict__ x, long ldx, int 
   const int r0 = blockIdx.x * RPB;
   for (int c = (blockIdx.y * blockDim.x + threadIdx.x) * 8; c < D; c += gridDim.y * blockDim.x * 8) {
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    for (int rr = 0; rr < RPB; ++rr) {
+    // fixed trip count so that several rows' loads are in flight at once
+    const int nr = min(RPB, R - r0);
+#pragma unroll 4
+    for (int rr = 0; rr < nr; ++rr) {
       const int row = r0 + rr;
-      if (row >= R) break;
       float f[8];
       load8(x + (long)row * ldx + c, f);
 #pragma unroll
@@ -639,9 +646,11 @@ __global__ void layernorm_mod_bwd_kernel(const bf16* __restrict__ x, long ldx, c
     float as_[8], ab[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) { as_[j] = 0.f; ab[j] = 0.f; }
-    for (int rr = 0; rr < RPB; ++rr) {
+    // fixed trip count so that several rows' loads are in flight at once
+    const int nr = min(RPB, R - r0);
+#pragma unroll 4
+    for (int rr = 0; rr < nr; ++rr) {
       const int row = r0 + rr;
-      if (row >= R) break;
       const float mu = mean_in[row], rs = rstd_in[row];
       const float m1 = sm[2 * rr], m2 = sm[2 * rr + 1];
       float xf[8], gf[8], o[8];

@@ -120,6 +120,15 @@ def rmsnorm_case(bwd: bool):
     return make
 
 
+def gate_case():
+    def make():
+        R = B * S
+        dy, a, g = _r(R, D), _r(R, D), _r(B, D, scale=0.1)
+        harp = lambda: Fn.gate_bwd(dy, a, g, S, want_bias=True)  # noqa: E731
+        return harp, None, {"bytes": 3 * R * D * 2, "shape": [R, D]}
+    return make
+
+
 def qknorm_case(bwd: bool):
     def make():
         from ..models.dit import joint_positions, rope_freqs
@@ -180,6 +189,7 @@ def build_cases(gemm_rows: int, adamw_n: int) -> Dict[str, Callable]:
         "attn_bwd_d128": attn_case(False, 128, 24),
         "rmsnorm_fwd": rmsnorm_case(False),
         "rmsnorm_bwd": rmsnorm_case(True),
+        "gate_bwd": gate_case(),
         "qknorm_fwd": qknorm_case(False),
         "qknorm_bwd": qknorm_case(True),
         "swiglu_fwd": swiglu_case(),
