@@ -58,6 +58,8 @@ def parse():
                     help="sequence-parallel attention: K/V gather (ring) or head all-to-all (ulysses)")
     ap.add_argument("--comm", default="auto", choices=["auto", "torch", "nvl"])
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--cuda-graph", type=int, default=1, choices=[0, 1],
+                    help="harp on one GPU: capture the whole step in a CUDA graph after the warm-up steps")
     ap.add_argument("--depth", type=int, default=0, help="override depth (debug only; not a valid bench)")
     ap.add_argument("--op", default="train", choices=["train", "ring-attn"],
                     help="ring-attn: sequence-parallel attention fwd+bwd of Q/K/V [1, 24, seq, 128]")
@@ -328,12 +330,12 @@ def main():
             loss_fn = M.mmdit_loss_local
         model.initialize_weights(seed=0)
         model = model.to(torch.bfloat16)
-        trainer = Trainer(model, par, TrainConfig(comm=args.comm), device, sp_backend=args.sp_backend,
-                          sp_mode=args.sp_mode, loss_fn=loss_fn)
+        trainer = Trainer(model, par, TrainConfig(comm=args.comm, cuda_graph=bool(args.cuda_graph)), device,
+                          sp_backend=args.sp_backend, sp_mode=args.sp_mode, loss_fn=loss_fn)
         cin, tdim = cfg.in_channels, cfg.text_dim
 
         def step(b):
-            return trainer.train_step(b["latent"], b["noise"], b["text"], b["sigmas"])
+            return trainer.run(b)
 
         def e2e_step(b):
             return trainer.step(b)
@@ -433,6 +435,7 @@ def main():
                 "text_tokens": args.text_len,
                 "latent": [16, args.latent, args.latent],
                 "parallelism": parallelism,
+                "cuda_graph": bool(getattr(trainer, "graph_enabled", False)),
                 "l2": "inputs larger than L2 (weights %.1f GB, activations > 10 GB per step)" %
                       (sum(p.numel() for p in trainer.model.parameters()) * 2 / 1e9 if args.impl == "harp"
                        else 1.35),

@@ -728,7 +728,12 @@ __device__ __forceinline__ void adam_elem(float& p, float& m, float& v, float g,
 // Flat buffers.  grad may be bf16 (grad_f32 == nullptr) or fp32.
 __global__ void adamw_flat_kernel(float* __restrict__ master, float* __restrict__ m, float* __restrict__ v,
                                   const bf16* __restrict__ grad_bf16, const float* __restrict__ grad_f32,
-                                  bf16* __restrict__ param, long n, AdamHyper h) {
+                                  bf16* __restrict__ param, long n, AdamHyper h, const float* __restrict__ hyp) {
+  if (hyp != nullptr) {
+    h.lr = hyp[0];
+    h.bc1 = hyp[1];
+    h.bc2_sqrt = hyp[2];
+  }
   for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
     float p = master[i], mm = m[i], vv = v[i];
     const float g = grad_f32 ? grad_f32[i] : __bfloat162float(grad_bf16[i]);
@@ -746,7 +751,13 @@ __global__ void __launch_bounds__(256) adamw_flat_vec_kernel(float* __restrict__
                                                              float* __restrict__ v,
                                                              const bf16* __restrict__ grad_bf16,
                                                              const float* __restrict__ grad_f32,
-                                                             bf16* __restrict__ param, long n8, AdamHyper h) {
+                                                             bf16* __restrict__ param, long n8, AdamHyper h,
+                                                             const float* __restrict__ hyp) {
+  if (hyp != nullptr) {
+    h.lr = hyp[0];
+    h.bc1 = hyp[1];
+    h.bc2_sqrt = hyp[2];
+  }
   for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (long)gridDim.x * blockDim.x) {
     float4* mp = reinterpret_cast<float4*>(master) + 2 * i;
     float4* mmp = reinterpret_cast<float4*>(m) + 2 * i;
@@ -1133,9 +1144,12 @@ void elementwise(int64_t op, const at::Tensor& a, const c10::optional<at::Tensor
   count_launch();
 }
 
+// `hyper` (optional fp32 device tensor [lr, 1 - beta1^t, sqrt(1 - beta2^t)])
+// overrides lr and the bias corrections at run time, so a captured CUDA graph
+// replays the update with the current step's values.
 void adamw_flat(at::Tensor& master, at::Tensor& m, at::Tensor& v, const at::Tensor& grad,
                 const c10::optional<at::Tensor>& param, double lr, double beta1, double beta2, double eps, double wd,
-                int64_t step, double grad_scale) {
+                int64_t step, double grad_scale, const c10::optional<at::Tensor>& hyper) {
   const long n = master.numel();
   if (n == 0) return;
   const at::cuda::CUDAGuard g(master.device());
@@ -1144,6 +1158,12 @@ void adamw_flat(at::Tensor& master, at::Tensor& m, at::Tensor& v, const at::Tens
   h.bc1 = 1.0 - std::pow(beta1, (double)step);
   h.bc2_sqrt = std::sqrt(1.0 - std::pow(beta2, (double)step));
   h.grad_scale = grad_scale;
+  const float* hyp = nullptr;
+  if (hyper.has_value()) {
+    TORCH_CHECK(hyper->is_cuda() && hyper->scalar_type() == at::kFloat && hyper->numel() >= 3 &&
+                    hyper->is_contiguous(), "adamw_flat: hyper must be a contiguous fp32 CUDA tensor of 3");
+    hyp = hyper->data_ptr<float>();
+  }
   const bool gf32 = grad.scalar_type() == at::kFloat;
   auto al = [](const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; };
   if (n % 8 == 0 && al(master.data_ptr()) && al(m.data_ptr()) && al(v.data_ptr()) && al(grad.data_ptr()) &&
@@ -1153,7 +1173,7 @@ void adamw_flat(at::Tensor& master, at::Tensor& m, at::Tensor& v, const at::Tens
     adamw_flat_vec_kernel<<<vgrid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
         master.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), gf32 ? nullptr : bp(grad),
         gf32 ? grad.data_ptr<float>() : nullptr,
-        param.has_value() ? reinterpret_cast<bf16*>(param->data_ptr()) : nullptr, n8, h);
+        param.has_value() ? reinterpret_cast<bf16*>(param->data_ptr()) : nullptr, n8, h, hyp);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
     count_launch();
     return;
@@ -1162,7 +1182,7 @@ void adamw_flat(at::Tensor& master, at::Tensor& m, at::Tensor& v, const at::Tens
   adamw_flat_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       master.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), gf32 ? nullptr : bp(grad),
       gf32 ? grad.data_ptr<float>() : nullptr, param.has_value() ? reinterpret_cast<bf16*>(param->data_ptr()) : nullptr,
-      n, h);
+      n, h, hyp);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   count_launch();
 }

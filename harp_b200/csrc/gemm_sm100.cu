@@ -842,6 +842,7 @@ int set_gemm_pair_mode(int mode) {
 }
 void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 long long launch_count() { return g_launches.load(); }
+void add_launch_count(long long n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 void reset_launch_count() { g_launches.store(0); }
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }

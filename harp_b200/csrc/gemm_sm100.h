@@ -27,6 +27,7 @@ void gemm(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, at::Te
 // `gpu_launches` field).  Every launcher in the library calls count_launch().
 void count_launch();
 long long launch_count();
+void add_launch_count(long long n);
 void reset_launch_count();
 // select CTA-pair tiles for large GEMMs (mode 1), single-CTA only (0), or
 // just query (-1); returns the previous mode

@@ -50,7 +50,7 @@ void layernorm_mod_bwd(const at::Tensor& x, const at::Tensor& mean, const at::Te
 void elementwise(int64_t op, const at::Tensor& a, const c10::optional<at::Tensor>& b, double s, at::Tensor& out);
 void adamw_flat(at::Tensor& master, at::Tensor& m, at::Tensor& v, const at::Tensor& grad,
                 const c10::optional<at::Tensor>& param, double lr, double beta1, double beta2, double eps, double wd,
-                int64_t step, double grad_scale);
+                int64_t step, double grad_scale, const c10::optional<at::Tensor>& hyper);
 void adamw_list(at::TensorList params, at::TensorList grads, at::TensorList exp_avgs, at::TensorList exp_avg_sqs,
                 double lr, double beta1, double beta2, double eps, double wd, int64_t step);
 void philox_uniform(at::Tensor& out, int64_t seed, int64_t offset, double lo, double hi);
@@ -185,6 +185,9 @@ void foreach_adamw_wd(at::TensorList params, at::TensorList grads, at::TensorLis
 }
 
 int64_t launch_count_op() { return launch_count(); }
+// Replays of a captured CUDA graph launch the captured harp kernels again
+// without passing through the launchers; the caller adds them here.
+void add_launch_count_op(int64_t n) { add_launch_count(n); }
 void reset_launch_count_op() { reset_launch_count(); }
 int64_t gemm_pair_mode_op(int64_t mode) { return set_gemm_pair_mode((int)mode); }
 int64_t rows_per_block_op(int64_t rpb) { return rows_per_block_for((int)rpb); }
@@ -217,10 +220,11 @@ TORCH_LIBRARY(harp, m) {
         "Tensor(a!) dx, Tensor(b!)? ps, Tensor(c!)? pb, int rpb) -> ()");
   m.def("elementwise(int op, Tensor a, Tensor? b, float s, Tensor(a!) out) -> ()");
   m.def("adamw_flat(Tensor(a!) master, Tensor(b!) m, Tensor(c!) v, Tensor grad, Tensor(d!)? param, float lr, "
-        "float beta1, float beta2, float eps, float wd, int step, float grad_scale) -> ()");
+        "float beta1, float beta2, float eps, float wd, int step, float grad_scale, Tensor? hyper=None) -> ()");
   m.def("philox_uniform(Tensor(a!) out, int seed, int offset, float lo, float hi) -> ()");
   m.def("rowdot(Tensor a, Tensor b, int H, int Dh, int S, Tensor(a!) out) -> ()");
   m.def("launch_count() -> int");
+  m.def("add_launch_count(int n) -> ()");
   m.def("reset_launch_count() -> ()");
   m.def("rows_per_block(int rows_per_batch) -> int");
   m.def("gemm_pair_mode(int mode) -> int");
@@ -248,6 +252,7 @@ TORCH_LIBRARY_IMPL(harp, CUDA, m) {
 
 TORCH_LIBRARY_IMPL(harp, CompositeExplicitAutograd, m) {
   m.impl("launch_count", &harp::launch_count_op);
+  m.impl("add_launch_count", &harp::add_launch_count_op);
   m.impl("reset_launch_count", &harp::reset_launch_count_op);
   m.impl("rows_per_block", &harp::rows_per_block_op);
   m.impl("gemm_pair_mode", &harp::gemm_pair_mode_op);

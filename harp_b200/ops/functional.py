@@ -492,9 +492,12 @@ def attn_bwd(q, k, v, o, do, lse, B, Sq, Skv, H, Dh, scale=None, dk_out=None, dv
 # ---------------------------------------------------------------------------
 # optimizer
 # ---------------------------------------------------------------------------
-def adamw_flat(master, m, v, grad, param, lr, beta1, beta2, eps, wd, step, grad_scale=1.0):
+def adamw_flat(master, m, v, grad, param, lr, beta1, beta2, eps, wd, step, grad_scale=1.0, hyper=None):
+    """AdamW on flat fp32 state.  `hyper` (CUDA only): fp32 device tensor
+    [lr, 1 - beta1^step, sqrt(1 - beta2^step)] read at run time instead of
+    `lr` / `step` (CUDA-graph replays)."""
     if _cuda(master):
-        torch.ops.harp.adamw_flat(master, m, v, grad, param, lr, beta1, beta2, eps, wd, step, grad_scale)
+        torch.ops.harp.adamw_flat(master, m, v, grad, param, lr, beta1, beta2, eps, wd, step, grad_scale, hyper)
         return
     g = grad.float() * grad_scale
     master.mul_(1 - lr * wd)

@@ -43,6 +43,10 @@ class TrainConfig:
     grad_scale: float = 1.0
     comm: str = "auto"  # "auto" | "torch" | "nvl"
     align: int = 256  # elements; every parameter starts on a 512-byte boundary
+    # Capture the whole step (zero-grad, forward, backward, AdamW) in one CUDA
+    # graph after `graph_warmup` eager steps and replay it (single-GPU runs).
+    cuda_graph: bool = False
+    graph_warmup: int = 2
 
 
 class FlatParams:
@@ -122,16 +126,38 @@ class ShardedAdamW:
         self.grad_shard = torch.empty(n, device=flat.flat.device, dtype=flat.grad.dtype)
         self.step_count = 0
         self.lr = cfg.lr
+        # [lr, 1 - beta1^t, sqrt(1 - beta2^t)] on the device for CUDA-graph replays
+        self.hyper: Optional[torch.Tensor] = None
+        self._hyper_host: Optional[torch.Tensor] = None
+
+    def use_device_hyper(self):
+        """Read lr and the bias corrections from a device tensor that
+        `advance()` refreshes before every step (a captured step then replays
+        with the current values)."""
+        if self.hyper is None:
+            self.hyper = torch.zeros(3, device=self.master.device, dtype=torch.float32)
+            self._hyper_host = torch.zeros(3, dtype=torch.float32).pin_memory()
+
+    def advance(self):
+        """Count the next step and stage its hyper-parameters on the device
+        (device-hyper mode; ordered on the current stream)."""
+        self.step_count += 1
+        t = self.step_count
+        self._hyper_host.copy_(torch.tensor([self.lr, 1.0 - self.cfg.beta1 ** t,
+                                             math.sqrt(1.0 - self.cfg.beta2 ** t)], dtype=torch.float32))
+        self.hyper.copy_(self._hyper_host, non_blocking=True)
 
     def param_shard(self) -> torch.Tensor:
         n = self.shard_numel
         return self.flat.flat[self.rank * n:(self.rank + 1) * n]
 
     def step(self, grad_shard: Optional[torch.Tensor] = None):
-        self.step_count += 1
+        if self.hyper is None:
+            self.step_count += 1
         g = grad_shard if grad_shard is not None else self.grad_shard
         Fn.adamw_flat(self.master, self.m, self.v, g, self.param_shard(), self.lr, self.cfg.beta1, self.cfg.beta2,
-                      self.cfg.eps, self.cfg.weight_decay, self.step_count, self.cfg.grad_scale)
+                      self.cfg.eps, self.cfg.weight_decay, max(1, self.step_count), self.cfg.grad_scale,
+                      hyper=self.hyper)
 
     def state_dict(self):
         return {"step": self.step_count, "lr": self.lr, "master": self.master.cpu(), "exp_avg": self.m.cpu(),
@@ -231,6 +257,13 @@ class Trainer:
         self.sp = SPContext.from_group(par.sp_group, backend=backend, comm=comm, mode=mode) \
             if par.sp_size > 1 else SPContext()
         self.global_step = 0
+        # CUDA-graph state (single GPU): static inputs, the captured step, its loss
+        self._graph = None
+        self._graph_inputs: Optional[Dict[str, torch.Tensor]] = None
+        self._graph_loss: Optional[torch.Tensor] = None
+        self._graph_launches = 0
+        self._eager_steps = 0
+        self.graph_enabled = bool(cfg.cuda_graph) and on_gpu and par.world_size == 1
 
     # -- device-resident step (inputs already on the GPU) -------------------
     def train_step(self, latent, noise, text, sigmas, **extra) -> torch.Tensor:
@@ -264,10 +297,67 @@ class Trainer:
         self.opt.step()
         C.all_gather_flat(self.opt.param_shard(), self.flat.flat, self.par.world_group)
 
+    # -- CUDA-graph replay of the whole step (single GPU) ---------------------------
+    def run(self, batch: Dict[str, torch.Tensor]) -> torch.Tensor:
+        """One step from a batch of device or (pinned) host tensors, returning
+        the loss as a device tensor.  With `cuda_graph`, the first
+        `graph_warmup` steps run eagerly, the next one is captured, and later
+        steps copy the batch into the captured step's inputs and replay it."""
+        if not self.graph_enabled:
+            dev = self.device
+            b = {k: _to_dev(v, dev) for k, v in batch.items()}
+            extra = {k: v for k, v in b.items() if k not in ("latent", "noise", "text", "sigmas")}
+            return self.train_step(b["latent"], b["noise"], b["text"], b["sigmas"], **extra)
+        if self._graph is None and self._eager_steps < self.cfg.graph_warmup:
+            self._eager_steps += 1
+            b = {k: _to_dev(v, self.device) for k, v in batch.items()}
+            extra = {k: v for k, v in b.items() if k not in ("latent", "noise", "text", "sigmas")}
+            return self.train_step(b["latent"], b["noise"], b["text"], b["sigmas"], **extra)
+        if self._graph is None:
+            try:
+                self._capture(batch)
+            except RuntimeError as e:  # an op that cannot be captured: stay eager
+                import warnings
+
+                warnings.warn(f"harp_b200: CUDA-graph capture of the step failed ({e}); running eagerly")
+                self.graph_enabled = False
+                self.opt.hyper = None
+                return self.run(batch)
+        for k, v in batch.items():
+            self._graph_inputs[k].copy_(v, non_blocking=True)
+        self.opt.advance()
+        self._graph.replay()
+        torch.ops.harp.add_launch_count(self._graph_launches)
+        self.global_step += 1
+        return self._graph_loss
+
+    def _capture(self, batch: Dict[str, torch.Tensor]):
+        dev = self.device
+        self._graph_inputs = {k: torch.empty(v.shape, dtype=v.dtype, device=dev) for k, v in batch.items()}
+        for k, v in batch.items():
+            self._graph_inputs[k].copy_(v, non_blocking=True)
+        self.opt.use_device_hyper()
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        b = self._graph_inputs
+        extra = {k: v for k, v in b.items() if k not in ("latent", "noise", "text", "sigmas")}
+        before = int(torch.ops.harp.launch_count())
+        step_count, global_step = self.opt.step_count, self.global_step
+        with torch.cuda.graph(graph):
+            loss = self.train_step(b["latent"], b["noise"], b["text"], b["sigmas"], **extra)
+        # capture recorded the kernels without running them: take back the
+        # launch count and step counters it advanced; every replay re-adds them
+        self._graph_launches = int(torch.ops.harp.launch_count()) - before
+        torch.ops.harp.add_launch_count(-self._graph_launches)
+        self.opt.step_count, self.global_step = step_count, global_step
+        self._graph, self._graph_loss = graph, loss
+
     # -- public end-to-end step ------------------------------------------------
     def step(self, batch: Dict[str, torch.Tensor]) -> float:
         """batch: host tensors 'latent' [B,C,H,W], 'noise' [B,C,H,W], 'text' [B,L,Dt], 'sigmas' [B]
         (pinned for asynchronous copies).  Returns the loss (global mean)."""
+        if self.graph_enabled:
+            return float(self.run(batch).item())
         dev = self.device
         latent = batch["latent"].to(dev, non_blocking=True)
         noise = batch["noise"].to(dev, non_blocking=True)
