@@ -256,6 +256,68 @@ __global__ void qknorm_rope_fwd_kernel(const bf16* __restrict__ qkv, long ld, in
   }
 }
 
+// Vector form of the forward for head dims that are a multiple of 8: one
+// thread per (row, head, q-or-k) item, the head's DH elements as DH/8 16-byte
+// loads kept in registers (one read, no shuffles), scale * weight * rotation
+// per 8-element chunk, 16-byte stores.  Consecutive threads take consecutive
+// heads, so a warp reads and writes contiguous runs of the q (or k) columns.
+template <int DH>
+__global__ void __launch_bounds__(256, 2) qknorm_rope_fwd_vec_kernel(
+    const bf16* __restrict__ qkv, long ld, int R, int H, const bf16* __restrict__ wq, const bf16* __restrict__ wk,
+    const float2* __restrict__ freqs, int freq_rows, float eps, bf16* __restrict__ qo, bf16* __restrict__ ko, long ldo,
+    float* __restrict__ rstd_q, float* __restrict__ rstd_k) {
+  constexpr int NC = DH / 8;
+  const long RH = (long)R * H;
+  const long t = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= 2 * RH) return;
+  const int which = t >= RH ? 1 : 0;  // 0 = q, 1 = k
+  const long item = t - which * RH;
+  const int row = (int)(item / H), h = (int)(item % H);
+  const bf16* src = qkv + (long)row * ld + (long)which * H * DH + h * DH;
+  uint4 x[NC];
+#pragma unroll
+  for (int c = 0; c < NC; ++c) x[c] = *reinterpret_cast<const uint4*>(src + 8 * c);
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    const uint32_t wds[4] = {x[c].x, x[c].y, x[c].z, x[c].w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = unpack_bf16x2(wds[j]);
+      ss += f.x * f.x + f.y * f.y;
+    }
+  }
+  const float rs = rsqrtf(ss / DH + eps);
+  float* rstd_out = which ? rstd_k : rstd_q;
+  if (rstd_out) rstd_out[item] = rs;
+  const bf16* w = which ? wk : wq;
+  const float2* fr = freqs ? freqs + (long)(row % freq_rows) * (DH / 2) : nullptr;
+  bf16* dst = (which ? ko : qo) + (long)row * ldo + h * DH;
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    const uint32_t wds[4] = {x[c].x, x[c].y, x[c].z, x[c].w};
+    uint4 wv = make_uint4(0x3f803f80u, 0x3f803f80u, 0x3f803f80u, 0x3f803f80u);  // bf16 1.0 pairs
+    if (w) wv = *reinterpret_cast<const uint4*>(w + 8 * c);
+    const uint32_t wws[4] = {wv.x, wv.y, wv.z, wv.w};
+    float4 cs01 = make_float4(1.f, 0.f, 1.f, 0.f), cs23 = cs01;
+    if (fr) {
+      cs01 = *reinterpret_cast<const float4*>(fr + 4 * c);
+      cs23 = *reinterpret_cast<const float4*>(fr + 4 * c + 2);
+    }
+    const float2 css[4] = {make_float2(cs01.x, cs01.y), make_float2(cs01.z, cs01.w), make_float2(cs23.x, cs23.y),
+                           make_float2(cs23.z, cs23.w)};
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = unpack_bf16x2(wds[j]);
+      const float2 wf = unpack_bf16x2(wws[j]);
+      const float a = f.x * rs * wf.x, b = f.y * rs * wf.y;
+      o[j] = pack_bf16x2(a * css[j].x - b * css[j].y, a * css[j].y + b * css[j].x);
+    }
+    *reinterpret_cast<uint4*>(dst + 8 * c) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
 // Backward of y = rope(rmsnorm(x)*w).  dy -> dx written into dqkv (ld), dw
 // partials per block into pw [nblk, Dh] (fp32).  Block handles `items_per_block`
 // (row, head) items, 8 warps.
@@ -984,6 +1046,29 @@ void qknorm_rope_fwd(const at::Tensor& qkv, int64_t H, int64_t Dh, const c10::op
   const at::cuda::CUDAGuard g(qkv.device());
   const long items = (long)R * H;
   const int threads = 256;
+  auto al16 = [](const void* p) { return p == nullptr || reinterpret_cast<uintptr_t>(p) % 16 == 0; };
+  const bool vec_ok = do_norm && al16(qkv.data_ptr()) && al16(qo.data_ptr()) && al16(ko.data_ptr()) &&
+                      (qkv.stride(0) * 2) % 16 == 0 && (qo.stride(0) * 2) % 16 == 0 &&
+                      al16(wq.has_value() ? wq->data_ptr() : nullptr) && al16(wk.has_value() ? wk->data_ptr() : nullptr) &&
+                      al16(freqs.has_value() ? freqs->data_ptr() : nullptr);
+#define HARP_QKN_FWD_VEC(DHV)                                                                                   \
+  if (vec_ok && Dh == DHV) {                                                                                    \
+    const long vgrid = (2 * items + threads - 1) / threads;                                                    \
+    qknorm_rope_fwd_vec_kernel<DHV><<<vgrid, threads, 0, at::cuda::getCurrentCUDAStream()>>>(                  \
+        bp(qkv), qkv.stride(0), R, (int)H, bp(wq), bp(wk),                                                     \
+        freqs.has_value() ? reinterpret_cast<const float2*>(freqs->data_ptr<float>()) : nullptr, (int)freq_rows, \
+        (float)eps, bpm(qo), bpm(ko), qo.stride(0), rstd_q.has_value() ? rstd_q->data_ptr<float>() : nullptr,    \
+        rstd_k.has_value() ? rstd_k->data_ptr<float>() : nullptr);                                              \
+    C10_CUDA_KERNEL_LAUNCH_CHECK();                                                                              \
+    count_launch();                                                                                              \
+    return;                                                                                                      \
+  }
+  HARP_QKN_FWD_VEC(64)
+  HARP_QKN_FWD_VEC(72)
+  HARP_QKN_FWD_VEC(80)
+  HARP_QKN_FWD_VEC(96)
+  HARP_QKN_FWD_VEC(128)
+#undef HARP_QKN_FWD_VEC
   const long grid = (items + 7) / 8;
   qknorm_rope_fwd_kernel<<<grid, threads, 0, at::cuda::getCurrentCUDAStream()>>>(
       bp(qkv), qkv.stride(0), R, H, Dh, bp(wq), bp(wk),
