@@ -172,6 +172,114 @@ __global__ void rmsnorm_mod_bwd_kernel(const bf16* __restrict__ x, long ldx, con
   }
 }
 
+// Row-parallel form of the backward for D % 128 == 0 (D <= 2304): a warp per
+// row, each lane holding 4 * NC4 elements of x and dy as 8-byte loads, so x
+// and dy are read once.  1 + scale[b] and w sit in shared memory; the column
+// partial sums (dw, dscale, dshift) accumulate in a shared-memory slab per
+// warp (each lane owns its columns: no atomics) and are summed over the 4
+// warps in a fixed order at the end (deterministic).  Block = 4 warps, RPB
+// rows of one batch sample.
+template <int NC4, bool HAS_W>
+__global__ void __launch_bounds__(128) rmsnorm_mod_bwd_rows_kernel(
+    const bf16* __restrict__ x, long ldx, const float* __restrict__ rstd, const bf16* __restrict__ dy, long lddy,
+    const bf16* __restrict__ w, const bf16* __restrict__ scale, long ldm, int rows_per_batch, int R, int D, int RPB,
+    const bf16* __restrict__ dres, long ldres, bf16* __restrict__ dx, long lddx, float* __restrict__ pw,
+    float* __restrict__ ps, float* __restrict__ pb) {
+  constexpr int NACC = HAS_W ? 3 : 2;  // per warp: [dshift | dscale (| dw)] x D
+  extern __shared__ float sm[];
+  float* s_sc1 = sm;                                // [D] 1 + scale[b]
+  float* s_w = sm + D;                              // [D] w (HAS_W)
+  float* s_acc = sm + (HAS_W ? 2 : 1) * D;          // [4][NACC][D]
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int r0 = blockIdx.x * RPB;
+  const int b = r0 / rows_per_batch;
+  for (int c = threadIdx.x; c < D; c += blockDim.x) {
+    s_sc1[c] = scale ? 1.f + __bfloat162float(scale[(long)b * ldm + c]) : 1.f;
+    if (HAS_W) s_w[c] = __bfloat162float(w[c]);
+  }
+  float* acc = s_acc + (long)warp * NACC * D;
+  for (int c = lane * 4; c < NACC * D; c += 128) *reinterpret_cast<float4*>(acc + c) = make_float4(0.f, 0.f, 0.f, 0.f);
+  __syncthreads();
+  const int nr = min(RPB, R - r0);
+  for (int rr = warp; rr < nr; rr += 4) {
+    const int row = r0 + rr;
+    const float rs = rstd[row];
+    uint2 xv[NC4], gv[NC4];
+#pragma unroll
+    for (int k = 0; k < NC4; ++k) {
+      xv[k] = *reinterpret_cast<const uint2*>(x + (long)row * ldx + 4 * (lane + 32 * k));
+      gv[k] = *reinterpret_cast<const uint2*>(dy + (long)row * lddy + 4 * (lane + 32 * k));
+    }
+    float dot = 0.f;
+#pragma unroll
+    for (int k = 0; k < NC4; ++k) {
+      const int c = 4 * (lane + 32 * k);
+      const float4 s4 = *reinterpret_cast<const float4*>(s_sc1 + c);
+      float4 w4 = make_float4(1.f, 1.f, 1.f, 1.f);
+      if (HAS_W) w4 = *reinterpret_cast<const float4*>(s_w + c);
+      const float2 x0 = unpack_bf16x2(xv[k].x), x1 = unpack_bf16x2(xv[k].y);
+      const float2 g0 = unpack_bf16x2(gv[k].x), g1 = unpack_bf16x2(gv[k].y);
+      dot += g0.x * s4.x * w4.x * x0.x + g0.y * s4.y * w4.y * x0.y + g1.x * s4.z * w4.z * x1.x +
+             g1.y * s4.w * w4.w * x1.y;
+    }
+    const float mu = warp_sum(dot) * rs / D;
+#pragma unroll
+    for (int k = 0; k < NC4; ++k) {
+      const int c = 4 * (lane + 32 * k);
+      const float4 s4 = *reinterpret_cast<const float4*>(s_sc1 + c);
+      float4 w4 = make_float4(1.f, 1.f, 1.f, 1.f);
+      if (HAS_W) w4 = *reinterpret_cast<const float4*>(s_w + c);
+      const float2 x0 = unpack_bf16x2(xv[k].x), x1 = unpack_bf16x2(xv[k].y);
+      const float2 g0 = unpack_bf16x2(gv[k].x), g1 = unpack_bf16x2(gv[k].y);
+      const float xf[4] = {x0.x, x0.y, x1.x, x1.y}, gf[4] = {g0.x, g0.y, g1.x, g1.y};
+      const float sf[4] = {s4.x, s4.y, s4.z, s4.w}, wf[4] = {w4.x, w4.y, w4.z, w4.w};
+      float rf[4] = {0.f, 0.f, 0.f, 0.f};
+      if (dres) {
+        const uint2 r2 = *reinterpret_cast<const uint2*>(dres + (long)row * ldres + c);
+        const float2 ra = unpack_bf16x2(r2.x), rb = unpack_bf16x2(r2.y);
+        rf[0] = ra.x; rf[1] = ra.y; rf[2] = rb.x; rf[3] = rb.y;
+      }
+      float o[4], db[4], dsc[4], dwv[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float xh = xf[j] * rs;
+        const float g = gf[j] * sf[j];
+        o[j] = rs * (g * wf[j] - xh * mu) + rf[j];
+        db[j] = gf[j];
+        dsc[j] = gf[j] * xh * wf[j];
+        dwv[j] = g * xh;
+      }
+      *reinterpret_cast<uint2*>(dx + (long)row * lddx + c) = make_uint2(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]));
+      float4* ab = reinterpret_cast<float4*>(acc + c);
+      float4* as = reinterpret_cast<float4*>(acc + D + c);
+      float4 t = *ab;
+      *ab = make_float4(t.x + db[0], t.y + db[1], t.z + db[2], t.w + db[3]);
+      t = *as;
+      *as = make_float4(t.x + dsc[0], t.y + dsc[1], t.z + dsc[2], t.w + dsc[3]);
+      if (HAS_W) {
+        float4* aw = reinterpret_cast<float4*>(acc + 2 * D + c);
+        t = *aw;
+        *aw = make_float4(t.x + dwv[0], t.y + dwv[1], t.z + dwv[2], t.w + dwv[3]);
+      }
+    }
+  }
+  __syncthreads();
+  const long base = (long)blockIdx.x * D;
+  for (int c = threadIdx.x; c < D; c += blockDim.x) {
+    float s_b = 0.f, s_s = 0.f, s_w2 = 0.f;
+#pragma unroll
+    for (int wi = 0; wi < 4; ++wi) {
+      const float* a = s_acc + (long)wi * NACC * D;
+      s_b += a[c];
+      s_s += a[D + c];
+      if (HAS_W) s_w2 += a[2 * D + c];
+    }
+    if (pb) pb[base + c] = s_b;
+    if (ps) ps[base + c] = s_s;
+    if (HAS_W && pw) pw[base + c] = s_w2;
+  }
+}
+
 // out[g, d] (+)= sum_{j in group g} partial[j, d]; groups of `per_group`
 // consecutive partial rows.  out fp32 or bf16 with row stride ldo.
 // Block = 32 columns x 8 warps: lane = column, warp w sums rows w, w+8, ...
@@ -1006,6 +1114,46 @@ void rmsnorm_mod_bwd(const at::Tensor& x, const at::Tensor& rstd, const at::Tens
   if (R == 0) return;
   const at::cuda::CUDAGuard g(x.device());
   const int nblk = (R + rpb - 1) / rpb;
+  auto al = [](const void* p, long ld) { return p == nullptr || (reinterpret_cast<uintptr_t>(p) % 8 == 0 && ld % 4 == 0); };
+  const bool rows_ok = D % 128 == 0 && D <= 2304 && al(x.data_ptr(), x.stride(0)) && al(dy.data_ptr(), dy.stride(0)) &&
+                       al(dx.data_ptr(), dx.stride(0)) && al(dres.has_value() ? dres->data_ptr() : nullptr, ld_of(dres)) &&
+                       al(scale.has_value() ? scale->data_ptr() : nullptr, ld_of(scale)) &&
+                       al(w.has_value() ? w->data_ptr() : nullptr, 0);
+  if (rows_ok) {
+#define HARP_RMS_BWD_ROWS(N4)                                                                                      \
+  case N4: {                                                                                                       \
+    const bool has_w = w.has_value();                                                                              \
+    auto* kern = has_w ? rmsnorm_mod_bwd_rows_kernel<N4, true> : rmsnorm_mod_bwd_rows_kernel<N4, false>;            \
+    const int smem = ((has_w ? 2 : 1) * D + 4 * (has_w ? 3 : 2) * D) * (int)sizeof(float);                          \
+    static bool cfg = false;                                                                                       \
+    if (!cfg) {                                                                                                    \
+      C10_CUDA_CHECK(cudaFuncSetAttribute(rmsnorm_mod_bwd_rows_kernel<N4, true>,                                   \
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, 14 * 128 * N4 * 4));        \
+      C10_CUDA_CHECK(cudaFuncSetAttribute(rmsnorm_mod_bwd_rows_kernel<N4, false>,                                  \
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, 14 * 128 * N4 * 4));        \
+      cfg = true;                                                                                                  \
+    }                                                                                                              \
+    kern<<<nblk, 128, smem, at::cuda::getCurrentCUDAStream()>>>(                                                   \
+        bp(x), x.stride(0), rstd.data_ptr<float>(), bp(dy), dy.stride(0), bp(w), bp(scale), ld_of(scale),          \
+        (int)rows_per_batch, R, D, (int)rpb, bp(dres), ld_of(dres), bpm(dx), dx.stride(0),                         \
+        pw.has_value() ? pw->data_ptr<float>() : nullptr, ps.has_value() ? ps->data_ptr<float>() : nullptr,        \
+        pb.has_value() ? pb->data_ptr<float>() : nullptr);                                                         \
+    C10_CUDA_KERNEL_LAUNCH_CHECK();                                                                                \
+    count_launch();                                                                                                \
+    return;                                                                                                        \
+  }
+    switch (D / 128) {
+      HARP_RMS_BWD_ROWS(4)
+      HARP_RMS_BWD_ROWS(6)
+      HARP_RMS_BWD_ROWS(8)
+      HARP_RMS_BWD_ROWS(9)
+      HARP_RMS_BWD_ROWS(12)
+      HARP_RMS_BWD_ROWS(16)
+      HARP_RMS_BWD_ROWS(18)
+      default: break;  // wider rows keep the column-parallel kernel (registers)
+    }
+#undef HARP_RMS_BWD_ROWS
+  }
   const int threads = 256;
   rmsnorm_mod_bwd_kernel<<<nblk, threads, rpb * sizeof(float), at::cuda::getCurrentCUDAStream()>>>(
       bp(x), x.stride(0), rstd.data_ptr<float>(), bp(dy), dy.stride(0), bp(w), bp(scale), ld_of(scale),

@@ -138,9 +138,11 @@ def _rms_ref(x, w, scale, shift, rpb, eps):
     return y
 
 
+@pytest.mark.parametrize("D,use_dres", [(1152, False), (1152, True), (1000, True)])
 @pytest.mark.parametrize("use_w,use_mod", [(True, False), (False, True), (True, True)])
-def test_rmsnorm_mod_fwd_bwd(use_w, use_mod):
-    Bn, S, D, eps = 3, 96, 1152, 1e-6
+def test_rmsnorm_mod_fwd_bwd(use_w, use_mod, D, use_dres):
+    """D=1152 runs the row-parallel backward, D=1000 the column-parallel one."""
+    Bn, S, eps = 3, 96, 1e-6
     R = Bn * S
     x = torch.randn(R, D, device="cuda").to(torch.bfloat16)
     w = (torch.rand(D, device="cuda") + 0.5).to(torch.bfloat16) if use_w else None
@@ -160,7 +162,10 @@ def test_rmsnorm_mod_fwd_bwd(use_w, use_mod):
     ps = torch.empty(nblk, D, device="cuda") if use_mod else None
     pb = torch.empty(nblk, D, device="cuda") if use_mod else None
     dx = torch.empty_like(x)
-    torch.ops.harp.rmsnorm_mod_bwd(x, rstd, dy, w, scale, S, None, dx, pw, ps, pb, rpb)
+    dres = torch.randn(R, D, device="cuda").to(torch.bfloat16) if use_dres else None
+    torch.ops.harp.rmsnorm_mod_bwd(x, rstd, dy, w, scale, S, dres, dx, pw, ps, pb, rpb)
+    if use_dres:
+        dx = (dx.float() - dres.float()).to(torch.bfloat16)
     xr = x.float().requires_grad_()
     wr = w.float().requires_grad_() if use_w else None
     scr = scale.float().requires_grad_() if use_mod else None
