@@ -716,6 +716,70 @@ __global__ void gate_bwd_kernel(const bf16* __restrict__ dy, long lddy, const bf
   }
 }
 
+// Row-parallel form for D % 128 == 0 (D <= 2304), same layout as
+// rmsnorm_mod_bwd_rows_kernel: a warp per row, 8-byte loads held in
+// registers, gate[b] in shared memory, column partials (dgate, dbias) in a
+// shared-memory slab per warp, summed over the 4 warps in a fixed order.
+template <int NC4>
+__global__ void __launch_bounds__(128) gate_bwd_rows_kernel(const bf16* __restrict__ dy, long lddy,
+                                                           const bf16* __restrict__ a, long lda,
+                                                           const bf16* __restrict__ gate, long ldg, int rows_per_batch,
+                                                           int R, int D, int RPB, bf16* __restrict__ da, long ldda,
+                                                           float* __restrict__ pg, float* __restrict__ pb) {
+  extern __shared__ float sm[];
+  float* s_g = sm;          // [D] gate[b]
+  float* s_acc = sm + D;    // [4][2][D]: dbias | dgate
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int r0 = blockIdx.x * RPB;
+  const int b = r0 / rows_per_batch;
+  for (int c = threadIdx.x; c < D; c += blockDim.x) s_g[c] = __bfloat162float(gate[(long)b * ldg + c]);
+  float* acc = s_acc + (long)warp * 2 * D;
+  for (int c = lane * 4; c < 2 * D; c += 128) *reinterpret_cast<float4*>(acc + c) = make_float4(0.f, 0.f, 0.f, 0.f);
+  __syncthreads();
+  const int nr = min(RPB, R - r0);
+  for (int rr = warp; rr < nr; rr += 4) {
+    const int row = r0 + rr;
+    uint2 gv[NC4], av[NC4];
+#pragma unroll
+    for (int k = 0; k < NC4; ++k) {
+      gv[k] = *reinterpret_cast<const uint2*>(dy + (long)row * lddy + 4 * (lane + 32 * k));
+      if (a) av[k] = *reinterpret_cast<const uint2*>(a + (long)row * lda + 4 * (lane + 32 * k));
+    }
+#pragma unroll
+    for (int k = 0; k < NC4; ++k) {
+      const int c = 4 * (lane + 32 * k);
+      const float4 g4 = *reinterpret_cast<const float4*>(s_g + c);
+      const float2 d0 = unpack_bf16x2(gv[k].x), d1 = unpack_bf16x2(gv[k].y);
+      const float df[4] = {d0.x, d0.y, d1.x, d1.y}, gf[4] = {g4.x, g4.y, g4.z, g4.w};
+      float o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) o[j] = df[j] * gf[j];
+      *reinterpret_cast<uint2*>(da + (long)row * ldda + c) = make_uint2(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]));
+      float4* ab = reinterpret_cast<float4*>(acc + c);
+      float4 t = *ab;
+      *ab = make_float4(t.x + o[0], t.y + o[1], t.z + o[2], t.w + o[3]);
+      if (a) {
+        const float2 a0 = unpack_bf16x2(av[k].x), a1 = unpack_bf16x2(av[k].y);
+        float4* ag = reinterpret_cast<float4*>(acc + D + c);
+        t = *ag;
+        *ag = make_float4(t.x + df[0] * a0.x, t.y + df[1] * a0.y, t.z + df[2] * a1.x, t.w + df[3] * a1.y);
+      }
+    }
+  }
+  __syncthreads();
+  const long base = (long)blockIdx.x * D;
+  for (int c = threadIdx.x; c < D; c += blockDim.x) {
+    float s_b = 0.f, s_gt = 0.f;
+#pragma unroll
+    for (int wi = 0; wi < 4; ++wi) {
+      s_b += s_acc[(long)wi * 2 * D + c];
+      s_gt += s_acc[(long)wi * 2 * D + D + c];
+    }
+    if (pb) pb[base + c] = s_b;
+    if (pg) pg[base + c] = s_gt;
+  }
+}
+
 // Column partial sums of a bf16 matrix (bias grad): partial[blk, d] = sum rows.
 __global__ void colsum_partial_kernel(const bf16* __restrict__ x, long ldx, int R, int D, int RPB,
                                       float* __restrict__ part) {
@@ -1310,6 +1374,38 @@ void gate_bwd(const at::Tensor& dy, const c10::optional<at::Tensor>& a, const at
   TORCH_CHECK(D % 8 == 0, "gate_bwd: D % 8");
   const at::cuda::CUDAGuard g(dy.device());
   const int nblk = (R + rpb - 1) / rpb;
+  auto al = [](const void* p, long ld) { return p == nullptr || (reinterpret_cast<uintptr_t>(p) % 8 == 0 && ld % 4 == 0); };
+  if (D % 128 == 0 && D <= 2304 && al(dy.data_ptr(), dy.stride(0)) && al(da.data_ptr(), da.stride(0)) &&
+      al(a.has_value() ? a->data_ptr() : nullptr, ld_of(a))) {
+    const int smem = 9 * D * (int)sizeof(float);
+#define HARP_GATE_BWD_ROWS(N4)                                                                                      \
+  case N4: {                                                                                                        \
+    static bool cfg = false;                                                                                        \
+    if (!cfg) {                                                                                                     \
+      C10_CUDA_CHECK(cudaFuncSetAttribute(gate_bwd_rows_kernel<N4>, cudaFuncAttributeMaxDynamicSharedMemorySize,    \
+                                          9 * 128 * N4 * 4));                                                       \
+      cfg = true;                                                                                                   \
+    }                                                                                                               \
+    gate_bwd_rows_kernel<N4><<<nblk, 128, smem, at::cuda::getCurrentCUDAStream()>>>(                                \
+        bp(dy), dy.stride(0), bp(a), ld_of(a), bp(gate), gate.stride(0), (int)rows_per_batch, R, D, (int)rpb,       \
+        bpm(da), da.stride(0), pg.has_value() ? pg->data_ptr<float>() : nullptr,                                   \
+        pb.has_value() ? pb->data_ptr<float>() : nullptr);                                                          \
+    C10_CUDA_KERNEL_LAUNCH_CHECK();                                                                                 \
+    count_launch();                                                                                                 \
+    return;                                                                                                         \
+  }
+    switch (D / 128) {
+      HARP_GATE_BWD_ROWS(4)
+      HARP_GATE_BWD_ROWS(6)
+      HARP_GATE_BWD_ROWS(8)
+      HARP_GATE_BWD_ROWS(9)
+      HARP_GATE_BWD_ROWS(12)
+      HARP_GATE_BWD_ROWS(16)
+      HARP_GATE_BWD_ROWS(18)
+      default: break;
+    }
+#undef HARP_GATE_BWD_ROWS
+  }
   const int threads = 128;
   const int ycols = std::max(1, std::min(8, (D / 8 + threads - 1) / threads));
   dim3 grid(nblk, ycols);

@@ -249,8 +249,13 @@ def test_swiglu_and_gate_bwd():
     hr.backward(dh.float())
     assert (dgu[:, :F].float() - g.grad).abs().max() < 0.05
     assert (dgu[:, F:].float() - u.grad).abs().max() < 0.05
-    # gated residual backward
-    Bn, S, D = 2, 128, 384
+
+
+
+@pytest.mark.parametrize("D", [384, 1152])
+def test_gate_bwd(D):
+    """Gated-residual backward: D=1152 takes the row-parallel kernel, D=384 the column-parallel one."""
+    Bn, S = 2, 128
     dy = torch.randn(Bn * S, D, device="cuda").to(torch.bfloat16)
     a = torch.randn(Bn * S, D, device="cuda").to(torch.bfloat16)
     gate = torch.randn(Bn, D, device="cuda").to(torch.bfloat16)
@@ -266,6 +271,9 @@ def test_swiglu_and_gate_bwd():
     torch.ops.harp.reduce_partials(pg, S // rpb, gg, False)
     ref_g = (dy.float() * a.float()).view(Bn, S, D).sum(1)
     assert torch.allclose(gg, ref_g, atol=0.3, rtol=1e-2)
+    gb = torch.empty(1, D, device="cuda")
+    torch.ops.harp.reduce_partials(pb, nblk, gb, False)
+    assert torch.allclose(gb[0], ref_da.sum(0), atol=0.3, rtol=1e-2)
 
 
 def test_adamw_flat_matches_torch():
