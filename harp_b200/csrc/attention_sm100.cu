@@ -139,6 +139,13 @@ __device__ __forceinline__ uint64_t mnmajor_desc(uint32_t tile_addr, int ks) {
   return make_sdesc(tile_addr + ks * 256, 128, 2048, kLayoutNone);
 }
 
+// TMEM column of a packed bf16 P (forward) or P^T / dS^T (backward) chunk:
+// the 32 scores of chunk c (columns [32c, 32c + 32)) pack into 16 columns at
+// pcol(c), i.e. chunks 0-1 at 0-31 and chunks 2-3 at 64-95.  Two warps share a
+// TMEM lane quarter, one per half of the columns; each writes only inside the
+// half it has already read, so neither overwrites scores the other still reads.
+__device__ __forceinline__ constexpr uint32_t pcol(int c) { return c * 16 + (c >= 2 ? 32 : 0); }
+
 // ===========================================================================
 // Forward
 // ===========================================================================
@@ -172,9 +179,12 @@ struct FwdCfg {
   static constexpr int DPAD = NCH * 8;
   static constexpr int TILE = NCH * 2048;
   static constexpr int STAGES = (NCH <= 10) ? 3 : 2;
-  static constexpr int SMEM = 2 * TILE + STAGES * 2 * TILE + 256 + 256;  // 256-B alignment slack + barriers
+  static constexpr int XCH = (2 * 2 * 2 * 128 + 2 * 2 * 128) * 4;  // row-max (by key-step parity) and row-sum exchange
+  static constexpr int SMEM = 2 * TILE + STAGES * 2 * TILE + 256 + 256 + XCH;  // 256-B alignment slack + barriers
 };
-constexpr int kFwdThreads = 384;  // w0 TMA, w1 MMA, w2-3 spare, w4-7 softmax tile 0, w8-11 softmax tile 1
+// w0 TMA, w1 MMA, w2..17 softmax: 8 warps per query tile, two per TMEM lane
+// quarter (key columns 0-63 / 64-127 of each score tile)
+constexpr int kFwdThreads = 576;
 
 template <int NCH, int NPOLY>
 __global__ void __launch_bounds__(kFwdThreads, 1)
@@ -197,6 +207,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   uint64_t* p_full = s_full + 2;    // [2]
   uint64_t* o_final = p_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_final + 1);
+  float* xch = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 256);  // [2][2][2][128] max | [2][2][128] sum
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int nqp = (a.Sq + 255) / 256;
@@ -222,7 +233,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(&s_full[t], 1);
-      mbar_init(&p_full[t], 4);
+      mbar_init(&p_full[t], 8);
     }
     mbar_init(o_final, 1);
     fence_mbar_init();
@@ -312,7 +323,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           tc_fence_after();
 #pragma unroll
           for (int ks = 0; ks < 8; ++ks)
-            mma_ts(tmem + 256 + t * 128, tmem + t * 128 + ks * 8, mnmajor_sw32(va, ks), idO,
+            mma_ts(tmem + 256 + t * 128, tmem + t * 128 + pcol(ks / 2) + (ks & 1) * 8, mnmajor_sw32(va, ks), idO,
                    (jj > 0 || ks > 0) ? 1u : 0u);
           if (has_next) {
             if (t == 0) {
@@ -331,26 +342,37 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       mma_commit(o_final);
       mbar_wait_drain(o_final, 0);
     }
-  } else if (warp >= 4) {
-    const int t = (warp - 4) / 4;
+  } else {
+    // softmax warps: t = query tile, hf = half of the 128 key columns
+    const int sw = warp - 2;
+    const int t = sw / 8, hf = (sw / 4) & 1;
     const int quarter = warp & 3;
     if (t < ntile) {
       const int rloc = quarter * 32 + lane;
       const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
       const uint32_t tS = tmem + lane_off + t * 128;
       const uint32_t tO = tmem + lane_off + 256 + t * 128;
+      const int bar_id = 1 + t * 4 + quarter;  // the two warps of this lane quarter and tile
+      float* xmax = xch;                       // [parity][tile][half][row]
+      float* xsum = xch + 2 * 2 * 2 * 128;     // [tile][half][row]
+      // O columns this warp rescales / stores: 16-column chunks [o_lo, o_hi)
+      constexpr int OCH = C::DPAD / 16;
+      const int o_lo = hf ? (OCH + 1) / 2 : 0, o_hi = hf ? OCH : (OCH + 1) / 2;
       float m = -INFINITY, l = 0.f;
       bool ok = true;
       for (int jj = 0; jj < nkv; ++jj) {
         const int j = (a.start_tile + jj) % nkv;
         const int nvalid = min(128, a.Skv - j * 128);
-        if (!mbar_wait(&s_full[t], jj & 1, err, 40)) { ok = false; break; }
-        if (quarter == 0 && lane == 0) FWD_PROBE(jj, 4 + 3 * t);
+        // no early exit: both warps of the lane quarter must meet at every
+        // named barrier below; after an error the bounded waits return at once
+        if (!mbar_wait(&s_full[t], jj & 1, err, 40)) ok = false;
+        if (hf == 0 && quarter == 0 && lane == 0) FWD_PROBE(jj, 4 + 3 * t);
         tc_fence_after();
         const bool full_tile = (nvalid == 128);  // only the last key tile of a sequence is partial
         float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int cc = 0; cc < 2; ++cc) {
+          const int c = 2 * hf + cc;
           uint32_t v[32];
           tmem_ld32(tS + c * 32, v);
           tmem_wait_ld();
@@ -368,32 +390,37 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
               if (c * 32 + i < nvalid) mx0 = fmaxf(mx0, __uint_as_float(v[i]));
           }
         }
-        const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
-        if (quarter == 0 && lane == 0) FWD_PROBE(jj, 5 + 3 * t);
+        // combine the two halves' row maxima (buffer by key-step parity: the
+        // other warp may still read the previous step's value)
+        float* xm = xmax + ((jj & 1) * 2 + t) * 2 * 128;
+        xm[hf * 128 + rloc] = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
+        asm volatile("bar.sync %0, 64;" ::"r"(bar_id) : "memory");
+        const float mx = fmaxf(xm[rloc], xm[128 + rloc]);
+        if (hf == 0 && quarter == 0 && lane == 0) FWD_PROBE(jj, 5 + 3 * t);
         const float m_new = fmaxf(m, mx * a.scale_log2);
         const bool need = m_new > m + kRescaleThreshold;
         if (__any_sync(0xffffffffu, need)) {
           if (jj > 0) {
             const float alpha = ex2_approx(m - m_new);
             l *= alpha;
-#pragma unroll
-            for (int c = 0; c < C::DPAD; c += 16) {
+            for (int oc = o_lo; oc < o_hi; ++oc) {
               uint32_t v[16];
-              tmem_ld16(tO + c, v);
+              tmem_ld16(tO + oc * 16, v);
               tmem_wait_ld();
 #pragma unroll
               for (int i = 0; i < 16; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
-              tmem_st16(tO + c, v);
+              tmem_st16(tO + oc * 16, v);
             }
           }
           m = m_new;
         }
-        // p = 2^(s*scale*log2e - m): one packed FMA per pair, MUFU ex2, packed sum.
+        // p = 2^(s*scale*log2e - m): one packed FMA per pair, ex2, packed sum.
         const float2 scl = make_float2(a.scale_log2, a.scale_log2);
         const float2 negm = make_float2(-m, -m);
         float2 lacc = make_float2(0.f, 0.f);
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int cc = 0; cc < 2; ++cc) {
+          const int c = 2 * hf + cc;
           uint32_t v[32];
           tmem_ld32(tS + c * 32, v);
           tmem_wait_ld();
@@ -410,22 +437,26 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             lacc = __fadd2_rn(lacc, p);
             pk[i] = pack_bf16x2(p.x, p.y);
           }
-          tmem_st16(tS + c * 16, pk);
+          tmem_st16(tS + pcol(c), pk);
         }
         l += lacc.x + lacc.y;
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[t]);
-        if (quarter == 0 && lane == 0) FWD_PROBE(jj, 6 + 3 * t);
+        if (hf == 0 && quarter == 0 && lane == 0) FWD_PROBE(jj, 6 + 3 * t);
       }
+      // row sum over both halves
+      xsum[(t * 2 + hf) * 128 + rloc] = l;
+      asm volatile("bar.sync %0, 64;" ::"r"(bar_id) : "memory");
+      l = xsum[(t * 2) * 128 + rloc] + xsum[(t * 2 + 1) * 128 + rloc];
       if (ok) ok = mbar_wait(o_final, 0, err, 41);
       tc_fence_after();
       const int s = q0 + t * 128 + rloc;
       const float inv_l = (l > 0.f) ? 1.f / l : 0.f;
       bf16* orow = a.O + (long)(b * a.Sq + s) * a.ldo + h * a.Dh;
-#pragma unroll
-      for (int c = 0; c < C::DPAD; c += 16) {
+      for (int oc = o_lo; oc < o_hi; ++oc) {
+        const int c = oc * 16;
         uint32_t v[16];
         tmem_ld16(tO + c, v);
         tmem_wait_ld();
@@ -444,7 +475,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           }
         }
       }
-      if (s < a.Sq && ok) a.lse[(long)(b * a.H + h) * a.lse_ld + s] = (m + log2f(l)) * kLn2;
+      if (hf == 0 && s < a.Sq && ok) a.lse[(long)(b * a.H + h) * a.lse_ld + s] = (m + log2f(l)) * kLn2;
     }
   }
 
@@ -511,9 +542,7 @@ constexpr int kBwdThreads = 320;  // overlapped schedule: w0 TMA, w1 MMA, w2-5 /
 // dQ warps, w10-13 dS warps (columns 64-127).  Two dS warps per SM sub-partition
 // hide each other's TMEM-load and exp latencies.
 constexpr int kBwdThreads1 = 448;
-// TMEM column of the packed bf16 P^T / dS^T for queries [32c, 32c + 32):
-// chunks 0-1 (warps 2-5) at 0-31, chunks 2-3 (warps 10-13) at 64-95.
-__device__ __forceinline__ constexpr uint32_t pcol(int c) { return c * 16 + (c >= 2 ? 32 : 0); }
+
 
 template <int NCH>
 __global__ void __launch_bounds__(kBwdThreads1, 1)
