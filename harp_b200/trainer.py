@@ -303,6 +303,8 @@ class Trainer:
         the loss as a device tensor.  With `cuda_graph`, the first
         `graph_warmup` steps run eagerly, the next one is captured, and later
         steps copy the batch into the captured step's inputs and replay it."""
+        if self.graph_enabled and not all(isinstance(v, torch.Tensor) for v in batch.values()):
+            self.graph_enabled = False  # list-valued inputs (e.g. Z-Image conditions) run eagerly
         if not self.graph_enabled:
             dev = self.device
             b = {k: _to_dev(v, dev) for k, v in batch.items()}

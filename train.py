@@ -79,6 +79,8 @@ def parse_args(argv=None):
     p.add_argument("--sp_mode", type=str, default="auto", choices=["auto", "ring", "ulysses"],
                    help="sequence-parallel attention: K/V gather (the reference's ring) or head all-to-all")
     p.add_argument("--enable_profiler", action="store_true")
+    p.add_argument("--cuda_graph", action="store_true",
+                   help="single GPU: capture the whole training step in one CUDA graph after two eager steps")
     p.add_argument("--harp_block_compat", action="store_true", help="Z-Image: reproduce HARP's block residual")
     # accepted for command-line compatibility, unused (as in the reference)
     for flag, typ in (("--use_8bit_adam", bool), ("--rank", int), ("--resolution", int), ("--cache_dir", str),
@@ -210,7 +212,8 @@ def main(args):
     model, loss_fn, shapes = build_model(args, device, par.sp_group)
     lr = args.learning_rate * (world * args.train_batch_size if args.scale_lr else 1)
     tcfg = TrainConfig(lr=lr, beta1=args.adam_beta1, beta2=args.adam_beta2, eps=args.adam_epsilon,
-                       weight_decay=args.adam_weight_decay, comm=args.comm_backend)
+                       weight_decay=args.adam_weight_decay, comm=args.comm_backend,
+                       cuda_graph=bool(getattr(args, "cuda_graph", False)))
     trainer = Trainer(model, par, tcfg, device, sp_backend=args.comm_backend, loss_fn=loss_fn,
                       sp_mode=args.sp_mode)
     sched = D.FlowMatchEulerDiscreteScheduler.from_pretrained(args.pretrained_model_name_or_path or ".",
