@@ -531,17 +531,24 @@ __global__ void qknorm_rope_bwd_kernel(const bf16* __restrict__ dq, const bf16* 
   }
 }
 
-// Vectorized backward: one thread per (row, head) of q (blockIdx.y == 0) or k
-// (blockIdx.y == 1), 16-byte loads, two passes over the head (the second hits
-// L1).  Block b owns items [b*ipb, (b+1)*ipb); its threads stride over them and
-// accumulate d(w) in registers, reduced once per block into pw[b].
-template <int DH>
+// Vectorized backward: TPI threads per (row, head) of q (blockIdx.y == 0) or
+// k (blockIdx.y == 1), each holding every TPI-th 8-element chunk of the head
+// as 16-byte loads in registers (one read of dy and x); the row dot product
+// meets over the TPI lanes with shuffles.  Block b owns items
+// [b*ipb, (b+1)*ipb); its item slots stride over them and accumulate d(w) in
+// registers, reduced once per block into pw[b] (fixed order: deterministic).
+// Splitting a head over TPI threads keeps the registers low enough for
+// several blocks per SM.
+template <int DH, int TPI>
 __global__ void __launch_bounds__(128) qknorm_rope_bwd_vec_kernel(
     const bf16* __restrict__ dq, const bf16* __restrict__ dk, long lddq, long lddk, const bf16* __restrict__ qkv,
     long ld, const float* __restrict__ rstd_q, const float* __restrict__ rstd_k, int R, int H,
     const bf16* __restrict__ wq, const bf16* __restrict__ wk, const float2* __restrict__ freqs, int freq_rows,
     int do_norm, long ipb, bf16* __restrict__ dqkv, long lddx, float* __restrict__ pwq, float* __restrict__ pwk) {
   constexpr int NV = DH / 8;
+  constexpr int NVT = (NV + TPI - 1) / TPI;  // chunks per thread (the last ones may be past NV)
+  constexpr int SLOTS = 128 / TPI;
+  static_assert(32 % TPI == 0, "a head's lanes stay in one warp");
   const bool isk = blockIdx.y != 0;
   const bf16* gbase = isk ? dk : dq;
   const long ldg = isk ? lddk : lddq;
@@ -555,57 +562,70 @@ __global__ void __launch_bounds__(128) qknorm_rope_bwd_vec_kernel(
   __shared__ float sred[4][DH];
   for (int i = threadIdx.x; i < DH; i += blockDim.x) sw[i] = (w && do_norm) ? __bfloat162float(w[i]) : 1.f;
   __syncthreads();
-  float acc[DH];
+  const int sub = threadIdx.x % TPI, slot = threadIdx.x / TPI;
+  float acc[NVT * 8];
 #pragma unroll
-  for (int i = 0; i < DH; ++i) acc[i] = 0.f;
+  for (int i = 0; i < NVT * 8; ++i) acc[i] = 0.f;
   const long items = (long)R * H;
   const long lo = (long)blockIdx.x * ipb, hi = min(lo + ipb, items);
-  for (long item = lo + threadIdx.x; item < hi; item += blockDim.x) {
-    const int row = (int)(item / H), h = (int)(item % H);
+  // Every lane of a warp runs the same number of iterations (the shuffles
+  // below need all 32 lanes); lanes past the block's last item are inactive.
+  for (long base = lo; base < hi; base += SLOTS) {
+    const long item = base + slot;
+    const bool active = item < hi;
+    const long it = active ? item : lo;  // any valid item for the inactive lanes' address math
+    const int row = (int)(it / H), h = (int)(it % H);
     const bf16* gp = gbase + (long)row * ldg + h * DH;
     const bf16* xp = xbase + (long)row * ld + h * DH;
     const float4* fp = freqs ? reinterpret_cast<const float4*>(freqs + (long)(row % freq_rows) * (DH / 2)) : nullptr;
-    const float rs = do_norm ? rstd[item] : 1.f;
+    const float rs = do_norm ? rstd[it] : 1.f;
+    uint4 g4[NVT], x4[NVT];
+    float4 fa[NVT], fb[NVT];
+#pragma unroll
+    for (int u = 0; u < NVT; ++u) {
+      const int v = sub + TPI * u;
+      g4[u] = make_uint4(0u, 0u, 0u, 0u);
+      x4[u] = make_uint4(0u, 0u, 0u, 0u);
+      fa[u] = make_float4(1.f, 0.f, 1.f, 0.f);
+      fb[u] = fa[u];
+      if (active && v < NV) {
+        g4[u] = *reinterpret_cast<const uint4*>(gp + 8 * v);
+        if (do_norm) x4[u] = *reinterpret_cast<const uint4*>(xp + 8 * v);
+        if (fp) {
+          fa[u] = fp[2 * v];
+          fb[u] = fp[2 * v + 1];
+        }
+      }
+    }
     float dot = 0.f;
     if (do_norm) {
 #pragma unroll
-      for (int v = 0; v < NV; ++v) {
-        const uint4 g4 = *reinterpret_cast<const uint4*>(gp + 8 * v);
-        const uint4 x4 = *reinterpret_cast<const uint4*>(xp + 8 * v);
-        const uint32_t gw[4] = {g4.x, g4.y, g4.z, g4.w}, xw[4] = {x4.x, x4.y, x4.z, x4.w};
-        float4 fa = make_float4(1.f, 0.f, 1.f, 0.f), fb = fa;
-        if (fp) {
-          fa = fp[2 * v];
-          fb = fp[2 * v + 1];
-        }
-        const float cs[8] = {fa.x, fa.y, fa.z, fa.w, fb.x, fb.y, fb.z, fb.w};
+      for (int u = 0; u < NVT; ++u) {
+        const int v = sub + TPI * u;
+        if (v < NV) {
+          const uint32_t gw[4] = {g4[u].x, g4[u].y, g4[u].z, g4[u].w}, xw[4] = {x4[u].x, x4[u].y, x4[u].z, x4[u].w};
+          const float cs[8] = {fa[u].x, fa[u].y, fa[u].z, fa[u].w, fb[u].x, fb[u].y, fb[u].z, fb[u].w};
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float2 g = unpack_bf16x2(gw[j]), x = unpack_bf16x2(xw[j]);
-          const float c = cs[2 * j], sn = cs[2 * j + 1];
-          const float g0 = g.x * c + g.y * sn, g1 = -g.x * sn + g.y * c;  // inverse rotation
-          dot += g0 * sw[8 * v + 2 * j] * x.x + g1 * sw[8 * v + 2 * j + 1] * x.y;
+          for (int j = 0; j < 4; ++j) {
+            const float2 g = unpack_bf16x2(gw[j]), x = unpack_bf16x2(xw[j]);
+            const float c = cs[2 * j], sn = cs[2 * j + 1];
+            const float g0 = g.x * c + g.y * sn, g1 = -g.x * sn + g.y * c;  // inverse rotation
+            dot += g0 * sw[8 * v + 2 * j] * x.x + g1 * sw[8 * v + 2 * j + 1] * x.y;
+          }
         }
       }
+#pragma unroll
+      for (int o = 1; o < TPI; o <<= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
       dot *= rs;
     }
     const float mu = dot / DH;
     bf16* dxp = dxbase + (long)row * lddx + h * DH;
 #pragma unroll
-    for (int v = 0; v < NV; ++v) {
-      const uint4 g4 = *reinterpret_cast<const uint4*>(gp + 8 * v);
-      const uint32_t gw[4] = {g4.x, g4.y, g4.z, g4.w};
-      uint32_t xw[4] = {0u, 0u, 0u, 0u};
-      if (do_norm) {
-        const uint4 x4 = *reinterpret_cast<const uint4*>(xp + 8 * v);
-        xw[0] = x4.x; xw[1] = x4.y; xw[2] = x4.z; xw[3] = x4.w;
-      }
-      float4 fa = make_float4(1.f, 0.f, 1.f, 0.f), fb = fa;
-      if (fp) {
-        fa = fp[2 * v];
-        fb = fp[2 * v + 1];
-      }
-      const float cs[8] = {fa.x, fa.y, fa.z, fa.w, fb.x, fb.y, fb.z, fb.w};
+    for (int u = 0; u < NVT; ++u) {
+      const int v = sub + TPI * u;
+      if (!active || v >= NV) continue;
+      const uint32_t gw[4] = {g4[u].x, g4[u].y, g4[u].z, g4[u].w}, xw[4] = {x4[u].x, x4[u].y, x4[u].z, x4[u].w};
+      const float cs[8] = {fa[u].x, fa[u].y, fa[u].z, fa[u].w, fb[u].x, fb[u].y, fb[u].z, fb[u].w};
       uint32_t ow[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
@@ -616,8 +636,8 @@ __global__ void __launch_bounds__(128) qknorm_rope_bwd_vec_kernel(
           const float2 x = unpack_bf16x2(xw[j]);
           const float xh0 = x.x * rs, xh1 = x.y * rs;
           ow[j] = pack_bf16x2(rs * (g0 * sw[8 * v + 2 * j] - xh0 * mu), rs * (g1 * sw[8 * v + 2 * j + 1] - xh1 * mu));
-          acc[8 * v + 2 * j] += g0 * xh0;
-          acc[8 * v + 2 * j + 1] += g1 * xh1;
+          acc[8 * u + 2 * j] += g0 * xh0;
+          acc[8 * u + 2 * j + 1] += g1 * xh1;
         } else {
           ow[j] = pack_bf16x2(g0, g1);
         }
@@ -627,10 +647,23 @@ __global__ void __launch_bounds__(128) qknorm_rope_bwd_vec_kernel(
   }
   if (!want_w) return;
   const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
+  // sum over the warp's lanes that own the same chunks (same sub), fixed order
 #pragma unroll
-  for (int i = 0; i < DH; ++i) {
-    const float t = warp_sum(acc[i]);
-    if (lane == 0) sred[warp][i] = t;
+  for (int i = 0; i < NVT * 8; ++i) {
+    float t = acc[i];
+#pragma unroll
+    for (int o = TPI; o < 32; o <<= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    acc[i] = t;
+  }
+  if (lane < TPI) {
+#pragma unroll
+    for (int u = 0; u < NVT; ++u) {
+      const int v = lane + TPI * u;
+      if (v < NV) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) sred[warp][8 * v + j] = acc[8 * u + j];
+      }
+    }
   }
   __syncthreads();
   for (int i = threadIdx.x; i < DH; i += blockDim.x)
@@ -1312,7 +1345,7 @@ void qknorm_rope_bwd(const at::Tensor& dq, const at::Tensor& dk, const at::Tenso
   if (vec_ok) {
     const dim3 vgrid((unsigned)grid, 2);
 #define HARP_QKB(DHV)                                                                                              \
-  qknorm_rope_bwd_vec_kernel<DHV><<<vgrid, 128, 0, at::cuda::getCurrentCUDAStream()>>>(                          \
+  qknorm_rope_bwd_vec_kernel<DHV, 4><<<vgrid, 128, 0, at::cuda::getCurrentCUDAStream()>>>(                       \
       bp(dq), bp(dk), dq.stride(0), dk.stride(0), bp(qkv), qkv.stride(0),                                          \
       rstd_q.has_value() ? rstd_q->data_ptr<float>() : nullptr,                                                    \
       rstd_k.has_value() ? rstd_k->data_ptr<float>() : nullptr, R, (int)H, bp(wq), bp(wk),                         \

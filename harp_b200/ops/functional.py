@@ -311,7 +311,8 @@ def qknorm_rope_bwd(dq, dk, qkv, rq, rk, H, Dh, wq, wk, freqs, do_norm, dqkv, wa
     R = qkv.shape[0]
     frows = freqs.shape[0] if freqs is not None else 1
     if _cuda(qkv):
-        # about 4 blocks per SM, each thread striding over ~ipb/128 (row, head) items
+        # about 4 blocks per SM; a block's 32 item slots (4 threads per head)
+        # each stride over ~ipb/32 (row, head) items
         ipb = max(128, -(-R * H // (4 * _num_sms(qkv.device))))
         nblk = (R * H + ipb - 1) // ipb
         want = want_dw and do_norm and wq is not None
