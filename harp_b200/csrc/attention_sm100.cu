@@ -920,6 +920,7 @@ __global__ void __launch_bounds__(kBwdPipeThreads, 1)
   uint64_t* dqs_bar = dq_free + 1;
   uint64_t* fin = dqs_bar + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fin + 1);
+  static_assert((1 + 2 * ST + 8) * 8 + 4 <= 128, "barrier region");
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int nkt = (a.Skv + 127) / 128;
@@ -1236,6 +1237,366 @@ __global__ void __launch_bounds__(kBwdPipeThreads, 1)
   }
 }
 
+// ===========================================================================
+// Backward for head dim 128, pipelined over 64-query tiles.  With 128-query
+// tiles S, dP, dV and dK fill all 512 TMEM columns and dQ has to share S's
+// columns, which serializes the loop.  Here a query tile is 64 wide and dQ is
+// computed transposed, dQ^T = K^T dS^T (M = head dim on the TMEM lanes, N = 64
+// queries), so S^T, dP^T (64 columns each), dV, dK (128 each) and two dQ^T
+// slots (64 each) fit side by side and the schedule of attn_bwd_pipe_kernel
+// applies: the MMA warp issues S/dP of tile i+1 before dV/dK/dQ of tile i,
+// the dS warps release S/dP as soon as the scores are in registers, and dQ^T
+// of tile i is read out while tile i+1 runs.  The dQ warps stage dQ (query
+// rows, fp32) in the tile's Q/dO stage and reduce-add it with one TMA.
+//   s_full / s_free / p_full / p_free   as in attn_bwd_pipe_kernel
+//   dq_full[2] / dq_free[2]             dQ^T slot written / read out
+// ===========================================================================
+template <int NCH>
+struct BwdQ64Cfg {
+  static constexpr int DPAD = NCH * 8;
+  static constexpr int KTILE = NCH * 2048;  // 128 keys x DPAD, 32-byte swizzled atoms of 4 KB
+  static constexpr int QTILE = NCH * 1024;  // 64 queries x DPAD, atoms of 2 KB
+  static constexpr int PS_BYTES = 128 * 64 * 2;  // P^T or dS: 128 keys x 64 queries bf16, 8-query strips
+  static constexpr int LD_BYTES = 2 * 128 * 4;   // lse | delta of a 64-query tile, double-buffered
+  // 256 bytes of alignment slack, 256 for the barriers (at most 2 + 2 * 4 + 10) and the TMEM address
+  static constexpr int smem_for(int st) { return 2 * KTILE + st * 2 * QTILE + 2 * PS_BYTES + LD_BYTES + 256 + 256; }
+  static constexpr int STAGES = smem_for(4) <= 232448 ? 4 : 3;
+  static constexpr int SMEM = smem_for(STAGES);
+  static_assert(SMEM <= 232448, "exceeds the 227 KB per-CTA shared memory limit");
+  static_assert(DPAD == 128, "dQ^T puts the head dim on the 128 TMEM lanes");
+  static_assert(2 * QTILE >= 64 * DPAD * 4, "dQ staging (64 x Dh fp32) must fit in one Q/dO stage");
+  static constexpr int DV_COL = 128;
+  static constexpr int DK_COL = 128 + DPAD;
+  static constexpr int DQ_COL = 128 + 2 * DPAD;  // two 64-column slots
+  static_assert(DQ_COL + 128 <= 512, "TMEM columns");
+};
+constexpr int kBwdQ64Threads = 512;  // WG0: w0 TMA, w1 MMA; WG1/WG2: dS warps (queries 0-31 / 32-63); WG3: dQ warps
+
+// 64-row tiles: atom a of a 64 x DPAD tile at + a * 2048
+template <int NCH>
+__device__ __forceinline__ void load_sw32_tile64(uint8_t* dst, const CUtensorMap* map, uint64_t* bar, int row0, int h,
+                                                 int b) {
+#pragma unroll
+  for (int at = 0; at < NCH / 2; ++at) tma_load_4d(dst + at * 2048, map, bar, at * 16, h, row0, b);
+}
+__device__ __forceinline__ uint64_t kmajor_sw32_r64(uint32_t tile_addr, int ks) {
+  return make_sdesc(tile_addr + ks * 2048, 16, 256, kLayoutSw32);
+}
+__device__ __forceinline__ uint64_t mnmajor_sw32_r64(uint32_t tile_addr, int ks) {
+  return make_sdesc(tile_addr + ks * 512, 2048, 256, kLayoutSw32);
+}
+
+template <int NCH>
+__global__ void __launch_bounds__(kBwdQ64Threads, 1)
+    attn_bwd_q64_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                        const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
+                        const __grid_constant__ CUtensorMap tmdQ, const BwdArgs a) {
+  using C = BwdQ64Cfg<NCH>;
+  constexpr int ST = C::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sK = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 255) & ~uintptr_t(255));
+  uint8_t* sV = sK + C::KTILE;
+  uint8_t* sQD = sV + C::KTILE;          // stage st: Q at 2*st*QTILE, dO right after; later the dQ staging
+  uint8_t* sP = sQD + 2 * ST * C::QTILE;  // P^T: 128 keys x 64 queries, 8-query strips
+  uint8_t* sdS = sP + C::PS_BYTES;        // dS, same layout
+  float* sLD = reinterpret_cast<float*>(sdS + C::PS_BYTES);  // [2][lse 64 | delta 64]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(sLD) + C::LD_BYTES);
+  uint64_t* kv_full = bars;
+  uint64_t* qdo_full = bars + 1;        // [ST]
+  uint64_t* qdo_empty = qdo_full + ST;  // [ST]
+  uint64_t* s_full = qdo_empty + ST;
+  uint64_t* s_free = s_full + 1;
+  uint64_t* p_full = s_free + 1;
+  uint64_t* p_free = p_full + 1;
+  uint64_t* dq_full = p_free + 1;   // [2]
+  uint64_t* dq_free = dq_full + 2;  // [2]
+  uint64_t* dqs_bar = dq_free + 2;
+  uint64_t* fin = dqs_bar + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fin + 1);
+  static_assert((1 + 2 * ST + 4 + 4 + 2) * 8 + 4 <= 256, "barrier region");
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int nkt = (a.Skv + 127) / 128;
+  const int bh = blockIdx.x / nkt, kt = blockIdx.x % nkt;
+  const int b = bh / a.H, h = bh % a.H;
+  const int k0 = kt * 128;
+  const int nq = (a.Sq + 63) / 64;
+  int* err = a.err;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(&qdo_full[s], 1);
+      mbar_init(&qdo_empty[s], 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(s_free, 8);
+    mbar_init(p_full, 8);
+    mbar_init(p_free, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&dq_full[s], 1);
+      mbar_init(&dq_free[s], 4);
+    }
+    mbar_init(dqs_bar, 4);
+    mbar_init(fin, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS = tmem, tdP = tmem + 64, tdV = tmem + C::DV_COL, tdK = tmem + C::DK_COL,
+                 tdQ = tmem + C::DQ_COL;
+  const int wg = warp / 4;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      tma_prefetch_desc(&tmdO);
+      int issued[ST] = {};
+      bool ok = true;
+      mbar_arrive_expect_tx(kv_full, 2 * C::KTILE);
+      load_sw32_tile<NCH>(sK, &tmK, kv_full, k0, h, b);
+      load_sw32_tile<NCH>(sV, &tmV, kv_full, k0, h, b);
+      for (int i = 0; i < nq && ok; ++i) {
+        const int st = i % ST;
+        const uint32_t ph = (i / ST) & 1;
+        if (!mbar_wait(&qdo_empty[st], ph ^ 1, err, 250)) { ok = false; break; }
+        mbar_arrive_expect_tx(&qdo_full[st], 2 * C::QTILE);
+        load_sw32_tile64<NCH>(sQD + 2 * st * C::QTILE, &tmQ, &qdo_full[st], i * 64, h, b);
+        load_sw32_tile64<NCH>(sQD + (2 * st + 1) * C::QTILE, &tmdO, &qdo_full[st], i * 64, h, b);
+        issued[st]++;
+      }
+      mbar_wait_drain(kv_full, 0);
+      for (int s = 0; s < ST; ++s)
+        if (issued[s]) mbar_wait_drain(&qdo_full[s], (issued[s] - 1) & 1);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idS = make_idesc_bf16(128, 64, false, false);
+      constexpr uint32_t idO = make_idesc_bf16(128, C::DPAD, false, true);
+      constexpr uint32_t idQT = make_idesc_bf16(128, 64, true, true);
+      const uint32_t ka = smem_u32(sK), va = smem_u32(sV), pa = smem_u32(sP), dsa = smem_u32(sdS);
+      // dV(j) += P^T(j) dO(j), dK(j) += dS^T(j) Q(j), dQ^T(j) = K^T dS^T(j)
+      auto rest = [&](int j) -> bool {
+        const int stj = j % ST;
+        if (!mbar_wait(p_full, j & 1, err, 263)) return false;
+        tc_fence_after();
+        const uint32_t qa = smem_u32(sQD + 2 * stj * C::QTILE), doa = smem_u32(sQD + (2 * stj + 1) * C::QTILE);
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+          mma_ss(tdV, kmajor_desc(pa, ks), mnmajor_sw32_r64(doa, ks), idO, (j > 0 || ks > 0) ? 1u : 0u);
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+          mma_ss(tdK, kmajor_desc(dsa, ks), mnmajor_sw32_r64(qa, ks), idO, (j > 0 || ks > 0) ? 1u : 0u);
+        const int slot = j & 1;
+        if (j >= 2) {
+          if (!mbar_wait(&dq_free[slot], (uint32_t)(((j >> 1) - 1) & 1), err, 264)) return false;
+          tc_fence_after();
+        }
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks)
+          mma_ss(tdQ + slot * 64, mnmajor_sw32(ka, ks), mnmajor_desc(dsa, ks), idQT, ks > 0 ? 1u : 0u);
+        mma_commit(p_free);
+        mma_commit(&dq_full[slot]);
+        return true;
+      };
+      bool ok = mbar_wait(kv_full, 0, err, 260);
+      for (int i = 0; i < nq && ok; ++i) {
+        const int st = i % ST;
+        const uint32_t ph = (i / ST) & 1;
+        if (!mbar_wait(&qdo_full[st], ph, err, 261)) { ok = false; break; }
+        if (i > 0 && !mbar_wait(s_free, (i - 1) & 1, err, 262)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t qa = smem_u32(sQD + 2 * st * C::QTILE), doa = smem_u32(sQD + (2 * st + 1) * C::QTILE);
+#pragma unroll
+        for (int ks = 0; ks < NCH / 2; ++ks)
+          mma_ss(tS, kmajor_sw32(ka, ks), kmajor_sw32_r64(qa, ks), idS, ks > 0 ? 1u : 0u);
+#pragma unroll
+        for (int ks = 0; ks < NCH / 2; ++ks)
+          mma_ss(tdP, kmajor_sw32(va, ks), kmajor_sw32_r64(doa, ks), idS, ks > 0 ? 1u : 0u);
+        mma_commit(s_full);
+        if (i > 0) ok = rest(i - 1);
+      }
+      if (ok && nq > 0) ok = rest(nq - 1);
+      mma_commit(fin);
+      mbar_wait_drain(fin, 0);
+    }
+  } else if (wg == 1 || wg == 2) {
+    // ---------------- dS warps: thread = key row, 32 of the 64 query columns ----------------
+    const int quarter = warp & 3;
+    const int c = wg - 1;  // 32-query chunk
+    const int kr = quarter * 32 + lane;
+    const int key = k0 + kr;
+    const bool key_ok = key < a.Skv;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const float2 scl = make_float2(a.scale_log2, a.scale_log2);
+    const float2 kmask = make_float2(key_ok ? 1.f : 0.f, key_ok ? 1.f : 0.f);
+    const float2 nl2e = make_float2(-kLog2e, -kLog2e);
+    const int ldt = (wg - 1) * 128 + kr;  // 0..255; the first 128 load lse (64) | delta (64)
+    const float* ld_src =
+        ldt < 128 ? ((ldt < 64 ? a.lse : a.delta) + (long)(b * a.H + h) * a.lse_ld + (ldt & 63)) : nullptr;
+    bool ok = true;
+    // lse / delta of a tile's 64 queries (+inf / 0 past Sq) in the buffer of the
+    // tile's parity: tile 0's now, tile i+1's at the end of tile i; the barrier
+    // at the top of a tile makes them visible.  All eight dS warps run every
+    // iteration (no early exit) so the named barrier always sees 256 threads.
+    if (ld_src) sLD[ldt] = __ldg(ld_src);
+    for (int i = 0; i < nq; ++i) {
+      const float ld_next = (ld_src && i + 1 < nq) ? __ldg(ld_src + (i + 1) * 64) : 0.f;
+      const float* ldb = sLD + (i & 1) * 128;
+      asm volatile("bar.sync 2, 256;" ::: "memory");
+      if (!mbar_wait(s_full, i & 1, err, 270)) ok = false;
+      tc_fence_after();
+      uint32_t sv[32], dp[32];
+      tmem_ld32(tS + lane_off + c * 32, sv);
+      tmem_ld32(tdP + lane_off + c * 32, dp);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(s_free);  // the MMA warp may overwrite S / dP now
+      const float* sL = ldb;
+      const float* sDl = ldb + 64;
+      uint32_t pp[16], dd[16];
+#pragma unroll
+      for (int k4 = 0; k4 < 8; ++k4) {
+        const float4 L4 = *reinterpret_cast<const float4*>(sL + c * 32 + 4 * k4);  // smem broadcast
+        const float4 D4 = *reinterpret_cast<const float4*>(sDl + c * 32 + 4 * k4);
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2) {
+          const int k2 = 2 * k4 + h2;
+          const float2 Lp = h2 ? make_float2(L4.z, L4.w) : make_float2(L4.x, L4.y);
+          const float2 Dp = h2 ? make_float2(D4.z, D4.w) : make_float2(D4.x, D4.y);
+          const float2 x = __ffma2_rn(make_float2(__uint_as_float(sv[2 * k2]), __uint_as_float(sv[2 * k2 + 1])), scl,
+                                      __fmul2_rn(Lp, nl2e));
+          const float2 p = __fmul2_rn(make_float2(ex2_approx(x.x), ex2_approx(x.y)), kmask);
+          const float2 ds = __fmul2_rn(
+              p, __fadd2_rn(make_float2(__uint_as_float(dp[2 * k2]), __uint_as_float(dp[2 * k2 + 1])),
+                            make_float2(-Dp.x, -Dp.y)));
+          pp[k2] = pack_bf16x2(p.x, p.y);
+          dd[k2] = pack_bf16x2(ds.x, ds.y);
+        }
+      }
+      // the previous tile's dV/dK/dQ must be done reading P^T / dS
+      if (i > 0 && !mbar_wait(p_free, (i - 1) & 1, err, 271)) ok = false;
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        *reinterpret_cast<uint4*>(sP + (c * 4 + g) * 2048 + kr * 16) =
+            make_uint4(pp[4 * g], pp[4 * g + 1], pp[4 * g + 2], pp[4 * g + 3]);
+        *reinterpret_cast<uint4*>(sdS + (c * 4 + g) * 2048 + kr * 16) =
+            make_uint4(dd[4 * g], dd[4 * g + 1], dd[4 * g + 2], dd[4 * g + 3]);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+      if (ld_src) sLD[((i + 1) & 1) * 128 + ldt] = ld_next;
+    }
+    if (wg == 1) {  // dV is stored by warpgroup 1
+      if (ok) ok = mbar_wait(fin, 0, err, 272);
+      tc_fence_after();
+      bf16* vrow = a.dV + (long)(b * a.Skv + key) * a.lddv + h * a.Dh;
+#pragma unroll 1
+      for (int cc = 0; cc < C::DPAD; cc += 16) {
+        uint32_t v[16];
+        tmem_ld16(tdV + lane_off + cc, v);
+        tmem_wait_ld();
+        if (key_ok && ok) {
+#pragma unroll
+          for (int g = 0; g < 2; ++g) {
+            const int d = cc + 8 * g;
+            if (d < a.Dh) {
+              uint4 pk;
+              pk.x = pack_bf16x2(__uint_as_float(v[8 * g + 0]), __uint_as_float(v[8 * g + 1]));
+              pk.y = pack_bf16x2(__uint_as_float(v[8 * g + 2]), __uint_as_float(v[8 * g + 3]));
+              pk.z = pack_bf16x2(__uint_as_float(v[8 * g + 4]), __uint_as_float(v[8 * g + 5]));
+              pk.w = pack_bf16x2(__uint_as_float(v[8 * g + 6]), __uint_as_float(v[8 * g + 7]));
+              *reinterpret_cast<uint4*>(vrow + d) = pk;
+            }
+          }
+        }
+      }
+    }
+  } else if (wg == 3) {
+    // ---------------- dQ warps: thread = head-dim index of dQ^T ----------------
+    const int quarter = warp & 3;
+    const int dd = quarter * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    bool ok = true;
+    for (int i = 0; i < nq; ++i) {
+      const int slot = i & 1;
+      if (!mbar_wait(&dq_full[slot], (uint32_t)((i >> 1) & 1), err, 280)) { ok = false; break; }
+      tc_fence_after();
+      const int st = i % ST;
+      float* stage = reinterpret_cast<float*>(sQD + 2 * st * C::QTILE);  // [64 queries][Dh] fp32
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        uint32_t v[32];
+        tmem_ld32(tdQ + slot * 64 + lane_off + half * 32, v);
+        tmem_wait_ld();
+        if (dd < a.Dh) {
+#pragma unroll
+          for (int qq = 0; qq < 32; ++qq) stage[(half * 32 + qq) * a.Dh + dd] = __uint_as_float(v[qq]);
+        }
+      }
+      tc_fence_before();
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&dq_free[slot]);
+        mbar_arrive(dqs_bar);
+      }
+      if (warp == 12 && lane == 0) {
+        // when all four dQ warps staged their columns, reduce-add the [64 x Dh]
+        // tile into dq_acc (rows past Sq are clipped by TMA), then give the
+        // stage back to the TMA producer
+        if (!mbar_wait(dqs_bar, i & 1, err, 282)) { ok = false; break; }
+        if (!a.skip_dq) tma_reduce_add_4d(&tmdQ, stage, 0, h, i * 64, b);
+        bulk_wait_read_all();
+        mbar_arrive(&qdo_empty[st]);
+      }
+    }
+    if (warp == 12 && lane == 0) bulk_wait_all();
+    if (ok) ok = mbar_wait(fin, 0, err, 281);
+    tc_fence_after();
+    const int kr = quarter * 32 + lane;
+    const int key = k0 + kr;
+    bf16* krow = a.dK + (long)(b * a.Skv + key) * a.lddk + h * a.Dh;
+#pragma unroll 1
+    for (int cc = 0; cc < C::DPAD; cc += 16) {
+      uint32_t v[16];
+      tmem_ld16(tdK + lane_off + cc, v);
+      tmem_wait_ld();
+      if (key < a.Skv && ok) {
+#pragma unroll
+        for (int g = 0; g < 2; ++g) {
+          const int d = cc + 8 * g;
+          if (d < a.Dh) {
+            uint4 pk;
+            pk.x = pack_bf16x2(__uint_as_float(v[8 * g + 0]) * a.scale, __uint_as_float(v[8 * g + 1]) * a.scale);
+            pk.y = pack_bf16x2(__uint_as_float(v[8 * g + 2]) * a.scale, __uint_as_float(v[8 * g + 3]) * a.scale);
+            pk.z = pack_bf16x2(__uint_as_float(v[8 * g + 4]) * a.scale, __uint_as_float(v[8 * g + 5]) * a.scale);
+            pk.w = pack_bf16x2(__uint_as_float(v[8 * g + 6]) * a.scale, __uint_as_float(v[8 * g + 7]) * a.scale);
+            *reinterpret_cast<uint4*>(krow + d) = pk;
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
 // dQ = scale * dq_acc  (fp32 [B][H][Sq][Dh] -> bf16 [B*Sq, ld] token-major)
 __global__ void dq_finalize_kernel(const float* __restrict__ acc, int B, int Sq, int H, int Dh, float scale,
                                    bf16* __restrict__ out, long ldo) {
@@ -1289,6 +1650,31 @@ bool bwd_pipe_enabled() {
     return !(e && e[0] == '0');
   }();
   return on;
+}
+
+// HARP_ATTN_BWD_Q64=1 runs head dim 128 on the 64-query-tile pipelined
+// schedule, =0 on the single-tile one.
+bool bwd_q64_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("HARP_ATTN_BWD_Q64");
+    return e && e[0] == '1';
+  }();
+  return on;
+}
+
+// mq / mdo / mdq here are the 64-row maps
+void launch_bwd_q64(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mdo,
+                    const CUtensorMap& mdq, const BwdArgs& args, cudaStream_t stream) {
+  using C = BwdQ64Cfg<16>;
+  static bool configured = false;
+  if (!configured) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_q64_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    configured = true;
+  }
+  const int grid = args.B * args.H * ((args.Skv + 127) / 128);
+  attn_bwd_q64_kernel<16><<<grid, kBwdQ64Threads, C::SMEM, stream>>>(mq, mk, mv, mdo, mdq, args);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  count_launch();
 }
 
 template <int NCH>
@@ -1437,6 +1823,13 @@ void attn_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, con
   }();
   args.skip_dq = skip_dq ? 1 : 0;
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  if (nch == 16 && bwd_q64_enabled()) {
+    const CUtensorMap mq64 = make_sw32_map(q.data_ptr(), B, Sq, q.stride(0), H, Dh, 64);
+    const CUtensorMap mdo64 = make_sw32_map(dout.data_ptr(), B, Sq, dout.stride(0), H, Dh, 64);
+    const CUtensorMap mdq64 = make_f32_bhsd_map(dq_acc.data_ptr(), B, Sq, H, Dh, 64);
+    launch_bwd_q64(mq64, mk, mv, mdo64, mdq64, args, stream);
+    return;
+  }
   switch (nch) {
     case 8: launch_bwd<8>(mq, mk, mv, mdo, mdq, args, stream); break;
     case 10: launch_bwd<10>(mq, mk, mv, mdo, mdq, args, stream); break;
