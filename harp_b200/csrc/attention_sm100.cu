@@ -1258,12 +1258,15 @@ struct BwdQ64Cfg {
   static constexpr int QTILE = NCH * 1024;  // 64 queries x DPAD, atoms of 2 KB
   static constexpr int PS_BYTES = 128 * 64 * 2;  // P^T or dS: 128 keys x 64 queries bf16, 8-query strips
   static constexpr int LD_BYTES = 2 * 128 * 4;   // lse | delta of a 64-query tile, double-buffered
-  // 256 bytes of alignment slack, 256 for the barriers (at most 2 + 2 * 4 + 10) and the TMEM address
+  // 256 bytes of alignment slack, 256 for the barriers (at most 2 + 2 * 7 + 10) and the TMEM address
   static constexpr int smem_for(int st) { return 2 * KTILE + st * 2 * QTILE + 2 * PS_BYTES + LD_BYTES + 256 + 256; }
-  static constexpr int STAGES = smem_for(4) <= 232448 ? 4 : 3;
+  static constexpr int STAGES = smem_for(7) <= 232448 ? 7 : (smem_for(5) <= 232448 ? 5 : (smem_for(4) <= 232448 ? 4 : 3));
   static constexpr int SMEM = smem_for(STAGES);
   static_assert(SMEM <= 232448, "exceeds the 227 KB per-CTA shared memory limit");
-  static_assert(DPAD == 128, "dQ^T puts the head dim on the 128 TMEM lanes");
+  // dQ^T puts the head dim on the TMEM lanes with M = 128: for DPAD < 128 the
+  // MMA's A operand (K^T) runs on past the K tile into the V tile, and the
+  // extra lanes of dQ^T (head-dim index >= DPAD) are never read out
+  static_assert(DPAD <= 128, "head dim on at most 128 TMEM lanes");
   static_assert(2 * QTILE >= 64 * DPAD * 4, "dQ staging (64 x Dh fp32) must fit in one Q/dO stage");
   static constexpr int DV_COL = 128;
   static constexpr int DK_COL = 128 + DPAD;
@@ -1652,27 +1655,30 @@ bool bwd_pipe_enabled() {
   return on;
 }
 
-// Head dim 128 runs on the 64-query-tile pipelined schedule (1.4x the
-// single-tile one on B200); HARP_ATTN_BWD_Q64=0 keeps the single-tile one.
-bool bwd_q64_enabled() {
-  static const bool on = [] {
+// Which head dims take the 64-query-tile pipelined schedule.  Default: head
+// dim 128 (1.4x the single-tile schedule on B200).  HARP_ATTN_BWD_Q64=0: none;
+// =1: also head dims 64 / 72 / 80 (instead of the 128-query pipelined one).
+int bwd_q64_mode() {
+  static const int m = [] {
     const char* e = std::getenv("HARP_ATTN_BWD_Q64");
-    return !(e && e[0] == '0');
+    return (e && e[0] == '0') ? 0 : ((e && e[0] == '1') ? 2 : 1);
   }();
-  return on;
+  return m;
 }
 
 // mq / mdo / mdq here are the 64-row maps
+template <int NCH>
 void launch_bwd_q64(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mdo,
                     const CUtensorMap& mdq, const BwdArgs& args, cudaStream_t stream) {
-  using C = BwdQ64Cfg<16>;
+  using C = BwdQ64Cfg<NCH>;
   static bool configured = false;
   if (!configured) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_q64_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    C10_CUDA_CHECK(
+        cudaFuncSetAttribute(attn_bwd_q64_kernel<NCH>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     configured = true;
   }
   const int grid = args.B * args.H * ((args.Skv + 127) / 128);
-  attn_bwd_q64_kernel<16><<<grid, kBwdQ64Threads, C::SMEM, stream>>>(mq, mk, mv, mdo, mdq, args);
+  attn_bwd_q64_kernel<NCH><<<grid, kBwdQ64Threads, C::SMEM, stream>>>(mq, mk, mv, mdo, mdq, args);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   count_launch();
 }
@@ -1823,11 +1829,14 @@ void attn_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, con
   }();
   args.skip_dq = skip_dq ? 1 : 0;
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
-  if (nch == 16 && bwd_q64_enabled()) {
+  const int q64 = bwd_q64_mode();
+  if ((nch == 16 && q64 >= 1) || ((nch == 8 || nch == 10) && q64 == 2)) {
     const CUtensorMap mq64 = make_sw32_map(q.data_ptr(), B, Sq, q.stride(0), H, Dh, 64);
     const CUtensorMap mdo64 = make_sw32_map(dout.data_ptr(), B, Sq, dout.stride(0), H, Dh, 64);
     const CUtensorMap mdq64 = make_f32_bhsd_map(dq_acc.data_ptr(), B, Sq, H, Dh, 64);
-    launch_bwd_q64(mq64, mk, mv, mdo64, mdq64, args, stream);
+    if (nch == 8) launch_bwd_q64<8>(mq64, mk, mv, mdo64, mdq64, args, stream);
+    else if (nch == 10) launch_bwd_q64<10>(mq64, mk, mv, mdo64, mdq64, args, stream);
+    else launch_bwd_q64<16>(mq64, mk, mv, mdo64, mdq64, args, stream);
     return;
   }
   switch (nch) {
