@@ -30,6 +30,8 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/library.h>
 
+#include <string>
+
 namespace harp {
 namespace {
 
@@ -1655,13 +1657,16 @@ bool bwd_pipe_enabled() {
   return on;
 }
 
-// Which head dims take the 64-query-tile pipelined schedule.  Default: head
-// dim 128 (1.4x the single-tile schedule on B200).  HARP_ATTN_BWD_Q64=0: none;
-// =1: also head dims 64 / 72 / 80 (instead of the 128-query pipelined one).
+// Which head dims take the 64-query-tile pipelined schedule.  Default: 64 / 72
+// / 80 and 128 (measured on B200 at 4x4352 tokens: head dim 72 1.72 ms against
+// 1.83 ms for the 128-query pipelined schedule; head dim 128 1.4x the
+// single-tile schedule).  HARP_ATTN_BWD_Q64=0: none; =128: head dim 128 only.
 int bwd_q64_mode() {
   static const int m = [] {
     const char* e = std::getenv("HARP_ATTN_BWD_Q64");
-    return (e && e[0] == '0') ? 0 : ((e && e[0] == '1') ? 2 : 1);
+    if (e && std::string(e) == "0") return 0;
+    if (e && std::string(e) == "128") return 1;
+    return 2;
   }();
   return m;
 }
