@@ -188,6 +188,126 @@ struct FwdCfg {
 // quarter (key columns 0-63 / 64-127 of each score tile)
 constexpr int kFwdThreads = 576;
 
+// Shared memory and barriers of one forward CTA.
+struct FwdSmem {
+  uint8_t *sQ, *sK, *sV;
+  uint64_t *q_full, *k_full, *k_empty, *v_full, *v_empty, *s_full, *p_full, *o_final;
+};
+
+// TMA producer of the forward (one thread): both query tiles once, then the
+// key/value tiles through the stage ring, in key-tile order starting at
+// start_tile; with readiness flags it first waits (bounded) for the chunks a
+// tile touches.
+template <int NCH>
+__device__ __forceinline__ void fwd_load_role(const CUtensorMap* tmQ, const CUtensorMap* tmK, const CUtensorMap* tmV,
+                                              const FwdArgs& a, const FwdSmem& m, int q0, int ntile, int nkv, int h,
+                                              int b) {
+  using C = FwdCfg<NCH>;
+  constexpr int ST = C::STAGES;
+  int* err = a.err;
+  tma_prefetch_desc(tmQ);
+  tma_prefetch_desc(tmK);
+  tma_prefetch_desc(tmV);
+  int issued_k[4] = {0, 0, 0, 0}, issued_v[4] = {0, 0, 0, 0};
+  bool ok = true;
+  if (a.ready != nullptr && a.wait_q) {
+    const int qend = min(q0 + 128 * ntile, a.Sq) - 1;
+    for (int c = q0 / a.chunk_len; c <= qend / a.chunk_len && ok; ++c)
+      ok = wait_flag_geq(a.ready + c, a.epoch, a.timeout_ns, err, 19);
+    fence_proxy_async_global();
+  }
+  mbar_arrive_expect_tx(m.q_full, ntile * C::TILE);
+  for (int t = 0; t < ntile; ++t) load_sw32_tile<NCH>(m.sQ + t * C::TILE, tmQ, m.q_full, q0 + 128 * t, h, b);
+  for (int jj = 0; jj < nkv && ok; ++jj) {
+    const int j = (a.start_tile + jj) % nkv;
+    const int key0 = j * 128;
+    if (a.ready != nullptr) {
+      const int kend = min(key0 + 128, a.Skv) - 1;
+      for (int c = key0 / a.chunk_len; c <= kend / a.chunk_len && ok; ++c)
+        ok = wait_flag_geq(a.ready + c, a.epoch, a.timeout_ns, err, 20);
+      if (!ok) break;
+      fence_proxy_async_global();
+    }
+    const int st = jj % ST;
+    const uint32_t ph = (jj / ST) & 1;
+    if (!mbar_wait(&m.k_empty[st], ph ^ 1, err, 21)) { ok = false; break; }
+    mbar_arrive_expect_tx(&m.k_full[st], C::TILE);
+    load_sw32_tile<NCH>(m.sK + st * C::TILE, tmK, &m.k_full[st], key0, h, b);
+    issued_k[st]++;
+    if (!mbar_wait(&m.v_empty[st], ph ^ 1, err, 22)) { ok = false; break; }
+    mbar_arrive_expect_tx(&m.v_full[st], C::TILE);
+    load_sw32_tile<NCH>(m.sV + st * C::TILE, tmV, &m.v_full[st], key0, h, b);
+    issued_v[st]++;
+  }
+  mbar_wait_drain(m.q_full, 0);
+  for (int s = 0; s < ST; ++s) {
+    if (issued_k[s]) mbar_wait_drain(&m.k_full[s], (issued_k[s] - 1) & 1);
+    if (issued_v[s]) mbar_wait_drain(&m.v_full[s], (issued_v[s] - 1) & 1);
+  }
+}
+
+// MMA issuer of the forward (one thread).  Per key step and query tile t:
+// O_t += P_t V (P from TMEM), then S_t = Q_t K^T of the next key tile into the
+// columns P_t occupied.  ROWP: P_t packed into columns [0, 64) of its S tile
+// (one softmax thread per row); else at pcol() (two warps per row).
+template <int NCH, bool ROWP>
+__device__ __forceinline__ void fwd_mma_role(const FwdArgs& a, const FwdSmem& m, uint32_t tmem, int ntile, int nkv) {
+  using C = FwdCfg<NCH>;
+  constexpr int ST = C::STAGES;
+  int* err = a.err;
+  auto pa_col = [](int ks) -> uint32_t { return ROWP ? (uint32_t)ks * 8 : pcol(ks / 2) + (ks & 1) * 8; };
+  constexpr uint32_t idS = make_idesc_bf16(128, 128, false, false);
+  constexpr uint32_t idO = make_idesc_bf16(128, C::DPAD, false, true);
+  auto issue_S = [&](int t, int st) {
+    const uint32_t qa = smem_u32(m.sQ + t * C::TILE), ka = smem_u32(m.sK + st * C::TILE);
+#pragma unroll
+    for (int ks = 0; ks < NCH / 2; ++ks)
+      mma_ss(tmem + t * 128, kmajor_sw32(qa, ks), kmajor_sw32(ka, ks), idS, ks > 0 ? 1u : 0u);
+  };
+  bool ok = mbar_wait(m.q_full, 0, err, 30);
+  if (ok) ok = mbar_wait(&m.k_full[0], 0, err, 31);
+  if (ok) {
+    tc_fence_after();
+    for (int t = 0; t < ntile; ++t) {
+      issue_S(t, 0);
+      mma_commit(&m.s_full[t]);
+    }
+    mma_commit(&m.k_empty[0]);
+  }
+  for (int jj = 0; jj < nkv && ok; ++jj) {
+    const int st = jj % ST;
+    const uint32_t ph = (jj / ST) & 1;
+    if (!mbar_wait(&m.v_full[st], ph, err, 32)) { ok = false; break; }
+    const bool has_next = jj + 1 < nkv;
+    const int st2 = (jj + 1) % ST;
+    const uint32_t ph2 = ((jj + 1) / ST) & 1;
+    const uint32_t va = smem_u32(m.sV + st * C::TILE);
+    for (int t = 0; t < ntile; ++t) {
+      if (!mbar_wait(&m.p_full[t], jj & 1, err, 33)) { ok = false; break; }
+      FWD_PROBE(jj, t);
+      tc_fence_after();
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks)
+        mma_ts(tmem + 256 + t * 128, tmem + t * 128 + pa_col(ks), mnmajor_sw32(va, ks), idO,
+               (jj > 0 || ks > 0) ? 1u : 0u);
+      if (has_next) {
+        if (t == 0) {
+          if (!mbar_wait(&m.k_full[st2], ph2, err, 34)) { ok = false; break; }
+          tc_fence_after();
+        }
+        issue_S(t, st2);
+        mma_commit(&m.s_full[t]);
+        FWD_PROBE(jj, 2 + t);
+      }
+    }
+    if (!ok) break;
+    if (has_next) mma_commit(&m.k_empty[st2]);
+    mma_commit(&m.v_empty[st]);
+  }
+  mma_commit(m.o_final);
+  mbar_wait_drain(m.o_final, 0);
+}
+
 template <int NCH, int NPOLY>
 __global__ void __launch_bounds__(kFwdThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -210,6 +330,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   uint64_t* o_final = p_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_final + 1);
   float* xch = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 256);  // [2][2][2][128] max | [2][2][128] sum
+  const FwdSmem sm{sQ, sK, sV, q_full, k_full, k_empty, v_full, v_empty, s_full, p_full, o_final};
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int nqp = (a.Sq + 255) / 256;
@@ -250,100 +371,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    if (lane == 0) {
-      tma_prefetch_desc(&tmQ);
-      tma_prefetch_desc(&tmK);
-      tma_prefetch_desc(&tmV);
-      int issued_k[4] = {0, 0, 0, 0}, issued_v[4] = {0, 0, 0, 0};
-      bool ok = true;
-      if (a.ready != nullptr && a.wait_q) {
-        const int qend = min(q0 + 128 * ntile, a.Sq) - 1;
-        for (int c = q0 / a.chunk_len; c <= qend / a.chunk_len && ok; ++c)
-          ok = wait_flag_geq(a.ready + c, a.epoch, a.timeout_ns, err, 19);
-        fence_proxy_async_global();
-      }
-      mbar_arrive_expect_tx(q_full, ntile * C::TILE);
-      for (int t = 0; t < ntile; ++t) load_sw32_tile<NCH>(sQ + t * C::TILE, &tmQ, q_full, q0 + 128 * t, h, b);
-      for (int jj = 0; jj < nkv && ok; ++jj) {
-        const int j = (a.start_tile + jj) % nkv;
-        const int key0 = j * 128;
-        if (a.ready != nullptr) {
-          const int kend = min(key0 + 128, a.Skv) - 1;
-          for (int c = key0 / a.chunk_len; c <= kend / a.chunk_len && ok; ++c)
-            ok = wait_flag_geq(a.ready + c, a.epoch, a.timeout_ns, err, 20);
-          if (!ok) break;
-          fence_proxy_async_global();
-        }
-        const int st = jj % ST;
-        const uint32_t ph = (jj / ST) & 1;
-        if (!mbar_wait(&k_empty[st], ph ^ 1, err, 21)) { ok = false; break; }
-        mbar_arrive_expect_tx(&k_full[st], C::TILE);
-        load_sw32_tile<NCH>(sK + st * C::TILE, &tmK, &k_full[st], key0, h, b);
-        issued_k[st]++;
-        if (!mbar_wait(&v_empty[st], ph ^ 1, err, 22)) { ok = false; break; }
-        mbar_arrive_expect_tx(&v_full[st], C::TILE);
-        load_sw32_tile<NCH>(sV + st * C::TILE, &tmV, &v_full[st], key0, h, b);
-        issued_v[st]++;
-      }
-      mbar_wait_drain(q_full, 0);
-      for (int s = 0; s < ST; ++s) {
-        if (issued_k[s]) mbar_wait_drain(&k_full[s], (issued_k[s] - 1) & 1);
-        if (issued_v[s]) mbar_wait_drain(&v_full[s], (issued_v[s] - 1) & 1);
-      }
-    }
+    if (lane == 0) fwd_load_role<NCH>(&tmQ, &tmK, &tmV, a, sm, q0, ntile, nkv, h, b);
   } else if (warp == 1) {
-    if (lane == 0) {
-      constexpr uint32_t idS = make_idesc_bf16(128, 128, false, false);
-      constexpr uint32_t idO = make_idesc_bf16(128, C::DPAD, false, true);
-      auto issue_S = [&](int t, int st) {
-        const uint32_t qa = smem_u32(sQ + t * C::TILE), ka = smem_u32(sK + st * C::TILE);
-#pragma unroll
-        for (int ks = 0; ks < NCH / 2; ++ks)
-          mma_ss(tmem + t * 128, kmajor_sw32(qa, ks), kmajor_sw32(ka, ks), idS, ks > 0 ? 1u : 0u);
-      };
-      bool ok = mbar_wait(q_full, 0, err, 30);
-      if (ok) ok = mbar_wait(&k_full[0], 0, err, 31);
-      if (ok) {
-        tc_fence_after();
-        for (int t = 0; t < ntile; ++t) {
-          issue_S(t, 0);
-          mma_commit(&s_full[t]);
-        }
-        mma_commit(&k_empty[0]);
-      }
-      for (int jj = 0; jj < nkv && ok; ++jj) {
-        const int st = jj % ST;
-        const uint32_t ph = (jj / ST) & 1;
-        if (!mbar_wait(&v_full[st], ph, err, 32)) { ok = false; break; }
-        const bool has_next = jj + 1 < nkv;
-        const int st2 = (jj + 1) % ST;
-        const uint32_t ph2 = ((jj + 1) / ST) & 1;
-        const uint32_t va = smem_u32(sV + st * C::TILE);
-        for (int t = 0; t < ntile; ++t) {
-          if (!mbar_wait(&p_full[t], jj & 1, err, 33)) { ok = false; break; }
-          FWD_PROBE(jj, t);
-          tc_fence_after();
-#pragma unroll
-          for (int ks = 0; ks < 8; ++ks)
-            mma_ts(tmem + 256 + t * 128, tmem + t * 128 + pcol(ks / 2) + (ks & 1) * 8, mnmajor_sw32(va, ks), idO,
-                   (jj > 0 || ks > 0) ? 1u : 0u);
-          if (has_next) {
-            if (t == 0) {
-              if (!mbar_wait(&k_full[st2], ph2, err, 34)) { ok = false; break; }
-              tc_fence_after();
-            }
-            issue_S(t, st2);
-            mma_commit(&s_full[t]);
-            FWD_PROBE(jj, 2 + t);
-          }
-        }
-        if (!ok) break;
-        if (has_next) mma_commit(&k_empty[st2]);
-        mma_commit(&v_empty[st]);
-      }
-      mma_commit(o_final);
-      mbar_wait_drain(o_final, 0);
-    }
+    if (lane == 0) fwd_mma_role<NCH, false>(a, sm, tmem, ntile, nkv);
   } else {
     // softmax warps: t = query tile, hf = half of the 128 key columns
     const int sw = warp - 2;
@@ -478,6 +508,214 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         }
       }
       if (hf == 0 && s < a.Sq && ok) a.lse[(long)(b * a.H + h) * a.lse_ld + s] = (m + log2f(l)) * kLn2;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// Forward with one softmax thread per query row.  384 threads: WG0 = w0 TMA,
+// w1 MMA (w2-3 idle); WG1 (w4-7) and WG2 (w8-11) own query tiles 0 and 1, warp
+// w reading TMEM lanes 32*(w%4).. of its tile.  A thread loads its row's 128
+// scores with four tcgen05.ld and one wait, takes the row max in registers
+// (no exchange between warps), writes P packed to columns [0, 64) of the
+// same score tile and keeps its row sum; the rare O rescale (when the running
+// max grows by more than 2^8) is done by the same thread on its own row.
+// Registers move from WG0 to the softmax warpgroups with setmaxnreg:
+// 56 + 2 x 224 = 3 x 168, the launch's per-thread budget for 384 threads.
+constexpr int kFwdRowThreads = 384;
+constexpr int kFwdRowRegsCtl = 56, kFwdRowRegsSm = 224, kFwdRowRegsLaunch = 168;
+static_assert(kFwdRowRegsCtl + 2 * kFwdRowRegsSm == 3 * kFwdRowRegsLaunch,
+              "warpgroup register split must add up to the launch budget");
+static_assert(kFwdRowRegsLaunch * kFwdRowThreads <= 65536, "launch budget fits the register file");
+
+template <int NCH>
+__global__ void __launch_bounds__(kFwdRowThreads, 1)
+    attn_fwd_row_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                        const __grid_constant__ CUtensorMap tmV, const FwdArgs a) {
+  using C = FwdCfg<NCH>;
+  constexpr int ST = C::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 255) & ~uintptr_t(255));
+  uint8_t* sQ = smem;
+  uint8_t* sK = sQ + 2 * C::TILE;
+  uint8_t* sV = sK + ST * C::TILE;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + ST * C::TILE);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;
+  uint64_t* k_empty = k_full + ST;
+  uint64_t* v_full = k_empty + ST;
+  uint64_t* v_empty = v_full + ST;
+  uint64_t* s_full = v_empty + ST;  // [2]
+  uint64_t* p_full = s_full + 2;    // [2]
+  uint64_t* o_final = p_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_final + 1);
+  static_assert((1 + 4 * ST + 5) * 8 + 4 <= 256, "barrier region");
+  const FwdSmem sm{sQ, sK, sV, q_full, k_full, k_empty, v_full, v_empty, s_full, p_full, o_final};
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int nqp = (a.Sq + 255) / 256;
+  const int nbh = a.B * a.H;
+  const int bh = a.wait_q ? (int)(blockIdx.x % nbh) : (int)(blockIdx.x / nqp);
+  const int qp = a.wait_q ? (int)((blockIdx.x / nbh + a.q_rot) % nqp) : (int)(blockIdx.x % nqp);
+  const int b = bh / a.H, h = bh % a.H;
+  const int q0 = qp * 256;
+  const int ntile = (q0 + 128 < a.Sq) ? 2 : 1;
+  const int nkv = (a.Skv + 127) / 128;
+  int* err = a.err;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&p_full[t], 4);
+    }
+    mbar_init(o_final, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int wg = warp / 4;
+
+  // each role's code sits inside the branch that sets its register budget
+  if (wg == 0) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kFwdRowRegsCtl));
+    if (warp == 0) {
+      if (lane == 0) fwd_load_role<NCH>(&tmQ, &tmK, &tmV, a, sm, q0, ntile, nkv, h, b);
+    } else if (warp == 1) {
+      if (lane == 0) fwd_mma_role<NCH, true>(a, sm, tmem, ntile, nkv);
+    }
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kFwdRowRegsSm));
+    const int t = wg - 1;
+    const int quarter = warp & 3;
+    if (t < ntile) {
+      const int rloc = quarter * 32 + lane;
+      const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+      const uint32_t tS = tmem + lane_off + t * 128;
+      const uint32_t tO = tmem + lane_off + 256 + t * 128;
+      constexpr int OCH = C::DPAD / 16;
+      float m = -INFINITY, l = 0.f;
+      bool ok = true;
+      for (int jj = 0; jj < nkv; ++jj) {
+        const int j = (a.start_tile + jj) % nkv;
+        const int nvalid = min(128, a.Skv - j * 128);
+        // no early exit: after an error the bounded waits return at once
+        if (!mbar_wait(&s_full[t], jj & 1, err, 40)) ok = false;
+        if (quarter == 0 && lane == 0) FWD_PROBE(jj, 4 + 3 * t);
+        tc_fence_after();
+        uint32_t v[4][32];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, v[c]);
+        tmem_wait_ld();
+        const bool full_tile = (nvalid == 128);  // only the last key tile of a sequence is partial
+        if (!full_tile) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (c * 32 + i >= nvalid) v[c][i] = __float_as_uint(-INFINITY);
+        }
+        float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int i = 0; i < 32; i += 4) {
+            mx0 = fmaxf(mx0, __uint_as_float(v[c][i]));
+            mx1 = fmaxf(mx1, __uint_as_float(v[c][i + 1]));
+            mx2 = fmaxf(mx2, __uint_as_float(v[c][i + 2]));
+            mx3 = fmaxf(mx3, __uint_as_float(v[c][i + 3]));
+          }
+        const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
+        if (quarter == 0 && lane == 0) FWD_PROBE(jj, 5 + 3 * t);
+        const float m_new = fmaxf(m, mx * a.scale_log2);
+        const bool need = m_new > m + kRescaleThreshold;
+        if (__any_sync(0xffffffffu, need)) {
+          if (jj > 0) {
+            const float alpha = ex2_approx(m - m_new);
+            l *= alpha;
+#pragma unroll
+            for (int oc = 0; oc < OCH; ++oc) {
+              uint32_t o[16];
+              tmem_ld16(tO + oc * 16, o);
+              tmem_wait_ld();
+#pragma unroll
+              for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+              tmem_st16(tO + oc * 16, o);
+            }
+          }
+          m = m_new;
+        }
+        // p = 2^(s*scale*log2e - m): one packed FMA per pair, ex2, packed sum;
+        // chunk c's 32 probabilities pack into columns [16c, 16c + 16)
+        const float2 scl = make_float2(a.scale_log2, a.scale_log2);
+        const float2 negm = make_float2(-m, -m);
+        float2 lacc0 = make_float2(0.f, 0.f), lacc1 = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float2 x =
+                __ffma2_rn(make_float2(__uint_as_float(v[c][2 * i]), __uint_as_float(v[c][2 * i + 1])), scl, negm);
+            const float2 p = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+            if (i & 1) lacc1 = __fadd2_rn(lacc1, p);
+            else lacc0 = __fadd2_rn(lacc0, p);
+            pk[i] = pack_bf16x2(p.x, p.y);
+          }
+          tmem_st16(tS + c * 16, pk);
+        }
+        l += (lacc0.x + lacc0.y) + (lacc1.x + lacc1.y);
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[t]);
+        if (quarter == 0 && lane == 0) FWD_PROBE(jj, 6 + 3 * t);
+      }
+      if (ok) ok = mbar_wait(o_final, 0, err, 41);
+      tc_fence_after();
+      const int s = q0 + t * 128 + rloc;
+      const float inv_l = (l > 0.f) ? 1.f / l : 0.f;
+      bf16* orow = a.O + (long)(b * a.Sq + s) * a.ldo + h * a.Dh;
+#pragma unroll
+      for (int oc = 0; oc < OCH; ++oc) {
+        const int c = oc * 16;
+        uint32_t o[16];
+        tmem_ld16(tO + c, o);
+        tmem_wait_ld();
+        if (s < a.Sq && ok) {
+#pragma unroll
+          for (int g = 0; g < 2; ++g) {
+            const int d = c + 8 * g;
+            if (d < a.Dh) {
+              uint4 pk;
+              pk.x = pack_bf16x2(__uint_as_float(o[8 * g + 0]) * inv_l, __uint_as_float(o[8 * g + 1]) * inv_l);
+              pk.y = pack_bf16x2(__uint_as_float(o[8 * g + 2]) * inv_l, __uint_as_float(o[8 * g + 3]) * inv_l);
+              pk.z = pack_bf16x2(__uint_as_float(o[8 * g + 4]) * inv_l, __uint_as_float(o[8 * g + 5]) * inv_l);
+              pk.w = pack_bf16x2(__uint_as_float(o[8 * g + 6]) * inv_l, __uint_as_float(o[8 * g + 7]) * inv_l);
+              *reinterpret_cast<uint4*>(orow + d) = pk;
+            }
+          }
+        }
+      }
+      if (s < a.Sq && ok) a.lse[(long)(b * a.H + h) * a.lse_ld + s] = (m + log2f(l)) * kLn2;
     }
   }
 
@@ -1627,10 +1865,42 @@ int nch_for(int Dh) {
   return 16;
 }
 
+// Which forward schedule runs: one softmax thread per query row (default) or
+// two warps per row with a shared-memory max exchange (HARP_ATTN_FWD=split,
+// and whenever the FMA-pipe exponential is asked for).
+bool fwd_row_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("HARP_ATTN_FWD");
+    return !(e && std::string(e) == "split");
+  }();
+  return on;
+}
+
 template <int NCH>
 void launch_fwd(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const FwdArgs& args,
                 cudaStream_t stream) {
   using C = FwdCfg<NCH>;
+  // The setmaxnreg split assumes the row kernel launches with exactly
+  // kFwdRowRegsLaunch registers per thread; a build with any other count
+  // keeps the two-warps-per-row schedule.
+  static const bool row_ok = [] {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_row_kernel<NCH>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    cudaFuncAttributes fa;
+    C10_CUDA_CHECK(cudaFuncGetAttributes(&fa, attn_fwd_row_kernel<NCH>));
+    const bool ok = fa.numRegs == kFwdRowRegsLaunch;
+    if (!ok)
+      TORCH_WARN_ONCE("harp attention: row forward built with ", fa.numRegs,
+                      " registers per thread; using the two-warps-per-row schedule");
+    return ok;
+  }();
+  const int nqp = (args.Sq + 255) / 256;
+  const int grid = args.B * args.H * nqp;
+  if (row_ok && fwd_row_enabled() && args.npoly == 0) {
+    attn_fwd_row_kernel<NCH><<<grid, kFwdRowThreads, C::SMEM, stream>>>(mq, mk, mv, args);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    count_launch();
+    return;
+  }
   auto* kern = args.npoly >= 8 ? attn_fwd_kernel<NCH, 8> : (args.npoly >= 4 ? attn_fwd_kernel<NCH, 4>
                                                                             : attn_fwd_kernel<NCH, 0>);
   static bool configured = false;
@@ -1640,8 +1910,6 @@ void launch_fwd(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap&
     C10_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_kernel<NCH, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     configured = true;
   }
-  const int nqp = (args.Sq + 255) / 256;
-  const int grid = args.B * args.H * nqp;
   kern<<<grid, kFwdThreads, C::SMEM, stream>>>(mq, mk, mv, args);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   count_launch();
