@@ -154,7 +154,7 @@ __device__ __forceinline__ constexpr uint32_t pcol(int c) { return c * 16 + (c >
 __device__ unsigned long long g_bwd_probe[64 * 16];
 #define FWD_PROBE(i, slot)                                                                              \
   do {                                                                                                  \
-    if (a.probe && blockIdx.x == 0 && (i) < 64) g_bwd_probe[(i) * 16 + (slot)] = globaltimer_ns();    \
+    if (a.probe && blockIdx.x == 0 && (i) < 64) g_bwd_probe[(i) * 16 + (slot)] = clock64();           \
   } while (0)
 
 struct FwdArgs {
@@ -534,7 +534,7 @@ static_assert(kFwdRowRegsCtl + 2 * kFwdRowRegsSm == 3 * kFwdRowRegsLaunch,
               "warpgroup register split must add up to the launch budget");
 static_assert(kFwdRowRegsLaunch * kFwdRowThreads <= 65536, "launch budget fits the register file");
 
-template <int NCH>
+template <int NCH, int NPOLY>
 __global__ void __launch_bounds__(kFwdRowThreads, 1)
     attn_fwd_row_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV, const FwdArgs a) {
@@ -625,6 +625,7 @@ __global__ void __launch_bounds__(kFwdRowThreads, 1)
 #pragma unroll
         for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, v[c]);
         tmem_wait_ld();
+        if (quarter == 0 && lane == 0) FWD_PROBE(jj, 10 + t);
         const bool full_tile = (nvalid == 128);  // only the last key tile of a sequence is partial
         if (!full_tile) {
 #pragma unroll
@@ -675,7 +676,8 @@ __global__ void __launch_bounds__(kFwdRowThreads, 1)
           for (int i = 0; i < 16; ++i) {
             const float2 x =
                 __ffma2_rn(make_float2(__uint_as_float(v[c][2 * i]), __uint_as_float(v[c][2 * i + 1])), scl, negm);
-            const float2 p = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+            // NPOLY of the 16 pairs, spread over the chunk, on the FMA pipe
+            const float2 p = ((i * NPOLY) % 16 < NPOLY) ? ex2_poly2(x) : make_float2(ex2_approx(x.x), ex2_approx(x.y));
             if (i & 1) lacc1 = __fadd2_rn(lacc1, p);
             else lacc0 = __fadd2_rn(lacc0, p);
             pk[i] = pack_bf16x2(p.x, p.y);
@@ -683,6 +685,7 @@ __global__ void __launch_bounds__(kFwdRowThreads, 1)
           tmem_st16(tS + c * 16, pk);
         }
         l += (lacc0.x + lacc0.y) + (lacc1.x + lacc1.y);
+        if (quarter == 0 && lane == 0) FWD_PROBE(jj, 12 + t);
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
@@ -751,11 +754,11 @@ struct BwdArgs {
 };
 
 // Phase timeline of CTA 0 of the backward kernels: 64 query tiles x 16 slots
-// of %globaltimer values, read back with attn_bwd_probe() (the forward kernel
+// of SM clock64 values, read back with attn_bwd_probe() (the forward kernel
 // records its key-tile steps into the same buffer).
 #define BWD_PROBE(i, slot)                                                                              \
   do {                                                                                                  \
-    if (a.probe && blockIdx.x == 0 && (i) < 64) g_bwd_probe[(i) * 16 + (slot)] = globaltimer_ns();    \
+    if (a.probe && blockIdx.x == 0 && (i) < 64) g_bwd_probe[(i) * 16 + (slot)] = clock64();           \
   } while (0)
 
 template <int NCH>
@@ -1866,8 +1869,7 @@ int nch_for(int Dh) {
 }
 
 // Which forward schedule runs: one softmax thread per query row (default) or
-// two warps per row with a shared-memory max exchange (HARP_ATTN_FWD=split,
-// and whenever the FMA-pipe exponential is asked for).
+// two warps per row with a shared-memory max exchange (HARP_ATTN_FWD=split).
 bool fwd_row_enabled() {
   static const bool on = [] {
     const char* e = std::getenv("HARP_ATTN_FWD");
@@ -1884,19 +1886,24 @@ void launch_fwd(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap&
   // kFwdRowRegsLaunch registers per thread; a build with any other count
   // keeps the two-warps-per-row schedule.
   static const bool row_ok = [] {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_row_kernel<NCH>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
-    cudaFuncAttributes fa;
-    C10_CUDA_CHECK(cudaFuncGetAttributes(&fa, attn_fwd_row_kernel<NCH>));
-    const bool ok = fa.numRegs == kFwdRowRegsLaunch;
+    bool ok = true;
+    for (auto* k : {attn_fwd_row_kernel<NCH, 0>, attn_fwd_row_kernel<NCH, 2>, attn_fwd_row_kernel<NCH, 4>}) {
+      C10_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+      cudaFuncAttributes fa;
+      C10_CUDA_CHECK(cudaFuncGetAttributes(&fa, k));
+      ok = ok && fa.numRegs == kFwdRowRegsLaunch;
+    }
     if (!ok)
-      TORCH_WARN_ONCE("harp attention: row forward built with ", fa.numRegs,
+      TORCH_WARN_ONCE("harp attention: row forward not built with ", kFwdRowRegsLaunch,
                       " registers per thread; using the two-warps-per-row schedule");
     return ok;
   }();
   const int nqp = (args.Sq + 255) / 256;
   const int grid = args.B * args.H * nqp;
-  if (row_ok && fwd_row_enabled() && args.npoly == 0) {
-    attn_fwd_row_kernel<NCH><<<grid, kFwdRowThreads, C::SMEM, stream>>>(mq, mk, mv, args);
+  if (row_ok && fwd_row_enabled()) {
+    auto* rk = args.npoly >= 4 ? attn_fwd_row_kernel<NCH, 4>
+                               : (args.npoly >= 2 ? attn_fwd_row_kernel<NCH, 2> : attn_fwd_row_kernel<NCH, 0>);
+    rk<<<grid, kFwdRowThreads, C::SMEM, stream>>>(mq, mk, mv, args);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
     count_launch();
     return;
@@ -2121,7 +2128,8 @@ void attn_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, con
 }
 
 // Timeline of CTA 0 of the last backward launch with HARP_ATTN_PROBE=1: int64
-// [64 tiles, 16 slots] of %globaltimer nanoseconds (0 = slot not reached).
+// [64 tiles, 16 slots] of SM clock64 cycles (0 = slot not reached; all slots
+// of one launch come from the one SM that ran CTA 0).
 at::Tensor attn_bwd_probe() {
   auto out = at::zeros({64, 16}, at::TensorOptions().dtype(at::kLong));
   C10_CUDA_CHECK(cudaMemcpyFromSymbol(out.data_ptr(), g_bwd_probe, sizeof(unsigned long long) * 64 * 16));
