@@ -1932,16 +1932,18 @@ bool bwd_pipe_enabled() {
   return on;
 }
 
-// Which head dims take the 64-query-tile pipelined schedule.  Default: 64 / 72
-// / 80 and 128 (measured on B200 at 4x4352 tokens: head dim 72 1.72 ms against
-// 1.83 ms for the 128-query pipelined schedule; head dim 128 1.4x the
-// single-tile schedule).  HARP_ATTN_BWD_Q64=0: none; =128: head dim 128 only.
+// Which head dims take the 64-query-tile pipelined schedule.  Default: head
+// dim 128 only (1.4x the single-tile schedule on B200).  Head dims 64-80 keep
+// the 128-query pipelined schedule: alone the 64-query kernel timed 1.72 ms
+// against 1.83 ms at head dim 72, but a whole DiT-XL/2 training step on the
+// same B200 took 157.3-158.2 ms with it and 153.8 ms without.
+// HARP_ATTN_BWD_Q64=0: none; =all: head dims 64-80 as well.
 int bwd_q64_mode() {
   static const int m = [] {
     const char* e = std::getenv("HARP_ATTN_BWD_Q64");
     if (e && std::string(e) == "0") return 0;
-    if (e && std::string(e) == "128") return 1;
-    return 2;
+    if (e && std::string(e) == "all") return 2;
+    return 1;
   }();
   return m;
 }

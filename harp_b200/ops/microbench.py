@@ -197,6 +197,28 @@ def build_cases(gemm_rows: int, adamw_n: int) -> Dict[str, Callable]:
     }
 
 
+def fwd_timeline(fn) -> Dict[str, float]:
+    """Median phase durations (SM cycles) of CTA 0 of one forward launch, from
+    the probe slots the forward kernels record per key step: 0/1 the MMA warp
+    sees P of query tile 0/1, 4/7 the softmax warps of tile 0/1 see S, 10/11
+    their TMEM loads landed, 12/13 exponentials done, 6/9 P handed over."""
+    torch.cuda.synchronize()
+    torch.ops.harp.attn_bwd_probe()  # clears the slots
+    fn()
+    torch.cuda.synchronize()
+    t = torch.ops.harp.attn_bwd_probe().double()
+    steps = int((t[:, 4] > 0).sum().item())
+    d = t[2:max(3, steps - 1)]  # steady state: skip the first two and the last key steps
+
+    def med(a, b):
+        return round((d[:, b] - d[:, a]).median().item(), 1)
+
+    return {"key_steps": steps, "period": round((t[3:steps, 4] - t[2:steps - 1, 4]).median().item(), 1),
+            "s_seen_to_loads": med(4, 10), "loads_to_exp_done": med(10, 12), "exp_done_to_p_ready": med(12, 6),
+            "p_ready_to_mma_sees_p": med(6, 0), "mma_sees_p_to_next_s_seen": round(
+                (t[3:steps, 4] - t[2:steps - 1, 0]).median().item(), 1)}
+
+
 def main(argv=None):
     global B, S
     ap = argparse.ArgumentParser()
@@ -206,7 +228,11 @@ def main(argv=None):
     ap.add_argument("--no-ref", action="store_true")
     ap.add_argument("--gemm-single", action="store_true",
                     help="also time GEMM cases with CTA-pair tiles switched off (harp1)")
+    ap.add_argument("--timeline", action="store_true",
+                    help="attention forward cases: also print the per-key-step phase timeline of CTA 0 (SM cycles)")
     args = ap.parse_args(argv)
+    if args.timeline:
+        os.environ["HARP_ATTN_PROBE"] = "1"  # read by the library at its first attention launch
     from .. import _native
 
     _native.require()
@@ -238,6 +264,8 @@ def main(argv=None):
                 gbs = info["bytes"] / ms / 1e6
                 rec[f"{tag}_gbs"] = round(gbs, 1)
                 rec[f"{tag}_frac_of_{peaks['src']}_hbm"] = round(gbs / peaks["hbm_gbs"], 3)
+        if args.timeline and name.startswith("attn_fwd"):
+            rec["timeline_cycles"] = fwd_timeline(harp)
         print(json.dumps(rec), flush=True)
         del harp, ref
         torch.cuda.empty_cache()

@@ -159,3 +159,20 @@ def test_attn_fwd_poly_exp(npoly):
     env = dict(os.environ, HARP_ATTN_POLY=npoly)
     r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0 and "ok" in r.stdout, r.stdout + r.stderr
+
+
+@pytest.mark.parametrize("env", [{"HARP_ATTN_BWD_Q64": "all"}, {"HARP_ATTN_FWD": "split"}])
+def test_attention_alternative_schedules(env):
+    """The schedules chosen by environment variables (read once per process):
+    the 64-query-tile backward for head dims 64-80 and the two-warps-per-row
+    forward, run through the same checks in a child process."""
+    import os
+    import subprocess
+    import sys
+
+    if os.environ.get("HARP_ATTN_CHILD"):
+        pytest.skip("already inside the child run")
+    child_env = dict(os.environ, HARP_ATTN_CHILD="1", **env)
+    r = subprocess.run([sys.executable, "-m", "pytest", __file__, "-x", "-q", "-k", "test_attn_bwd or test_attn_fwd"],
+                       env=child_env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
