@@ -73,6 +73,27 @@ def test_attn_fwd_chunked_ring_order():
     assert (lse.view(B, H, -1)[:, :, :Sq] - lse2.view(B, H, -1)[:, :, :Sq]).abs().max() < 1e-3
 
 
+@pytest.mark.parametrize("Dh", [72, 128])
+def test_attn_fwd_queries_by_chunk_rotated(Dh):
+    """Queries and keys both arrive by chunk (the fused Ulysses exchange): the
+    grid visits query pairs starting at q_rot and waits for each query chunk's
+    flag too; the result equals the plain forward."""
+    B, H, P, C = 2, 3, 4, 272
+    S = P * C
+    q, k, v = _make(B, S, S, H, Dh)
+    ready = torch.full((P,), 5, dtype=torch.int32, device="cuda")
+    o = torch.empty(B * S, H * Dh, device="cuda", dtype=torch.bfloat16)
+    lse = torch.full((B * H * _ld(S),), float("inf"), device="cuda")
+    err = torch.zeros(4, dtype=torch.int32, device="cuda")
+    torch.ops.harp.attn_fwd(q, k, v, B, S, S, H, Dh, 1.0 / math.sqrt(Dh), o, lse, ready, C, (2 * C) // 128, 5, 5.0,
+                            err, (2 * C) // 256, True)
+    torch.cuda.synchronize()
+    assert err.cpu()[0].item() == 0, err.cpu().tolist()
+    o2, lse2 = _fwd(q, k, v, B, S, S, H, Dh)
+    assert (o.float() - o2.float()).abs().max() < 1e-2
+    assert (lse.view(B, H, -1)[:, :, :S] - lse2.view(B, H, -1)[:, :, :S]).abs().max() < 1e-3
+
+
 def test_attn_fwd_ready_timeout_reports_error():
     """A chunk flag that never arrives ends the kernel with an error word, not a hang."""
     B, Sq, H, Dh, P = 1, 128, 1, 64, 2
