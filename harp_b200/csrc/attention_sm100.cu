@@ -2107,7 +2107,9 @@ void attn_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, con
   args.probe = probe ? 1 : 0;
   static const bool skip_dq = [] {
     const char* e = std::getenv("HARP_ATTN_DEBUG_SKIP_DQ");
-    return e && e[0] == '1';
+    const bool on = e && e[0] == '1';
+    if (on) TORCH_WARN_ONCE("harp attention: HARP_ATTN_DEBUG_SKIP_DQ=1, the backward leaves dQ out (timing only)");
+    return on;
   }();
   args.skip_dq = skip_dq ? 1 : 0;
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
