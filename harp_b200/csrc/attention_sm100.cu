@@ -14,13 +14,15 @@
 //     readiness flag of every chunk it touches, and tiles are visited starting
 //     at this rank's own chunk, so compute starts while peer chunks land.
 //
-// Operand layout.  Every Q/K/V/dO tile is loaded by TMA as 8-element (16-byte)
-// column strips: strip c of a 128-row tile lives at smem offset c*2048 and row r
-// at +16*r.  That is the no-swizzle canonical core-matrix layout, valid for the
-// tensor core both as a K-major operand (head dim = reduction) and as an
-// MN-major operand (head dim = output columns), so one tile serves S = Q K^T,
-// O = P V and all five backward products.  head_dim is zero-padded to a
-// multiple of 16 by loading strips past the end of the head (TMA fills zeros).
+// Operand layout.  Every Q/K/V/dO tile is loaded by TMA in 32-byte swizzled
+// atoms: atom a holds head-dim elements [16a, 16a + 16) of all rows, 32 bytes
+// per row, at a * 4096 (128-row tiles) or a * 2048 (64-row tiles).  The same
+// tile is valid for the tensor core both as a K-major operand (head dim =
+// reduction) and as an MN-major operand (head dim = output columns), so one
+// tile serves S = Q K^T, O = P V and all five backward products.  head_dim is
+// zero-padded to a multiple of 16 by loading atoms past the end of the head
+// (TMA fills zeros).  Operands the warps write themselves (P^T, dS) use the
+// unswizzled layout of 8-element strips (strip c at c * 2048, row r at +16 r).
 #include "common.cuh"
 #include "gemm_sm100.h"
 
@@ -171,7 +173,7 @@ struct FwdArgs {
   int wait_q;  // queries arrive by chunk too (same flags): wait before loading a Q tile
   int q_rot;   // query-pair index rotation (start with the pairs whose chunk is local)
   int probe;   // record key-tile step timestamps of CTA 0 (HARP_ATTN_PROBE=1)
-  int npoly;   // of every 16 exponential pairs of a row chunk, the first npoly run on the FMA pipe
+  int npoly;   // how many of every 16 exponential pairs of a row chunk run on the FMA pipe
   unsigned long long timeout_ns;
   int* err;
 };
