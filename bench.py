@@ -36,6 +36,11 @@ if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
 METRIC = "DiT train image-tokens/sec (max over ranks)"
+# The baseline numbers recorded in BASELINE.md for the headline configuration
+# (DiT-XL/2, 1024 px, 4 samples per GPU): the NCCL + cuBLAS/SDPA implementation in
+# baseline/, measured on this pool's B200s; vs_baseline divides by the entry of
+# the same GPU count.
+BASELINE_IMG_TOK_S = {1: 86322.0, 2: 146000.0, 4: 261504.0, 8: 422822.0}
 IMG_TOKENS = 4096
 TEXT_TOKENS = 256
 
@@ -411,6 +416,8 @@ def main():
                "ms_per_step": 1000.0 * el / args.steps, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
                "api": "Trainer.step" if args.impl == "harp" else "BaselineTrainer.step", "last_loss": last}
 
+    headline = (args.model == "dit-xl-2" and not args.depth and weak and args.batch_per_gpu == 4 and
+                args.latent == 128 and args.text_len == TEXT_TOKENS and sp == ws)
     if rank == 0:
         out = {
             "metric": METRIC,
@@ -422,7 +429,8 @@ def main():
             "ms_per_step": ms,
             "higher_is_better": True,
             "scaling": "weak" if weak else "strong",
-            "vs_baseline": None,
+            "vs_baseline": (value / BASELINE_IMG_TOK_S[ws]
+                            if headline and args.impl == "harp" and ws in BASELINE_IMG_TOK_S else None),
             "dtype": "bf16",
             "data": "synthetic (random latents/text embeddings of the named shapes, random-init weights)",
             "impl": args.impl,
