@@ -36,11 +36,21 @@ if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
 METRIC = "DiT train image-tokens/sec (max over ranks)"
-# The baseline numbers recorded in BASELINE.md for the headline configuration
-# (DiT-XL/2, 1024 px, 4 samples per GPU): the NCCL + cuBLAS/SDPA implementation in
-# baseline/, measured on this pool's B200s; vs_baseline divides by the entry of
-# the same GPU count.
-BASELINE_IMG_TOK_S = {1: 86322.0, 2: 146000.0, 4: 261504.0, 8: 422822.0}
+# Measured throughput of the NCCL + cuBLAS/SDPA comparison arm (baseline/,
+# `--impl baseline`) for the headline configuration, per GPU count, with the
+# commit and date of each measurement; vs_baseline divides by the entry of the
+# same GPU count.
+BASELINE_FILE = os.path.join(ROOT, "baseline", "measured.json")
+
+
+def baseline_entry(model: str, n: int):
+    try:
+        with open(BASELINE_FILE) as fh:
+            return json.load(fh).get(model, {}).get(str(n))
+    except (OSError, ValueError):
+        return None
+
+
 IMG_TOKENS = 4096
 TEXT_TOKENS = 256
 
@@ -418,6 +428,7 @@ def main():
 
     headline = (args.model == "dit-xl-2" and not args.depth and weak and args.batch_per_gpu == 4 and
                 args.latent == 128 and args.text_len == TEXT_TOKENS and sp == ws)
+    base = baseline_entry(args.model, ws) if headline and args.impl == "harp" else None
     if rank == 0:
         out = {
             "metric": METRIC,
@@ -429,8 +440,8 @@ def main():
             "ms_per_step": ms,
             "higher_is_better": True,
             "scaling": "weak" if weak else "strong",
-            "vs_baseline": (value / BASELINE_IMG_TOK_S[ws]
-                            if headline and args.impl == "harp" and ws in BASELINE_IMG_TOK_S else None),
+            "vs_baseline": (value / base["value"] if base else None),
+            "baseline_source": ({k: base[k] for k in ("value", "commit", "date") if k in base} if base else None),
             "dtype": "bf16",
             "data": "synthetic (random latents/text embeddings of the named shapes, random-init weights)",
             "impl": args.impl,

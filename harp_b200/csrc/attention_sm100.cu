@@ -752,7 +752,6 @@ struct BwdArgs {
   long lddv;
   int* err;
   int probe;  // record phase timestamps of CTA 0 into g_bwd_probe (HARP_ATTN_PROBE=1)
-  int skip_dq;  // HARP_ATTN_DEBUG_SKIP_DQ=1: leave dQ out (timing experiments; dQ is then wrong)
 };
 
 // Phase timeline of CTA 0 of the backward kernels: 64 query tiles x 16 slots
@@ -1440,7 +1439,7 @@ __global__ void __launch_bounds__(kBwdPipeThreads, 1)
         if (!mbar_wait(dqs_bar, i & 1, err, 182)) ok = false;
         if (ok) {
           BWD_PROBE(i, 7);
-          if (!a.skip_dq) tma_reduce_add_4d(&tmdQ, stage, 0, h, i * 128, b);
+          tma_reduce_add_4d(&tmdQ, stage, 0, h, i * 128, b);
           bulk_wait_read_all();
           BWD_PROBE(i, 9);
         }
@@ -1804,7 +1803,7 @@ __global__ void __launch_bounds__(kBwdQ64Threads, 1)
         // tile into dq_acc (rows past Sq are clipped by TMA), then give the
         // stage back to the TMA producer
         if (!mbar_wait(dqs_bar, i & 1, err, 282)) { ok = false; break; }
-        if (!a.skip_dq) tma_reduce_add_4d(&tmdQ, stage, 0, h, i * 64, b);
+        tma_reduce_add_4d(&tmdQ, stage, 0, h, i * 64, b);
         bulk_wait_read_all();
         mbar_arrive(&qdo_empty[st]);
       }
@@ -2107,13 +2106,6 @@ void attn_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, con
     return e && e[0] == '1';
   }();
   args.probe = probe ? 1 : 0;
-  static const bool skip_dq = [] {
-    const char* e = std::getenv("HARP_ATTN_DEBUG_SKIP_DQ");
-    const bool on = e && e[0] == '1';
-    if (on) TORCH_WARN_ONCE("harp attention: HARP_ATTN_DEBUG_SKIP_DQ=1, the backward leaves dQ out (timing only)");
-    return on;
-  }();
-  args.skip_dq = skip_dq ? 1 : 0;
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
   const int q64 = bwd_q64_mode();
   if ((nch == 16 && q64 >= 1) || ((nch == 8 || nch == 10) && q64 == 2)) {

@@ -1,62 +1,48 @@
 // RMSNorm backward that allocates no memory: a C entry point for callers that
-// cannot call cudaMalloc.
+// cannot call cudaMalloc (declared, with its contract, in harp_noalloc.h).
 //
 // This entry point has no counterpart in the reference (wxyww2049/HARP has no
 // GPU code at all).  It is a variant of the library's RMSNorm backward
 // (async_op::rmsnorm_backward_out, which takes its partial-sum scratch from the
 // PyTorch caching allocator) for code that must not allocate device memory
-// while it runs, for example:
-//   * a plugin or callback inside another runtime (an inference engine, a
-//     graph executor) that plans every byte of device memory ahead of time and
-//     forbids allocation during execution;
-//   * a process whose device memory is already fully reserved by a pool or a
-//     caching allocator, where cudaMalloc would fail;
-//   * latency-critical loops that cannot afford cudaMalloc/cudaFree, which may
-//     synchronize the whole device.
-// The caller still provides every input and output buffer.  The only scratch,
-// the per-block partial sums of the weight gradient, lives in a file-scope
-// `static __device__` array of fixed size (kScratchFloats fp32 = 4 MiB), which
-// every GPU that loads this library holds until the process exits.
+// while it runs: plugins of runtimes that plan every byte of device memory
+// ahead and forbid allocation during execution, processes whose memory is
+// fully reserved by a pool (cudaMalloc would fail), and loops that cannot
+// afford cudaMalloc/cudaFree (they may synchronize the device).  The caller
+// still provides every input and output buffer.  The only scratch, the
+// per-block partial sums of the weight gradient, lives in a file-scope
+// `static __device__` array of fixed size (2^20 fp32 = 4 MiB), which every GPU
+// that loads this library holds until the process exits.
 //
-// Contract:
-//   * input, grad_out, grad_input: bf16 [rows, dim] row-major; weight,
-//     grad_weight: bf16 [dim]; rms: fp32 [rows], the per-row root mean square
-//     saved by the forward (not its inverse), as async_op::rmsnorm_forward_out
-//     stores it.  dim must be a multiple of 8 and every pointer 16-byte aligned.
-//   * grad_input = rstd*(g*w - xhat*mean(g*w*xhat)), grad_weight = sum_rows g*xhat,
-//     with rstd = 1/rms and xhat = x*rstd; the kernels are enqueued on `stream`
-//     (0 = the legacy default stream) and the call returns without waiting.
-//   * Size limit: a call needs ceil(rows / rows_per_block) * dim partial sums
-//     with at most kMaxRowsPerBlock rows per block, i.e. it is rejected (return
-//     kNoallocTooLarge, nothing enqueued) when
-//     rows > kMaxRowsPerBlock * floor(kScratchFloats / dim).
-//   * Set-up: the first call on a device (with that device current) looks up
-//     the device address of the scratch array with cudaGetSymbolAddress and
-//     caches it; make that first call before any stream capture.
-//   * Every call shares the one scratch array.  Each call overwrites the
-//     partial sums it reads, so nothing must start at zero and stale contents
-//     from an earlier call are never used; but calls that overlap on the GPU
-//     (for example on two concurrent streams of one process) race on the
-//     scratch, so the caller must order them.
+// Host code must not pass the array's name to a kernel: on the host it is a
+// stand-in, not a device address.  The first call on each device looks up the
+// real address with cudaGetSymbolAddress (with that device current), checks the
+// result and caches it; that first call should come before any stream capture,
+// and the cache is not refreshed after cudaDeviceReset.  Every call shares the
+// array and it keeps the last call's contents: each call writes every partial
+// sum it reads, and calls that overlap on the GPU race, so callers order them.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
 #include <mutex>
 
+#include "harp_noalloc.h"
+
 namespace {
 
-constexpr long long kScratchFloats = 1ll << 20;  // 4 MiB of fp32 partial sums
-constexpr int kMaxRowsPerBlock = 4096;           // per-row statistics live in 16 KiB of shared memory
+constexpr long long kScratchFloats = HARP_NOALLOC_SCRATCH_FLOATS;  // 4 MiB of fp32 partial sums
+constexpr int kMaxRowsPerBlock = HARP_NOALLOC_MAX_ROWS_PER_BLOCK;  // per-row statistics: 16 KiB of shared memory
 constexpr int kThreads = 256;
+// Blocks a call aims for when rows allow it: a few per SM, so that the final
+// per-column reduction reads a bounded number of partial rows.
+constexpr long long kTargetBlocks = 1184;
 
-enum NoallocStatus : int {
-  kNoallocOk = 0,
-  kNoallocBadArgs = -1,
-  kNoallocTooLarge = -2,
-  kNoallocSetupFailed = -3,
-  kNoallocLaunchFailed = -4,
-};
+constexpr int kNoallocOk = HARP_NOALLOC_OK;
+constexpr int kNoallocBadArgs = HARP_NOALLOC_BAD_ARGS;
+constexpr int kNoallocTooLarge = HARP_NOALLOC_TOO_LARGE;
+constexpr int kNoallocSetupFailed = HARP_NOALLOC_SETUP_FAILED;
+constexpr int kNoallocLaunchFailed = HARP_NOALLOC_LAUNCH_FAILED;
 
 static __device__ __align__(256) float g_noalloc_scratch[kScratchFloats];
 
@@ -193,7 +179,15 @@ extern "C" int harp_rmsnorm_backward_noalloc(const void* input, const void* grad
     if (cudaMemsetAsync(grad_weight, 0, dim * sizeof(bf16), s) != cudaSuccess) return kNoallocLaunchFailed;
     return kNoallocOk;
   }
-  const int rpb = (int)(rpb_min > 32 ? rpb_min : (rows < 32 ? rows : 32));
+  // At least 32 rows per block (fewer only when the call has fewer rows), at
+  // least what the scratch size forces, and enough that the partial rows stay
+  // near kTargetBlocks for narrow, tall inputs.
+  long long rpb_l = (rows + kTargetBlocks - 1) / kTargetBlocks;
+  if (rpb_l < 32) rpb_l = 32;
+  if (rpb_l > kMaxRowsPerBlock) rpb_l = kMaxRowsPerBlock;
+  if (rpb_l < rpb_min) rpb_l = rpb_min;
+  if (rpb_l > rows) rpb_l = rows;
+  const int rpb = (int)rpb_l;
   const int nblk = (int)((rows + rpb - 1) / rpb);
   noalloc_rmsnorm_bwd_partials<<<nblk, kThreads, rpb * sizeof(float), s>>>(
       static_cast<const bf16*>(input), static_cast<const bf16*>(grad_out), static_cast<const bf16*>(weight), rms,

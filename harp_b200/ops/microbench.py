@@ -219,6 +219,37 @@ def fwd_timeline(fn) -> Dict[str, float]:
                 (t[3:steps, 4] - t[2:steps - 1, 0]).median().item(), 1)}
 
 
+def bwd_timeline(fn) -> Dict[str, float]:
+    """Median per-query-tile phase durations (SM cycles) of CTA 0 of one
+    backward launch (128-query pipelined schedule).  Probe slots per tile i:
+    10 the TMA warp issues the Q/dO loads, 0 the MMA warp has issued S/dP,
+    4 the dS warps see S/dP, 11 their TMEM loads landed, 12 P/dS computed,
+    13 the previous tile's products released P/dS, 5 P/dS stored, 1 the MMA
+    warp sees P/dS, 3 dV/dK/dQ issued, 6 the dQ warps see dQ, 7 dQ staged,
+    9 its reduce-add has read the staging buffer."""
+    torch.cuda.synchronize()
+    torch.ops.harp.attn_bwd_probe()
+    fn()
+    torch.cuda.synchronize()
+    t = torch.ops.harp.attn_bwd_probe().double()
+    tiles = int((t[:, 4] > 0).sum().item())
+    lo, hi = 2, max(3, tiles - 1)
+    d = t[lo:hi]
+
+    def med(a, b, shift=0):
+        return round((t[lo + shift:hi + shift, b] - d[:, a]).median().item(), 1)
+
+    out = {"tiles": tiles, "period": round((t[lo + 1:hi + 1, 4] - d[:, 4]).median().item(), 1)}
+    for name, a, b in (("load_issue_to_s_issued", 10, 0), ("s_issued_to_ds_sees_s", 0, 4),
+                       ("ds_sees_s_to_loaded", 4, 11), ("loaded_to_computed", 11, 12),
+                       ("computed_to_prev_free", 12, 13), ("prev_free_to_stored", 13, 5),
+                       ("stored_to_mma_sees_p", 5, 1), ("mma_sees_p_to_issued", 1, 3),
+                       ("issued_to_dq_seen", 3, 6), ("dq_seen_to_staged", 6, 7), ("staged_to_reduced", 7, 9)):
+        out[name] = med(a, b)
+    out["ds_compute_cycles"] = round(d[:, 14].median().item(), 1)
+    return out
+
+
 def main(argv=None):
     global B, S
     ap = argparse.ArgumentParser()
@@ -229,7 +260,8 @@ def main(argv=None):
     ap.add_argument("--gemm-single", action="store_true",
                     help="also time GEMM cases with CTA-pair tiles switched off (harp1)")
     ap.add_argument("--timeline", action="store_true",
-                    help="attention forward cases: also print the per-key-step phase timeline of CTA 0 (SM cycles)")
+                    help="attention cases: also print the per-key-step (forward) or per-query-tile "
+                         "(backward) phase timeline of CTA 0 (SM cycles)")
     args = ap.parse_args(argv)
     if args.timeline:
         os.environ["HARP_ATTN_PROBE"] = "1"  # read by the library at its first attention launch
@@ -266,6 +298,8 @@ def main(argv=None):
                 rec[f"{tag}_frac_of_{peaks['src']}_hbm"] = round(gbs / peaks["hbm_gbs"], 3)
         if args.timeline and name.startswith("attn_fwd"):
             rec["timeline_cycles"] = fwd_timeline(harp)
+        elif args.timeline and name.startswith("attn_bwd"):
+            rec["timeline_cycles"] = bwd_timeline(harp)
         print(json.dumps(rec), flush=True)
         del harp, ref
         torch.cuda.empty_cache()
