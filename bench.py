@@ -73,6 +73,10 @@ def parse():
                     help="sequence-parallel attention: K/V gather (ring) or head all-to-all (ulysses)")
     ap.add_argument("--comm", default="auto", choices=["auto", "torch", "nvl"])
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--phases", action="store_true",
+                    help="after the timed steps, run --steps more with per-phase CUDA events (forward, backward, "
+                         "gradient sync, each sequence-parallel exchange and wait) and print their per-step device "
+                         "time, max over ranks, as a second JSON line (implies --cuda-graph 0)")
     ap.add_argument("--cuda-graph", type=int, default=1, choices=[0, 1],
                     help="harp on one GPU: capture the whole step in a CUDA graph after the warm-up steps")
     ap.add_argument("--depth", type=int, default=0, help="override depth (debug only; not a valid bench)")
@@ -289,6 +293,8 @@ def run_ring_attn(args):
 
 def main():
     args = parse()
+    if args.phases:
+        args.cuda_graph = 0
     if args.impl == "reference":
         return run_reference(args)
     if args.op == "ring-attn":
@@ -465,6 +471,19 @@ def main():
             "e2e": e2e,
         }
         print(json.dumps(out), flush=True)
+    if args.phases and args.impl == "harp":
+        from harp_b200.utils import observability as obs
+
+        timer = obs.enable_phases(True)
+        for _ in range(args.steps):
+            step(dev_batch)
+        rep = timer.report()  # syncs; max over ranks
+        obs.enable_phases(False)
+        if rank == 0:
+            print(json.dumps({"phases_ms_per_step": {k: round(v / args.steps, 3) for k, v in sorted(rep.items())},
+                              "n_gpus": ws, "steps": args.steps, "ms_per_step_timed": ms,
+                              "note": "CUDA events on the launching stream, summed per step, max over ranks; "
+                                      "nested phases (uly.*) are inside forward/backward"}), flush=True)
     if ws > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -313,8 +313,9 @@ void reduce_scatter(const std::vector<int64_t>& src_bases, int64_t src_off, int6
 void rs_adamw_ag(const std::vector<int64_t>& grad_bases, const std::vector<int64_t>& param_bases, int64_t lo, int64_t n,
                  at::Tensor& master, at::Tensor& m, at::Tensor& v, double lr, double beta1, double beta2, double eps,
                  double wd, int64_t step, double grad_scale, int64_t rank, const c10::optional<at::Tensor>& flags,
-                 int64_t flag_first, int64_t value, double timeout_s, at::Tensor& err) {
+                 int64_t flag_first, int64_t value, double timeout_s, at::Tensor& err, int64_t blocks) {
   TORCH_CHECK(n % 8 == 0 && lo % 8 == 0, "harp_comm rs_adamw_ag: 8-element granularity");
+  TORCH_CHECK(master.is_contiguous() && m.is_contiguous() && v.is_contiguous(), "harp_comm rs_adamw_ag: contiguous state");
   TORCH_CHECK(master.numel() == n && m.numel() == n && v.numel() == n, "harp_comm rs_adamw_ag: state size");
   AdamHyper h;
   h.lr = lr; h.beta1 = beta1; h.beta2 = beta2; h.eps = eps; h.wd = wd;
@@ -323,7 +324,12 @@ void rs_adamw_ag(const std::vector<int64_t>& grad_bases, const std::vector<int64
   h.grad_scale = grad_scale;
   const int world = grad_bases.size();
   const int threads = 256;
-  rs_adamw_ag_kernel<<<grid_for(n / 8, threads), threads, 0, at::cuda::getCurrentCUDAStream()>>>(
+  // blocks > 0 caps the grid (the kernel is grid-stride), so that a bucket's
+  // kernel running beside the backward occupies only a few SMs
+  int grid = grid_for(n / 8, threads);
+  if (blocks > 0 && grid > blocks) grid = (int)blocks;
+  if (n == 0) return;
+  rs_adamw_ag_kernel<<<grid, threads, 0, at::cuda::getCurrentCUDAStream()>>>(
       make_table(grad_bases, 0), make_table(param_bases, 0), lo, n, master.data_ptr<float>(), m.data_ptr<float>(),
       v.data_ptr<float>(), h, world, (int)rank,
       flags.has_value() ? reinterpret_cast<const unsigned int*>(flags->data_ptr()) : nullptr, (int)flag_first,
@@ -349,7 +355,7 @@ TORCH_LIBRARY(harp_comm, m) {
         "int nseg, int rank, Tensor? flags, int flag_first, int value, float timeout_s, Tensor(b!) err) -> ()");
   m.def("rs_adamw_ag(int[] grad_bases, int[] param_bases, int lo, int n, Tensor(a!) master, Tensor(b!) m, "
         "Tensor(c!) v, float lr, float beta1, float beta2, float eps, float wd, int step, float grad_scale, int rank, "
-        "Tensor? flags, int flag_first, int value, float timeout_s, Tensor(d!) err) -> ()");
+        "Tensor? flags, int flag_first, int value, float timeout_s, Tensor(d!) err, int blocks=0) -> ()");
 }
 TORCH_LIBRARY_IMPL(harp_comm, CompositeExplicitAutograd, m) {
   m.impl("ipc_alloc", &harp::comm::ipc_alloc);

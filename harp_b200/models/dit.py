@@ -296,6 +296,11 @@ def _emit(p: torch.Tensor, g: torch.Tensor):
         return g.to(p.dtype)
     if g.data_ptr() != tgt.data_ptr():
         tgt.copy_(g.view_as(tgt))
+    # the slot now holds this step's complete gradient (enqueued on the current
+    # stream): tell the trainer, which may send the bucket that holds it
+    cb = getattr(p, "_harp_grad_ready", None)
+    if cb is not None:
+        cb(p)
     return None
 
 

@@ -24,6 +24,11 @@ Purposes and buffers:
   GRAD / PARAM  the fused gradient reduce-scatter + AdamW + parameter push
           waits for every peer's GRAD flag; PARAM tells peers the new
           parameters have landed, which the next step waits for.
+  GRADB   per-bucket GRAD flags of the overlapped gradient sync: a rank sets
+          its bucket-b slot from the compute stream once that bucket's
+          gradients are written; the bucket's fused kernel (side stream) waits
+          for every peer's slot.  Signals never wait, so ranks cannot block
+          one another through the order of their side-stream kernels.
   UQKV / UO / UDO / UDQ  Ulysses exchanges, one set of symmetric buffers
           per layer (q|k|v head-sharded over the full sequence, the
           sequence-sharded attention output, dO head-sharded, dq|dk|dv
@@ -42,12 +47,19 @@ import torch.distributed as dist
 from .. import _native
 from ..ops import functional as Fn
 from ..runtime import errors
+from ..utils.observability import phase
 from . import collectives as C
 
 # flag slot layout (int32 per slot, world <= 8)
 _KV, _DKV, _DKV_ACK0, _DKV_ACK1, _GRAD, _PARAM, _BARRIER = 0, 8, 16, 24, 32, 40, 48
 _UQKV, _UO, _UDO, _UDQ = 56, 64, 72, 80
-_NFLAGS = 96
+_GRADB = 96  # per-bucket gradient-ready slots: _GRADB + 8 * bucket + rank
+_MAX_BUCKETS = 32
+_NFLAGS = _GRADB + 8 * _MAX_BUCKETS
+# CTAs of one bucket's fused reduce-scatter + AdamW + push kernel: enough
+# outstanding 16-byte NVLink loads to keep the links busy, few enough SMs that
+# the backward it overlaps keeps most of the GPU
+BUCKET_CTAS = int(os.environ.get("HARP_BUCKET_CTAS", "24"))
 DEFAULT_TIMEOUT_S = float(os.environ.get("HARP_COMM_TIMEOUT_S", "120"))
 
 
@@ -240,18 +252,22 @@ class NVLinkComm:
         rk = torch.empty_like(rq) if do_norm else None
         self.epoch["uq"] += 1
         e = self.epoch["uq"]
-        torch.ops.harp_comm.uly_dispatch_qkv(qkv, S, H, Dh, r, bufs["qkvf"].bases, part, wq, wk, freqs,
-                                             freqs.shape[0] if freqs is not None else 1, eps, do_norm, rq, rk)
-        self.signal(_UQKV, e)
+        with phase("uly.dispatch_qkv"):
+            torch.ops.harp_comm.uly_dispatch_qkv(qkv, S, H, Dh, r, bufs["qkvf"].bases, part, wq, wk, freqs,
+                                                 freqs.shape[0] if freqs is not None else 1, eps, do_norm, rq, rk)
+            self.signal(_UQKV, e)
         qkvf = bufs["qkvf"].tensor(3 * part, torch.bfloat16).view(3, B * Sf, Hn * Dh)
-        o_f, lse = Fn.attn_fwd(qkvf[0], qkvf[1], qkvf[2], B, Sf, Sf, Hn, Dh, ready=self.flags[_UQKV:_UQKV + W],
-                               chunk_len=S, start_tile=(r * S) // 128, epoch=e, timeout_s=self.timeout_s,
-                               q_rot=(r * S) // 256, wait_q=True)
+        with phase("uly.attn_fwd"):
+            o_f, lse = Fn.attn_fwd(qkvf[0], qkvf[1], qkvf[2], B, Sf, Sf, Hn, Dh, ready=self.flags[_UQKV:_UQKV + W],
+                                   chunk_len=S, start_tile=(r * S) // 128, epoch=e, timeout_s=self.timeout_s,
+                                   q_rot=(r * S) // 256, wait_q=True)
         self.epoch["uo"] += 1
         eo = self.epoch["uo"]
-        torch.ops.harp_comm.uly_remap([o_f], 1, B, S, r, H, Dh, bufs["o"].bases, 0, HD, 0)
-        self.signal(_UO, eo)
-        self.wait_all(_UO, eo)
+        with phase("uly.o_remap"):
+            torch.ops.harp_comm.uly_remap([o_f], 1, B, S, r, H, Dh, bufs["o"].bases, 0, HD, 0)
+            self.signal(_UO, eo)
+        with phase("uly.o_wait"):
+            self.wait_all(_UO, eo)
         o = bufs["o"].tensor(B * S * HD, torch.bfloat16).view(B * S, HD)
         return o, rq, rk, {"i": i, "qkvf": qkvf, "o_f": o_f, "lse": lse}
 
@@ -264,17 +280,23 @@ class NVLinkComm:
         bufs = self._uly[saved["i"]]
         self.epoch["udo"] += 1
         e = self.epoch["udo"]
-        torch.ops.harp_comm.uly_remap([do], 0, B, S, r, H, Dh, bufs["dof"].bases, 0, 0, 0)
-        self.signal(_UDO, e)
-        self.wait_all(_UDO, e)
+        with phase("uly.do_remap"):
+            torch.ops.harp_comm.uly_remap([do], 0, B, S, r, H, Dh, bufs["dof"].bases, 0, 0, 0)
+            self.signal(_UDO, e)
+        with phase("uly.do_wait"):
+            self.wait_all(_UDO, e)
         dof = bufs["dof"].tensor(B * Sf * Hn * Dh, torch.bfloat16).view(B * Sf, Hn * Dh)
         qkvf = saved["qkvf"]
-        dq_f, dk_f, dv_f = Fn.attn_bwd(qkvf[0], qkvf[1], qkvf[2], saved["o_f"], dof, saved["lse"], B, Sf, Sf, Hn, Dh)
+        with phase("uly.attn_bwd"):
+            dq_f, dk_f, dv_f = Fn.attn_bwd(qkvf[0], qkvf[1], qkvf[2], saved["o_f"], dof, saved["lse"], B, Sf, Sf,
+                                           Hn, Dh)
         self.epoch["udq"] += 1
         e2 = self.epoch["udq"]
-        torch.ops.harp_comm.uly_remap([dq_f, dk_f, dv_f], 1, B, S, r, H, Dh, bufs["dqkv"].bases, 0, 3 * HD, HD)
-        self.signal(_UDQ, e2)
-        self.wait_all(_UDQ, e2)
+        with phase("uly.dqkv_remap"):
+            torch.ops.harp_comm.uly_remap([dq_f, dk_f, dv_f], 1, B, S, r, H, Dh, bufs["dqkv"].bases, 0, 3 * HD, HD)
+            self.signal(_UDQ, e2)
+        with phase("uly.dqkv_wait"):
+            self.wait_all(_UDQ, e2)
         return bufs["dqkv"].tensor(B * S * 3 * HD, torch.bfloat16).view(B * S, 3 * HD)
 
     # -- gradients: fused reduce-scatter + AdamW + parameter push ---------------
@@ -291,19 +313,52 @@ class NVLinkComm:
         if self.epoch["grad"] > 0:
             self.wait_all(_PARAM, self.epoch["grad"])
 
+    def _rs_adamw_segment(self, opt, seg, slot: int, e: int, blocks: int = 0):
+        f, n, o = seg
+        cfg = opt.cfg
+        torch.ops.harp_comm.rs_adamw_ag(self._flat["grad"].bases, self._flat["param"].bases, f, n,
+                                        opt.master[o:o + n], opt.m[o:o + n], opt.v[o:o + n], opt.lr, cfg.beta1,
+                                        cfg.beta2, cfg.eps, cfg.weight_decay, opt.step_count, cfg.grad_scale,
+                                        self.rank, self.flags, slot, e, self.timeout_s, self.err, blocks)
+
     def rs_adamw_ag(self, flat, opt):
+        """Whole-buffer form, after backward: one signal, one fused kernel per bucket."""
         assert self._flat is not None, "flat buffers must come from allocate_flat()"
         self.epoch["grad"] += 1
         e = self.epoch["grad"]
         self.signal(_GRAD, e)
         opt.step_count += 1
-        cfg = opt.cfg
-        n = opt.shard_numel
-        torch.ops.harp_comm.rs_adamw_ag(self._flat["grad"].bases, self._flat["param"].bases, self.rank * n, n,
-                                        opt.master, opt.m, opt.v, opt.lr, cfg.beta1, cfg.beta2, cfg.eps,
-                                        cfg.weight_decay, opt.step_count, cfg.grad_scale, self.rank, self.flags,
-                                        _GRAD, e, self.timeout_s, self.err)
+        with phase("grad.rs_adamw_push"):
+            for seg in opt.segments:
+                self._rs_adamw_segment(opt, seg, _GRAD, e)
         self.signal(_PARAM, e)
+
+    # overlapped form: begin_grad_sync, then rs_adamw_bucket per bucket in a
+    # fixed order as gradients complete, then end_grad_sync
+    def begin_grad_sync(self, opt):
+        assert self._flat is not None, "flat buffers must come from allocate_flat()"
+        assert len(opt.segments) <= _MAX_BUCKETS, "too many gradient buckets"
+        self.epoch["grad"] += 1
+        opt.step_count += 1
+
+    def rs_adamw_bucket(self, flat, opt, b: int, stream: torch.cuda.Stream):
+        """Bucket b's gradients are written (on the current stream): signal the
+        peers from this stream, then enqueue the bucket's pull-reduce + AdamW +
+        push on `stream` behind that point."""
+        e = self.epoch["grad"]
+        self.signal(_GRADB + 8 * b, e)
+        ev = torch.cuda.Event()
+        ev.record()
+        stream.wait_event(ev)
+        with torch.cuda.stream(stream):
+            self._rs_adamw_segment(opt, opt.segments[b], _GRADB + 8 * b, e, BUCKET_CTAS)
+
+    def end_grad_sync(self, stream: torch.cuda.Stream):
+        """After the last bucket: announce the new parameters, and make the
+        current stream wait for the side stream."""
+        with torch.cuda.stream(stream):
+            self.signal(_PARAM, self.epoch["grad"])
+        torch.cuda.current_stream().wait_stream(stream)
 
     def close(self):
         torch.cuda.synchronize(self.device)

@@ -8,13 +8,24 @@ Mapping to the reference:
     group, steps AdamW on row chunks and all-gathers the chunks back
     (COMM_MODE 1; managers/weight_manager.py:127-208).
   * Here every rank owns a replica of the bf16 weights in ONE flat buffer
-    (parameters are views into it) and a flat bf16 gradient buffer.  After
-    backward, gradients are summed over every rank (SP and DP alike) by a
-    reduce-scatter of the flat buffer, each rank runs AdamW (fp32 master, m, v)
-    on its 1/world shard, and the updated bf16 shards are all-gathered.  That is
-    the reference's COMM_MODE 1 with rs_size = world, done on the whole buffer.
-  * comm="nvl" routes the reduce-scatter / AdamW / all-gather through the
-    NVLink kernels of harp_b200.parallel.nvlink (one fused kernel per bucket).
+    (parameters are views into it) and a flat bf16 gradient buffer, laid out
+    bucket by bucket: a bucket is a group of consecutive blocks (in the order
+    their backward finishes) and every rank owns an equal 1/world slice of
+    every bucket.  Gradients are summed over every rank (SP and DP alike) by a
+    reduce-scatter of each bucket, each rank runs AdamW (fp32 master, m, v) on
+    its slices, and the updated bf16 slices are all-gathered.  That is the
+    reference's COMM_MODE 1 with rs_size = world.
+  * comm="nvl": the moment a bucket's last gradient is written (the fused
+    blocks report their direct gradient writes, autograd reports the rest
+    through post-accumulate hooks), the rank signals its peers on the compute
+    stream and enqueues ONE fused kernel for that bucket on a side stream:
+    pull-reduce of its slice from every peer over NVLink, AdamW, and a push of
+    the new bf16 slice into every peer's parameter buffer
+    (harp_b200.parallel.nvlink).  These kernels run while the backward of the
+    earlier blocks continues, as the reference's grad-ready hooks feed its
+    communication threads (managers/grad_manager.py:41-159,
+    accumulate_sp/accumulate.cpp:389-484).  Buckets are enqueued in one fixed
+    order on every rank.
 """
 from __future__ import annotations
 
@@ -31,6 +42,7 @@ from .ops import functional as Fn
 from .parallel import collectives as C
 from .parallel.sequence import SPContext, resolve_mode
 from .runtime import errors
+from .utils.observability import phase
 
 
 @dataclass
@@ -47,35 +59,71 @@ class TrainConfig:
     # graph after `graph_warmup` eager steps and replay it (single-GPU runs).
     cuda_graph: bool = False
     graph_warmup: int = 2
+    # multi-GPU NVLink gradient sync: send each bucket (about this many
+    # parameters) as soon as its gradients are complete, overlapping the rest
+    # of the backward; False = one fused kernel over everything after backward
+    overlap_grad_sync: bool = True
+    bucket_params: int = 64_000_000
 
 
 class FlatParams:
     """Packs every parameter of `model` into one contiguous buffer (and one for
-    gradients).  Parameters become views; registration order is kept, so
-    adjacently registered weights (e.g. SwiGLU w1, w3) stay adjacent."""
+    gradients).  Parameters become views; registration order is kept inside a
+    bucket, so adjacently registered weights (e.g. SwiGLU w1, w3) stay adjacent.
+
+    `buckets` (optional) is a list of parameter groups; the flat layout holds
+    them one after the other, each starting on a world*align boundary and
+    padded to a multiple of it, so that every rank owns an equal, aligned
+    1/world slice of every bucket.  Parameters in no group form a last bucket.
+    ``self.buckets`` lists each bucket's [lo, hi) range of the flat buffer."""
 
     def __init__(self, model: torch.nn.Module, device, dtype=torch.bfloat16, align: int = 256, world: int = 1,
-                 alloc=None):
+                 alloc=None, buckets: Optional[List[List[torch.Tensor]]] = None):
         self.params: List[torch.nn.Parameter] = []
         self.names: List[str] = []
-        offs = []
-        off = 0
+        named = []
         seen = set()
-        prev_end = None
         for name, p in model.named_parameters():
             if id(p) in seen:
                 continue
             seen.add(id(p))
-            # keep tightly-packed neighbours contiguous (w1 directly followed by w3)
-            if not (name.endswith("w3.weight") and prev_end is not None):
-                off = (off + align - 1) // align * align
-            offs.append(off)
-            self.params.append(p)
-            self.names.append(name)
-            off += p.numel()
-            prev_end = off
+            named.append((name, p))
+        order = {id(p): i for i, (_, p) in enumerate(named)}
+        groups: List[List[int]] = []
+        placed = set()
+        for grp in buckets or []:
+            idx = sorted({order[id(p)] for p in grp if id(p) in order and id(p) not in placed})
+            placed.update(id(named[i][1]) for i in idx)
+            if idx:
+                groups.append(idx)
+        rest = [i for i, (_, p) in enumerate(named) if id(p) not in placed]
+        if rest:
+            groups.append(rest)
         quantum = align * max(1, world)
-        self.numel = (off + quantum - 1) // quantum * quantum
+        offs = []
+        off = 0
+        self.buckets: List[tuple] = []
+        self.bucket_of: Dict[int, int] = {}
+        for gi, idx in enumerate(groups):
+            off = (off + quantum - 1) // quantum * quantum
+            lo = off
+            prev_end = None
+            for i in idx:
+                name, p = named[i]
+                # keep tightly-packed neighbours contiguous (w1 directly followed by w3)
+                if not (name.endswith("w3.weight") and prev_end is not None):
+                    off = (off + align - 1) // align * align
+                offs.append(off)
+                self.params.append(p)
+                self.names.append(name)
+                self.bucket_of[id(p)] = gi
+                off += p.numel()
+                prev_end = off
+            off = (off + quantum - 1) // quantum * quantum
+            self.buckets.append((lo, off))
+        self.numel = max(off, quantum)
+        if not self.buckets:
+            self.buckets.append((0, self.numel))
         self.offsets = offs
         if alloc is not None:
             # e.g. symmetric (peer-mapped) buffers of the NVLink communicator
@@ -111,19 +159,26 @@ class FlatParams:
 
 class ShardedAdamW:
     """AdamW with fp32 master weights and moments for this rank's 1/world
-    slice of the flat parameter buffer."""
+    slice of every bucket of the flat parameter buffer.  The slices are
+    concatenated in bucket order into one state vector; ``segments`` lists
+    (flat offset, length, state offset) per bucket."""
 
     def __init__(self, flat: FlatParams, cfg: TrainConfig, group=None):
         self.flat, self.cfg, self.group = flat, cfg, group
         self.world = C.world(group)
         self.rank = C.rank(group)
-        n = flat.numel // self.world
-        self.shard_numel = n
-        lo = self.rank * n
-        self.master = flat.flat[lo:lo + n].float().clone()
+        self.segments: List[tuple] = []
+        off = 0
+        for lo, hi in flat.buckets:
+            n = (hi - lo) // self.world
+            self.segments.append((lo + self.rank * n, n, off))
+            off += n
+        self.shard_numel = off
+        self.master = torch.cat([flat.flat[f:f + n].float() for f, n, _ in self.segments]) \
+            if len(self.segments) > 1 else flat.flat[self.segments[0][0]:self.segments[0][0] + off].float().clone()
         self.m = torch.zeros_like(self.master)
         self.v = torch.zeros_like(self.master)
-        self.grad_shard = torch.empty(n, device=flat.flat.device, dtype=flat.grad.dtype)
+        self.grad_shard = torch.empty(off, device=flat.flat.device, dtype=flat.grad.dtype)
         self.step_count = 0
         self.lr = cfg.lr
         # [lr, 1 - beta1^t, sqrt(1 - beta2^t)] on the device for CUDA-graph replays
@@ -147,31 +202,42 @@ class ShardedAdamW:
                                              math.sqrt(1.0 - self.cfg.beta2 ** t)], dtype=torch.float32))
         self.hyper.copy_(self._hyper_host, non_blocking=True)
 
-    def param_shard(self) -> torch.Tensor:
-        n = self.shard_numel
-        return self.flat.flat[self.rank * n:(self.rank + 1) * n]
+    def param_segments(self) -> List[torch.Tensor]:
+        """Views of the flat parameter buffer that this rank's state covers."""
+        return [self.flat.flat[f:f + n] for f, n, _ in self.segments]
+
+    def grad_segments(self, grad: torch.Tensor) -> List[torch.Tensor]:
+        return [grad[f:f + n] for f, n, _ in self.segments]
 
     def step(self, grad_shard: Optional[torch.Tensor] = None):
+        """AdamW on this rank's slices.  grad_shard: the summed gradient in state
+        order (default: self.grad_shard); with one rank the flat gradient buffer
+        itself may be passed."""
         if self.hyper is None:
             self.step_count += 1
         g = grad_shard if grad_shard is not None else self.grad_shard
-        Fn.adamw_flat(self.master, self.m, self.v, g, self.param_shard(), self.lr, self.cfg.beta1, self.cfg.beta2,
-                      self.cfg.eps, self.cfg.weight_decay, max(1, self.step_count), self.cfg.grad_scale,
-                      hyper=self.hyper)
+        for (f, n, o), p in zip(self.segments, self.param_segments()):
+            gs = g[f:f + n] if (self.world == 1 and g.numel() == self.flat.numel) else g[o:o + n]
+            Fn.adamw_flat(self.master[o:o + n], self.m[o:o + n], self.v[o:o + n], gs, p, self.lr, self.cfg.beta1,
+                          self.cfg.beta2, self.cfg.eps, self.cfg.weight_decay, max(1, self.step_count),
+                          self.cfg.grad_scale, hyper=self.hyper)
 
     def state_dict(self):
         return {"step": self.step_count, "lr": self.lr, "master": self.master.cpu(), "exp_avg": self.m.cpu(),
                 "exp_avg_sq": self.v.cpu(), "rank": self.rank, "world": self.world,
-                "shard_numel": self.shard_numel}
+                "shard_numel": self.shard_numel, "segments": [list(s) for s in self.segments]}
 
     def load_state_dict(self, sd):
         assert sd["world"] == self.world and sd["shard_numel"] == self.shard_numel, "optimizer shard layout mismatch"
+        if "segments" in sd:
+            assert [tuple(s) for s in sd["segments"]] == self.segments, "optimizer shard layout mismatch"
         self.step_count = sd["step"]
         self.lr = sd["lr"]
         self.master.copy_(sd["master"])
         self.m.copy_(sd["exp_avg"])
         self.v.copy_(sd["exp_avg_sq"])
-        self.param_shard().copy_(self.master.to(self.param_shard().dtype))
+        for (f, n, o), p in zip(self.segments, self.param_segments()):
+            p.copy_(self.master[o:o + n].to(p.dtype))
 
 
 @dataclass
@@ -241,8 +307,21 @@ class Trainer:
 
             self.grad_comm = NVLinkComm.get(par.world_group, device)
         alloc = self.grad_comm.allocate_flat if self.grad_comm is not None else None
-        self.flat = FlatParams(model, device, align=cfg.align, world=par.world_size, alloc=alloc)
+        buckets = grad_buckets(model, cfg.bucket_params) if par.world_size > 1 else None
+        self.flat = FlatParams(model, device, align=cfg.align, world=par.world_size, alloc=alloc, buckets=buckets)
         self.opt = ShardedAdamW(self.flat, cfg, par.world_group)
+        # overlapped gradient sync: buckets go out as their gradients complete
+        self._overlap = self.grad_comm is not None and cfg.overlap_grad_sync and len(self.flat.buckets) > 1
+        self._ready: set = set()
+        self._next_bucket = 0
+        self._bucket_left: List[int] = []
+        self._sync_active = False
+        self._comm_stream = None
+        if self._overlap:
+            self._comm_stream = torch.cuda.Stream(device=device)
+            for p in self.flat.params:
+                p.register_post_accumulate_grad_hook(self._on_grad_ready)
+                p._harp_grad_ready = self._on_grad_ready
         backend = sp_backend
         comm = None
         if par.sp_size > 1:
@@ -274,11 +353,15 @@ class Trainer:
             # are done reading our gradient buffer: safe to zero it and run
             self.grad_comm.wait_params()
         self.flat.zero_grad()
-        loss = self.loss_fn(self.model, latent, noise, text, sigmas, self.sp, **extra)
-        if self.par.dp_size > 1:
-            loss = loss / self.par.dp_size
-        loss.backward()
-        self.sync_and_step()
+        self._begin_sync()
+        with phase("forward"):
+            loss = self.loss_fn(self.model, latent, noise, text, sigmas, self.sp, **extra)
+            if self.par.dp_size > 1:
+                loss = loss / self.par.dp_size
+        with phase("backward"):
+            loss.backward()
+        with phase("grad_sync_optimizer"):
+            self.sync_and_step()
         self.global_step += 1
         lsum = loss.detach().float().reshape(1)
         if self.par.world_size > 1:
@@ -286,16 +369,53 @@ class Trainer:
             # each SP group holds one sample set: undo the dp split and sum of SP partials
         return lsum
 
+    # -- gradient sync -----------------------------------------------------------
+    def _begin_sync(self):
+        """Start of a step's backward: count the step, reset the bucket marks."""
+        if not self._overlap:
+            return
+        self.grad_comm.begin_grad_sync(self.opt)
+        self._ready = set()
+        self._next_bucket = 0
+        self._bucket_left = [0] * len(self.flat.buckets)
+        for p in self.flat.params:
+            self._bucket_left[self.flat.bucket_of[id(p)]] += 1
+        self._sync_active = True
+
+    def _on_grad_ready(self, p):
+        """A parameter's gradient of this step is complete (enqueued on the
+        current stream): mark it and send every bucket that is complete, in
+        bucket order."""
+        if not self._sync_active or id(p) in self._ready:
+            return
+        self._ready.add(id(p))
+        self._bucket_left[self.flat.bucket_of[id(p)]] -= 1
+        self._launch_ready()
+
+    def _launch_ready(self, flush: bool = False):
+        nb = len(self.flat.buckets)
+        while self._next_bucket < nb and (flush or self._bucket_left[self._next_bucket] == 0):
+            self.grad_comm.rs_adamw_bucket(self.flat, self.opt, self._next_bucket, self._comm_stream)
+            self._next_bucket += 1
+
     def sync_and_step(self):
         if self.par.world_size == 1:
             self.opt.step(self.flat.grad)
             return
         if self.grad_comm is not None:
-            self.grad_comm.rs_adamw_ag(self.flat, self.opt)
+            if self._overlap:
+                self._launch_ready(flush=True)  # buckets whose gradients nothing reported
+                self._sync_active = False
+                self.grad_comm.end_grad_sync(self._comm_stream)
+            else:
+                self.grad_comm.rs_adamw_ag(self.flat, self.opt)
             return
-        C.reduce_scatter_flat(self.flat.grad, self.opt.grad_shard, self.par.world_group)
+        g = self.opt.grad_shard
+        for (lo, hi), (f, n, o) in zip(self.flat.buckets, self.opt.segments):
+            C.reduce_scatter_flat(self.flat.grad[lo:hi], g[o:o + n], self.par.world_group)
         self.opt.step()
-        C.all_gather_flat(self.opt.param_shard(), self.flat.flat, self.par.world_group)
+        for (lo, hi), p in zip(self.flat.buckets, self.opt.param_segments()):
+            C.all_gather_flat(p, self.flat.flat[lo:hi], self.par.world_group)
 
     # -- CUDA-graph replay of the whole step (single GPU) ---------------------------
     def run(self, batch: Dict[str, torch.Tensor]) -> torch.Tensor:
@@ -372,6 +492,31 @@ class Trainer:
     def check_errors(self):
         if torch.device(self.device).type == "cuda":
             errors.check(torch.device(self.device))
+
+
+def grad_buckets(model: torch.nn.Module, target: int) -> List[List[torch.Tensor]]:
+    """Parameter groups in the order their gradients complete in backward:
+    the elements of the model's top-level ModuleLists (blocks), last-run
+    first, merged into groups of about `target` parameters.  Parameters
+    outside those lists (embedders, final layer) are left to the last group
+    that FlatParams forms from whatever no group holds."""
+    units: List[List[torch.Tensor]] = []
+    for _, child in model.named_children():
+        if isinstance(child, torch.nn.ModuleList):
+            units.extend([list(m.parameters()) for m in child])
+    units.reverse()  # lists registered (and run) later finish their backward first
+    groups: List[List[torch.Tensor]] = []
+    cur: List[torch.Tensor] = []
+    size = 0
+    for u in units:
+        cur.extend(u)
+        size += sum(p.numel() for p in u)
+        if size >= target:
+            groups.append(cur)
+            cur, size = [], 0
+    if cur:
+        groups.append(cur)
+    return groups
 
 
 def _model_heads(model) -> int:

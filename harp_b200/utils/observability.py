@@ -5,6 +5,9 @@ prints; async_rt/cpp_async_runtime.cpp RECORD_FUNCTION for native ops).
   setup_logger(log_file, is_main)  INFO on rank 0 (stream + train.log), ERROR elsewhere
   PhaseTimer                       CUDA-event timing of named phases per step,
                                    reported as the max over ranks (JSONL)
+  phase(name) / enable_phases()    process-wide phase timer that the trainer
+                                   and the NVLink exchanges report into (off
+                                   unless enabled or HARP_PHASES=1)
   nvtx(name)                       NVTX range context manager (no-op on CPU)
   make_profiler(out_dir)           torch.profiler with CPU+CUDA activities,
                                    schedule(wait=0, warmup=2, active=4)
@@ -98,6 +101,32 @@ class PhaseTimer:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             out = dict(zip(keys, t.tolist()))
         return out
+
+
+_PHASES: Optional[PhaseTimer] = PhaseTimer() if os.environ.get("HARP_PHASES", "") == "1" else None
+
+
+def enable_phases(on: bool = True) -> Optional[PhaseTimer]:
+    """Switch the process-wide phase timer on (or off); returns it."""
+    global _PHASES
+    _PHASES = PhaseTimer() if on else None
+    return _PHASES
+
+
+def phase_timer() -> Optional[PhaseTimer]:
+    return _PHASES
+
+
+@contextmanager
+def phase(name: str):
+    """Time a named phase on the current stream when the process-wide timer
+    is on; otherwise a no-op that costs one attribute lookup."""
+    t = _PHASES
+    if t is None:
+        yield
+        return
+    with t.phase(name):
+        yield
 
 
 class JsonlWriter:

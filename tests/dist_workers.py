@@ -65,7 +65,9 @@ def trainer_run(rank, world, out, args):
     for step in range(args["steps"]):
         b = {k: v[sel] for k, v in batch.items()}
         losses.append(tr.step(b))
-    return {"losses": losses, "flat": tr.flat.flat.clone(), "sd": {k: v.clone() for k, v in model.state_dict().items()}}
+    # parameters in registration order (independent of the flat buffer's bucket layout)
+    flat = torch.cat([p.detach().reshape(-1) for p in model.parameters()])
+    return {"losses": losses, "flat": flat, "sd": {k: v.clone() for k, v in model.state_dict().items()}}
 
 
 def managers(rank, world, out, args):

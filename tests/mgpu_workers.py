@@ -36,12 +36,16 @@ def train(rank, world, out, args):
     model.initialize_weights(0)
     model = model.to(torch.bfloat16)
     par = ParallelState.build(world)
-    tr = Trainer(model, par, TrainConfig(lr=1e-3, comm=args["comm"]), dev, sp_backend=args["backend"],
-                 sp_mode=args["mode"])
+    cfg = TrainConfig(lr=1e-3, comm=args["comm"], overlap_grad_sync=args.get("overlap", True),
+                      bucket_params=args.get("bucket_params", 64_000_000))
+    tr = Trainer(model, par, cfg, dev, sp_backend=args["backend"], sp_mode=args["mode"])
     batch = torch.load(args["batch"])
     losses = [tr.step({k: v.pin_memory() for k, v in batch.items()}) for _ in range(args["steps"])]
     tr.check_errors()
-    return {"losses": losses, "flat": tr.flat.flat.cpu(), "mode": tr.sp.mode, "backend": tr.sp.backend}
+    # parameters in registration order (independent of the flat buffer's bucket layout)
+    flat = torch.cat([p.detach().reshape(-1) for p in model.parameters()]).cpu()
+    return {"losses": losses, "flat": flat, "mode": tr.sp.mode, "backend": tr.sp.backend,
+            "buckets": len(tr.flat.buckets), "overlap": tr._overlap}
 
 
 def flag_timeout(rank, world, out, args):
