@@ -34,6 +34,7 @@ SOURCES = [
     "noalloc_rmsnorm.cu",
     "alloc.cpp",
     "ulysses.cu",
+    "ring.cu",
 ]
 CUDA_FLAGS = [
     "-gencode",

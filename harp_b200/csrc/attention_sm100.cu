@@ -752,7 +752,29 @@ struct BwdArgs {
   long lddv;
   int* err;
   int probe;  // record phase timestamps of CTA 0 into g_bwd_probe (HARP_ATTN_PROBE=1)
+  // Sequence-parallel push of dK/dV (push_chunk > 0): the keys of each sample
+  // are W chunks of push_chunk rows owned by ranks 0..W-1; the dK/dV rows of
+  // chunk c are stored into rank c's receive buffer (peer address push_base[c],
+  // slot push_rank of push_slot elements, rows b*push_chunk + key % push_chunk
+  // with stride lddk, dV push_vcol columns after dK) instead of dK/dV.
+  unsigned long long push_base[8];
+  int push_chunk;
+  int push_rank;
+  long long push_slot;
+  long long push_vcol;
 };
+
+// Destination row of key `key` of sample b in dK (is_v = false) or dV; the
+// caller has checked key < Skv.
+__device__ __forceinline__ bf16* dkv_dst_row(const BwdArgs& a, bool is_v, int b, int h, int key) {
+  if (a.push_chunk > 0) {
+    const int c = min(key / a.push_chunk, 7);
+    const int kl = key - c * a.push_chunk;
+    bf16* base = reinterpret_cast<bf16*>(a.push_base[c]) + (long long)a.push_rank * a.push_slot;
+    return base + ((long long)b * a.push_chunk + kl) * a.lddk + (is_v ? a.push_vcol : 0) + (long long)h * a.Dh;
+  }
+  return is_v ? a.dV + (long)(b * a.Skv + key) * a.lddv + h * a.Dh : a.dK + (long)(b * a.Skv + key) * a.lddk + h * a.Dh;
+}
 
 // Phase timeline of CTA 0 of the backward kernels: 64 query tiles x 16 slots
 // of SM clock64 values, read back with attn_bwd_probe() (the forward kernel
@@ -989,7 +1011,7 @@ __global__ void __launch_bounds__(kBwdThreads1, 1)
     if (warp < 10) {  // dV is stored by warps 2-5
       if (ok) ok = mbar_wait(fin, 0, err, 71);
       tc_fence_after();
-      bf16* vrow = a.dV + (long)(b * a.Skv + key) * a.lddv + h * a.Dh;
+      bf16* vrow = key_ok ? dkv_dst_row(a, true, b, h, key) : nullptr;
 #pragma unroll
       for (int c = 0; c < C::DPAD; c += 16) {
         uint32_t v[16];
@@ -1061,7 +1083,7 @@ __global__ void __launch_bounds__(kBwdThreads1, 1)
     if (ok) ok = mbar_wait(fin, 0, err, 81);
     tc_fence_after();
     const int key = k0 + qr;
-    bf16* krow = a.dK + (long)(b * a.Skv + key) * a.lddk + h * a.Dh;
+    bf16* krow = key < a.Skv ? dkv_dst_row(a, false, b, h, key) : nullptr;
 #pragma unroll
     for (int c = 0; c < C::DPAD; c += 16) {
       uint32_t v[16];
@@ -1377,7 +1399,7 @@ __global__ void __launch_bounds__(kBwdPipeThreads, 1)
     if (wg == 1) {  // dV is stored by warpgroup 1
       if (ok) ok = mbar_wait(fin, 0, err, 172);
       tc_fence_after();
-      bf16* vrow = a.dV + (long)(b * a.Skv + key) * a.lddv + h * a.Dh;
+      bf16* vrow = key_ok ? dkv_dst_row(a, true, b, h, key) : nullptr;
 #pragma unroll
       for (int c = 0; c < C::DPAD; c += 16) {
         uint32_t v[16];
@@ -1450,7 +1472,7 @@ __global__ void __launch_bounds__(kBwdPipeThreads, 1)
     if (ok) ok = mbar_wait(fin, 0, err, 181);
     tc_fence_after();
     const int key = k0 + qr;
-    bf16* krow = a.dK + (long)(b * a.Skv + key) * a.lddk + h * a.Dh;
+    bf16* krow = key < a.Skv ? dkv_dst_row(a, false, b, h, key) : nullptr;
 #pragma unroll
     for (int c = 0; c < C::DPAD; c += 16) {
       uint32_t v[16];
@@ -1747,7 +1769,7 @@ __global__ void __launch_bounds__(kBwdQ64Threads, 1)
     if (wg == 1) {  // dV is stored by warpgroup 1
       if (ok) ok = mbar_wait(fin, 0, err, 272);
       tc_fence_after();
-      bf16* vrow = a.dV + (long)(b * a.Skv + key) * a.lddv + h * a.Dh;
+      bf16* vrow = key_ok ? dkv_dst_row(a, true, b, h, key) : nullptr;
 #pragma unroll 1
       for (int cc = 0; cc < C::DPAD; cc += 16) {
         uint32_t v[16];
@@ -1813,7 +1835,7 @@ __global__ void __launch_bounds__(kBwdQ64Threads, 1)
     tc_fence_after();
     const int kr = quarter * 32 + lane;
     const int key = k0 + kr;
-    bf16* krow = a.dK + (long)(b * a.Skv + key) * a.lddk + h * a.Dh;
+    bf16* krow = key < a.Skv ? dkv_dst_row(a, false, b, h, key) : nullptr;
 #pragma unroll 1
     for (int cc = 0; cc < C::DPAD; cc += 16) {
       uint32_t v[16];
@@ -2069,9 +2091,14 @@ void attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, int
 
 // Backward.  delta = rowsum(dO * O) fp32 [B*Sq*H]; dq_acc fp32 [B*Sq*H*Dh],
 // zeroed by the caller; dk/dv written (bf16, token-major).
+// With push_chunk > 0 the dK/dV rows go to the owners' receive buffers
+// (peer addresses push_bases, one per rank of the sequence-parallel group)
+// instead of dk/dv: see BwdArgs.
 void attn_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& dout,
               const at::Tensor& lse, const at::Tensor& delta, int64_t B, int64_t Sq, int64_t Skv, int64_t H,
-              int64_t Dh, double scale, at::Tensor& dq_acc, at::Tensor& dk, at::Tensor& dv, at::Tensor& err) {
+              int64_t Dh, double scale, at::Tensor& dq_acc, at::Tensor& dk, at::Tensor& dv, at::Tensor& err,
+              const std::vector<int64_t>& push_bases, int64_t push_chunk, int64_t push_rank, int64_t push_slot,
+              int64_t push_ld, int64_t push_vcol) {
   TORCH_CHECK(dq_acc.scalar_type() == at::kFloat && dq_acc.is_contiguous(), "attn_bwd: dq_acc fp32 contiguous");
   const long lse_ld = ((Sq + 127) / 128) * 128;
   TORCH_CHECK(lse.numel() >= B * H * lse_ld && delta.numel() >= B * H * lse_ld, "attn_bwd: lse/delta layout");
@@ -2106,6 +2133,23 @@ void attn_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, con
     return e && e[0] == '1';
   }();
   args.probe = probe ? 1 : 0;
+  for (int i = 0; i < 8; ++i) args.push_base[i] = 0;
+  args.push_chunk = 0;
+  args.push_rank = 0;
+  args.push_slot = 0;
+  args.push_vcol = 0;
+  if (push_chunk > 0) {
+    const int W = (int)push_bases.size();
+    TORCH_CHECK(W >= 1 && W <= 8 && (long long)W * push_chunk == Skv, "attn_bwd push: Skv = ranks x chunk, <= 8 ranks");
+    TORCH_CHECK(push_ld % 8 == 0 && push_slot % 8 == 0 && push_vcol % 8 == 0 && push_rank >= 0 && push_rank < W,
+                "attn_bwd push: 16-byte aligned rows and slots");
+    for (int i = 0; i < W; ++i) args.push_base[i] = (unsigned long long)push_bases[i];
+    args.push_chunk = (int)push_chunk;
+    args.push_rank = (int)push_rank;
+    args.push_slot = push_slot;
+    args.push_vcol = push_vcol;
+    args.lddk = push_ld;
+  }
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
   const int q64 = bwd_q64_mode();
   if ((nch == 16 && q64 >= 1) || ((nch == 8 || nch == 10) && q64 == 2)) {
@@ -2184,7 +2228,8 @@ TORCH_LIBRARY_FRAGMENT(harp, m) {
         "Tensor(b!) lse, Tensor? ready, int chunk_len, int start_tile, int epoch, float timeout_s, Tensor(c!) err, "
         "int q_rot=0, bool wait_q=False) -> ()");
   m.def("attn_bwd(Tensor q, Tensor k, Tensor v, Tensor dout, Tensor lse, Tensor delta, int B, int Sq, int Skv, "
-        "int H, int Dh, float scale, Tensor(a!) dq_acc, Tensor(b!) dk, Tensor(c!) dv, Tensor(d!) err) -> ()");
+        "int H, int Dh, float scale, Tensor(a!) dq_acc, Tensor(b!) dk, Tensor(c!) dv, Tensor(d!) err, "
+        "int[] push_bases=[], int push_chunk=0, int push_rank=0, int push_slot=0, int push_ld=0, int push_vcol=0) -> ()");
   m.def("dq_finalize(Tensor acc, int H, int Dh, float scale, Tensor(a!) out, int Sq) -> ()");
   m.def("attn_bwd_probe() -> Tensor");
   m.def("exp2_poly(Tensor x) -> Tensor");

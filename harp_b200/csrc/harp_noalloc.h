@@ -40,7 +40,8 @@ enum HarpNoallocStatus {
 //   weight, grad_weight: bf16 [dim];
 //   rms: fp32 [rows], the per-row root mean square (not its inverse) that the
 //        library's RMSNorm forward (async_op::rmsnorm_forward_out) saves.
-//   dim % 8 == 0; input, grad_out, weight and grad_input 16-byte aligned.
+//   dim % 8 == 0; input, grad_out, weight and grad_input 16-byte aligned
+//   (with rows == 0 the row buffers are not read and may be null).
 // Computes grad_input = rstd * (g*w - xhat * mean(g*w*xhat)) and
 // grad_weight = sum over rows of g*xhat (rstd = 1/rms, xhat = x*rstd), fp32
 // inside, enqueued on `stream` (a cudaStream_t; 0 = the legacy default stream).

@@ -162,10 +162,12 @@ float* scratch_on_current_device(int* status) {
 extern "C" int harp_rmsnorm_backward_noalloc(const void* input, const void* grad_out, const void* weight,
                                              const float* rms, void* grad_input, void* grad_weight, long long rows,
                                              long long dim, void* stream) {
-  if (input == nullptr || grad_out == nullptr || weight == nullptr || rms == nullptr || grad_input == nullptr ||
-      grad_weight == nullptr || rows < 0 || dim <= 0 || dim % 8 != 0 || dim > kScratchFloats)
+  // an empty batch reads no row buffer, so those may be null (as empty tensors' pointers are)
+  if (weight == nullptr || grad_weight == nullptr || rows < 0 || dim <= 0 || dim % 8 != 0 || dim > kScratchFloats)
     return kNoallocBadArgs;
-  if (!aligned16(input) || !aligned16(grad_out) || !aligned16(weight) || !aligned16(grad_input))
+  if (rows > 0 && (input == nullptr || grad_out == nullptr || rms == nullptr || grad_input == nullptr))
+    return kNoallocBadArgs;
+  if (rows > 0 && (!aligned16(input) || !aligned16(grad_out) || !aligned16(weight) || !aligned16(grad_input)))
     return kNoallocBadArgs;
   const long long max_blocks = kScratchFloats / dim;
   const long long rpb_min = (rows + max_blocks - 1) / max_blocks;  // rows per block forced by the scratch size

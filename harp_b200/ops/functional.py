@@ -459,14 +459,35 @@ def attn_fwd(q, k, v, B, Sq, Skv, H, Dh, scale=None, ready=None, chunk_len=0, st
     return o, lse
 
 
-def attn_bwd(q, k, v, o, do, lse, B, Sq, Skv, H, Dh, scale=None, dk_out=None, dv_out=None, dq_out=None):
-    """Returns (dq [B*Sq,H*Dh] bf16, dk, dv [B*Skv, H*Dh] bf16)."""
+def attn_bwd(q, k, v, o, do, lse, B, Sq, Skv, H, Dh, scale=None, dk_out=None, dv_out=None, dq_out=None,
+             push=None, delta=None):
+    """Returns (dq [B*Sq,H*Dh] bf16, dk, dv [B*Skv, H*Dh] bf16).
+
+    delta (optional): rowsum(dO * O) fp32 in the lse layout [B, H, lse_ld(Sq)],
+    0 past Sq; when given, `o` is not read (may be None).
+
+    push (CUDA, sequence parallel): dict(bases, chunk, rank, slot, ld, vcol):
+    the keys are len(bases) chunks of `chunk` rows per sample; the kernel
+    stores the dK/dV rows of chunk c straight into rank c's receive buffer
+    (peer address bases[c], slot `rank` of `slot` elements, row stride `ld`,
+    dV `vcol` columns after dK) and returns (dq, None, None)."""
     scale = scale if scale is not None else 1.0 / math.sqrt(Dh)
+    if push is not None:
+        assert _cuda(q), "dK/dV push needs the CUDA kernels"
+        dq = dq_out if dq_out is not None else torch.empty(B * Sq, H * Dh, device=q.device, dtype=q.dtype)
+        delta = rowdot(do, o, H, Dh, Sq) if delta is None else delta
+        dq_acc = torch.zeros(B * H * Sq * Dh, device=q.device)
+        dummy = torch.empty(0, H * Dh, device=q.device, dtype=q.dtype)
+        torch.ops.harp.attn_bwd(q, k, v, do, lse, delta, B, Sq, Skv, H, Dh, scale, dq_acc, dummy, dummy,
+                                errors.word(q.device), push["bases"], push["chunk"], push["rank"], push["slot"],
+                                push["ld"], push["vcol"])
+        torch.ops.harp.dq_finalize(dq_acc, H, Dh, scale, dq, Sq)
+        return dq, None, None
     dk = dk_out if dk_out is not None else torch.empty(B * Skv, H * Dh, device=q.device, dtype=q.dtype)
     dv = dv_out if dv_out is not None else torch.empty(B * Skv, H * Dh, device=q.device, dtype=q.dtype)
     dq = dq_out if dq_out is not None else torch.empty(B * Sq, H * Dh, device=q.device, dtype=q.dtype)
     if _cuda(q):
-        delta = rowdot(do, o, H, Dh, Sq)
+        delta = rowdot(do, o, H, Dh, Sq) if delta is None else delta
         dq_acc = torch.zeros(B * H * Sq * Dh, device=q.device)  # [B, H, Sq, Dh]
         torch.ops.harp.attn_bwd(q, k, v, do, lse, delta, B, Sq, Skv, H, Dh, scale, dq_acc, dk, dv,
                                 errors.word(q.device))
@@ -480,7 +501,10 @@ def attn_bwd(q, k, v, o, do, lse, B, Sq, Skv, H, Dh, scale=None, dk_out=None, dv
     p = torch.exp(s - lse.view(B, H, -1)[:, :, :Sq, None])
     dvf = torch.einsum("bhqk,bqhd->bkhd", p, dof)
     dp = torch.einsum("bqhd,bkhd->bhqk", dof, vf)
-    delta = (dof * o.float().view(B, Sq, H, Dh)).sum(-1).permute(0, 2, 1)[..., None]
+    if delta is None:
+        delta = (dof * o.float().view(B, Sq, H, Dh)).sum(-1).permute(0, 2, 1)[..., None]
+    else:
+        delta = delta.view(B, H, -1)[:, :, :Sq, None].float()
     ds = p * (dp - delta)
     dqf = torch.einsum("bhqk,bkhd->bqhd", ds, kf) * scale
     dkf = torch.einsum("bhqk,bqhd->bkhd", ds, qf) * scale

@@ -10,9 +10,10 @@ token-major views; out fp32 [B, H, T, D]; running max m_i bf16 and sum l_i
 fp32 [B, H, T, 1]; D = rowsum(dO * O) fp32), so code written against the
 reference's op library runs unchanged.  Here the statistics encode the
 log-sum-exp: m_i = bf16(lse) and l_i = exp(lse - m_i), i.e.
-lse = m_i + log(l_i) exactly as the reference combines them.  The ops run
-the sequence-parallel attention of harp_b200.parallel.sequence over the SP
-group set with set_sp_context() (sp_size must match its size); on CPU
+lse = m_i + log(l_i) exactly as the reference combines them, and the
+backward takes the LSE and D from its arguments.  The ops gather the K/V
+chunks of the SP group set with set_sp_context() (sp_size must match its
+size) and run the harp attention kernels with any softmax scale; on CPU
 tensors they use the fp32 restatements.  `CPURingAttention` is the
 reference's autograd wrapper (src/models/z_image/module/attn.py:15-50).
 """
@@ -23,7 +24,8 @@ from typing import Optional
 
 import torch
 
-from ..parallel.sequence import SPContext, sp_attention_backward, sp_attention_forward
+from . import functional as Fn
+from ..parallel.sequence import SPContext, _dkv_scatter_torch, _kv_gather_torch
 
 _ctx: SPContext = SPContext()
 _lib = torch.library.Library("ring_attention_ops", "DEF")
@@ -52,14 +54,24 @@ def _check(sp_size: int):
                            "(harp_b200.ops.ring_ops.set_sp_context)")
 
 
+def _gather_kv(kt, vt, B, T, HD):
+    """Every rank's K|V chunk of the SP group, sample-major [B*sp*T, 2*HD]
+    (the reference's ring passes the same chunks around its dies)."""
+    if _ctx.size == 1:
+        return torch.cat([kt, vt], 1)
+    return _kv_gather_torch(kt, vt, B, T, HD, _ctx)
+
+
 def _forward(q, k, v, out, m_i, l_i, sp_size, scale):
+    """Attention of the local queries over the keys of every SP rank, with the
+    given softmax scale."""
     _check(sp_size)
     B, H, T, D = q.shape
-    o, saved = sp_attention_forward(_tok(q).contiguous(), _tok(k).contiguous(), _tok(v).contiguous(), B, T, H, D,
-                                    _ctx) if math.isclose(scale, 1.0 / math.sqrt(D)) else (None, None)
-    if o is None:
-        raise NotImplementedError("ring_attention_ops: only the default softmax scale 1/sqrt(D) is supported")
-    lse = saved["lse"].view(B, H, -1)[:, :, :T]
+    HD = H * D
+    qt = _tok(q).contiguous()
+    kv = _gather_kv(_tok(k).contiguous(), _tok(v).contiguous(), B, T, HD)
+    o, lse = Fn.attn_fwd(qt, kv[:, :HD], kv[:, HD:], B, T, _ctx.size * T, H, D, scale=scale)
+    lse = lse.view(B, H, -1)[:, :, :T]
     out.copy_(o.view(B, T, H, D).transpose(1, 2))
     m_i.copy_(lse.unsqueeze(-1))
     l_i.copy_(torch.exp(lse.unsqueeze(-1) - m_i.float()))
@@ -67,18 +79,30 @@ def _forward(q, k, v, out, m_i, l_i, sp_size, scale):
 
 
 def _backward(q, grad_q, k, dK, v, dV, grad_out, m_i, l_i, D, sp_size, scale):
-    """The exchange state of the forward (gathered K/V or head-sharded q/k/v
-    and the LSE) is not part of the op contract, so it is rebuilt by running
-    the forward again; its LSE equals m_i + log(l_i) up to rounding.  D is
-    recomputed inside the attention backward as rowsum(dO * O)."""
+    """Uses the forward's statistics as the op contract passes them: the
+    log-sum-exp is m_i + log(l_i) and D = rowsum(dO * O) is the softmax
+    backward's row term, so nothing of the forward is recomputed; only the K/V
+    chunks are gathered again (they are not part of the contract), and the
+    dK/dV of every chunk are summed back to its owner."""
     _check(sp_size)
     B, H, T, Dh = q.shape
+    HD = H * Dh
+    W = _ctx.size
     qt, kt, vt = _tok(q).contiguous(), _tok(k).contiguous(), _tok(v).contiguous()
-    o, saved = sp_attention_forward(qt, kt, vt, B, T, H, Dh, _ctx)
-    dq, dk, dv = sp_attention_backward(saved, qt, kt, vt, o, _tok(grad_out).contiguous(), B, T, H, Dh, _ctx)
+    ld = Fn.lse_ld(T)
+    lse = torch.full((B, H, ld), float("inf"), device=q.device, dtype=torch.float32)
+    lse[:, :, :T] = (m_i.float() + torch.log(l_i.float()))[..., 0]
+    delta = torch.zeros((B, H, ld), device=q.device, dtype=torch.float32)
+    delta[:, :, :T] = D.float()[..., 0]
+    kv = _gather_kv(kt, vt, B, T, HD)
+    dq, dk, dv = Fn.attn_bwd(qt, kv[:, :HD], kv[:, HD:], None, _tok(grad_out).contiguous(), lse.reshape(-1), B, T,
+                             W * T, H, Dh, scale=scale, delta=delta.reshape(-1))
+    if W > 1:
+        dkv = _dkv_scatter_torch(torch.cat([dk, dv], 1), B, T, HD, _ctx)
+        dk, dv = dkv[:, :HD], dkv[:, HD:]
     grad_q.copy_(dq.view(B, T, H, Dh).transpose(1, 2))
-    dK.copy_(dk.view(B, T, H, Dh).transpose(1, 2))
-    dV.copy_(dv.view(B, T, H, Dh).transpose(1, 2))
+    dK.copy_(dk.reshape(B, T, H, Dh).transpose(1, 2))
+    dV.copy_(dv.reshape(B, T, H, Dh).transpose(1, 2))
     return grad_q, dK, dV
 
 

@@ -137,6 +137,8 @@ class NVLinkComm:
         self._uly_idx = 0
         self._kv_bufs: List[SymBuffer] = []
         self._kv_idx = 0
+        self._ring_bufs: List[SymBuffer] = []
+        self._dkv_push: List[SymBuffer] = []
         self._dkv_bufs: List[SymBuffer] = []
         self._dkv_idx = 0
         self._dkv_last_epoch = [0, 0]
@@ -192,6 +194,82 @@ class NVLinkComm:
         torch.ops.harp_comm.gather(buf.bases, 0, S * row, kv_full, 0, S * row, W * S * row, S * row, B, self.rank,
                                    self.flags, _KV, e, self.timeout_s, self.err)
         return kv_full, None, 0
+
+    # -- ring (K/V gather) fused with its producer ------------------------------
+    def ring_forward(self, q, k, v, B: int, S: int, H: int, Dh: int, wq=None, wk=None, freqs=None, eps: float = 1e-6,
+                     do_norm: bool = False, q_ready: bool = False):
+        """q, k, v: this rank's pre-norm rows [B*S, >=H*Dh] (views of one q|k|v
+        tensor or separate tensors).  One kernel applies QK-norm + RoPE (when
+        do_norm / freqs) and stores K, V into every rank's gathered K|V buffer
+        at this rank's chunk; the attention over the full key sequence starts
+        on the local chunk and takes each peer chunk as its flag arrives.
+        q_ready: q is already final (no norm, no RoPE) and is used as is.
+        Returns (o, q_final, rstd_q, rstd_k, saved)."""
+        i = self._kv_idx
+        self._kv_idx += 1
+        W, r = self.world, self.rank
+        HD = H * Dh
+        nbytes = B * W * S * 2 * HD * 2
+        while len(self._ring_bufs) <= i:
+            self._ring_bufs.append(SymBuffer(self.group, nbytes, self.device))
+        buf = self._ring_bufs[i]
+        assert buf.nbytes >= nbytes, "ring K/V buffer shape changed between steps"
+        qf = None if q_ready else torch.empty(B * S, HD, device=q.device, dtype=torch.bfloat16)
+        rq = torch.empty(B * S * H, device=q.device, dtype=torch.float32) if do_norm and not q_ready else None
+        rk = torch.empty(B * S * H, device=q.device, dtype=torch.float32) if do_norm else None
+        self.epoch["kv"] += 1
+        e = self.epoch["kv"]
+        with phase("ring.dispatch_kv"):
+            torch.ops.harp_comm.ring_dispatch_qkv(q, k, v, S, H, Dh, r, buf.bases, 2 * HD, qf, wq, wk, freqs,
+                                                  freqs.shape[0] if freqs is not None else 1, eps, do_norm, rq, rk)
+            self.signal(_KV, e)
+        kv = buf.tensor(B * W * S * 2 * HD, torch.bfloat16).view(B * W * S, 2 * HD)
+        qq = q if q_ready else qf
+        with phase("ring.attn_fwd"):
+            o, lse = Fn.attn_fwd(qq, kv[:, :HD], kv[:, HD:], B, S, W * S, H, Dh, ready=self.flags[_KV:_KV + W],
+                                 chunk_len=S, start_tile=(r * S) // 128, epoch=e, timeout_s=self.timeout_s)
+        return o, qq, rq, rk, {"lse": lse, "kv": kv}
+
+    def ring_backward(self, saved, q, o, do, B: int, S: int, H: int, Dh: int, out: Optional[torch.Tensor] = None,
+                      out_ld: int = 0):
+        """Attention backward over the gathered keys; the kernel stores the
+        dK/dV rows of every chunk straight into its owner's receive buffer
+        (slot = this rank), then one kernel per rank waits for every peer's
+        flag and sums the slots.  Returns (dq [B*S, H*Dh], dkv): dkv is `out`
+        (rows of stride out_ld holding dK at column 0, dV at H*Dh) or a new
+        [B*S, 2*H*Dh] tensor."""
+        W, r = self.world, self.rank
+        HD = H * Dh
+        slot = B * S * 2 * HD
+        j = self._dkv_idx % 2
+        self._dkv_idx += 1
+        while len(self._dkv_push) < 2:
+            self._dkv_push.append(SymBuffer(self.group, W * slot * 2, self.device))
+        buf = self._dkv_push[j]
+        assert buf.nbytes >= W * slot * 2, "ring dK/dV buffer shape changed between steps"
+        last = self._dkv_last_epoch[j]
+        if last > 0:  # every rank has summed what this buffer held two layers ago
+            with phase("ring.dkv_ack_wait"):
+                self.wait_all(_DKV_ACK0 if j == 0 else _DKV_ACK1, last)
+        kv = saved["kv"]
+        with phase("ring.attn_bwd"):
+            dq, _, _ = Fn.attn_bwd(q, kv[:, :HD], kv[:, HD:], o, do, saved["lse"], B, S, W * S, H, Dh,
+                                   push={"bases": buf.bases, "chunk": S, "rank": r, "slot": slot, "ld": 2 * HD,
+                                         "vcol": HD})
+        self.epoch["dkv"] += 1
+        e = self.epoch["dkv"]
+        self.signal(_DKV, e)
+        if out is None:
+            out = torch.empty(B * S, 2 * HD, device=q.device, dtype=torch.bfloat16)
+            out_ld = 2 * HD
+        own = buf.bases[r]
+        with phase("ring.dkv_reduce"):
+            # sum of the W slots (slot c written by rank c), row by row into `out`
+            torch.ops.harp_comm.reduce_scatter([own + c * slot * 2 for c in range(W)], 0, 2 * HD, out, out_ld,
+                                               2 * HD, B * S, r, self.flags, _DKV, e, self.timeout_s, self.err)
+        self._dkv_last_epoch[j] = e
+        self.signal(_DKV_ACK0 if j == 0 else _DKV_ACK1, e)
+        return dq, out
 
     # -- sequence-parallel dK/dV reduce-scatter (backward) ----------------------
     def dkv_buffer(self, rows: int, cols: int, dtype) -> torch.Tensor:
@@ -363,6 +441,8 @@ class NVLinkComm:
     def close(self):
         torch.cuda.synchronize(self.device)
         uly = [b for layer in self._uly for b in layer.values()]
-        for b in self._kv_bufs + self._dkv_bufs + uly + list((self._flat or {}).values()) + [self.flags_buf]:
+        for b in (self._kv_bufs + self._dkv_bufs + self._ring_bufs + self._dkv_push + uly +
+                  list((self._flat or {}).values()) + [self.flags_buf]):
             b.release()
         self._kv_bufs, self._dkv_bufs, self._flat, self._uly = [], [], None, []
+        self._ring_bufs, self._dkv_push = [], []

@@ -24,9 +24,12 @@ sp/2 times less traffic at sp >= 4.  The reference has no Ulysses mode.
 
 Exchange backends:
   "torch"  torch.distributed all-gather / reduce-scatter (gloo or NCCL)
-  "nvl"    harp NVLink exchange: peers' K/V pulled over NVLink into a
-           local buffer chunk by chunk with per-chunk readiness flags that
-           the attention kernel waits on (harp_b200.parallel.nvlink)
+  "nvl"    harp NVLink exchange (harp_b200.parallel.nvlink): ring mode's
+           QK-norm/RoPE kernel stores K/V into every rank's gathered buffer,
+           the attention kernel waits per key tile for the flag of the chunk
+           it reads, and the attention backward stores each chunk's dK/dV
+           into its owner's receive buffer; Ulysses mode's exchanges are
+           fused with their producers the same way
 """
 from __future__ import annotations
 
@@ -111,12 +114,9 @@ def sp_attention_forward(q, k, v, B: int, S: int, H: int, Dh: int, sp: SPContext
         o_f, lse = Fn.attn_fwd(qkv_f[0], qkv_f[1], qkv_f[2], B, Sf, Sf, Hn, Dh)
         o = _heads_to_seq((o_f,), B, S, H, Dh, sp)[0]
         return o, {"lse": lse, "qkv_f": qkv_f, "o_f": o_f}
-    if sp.backend == "nvl" and sp.comm is not None:
-        kv_full, ready, epoch = sp.comm.kv_exchange(k, v, B, S, HD)
-        start_tile = (sp.rank * S) // 128
-        o, lse = Fn.attn_fwd(q, kv_full[:, :HD], kv_full[:, HD:], B, S, sp.size * S, H, Dh, ready=ready,
-                             chunk_len=S, start_tile=start_tile, epoch=epoch)
-        return o, {"lse": lse, "kv": kv_full}
+    if ring_nvl(sp):
+        o, _, _, _, saved = sp.comm.ring_forward(q, k, v, B, S, H, Dh, q_ready=True)
+        return o, saved
     kv_full = _kv_gather_torch(k, v, B, S, HD, sp)
     o, lse = Fn.attn_fwd(q, kv_full[:, :HD], kv_full[:, HD:], B, S, sp.size * S, H, Dh)
     return o, {"lse": lse, "kv": kv_full}
@@ -143,21 +143,25 @@ def sp_attention_backward(saved, q, k, v, o, do, B: int, S: int, H: int, Dh: int
         return dqkv[0], dqkv[1], dqkv[2]
     kv_full = saved["kv"]
     Skv = sp.size * S
-    if sp.backend == "nvl" and sp.comm is not None:
-        dkv_full = sp.comm.dkv_buffer(B * Skv, 2 * HD, q.dtype)
+    if ring_nvl(sp):
+        dq, dkv = sp.comm.ring_backward(saved, q, o, do, B, S, H, Dh)
     else:
         dkv_full = torch.empty(B * Skv, 2 * HD, device=q.device, dtype=q.dtype)
-    dq, _, _ = Fn.attn_bwd(q, kv_full[:, :HD], kv_full[:, HD:], o, do, lse, B, S, Skv, H, Dh,
-                           dk_out=dkv_full[:, :HD], dv_out=dkv_full[:, HD:])
-    if sp.backend == "nvl" and sp.comm is not None:
-        dkv = sp.comm.dkv_reduce_scatter(dkv_full, B, S, HD)
-    else:
+        dq, _, _ = Fn.attn_bwd(q, kv_full[:, :HD], kv_full[:, HD:], o, do, lse, B, S, Skv, H, Dh,
+                               dk_out=dkv_full[:, :HD], dv_out=dkv_full[:, HD:])
         dkv = _dkv_scatter_torch(dkv_full, B, S, HD, sp)
     dk = dkv[:, :HD]
     if dv_out is not None:
         dv_out.copy_(dkv[:, HD:])
         return dq, dk
     return dq, dk, dkv[:, HD:]
+
+
+def ring_nvl(sp: SPContext) -> bool:
+    """The fused NVLink ring path (K/V stored into every rank by their
+    producer, attention consuming chunks as their flags arrive, dK/dV stored
+    into their owners by the attention backward)."""
+    return sp.size > 1 and sp.mode == "ring" and sp.backend == "nvl" and sp.comm is not None
 
 
 def ulysses_nvl(sp: SPContext) -> bool:
@@ -175,6 +179,10 @@ def qkv_attention_forward(qkv, B: int, S: int, H: int, Dh: int, wq, wk, freqs, e
     if ulysses_nvl(sp):
         o, rq, rk, saved = sp.comm.uly_forward(qkv, B, S, H, Dh, wq, wk, freqs, eps, do_norm)
         return o, rq, rk, None, None, saved
+    if ring_nvl(sp):
+        o, q, rq, rk, saved = sp.comm.ring_forward(qkv[:, :HD], qkv[:, HD:2 * HD], qkv[:, 2 * HD:], B, S, H, Dh,
+                                                   wq, wk, freqs, eps, do_norm)
+        return o, rq, rk, q, None, saved
     q, k, rq, rk = Fn.qknorm_rope_fwd(qkv, H, Dh, wq, wk, freqs, eps, do_norm=do_norm)
     o, saved = sp_attention_forward(q, k, qkv[:, 2 * HD:], B, S, H, Dh, sp)
     return o, rq, rk, q, k, saved
@@ -194,6 +202,12 @@ def qkv_attention_backward(saved, qkv, q, k, o, do, rq, rk, wq, wk, freqs, do_no
         return g, dwq, dwk
     if dqkv is None:
         dqkv = torch.empty(B * S, 3 * HD, device=qkv.device, dtype=qkv.dtype)
+    if ring_nvl(sp):
+        # dK|dV land summed in dqkv[:, HD:3HD]; d(post-RoPE k) -> d(pre-norm k) in place
+        dq, _ = sp.comm.ring_backward(saved, q, o, do, B, S, H, Dh, out=dqkv[:, HD:], out_ld=3 * HD)
+        dwq, dwk = Fn.qknorm_rope_bwd(dq, dqkv[:, HD:2 * HD], qkv, rq, rk, H, Dh, wq, wk, freqs, do_norm, dqkv,
+                                      want_dw=do_norm)
+        return dqkv, dwq, dwk
     dq, dk = sp_attention_backward(saved, q, k, qkv[:, 2 * HD:], o, do, B, S, H, Dh, sp, dv_out=dqkv[:, 2 * HD:])
     dwq, dwk = Fn.qknorm_rope_bwd(dq, dk, qkv, rq, rk, H, Dh, wq, wk, freqs, do_norm, dqkv, want_dw=do_norm)
     return dqkv, dwq, dwk

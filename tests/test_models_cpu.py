@@ -222,6 +222,32 @@ def test_ring_attention_ops_match_sdpa():
         ring_ops.CPURingAttention.apply(q, k, v, 2)
 
 
+def test_ring_attention_ops_any_scale_and_saved_statistics():
+    """The op pair with a non-default softmax scale; the backward takes the
+    LSE (m_i, l_i) and D from its arguments."""
+    from harp_b200.ops import ring_ops
+
+    ring_ops.set_sp_context(None)
+    g = torch.Generator().manual_seed(5)
+    B, T, H, D = 2, 40, 3, 16
+    scale = 0.37
+    q, k, v = (torch.randn(B, T, H, D, generator=g).bfloat16().transpose(1, 2) for _ in range(3))
+    out = torch.zeros(B, H, T, D)
+    m_i = torch.empty(B, H, T, 1, dtype=torch.bfloat16)
+    l_i = torch.empty(B, H, T, 1)
+    torch.ops.ring_attention_ops.ring_attention_forward(q, k, v, out, m_i, l_i, 1, scale)
+    qr, kr, vr = (t.float().requires_grad_(True) for t in (q, k, v))
+    ref = F.scaled_dot_product_attention(qr, kr, vr, scale=scale)
+    torch.testing.assert_close(out, ref.detach(), rtol=2e-2, atol=2e-2)
+    do = torch.randn(B, H, T, D, generator=g).bfloat16()
+    ref.backward(do.float())
+    Dt = (do.float() * out).sum(-1, keepdim=True)
+    gq, gk, gv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    torch.ops.ring_attention_ops.ring_attention_backward(q, gq, k, gk, v, gv, do, m_i, l_i, Dt, 1, scale)
+    for a, b in ((gq, qr), (gk, kr), (gv, vr)):
+        torch.testing.assert_close(a.float(), b.grad, rtol=5e-2, atol=5e-2)
+
+
 def test_timestep_embeddings_closed_form():
     from harp_b200.models import embedding as E
 
