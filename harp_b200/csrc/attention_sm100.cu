@@ -1129,6 +1129,18 @@ __global__ void __launch_bounds__(kBwdThreads1, 1)
 // The Q/dO stage of tile i goes back to the TMA warp when dV(i) and dK(i) are
 // done; dQ partials are staged in a buffer of their own for the TMA reduce.
 // ===========================================================================
+// Row d0..d0+15 of a thread's fp32 dQ partial (from one 16-column TMEM load)
+// into its staging row; columns at or past Dh are not stored.
+__device__ __forceinline__ void stage_row16(float* srow, int d0, const uint32_t (&v)[16], int Dh) {
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    const int d = d0 + 4 * g;
+    if (d < Dh)
+      *reinterpret_cast<float4*>(srow + d) = make_float4(__uint_as_float(v[4 * g]), __uint_as_float(v[4 * g + 1]),
+                                                         __uint_as_float(v[4 * g + 2]), __uint_as_float(v[4 * g + 3]));
+  }
+}
+
 template <int NCH>
 struct BwdPipeCfg {
   static constexpr int DPAD = NCH * 8;
@@ -1136,8 +1148,8 @@ struct BwdPipeCfg {
   static constexpr int PS_BYTES = 128 * 128 * 2;  // one 128 x 128 bf16 operand (P^T or dS)
   static constexpr int LD_BYTES = 2 * 256 * 4;     // lse | delta of a query tile, double-buffered
   // 256 bytes of slack align the swizzled tiles (the 32-byte swizzle repeats
-  // every 256 B); 128 bytes hold the 15 barriers and the TMEM address.
-  static constexpr int smem_for(int st) { return 2 * TILE + st * 2 * TILE + 2 * PS_BYTES + LD_BYTES + 256 + 128; }
+  // every 256 B); 256 bytes hold the barriers and the TMEM address.
+  static constexpr int smem_for(int st) { return 2 * TILE + st * 2 * TILE + 2 * PS_BYTES + LD_BYTES + 256 + 256; }
   static constexpr int STAGES = smem_for(3) <= 232448 ? 3 : 2;
   static constexpr int SMEM = smem_for(STAGES);
   static_assert(SMEM <= 232448, "exceeds the 227 KB per-CTA shared memory limit");
@@ -1183,10 +1195,10 @@ __global__ void __launch_bounds__(kBwdPipeThreads, 1)
   uint64_t* p_free = p_full + 1;
   uint64_t* dq_full = p_free + 1;
   uint64_t* dq_free = dq_full + 1;
-  uint64_t* dqs_bar = dq_free + 1;
-  uint64_t* fin = dqs_bar + 1;
+  uint64_t* dqs_bar = dq_free + 1;  // [ST]: dQ of the tile in stage st is staged
+  uint64_t* fin = dqs_bar + ST;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fin + 1);
-  static_assert((1 + 2 * ST + 8) * 8 + 4 <= 128, "barrier region");
+  static_assert((1 + 3 * ST + 7) * 8 + 4 <= 256, "barrier region");
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int nkt = (a.Skv + 127) / 128;
@@ -1208,7 +1220,7 @@ __global__ void __launch_bounds__(kBwdPipeThreads, 1)
     mbar_init(p_free, 1);
     mbar_init(dq_full, 1);
     mbar_init(dq_free, 4);
-    mbar_init(dqs_bar, 4);
+    for (int st2 = 0; st2 < ST; ++st2) mbar_init(&dqs_bar[st2], 4);
     mbar_init(fin, 1);
     fence_mbar_init();
   }
@@ -1304,6 +1316,26 @@ __global__ void __launch_bounds__(kBwdPipeThreads, 1)
       if (ok && nq > 0) ok = rest(nq - 1);
       mma_commit(fin);
       mbar_wait_drain(fin, 0);
+    }
+   } else if (warp == 2) {
+    // dQ reducer: once the four dQ warps have staged tile i's fp32 partial in
+    // its Q/dO stage, reduce-add it into dq_acc with one TMA, and give the
+    // stage back to the TMA warp when the copy engine has read it.  Keeping
+    // this wait off the dQ warps lets them stage tile i+1 meanwhile.
+    if (lane == 0) {
+      bool ok = true;
+      for (int i = 0; i < nq; ++i) {
+        const int st = i % ST;
+        if (!mbar_wait(&dqs_bar[st], (i / ST) & 1, err, 182)) ok = false;
+        if (ok) {
+          BWD_PROBE(i, 7);
+          tma_reduce_add_4d(&tmdQ, reinterpret_cast<float*>(sQD + 2 * st * C::TILE), 0, h, i * 128, b);
+          bulk_wait_read_all();
+          BWD_PROBE(i, 9);
+        }
+        mbar_arrive(&qdo_empty[st]);
+      }
+      bulk_wait_all();
     }
    }
   } else if (wg == 1 || wg == 2) {
@@ -1436,39 +1468,34 @@ __global__ void __launch_bounds__(kBwdPipeThreads, 1)
       const int st = i % ST;
       float* stage = reinterpret_cast<float*>(sQD + 2 * st * C::TILE);  // [128][Dh] fp32
       float* srow = stage + qr * a.Dh;
-#pragma unroll
-      for (int c = 0; c < C::DPAD; c += 16) {
-        uint32_t v[16];
-        tmem_ld16(tdQ + lane_off + c, v);
+      // the dQ row (64 or 80 columns) in two TMEM round trips: columns 0-47,
+      // then the rest
+      {
+        uint32_t v0[16], v1[16], v2[16];
+        tmem_ld16(tdQ + lane_off, v0);
+        tmem_ld16(tdQ + lane_off + 16, v1);
+        tmem_ld16(tdQ + lane_off + 32, v2);
         tmem_wait_ld();
-#pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          const int d = c + 4 * g;
-          if (d < a.Dh)
-            *reinterpret_cast<float4*>(srow + d) =
-                make_float4(__uint_as_float(v[4 * g]), __uint_as_float(v[4 * g + 1]), __uint_as_float(v[4 * g + 2]),
-                            __uint_as_float(v[4 * g + 3]));
-        }
+        stage_row16(srow, 0, v0, a.Dh);
+        stage_row16(srow, 16, v1, a.Dh);
+        stage_row16(srow, 32, v2, a.Dh);
+      }
+      {
+        uint32_t v0[16], v1[16];
+        tmem_ld16(tdQ + lane_off + 48, v0);
+        if (C::DPAD > 64) tmem_ld16(tdQ + lane_off + 64, v1);
+        tmem_wait_ld();
+        stage_row16(srow, 48, v0, a.Dh);
+        if (C::DPAD > 64) stage_row16(srow, 64, v1, a.Dh);
       }
       tc_fence_before();
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(dq_free);
-        mbar_arrive(dqs_bar);
-      }
-      if (warp == 12 && lane == 0) {
-        if (!mbar_wait(dqs_bar, i & 1, err, 182)) ok = false;
-        if (ok) {
-          BWD_PROBE(i, 7);
-          tma_reduce_add_4d(&tmdQ, stage, 0, h, i * 128, b);
-          bulk_wait_read_all();
-          BWD_PROBE(i, 9);
-        }
-        mbar_arrive(&qdo_empty[st]);  // the stage goes back to the TMA warp
+        mbar_arrive(&dqs_bar[st]);  // warp 2 reduce-adds the staged tile
       }
     }
-    if (warp == 12 && lane == 0) bulk_wait_all();
     if (ok) ok = mbar_wait(fin, 0, err, 181);
     tc_fence_after();
     const int key = k0 + qr;
@@ -1579,10 +1606,10 @@ __global__ void __launch_bounds__(kBwdQ64Threads, 1)
   uint64_t* p_free = p_full + 1;
   uint64_t* dq_full = p_free + 1;   // [2]
   uint64_t* dq_free = dq_full + 2;  // [2]
-  uint64_t* dqs_bar = dq_free + 2;
-  uint64_t* fin = dqs_bar + 1;
+  uint64_t* dqs_bar = dq_free + 2;  // [ST]: dQ of the tile in stage st is staged
+  uint64_t* fin = dqs_bar + ST;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fin + 1);
-  static_assert((1 + 2 * ST + 4 + 4 + 2) * 8 + 4 <= 256, "barrier region");
+  static_assert((1 + 3 * ST + 4 + 4 + 1) * 8 + 4 <= 256, "barrier region");
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int nkt = (a.Skv + 127) / 128;
@@ -1606,7 +1633,7 @@ __global__ void __launch_bounds__(kBwdQ64Threads, 1)
       mbar_init(&dq_full[s], 1);
       mbar_init(&dq_free[s], 4);
     }
-    mbar_init(dqs_bar, 4);
+    for (int s = 0; s < ST; ++s) mbar_init(&dqs_bar[s], 4);
     mbar_init(fin, 1);
     fence_mbar_init();
   }
@@ -1696,6 +1723,23 @@ __global__ void __launch_bounds__(kBwdQ64Threads, 1)
       if (ok && nq > 0) ok = rest(nq - 1);
       mma_commit(fin);
       mbar_wait_drain(fin, 0);
+    }
+  } else if (warp == 2) {
+    // dQ reducer: once the four dQ warps have staged tile i's [64 x Dh] fp32
+    // partial in its Q/dO stage, reduce-add it into dq_acc (rows past Sq are
+    // clipped by TMA) and give the stage back to the TMA warp once read
+    if (lane == 0) {
+      bool ok = true;
+      for (int i = 0; i < nq; ++i) {
+        const int st = i % ST;
+        if (!mbar_wait(&dqs_bar[st], (i / ST) & 1, err, 282)) ok = false;
+        if (ok) {
+          tma_reduce_add_4d(&tmdQ, reinterpret_cast<float*>(sQD + 2 * st * C::QTILE), 0, h, i * 64, b);
+          bulk_wait_read_all();
+        }
+        mbar_arrive(&qdo_empty[st]);
+      }
+      bulk_wait_all();
     }
   } else if (wg == 1 || wg == 2) {
     // ---------------- dS warps: thread = key row, 32 of the 64 query columns ----------------
@@ -1818,19 +1862,9 @@ __global__ void __launch_bounds__(kBwdQ64Threads, 1)
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(&dq_free[slot]);
-        mbar_arrive(dqs_bar);
-      }
-      if (warp == 12 && lane == 0) {
-        // when all four dQ warps staged their columns, reduce-add the [64 x Dh]
-        // tile into dq_acc (rows past Sq are clipped by TMA), then give the
-        // stage back to the TMA producer
-        if (!mbar_wait(dqs_bar, i & 1, err, 282)) { ok = false; break; }
-        tma_reduce_add_4d(&tmdQ, stage, 0, h, i * 64, b);
-        bulk_wait_read_all();
-        mbar_arrive(&qdo_empty[st]);
+        mbar_arrive(&dqs_bar[st]);  // warp 2 reduce-adds the staged tile
       }
     }
-    if (warp == 12 && lane == 0) bulk_wait_all();
     if (ok) ok = mbar_wait(fin, 0, err, 281);
     tc_fence_after();
     const int kr = quarter * 32 + lane;

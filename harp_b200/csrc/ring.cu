@@ -134,6 +134,74 @@ __global__ void ring_dispatch_qkv_kernel(const bf16* __restrict__ qsrc, long ldq
   __threadfence_system();
 }
 
+// Staged form (head_dim in {64, 72, 80, 96, 128}, 16-byte aligned rows).  A
+// block takes kRingRows consecutive local rows: one thread per (row, head,
+// q|k|v) normalises and rotates a head held in DH/8 16-byte registers; q goes
+// straight to q_out, k and v to a shared-memory tile laid out exactly as the
+// destination rows (K | V, 2*H*DH per row).  The tile is then copied to every
+// rank with consecutive threads storing consecutive 16-byte pieces, so each
+// warp writes 512 contiguous bytes of a peer's buffer per instruction (rows
+// of one sample are contiguous there too).  first_which = 1 skips q.
+constexpr int kRingRows = 8;
+template <int DH>
+__global__ void __launch_bounds__(256) ring_dispatch_staged_kernel(
+    const bf16* __restrict__ qsrc, long ldq_in, const bf16* __restrict__ ksrc, long ldk_in,
+    const bf16* __restrict__ vsrc, long ldv_in, int R, int S, int H, int rank, int W, PeerTable dst, long long dst_ld,
+    bf16* __restrict__ q_out, long ldq, const bf16* __restrict__ wq, const bf16* __restrict__ wk,
+    const float2* __restrict__ freqs, int freq_rows, float eps, int do_norm, float* __restrict__ rstd_q,
+    float* __restrict__ rstd_k, int first_which) {
+  constexpr int NC = DH / 8;
+  extern __shared__ uint4 tile[];  // [kRingRows][2*H*DH / 8]
+  const int HD = H * DH;
+  const int row0 = blockIdx.x * kRingRows;
+  const int nrows = min(kRingRows, R - row0);
+  const int nitems = nrows * H * (3 - first_which);
+  for (int it = threadIdx.x; it < nitems; it += blockDim.x) {
+    const int which = first_which + it / (nrows * H);
+    const int rem = it % (nrows * H);
+    const int rl = rem / H, h = rem % H;
+    const int row = row0 + rl;
+    const long long item = (long long)row * H + h;
+    const float2* fr = freqs ? freqs + (long long)(row % freq_rows) * (DH / 2) : nullptr;
+    uint4 o[NC];
+    if (which == 2) {
+      const bf16* src = vsrc + (long long)row * ldv_in + (long long)h * DH;
+#pragma unroll
+      for (int c = 0; c < NC; ++c) o[c] = *reinterpret_cast<const uint4*>(src + 8 * c);
+    } else {
+      const bf16* src = (which ? ksrc + (long long)row * ldk_in : qsrc + (long long)row * ldq_in) + (long long)h * DH;
+      float* rs_out = which ? (rstd_k ? rstd_k + item : nullptr) : (rstd_q ? rstd_q + item : nullptr);
+      norm_rope_vec<DH>(src, which ? wk : wq, fr, eps, do_norm != 0, rs_out, o);
+    }
+    if (which == 0) {
+      bf16* d = q_out + (long long)row * ldq + (long long)h * DH;
+#pragma unroll
+      for (int c = 0; c < NC; ++c) *reinterpret_cast<uint4*>(d + 8 * c) = o[c];
+    } else {
+      uint4* t = tile + (long long)rl * (2 * HD / 8) + (which == 1 ? 0 : HD / 8) + h * NC;
+#pragma unroll
+      for (int c = 0; c < NC; ++c) t[c] = o[c];
+    }
+  }
+  __syncthreads();
+  const int vpr = 2 * HD / 8;  // 16-byte pieces per row
+  const int nv = nrows * vpr;
+  for (int jj = 0; jj < W; ++jj) {
+    const int j = (rank + 1 + jj) % W;
+    bf16* base = reinterpret_cast<bf16*>(dst.base[j]);
+    for (int v = threadIdx.x; v < nv; v += blockDim.x) {
+      const int rl = v / vpr, c = v % vpr;
+      const int row = row0 + rl;
+      const int b = row / S, s = row % S;
+      const long long drow = ((long long)b * W + rank) * S + s;
+      *reinterpret_cast<uint4*>(base + drow * dst_ld + 8LL * c) = tile[v];
+    }
+  }
+  __threadfence_system();
+}
+
+bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
 }  // namespace
 
 void ring_dispatch_qkv(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, int64_t S, int64_t H,
@@ -162,6 +230,45 @@ void ring_dispatch_qkv(const at::Tensor& q, const at::Tensor& k, const at::Tenso
   const long long items = R * H;
   const int grid = (int)std::min<long long>((items + 7) / 8, (long long)num_sms() * 8);
   auto bp = [](const at::Tensor& t) { return reinterpret_cast<const bf16*>(t.data_ptr()); };
+  bool vec_ok = (Dh == 64 || Dh == 72 || Dh == 80 || Dh == 96 || Dh == 128) && dst_ld % 8 == 0 &&
+                q.stride(0) % 8 == 0 && k.stride(0) % 8 == 0 && v.stride(0) % 8 == 0 && al16(q.data_ptr()) &&
+                al16(k.data_ptr()) && al16(v.data_ptr()) &&
+                (!q_out.has_value() || (q_out->stride(0) % 8 == 0 && al16(q_out->data_ptr()))) &&
+                (!wq.has_value() || al16(wq->data_ptr())) && (!wk.has_value() || al16(wk->data_ptr())) &&
+                (!freqs.has_value() || al16(freqs->data_ptr()));
+  for (int64_t b : dst_bases) vec_ok = vec_ok && (b & 15) == 0;
+  const size_t tile_bytes = (size_t)kRingRows * 2 * H * Dh * 2;
+  vec_ok = vec_ok && tile_bytes <= 200 * 1024;
+  if (vec_ok) {
+    const int first = q_out.has_value() ? 0 : 1;
+    const unsigned sgrid = (unsigned)((R + kRingRows - 1) / kRingRows);
+#define HARP_RING_STAGED(DHV)                                                                                       \
+  if (Dh == DHV) {                                                                                                  \
+    static bool attr = false;                                                                                       \
+    if (!attr) {                                                                                                    \
+      C10_CUDA_CHECK(cudaFuncSetAttribute(ring_dispatch_staged_kernel<DHV>,                                         \
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));                \
+      attr = true;                                                                                                  \
+    }                                                                                                               \
+    ring_dispatch_staged_kernel<DHV><<<sgrid, threads, tile_bytes, at::cuda::getCurrentCUDAStream()>>>(             \
+        bp(q), q.stride(0), bp(k), k.stride(0), bp(v), v.stride(0), (int)R, (int)S, (int)H, (int)rank, W,           \
+        make_table(dst_bases, 0), dst_ld, q_out.has_value() ? reinterpret_cast<bf16*>(q_out->data_ptr()) : nullptr, \
+        q_out.has_value() ? q_out->stride(0) : 0, wq.has_value() ? bp(*wq) : nullptr,                               \
+        wk.has_value() ? bp(*wk) : nullptr,                                                                          \
+        freqs.has_value() ? reinterpret_cast<const float2*>(freqs->data_ptr<float>()) : nullptr, (int)freq_rows,    \
+        (float)eps, do_norm ? 1 : 0, rstd_q.has_value() ? rstd_q->data_ptr<float>() : nullptr,                      \
+        rstd_k.has_value() ? rstd_k->data_ptr<float>() : nullptr, first);                                           \
+  }
+    HARP_RING_STAGED(64)
+    HARP_RING_STAGED(72)
+    HARP_RING_STAGED(80)
+    HARP_RING_STAGED(96)
+    HARP_RING_STAGED(128)
+#undef HARP_RING_STAGED
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    count_launch();
+    return;
+  }
   ring_dispatch_qkv_kernel<<<grid, threads, 0, at::cuda::getCurrentCUDAStream()>>>(
       bp(q), q.stride(0), bp(k), k.stride(0), bp(v), v.stride(0), (int)R, (int)S, (int)H, (int)Dh, (int)rank, W,
       make_table(dst_bases, 0), dst_ld, q_out.has_value() ? reinterpret_cast<bf16*>(q_out->data_ptr()) : nullptr,

@@ -77,6 +77,68 @@ __global__ void uly_dispatch_qkv_kernel(const bf16* __restrict__ qkv, long ld, i
   __threadfence_system();
 }
 
+// Staged form of uly_dispatch_qkv_kernel (head_dim in {64, 72, 80, 96, 128},
+// 16-byte aligned rows).  A block takes kUlyRows consecutive local rows: one
+// thread per (row, head, q|k|v) normalises and rotates a head held in DH/8
+// 16-byte registers into a shared-memory tile [row][q|k|v][H*DH]; the tile is
+// then copied out part by part and rank by rank with consecutive threads
+// storing consecutive 16-byte pieces: rank j's heads of one row are Hn*DH
+// contiguous elements of its buffer, and consecutive rows of one sample are
+// consecutive there, so each warp writes contiguous runs of a peer's buffer.
+constexpr int kUlyRows = 8;
+template <int DH>
+__global__ void __launch_bounds__(256) uly_dispatch_staged_kernel(const bf16* __restrict__ qkv, long ld, int R, int S,
+                                                                  int H, int Hn, int rank, int W, PeerTable dst,
+                                                                  long long part, const bf16* __restrict__ wq,
+                                                                  const bf16* __restrict__ wk,
+                                                                  const float2* __restrict__ freqs, int freq_rows,
+                                                                  float eps, int do_norm, float* __restrict__ rstd_q,
+                                                                  float* __restrict__ rstd_k) {
+  constexpr int NC = DH / 8;
+  extern __shared__ uint4 tile[];  // [kUlyRows][3][H*DH / 8]
+  const int HD = H * DH;
+  const int row0 = blockIdx.x * kUlyRows;
+  const int nrows = min(kUlyRows, R - row0);
+  const int nitems = nrows * H * 3;
+  for (int it = threadIdx.x; it < nitems; it += blockDim.x) {
+    const int which = it / (nrows * H);
+    const int rem = it % (nrows * H);
+    const int rl = rem / H, h = rem % H;
+    const int row = row0 + rl;
+    const float2* fr = freqs ? freqs + (long long)(row % freq_rows) * (DH / 2) : nullptr;
+    const bf16* src = qkv + (long long)row * ld + (long long)which * HD + (long long)h * DH;
+    const long long rid = (long long)row * H + h;
+    uint4 o[NC];
+    if (which == 2) {
+#pragma unroll
+      for (int c = 0; c < NC; ++c) o[c] = *reinterpret_cast<const uint4*>(src + 8 * c);
+    } else {
+      float* rs_out = which ? (rstd_k ? rstd_k + rid : nullptr) : (rstd_q ? rstd_q + rid : nullptr);
+      norm_rope_vec<DH>(src, which ? wk : wq, fr, eps, do_norm != 0, rs_out, o);
+    }
+    uint4* t = tile + ((long long)rl * 3 + which) * (HD / 8) + h * NC;
+#pragma unroll
+    for (int c = 0; c < NC; ++c) t[c] = o[c];
+  }
+  __syncthreads();
+  const int vr = Hn * DH / 8;  // 16-byte pieces of one rank's heads in one row
+  const int nv = nrows * vr;
+  for (int jj = 0; jj < W; ++jj) {
+    const int j = (rank + 1 + jj) % W;
+    bf16* base = reinterpret_cast<bf16*>(dst.base[j]);
+    for (int pp = 0; pp < 3; ++pp) {
+      for (int v = threadIdx.x; v < nv; v += blockDim.x) {
+        const int rl = v / vr, c = v % vr;
+        const int row = row0 + rl;
+        const int b = row / S, s = row % S;
+        const long long off = (long long)pp * part + ((long long)b * W * S + (long long)rank * S + s) * (Hn * DH);
+        *reinterpret_cast<uint4*>(base + off + 8LL * c) = tile[((long long)rl * 3 + pp) * (HD / 8) + j * vr + c];
+      }
+    }
+  }
+  __threadfence_system();
+}
+
 struct RemapSrc {
   const bf16* p[3];
   long long ld[3];
@@ -147,6 +209,39 @@ void uly_dispatch_qkv(const at::Tensor& qkv, int64_t S, int64_t H, int64_t Dh, i
   const at::cuda::CUDAGuard g(qkv.device());
   const int threads = 256;
   const long long items = R * H;
+  auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  bool vec_ok = (Dh == 64 || Dh == 72 || Dh == 80 || Dh == 96 || Dh == 128) && qkv.stride(0) % 8 == 0 &&
+                part % 8 == 0 && al16(qkv.data_ptr()) && (!wq.has_value() || al16(wq->data_ptr())) &&
+                (!wk.has_value() || al16(wk->data_ptr())) && (!freqs.has_value() || al16(freqs->data_ptr()));
+  for (int64_t bse : dst_bases) vec_ok = vec_ok && (bse & 15) == 0;
+  const size_t tile_bytes = (size_t)kUlyRows * 3 * H * Dh * 2;
+  vec_ok = vec_ok && tile_bytes <= 200 * 1024 && (H / W) * Dh % 8 == 0;
+  if (vec_ok) {
+    const unsigned sgrid = (unsigned)((R + kUlyRows - 1) / kUlyRows);
+#define HARP_ULY_STAGED(DHV)                                                                                       \
+  if (Dh == DHV) {                                                                                                 \
+    static bool attr = false;                                                                                      \
+    if (!attr) {                                                                                                   \
+      C10_CUDA_CHECK(cudaFuncSetAttribute(uly_dispatch_staged_kernel<DHV>,                                         \
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));               \
+      attr = true;                                                                                                 \
+    }                                                                                                              \
+    uly_dispatch_staged_kernel<DHV><<<sgrid, threads, tile_bytes, at::cuda::getCurrentCUDAStream()>>>(             \
+        cbp(qkv), qkv.stride(0), (int)R, (int)S, (int)H, (int)(H / W), (int)rank, W, make_table(dst_bases, 0), part, \
+        cbpo(wq), cbpo(wk), freqs.has_value() ? reinterpret_cast<const float2*>(freqs->data_ptr<float>()) : nullptr, \
+        (int)freq_rows, (float)eps, do_norm ? 1 : 0, rstd_q.has_value() ? rstd_q->data_ptr<float>() : nullptr,      \
+        rstd_k.has_value() ? rstd_k->data_ptr<float>() : nullptr);                                                  \
+  }
+    HARP_ULY_STAGED(64)
+    HARP_ULY_STAGED(72)
+    HARP_ULY_STAGED(80)
+    HARP_ULY_STAGED(96)
+    HARP_ULY_STAGED(128)
+#undef HARP_ULY_STAGED
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    count_launch();
+    return;
+  }
   const int grid = (int)std::min<long long>((items + 7) / 8, (long long)num_sms() * 8);
   uly_dispatch_qkv_kernel<<<grid, threads, 0, at::cuda::getCurrentCUDAStream()>>>(
       cbp(qkv), qkv.stride(0), (int)R, (int)S, (int)H, (int)Dh, (int)(H / W), (int)rank, W, make_table(dst_bases, 0),
