@@ -1169,7 +1169,16 @@ constexpr int kPipeRegsCtl = 88, kPipeRegsDs = 168, kPipeRegsDq = 88;
 static_assert(kPipeRegsCtl + 2 * kPipeRegsDs + kPipeRegsDq == 4 * (65536 / kBwdPipeThreads),
               "warpgroup register split must add up to the launch budget");
 
-template <int NCH>
+// FOLD (head_dim + 2 <= DPAD, e.g. 72 in 80): the softmax statistics ride in
+// the zero padding of the head dim.  Columns Dh, Dh+1 of K and V are set to 1
+// once; those of each Q tile hold -lse/scale split into a bf16 high and low
+// part, those of each dO tile -delta likewise (warp 3 writes them after the
+// tile lands).  The MMAs then produce S - lse/scale and dP - delta directly
+// (fp32 accumulation of exact bf16 products), so the dS warps read no
+// per-query statistics from shared memory, whose bandwidth the tensor core
+// saturates while they run.  The padding columns of dV, dK and dQ take the
+// products of these columns and are never stored.
+template <int NCH, bool FOLD>
 __global__ void __launch_bounds__(kBwdPipeThreads, 1)
     attn_bwd_pipe_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                          const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
@@ -1197,8 +1206,9 @@ __global__ void __launch_bounds__(kBwdPipeThreads, 1)
   uint64_t* dq_free = dq_full + 1;
   uint64_t* dqs_bar = dq_free + 1;  // [ST]: dQ of the tile in stage st is staged
   uint64_t* fin = dqs_bar + ST;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fin + 1);
-  static_assert((1 + 3 * ST + 7) * 8 + 4 <= 256, "barrier region");
+  uint64_t* q_ready = fin + 1;  // [ST] (FOLD): the tile's statistics columns are written
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(q_ready + ST);
+  static_assert((1 + 4 * ST + 7) * 8 + 4 <= 256, "barrier region");
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int nkt = (a.Skv + 127) / 128;
@@ -1222,6 +1232,7 @@ __global__ void __launch_bounds__(kBwdPipeThreads, 1)
     mbar_init(dq_free, 4);
     for (int st2 = 0; st2 < ST; ++st2) mbar_init(&dqs_bar[st2], 4);
     mbar_init(fin, 1);
+    for (int st2 = 0; st2 < ST; ++st2) mbar_init(&q_ready[st2], 1);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -1299,7 +1310,7 @@ __global__ void __launch_bounds__(kBwdPipeThreads, 1)
       for (int i = 0; i < nq && ok; ++i) {
         const int st = i % ST;
         const uint32_t ph = (i / ST) & 1;
-        if (!mbar_wait(&qdo_full[st], ph, err, 161)) { ok = false; break; }
+        if (!mbar_wait(FOLD ? &q_ready[st] : &qdo_full[st], ph, err, 161)) { ok = false; break; }
         if (i > 0 && !mbar_wait(s_free, (i - 1) & 1, err, 162)) { ok = false; break; }
         tc_fence_after();
         const uint32_t qa = smem_u32(sQD + 2 * st * C::TILE), doa = smem_u32(sQD + (2 * st + 1) * C::TILE);
@@ -1337,6 +1348,57 @@ __global__ void __launch_bounds__(kBwdPipeThreads, 1)
       }
       bulk_wait_all();
     }
+   } else if (FOLD && warp == 3) {
+    // statistics writer: padding columns Dh, Dh+1 (atom Dh/16, 16-byte chunk
+    // (Dh%16)/8 of the 32-byte swizzled row: chunk bit XOR row bit 2)
+    const int atom = a.Dh / 16, chunk = (a.Dh % 16) / 8;
+    auto pad_word = [&](uint8_t* tile, int r) -> uint32_t* {
+      return reinterpret_cast<uint32_t*>(tile + atom * 4096 + r * 32 + ((chunk ^ ((r >> 2) & 1)) * 16));
+    };
+    auto split = [](float x) -> uint32_t {  // bf16 high part | low part of x
+      const float hi = __bfloat162float(__float2bfloat16_rn(x));
+      const float lo = isfinite(x) ? x - hi : 0.f;
+      return pack_bf16x2(hi, lo);
+    };
+    bool ok = mbar_wait(kv_full, 0, err, 190);
+    const uint32_t ones = pack_bf16x2(1.f, 1.f);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      *pad_word(sK, lane + 32 * j) = ones;
+      *pad_word(sV, lane + 32 * j) = ones;
+    }
+    const float* lrow = a.lse + (long)(b * a.H + h) * a.lse_ld;
+    const float* drow = a.delta + (long)(b * a.H + h) * a.lse_ld;
+    const float inv_scale = 1.f / a.scale;
+    float nl[4], nd[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      nl[j] = __ldg(lrow + lane + 32 * j);
+      nd[j] = __ldg(drow + lane + 32 * j);
+    }
+    for (int i = 0; i < nq; ++i) {
+      const int st = i % ST;
+      if (!mbar_wait(&qdo_full[st], (i / ST) & 1, err, 191)) ok = false;
+      uint8_t* qt = sQD + 2 * st * C::TILE;
+      uint8_t* dt = qt + C::TILE;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        // lse is +inf past Sq: -inf there makes those queries' P exactly 0
+        *pad_word(qt, lane + 32 * j) = split(-nl[j] * inv_scale);
+        *pad_word(dt, lane + 32 * j) = split(-nd[j]);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&q_ready[st]);
+      if (i + 1 < nq) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          nl[j] = __ldg(lrow + (i + 1) * 128 + lane + 32 * j);
+          nd[j] = __ldg(drow + (i + 1) * 128 + lane + 32 * j);
+        }
+      }
+    }
+    (void)ok;
    }
   } else if (wg == 1 || wg == 2) {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kPipeRegsDs));
@@ -1355,14 +1417,14 @@ __global__ void __launch_bounds__(kBwdPipeThreads, 1)
     const float* ld_src = (ldt < 128 ? a.lse : a.delta) + (long)(b * a.H + h) * a.lse_ld + (ldt & 127);
     // All eight dS warps run every iteration (errors only make the bounded
     // waits return at once), so the named barrier always sees 256 threads.
-    // lse / delta of a tile's 128 queries (+inf / 0 past Sq) go to the buffer
-    // of the tile's parity: tile 0's now, tile i+1's (loaded during tile i) at
-    // the end of tile i.  The barrier at the top of tile i makes the writes
-    // visible and means every dS warp is done with tile i-2, the buffer's
-    // previous user.
-    sLD[ldt] = __ldg(ld_src);
+    // Without FOLD, lse / delta of a tile's 128 queries (+inf / 0 past Sq) go
+    // to the buffer of the tile's parity: tile 0's now, tile i+1's (loaded
+    // during tile i) at the end of tile i.  The barrier at the top of tile i
+    // makes the writes visible and means every dS warp is done with tile i-2,
+    // the buffer's previous user.
+    if (!FOLD) sLD[ldt] = __ldg(ld_src);
     for (int i = 0; i < nq; ++i) {
-      const float ld_next = (i + 1 < nq) ? __ldg(ld_src + (i + 1) * 128) : 0.f;
+      const float ld_next = (!FOLD && i + 1 < nq) ? __ldg(ld_src + (i + 1) * 128) : 0.f;
       const float* ldb = sLD + (i & 1) * 256;
       asm volatile("bar.sync 2, 256;" ::: "memory");
       if (!mbar_wait(s_full, i & 1, err, 170)) ok = false;
@@ -1383,6 +1445,21 @@ __global__ void __launch_bounds__(kBwdPipeThreads, 1)
       const float* sL = ldb;
       const float* sDl = ldb + 128;
       uint32_t pp[2][16], dd[2][16];
+      if (FOLD) {
+        // S and dP arrive as S - lse/scale and dP - delta
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc)
+#pragma unroll
+          for (int k2 = 0; k2 < 16; ++k2) {
+            const float2 x =
+                __fmul2_rn(make_float2(__uint_as_float(s[cc][2 * k2]), __uint_as_float(s[cc][2 * k2 + 1])), scl);
+            const float2 p = __fmul2_rn(make_float2(ex2_approx(x.x), ex2_approx(x.y)), kmask);
+            const float2 ds =
+                __fmul2_rn(p, make_float2(__uint_as_float(dp[cc][2 * k2]), __uint_as_float(dp[cc][2 * k2 + 1])));
+            pp[cc][k2] = pack_bf16x2(p.x, p.y);
+            dd[cc][k2] = pack_bf16x2(ds.x, ds.y);
+          }
+      } else {
 #pragma unroll
       for (int cc = 0; cc < 2; ++cc) {
         const int c = c_begin + cc;
@@ -1406,6 +1483,7 @@ __global__ void __launch_bounds__(kBwdPipeThreads, 1)
           }
         }
       }
+      }
       if (warp == 4 && lane == 0) BWD_PROBE(i, 12);
       if (a.probe && blockIdx.x == 0 && warp == 4 && lane == 0 && i < 64) g_bwd_probe[i * 16 + 14] = clock64() - c_start;
       // the previous tile's dV/dK/dQ must be done reading P^T / dS
@@ -1426,7 +1504,7 @@ __global__ void __launch_bounds__(kBwdPipeThreads, 1)
       __syncwarp();
       if (warp == 4 && lane == 0) BWD_PROBE(i, 5);
       if (lane == 0) mbar_arrive(p_full);
-      sLD[((i + 1) & 1) * 256 + ldt] = ld_next;
+      if (!FOLD) sLD[((i + 1) & 1) * 256 + ldt] = ld_next;
     }
     if (wg == 1) {  // dV is stored by warpgroup 1
       if (ok) ok = mbar_wait(fin, 0, err, 172);
@@ -2031,20 +2109,23 @@ void launch_bwd(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap&
     // registers per thread (512 x 128 = the register file); with any other
     // count the increase could never be granted, so such a build keeps the
     // single-tile schedule.
-    static const bool pipe_ok = [] {
-      C10_CUDA_CHECK(
-          cudaFuncSetAttribute(attn_bwd_pipe_kernel<NCH>, cudaFuncAttributeMaxDynamicSharedMemorySize, P::SMEM));
+    auto setup = [](auto kern) {
+      C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, P::SMEM));
       cudaFuncAttributes fa;
-      C10_CUDA_CHECK(cudaFuncGetAttributes(&fa, attn_bwd_pipe_kernel<NCH>));
+      C10_CUDA_CHECK(cudaFuncGetAttributes(&fa, kern));
       const bool ok = fa.numRegs * kBwdPipeThreads == 65536;
       if (!ok)
         TORCH_WARN_ONCE("harp attention: pipelined backward built with ", fa.numRegs,
                         " registers per thread; using the single-tile schedule");
       return ok;
-    }();
+    };
+    static const bool pipe_ok =
+        setup(attn_bwd_pipe_kernel<NCH, false>) && setup(attn_bwd_pipe_kernel<NCH, true>);
+    const bool fold = args.Dh + 2 <= P::DPAD;
     if (bwd_pipe_enabled() && pipe_ok) {
       const int grid = args.B * args.H * ((args.Skv + 127) / 128);
-      attn_bwd_pipe_kernel<NCH><<<grid, kBwdPipeThreads, P::SMEM, stream>>>(mq, mk, mv, mdo, mdq, args);
+      auto* kern = fold ? attn_bwd_pipe_kernel<NCH, true> : attn_bwd_pipe_kernel<NCH, false>;
+      kern<<<grid, kBwdPipeThreads, P::SMEM, stream>>>(mq, mk, mv, mdo, mdq, args);
       C10_CUDA_KERNEL_LAUNCH_CHECK();
       count_launch();
       return;
