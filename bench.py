@@ -73,6 +73,8 @@ def parse():
                     help="sequence-parallel attention: K/V gather (ring) or head all-to-all (ulysses)")
     ap.add_argument("--comm", default="auto", choices=["auto", "torch", "nvl"])
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--shard-params", action="store_true",
+                    help="harp, N > 1: keep 1/N of every block's weights per GPU and gather them per block")
     ap.add_argument("--phases", action="store_true",
                     help="after the timed steps, run --steps more with per-phase CUDA events (forward, backward, "
                          "gradient sync, each sequence-parallel exchange and wait) and print their per-step device "
@@ -351,7 +353,8 @@ def main():
             loss_fn = M.mmdit_loss_local
         model.initialize_weights(seed=0)
         model = model.to(torch.bfloat16)
-        trainer = Trainer(model, par, TrainConfig(comm=args.comm, cuda_graph=bool(args.cuda_graph)), device,
+        trainer = Trainer(model, par, TrainConfig(comm=args.comm, cuda_graph=bool(args.cuda_graph),
+                                                  shard_params=args.shard_params and ws > 1), device,
                           sp_backend=args.sp_backend, sp_mode=args.sp_mode, loss_fn=loss_fn)
         cin, tdim = cfg.in_channels, cfg.text_dim
 
@@ -363,7 +366,8 @@ def main():
 
         count_launches = lambda: int(torch.ops.harp.launch_count())  # noqa: E731
         reset_launches = lambda: torch.ops.harp.reset_launch_count()  # noqa: E731
-        parallelism = f"sp{sp}" + (f"xdp{dp}" if dp > 1 else "") + (f"-{trainer.sp.mode}" if sp > 1 else "")
+        parallelism = (f"sp{sp}" + (f"xdp{dp}" if dp > 1 else "") + (f"-{trainer.sp.mode}" if sp > 1 else "") +
+                       ("-sharded-weights" if trainer.gatherer is not None else ""))
     else:
         sys.path.insert(0, os.path.join(ROOT, "baseline"))
         from baseline.dit_baseline import BaselineTrainer

@@ -149,10 +149,13 @@ struct AdamHyper {
 //   master, m, v <- AdamW(master, m, v, g)                 (fp32, local shard)
 //   param_c[lo + i] = bf16(master) for every rank c        (push)
 // Waits first for every peer's "gradients ready" flag.
+// local_out != nullptr (sharded parameters): the new bf16 slice is written
+// there (local_out[i - lo]) instead of being pushed to every rank.
 __global__ void rs_adamw_ag_kernel(PeerTable grads, PeerTable params, long long lo, long long n,
                                    float* __restrict__ master, float* __restrict__ m, float* __restrict__ v,
                                    AdamHyper h, int world, int rank, const unsigned int* flags, int flag_first,
-                                   unsigned int value, unsigned long long timeout_ns, int* err) {
+                                   unsigned int value, unsigned long long timeout_ns, int* err,
+                                   bf16* __restrict__ local_out) {
   if (flags != nullptr) {
     if (threadIdx.x < world && threadIdx.x != rank)
       wait_flag_geq(flags + flag_first + threadIdx.x, value, timeout_ns, err, 130 + threadIdx.x);
@@ -196,10 +199,29 @@ __global__ void rs_adamw_ag_kernel(PeerTable grads, PeerTable params, long long 
     out.y = pack_bf16x2(p[2], p[3]);
     out.z = pack_bf16x2(p[4], p[5]);
     out.w = pack_bf16x2(p[6], p[7]);
-    for (int c = 0; c < world; ++c) {
-      const int dst = (rank + c) % world;  // stagger destinations across ranks
-      *reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(params.base[dst]) + i) = out;
+    if (local_out != nullptr) {
+      *reinterpret_cast<uint4*>(local_out + li) = out;
+    } else {
+      for (int c = 0; c < world; ++c) {
+        const int dst = (rank + c) % world;  // stagger destinations across ranks
+        *reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(params.base[dst]) + i) = out;
+      }
     }
+  }
+  __threadfence_system();
+}
+
+// All-gather push: n bf16 elements from local src into dst_c + off of every
+// rank c (16-byte vectors, destinations staggered by rank), then a
+// system-scope fence; the host follows with a release-store signal.
+__global__ void push_slice_kernel(const bf16* __restrict__ src, PeerTable dst, long long off, long long n, int world,
+                                  int rank) {
+  const long long nv = n / 8;
+  for (int c = 0; c < world; ++c) {
+    const int d = (rank + 1 + c) % world;
+    bf16* out = reinterpret_cast<bf16*>(dst.base[d]) + off;
+    for (long long v = (long long)blockIdx.x * blockDim.x + threadIdx.x; v < nv; v += (long long)gridDim.x * blockDim.x)
+      reinterpret_cast<uint4*>(out)[v] = reinterpret_cast<const uint4*>(src)[v];
   }
   __threadfence_system();
 }
@@ -313,7 +335,8 @@ void reduce_scatter(const std::vector<int64_t>& src_bases, int64_t src_off, int6
 void rs_adamw_ag(const std::vector<int64_t>& grad_bases, const std::vector<int64_t>& param_bases, int64_t lo, int64_t n,
                  at::Tensor& master, at::Tensor& m, at::Tensor& v, double lr, double beta1, double beta2, double eps,
                  double wd, int64_t step, double grad_scale, int64_t rank, const c10::optional<at::Tensor>& flags,
-                 int64_t flag_first, int64_t value, double timeout_s, at::Tensor& err, int64_t blocks) {
+                 int64_t flag_first, int64_t value, double timeout_s, at::Tensor& err, int64_t blocks,
+                 const c10::optional<at::Tensor>& local_out) {
   TORCH_CHECK(n % 8 == 0 && lo % 8 == 0, "harp_comm rs_adamw_ag: 8-element granularity");
   TORCH_CHECK(master.is_contiguous() && m.is_contiguous() && v.is_contiguous(), "harp_comm rs_adamw_ag: contiguous state");
   TORCH_CHECK(master.numel() == n && m.numel() == n && v.numel() == n, "harp_comm rs_adamw_ag: state size");
@@ -333,7 +356,24 @@ void rs_adamw_ag(const std::vector<int64_t>& grad_bases, const std::vector<int64
       make_table(grad_bases, 0), make_table(param_bases, 0), lo, n, master.data_ptr<float>(), m.data_ptr<float>(),
       v.data_ptr<float>(), h, world, (int)rank,
       flags.has_value() ? reinterpret_cast<const unsigned int*>(flags->data_ptr()) : nullptr, (int)flag_first,
-      (unsigned)value, (unsigned long long)(timeout_s * 1e9), err.data_ptr<int>());
+      (unsigned)value, (unsigned long long)(timeout_s * 1e9), err.data_ptr<int>(),
+      local_out.has_value() ? reinterpret_cast<bf16*>(local_out->data_ptr()) : nullptr);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  count_launch();
+}
+
+void push_slice(const at::Tensor& src, const std::vector<int64_t>& dst_bases, int64_t off, int64_t rank,
+                int64_t blocks) {
+  TORCH_CHECK(src.scalar_type() == at::kBFloat16 && src.is_contiguous() && src.numel() % 8 == 0 && off % 8 == 0 &&
+                  (reinterpret_cast<uintptr_t>(src.data_ptr()) & 15) == 0,
+              "harp_comm push_slice: contiguous bf16, 16-byte granularity");
+  const long long n = src.numel();
+  if (n == 0) return;
+  int grid = grid_for(n / 8, 256);
+  if (blocks > 0 && grid > blocks) grid = (int)blocks;
+  push_slice_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const bf16*>(src.data_ptr()), make_table(dst_bases, 0), off, n, (int)dst_bases.size(),
+      (int)rank);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   count_launch();
 }
@@ -355,7 +395,9 @@ TORCH_LIBRARY(harp_comm, m) {
         "int nseg, int rank, Tensor? flags, int flag_first, int value, float timeout_s, Tensor(b!) err) -> ()");
   m.def("rs_adamw_ag(int[] grad_bases, int[] param_bases, int lo, int n, Tensor(a!) master, Tensor(b!) m, "
         "Tensor(c!) v, float lr, float beta1, float beta2, float eps, float wd, int step, float grad_scale, int rank, "
-        "Tensor? flags, int flag_first, int value, float timeout_s, Tensor(d!) err, int blocks=0) -> ()");
+        "Tensor? flags, int flag_first, int value, float timeout_s, Tensor(d!) err, int blocks=0, "
+        "Tensor(e!)? local_out=None) -> ()");
+  m.def("push_slice(Tensor src, int[] dst_bases, int off, int rank, int blocks=0) -> ()");
 }
 TORCH_LIBRARY_IMPL(harp_comm, CompositeExplicitAutograd, m) {
   m.impl("ipc_alloc", &harp::comm::ipc_alloc);
@@ -369,4 +411,5 @@ TORCH_LIBRARY_IMPL(harp_comm, CUDA, m) {
   m.impl("gather", &harp::comm::gather);
   m.impl("reduce_scatter", &harp::comm::reduce_scatter);
   m.impl("rs_adamw_ag", &harp::comm::rs_adamw_ag);
+  m.impl("push_slice", &harp::comm::push_slice);
 }

@@ -24,6 +24,8 @@
 #include <ATen/ATen.h>
 #include <c10/cuda/CUDAException.h>
 
+#include <mutex>
+
 
 namespace harp {
 
@@ -31,6 +33,15 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 64;  // one 128-byte swizzle atom of bf16
+
+struct WeightGate {
+  const unsigned int* flags = nullptr;
+  int n = 0;
+  unsigned int epoch = 0;
+  unsigned long long timeout_ns = 0;
+};
+std::mutex g_gate_mu;
+WeightGate g_gate;
 constexpr int kThreads = 192;
 constexpr int kGroupM = 8;
 
@@ -50,7 +61,23 @@ struct GemmArgs {
   long ldc2;
   int* err;
   int probe;  // accumulate per-role wait cycles into g_gemm_probe (HARP_GEMM_PROBE=1)
+  // Weight-readiness gate (sharded parameters): before its first operand load
+  // the producer waits (bounded) until gate_flags[0 .. gate_n) >= gate_epoch;
+  // peers set those flags once their slice of the gathered weights has landed
+  // in this GPU's memory.  gate_flags == nullptr: no gate.
+  const unsigned int* gate_flags;
+  int gate_n;
+  unsigned int gate_epoch;
+  unsigned long long gate_timeout_ns;
 };
+
+// Wait for the weight-readiness gate (one thread).
+__device__ __forceinline__ bool wait_weight_gate(const GemmArgs& a, int* err) {
+  if (a.gate_flags == nullptr) return true;
+  bool ok = true;
+  for (int i = 0; i < a.gate_n && ok; ++i) ok = wait_flag_geq(a.gate_flags + i, a.gate_epoch, a.gate_timeout_ns, err, 30 + i);
+  return ok;
+}
 
 // Per-role cycle counters of the CTA-pair kernel, summed over CTAs and read
 // back with gemm_probe(): 0 MMA wait full, 1 MMA wait tempty, 2 producer wait
@@ -239,7 +266,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       int issued[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-      bool ok = true;
+      bool ok = wait_weight_gate(args, err);
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
         int mt, nt;
         tile_coords(t, num_m, num_n, mt, nt);
@@ -487,7 +514,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       int issued[C_::STAGES] = {};
-      bool ok = true;
+      bool ok = wait_weight_gate(args, err);
       const uint32_t fb0 = peer_addr(smem_u32(&full_bar[0]), 0);  // the leader's barriers
       for (int t = pair; t < num_tiles && ok; t += npairs) {
         int mt, nt;
@@ -637,6 +664,10 @@ __global__ void gemm_bf16_simt(const __nv_bfloat16* __restrict__ A, long sam, lo
                                const __nv_bfloat16* __restrict__ B, long sbk, long sbn, const GemmArgs args) {
   __shared__ float As[32][33];
   __shared__ float Bs[32][33];
+  if (args.gate_flags != nullptr) {
+    if (threadIdx.x == 0) wait_weight_gate(args, args.err);
+    __syncthreads();
+  }
   const int tx = threadIdx.x % 32, ty = threadIdx.x / 32;  // 32 x 8 threads
   const int m0 = blockIdx.y * 32, n0 = blockIdx.x * 32;
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
@@ -895,6 +926,13 @@ void gemm(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, at::Te
     return e != nullptr && e[0] == '1';
   }();
   args.probe = probe ? 1 : 0;
+  {
+    std::lock_guard<std::mutex> lock(g_gate_mu);
+    args.gate_flags = g_gate.flags;
+    args.gate_n = g_gate.n;
+    args.gate_epoch = g_gate.epoch;
+    args.gate_timeout_ns = g_gate.timeout_ns;
+  }
   if (K == 0) {
     // Degenerate: treat as zero accumulator.  Route through SIMT (K loop is empty).
     force_simt = true;
@@ -935,6 +973,24 @@ void gemm(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, at::Te
     case 192: dispatch_major<192>(a_mn, b_mn, ta, tb, args, stream); break;
     default: dispatch_major<128>(a_mn, b_mn, ta, tb, args, stream); break;
   }
+}
+
+// Process-wide weight-readiness gate for the GEMMs launched while it is set
+// (sharded parameters: the trainer sets it around a block whose gathered
+// weights are still arriving from peers; flags must stay alive while set).
+void set_weight_gate(const c10::optional<at::Tensor>& flags, int64_t first, int64_t count, int64_t epoch,
+                     double timeout_s) {
+  std::lock_guard<std::mutex> lock(g_gate_mu);
+  if (!flags.has_value() || count <= 0) {
+    g_gate = WeightGate{};
+    return;
+  }
+  TORCH_CHECK(flags->is_cuda() && flags->scalar_type() == at::kInt && first >= 0 && first + count <= flags->numel(),
+              "set_weight_gate: int32 CUDA flags");
+  g_gate.flags = reinterpret_cast<const unsigned int*>(flags->data_ptr<int>()) + first;
+  g_gate.n = (int)count;
+  g_gate.epoch = (unsigned int)epoch;
+  g_gate.timeout_ns = (unsigned long long)(timeout_s * 1e9);
 }
 
 at::Tensor gemm_probe() {

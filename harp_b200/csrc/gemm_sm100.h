@@ -34,6 +34,11 @@ void reset_launch_count();
 int set_gemm_pair_mode(int mode);
 // per-role cycle counters of the CTA-pair kernel (HARP_GEMM_PROBE=1); read and reset
 at::Tensor gemm_probe();
+// Gate every GEMM launched from now on: its producer waits until
+// flags[first .. first+count) >= epoch (flags written by peers when their
+// slices of gathered weights have landed); flags = None clears the gate.
+void set_weight_gate(const c10::optional<at::Tensor>& flags, int64_t first, int64_t count, int64_t epoch,
+                     double timeout_s);
 
 // Shared host helpers (runtime.cpp).
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,

@@ -229,6 +229,7 @@ TORCH_LIBRARY(harp, m) {
   m.def("rows_per_block(int rows_per_batch) -> int");
   m.def("gemm_pair_mode(int mode) -> int");
   m.def("gemm_probe() -> Tensor");
+  m.def("set_weight_gate(Tensor? flags, int first, int count, int epoch, float timeout_s) -> ()");
 }
 
 TORCH_LIBRARY_IMPL(harp, CUDA, m) {
@@ -257,6 +258,7 @@ TORCH_LIBRARY_IMPL(harp, CompositeExplicitAutograd, m) {
   m.impl("rows_per_block", &harp::rows_per_block_op);
   m.impl("gemm_pair_mode", &harp::gemm_pair_mode_op);
   m.impl("gemm_probe", &harp::gemm_probe);
+  m.impl("set_weight_gate", &harp::set_weight_gate);
 }
 
 TORCH_LIBRARY(xhpops, m) {

@@ -24,6 +24,13 @@ Purposes and buffers:
   GRAD / PARAM  the fused gradient reduce-scatter + AdamW + parameter push
           waits for every peer's GRAD flag; PARAM tells peers the new
           parameters have landed, which the next step waits for.
+  GATH / GACK  sharded parameters (harp_b200.parallel.param_shard): each rank
+          pushes its slice of a block's weights into every rank's staging
+          slot s and sets GATH[s] to the slot's gather count; the GEMMs of
+          that block wait for every GATH[s] inside their producer warp.  A
+          rank sets GACK[s] to the number of uses of slot s it has finished;
+          a push into slot s first waits until every rank has finished all
+          earlier uses.
   GRADB   per-bucket GRAD flags of the overlapped gradient sync: a rank sets
           its bucket-b slot from the compute stream once that bucket's
           gradients are written; the bucket's fused kernel (side stream) waits
@@ -55,7 +62,9 @@ _KV, _DKV, _DKV_ACK0, _DKV_ACK1, _GRAD, _PARAM, _BARRIER = 0, 8, 16, 24, 32, 40,
 _UQKV, _UO, _UDO, _UDQ = 56, 64, 72, 80
 _GRADB = 96  # per-bucket gradient-ready slots: _GRADB + 8 * bucket + rank
 _MAX_BUCKETS = 32
-_NFLAGS = _GRADB + 8 * _MAX_BUCKETS
+_GATH = _GRADB + 8 * _MAX_BUCKETS  # sharded parameters: slice landed in staging slot s (_GATH + 8 * s + rank)
+_GACK = _GATH + 16                 # sharded parameters: uses of staging slot s completed (_GACK + 8 * s + rank)
+_NFLAGS = _GACK + 16
 # CTAs of one bucket's fused reduce-scatter + AdamW + push kernel: enough
 # outstanding 16-byte NVLink loads to keep the links busy, few enough SMs that
 # the backward it overlaps keeps most of the GPU
@@ -378,12 +387,15 @@ class NVLinkComm:
         return bufs["dqkv"].tensor(B * S * 3 * HD, torch.bfloat16).view(B * S, 3 * HD)
 
     # -- gradients: fused reduce-scatter + AdamW + parameter push ---------------
-    def allocate_flat(self, numel: int):
-        """Symmetric flat parameter and gradient buffers (bf16)."""
+    def allocate_flat(self, numel: int, param_numel: Optional[int] = None):
+        """Symmetric flat parameter and gradient buffers (bf16); the parameter
+        buffer may be shorter (sharded parameters keep only the replicated
+        ones there)."""
+        pn = numel if param_numel is None else param_numel
         if self._flat is None:
-            self._flat = {"param": SymBuffer(self.group, numel * 2, self.device),
+            self._flat = {"param": SymBuffer(self.group, pn * 2, self.device),
                           "grad": SymBuffer(self.group, numel * 2, self.device)}
-        return (self._flat["param"].tensor(numel, torch.bfloat16), self._flat["grad"].tensor(numel, torch.bfloat16))
+        return (self._flat["param"].tensor(pn, torch.bfloat16), self._flat["grad"].tensor(numel, torch.bfloat16))
 
     def wait_params(self):
         """Before touching parameters or gradients of a new step: every peer has
@@ -407,9 +419,56 @@ class NVLinkComm:
         self.signal(_GRAD, e)
         opt.step_count += 1
         with phase("grad.rs_adamw_push"):
-            for seg in opt.segments:
-                self._rs_adamw_segment(opt, seg, _GRAD, e)
+            for b, seg in enumerate(opt.segments):
+                out = opt.local_param_out(b)
+                if out is None:
+                    self._rs_adamw_segment(opt, seg, _GRAD, e)
+                else:
+                    self._rs_adamw_local(opt, seg, _GRAD, e, out)
         self.signal(_PARAM, e)
+
+    # -- sharded parameters: staging slots, all-gather push, acks --------------
+    def param_slots(self, numel: int) -> SymBuffer:
+        """Two symmetric staging slots of `numel` bf16 each (allocated once)."""
+        if getattr(self, "_slots", None) is None:
+            self._slots = SymBuffer(self.group, 2 * numel * 2, self.device)
+            self._slot_numel = numel
+        assert self._slot_numel >= numel
+        return self._slots
+
+    def slot_view(self, s: int) -> torch.Tensor:
+        n = self._slot_numel
+        return self._slots.tensor(2 * n, torch.bfloat16)[s * n:(s + 1) * n]
+
+    def gather_slice(self, s: int, src: torch.Tensor, off: int, epoch: int, wait_uses: int, blocks: int = 32):
+        """Push this rank's slice `src` into offset `off` of staging slot s on
+        every rank, after every rank has finished `wait_uses` uses of the
+        slot; then set GATH[s] = epoch (all on the current stream)."""
+        if wait_uses > 0:
+            self.wait_all(_GACK + 8 * s, wait_uses)
+        n = self._slot_numel
+        bases = [b + (s * n + off) * 2 for b in self._slots.bases]
+        torch.ops.harp_comm.push_slice(src, bases, 0, self.rank, blocks)
+        self.signal(_GATH + 8 * s, epoch)
+
+    def gate_slot(self, s: int, epoch: int):
+        """GEMMs launched from now on wait for every rank's GATH[s] >= epoch."""
+        torch.ops.harp.set_weight_gate(self.flags, _GATH + 8 * s, self.world, epoch, self.timeout_s)
+
+    @staticmethod
+    def clear_gate():
+        torch.ops.harp.set_weight_gate(None, 0, 0, 0, 0.0)
+
+    def ack_slot(self, s: int, uses: int):
+        self.signal(_GACK + 8 * s, uses)
+
+    def _rs_adamw_local(self, opt, seg, slot: int, e: int, out: torch.Tensor, blocks: int = 0):
+        f, n, o = seg
+        cfg = opt.cfg
+        torch.ops.harp_comm.rs_adamw_ag(self._flat["grad"].bases, self._flat["param"].bases, f, n,
+                                        opt.master[o:o + n], opt.m[o:o + n], opt.v[o:o + n], opt.lr, cfg.beta1,
+                                        cfg.beta2, cfg.eps, cfg.weight_decay, opt.step_count, cfg.grad_scale,
+                                        self.rank, self.flags, slot, e, self.timeout_s, self.err, blocks, out)
 
     # overlapped form: begin_grad_sync, then rs_adamw_bucket per bucket in a
     # fixed order as gradients complete, then end_grad_sync
@@ -429,7 +488,11 @@ class NVLinkComm:
         ev.record()
         stream.wait_event(ev)
         with torch.cuda.stream(stream):
-            self._rs_adamw_segment(opt, opt.segments[b], _GRADB + 8 * b, e, BUCKET_CTAS)
+            out = opt.local_param_out(b)
+            if out is None:
+                self._rs_adamw_segment(opt, opt.segments[b], _GRADB + 8 * b, e, BUCKET_CTAS)
+            else:  # sharded parameters: the new slice stays with its owner
+                self._rs_adamw_local(opt, opt.segments[b], _GRADB + 8 * b, e, out, BUCKET_CTAS)
 
     def end_grad_sync(self, stream: torch.cuda.Stream):
         """After the last bucket: announce the new parameters, and make the
@@ -441,8 +504,10 @@ class NVLinkComm:
     def close(self):
         torch.cuda.synchronize(self.device)
         uly = [b for layer in self._uly for b in layer.values()]
-        for b in (self._kv_bufs + self._dkv_bufs + self._ring_bufs + self._dkv_push + uly +
+        slots = [self._slots] if getattr(self, "_slots", None) is not None else []
+        for b in (self._kv_bufs + self._dkv_bufs + self._ring_bufs + self._dkv_push + uly + slots +
                   list((self._flat or {}).values()) + [self.flags_buf]):
             b.release()
         self._kv_bufs, self._dkv_bufs, self._flat, self._uly = [], [], None, []
         self._ring_bufs, self._dkv_push = [], []
+        self._slots = None

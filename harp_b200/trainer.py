@@ -64,6 +64,10 @@ class TrainConfig:
     # of the backward; False = one fused kernel over everything after backward
     overlap_grad_sync: bool = True
     bucket_params: int = 64_000_000
+    # multi-GPU NVLink: keep only this rank's 1/world slice of every block's
+    # weights and gather a block's weights into a staging slot right before it
+    # runs, gated inside its GEMMs (harp_b200.parallel.param_shard)
+    shard_params: bool = False
 
 
 class FlatParams:
@@ -78,7 +82,17 @@ class FlatParams:
     ``self.buckets`` lists each bucket's [lo, hi) range of the flat buffer."""
 
     def __init__(self, model: torch.nn.Module, device, dtype=torch.bfloat16, align: int = 256, world: int = 1,
-                 alloc=None, buckets: Optional[List[List[torch.Tensor]]] = None):
+                 alloc=None, buckets: Optional[List[List[torch.Tensor]]] = None, rest_first: bool = False):
+        self._layout(model, align, world, buckets, rest_first)
+        self.device, self.dtype = device, dtype
+        self._allocate(alloc)
+        self._place()
+        self.attach_grads()
+
+    def _layout(self, model, align, world, buckets, rest_first):
+        """Offsets of every parameter: bucket by bucket (the last bucket holds
+        the parameters no group names; with rest_first it goes first in
+        memory but keeps the last index)."""
         self.params: List[torch.nn.Parameter] = []
         self.names: List[str] = []
         named = []
@@ -97,14 +111,19 @@ class FlatParams:
             if idx:
                 groups.append(idx)
         rest = [i for i, (_, p) in enumerate(named) if id(p) not in placed]
+        self.rest_bucket = len(groups) if rest else -1
         if rest:
             groups.append(rest)
+        mem_order = list(range(len(groups)))
+        if rest_first and rest:
+            mem_order = [len(groups) - 1] + mem_order[:-1]
         quantum = align * max(1, world)
         offs = []
         off = 0
-        self.buckets: List[tuple] = []
+        self.buckets: List[tuple] = [(0, 0)] * len(groups)
         self.bucket_of: Dict[int, int] = {}
-        for gi, idx in enumerate(groups):
+        for gi in mem_order:
+            idx = groups[gi]
             off = (off + quantum - 1) // quantum * quantum
             lo = off
             prev_end = None
@@ -120,24 +139,37 @@ class FlatParams:
                 off += p.numel()
                 prev_end = off
             off = (off + quantum - 1) // quantum * quantum
-            self.buckets.append((lo, off))
+            self.buckets[gi] = (lo, off)
         self.numel = max(off, quantum)
         if not self.buckets:
             self.buckets.append((0, self.numel))
         self.offsets = offs
+
+    def _allocate(self, alloc):
         if alloc is not None:
             # e.g. symmetric (peer-mapped) buffers of the NVLink communicator
             self.flat, self.grad = alloc(self.numel)
             self.flat.zero_()
             self.grad.zero_()
         else:
-            self.flat = torch.zeros(self.numel, device=device, dtype=dtype)
-            self.grad = torch.zeros(self.numel, device=device, dtype=dtype)
-        for p, o in zip(self.params, offs):
+            self.flat = torch.zeros(self.numel, device=self.device, dtype=self.dtype)
+            self.grad = torch.zeros(self.numel, device=self.device, dtype=self.dtype)
+
+    def _place(self):
+        for p, o in zip(self.params, self.offsets):
             n = p.numel()
-            self.flat[o:o + n].copy_(p.data.reshape(-1).to(device=device, dtype=dtype))
+            self.flat[o:o + n].copy_(p.data.reshape(-1).to(device=self.device, dtype=self.dtype))
             p.data = self.flat[o:o + n].view(p.shape)
-        self.attach_grads()
+
+    # hooks for the sharded-parameter variant (harp_b200.parallel.param_shard)
+    def segment_param(self, b: int, f: int, n: int) -> torch.Tensor:
+        """This rank's bf16 slice [f, f + n) of bucket b."""
+        return self.flat[f:f + n]
+
+    def local_out(self, b: int) -> Optional[torch.Tensor]:
+        """Where the optimizer writes bucket b's new slice when it is not
+        pushed to every rank (None: pushed)."""
+        return None
 
     def attach_grads(self):
         for p, o in zip(self.params, self.offsets):
@@ -174,8 +206,7 @@ class ShardedAdamW:
             self.segments.append((lo + self.rank * n, n, off))
             off += n
         self.shard_numel = off
-        self.master = torch.cat([flat.flat[f:f + n].float() for f, n, _ in self.segments]) \
-            if len(self.segments) > 1 else flat.flat[self.segments[0][0]:self.segments[0][0] + off].float().clone()
+        self.master = torch.cat([flat.segment_param(b, f, n).float() for b, (f, n, _) in enumerate(self.segments)])
         self.m = torch.zeros_like(self.master)
         self.v = torch.zeros_like(self.master)
         self.grad_shard = torch.empty(off, device=flat.flat.device, dtype=flat.grad.dtype)
@@ -203,8 +234,13 @@ class ShardedAdamW:
         self.hyper.copy_(self._hyper_host, non_blocking=True)
 
     def param_segments(self) -> List[torch.Tensor]:
-        """Views of the flat parameter buffer that this rank's state covers."""
-        return [self.flat.flat[f:f + n] for f, n, _ in self.segments]
+        """bf16 views of the parameter slices that this rank's state covers."""
+        return [self.flat.segment_param(b, f, n) for b, (f, n, _) in enumerate(self.segments)]
+
+    def local_param_out(self, b: int) -> Optional[torch.Tensor]:
+        """Destination of bucket b's updated slice when it stays with this rank
+        (sharded parameters); None when the update is pushed to every rank."""
+        return self.flat.local_out(b)
 
     def grad_segments(self, grad: torch.Tensor) -> List[torch.Tensor]:
         return [grad[f:f + n] for f, n, _ in self.segments]
@@ -307,11 +343,24 @@ class Trainer:
 
             self.grad_comm = NVLinkComm.get(par.world_group, device)
         alloc = self.grad_comm.allocate_flat if self.grad_comm is not None else None
-        buckets = grad_buckets(model, cfg.bucket_params) if par.world_size > 1 else None
-        self.flat = FlatParams(model, device, align=cfg.align, world=par.world_size, alloc=alloc, buckets=buckets)
+        self.gatherer = None
+        if cfg.shard_params and par.world_size > 1:
+            if self.grad_comm is None:
+                raise ValueError("shard_params needs the NVLink communicator (comm='nvl' on GPUs)")
+            from .parallel.param_shard import ParamGatherer, ShardedFlatParams
+
+            self.flat = ShardedFlatParams(model, device, self.grad_comm, align=cfg.align)
+            self.gatherer = ParamGatherer(model, self.flat, self.grad_comm, device)
+        else:
+            buckets = grad_buckets(model, cfg.bucket_params) if par.world_size > 1 else None
+            self.flat = FlatParams(model, device, align=cfg.align, world=par.world_size, alloc=alloc,
+                                   buckets=buckets)
         self.opt = ShardedAdamW(self.flat, cfg, par.world_group)
         # overlapped gradient sync: buckets go out as their gradients complete
-        self._overlap = self.grad_comm is not None and cfg.overlap_grad_sync and len(self.flat.buckets) > 1
+        # (sharded parameters always overlap: a block's staging slot is released
+        # when its gradients are reported)
+        self._overlap = self.grad_comm is not None and (cfg.overlap_grad_sync or self.gatherer is not None) and \
+            len(self.flat.buckets) > 1
         self._ready: set = set()
         self._next_bucket = 0
         self._bucket_left: List[int] = []
@@ -354,6 +403,8 @@ class Trainer:
             self.grad_comm.wait_params()
         self.flat.zero_grad()
         self._begin_sync()
+        if self.gatherer is not None:
+            self.gatherer.begin_step()
         with phase("forward"):
             loss = self.loss_fn(self.model, latent, noise, text, sigmas, self.sp, **extra)
             if self.par.dp_size > 1:
@@ -362,6 +413,8 @@ class Trainer:
             loss.backward()
         with phase("grad_sync_optimizer"):
             self.sync_and_step()
+        if self.gatherer is not None:
+            self.gatherer.end_step()
         self.global_step += 1
         lsum = loss.detach().float().reshape(1)
         if self.par.world_size > 1:
@@ -389,7 +442,10 @@ class Trainer:
         if not self._sync_active or id(p) in self._ready:
             return
         self._ready.add(id(p))
-        self._bucket_left[self.flat.bucket_of[id(p)]] -= 1
+        b = self.flat.bucket_of[id(p)]
+        self._bucket_left[b] -= 1
+        if self._bucket_left[b] == 0 and self.gatherer is not None:
+            self.gatherer.bucket_done(b)
         self._launch_ready()
 
     def _launch_ready(self, flush: bool = False):
@@ -404,6 +460,10 @@ class Trainer:
             return
         if self.grad_comm is not None:
             if self._overlap:
+                if self.gatherer is not None:  # blocks whose gradients nothing reported
+                    for b, left in enumerate(self._bucket_left):
+                        if left > 0:
+                            self.gatherer.bucket_done(b)
                 self._launch_ready(flush=True)  # buckets whose gradients nothing reported
                 self._sync_active = False
                 self.grad_comm.end_grad_sync(self._comm_stream)
@@ -488,6 +548,15 @@ class Trainer:
         extra = {k: _to_dev(v, dev) for k, v in batch.items() if k not in ("latent", "noise", "text", "sigmas")}
         loss = self.train_step(latent, noise, text, sigmas, **extra)
         return float(loss.item())
+
+    def model_state_dict(self) -> Dict[str, torch.Tensor]:
+        """The model's state dict with every parameter's current value (with
+        sharded parameters a collective: every rank must call it)."""
+        sd = self.model.state_dict()
+        if self.gatherer is not None:
+            views = self.flat.state_dict_views(self.par.world_group)
+            sd.update({k: v for k, v in views.items() if k in sd})
+        return sd
 
     def check_errors(self):
         if torch.device(self.device).type == "cuda":

@@ -59,8 +59,10 @@ def save_checkpoint(work_dir: str, step: int, trainer, schedule=None, consolidat
         os.makedirs(path, exist_ok=True)
     _barrier()
     torch.cuda.synchronize() if torch.cuda.is_available() else None
+    # every rank takes part: with sharded parameters this gathers the weights
+    full = trainer.model_state_dict() if hasattr(trainer, "model_state_dict") else trainer.model.state_dict()
     if rank == 0:
-        sd = {k: v.detach().cpu() for k, v in trainer.model.state_dict().items()}
+        sd = {k: v.detach().cpu() for k, v in full.items()}
         torch.save(sd, os.path.join(path, "pytorch_model.bin"))
         if schedule is not None:
             torch.save(schedule.state_dict(), os.path.join(path, "scheduler.bin"))

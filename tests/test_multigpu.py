@@ -65,20 +65,22 @@ def _single(batch, steps):
 
 
 # (sequence-parallel mode, SP exchange backend, gradient comm, overlapped bucketed gradient sync,
-#  parameters per bucket): the 1M buckets put about one block in each bucket of the small preset
-@pytest.mark.parametrize("mode,backend,comm,overlap,bucket", [
-    ("ulysses", "nvl", "nvl", True, 1_000_000), ("ring", "nvl", "nvl", True, 64_000_000),
-    ("ulysses", "nvl", "nvl", False, 1_000_000), ("ulysses", "torch", "torch", False, 64_000_000)])
-def test_sp2_training_matches_one_gpu(tmp_path, mode, backend, comm, overlap, bucket):
+#  parameters per bucket, sharded block weights): the 1M buckets put about one block in each
+#  bucket of the small preset
+@pytest.mark.parametrize("mode,backend,comm,overlap,bucket,shard", [
+    ("ulysses", "nvl", "nvl", True, 1_000_000, False), ("ring", "nvl", "nvl", True, 64_000_000, False),
+    ("ulysses", "nvl", "nvl", False, 1_000_000, False), ("ulysses", "torch", "torch", False, 64_000_000, False),
+    ("ulysses", "nvl", "nvl", True, 64_000_000, True), ("ring", "nvl", "nvl", True, 64_000_000, True)])
+def test_sp2_training_matches_one_gpu(tmp_path, mode, backend, comm, overlap, bucket, shard):
     _need(2)
     bpath = str(tmp_path / "batch.pt")
     batch = _batch(bpath)
     ref_losses, ref_flat = _single(batch, 3)
     res = _run("train", 2, tmp_path, {"batch": bpath, "steps": 3, "mode": mode, "backend": backend, "comm": comm,
-                                      "overlap": overlap, "bucket_params": bucket})
+                                      "overlap": overlap, "bucket_params": bucket, "shard": shard})
     for r in (0, 1):
         assert res[r]["mode"] == mode and res[r]["backend"] == backend
-        assert res[r]["overlap"] == (overlap and comm == "nvl") and res[r]["buckets"] > 1, res[r]
+        assert res[r]["overlap"] == ((overlap or shard) and comm == "nvl") and res[r]["buckets"] > 1, res[r]
         assert res[r]["losses"] == pytest.approx(ref_losses, rel=1e-2), (res[r]["losses"], ref_losses)
         torch.testing.assert_close(res[r]["flat"].float(), ref_flat.float(), rtol=2 ** -6, atol=2 * 3 * 1e-3)
     assert torch.equal(res[0]["flat"], res[1]["flat"])
