@@ -73,6 +73,8 @@ def parse():
                     help="sequence-parallel attention: K/V gather (ring) or head all-to-all (ulysses)")
     ap.add_argument("--comm", default="auto", choices=["auto", "torch", "nvl"])
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--offload-optimizer", action="store_true",
+                    help="harp: fp32 master weights and AdamW moments in pinned, mapped host memory")
     ap.add_argument("--shard-params", action="store_true",
                     help="harp, N > 1: keep 1/N of every block's weights per GPU and gather them per block")
     ap.add_argument("--phases", action="store_true",
@@ -354,7 +356,8 @@ def main():
         model.initialize_weights(seed=0)
         model = model.to(torch.bfloat16)
         trainer = Trainer(model, par, TrainConfig(comm=args.comm, cuda_graph=bool(args.cuda_graph),
-                                                  shard_params=args.shard_params and ws > 1), device,
+                                                  shard_params=args.shard_params and ws > 1,
+                                                  offload_optimizer=args.offload_optimizer), device,
                           sp_backend=args.sp_backend, sp_mode=args.sp_mode, loss_fn=loss_fn)
         cin, tdim = cfg.in_channels, cfg.text_dim
 
@@ -367,7 +370,8 @@ def main():
         count_launches = lambda: int(torch.ops.harp.launch_count())  # noqa: E731
         reset_launches = lambda: torch.ops.harp.reset_launch_count()  # noqa: E731
         parallelism = (f"sp{sp}" + (f"xdp{dp}" if dp > 1 else "") + (f"-{trainer.sp.mode}" if sp > 1 else "") +
-                       ("-sharded-weights" if trainer.gatherer is not None else ""))
+                       ("-sharded-weights" if trainer.gatherer is not None else "") +
+                       ("-offload-optimizer" if args.offload_optimizer else ""))
     else:
         sys.path.insert(0, os.path.join(ROOT, "baseline"))
         from baseline.dit_baseline import BaselineTrainer

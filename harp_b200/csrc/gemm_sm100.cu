@@ -61,8 +61,8 @@ struct GemmArgs {
   long ldc2;
   int* err;
   int probe;  // accumulate per-role wait cycles into g_gemm_probe (HARP_GEMM_PROBE=1)
-  // Weight-readiness gate (sharded parameters): before its first operand load
-  // the producer waits (bounded) until gate_flags[0 .. gate_n) >= gate_epoch;
+  // Weight-readiness gate (sharded parameters): before any role starts, thread
+  // 0 of each CTA waits (bounded) until gate_flags[0 .. gate_n) >= gate_epoch;
   // peers set those flags once their slice of the gathered weights has landed
   // in this GPU's memory.  gate_flags == nullptr: no gate.
   const unsigned int* gate_flags;
@@ -255,6 +255,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_alloc(tmem_slot, C_::TMEM_COLS);
     tmem_relinquish();
   }
+  // weight gate: no role starts (and no pipeline wait is timed) before the
+  // gathered weights have landed
+  if (threadIdx.x == 0) wait_weight_gate(args, err);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -266,7 +269,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       int issued[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-      bool ok = wait_weight_gate(args, err);
+      bool ok = true;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
         int mt, nt;
         tile_coords(t, num_m, num_n, mt, nt);
@@ -503,6 +506,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_alloc_pair(tmem_slot, C_::TMEM_COLS);
     tmem_relinquish_pair();
   }
+  // weight gate (see the single-CTA kernel); both CTAs wait before the sync
+  if (threadIdx.x == 0) wait_weight_gate(args, err);
   tc_fence_before();
   cluster_sync_all();  // both CTAs' barriers exist and the paired TMEM is allocated
   tc_fence_after();
@@ -514,7 +519,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       int issued[C_::STAGES] = {};
-      bool ok = wait_weight_gate(args, err);
+      bool ok = true;
       const uint32_t fb0 = peer_addr(smem_u32(&full_bar[0]), 0);  // the leader's barriers
       for (int t = pair; t < num_tiles && ok; t += npairs) {
         int mt, nt;

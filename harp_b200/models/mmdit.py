@@ -68,6 +68,10 @@ PRESETS = {
     # SwiGLU hidden 8/3 D has the parameter count of a GELU MLP of 4 D
     "flux-12b": MMDiTConfig(hidden=3072, heads=24, depth_double=19, depth_single=38, text_dim=4096,
                             mlp_ratio=8.0 / 3.0),
+    # Lumina-like ~2.3B: 24 joint (single-stream) blocks over image + text tokens,
+    # hidden 2304, 18 heads x 128, SwiGLU 8/3 D
+    "mmdit-2b": MMDiTConfig(hidden=2304, heads=18, depth_double=0, depth_single=24, text_dim=2304,
+                            mlp_ratio=8.0 / 3.0),
     "mmdit-tiny": MMDiTConfig(hidden=256, heads=2, depth_double=2, depth_single=0, text_dim=128,
                               axes_dims=(32, 48, 48)),
     "flux-tiny": MMDiTConfig(hidden=256, heads=2, depth_double=1, depth_single=2, text_dim=128,

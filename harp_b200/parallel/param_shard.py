@@ -19,9 +19,9 @@ Here (TrainConfig(shard_params=True), NVLink communicator, one process per GPU):
     (GACK[slot]).  The next block's gather is issued while the current block
     computes.
   * The block's parameters are re-pointed at their staging slot, and every
-    harp GEMM launched for the block carries a device-side gate: its TMA
-    producer waits (bounded) until every rank's GATH[slot] reached the slot's
-    gather count before its first operand load (gemm_sm100.cu
+    harp GEMM launched for the block carries a device-side gate: each CTA
+    waits (bounded) until every rank's GATH[slot] reached the slot's gather
+    count before its TMA producer, MMA and epilogue roles start (gemm_sm100.cu
     wait_weight_gate).  Nothing on the host waits for the gather.
   * This rank's own slice is ordered by a stream dependency (the compute
     stream waits for the side stream's push), never by a spin on a flag that

@@ -29,6 +29,7 @@ Mapping to the reference:
 """
 from __future__ import annotations
 
+import contextlib
 import math
 import os
 from dataclasses import dataclass
@@ -68,6 +69,12 @@ class TrainConfig:
     # weights and gather a block's weights into a staging slot right before it
     # runs, gated inside its GEMMs (harp_b200.parallel.param_shard)
     shard_params: bool = False
+    # keep the fp32 master weights and AdamW moments in pinned, mapped host
+    # memory (the optimizer kernels read and write them over the host link)
+    offload_optimizer: bool = False
+    # move activations saved for backward to pinned host memory during the
+    # forward and back during the backward (managers.mem_manager.HBMToDDROffloader)
+    offload_activations: bool = False
 
 
 class FlatParams:
@@ -206,9 +213,17 @@ class ShardedAdamW:
             self.segments.append((lo + self.rank * n, n, off))
             off += n
         self.shard_numel = off
-        self.master = torch.cat([flat.segment_param(b, f, n).float() for b, (f, n, _) in enumerate(self.segments)])
-        self.m = torch.zeros_like(self.master)
-        self.v = torch.zeros_like(self.master)
+        dev = flat.grad.device
+        ctx = contextlib.nullcontext()
+        if cfg.offload_optimizer and dev.type == "cuda":
+            from .runtime import alloc
+
+            ctx = alloc.use_tier("host", dev.index)  # pinned, mapped host memory
+        with ctx:
+            self.master = torch.cat([flat.segment_param(b, f, n).float()
+                                     for b, (f, n, _) in enumerate(self.segments)])
+            self.m = torch.zeros_like(self.master)
+            self.v = torch.zeros_like(self.master)
         self.grad_shard = torch.empty(off, device=flat.flat.device, dtype=flat.grad.dtype)
         self.step_count = 0
         self.lr = cfg.lr
@@ -405,7 +420,7 @@ class Trainer:
         self._begin_sync()
         if self.gatherer is not None:
             self.gatherer.begin_step()
-        with phase("forward"):
+        with phase("forward"), self._saved_tensor_ctx():
             loss = self.loss_fn(self.model, latent, noise, text, sigmas, self.sp, **extra)
             if self.par.dp_size > 1:
                 loss = loss / self.par.dp_size
@@ -421,6 +436,15 @@ class Trainer:
             C.all_reduce_sum_(lsum, self.par.world_group)
             # each SP group holds one sample set: undo the dp split and sum of SP partials
         return lsum
+
+    def _saved_tensor_ctx(self):
+        if not self.cfg.offload_activations or torch.device(self.device).type != "cuda":
+            return contextlib.nullcontext()
+        if getattr(self, "_offloader", None) is None:
+            from .managers.mem_manager import HBMToDDROffloader
+
+            self._offloader = HBMToDDROffloader()
+        return torch.autograd.graph.saved_tensors_hooks(self._offloader.pack_hook, self._offloader.unpack_hook)
 
     # -- gradient sync -----------------------------------------------------------
     def _begin_sync(self):
