@@ -1161,11 +1161,11 @@ struct BwdPipeCfg {
 };
 // Four warpgroups: WG0 = w0 TMA, w1 MMA (w2-3 idle); WG1 = w4-7 and WG2 = w8-11
 // dS warps (query columns 0-63 / 64-127); WG3 = w12-15 dQ warps.  The dS warps
-// hold a tile's S and dP for 64 columns in registers, so registers move to
-// them with setmaxnreg: 88 + 168 + 168 + 88 = 512 = 4 x 128, the launch's
-// per-thread budget for 512 threads.
+// hold a tile's S and dP for 64 columns in registers and the dQ warps a whole
+// dQ row, so registers move to them with setmaxnreg: 80 + 168 + 168 + 96 = 512
+// = 4 x 128, the launch's per-thread budget for 512 threads.
 constexpr int kBwdPipeThreads = 512;
-constexpr int kPipeRegsCtl = 88, kPipeRegsDs = 168, kPipeRegsDq = 88;
+constexpr int kPipeRegsCtl = 80, kPipeRegsDs = 168, kPipeRegsDq = 96;
 static_assert(kPipeRegsCtl + 2 * kPipeRegsDs + kPipeRegsDq == 4 * (65536 / kBwdPipeThreads),
               "warpgroup register split must add up to the launch budget");
 
@@ -1178,12 +1178,23 @@ static_assert(kPipeRegsCtl + 2 * kPipeRegsDs + kPipeRegsDq == 4 * (65536 / kBwdP
 // per-query statistics from shared memory, whose bandwidth the tensor core
 // saturates while they run.  The padding columns of dV, dK and dQ take the
 // products of these columns and are never stored.
-template <int NCH, bool FOLD>
+//
+// TM (with FOLD): P^T and dS^T go back into tensor memory, into the dP columns
+// each dS warp has already read (packed bf16: P^T of queries [64w, 64w + 64)
+// at dP columns 64w .. 64w+31, dS^T at 64w+32 ..), so dV += P^T dO and
+// dK += dS^T Q read their A operand from TMEM and only dS (for dQ = dS K)
+// goes through shared memory.  The MMA warp issues S(i+1) as soon as the dS
+// warps hold S(i) in registers and dP(i+1) right after dV(i), dK(i), whose
+// TMEM reads the tensor pipe completes first (MMAs of one thread execute in
+// issue order).  Per tile this moves 64 KB less through shared memory, whose
+// bandwidth the operand reads of the MMAs otherwise saturate.
+template <int NCH, bool FOLD, bool TM>
 __global__ void __launch_bounds__(kBwdPipeThreads, 1)
     attn_bwd_pipe_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                          const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
                          const __grid_constant__ CUtensorMap tmdQ, const BwdArgs a) {
   using C = BwdPipeCfg<NCH>;
+  static_assert(!TM || FOLD, "the TMEM-operand schedule reads no statistics from shared memory");
   constexpr int ST = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sK = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 255) & ~uintptr_t(255));
@@ -1307,6 +1318,67 @@ __global__ void __launch_bounds__(kBwdPipeThreads, 1)
         return true;
       };
       bool ok = mbar_wait(kv_full, 0, err, 160);
+      if constexpr (TM) {
+        // A operand columns (relative to dP) of k-step ks (queries 16ks..16ks+15)
+        auto pt = [](int ks) { return (uint32_t)((ks / 4) * 64 + (ks % 4) * 8); };
+        auto s_mmas = [&](int i) {
+          const uint32_t qa = smem_u32(sQD + 2 * (i % ST) * C::TILE);
+#pragma unroll
+          for (int ks = 0; ks < NCH / 2; ++ks)
+            mma_ss(tS, kmajor_sw32(ka, ks), kmajor_sw32(qa, ks), idS, ks > 0 ? 1u : 0u);
+        };
+        auto dp_mmas = [&](int i) {
+          const uint32_t doa = smem_u32(sQD + (2 * (i % ST) + 1) * C::TILE);
+#pragma unroll
+          for (int ks = 0; ks < NCH / 2; ++ks)
+            mma_ss(tdP, kmajor_sw32(va, ks), kmajor_sw32(doa, ks), idS, ks > 0 ? 1u : 0u);
+        };
+        if (ok && nq > 0) ok = mbar_wait(&q_ready[0], 0, err, 161);
+        if (ok && nq > 0) {
+          tc_fence_after();
+          s_mmas(0);
+          dp_mmas(0);
+          mma_commit(s_full);
+        }
+        for (int i = 0; i < nq && ok; ++i) {
+          const int st = i % ST;
+          const bool more = i + 1 < nq;
+          if (more) {
+            // S(i+1) once the tile's statistics are in place and the dS warps hold S(i)
+            if (!mbar_wait(&q_ready[(i + 1) % ST], ((i + 1) / ST) & 1, err, 161)) { ok = false; break; }
+            if (!mbar_wait(s_free, i & 1, err, 162)) { ok = false; break; }
+            tc_fence_after();
+            s_mmas(i + 1);
+          }
+          BWD_PROBE(i, 0);
+          if (!mbar_wait(p_full, i & 1, err, 163)) { ok = false; break; }
+          BWD_PROBE(i, 1);
+          tc_fence_after();
+          const uint32_t qa = smem_u32(sQD + 2 * st * C::TILE), doa = smem_u32(sQD + (2 * st + 1) * C::TILE);
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks)
+            mma_ts(tdV, tdP + pt(ks), mnmajor_sw32(doa, ks), idO, (i > 0 || ks > 0) ? 1u : 0u);
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks)
+            mma_ts(tdK, tdP + pt(ks) + 32, mnmajor_sw32(qa, ks), idO, (i > 0 || ks > 0) ? 1u : 0u);
+          if (more) {
+            dp_mmas(i + 1);  // over the P^T / dS^T columns dV(i) and dK(i) read before it
+            mma_commit(s_full);
+          }
+          if (i > 0) {
+            if (!mbar_wait(dq_free, (i - 1) & 1, err, 164)) { ok = false; break; }
+            tc_fence_after();
+          }
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks)
+            mma_ss(tdQ, mnmajor_desc(dsa, ks), mnmajor_sw32(ka, ks), idQ, ks > 0 ? 1u : 0u);
+          mma_commit(p_free);
+          mma_commit(dq_full);
+          BWD_PROBE(i, 3);
+        }
+        mma_commit(fin);
+        mbar_wait_drain(fin, 0);
+      } else {
       for (int i = 0; i < nq && ok; ++i) {
         const int st = i % ST;
         const uint32_t ph = (i / ST) & 1;
@@ -1327,6 +1399,7 @@ __global__ void __launch_bounds__(kBwdPipeThreads, 1)
       if (ok && nq > 0) ok = rest(nq - 1);
       mma_commit(fin);
       mbar_wait_drain(fin, 0);
+      }
     }
    } else if (warp == 2) {
     // dQ reducer: once the four dQ warps have staged tile i's fp32 partial in
@@ -1486,6 +1559,15 @@ __global__ void __launch_bounds__(kBwdPipeThreads, 1)
       }
       if (warp == 4 && lane == 0) BWD_PROBE(i, 12);
       if (a.probe && blockIdx.x == 0 && warp == 4 && lane == 0 && i < 64) g_bwd_probe[i * 16 + 14] = clock64() - c_start;
+      if constexpr (TM) {
+        // P^T / dS^T into this warp's own dP columns (already read above)
+        const uint32_t pbase = tdP + lane_off + (uint32_t)((wg - 1) * 64);
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc) {
+          tmem_st16(pbase + cc * 16, pp[cc]);
+          tmem_st16(pbase + 32 + cc * 16, dd[cc]);
+        }
+      }
       // the previous tile's dV/dK/dQ must be done reading P^T / dS
       if (i > 0 && !mbar_wait(p_free, (i - 1) & 1, err, 171)) ok = false;
       if (warp == 4 && lane == 0) BWD_PROBE(i, 13);
@@ -1494,12 +1576,14 @@ __global__ void __launch_bounds__(kBwdPipeThreads, 1)
         const int c = c_begin + cc;
 #pragma unroll
         for (int g = 0; g < 4; ++g) {
-          *reinterpret_cast<uint4*>(sP + (c * 4 + g) * 2048 + kr * 16) =
-              make_uint4(pp[cc][4 * g], pp[cc][4 * g + 1], pp[cc][4 * g + 2], pp[cc][4 * g + 3]);
+          if (!TM)
+            *reinterpret_cast<uint4*>(sP + (c * 4 + g) * 2048 + kr * 16) =
+                make_uint4(pp[cc][4 * g], pp[cc][4 * g + 1], pp[cc][4 * g + 2], pp[cc][4 * g + 3]);
           *reinterpret_cast<uint4*>(sdS + (c * 4 + g) * 2048 + kr * 16) =
               make_uint4(dd[cc][4 * g], dd[cc][4 * g + 1], dd[cc][4 * g + 2], dd[cc][4 * g + 3]);
         }
       }
+      if (TM) tmem_wait_st();
       fence_proxy_async_smem();
       __syncwarp();
       if (warp == 4 && lane == 0) BWD_PROBE(i, 5);
@@ -1546,33 +1630,26 @@ __global__ void __launch_bounds__(kBwdPipeThreads, 1)
       const int st = i % ST;
       float* stage = reinterpret_cast<float*>(sQD + 2 * st * C::TILE);  // [128][Dh] fp32
       float* srow = stage + qr * a.Dh;
-      // the dQ row (64 or 80 columns) in two TMEM round trips: columns 0-47,
-      // then the rest
-      {
-        uint32_t v0[16], v1[16], v2[16];
-        tmem_ld16(tdQ + lane_off, v0);
-        tmem_ld16(tdQ + lane_off + 16, v1);
-        tmem_ld16(tdQ + lane_off + 32, v2);
-        tmem_wait_ld();
-        stage_row16(srow, 0, v0, a.Dh);
-        stage_row16(srow, 16, v1, a.Dh);
-        stage_row16(srow, 32, v2, a.Dh);
-      }
-      {
-        uint32_t v0[16], v1[16];
-        tmem_ld16(tdQ + lane_off + 48, v0);
-        if (C::DPAD > 64) tmem_ld16(tdQ + lane_off + 64, v1);
-        tmem_wait_ld();
-        stage_row16(srow, 48, v0, a.Dh);
-        if (C::DPAD > 64) stage_row16(srow, 64, v1, a.Dh);
-      }
+      // the whole dQ row (64 or 80 columns) in one TMEM round trip; the MMA
+      // warp may overwrite the dQ columns as soon as it is in registers
+      uint32_t v0[16], v1[16], v2[16], v3[16], v4[16];
+      tmem_ld16(tdQ + lane_off, v0);
+      tmem_ld16(tdQ + lane_off + 16, v1);
+      tmem_ld16(tdQ + lane_off + 32, v2);
+      tmem_ld16(tdQ + lane_off + 48, v3);
+      if (C::DPAD > 64) tmem_ld16(tdQ + lane_off + 64, v4);
+      tmem_wait_ld();
       tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dq_free);
+      stage_row16(srow, 0, v0, a.Dh);
+      stage_row16(srow, 16, v1, a.Dh);
+      stage_row16(srow, 32, v2, a.Dh);
+      stage_row16(srow, 48, v3, a.Dh);
+      if (C::DPAD > 64) stage_row16(srow, 64, v4, a.Dh);
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(dq_free);
-        mbar_arrive(&dqs_bar[st]);  // warp 2 reduce-adds the staged tile
-      }
+      if (lane == 0) mbar_arrive(&dqs_bar[st]);  // warp 2 reduce-adds the staged tile
     }
     if (ok) ok = mbar_wait(fin, 0, err, 181);
     tc_fence_after();
@@ -2119,12 +2196,24 @@ void launch_bwd(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap&
                         " registers per thread; using the single-tile schedule");
       return ok;
     };
-    static const bool pipe_ok =
-        setup(attn_bwd_pipe_kernel<NCH, false>) && setup(attn_bwd_pipe_kernel<NCH, true>);
-    const bool fold = args.Dh + 2 <= P::DPAD;
+    static const bool pipe_ok = setup(attn_bwd_pipe_kernel<NCH, false, false>) &&
+                                setup(attn_bwd_pipe_kernel<NCH, true, false>) &&
+                                setup(attn_bwd_pipe_kernel<NCH, true, true>);
+    // HARP_ATTN_BWD_TM=0 keeps P^T / dS^T in shared memory (comparisons)
+    static const bool tm_on = [] {
+      const char* e = std::getenv("HARP_ATTN_BWD_TM");
+      return !(e && e[0] == '0');
+    }();
+    // HARP_ATTN_BWD_FOLD=0 keeps the statistics in shared memory (comparisons)
+    static const bool fold_on = [] {
+      const char* e = std::getenv("HARP_ATTN_BWD_FOLD");
+      return !(e && e[0] == '0');
+    }();
+    const bool fold = fold_on && args.Dh + 2 <= P::DPAD;
     if (bwd_pipe_enabled() && pipe_ok) {
       const int grid = args.B * args.H * ((args.Skv + 127) / 128);
-      auto* kern = fold ? attn_bwd_pipe_kernel<NCH, true> : attn_bwd_pipe_kernel<NCH, false>;
+      auto* kern = fold ? (tm_on ? attn_bwd_pipe_kernel<NCH, true, true> : attn_bwd_pipe_kernel<NCH, true, false>)
+                        : attn_bwd_pipe_kernel<NCH, false, false>;
       kern<<<grid, kBwdPipeThreads, P::SMEM, stream>>>(mq, mk, mv, mdo, mdq, args);
       C10_CUDA_KERNEL_LAUNCH_CHECK();
       count_launch();
