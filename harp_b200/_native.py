@@ -22,7 +22,11 @@ import torch
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(_HERE, "csrc")
-BUILD_DIR = os.path.join(_HERE, "_build")
+# HARP_DEBUG_BOUNDS=1 selects the bounds-checking build (its own directory):
+# the TMA and tcgen05 helpers check coordinates and tensor-memory columns,
+# record violations (torch.ops.harp.debug_bounds_status()) and skip the access.
+DEBUG_BOUNDS = os.environ.get("HARP_DEBUG_BOUNDS", "") == "1"
+BUILD_DIR = os.path.join(_HERE, "_build_bounds" if DEBUG_BOUNDS else "_build")
 NAME = "harp_b200_C"
 SOURCES = [
     "ops.cpp",
@@ -46,6 +50,8 @@ CUDA_FLAGS = [
     "-DNDEBUG",
 ]
 CXX_FLAGS = ["-O3", "-std=c++17"]
+if DEBUG_BOUNDS:
+    CUDA_FLAGS = CUDA_FLAGS + ["-DHARP_DEBUG_BOUNDS"]
 
 _lock = threading.Lock()
 _loaded = False
@@ -181,7 +187,9 @@ def build_c10d(verbose: bool = False):
     os.makedirs(BUILD_DIR, exist_ok=True)
     with _lock:
         _c10d_mod = _load(name=C10D_NAME, sources=[os.path.join(CSRC, s) for s in C10D_SOURCES],
-                          extra_cflags=CXX_FLAGS, extra_cuda_cflags=CUDA_FLAGS, extra_include_paths=[CSRC],
+                          extra_cflags=CXX_FLAGS,
+                          extra_cuda_cflags=[f for f in CUDA_FLAGS if f != "-DHARP_DEBUG_BOUNDS"],
+                          extra_include_paths=[CSRC],
                           build_directory=BUILD_DIR, is_python_module=True, verbose=verbose)
         with open(os.path.join(BUILD_DIR, C10D_NAME + ".stamp"), "w") as fh:
             fh.write(_c10d_hash())

@@ -87,6 +87,9 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
 // dst(global, via map) += src(smem) for one box; bulk-group completion.
 __device__ __forceinline__ void tma_reduce_add_4d(const CUtensorMap* map, const void* src, int c0, int c1, int c2,
                                                   int c3) {
+#ifdef HARP_DEBUG_BOUNDS
+  if (!bounds_ok((c0 & 3) == 0 && c0 >= 0 && c1 >= 0 && c2 >= 0 && c3 >= 0, 231, c2)) return;
+#endif
   asm volatile(
       "cp.reduce.async.bulk.tensor.4d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
           reinterpret_cast<uint64_t>(map)),

@@ -54,6 +54,59 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
 }
 
 // ---------------------------------------------------------------------------
+// Bounds-checking debug build (HARP_DEBUG_BOUNDS, built by
+// harp_b200._native.build(debug_bounds=True)): the TMA and tcgen05 helpers
+// below check their coordinates and tensor-memory columns, and a failed check
+// records {kErrBounds, site, block, info} in this translation unit's word and
+// skips the access (a skipped TMA load leaves its barrier short, so the
+// kernel's bounded wait then gives up too).  The host reads every
+// translation unit's word with torch.ops.harp.debug_bounds_status().
+// ---------------------------------------------------------------------------
+#ifdef HARP_DEBUG_BOUNDS
+}  // namespace harp
+static __device__ int g_harp_bounds[4];
+namespace harp {
+void register_bounds_reader(void (*fn)(int*));
+namespace {
+struct BoundsReader {
+  BoundsReader() { register_bounds_reader(&read); }
+  static void read(int* out) {
+    cudaMemcpyFromSymbol(out, g_harp_bounds, sizeof(int) * 4);
+    const int zeros[4] = {0, 0, 0, 0};
+    cudaMemcpyToSymbol(g_harp_bounds, zeros, sizeof(zeros));
+  }
+};
+const BoundsReader g_bounds_reader;
+}  // namespace
+__device__ __forceinline__ bool bounds_ok(bool cond, int site, int info) {
+  if (cond) return true;
+  if (atomicCAS(&g_harp_bounds[0], 0, kErrBounds) == 0) {
+    g_harp_bounds[1] = site;
+    g_harp_bounds[2] = blockIdx.x;
+    g_harp_bounds[3] = info;
+  }
+  return false;
+}
+// TMEM address: lane quarter base (0/32/64/96) in the high half, column in the
+// low half; `ncols` columns from it must lie inside the 512 of an SM.
+__device__ __forceinline__ bool tmem_ok(uint32_t taddr, int ncols, int site) {
+  const uint32_t lane = taddr >> 16, col = taddr & 0xFFFFu;
+  return bounds_ok(lane < 128 && (lane & 31) == 0 && col + (uint32_t)ncols <= 512u, site, (int)taddr);
+}
+#define HARP_CHECK_TMA_X(c0, site) \
+  if (!::harp::bounds_ok(((c0) & 7) == 0, site, c0)) return
+#define HARP_CHECK_TMEM(taddr, n, site) \
+  if (!::harp::tmem_ok(taddr, n, site)) return
+#else
+#define HARP_CHECK_TMA_X(c0, site) \
+  do {                             \
+  } while (0)
+#define HARP_CHECK_TMEM(taddr, n, site) \
+  do {                                  \
+  } while (0)
+#endif
+
+// ---------------------------------------------------------------------------
 // mbarrier
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
@@ -108,6 +161,7 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
+  HARP_CHECK_TMA_X(c0, 201);
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
       ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
@@ -115,6 +169,7 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
 }
 __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
                                             int c2, int c3) {
+  HARP_CHECK_TMA_X(c0, 202);
   asm volatile(
       "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], "
       "[%2];" ::"r"(smem_u32(dst)),
@@ -124,6 +179,7 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, u
 
 __device__ __forceinline__ void tma_load_5d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
                                             int c2, int c3, int c4) {
+  HARP_CHECK_TMA_X(c0, 203);
   asm volatile(
       "cp.async.bulk.tensor.5d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6, %7}], "
       "[%2];" ::"r"(smem_u32(dst)),
@@ -156,6 +212,7 @@ __device__ __forceinline__ void tc_fence_after() {
 // D(tmem) (+)= A(smem desc) * B(smem desc); kind::f16 (bf16 inputs, fp32 accum)
 __device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                        uint32_t accumulate) {
+  HARP_CHECK_TMEM(d_tmem, (int)(((idesc >> 17) & 0x3Fu) << 3), 211);  // N columns of fp32 accumulators
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
@@ -166,6 +223,8 @@ __device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_
 // D(tmem) (+)= A(tmem) * B(smem desc)
 __device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
                                        uint32_t accumulate) {
+  HARP_CHECK_TMEM(d_tmem, (int)(((idesc >> 17) & 0x3Fu) << 3), 212);
+  HARP_CHECK_TMEM(a_tmem, 8, 213);  // 16 bf16 of K packed in 8 columns
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
@@ -185,6 +244,12 @@ __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.
 // 32 lanes x 32 columns of 32-bit: thread t of the warp gets lane (base+t),
 // columns col..col+31 in r[0..31].
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+#ifdef HARP_DEBUG_BOUNDS
+  if (!tmem_ok(taddr, 32, 221)) {
+    for (int i = 0; i < 32; ++i) r[i] = 0u;
+    return;
+  }
+#endif
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
       "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
@@ -197,6 +262,12 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+#ifdef HARP_DEBUG_BOUNDS
+  if (!tmem_ok(taddr, 16, 222)) {
+    for (int i = 0; i < 16; ++i) r[i] = 0u;
+    return;
+  }
+#endif
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
       "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
@@ -205,12 +276,19 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
       : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+#ifdef HARP_DEBUG_BOUNDS
+  if (!tmem_ok(taddr, 8, 223)) {
+    for (int i = 0; i < 8; ++i) r[i] = 0u;
+    return;
+  }
+#endif
   asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
                  "=r"(r[7])
                : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  HARP_CHECK_TMEM(taddr, 16, 224);
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
       "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
@@ -219,6 +297,7 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
       : "memory");
 }
 __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+  HARP_CHECK_TMEM(taddr, 8, 225);
   asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr),
                "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
                : "memory");

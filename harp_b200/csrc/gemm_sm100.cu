@@ -407,6 +407,7 @@ __device__ __forceinline__ void cluster_sync_all() {
 }
 __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t bar_cluster, int c0,
                                                  int c1) {
+  HARP_CHECK_TMA_X(c0, 204);
   asm volatile(
       "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
       "[%2];" ::"r"(smem_u32(dst)),
@@ -415,6 +416,7 @@ __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* m
 }
 __device__ __forceinline__ void mma_ss_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                             uint32_t accumulate) {
+  HARP_CHECK_TMEM(d_tmem, (int)(((idesc >> 17) & 0x3Fu) << 3), 214);
   asm volatile(
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),

@@ -45,6 +45,8 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 EncodeTiledFn get_encode_fn();
+void register_bounds_reader(void (*fn)(int*));
+at::Tensor debug_bounds_status();
 int num_sms();
 // 4-D bf16 map over a token-major [B, S, ld] activation holding H heads of Dh
 // elements per token: dims {Dh, H, S, B}; the box is 16 elements x 1 head x

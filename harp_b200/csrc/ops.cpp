@@ -230,6 +230,7 @@ TORCH_LIBRARY(harp, m) {
   m.def("gemm_pair_mode(int mode) -> int");
   m.def("gemm_probe() -> Tensor");
   m.def("set_weight_gate(Tensor? flags, int first, int count, int epoch, float timeout_s) -> ()");
+  m.def("debug_bounds_status() -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(harp, CUDA, m) {
@@ -259,6 +260,7 @@ TORCH_LIBRARY_IMPL(harp, CompositeExplicitAutograd, m) {
   m.impl("gemm_pair_mode", &harp::gemm_pair_mode_op);
   m.impl("gemm_probe", &harp::gemm_probe);
   m.impl("set_weight_gate", &harp::set_weight_gate);
+  m.impl("debug_bounds_status", &harp::debug_bounds_status);
 }
 
 TORCH_LIBRARY(xhpops, m) {

@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 
 #include <mutex>
+#include <vector>
 
 #include "gemm_sm100.h"
 
@@ -22,6 +23,29 @@ EncodeTiledFn get_encode_fn() {
     fn = reinterpret_cast<EncodeTiledFn>(p);
   });
   return fn;
+}
+
+// Readers of the bounds-check words of every translation unit compiled with
+// HARP_DEBUG_BOUNDS (each registers itself at load time).
+static std::vector<void (*)(int*)>& bounds_readers() {
+  static std::vector<void (*)(int*)> v;
+  return v;
+}
+void register_bounds_reader(void (*fn)(int*)) { bounds_readers().push_back(fn); }
+
+// First recorded bounds violation of any translation unit ({code, site, block,
+// info}; zeros when none or in a build without HARP_DEBUG_BOUNDS), then clear.
+at::Tensor debug_bounds_status() {
+  auto out = at::zeros({5}, at::TensorOptions().dtype(at::kInt));
+  int* o = out.data_ptr<int>();
+  for (auto fn : bounds_readers()) {
+    int w[4] = {0, 0, 0, 0};
+    fn(w);
+    if (o[0] == 0 && w[0] != 0)
+      for (int i = 0; i < 4; ++i) o[i] = w[i];
+  }
+  o[4] = (int)bounds_readers().size();  // translation units with checks compiled in
+  return out;
 }
 
 int num_sms() {

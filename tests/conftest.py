@@ -22,3 +22,20 @@ def pytest_collection_modifyitems(config, items):
     for item in items:
         if "gpu" in item.keywords:
             item.add_marker(skip)
+
+
+@pytest.fixture(autouse=True)
+def _bounds_clean(request):
+    """With HARP_DEBUG_BOUNDS=1 (the bounds-checking build), every GPU test
+    must leave no recorded TMA-coordinate or tensor-memory-column violation."""
+    yield
+    if os.environ.get("HARP_DEBUG_BOUNDS") != "1" or "gpu" not in request.keywords:
+        return
+    import torch
+
+    if not torch.cuda.is_available() or not hasattr(torch.ops, "harp") or not hasattr(torch.ops.harp,
+                                                                                       "debug_bounds_status"):
+        return
+    st = torch.ops.harp.debug_bounds_status().tolist()
+    assert st[4] > 0, "HARP_DEBUG_BOUNDS=1 but the loaded library has no bounds checks compiled in"
+    assert st[0] == 0, f"bounds violation {st[:4]} (code, site, block, info)"
