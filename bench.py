@@ -492,6 +492,9 @@ def main():
                               "n_gpus": ws, "steps": args.steps, "ms_per_step_timed": ms,
                               "note": "CUDA events on the launching stream, summed per step, max over ranks; "
                                       "nested phases (uly.*) are inside forward/backward"}), flush=True)
+    if args.impl == "harp":
+        torch.cuda.synchronize()
+        trainer.close()  # a captured step holding NCCL work goes before the process group
     if ws > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -173,6 +173,8 @@ struct FwdArgs {
   int chunk_len;
   int start_tile;
   unsigned int epoch;
+  const int* epoch_sd;  // graph replays: epoch + epoch_per_step * *epoch_sd (see step_value)
+  int epoch_per_step;
   int wait_q;  // queries arrive by chunk too (same flags): wait before loading a Q tile
   int q_rot;   // query-pair index rotation (start with the pairs whose chunk is local)
   int probe;   // record key-tile step timestamps of CTA 0 (HARP_ATTN_PROBE=1)
@@ -218,7 +220,7 @@ __device__ __forceinline__ void fwd_load_role(const CUtensorMap* tmQ, const CUte
   if (a.ready != nullptr && a.wait_q) {
     const int qend = min(q0 + 128 * ntile, a.Sq) - 1;
     for (int c = q0 / a.chunk_len; c <= qend / a.chunk_len && ok; ++c)
-      ok = wait_flag_geq(a.ready + c, a.epoch, a.timeout_ns, err, 19);
+      ok = wait_flag_geq(a.ready + c, step_value(a.epoch, a.epoch_sd, a.epoch_per_step), a.timeout_ns, err, 19);
     fence_proxy_async_global();
   }
   mbar_arrive_expect_tx(m.q_full, ntile * C::TILE);
@@ -229,7 +231,7 @@ __device__ __forceinline__ void fwd_load_role(const CUtensorMap* tmQ, const CUte
     if (a.ready != nullptr) {
       const int kend = min(key0 + 128, a.Skv) - 1;
       for (int c = key0 / a.chunk_len; c <= kend / a.chunk_len && ok; ++c)
-        ok = wait_flag_geq(a.ready + c, a.epoch, a.timeout_ns, err, 20);
+        ok = wait_flag_geq(a.ready + c, step_value(a.epoch, a.epoch_sd, a.epoch_per_step), a.timeout_ns, err, 20);
       if (!ok) break;
       fence_proxy_async_global();
     }
@@ -2246,7 +2248,8 @@ void launch_bwd(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap&
 void attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, int64_t B, int64_t Sq, int64_t Skv,
               int64_t H, int64_t Dh, double scale, at::Tensor& o, at::Tensor& lse,
               const c10::optional<at::Tensor>& ready, int64_t chunk_len, int64_t start_tile, int64_t epoch,
-              double timeout_s, at::Tensor& err, int64_t q_rot, bool wait_q) {
+              double timeout_s, at::Tensor& err, int64_t q_rot, bool wait_q,
+              const c10::optional<at::Tensor>& step_delta, int64_t epoch_per_step) {
   TORCH_CHECK(q.is_cuda() && k.is_cuda() && v.is_cuda() && o.is_cuda(), "attn_fwd: CUDA tensors");
   TORCH_CHECK(q.scalar_type() == at::kBFloat16 && k.scalar_type() == at::kBFloat16 &&
                   v.scalar_type() == at::kBFloat16 && o.scalar_type() == at::kBFloat16,
@@ -2283,6 +2286,13 @@ void attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, int
   args.chunk_len = chunk_len > 0 ? (int)chunk_len : (int)Skv;
   args.start_tile = (int)start_tile;
   args.epoch = (unsigned int)epoch;
+  args.epoch_sd = nullptr;
+  args.epoch_per_step = 0;
+  if (step_delta.has_value()) {
+    TORCH_CHECK(step_delta->is_cuda() && step_delta->scalar_type() == at::kInt, "attn_fwd: step_delta int32 CUDA");
+    args.epoch_sd = step_delta->data_ptr<int>();
+    args.epoch_per_step = (int)epoch_per_step;
+  }
   args.wait_q = (wait_q && args.ready != nullptr) ? 1 : 0;
   args.q_rot = (int)(q_rot % ((Sq + 255) / 256));
   args.timeout_ns = (unsigned long long)(timeout_s * 1e9);
@@ -2433,7 +2443,7 @@ void dq_finalize(const at::Tensor& acc, int64_t H, int64_t Dh, double scale, at:
 TORCH_LIBRARY_FRAGMENT(harp, m) {
   m.def("attn_fwd(Tensor q, Tensor k, Tensor v, int B, int Sq, int Skv, int H, int Dh, float scale, Tensor(a!) o, "
         "Tensor(b!) lse, Tensor? ready, int chunk_len, int start_tile, int epoch, float timeout_s, Tensor(c!) err, "
-        "int q_rot=0, bool wait_q=False) -> ()");
+        "int q_rot=0, bool wait_q=False, Tensor? step_delta=None, int epoch_per_step=0) -> ()");
   m.def("attn_bwd(Tensor q, Tensor k, Tensor v, Tensor dout, Tensor lse, Tensor delta, int B, int Sq, int Skv, "
         "int H, int Dh, float scale, Tensor(a!) dq_acc, Tensor(b!) dk, Tensor(c!) dv, Tensor(d!) err, "
         "int[] push_bases=[], int push_chunk=0, int push_rank=0, int push_slot=0, int push_ld=0, int push_vcol=0) -> ()");

@@ -52,19 +52,20 @@ std::unordered_map<int64_t, Segment> g_segments;
 // ---------------------------------------------------------------------------
 
 // flags[slot] on every peer (except `skip`) <- value, release at system scope.
-__global__ void signal_kernel(PeerTable flags, int world, int slot, unsigned int value, int skip) {
+__global__ void signal_kernel(PeerTable flags, int world, int slot, unsigned int value, int skip,
+                              const int* step_delta, int per_step) {
   const int r = threadIdx.x;
   if (r >= world || r == skip) return;
   __threadfence_system();
-  st_release_sys(reinterpret_cast<unsigned int*>(flags.base[r]) + slot, value);
+  st_release_sys(reinterpret_cast<unsigned int*>(flags.base[r]) + slot, step_value(value, step_delta, per_step));
 }
 
 // Wait until local flags[first .. first+count) >= value.
 __global__ void wait_kernel(const unsigned int* flags, int first, int count, unsigned int value,
-                            unsigned long long timeout_ns, int* err) {
+                            unsigned long long timeout_ns, int* err, const int* step_delta, int per_step) {
   const int i = threadIdx.x;
   if (i >= count) return;
-  wait_flag_geq(flags + first + i, value, timeout_ns, err, 100 + i);
+  wait_flag_geq(flags + first + i, step_value(value, step_delta, per_step), timeout_ns, err, 100 + i);
 }
 
 // Gather: for each source rank c (visited from rank+1 onwards), once
@@ -113,10 +114,11 @@ __device__ __forceinline__ void acc8(float (&a)[8], const uint4& v) {
 __global__ void reduce_scatter_kernel(PeerTable src, long long src_off, long long src_stride, bf16* __restrict__ dst,
                                       long long dst_stride, long long seg_elems, int nseg, int world, int rank,
                                       const unsigned int* flags, int flag_first, unsigned int value,
-                                      unsigned long long timeout_ns, int* err) {
+                                      unsigned long long timeout_ns, int* err, const int* step_delta, int per_step) {
   if (flags != nullptr) {
     if (threadIdx.x < world && threadIdx.x != rank)
-      wait_flag_geq(flags + flag_first + threadIdx.x, value, timeout_ns, err, 120 + threadIdx.x);
+      wait_flag_geq(flags + flag_first + threadIdx.x, step_value(value, step_delta, per_step), timeout_ns, err,
+                    120 + threadIdx.x);
     __syncthreads();
     if (*(volatile int*)err != 0) return;
   }
@@ -155,12 +157,19 @@ __global__ void rs_adamw_ag_kernel(PeerTable grads, PeerTable params, long long 
                                    float* __restrict__ master, float* __restrict__ m, float* __restrict__ v,
                                    AdamHyper h, int world, int rank, const unsigned int* flags, int flag_first,
                                    unsigned int value, unsigned long long timeout_ns, int* err,
-                                   bf16* __restrict__ local_out) {
+                                   bf16* __restrict__ local_out, const int* step_delta, int per_step,
+                                   const float* __restrict__ hyper) {
   if (flags != nullptr) {
     if (threadIdx.x < world && threadIdx.x != rank)
-      wait_flag_geq(flags + flag_first + threadIdx.x, value, timeout_ns, err, 130 + threadIdx.x);
+      wait_flag_geq(flags + flag_first + threadIdx.x, step_value(value, step_delta, per_step), timeout_ns, err,
+                    130 + threadIdx.x);
     __syncthreads();
     if (*(volatile int*)err != 0) return;
+  }
+  if (hyper != nullptr) {  // [lr, 1 - beta1^t, sqrt(1 - beta2^t)] of this step, on the device
+    h.lr = hyper[0];
+    h.bc1 = hyper[1];
+    h.bc2_sqrt = hyper[2];
   }
   const long long nv = n / 8;
   for (long long vi = (long long)blockIdx.x * blockDim.x + threadIdx.x; vi < nv;
@@ -277,20 +286,29 @@ at::Tensor view(int64_t ptr, int64_t numel, at::ScalarType dtype, int64_t device
   return at::from_blob(reinterpret_cast<void*>(ptr), {numel}, [](void*) {}, opts);
 }
 
-void signal(const std::vector<int64_t>& flag_bases, int64_t slot, int64_t value, int64_t skip) {
+const int* sd_ptr(const c10::optional<at::Tensor>& step_delta) {
+  if (!step_delta.has_value()) return nullptr;
+  TORCH_CHECK(step_delta->is_cuda() && step_delta->scalar_type() == at::kInt, "harp_comm: step_delta int32 CUDA");
+  return step_delta->data_ptr<int>();
+}
+
+void signal(const std::vector<int64_t>& flag_bases, int64_t slot, int64_t value, int64_t skip,
+            const c10::optional<at::Tensor>& step_delta, int64_t per_step) {
   const int world = flag_bases.size();
   signal_kernel<<<1, 32, 0, at::cuda::getCurrentCUDAStream()>>>(make_table(flag_bases, 0), world, (int)slot,
-                                                                 (unsigned)value, (int)skip);
+                                                                 (unsigned)value, (int)skip, sd_ptr(step_delta),
+                                                                 (int)per_step);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   count_launch();
 }
 
-void wait(const at::Tensor& flags, int64_t first, int64_t count, int64_t value, double timeout_s, at::Tensor& err) {
+void wait(const at::Tensor& flags, int64_t first, int64_t count, int64_t value, double timeout_s, at::Tensor& err,
+          const c10::optional<at::Tensor>& step_delta, int64_t per_step) {
   TORCH_CHECK(count <= 1024, "harp_comm: wait on at most 1024 flags");
   if (count <= 0) return;
   wait_kernel<<<1, (unsigned)((count + 31) / 32 * 32), 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const unsigned int*>(flags.data_ptr()), (int)first, (int)count, (unsigned)value,
-      (unsigned long long)(timeout_s * 1e9), err.data_ptr<int>());
+      (unsigned long long)(timeout_s * 1e9), err.data_ptr<int>(), sd_ptr(step_delta), (int)per_step);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   count_launch();
 }
@@ -317,7 +335,7 @@ void gather(const std::vector<int64_t>& src_bases, int64_t src_off, int64_t src_
 void reduce_scatter(const std::vector<int64_t>& src_bases, int64_t src_off, int64_t src_stride, at::Tensor& dst,
                     int64_t dst_stride, int64_t seg_elems, int64_t nseg, int64_t rank,
                     const c10::optional<at::Tensor>& flags, int64_t flag_first, int64_t value, double timeout_s,
-                    at::Tensor& err) {
+                    at::Tensor& err, const c10::optional<at::Tensor>& step_delta, int64_t per_step) {
   TORCH_CHECK(dst.scalar_type() == at::kBFloat16 && seg_elems % 8 == 0 && src_off % 8 == 0 && src_stride % 8 == 0 &&
                   dst_stride % 8 == 0,
               "harp_comm reduce_scatter: bf16, 8-element granularity");
@@ -327,7 +345,8 @@ void reduce_scatter(const std::vector<int64_t>& src_bases, int64_t src_off, int6
       make_table(src_bases, 0), src_off, src_stride, reinterpret_cast<bf16*>(dst.data_ptr()), dst_stride, seg_elems,
       (int)nseg, world, (int)rank,
       flags.has_value() ? reinterpret_cast<const unsigned int*>(flags->data_ptr()) : nullptr, (int)flag_first,
-      (unsigned)value, (unsigned long long)(timeout_s * 1e9), err.data_ptr<int>());
+      (unsigned)value, (unsigned long long)(timeout_s * 1e9), err.data_ptr<int>(), sd_ptr(step_delta),
+      (int)per_step);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   count_launch();
 }
@@ -336,7 +355,11 @@ void rs_adamw_ag(const std::vector<int64_t>& grad_bases, const std::vector<int64
                  at::Tensor& master, at::Tensor& m, at::Tensor& v, double lr, double beta1, double beta2, double eps,
                  double wd, int64_t step, double grad_scale, int64_t rank, const c10::optional<at::Tensor>& flags,
                  int64_t flag_first, int64_t value, double timeout_s, at::Tensor& err, int64_t blocks,
-                 const c10::optional<at::Tensor>& local_out) {
+                 const c10::optional<at::Tensor>& local_out, const c10::optional<at::Tensor>& step_delta,
+                 int64_t per_step, const c10::optional<at::Tensor>& hyper) {
+  if (hyper.has_value())
+    TORCH_CHECK(hyper->is_cuda() && hyper->scalar_type() == at::kFloat && hyper->numel() >= 3,
+                "harp_comm rs_adamw_ag: hyper fp32 [3] on the device");
   TORCH_CHECK(n % 8 == 0 && lo % 8 == 0, "harp_comm rs_adamw_ag: 8-element granularity");
   TORCH_CHECK(master.is_contiguous() && m.is_contiguous() && v.is_contiguous(), "harp_comm rs_adamw_ag: contiguous state");
   TORCH_CHECK(master.numel() == n && m.numel() == n && v.numel() == n, "harp_comm rs_adamw_ag: state size");
@@ -357,7 +380,8 @@ void rs_adamw_ag(const std::vector<int64_t>& grad_bases, const std::vector<int64
       v.data_ptr<float>(), h, world, (int)rank,
       flags.has_value() ? reinterpret_cast<const unsigned int*>(flags->data_ptr()) : nullptr, (int)flag_first,
       (unsigned)value, (unsigned long long)(timeout_s * 1e9), err.data_ptr<int>(),
-      local_out.has_value() ? reinterpret_cast<bf16*>(local_out->data_ptr()) : nullptr);
+      local_out.has_value() ? reinterpret_cast<bf16*>(local_out->data_ptr()) : nullptr, sd_ptr(step_delta),
+      (int)per_step, hyper.has_value() ? hyper->data_ptr<float>() : nullptr);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   count_launch();
 }
@@ -386,17 +410,19 @@ TORCH_LIBRARY(harp_comm, m) {
   m.def("ipc_open(Tensor handle, int device) -> int");
   m.def("ipc_release(int ptr) -> ()");
   m.def("view(int ptr, int numel, ScalarType dtype, int device) -> Tensor");
-  m.def("signal(int[] flag_bases, int slot, int value, int skip) -> ()");
-  m.def("wait(Tensor flags, int first, int count, int value, float timeout_s, Tensor(a!) err) -> ()");
+  m.def("signal(int[] flag_bases, int slot, int value, int skip, Tensor? step_delta=None, int per_step=0) -> ()");
+  m.def("wait(Tensor flags, int first, int count, int value, float timeout_s, Tensor(a!) err, "
+        "Tensor? step_delta=None, int per_step=0) -> ()");
   m.def("gather(int[] src_bases, int src_off, int src_stride, Tensor(a!) dst, int dst_off, int dst_chunk_stride, "
         "int dst_stride, int seg_bytes, int nseg, int rank, Tensor? flags, int flag_first, int value, float timeout_s, "
         "Tensor(b!) err) -> ()");
   m.def("reduce_scatter(int[] src_bases, int src_off, int src_stride, Tensor(a!) dst, int dst_stride, int seg_elems, "
-        "int nseg, int rank, Tensor? flags, int flag_first, int value, float timeout_s, Tensor(b!) err) -> ()");
+        "int nseg, int rank, Tensor? flags, int flag_first, int value, float timeout_s, Tensor(b!) err, "
+        "Tensor? step_delta=None, int per_step=0) -> ()");
   m.def("rs_adamw_ag(int[] grad_bases, int[] param_bases, int lo, int n, Tensor(a!) master, Tensor(b!) m, "
         "Tensor(c!) v, float lr, float beta1, float beta2, float eps, float wd, int step, float grad_scale, int rank, "
         "Tensor? flags, int flag_first, int value, float timeout_s, Tensor(d!) err, int blocks=0, "
-        "Tensor(e!)? local_out=None) -> ()");
+        "Tensor(e!)? local_out=None, Tensor? step_delta=None, int per_step=0, Tensor? hyper=None) -> ()");
   m.def("push_slice(Tensor src, int[] dst_bases, int off, int rank, int blocks=0) -> ()");
 }
 TORCH_LIBRARY_IMPL(harp_comm, CompositeExplicitAutograd, m) {

@@ -365,6 +365,15 @@ __device__ __forceinline__ unsigned int ld_acquire_gpu(const unsigned int* p) {
   return v;
 }
 
+// Epoch of a flag operation inside a CUDA graph that is replayed once per
+// training step: the value captured at the first step plus per_step times the
+// number of steps since, which the host keeps in *step_delta (nullptr: eager,
+// the captured value itself).
+__device__ __forceinline__ unsigned int step_value(unsigned int value, const int* step_delta, int per_step) {
+  if (step_delta == nullptr) return value;
+  return value + (unsigned int)(per_step * *(volatile const int*)step_delta);
+}
+
 // Bounded wait for *flag >= target (flag written by this GPU or a peer).
 __device__ __forceinline__ bool wait_flag_geq(const unsigned int* flag, unsigned int target,
                                               unsigned long long timeout_ns, int* err, int site) {

@@ -39,6 +39,8 @@ struct WeightGate {
   int n = 0;
   unsigned int epoch = 0;
   unsigned long long timeout_ns = 0;
+  const int* sd = nullptr;
+  int per_step = 0;
 };
 std::mutex g_gate_mu;
 WeightGate g_gate;
@@ -69,13 +71,16 @@ struct GemmArgs {
   int gate_n;
   unsigned int gate_epoch;
   unsigned long long gate_timeout_ns;
+  const int* gate_sd;  // graph replays: gate_epoch + gate_per_step * *gate_sd
+  int gate_per_step;
 };
 
 // Wait for the weight-readiness gate (one thread).
 __device__ __forceinline__ bool wait_weight_gate(const GemmArgs& a, int* err) {
   if (a.gate_flags == nullptr) return true;
   bool ok = true;
-  for (int i = 0; i < a.gate_n && ok; ++i) ok = wait_flag_geq(a.gate_flags + i, a.gate_epoch, a.gate_timeout_ns, err, 30 + i);
+  const unsigned int target = step_value(a.gate_epoch, a.gate_sd, a.gate_per_step);
+  for (int i = 0; i < a.gate_n && ok; ++i) ok = wait_flag_geq(a.gate_flags + i, target, a.gate_timeout_ns, err, 30 + i);
   return ok;
 }
 
@@ -939,6 +944,8 @@ void gemm(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, at::Te
     args.gate_n = g_gate.n;
     args.gate_epoch = g_gate.epoch;
     args.gate_timeout_ns = g_gate.timeout_ns;
+    args.gate_sd = g_gate.sd;
+    args.gate_per_step = g_gate.per_step;
   }
   if (K == 0) {
     // Degenerate: treat as zero accumulator.  Route through SIMT (K loop is empty).
@@ -986,7 +993,7 @@ void gemm(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, at::Te
 // (sharded parameters: the trainer sets it around a block whose gathered
 // weights are still arriving from peers; flags must stay alive while set).
 void set_weight_gate(const c10::optional<at::Tensor>& flags, int64_t first, int64_t count, int64_t epoch,
-                     double timeout_s) {
+                     double timeout_s, const c10::optional<at::Tensor>& step_delta, int64_t per_step) {
   std::lock_guard<std::mutex> lock(g_gate_mu);
   if (!flags.has_value() || count <= 0) {
     g_gate = WeightGate{};
@@ -998,6 +1005,8 @@ void set_weight_gate(const c10::optional<at::Tensor>& flags, int64_t first, int6
   g_gate.n = (int)count;
   g_gate.epoch = (unsigned int)epoch;
   g_gate.timeout_ns = (unsigned long long)(timeout_s * 1e9);
+  g_gate.sd = step_delta.has_value() ? step_delta->data_ptr<int>() : nullptr;
+  g_gate.per_step = (int)per_step;
 }
 
 at::Tensor gemm_probe() {

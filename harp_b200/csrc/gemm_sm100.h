@@ -38,7 +38,8 @@ at::Tensor gemm_probe();
 // flags[first .. first+count) >= epoch (flags written by peers when their
 // slices of gathered weights have landed); flags = None clears the gate.
 void set_weight_gate(const c10::optional<at::Tensor>& flags, int64_t first, int64_t count, int64_t epoch,
-                     double timeout_s);
+                     double timeout_s, const c10::optional<at::Tensor>& step_delta = c10::nullopt,
+                     int64_t per_step = 0);
 
 // Shared host helpers (runtime.cpp).
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,

@@ -229,7 +229,8 @@ TORCH_LIBRARY(harp, m) {
   m.def("rows_per_block(int rows_per_batch) -> int");
   m.def("gemm_pair_mode(int mode) -> int");
   m.def("gemm_probe() -> Tensor");
-  m.def("set_weight_gate(Tensor? flags, int first, int count, int epoch, float timeout_s) -> ()");
+  m.def("set_weight_gate(Tensor? flags, int first, int count, int epoch, float timeout_s, Tensor? step_delta=None, "
+        "int per_step=0) -> ()");
   m.def("debug_bounds_status() -> Tensor");
 }
 

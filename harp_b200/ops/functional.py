@@ -435,7 +435,7 @@ def silu_bwd(dy: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
 # attention (local; ring variants live in harp_b200.parallel.ring_attention)
 # ---------------------------------------------------------------------------
 def attn_fwd(q, k, v, B, Sq, Skv, H, Dh, scale=None, ready=None, chunk_len=0, start_tile=0, epoch=0,
-             timeout_s=10.0, out=None, q_rot=0, wait_q=False):
+             timeout_s=10.0, out=None, q_rot=0, wait_q=False, step_delta=None, epoch_per_step=0):
     """q [B*Sq, >=H*Dh], k/v [B*Skv, >=H*Dh] token-major.  Returns (o [B*Sq, H*Dh],
     lse fp32 [B, H, lse_ld(Sq)] natural log, +inf past Sq).  With `ready`, key
     (and, with wait_q, query) rows of chunk c = row // chunk_len are used only
@@ -445,7 +445,7 @@ def attn_fwd(q, k, v, B, Sq, Skv, H, Dh, scale=None, ready=None, chunk_len=0, st
     lse = torch.full((B * H * lse_ld(Sq),), float("inf"), device=q.device)
     if _cuda(q):
         torch.ops.harp.attn_fwd(q, k, v, B, Sq, Skv, H, Dh, scale, o, lse, ready, chunk_len, start_tile, epoch,
-                                timeout_s, errors.word(q.device), q_rot, wait_q)
+                                timeout_s, errors.word(q.device), q_rot, wait_q, step_delta, epoch_per_step)
         return o, lse
     qf = q[:, : H * Dh].float().view(B, Sq, H, Dh)
     kf = k[:, : H * Dh].float().view(B, Skv, H, Dh)

@@ -141,7 +141,12 @@ class NVLinkComm:
         self.flags_buf = SymBuffer(group, _NFLAGS * 4, device)
         self.flags = self.flags_buf.tensor(_NFLAGS, torch.int32)
         self.flag_bases = self.flags_buf.bases
-        self.epoch = {"kv": 0, "dkv": 0, "grad": 0, "barrier": 0, "uq": 0, "uo": 0, "udo": 0, "udq": 0}
+        self.epoch = {"kv": 0, "dkv": 0, "grad": 0, "barrier": 0, "uq": 0, "uo": 0, "udo": 0, "udq": 0,
+                      "gath0": 0, "gath1": 0, "use0": 0, "use1": 0}
+        # CUDA-graph replays of a whole step: flag values are (captured value) +
+        # (increments per step of their counter) * step_delta[0]
+        self.step_delta = torch.zeros(1, dtype=torch.int32, device=device)
+        self._per_step: Optional[Dict[str, int]] = None
         self._uly: List[Dict[str, SymBuffer]] = []
         self._uly_idx = 0
         self._kv_bufs: List[SymBuffer] = []
@@ -160,19 +165,39 @@ class NVLinkComm:
     def err(self) -> torch.Tensor:
         return errors.word(self.device)
 
-    def signal(self, base: int, value: int):
-        """Store `value` into slot base+rank of every rank's flag array (self included)."""
-        torch.ops.harp_comm.signal([b + 4 * base for b in self.flag_bases], self.rank, value, -1)
+    # -- CUDA-graph capture of a step ---------------------------------------------
+    def begin_capture(self, per_step: Dict[str, int]):
+        """Kernels issued from now on compute their flag values on the device:
+        the value at capture plus per_step[counter] * step_delta[0]."""
+        self._per_step = dict(per_step)
+        self.step_delta.zero_()
 
-    def wait_all(self, base: int, value: int):
+    def end_capture(self):
+        self._per_step = None
+
+    def _sd(self, counter: Optional[str]):
+        if self._per_step is None or counter is None:
+            return None, 0
+        return self.step_delta, self._per_step.get(counter, 0)
+
+    def _eager_only(self, what: str):
+        assert self._per_step is None, f"{what} cannot be captured in a CUDA graph"
+
+    def signal(self, base: int, value: int, counter: Optional[str] = None):
+        """Store `value` into slot base+rank of every rank's flag array (self included)."""
+        sd, ps = self._sd(counter)
+        torch.ops.harp_comm.signal([b + 4 * base for b in self.flag_bases], self.rank, value, -1, sd, ps)
+
+    def wait_all(self, base: int, value: int, counter: Optional[str] = None):
         """Wait (on the current stream) until every rank's slot base+c >= value."""
-        torch.ops.harp_comm.wait(self.flags, base, self.world, value, self.timeout_s, self.err)
+        sd, ps = self._sd(counter)
+        torch.ops.harp_comm.wait(self.flags, base, self.world, value, self.timeout_s, self.err, sd, ps)
 
     def barrier(self):
         self.epoch["barrier"] += 1
         e = self.epoch["barrier"]
-        self.signal(_BARRIER, e)
-        self.wait_all(_BARRIER, e)
+        self.signal(_BARRIER, e, "barrier")
+        self.wait_all(_BARRIER, e, "barrier")
 
     def begin_step(self):
         self._kv_idx = 0
@@ -183,6 +208,7 @@ class NVLinkComm:
     def kv_exchange(self, k: torch.Tensor, v: torch.Tensor, B: int, S: int, HD: int):
         """k, v: local [B*S, HD] views.  Returns (kv_full [B*W*S, 2HD], None, 0):
         rows (b*W + c)*S .. +S of kv_full hold rank c's K|V of sample b."""
+        self._eager_only("kv_exchange")
         i = self._kv_idx
         self._kv_idx += 1
         nbytes = B * S * 2 * HD * 2
@@ -231,12 +257,14 @@ class NVLinkComm:
         with phase("ring.dispatch_kv"):
             torch.ops.harp_comm.ring_dispatch_qkv(q, k, v, S, H, Dh, r, buf.bases, 2 * HD, qf, wq, wk, freqs,
                                                   freqs.shape[0] if freqs is not None else 1, eps, do_norm, rq, rk)
-            self.signal(_KV, e)
+            self.signal(_KV, e, "kv")
         kv = buf.tensor(B * W * S * 2 * HD, torch.bfloat16).view(B * W * S, 2 * HD)
         qq = q if q_ready else qf
         with phase("ring.attn_fwd"):
+            sd, ps = self._sd("kv")
             o, lse = Fn.attn_fwd(qq, kv[:, :HD], kv[:, HD:], B, S, W * S, H, Dh, ready=self.flags[_KV:_KV + W],
-                                 chunk_len=S, start_tile=(r * S) // 128, epoch=e, timeout_s=self.timeout_s)
+                                 chunk_len=S, start_tile=(r * S) // 128, epoch=e, timeout_s=self.timeout_s,
+                                 step_delta=sd, epoch_per_step=ps)
         return o, qq, rq, rk, {"lse": lse, "kv": kv}
 
     def ring_backward(self, saved, q, o, do, B: int, S: int, H: int, Dh: int, out: Optional[torch.Tensor] = None,
@@ -259,7 +287,7 @@ class NVLinkComm:
         last = self._dkv_last_epoch[j]
         if last > 0:  # every rank has summed what this buffer held two layers ago
             with phase("ring.dkv_ack_wait"):
-                self.wait_all(_DKV_ACK0 if j == 0 else _DKV_ACK1, last)
+                self.wait_all(_DKV_ACK0 if j == 0 else _DKV_ACK1, last, "dkv")
         kv = saved["kv"]
         with phase("ring.attn_bwd"):
             dq, _, _ = Fn.attn_bwd(q, kv[:, :HD], kv[:, HD:], o, do, saved["lse"], B, S, W * S, H, Dh,
@@ -267,17 +295,18 @@ class NVLinkComm:
                                          "vcol": HD})
         self.epoch["dkv"] += 1
         e = self.epoch["dkv"]
-        self.signal(_DKV, e)
+        self.signal(_DKV, e, "dkv")
         if out is None:
             out = torch.empty(B * S, 2 * HD, device=q.device, dtype=torch.bfloat16)
             out_ld = 2 * HD
         own = buf.bases[r]
+        sd, ps = self._sd("dkv")
         with phase("ring.dkv_reduce"):
             # sum of the W slots (slot c written by rank c), row by row into `out`
             torch.ops.harp_comm.reduce_scatter([own + c * slot * 2 for c in range(W)], 0, 2 * HD, out, out_ld,
-                                               2 * HD, B * S, r, self.flags, _DKV, e, self.timeout_s, self.err)
+                                               2 * HD, B * S, r, self.flags, _DKV, e, self.timeout_s, self.err, sd, ps)
         self._dkv_last_epoch[j] = e
-        self.signal(_DKV_ACK0 if j == 0 else _DKV_ACK1, e)
+        self.signal(_DKV_ACK0 if j == 0 else _DKV_ACK1, e, "dkv")
         return dq, out
 
     # -- sequence-parallel dK/dV reduce-scatter (backward) ----------------------
@@ -294,6 +323,7 @@ class NVLinkComm:
         return self._dkv_bufs[slot].tensor(rows * cols, torch.bfloat16).view(rows, cols)
 
     def dkv_reduce_scatter(self, dkv_full: torch.Tensor, B: int, S: int, HD: int) -> torch.Tensor:
+        self._eager_only("dkv_reduce_scatter")
         slot = self._dkv_idx % 2
         self._dkv_idx += 1
         buf = self._dkv_bufs[slot]
@@ -342,19 +372,20 @@ class NVLinkComm:
         with phase("uly.dispatch_qkv"):
             torch.ops.harp_comm.uly_dispatch_qkv(qkv, S, H, Dh, r, bufs["qkvf"].bases, part, wq, wk, freqs,
                                                  freqs.shape[0] if freqs is not None else 1, eps, do_norm, rq, rk)
-            self.signal(_UQKV, e)
+            self.signal(_UQKV, e, "uq")
         qkvf = bufs["qkvf"].tensor(3 * part, torch.bfloat16).view(3, B * Sf, Hn * Dh)
+        sd, ps = self._sd("uq")
         with phase("uly.attn_fwd"):
             o_f, lse = Fn.attn_fwd(qkvf[0], qkvf[1], qkvf[2], B, Sf, Sf, Hn, Dh, ready=self.flags[_UQKV:_UQKV + W],
                                    chunk_len=S, start_tile=(r * S) // 128, epoch=e, timeout_s=self.timeout_s,
-                                   q_rot=(r * S) // 256, wait_q=True)
+                                   q_rot=(r * S) // 256, wait_q=True, step_delta=sd, epoch_per_step=ps)
         self.epoch["uo"] += 1
         eo = self.epoch["uo"]
         with phase("uly.o_remap"):
             torch.ops.harp_comm.uly_remap([o_f], 1, B, S, r, H, Dh, bufs["o"].bases, 0, HD, 0)
-            self.signal(_UO, eo)
+            self.signal(_UO, eo, "uo")
         with phase("uly.o_wait"):
-            self.wait_all(_UO, eo)
+            self.wait_all(_UO, eo, "uo")
         o = bufs["o"].tensor(B * S * HD, torch.bfloat16).view(B * S, HD)
         return o, rq, rk, {"i": i, "qkvf": qkvf, "o_f": o_f, "lse": lse}
 
@@ -369,9 +400,9 @@ class NVLinkComm:
         e = self.epoch["udo"]
         with phase("uly.do_remap"):
             torch.ops.harp_comm.uly_remap([do], 0, B, S, r, H, Dh, bufs["dof"].bases, 0, 0, 0)
-            self.signal(_UDO, e)
+            self.signal(_UDO, e, "udo")
         with phase("uly.do_wait"):
-            self.wait_all(_UDO, e)
+            self.wait_all(_UDO, e, "udo")
         dof = bufs["dof"].tensor(B * Sf * Hn * Dh, torch.bfloat16).view(B * Sf, Hn * Dh)
         qkvf = saved["qkvf"]
         with phase("uly.attn_bwd"):
@@ -381,9 +412,9 @@ class NVLinkComm:
         e2 = self.epoch["udq"]
         with phase("uly.dqkv_remap"):
             torch.ops.harp_comm.uly_remap([dq_f, dk_f, dv_f], 1, B, S, r, H, Dh, bufs["dqkv"].bases, 0, 3 * HD, HD)
-            self.signal(_UDQ, e2)
+            self.signal(_UDQ, e2, "udq")
         with phase("uly.dqkv_wait"):
-            self.wait_all(_UDQ, e2)
+            self.wait_all(_UDQ, e2, "udq")
         return bufs["dqkv"].tensor(B * S * 3 * HD, torch.bfloat16).view(B * S, 3 * HD)
 
     # -- gradients: fused reduce-scatter + AdamW + parameter push ---------------
@@ -401,22 +432,24 @@ class NVLinkComm:
         """Before touching parameters or gradients of a new step: every peer has
         pushed its updated shard (and therefore finished reading our gradients)."""
         if self.epoch["grad"] > 0:
-            self.wait_all(_PARAM, self.epoch["grad"])
+            self.wait_all(_PARAM, self.epoch["grad"], "grad")
 
-    def _rs_adamw_segment(self, opt, seg, slot: int, e: int, blocks: int = 0):
+    def _rs_adamw_segment(self, opt, seg, slot: int, e: int, blocks: int = 0, local_out=None):
         f, n, o = seg
         cfg = opt.cfg
+        sd, ps = self._sd("grad")
         torch.ops.harp_comm.rs_adamw_ag(self._flat["grad"].bases, self._flat["param"].bases, f, n,
                                         opt.master[o:o + n], opt.m[o:o + n], opt.v[o:o + n], opt.lr, cfg.beta1,
                                         cfg.beta2, cfg.eps, cfg.weight_decay, opt.step_count, cfg.grad_scale,
-                                        self.rank, self.flags, slot, e, self.timeout_s, self.err, blocks)
+                                        self.rank, self.flags, slot, e, self.timeout_s, self.err, blocks, local_out,
+                                        sd, ps, opt.hyper)
 
     def rs_adamw_ag(self, flat, opt):
         """Whole-buffer form, after backward: one signal, one fused kernel per bucket."""
         assert self._flat is not None, "flat buffers must come from allocate_flat()"
         self.epoch["grad"] += 1
         e = self.epoch["grad"]
-        self.signal(_GRAD, e)
+        self.signal(_GRAD, e, "grad")
         opt.step_count += 1
         with phase("grad.rs_adamw_push"):
             for b, seg in enumerate(opt.segments):
@@ -425,7 +458,7 @@ class NVLinkComm:
                     self._rs_adamw_segment(opt, seg, _GRAD, e)
                 else:
                     self._rs_adamw_local(opt, seg, _GRAD, e, out)
-        self.signal(_PARAM, e)
+        self.signal(_PARAM, e, "grad")
 
     # -- sharded parameters: staging slots, all-gather push, acks --------------
     def param_slots(self, numel: int) -> SymBuffer:
@@ -440,35 +473,39 @@ class NVLinkComm:
         n = self._slot_numel
         return self._slots.tensor(2 * n, torch.bfloat16)[s * n:(s + 1) * n]
 
-    def gather_slice(self, s: int, src: torch.Tensor, off: int, epoch: int, wait_uses: int, blocks: int = 32):
+    def gather_slice(self, s: int, src: torch.Tensor, off: int):
         """Push this rank's slice `src` into offset `off` of staging slot s on
-        every rank, after every rank has finished `wait_uses` uses of the
-        slot; then set GATH[s] = epoch (all on the current stream)."""
-        if wait_uses > 0:
-            self.wait_all(_GACK + 8 * s, wait_uses)
+        every rank, after every rank has finished every earlier use of the
+        slot; then set GATH[s] to the slot's new gather count (all on the
+        current stream).  Returns that count."""
+        uses = self.epoch[f"use{s}"]
+        if uses > 0:
+            self.wait_all(_GACK + 8 * s, uses, f"use{s}")
         n = self._slot_numel
         bases = [b + (s * n + off) * 2 for b in self._slots.bases]
-        torch.ops.harp_comm.push_slice(src, bases, 0, self.rank, blocks)
-        self.signal(_GATH + 8 * s, epoch)
+        torch.ops.harp_comm.push_slice(src, bases, 0, self.rank, 32)
+        self.epoch[f"gath{s}"] += 1
+        self.signal(_GATH + 8 * s, self.epoch[f"gath{s}"], f"gath{s}")
+        return self.epoch[f"gath{s}"]
 
-    def gate_slot(self, s: int, epoch: int):
-        """GEMMs launched from now on wait for every rank's GATH[s] >= epoch."""
-        torch.ops.harp.set_weight_gate(self.flags, _GATH + 8 * s, self.world, epoch, self.timeout_s)
+    def gate_slot(self, s: int):
+        """GEMMs launched from now on wait until every rank's GATH[s] reached
+        the slot's current gather count."""
+        sd, ps = self._sd(f"gath{s}")
+        torch.ops.harp.set_weight_gate(self.flags, _GATH + 8 * s, self.world, self.epoch[f"gath{s}"], self.timeout_s,
+                                       sd, ps)
 
     @staticmethod
     def clear_gate():
         torch.ops.harp.set_weight_gate(None, 0, 0, 0, 0.0)
 
-    def ack_slot(self, s: int, uses: int):
-        self.signal(_GACK + 8 * s, uses)
+    def ack_slot(self, s: int):
+        """This rank finished one more use of staging slot s."""
+        self.epoch[f"use{s}"] += 1
+        self.signal(_GACK + 8 * s, self.epoch[f"use{s}"], f"use{s}")
 
     def _rs_adamw_local(self, opt, seg, slot: int, e: int, out: torch.Tensor, blocks: int = 0):
-        f, n, o = seg
-        cfg = opt.cfg
-        torch.ops.harp_comm.rs_adamw_ag(self._flat["grad"].bases, self._flat["param"].bases, f, n,
-                                        opt.master[o:o + n], opt.m[o:o + n], opt.v[o:o + n], opt.lr, cfg.beta1,
-                                        cfg.beta2, cfg.eps, cfg.weight_decay, opt.step_count, cfg.grad_scale,
-                                        self.rank, self.flags, slot, e, self.timeout_s, self.err, blocks, out)
+        self._rs_adamw_segment(opt, seg, slot, e, blocks, local_out=out)
 
     # overlapped form: begin_grad_sync, then rs_adamw_bucket per bucket in a
     # fixed order as gradients complete, then end_grad_sync
@@ -483,7 +520,7 @@ class NVLinkComm:
         peers from this stream, then enqueue the bucket's pull-reduce + AdamW +
         push on `stream` behind that point."""
         e = self.epoch["grad"]
-        self.signal(_GRADB + 8 * b, e)
+        self.signal(_GRADB + 8 * b, e, "grad")
         ev = torch.cuda.Event()
         ev.record()
         stream.wait_event(ev)
@@ -498,7 +535,7 @@ class NVLinkComm:
         """After the last bucket: announce the new parameters, and make the
         current stream wait for the side stream."""
         with torch.cuda.stream(stream):
-            self.signal(_PARAM, self.epoch["grad"])
+            self.signal(_PARAM, self.epoch["grad"], "grad")
         torch.cuda.current_stream().wait_stream(stream)
 
     def close(self):

@@ -166,8 +166,6 @@ class ParamGatherer:
         self.bucket_block = {b: l for l, b in enumerate(self.block_bucket) if b >= 0}
         self.step = 0
         self.content: List[Optional[tuple]] = [None, None]
-        self.gathers = [0, 0]
-        self.uses = [0, 0]
         self._pushed: Dict[int, torch.cuda.Event] = {}
         self._released: set = set()
         self.active = False
@@ -198,10 +196,8 @@ class ParamGatherer:
         ev = torch.cuda.Event()
         ev.record()
         self.stream.wait_event(ev)
-        self.gathers[s] += 1
         with torch.cuda.stream(self.stream):
-            self.comm.gather_slice(s, self.flat.local_slice(b), self.comm.rank * self.flat.local_slice(b).numel(),
-                                   self.gathers[s], self.uses[s])
+            self.comm.gather_slice(s, self.flat.local_slice(b), self.comm.rank * self.flat.local_slice(b).numel())
         done = torch.cuda.Event()
         done.record(self.stream)
         self.content[s] = (b, self.step)
@@ -213,13 +209,12 @@ class ParamGatherer:
         # this rank's own slice: a stream dependency, not a flag spin
         torch.cuda.current_stream().wait_event(self._pushed[s])
         self.flat.point(self.block_bucket[l], s)
-        self.comm.gate_slot(s, self.gathers[s])
+        self.comm.gate_slot(s)
 
     def _release(self, l: int):
         s = l % 2
         self.comm.clear_gate()
-        self.uses[s] += 1
-        self.comm.ack_slot(s, self.uses[s])
+        self.comm.ack_slot(s)
 
     def _pre_forward(self, l, module, args):
         if not self.active:

@@ -406,11 +406,21 @@ class Trainer:
         self._graph_loss: Optional[torch.Tensor] = None
         self._graph_launches = 0
         self._eager_steps = 0
-        self.graph_enabled = bool(cfg.cuda_graph) and on_gpu and par.world_size == 1
+        self._replays = 0
+        self._epoch_incr: Dict[int, Dict[str, int]] = {}
+        # multi-GPU steps are captured when every exchange is an NVLink kernel
+        # (their flag values then come from the device: NVLinkComm.begin_capture)
+        multi_ok = (self.grad_comm is not None and (par.sp_size == 1 or self.sp_comm is not None)
+                    and os.environ.get("HARP_GRAPH_MULTI", "0") == "1")
+        self.graph_enabled = bool(cfg.cuda_graph) and on_gpu and (par.world_size == 1 or multi_ok)
 
     # -- device-resident step (inputs already on the GPU) -------------------
+    def _comms(self):
+        return list({id(c): c for c in (self.sp_comm, self.grad_comm) if c is not None}.values())
+
     def train_step(self, latent, noise, text, sigmas, **extra) -> torch.Tensor:
-        for comm in {id(c): c for c in (self.sp_comm, self.grad_comm) if c is not None}.values():
+        epochs0 = {id(c): dict(c.epoch) for c in self._comms()}
+        for comm in self._comms():
             comm.begin_step()
         if self.grad_comm is not None:
             # peers' parameter shards of the previous step have landed and they
@@ -435,6 +445,10 @@ class Trainer:
         if self.par.world_size > 1:
             C.all_reduce_sum_(lsum, self.par.world_group)
             # each SP group holds one sample set: undo the dp split and sum of SP partials
+        # increments of every flag counter over one step (what a captured step
+        # adds per replay)
+        self._epoch_incr = {id(c): {k: v - epochs0[id(c)].get(k, 0) for k, v in c.epoch.items()}
+                            for c in self._comms()}
         return lsum
 
     def _saved_tensor_ctx(self):
@@ -523,6 +537,8 @@ class Trainer:
             try:
                 self._capture(batch)
             except RuntimeError as e:  # an op that cannot be captured: stay eager
+                if self.par.world_size > 1:
+                    raise  # every rank must take the same path
                 import warnings
 
                 warnings.warn(f"harp_b200: CUDA-graph capture of the step failed ({e}); running eagerly")
@@ -532,6 +548,10 @@ class Trainer:
         for k, v in batch.items():
             self._graph_inputs[k].copy_(v, non_blocking=True)
         self.opt.advance()
+        if self._replays > 0:  # the captured flag values are those of the first replay
+            for c in self._comms():
+                c.step_delta.add_(1)
+        self._replays += 1
         self._graph.replay()
         torch.ops.harp.add_launch_count(self._graph_launches)
         self.global_step += 1
@@ -549,8 +569,16 @@ class Trainer:
         extra = {k: v for k, v in b.items() if k not in ("latent", "noise", "text", "sigmas")}
         before = int(torch.ops.harp.launch_count())
         step_count, global_step = self.opt.step_count, self.global_step
-        with torch.cuda.graph(graph):
-            loss = self.train_step(b["latent"], b["noise"], b["text"], b["sigmas"], **extra)
+        comms = self._comms()
+        for c in comms:  # flag values of the captured kernels advance per replay on the device
+            c.begin_capture(self._epoch_incr.get(id(c), {}))
+        try:
+            with torch.cuda.graph(graph):
+                loss = self.train_step(b["latent"], b["noise"], b["text"], b["sigmas"], **extra)
+        finally:
+            for c in comms:
+                c.end_capture()
+        self._replays = 0
         # capture recorded the kernels without running them: take back the
         # launch count and step counters it advanced; every replay re-adds them
         self._graph_launches = int(torch.ops.harp.launch_count()) - before
@@ -581,6 +609,13 @@ class Trainer:
             views = self.flat.state_dict_views(self.par.world_group)
             sd.update({k: v for k, v in views.items() if k in sd})
         return sd
+
+    def close(self):
+        """Release the captured step (it may hold NCCL work: release it before
+        the process group goes away)."""
+        self._graph = None
+        self._graph_loss = None
+        self._graph_inputs = None
 
     def check_errors(self):
         if torch.device(self.device).type == "cuda":

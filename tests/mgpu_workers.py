@@ -37,17 +37,20 @@ def train(rank, world, out, args):
     model = model.to(torch.bfloat16)
     par = ParallelState.build(world)
     cfg = TrainConfig(lr=1e-3, comm=args["comm"], overlap_grad_sync=args.get("overlap", True),
-                      bucket_params=args.get("bucket_params", 64_000_000), shard_params=args.get("shard", False))
+                      bucket_params=args.get("bucket_params", 64_000_000), shard_params=args.get("shard", False),
+                      cuda_graph=args.get("graph", False), graph_warmup=2)
     tr = Trainer(model, par, cfg, dev, sp_backend=args["backend"], sp_mode=args["mode"])
     batch = torch.load(args["batch"])
     losses = [tr.step({k: v.pin_memory() for k, v in batch.items()}) for _ in range(args["steps"])]
     tr.check_errors()
+    graph_replays = tr._replays
+    tr.close()
     # parameters in registration order (independent of the flat buffer's bucket
     # layout; with sharded parameters gathered from their owners)
     sd = tr.model_state_dict()
     flat = torch.cat([sd[n].detach().reshape(-1) for n, _ in model.named_parameters()]).cpu()
     return {"losses": losses, "flat": flat, "mode": tr.sp.mode, "backend": tr.sp.backend,
-            "buckets": len(tr.flat.buckets), "overlap": tr._overlap}
+            "buckets": len(tr.flat.buckets), "overlap": tr._overlap, "graph_replays": graph_replays}
 
 
 def flag_timeout(rank, world, out, args):

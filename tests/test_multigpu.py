@@ -86,6 +86,27 @@ def test_sp2_training_matches_one_gpu(tmp_path, mode, backend, comm, overlap, bu
     assert torch.equal(res[0]["flat"], res[1]["flat"])
 
 
+@pytest.mark.parametrize("mode,shard", [("ulysses", False), ("ring", True)])
+def test_sp2_cuda_graph_step_matches_eager(tmp_path, monkeypatch, mode, shard):
+    """The whole 2-GPU step captured once and replayed (flag values advanced on
+    the device per replay) gives the eager steps bit for bit."""
+    _need(2)
+    bpath = str(tmp_path / "batch.pt")
+    _batch(bpath)
+    res = {}
+    monkeypatch.setenv("HARP_GRAPH_MULTI", "1")
+    for graph in (False, True):
+        d = tmp_path / f"g{int(graph)}"
+        d.mkdir()
+        res[graph] = _run("train", 2, d, {"batch": bpath, "steps": 5, "mode": mode, "backend": "nvl", "comm": "nvl",
+                                          "overlap": True, "bucket_params": 1_000_000, "shard": shard,
+                                          "graph": graph})
+    for r in (0, 1):
+        assert res[True][r]["graph_replays"] == 3, res[True][r]["graph_replays"]
+        assert res[True][r]["losses"] == res[False][r]["losses"], (res[True][r]["losses"], res[False][r]["losses"])
+        assert torch.equal(res[True][r]["flat"], res[False][r]["flat"])
+
+
 def test_never_signalled_flag_times_out_cleanly(tmp_path):
     _need(2)
     res = _run("flag_timeout", 2, tmp_path, {})
