@@ -150,9 +150,10 @@ class ZImageTransformerBlock(nn.Module):
             return x + gate_mlp * self.ffn_norm2(self.feed_forward(self.ffn_norm1(x) * scale_mlp))
         a = attn(self.attention_norm1(x), freqs, sp)
         x = x + self.attention_norm2(a)
-        if compat:
+        if compat == "joint":  # HARP block.py:106-118: Z_JointBlock drops the input residual here too
             h = self.feed_forward(self.ffn_norm1(x))
             return h + self.ffn_norm2(h)
+        # Z_SingleBlock keeps the base model's residual without modulation (block.py:51-58)
         return x + self.ffn_norm2(self.feed_forward(self.ffn_norm1(x)))
 
 
@@ -335,7 +336,14 @@ class Z_SingleBlock(nn.Module):
         return self.z_block(hidden_states, RoPE_embeds, adaln_input, sp, attention=self.attention, compat=self.compat)
 
 
-Z_JointBlock = Z_SingleBlock
+class Z_JointBlock(Z_SingleBlock):
+    """module/block.py:62-118: same as Z_SingleBlock except, with
+    harp_block_compat and no modulation, the MLP output replaces the residual
+    stream (h + norm2(h)) instead of being added to it."""
+
+    def forward(self, hidden_states, attn_mask=None, RoPE_embeds=None, adaln_input=None, sp=None):
+        return self.z_block(hidden_states, RoPE_embeds, adaln_input, sp, attention=self.attention,
+                            compat="joint" if self.compat else False)
 
 
 class Z_Transformer(nn.Module):

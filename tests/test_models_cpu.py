@@ -264,3 +264,83 @@ def test_timestep_embeddings_closed_form():
     emb = E.TimestepEmbedder(32, frequency_embedding_size=16)
     assert {n for n, _ in emb.named_parameters()} == {"mlp.0.weight", "mlp.0.bias", "mlp.2.weight", "mlp.2.bias"}
     assert emb(t).shape == (3, 32)
+
+
+def test_zimage_legacy_matches_base_and_groups_variable_sizes():
+    """The legacy (non-SP, variable-size) Z-Image wrapper: on equal-size samples
+    without padding it gives the base model's output; a batch of mixed image
+    sizes and caption lengths gives each sample's output on its own; the LoRA
+    target names resolve to modules."""
+    import copy
+
+    from harp_b200.models import zimage_legacy as ZL
+
+    torch.manual_seed(0)
+    pre = Z.PRESETS["zimage-tiny"]
+    base = Z.ZImageTransformer2DModel(**pre)
+    with torch.no_grad():
+        for p in base.parameters():
+            p.normal_(0, 0.05)
+    base = base.bfloat16()
+    ref_base = copy.deepcopy(base)
+    model = ZL.Z_Transformer(base, num_metadata=0, use_cond=True)
+    cdim = pre["cap_feat_dim"]
+    x = [torch.randn(16, 1, 16, 16).bfloat16() for _ in range(2)]
+    t = torch.rand(2)
+    caps = [torch.randn(32, cdim).bfloat16() for _ in range(2)]
+    with torch.no_grad():
+        want = ref_base(x, t, caps)["sample"]
+        got = model(x, t, caps)["sample"]
+    for a, b in zip(got, want):
+        assert a.shape == b.shape == (16, 1, 16, 16)
+        torch.testing.assert_close(a.float(), b.float(), rtol=0, atol=0)
+
+    # mixed sizes: 16x16 and 12x20 latents (60 tokens -> padded to 64), captions of 20, 45, 20 tokens
+    xs = [torch.randn(16, 1, 16, 16).bfloat16(), torch.randn(16, 1, 12, 20).bfloat16(),
+          torch.randn(16, 1, 16, 16).bfloat16()]
+    ts = torch.rand(3)
+    cps = [torch.randn(20, cdim).bfloat16(), torch.randn(45, cdim).bfloat16(), torch.randn(20, cdim).bfloat16()]
+    conds = [torch.randn(192, 16, 16).bfloat16(), torch.randn(192, 12, 20).bfloat16(),
+             torch.randn(192, 16, 16).bfloat16()]
+    with torch.no_grad():
+        batch = model(xs, ts, cps, cond_list=conds)["sample"]
+        for i in range(3):
+            one = model([xs[i]], ts[i:i + 1], [cps[i]], cond_list=[conds[i]])["sample"][0]
+            assert batch[i].shape == xs[i].shape
+            torch.testing.assert_close(batch[i].float(), one.float(), rtol=0, atol=0)
+    # padded caption tokens take the learned pad token: changing it changes the output
+    with torch.no_grad():
+        model.z_transformer.cap_pad_token.add_(1.0)
+        moved = model([xs[0]], ts[:1], [cps[0]], cond_list=[conds[0]])["sample"][0]
+    assert not torch.equal(moved, batch[0])
+
+    out = model(xs[:2], ts[:2], cps[:2], cond_list=conds[:2])["sample"]
+    sum(o.float().square().mean() for o in out).backward()
+    assert model.cond_refiner[0].z_block.feed_forward.w1.weight.grad is not None
+    mods = dict(model.named_modules())
+    names = (model.get_noise_lora_branch() + model.get_context_lora_branch() + model.get_main_lora_branch())
+    assert names and all(n in mods for n in names), [n for n in names if n not in mods]
+    assert model.switch_cond_branch_grad(False) > 0
+    assert not model.cond_embedder.weight.requires_grad
+
+
+def test_zimage_compat_residuals_single_vs_joint():
+    """harp_block_compat: without modulation Z_SingleBlock keeps the residual
+    (x + norm2(ffn(norm1(x)))) and Z_JointBlock replaces it (h + norm2(h))."""
+    import copy
+
+    torch.manual_seed(0)
+    blk = Z.ZImageTransformerBlock(0, 64, 2, 2, 1e-5, True, modulation=False)
+    single = Z.Z_SingleBlock(copy.deepcopy(blk), 1, True)
+    joint = Z.Z_JointBlock(copy.deepcopy(blk), 1, True)
+    x = torch.randn(1, 32, 64)
+    ang = torch.rand(32, 16) * 3
+    freqs = torch.stack([ang.cos(), ang.sin()], -1)
+    with torch.no_grad():
+        ys = single(x, None, freqs)
+        yj = joint(x, None, freqs)
+        zb = single.z_block
+        a = x + zb.attention_norm2(single.attention(zb.attention_norm1(x), freqs, SPContext()))
+        h = zb.feed_forward(zb.ffn_norm1(a))
+    torch.testing.assert_close(ys, a + zb.ffn_norm2(h))
+    torch.testing.assert_close(yj, h + zb.ffn_norm2(h))
