@@ -85,6 +85,54 @@ __global__ void rmsnorm_mod_fwd_kernel(const bf16* __restrict__ x, long ldx, con
   }
 }
 
+// Register-resident form for D % 128 == 0: a warp per row, each lane holding
+// 4 * NC4 elements as 8-byte loads that are all issued before the first use,
+// so a warp keeps a whole row (2 * D bytes) in flight and x is read once.
+template <int NC4>
+__global__ void __launch_bounds__(256) rmsnorm_mod_fwd_rows_kernel(
+    const bf16* __restrict__ x, long ldx, const bf16* __restrict__ w, const bf16* __restrict__ scale,
+    const bf16* __restrict__ shift, long ldm, int rows_per_batch, int R, int D, float eps, bf16* __restrict__ y,
+    long ldy, float* __restrict__ rstd_out, int save_rms) {
+  const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (row >= R) return;
+  uint2 xv[NC4];
+#pragma unroll
+  for (int k = 0; k < NC4; ++k) xv[k] = *reinterpret_cast<const uint2*>(x + (long)row * ldx + 4 * (lane + 32 * k));
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < NC4; ++k) {
+    const float2 a = unpack_bf16x2(xv[k].x), b = unpack_bf16x2(xv[k].y);
+    ss += a.x * a.x + a.y * a.y + b.x * b.x + b.y * b.y;
+  }
+  ss = warp_sum(ss);
+  const float rstd = rsqrtf(ss / D + eps);
+  if (lane == 0 && rstd_out) rstd_out[row] = save_rms ? 1.f / rstd : rstd;
+  const long mb = (long)(row / rows_per_batch) * ldm;
+#pragma unroll
+  for (int k = 0; k < NC4; ++k) {
+    const int c = 4 * (lane + 32 * k);
+    const float2 a = unpack_bf16x2(xv[k].x), b = unpack_bf16x2(xv[k].y);
+    float f[4] = {a.x * rstd, a.y * rstd, b.x * rstd, b.y * rstd};
+    if (w) {
+      const uint2 t = *reinterpret_cast<const uint2*>(w + c);
+      const float2 p = unpack_bf16x2(t.x), q = unpack_bf16x2(t.y);
+      f[0] *= p.x; f[1] *= p.y; f[2] *= q.x; f[3] *= q.y;
+    }
+    if (scale) {
+      const uint2 t = *reinterpret_cast<const uint2*>(scale + mb + c);
+      const float2 p = unpack_bf16x2(t.x), q = unpack_bf16x2(t.y);
+      f[0] *= 1.f + p.x; f[1] *= 1.f + p.y; f[2] *= 1.f + q.x; f[3] *= 1.f + q.y;
+    }
+    if (shift) {
+      const uint2 t = *reinterpret_cast<const uint2*>(shift + mb + c);
+      const float2 p = unpack_bf16x2(t.x), q = unpack_bf16x2(t.y);
+      f[0] += p.x; f[1] += p.y; f[2] += q.x; f[3] += q.y;
+    }
+    *reinterpret_cast<uint2*>(y + (long)row * ldy + c) = make_uint2(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]));
+  }
+}
+
 // Backward.  Block = RPB rows of one batch sample.
 //  g = dy*(1+scale[b]);  dxhat = g*w;  dx = rstd*(dxhat - xhat*mean(dxhat*xhat)) (+dres)
 //  partials (per block, fp32 [nblk, D]):  pw += g*xhat ; ps += dy*xhat*w ; pb += dy
@@ -1196,6 +1244,32 @@ void rmsnorm_mod_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& w, co
   const int threads = 256;
   const int grid = (R + 7) / 8;
   if (R == 0) return;
+  auto al = [](const void* p, long ld) { return p == nullptr || (reinterpret_cast<uintptr_t>(p) % 8 == 0 && ld % 4 == 0); };
+  const bool rows_ok = D % 128 == 0 && D <= 2304 && al(x.data_ptr(), x.stride(0)) && al(y.data_ptr(), y.stride(0)) &&
+                       al(bp(w), 0) && al(bp(scale), ldm) && al(bp(shift), ldm);
+  if (rows_ok) {
+#define HARP_RMS_FWD_ROWS(N4)                                                                                    \
+  case N4:                                                                                                       \
+    rmsnorm_mod_fwd_rows_kernel<N4><<<grid, threads, 0, at::cuda::getCurrentCUDAStream()>>>(                     \
+        bp(x), x.stride(0), bp(w), bp(scale), bp(shift), ldm, (int)rows_per_batch, R, D, (float)eps, bpm(y),     \
+        y.stride(0), rstd.data_ptr<float>(), save_rms ? 1 : 0);                                                  \
+    C10_CUDA_KERNEL_LAUNCH_CHECK();                                                                              \
+    count_launch();                                                                                              \
+    return;
+    switch (D / 128) {
+      HARP_RMS_FWD_ROWS(1)
+      HARP_RMS_FWD_ROWS(2)
+      HARP_RMS_FWD_ROWS(4)
+      HARP_RMS_FWD_ROWS(6)
+      HARP_RMS_FWD_ROWS(8)
+      HARP_RMS_FWD_ROWS(9)
+      HARP_RMS_FWD_ROWS(12)
+      HARP_RMS_FWD_ROWS(16)
+      HARP_RMS_FWD_ROWS(18)
+      default: break;
+    }
+#undef HARP_RMS_FWD_ROWS
+  }
   rmsnorm_mod_fwd_kernel<<<grid, threads, 0, at::cuda::getCurrentCUDAStream()>>>(
       bp(x), x.stride(0), bp(w), bp(scale), bp(shift), ldm, (int)rows_per_batch, R, D, (float)eps, bpm(y),
       y.stride(0), rstd.data_ptr<float>(), save_rms ? 1 : 0);

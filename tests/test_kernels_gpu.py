@@ -138,10 +138,11 @@ def _rms_ref(x, w, scale, shift, rpb, eps):
     return y
 
 
-@pytest.mark.parametrize("D,use_dres", [(1152, False), (1152, True), (1000, True)])
+@pytest.mark.parametrize("D,use_dres", [(1152, False), (1152, True), (2304, True), (1000, True)])
 @pytest.mark.parametrize("use_w,use_mod", [(True, False), (False, True), (True, True)])
 def test_rmsnorm_mod_fwd_bwd(use_w, use_mod, D, use_dres):
-    """D=1152 runs the row-parallel backward, D=1000 the column-parallel one."""
+    """D=1152 and D=2304 run the register-resident forward and the row-parallel
+    backward, D=1000 the column-parallel ones."""
     Bn, S, eps = 3, 96, 1e-6
     R = Bn * S
     x = torch.randn(R, D, device="cuda").to(torch.bfloat16)
@@ -252,9 +253,10 @@ def test_swiglu_and_gate_bwd():
 
 
 
-@pytest.mark.parametrize("D", [384, 1152])
+@pytest.mark.parametrize("D", [384, 1152, 2048])
 def test_gate_bwd(D):
-    """Gated-residual backward: D=1152 takes the row-parallel kernel, D=384 the column-parallel one."""
+    """Gated-residual backward: D=1152 and D=2048 take the row-parallel kernel,
+    D=384 the column-parallel one."""
     Bn, S = 2, 128
     dy = torch.randn(Bn * S, D, device="cuda").to(torch.bfloat16)
     a = torch.randn(Bn * S, D, device="cuda").to(torch.bfloat16)
