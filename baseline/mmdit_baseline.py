@@ -14,9 +14,9 @@ from stock PyTorch pieces only:
     torch.optim.AdamW(fused=True) on fp32 master weights
   * sharded weights (shard=True): FSDP2 fully_shard per block (NCCL parameter
     all-gather before each block, gradient reduce-scatter after it), fp32
-    sharded parameters and AdamW state, bf16 compute; offload=True adds
-    FSDP2's pinned-host CPUOffloadPolicy (parameters, gradients and the
-    optimizer step on the host)
+    sharded parameters and AdamW state, bf16 compute.  (offload=True would
+    add FSDP2's pinned-host CPUOffloadPolicy; bench.py does not run it on
+    B200: it raised an illegal memory access there.)
 No harp kernel, model or engine code is used on this path.
 """
 from __future__ import annotations

@@ -74,8 +74,8 @@ def parse():
     ap.add_argument("--comm", default="auto", choices=["auto", "torch", "nvl"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--offload-optimizer", action="store_true",
-                    help="harp: fp32 master weights and AdamW moments in pinned, mapped host memory; baseline "
-                         "(with --shard-params): FSDP2 CPUOffloadPolicy")
+                    help="harp: fp32 master weights and AdamW moments in pinned, mapped host memory "
+                         "(the baseline arm does not run this configuration)")
     ap.add_argument("--shard-params", action="store_true",
                     help="harp, N > 1: keep 1/N of every block's weights per GPU and gather them per block; "
                          "baseline: FSDP2 fully_shard per block")
@@ -312,6 +312,12 @@ def main():
     args.latent = args.latent or (256 if args.model == "mmdit-2b" else 128)
     args.text_len = args.text_len or (512 if args.model == "flux-12b" else TEXT_TOKENS)
     img_tokens = (args.latent // 2) ** 2
+    if args.impl == "baseline" and args.offload_optimizer:
+        # FSDP2's CPUOffloadPolicy raised an illegal memory access on this pool's
+        # B200s (flux-12b, 2 GPUs); that configuration is not run
+        print(json.dumps({"impl": "baseline", "unavailable": "the baseline's FSDP2 CPU-offload configuration is "
+                          "not run on this pool (it raised an illegal memory access); use --shard-params alone"}))
+        return 0
     rank, ws, local = setup_dist(args.gpus)
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
