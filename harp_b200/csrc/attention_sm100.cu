@@ -103,6 +103,60 @@ __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wa
 __device__ __forceinline__ void bulk_wait_read_one_pending() {
   asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
 }
+// Thread-block cluster helpers (CTA pairs of the 64-query backward).
+__device__ __forceinline__ uint32_t cta_rank_in_cluster() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// shared::cluster address of `local` (an address in this CTA's shared memory)
+// in the shared memory of cluster CTA `rank`
+__device__ __forceinline__ uint32_t cluster_map(uint32_t local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+// arrive on an mbarrier of another CTA of the cluster, ordering this thread's
+// earlier memory accesses before it (cluster scope)
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait with cluster-scope acquire (a barrier that the other CTA of the
+// pair arrives on): false after kPipeTimeoutNs or once an error is recorded.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, int* err, int site) {
+  const unsigned long long t0 = globaltimer_ns();
+  uint32_t spins = 0;
+  while (!mbar_try_wait_cluster(bar, parity)) {
+    if ((++spins & 255u) == 0) {
+      if (err != nullptr && *(volatile int*)err != 0) return false;
+      if (globaltimer_ns() - t0 > kPipeTimeoutNs) {
+        report_error(err, kErrTimeout, site, (int)parity);
+        return false;
+      }
+    }
+  }
+  return true;
+}
+__device__ __forceinline__ void cluster_barrier() {
+  __syncwarp();
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
 __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity) {
   const unsigned long long t0 = globaltimer_ns();
   while (!mbar_try_wait(bar, parity))
@@ -1136,6 +1190,25 @@ __global__ void __launch_bounds__(kBwdThreads1, 1)
 // ===========================================================================
 // Row d0..d0+15 of a thread's fp32 dQ partial (from one 16-column TMEM load)
 // into its staging row; columns at or past Dh are not stored.
+// stage_row16 plus the same 16 columns of the pair CTA's staged row (at
+// shared::cluster address peer_row), added in
+__device__ __forceinline__ void stage_row16_add(float* srow, int d0, const uint32_t (&v)[16], int Dh,
+                                                uint32_t peer_row) {
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    const int d = d0 + 4 * g;
+    if (d < Dh) {
+      float4 r;
+      asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                   : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w)
+                   : "r"(peer_row + 4u * (uint32_t)d)
+                   : "memory");
+      *reinterpret_cast<float4*>(srow + d) =
+          make_float4(__uint_as_float(v[4 * g]) + r.x, __uint_as_float(v[4 * g + 1]) + r.y,
+                      __uint_as_float(v[4 * g + 2]) + r.z, __uint_as_float(v[4 * g + 3]) + r.w);
+    }
+  }
+}
 __device__ __forceinline__ void stage_row16(float* srow, int d0, const uint32_t (&v)[16], int Dh) {
 #pragma unroll
   for (int g = 0; g < 4; ++g) {
@@ -1193,7 +1266,12 @@ static_assert(kPipeRegsCtl + 2 * kPipeRegsDs + kPipeRegsDq == 4 * (65536 / kBwdP
 // TMEM reads the tensor pipe completes first (MMAs of one thread execute in
 // issue order).  Per tile this moves 64 KB less through shared memory, whose
 // bandwidth the operand reads of the MMAs otherwise saturate.
-template <int NCH, bool FOLD, bool TM>
+//
+// PAIR (with TM): CTAs run in clusters of two over adjacent key tiles, and the
+// second CTA's dQ partial of each query tile is added into the first's
+// staging buffer through distributed shared memory before the first CTA's one
+// reduce-add (as in attn_bwd_q64_kernel), halving the dQ traffic in L2.
+template <int NCH, bool FOLD, bool TM, bool PAIR = false>
 __global__ void __launch_bounds__(kBwdPipeThreads, 1)
     attn_bwd_pipe_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                          const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
@@ -1223,12 +1301,16 @@ __global__ void __launch_bounds__(kBwdPipeThreads, 1)
   uint64_t* dqs_bar = dq_free + 1;  // [ST]: dQ of the tile in stage st is staged
   uint64_t* fin = dqs_bar + ST;
   uint64_t* q_ready = fin + 1;  // [ST] (FOLD): the tile's statistics columns are written
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(q_ready + ST);
-  static_assert((1 + 4 * ST + 7) * 8 + 4 <= 256, "barrier region");
+  uint64_t* peer_staged = q_ready + ST;    // [ST] (PAIR, CTA 0)
+  uint64_t* peer_read = peer_staged + ST;  // [ST] (PAIR, CTA 1)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(peer_read + ST);
+  static_assert((1 + 6 * ST + 7) * 8 + 4 <= 256, "barrier region");
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int nkt = (a.Skv + 127) / 128;
-  const int bh = blockIdx.x / nkt, kt = blockIdx.x % nkt;
+  const int nkt_grid = PAIR ? 2 * ((nkt + 1) / 2) : nkt;  // pairs never straddle two heads
+  const int bh = blockIdx.x / nkt_grid, kt = blockIdx.x % nkt_grid;
+  const uint32_t crank = PAIR ? cta_rank_in_cluster() : 0u;
   const int b = bh / a.H, h = bh % a.H;
   const int k0 = kt * 128;
   const int nq = (a.Sq + 127) / 128;
@@ -1248,7 +1330,11 @@ __global__ void __launch_bounds__(kBwdPipeThreads, 1)
     mbar_init(dq_free, 4);
     for (int st2 = 0; st2 < ST; ++st2) mbar_init(&dqs_bar[st2], 4);
     mbar_init(fin, 1);
-    for (int st2 = 0; st2 < ST; ++st2) mbar_init(&q_ready[st2], 1);
+    for (int st2 = 0; st2 < ST; ++st2) {
+      mbar_init(&q_ready[st2], 1);
+      mbar_init(&peer_staged[st2], 4);
+      mbar_init(&peer_read[st2], 1);
+    }
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -1257,6 +1343,7 @@ __global__ void __launch_bounds__(kBwdPipeThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
+  if (PAIR) cluster_barrier();  // both CTAs' barriers are initialised
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t tS = tmem, tdP = tmem + 128, tdV = tmem + C::DV_COL, tdK = tmem + C::DK_COL,
@@ -1415,13 +1502,22 @@ __global__ void __launch_bounds__(kBwdPipeThreads, 1)
       bool ok = true;
       for (int i = 0; i < nq; ++i) {
         const int st = i % ST;
-        if (!mbar_wait(&dqs_bar[st], (i / ST) & 1, err, 182)) ok = false;
+        const uint32_t ph = (i / ST) & 1;
+        if (PAIR && crank == 1) {
+          // CTA 0 adds this CTA's staged partial into its own and reduces the sum
+          if (!mbar_wait_cluster(&peer_read[st], ph, err, 183)) ok = false;
+          mbar_arrive(&qdo_empty[st]);
+          continue;
+        }
+        if (!mbar_wait(&dqs_bar[st], ph, err, 182)) ok = false;
         if (ok) {
           BWD_PROBE(i, 7);
           tma_reduce_add_4d(&tmdQ, reinterpret_cast<float*>(sQD + 2 * st * C::TILE), 0, h, i * 128, b);
           bulk_wait_read_all();
           BWD_PROBE(i, 9);
         }
+        // the dQ warps read the pair's partial before they arrived on dqs_bar
+        if (PAIR) mbar_arrive_remote(cluster_map(smem_u32(&peer_read[st]), 1));
         mbar_arrive(&qdo_empty[st]);
       }
       bulk_wait_all();
@@ -1647,14 +1743,32 @@ __global__ void __launch_bounds__(kBwdPipeThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(dq_free);
-      stage_row16(srow, 0, v0, a.Dh);
-      stage_row16(srow, 16, v1, a.Dh);
-      stage_row16(srow, 32, v2, a.Dh);
-      stage_row16(srow, 48, v3, a.Dh);
-      if (C::DPAD > 64) stage_row16(srow, 64, v4, a.Dh);
+      bool add_peer = false;
+      if (PAIR && crank == 0) {
+        // CTA 1's partial of this tile sits in its stage of the same index
+        add_peer = mbar_wait_cluster(&peer_staged[st], (i / ST) & 1, err, 184);
+        if (!add_peer) ok = false;
+      }
+      if (add_peer) {
+        const uint32_t prow = cluster_map(smem_u32(srow), 1);
+        stage_row16_add(srow, 0, v0, a.Dh, prow);
+        stage_row16_add(srow, 16, v1, a.Dh, prow);
+        stage_row16_add(srow, 32, v2, a.Dh, prow);
+        stage_row16_add(srow, 48, v3, a.Dh, prow);
+        if (C::DPAD > 64) stage_row16_add(srow, 64, v4, a.Dh, prow);
+      } else {
+        stage_row16(srow, 0, v0, a.Dh);
+        stage_row16(srow, 16, v1, a.Dh);
+        stage_row16(srow, 32, v2, a.Dh);
+        stage_row16(srow, 48, v3, a.Dh);
+        if (C::DPAD > 64) stage_row16(srow, 64, v4, a.Dh);
+      }
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&dqs_bar[st]);  // warp 2 reduce-adds the staged tile
+      if (lane == 0) {
+        if (PAIR && crank == 1) mbar_arrive_remote(cluster_map(smem_u32(&peer_staged[st]), 0));
+        else mbar_arrive(&dqs_bar[st]);  // warp 2 reduce-adds the staged tile
+      }
     }
     if (ok) ok = mbar_wait(fin, 0, err, 181);
     tc_fence_after();
@@ -1684,6 +1798,7 @@ __global__ void __launch_bounds__(kBwdPipeThreads, 1)
 
   tc_fence_before();
   __syncthreads();
+  if (PAIR) cluster_barrier();  // no CTA of a pair leaves while the other may still use its memory
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
@@ -1711,8 +1826,8 @@ struct BwdQ64Cfg {
   static constexpr int QTILE = NCH * 1024;  // 64 queries x DPAD, atoms of 2 KB
   static constexpr int PS_BYTES = 128 * 64 * 2;  // P^T or dS: 128 keys x 64 queries bf16, 8-query strips
   static constexpr int LD_BYTES = 2 * 128 * 4;   // lse | delta of a 64-query tile, double-buffered
-  // 256 bytes of alignment slack, 256 for the barriers (at most 2 + 2 * 7 + 10) and the TMEM address
-  static constexpr int smem_for(int st) { return 2 * KTILE + st * 2 * QTILE + 2 * PS_BYTES + LD_BYTES + 256 + 256; }
+  // 256 bytes of alignment slack, 512 for the barriers (at most 1 + 5 * 7 + 10) and the TMEM address
+  static constexpr int smem_for(int st) { return 2 * KTILE + st * 2 * QTILE + 2 * PS_BYTES + LD_BYTES + 256 + 512; }
   static constexpr int STAGES = smem_for(7) <= 232448 ? 7 : (smem_for(5) <= 232448 ? 5 : (smem_for(4) <= 232448 ? 4 : 3));
   static constexpr int SMEM = smem_for(STAGES);
   static_assert(SMEM <= 232448, "exceeds the 227 KB per-CTA shared memory limit");
@@ -1726,7 +1841,7 @@ struct BwdQ64Cfg {
   static constexpr int DQ_COL = 128 + 2 * DPAD;  // two 64-column slots
   static_assert(DQ_COL + 128 <= 512, "TMEM columns");
 };
-constexpr int kBwdQ64Threads = 512;  // WG0: w0 TMA, w1 MMA; WG1/WG2: dS warps (queries 0-31 / 32-63); WG3: dQ warps
+constexpr int kBwdQ64Threads = 512;  // WG0: w0 TMA, w1 MMA, w2 dQ reducer; WG1/WG2: dS warps (queries 0-31 / 32-63); WG3: dQ warps
 
 // 64-row tiles: atom a of a 64 x DPAD tile at + a * 2048
 template <int NCH>
@@ -1742,7 +1857,15 @@ __device__ __forceinline__ uint64_t mnmajor_sw32_r64(uint32_t tile_addr, int ks)
   return make_sdesc(tile_addr + ks * 512, 2048, 256, kLayoutSw32);
 }
 
-template <int NCH>
+// PAIR: CTAs run in clusters of two over adjacent key tiles of one (b, h); per
+// query tile the second CTA's dQ partial is added into the first's staging
+// buffer through distributed shared memory, and only the first CTA
+// reduce-adds into dq_acc, which halves the dQ reduction traffic in L2.
+//   peer_staged[ST]  (CTA 0) the four dQ warps of CTA 1 staged tile i's partial
+//   peer_read[ST]    (CTA 1) CTA 0 has read it (CTA 1 may give the stage back)
+// A pair CTA past the last key tile (odd tile count) runs on zero keys and
+// contributes nothing.
+template <int NCH, bool PAIR>
 __global__ void __launch_bounds__(kBwdQ64Threads, 1)
     attn_bwd_q64_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
@@ -1767,13 +1890,17 @@ __global__ void __launch_bounds__(kBwdQ64Threads, 1)
   uint64_t* dq_full = p_free + 1;   // [2]
   uint64_t* dq_free = dq_full + 2;  // [2]
   uint64_t* dqs_bar = dq_free + 2;  // [ST]: dQ of the tile in stage st is staged
-  uint64_t* fin = dqs_bar + ST;
+  uint64_t* peer_staged = dqs_bar + ST;    // [ST] (PAIR, CTA 0)
+  uint64_t* peer_read = peer_staged + ST;  // [ST] (PAIR, CTA 1)
+  uint64_t* fin = peer_read + ST;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fin + 1);
-  static_assert((1 + 3 * ST + 4 + 4 + 1) * 8 + 4 <= 256, "barrier region");
+  static_assert((1 + 5 * ST + 4 + 4 + 1) * 8 + 4 <= 512, "barrier region");
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int nkt = (a.Skv + 127) / 128;
-  const int bh = blockIdx.x / nkt, kt = blockIdx.x % nkt;
+  const int nkt_grid = PAIR ? 2 * ((nkt + 1) / 2) : nkt;  // pairs never straddle two heads
+  const int bh = blockIdx.x / nkt_grid, kt = blockIdx.x % nkt_grid;
+  const uint32_t crank = PAIR ? cta_rank_in_cluster() : 0u;
   const int b = bh / a.H, h = bh % a.H;
   const int k0 = kt * 128;
   const int nq = (a.Sq + 63) / 64;
@@ -1793,7 +1920,11 @@ __global__ void __launch_bounds__(kBwdQ64Threads, 1)
       mbar_init(&dq_full[s], 1);
       mbar_init(&dq_free[s], 4);
     }
-    for (int s = 0; s < ST; ++s) mbar_init(&dqs_bar[s], 4);
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(&dqs_bar[s], 4);
+      mbar_init(&peer_staged[s], 4);
+      mbar_init(&peer_read[s], 1);
+    }
     mbar_init(fin, 1);
     fence_mbar_init();
   }
@@ -1803,6 +1934,9 @@ __global__ void __launch_bounds__(kBwdQ64Threads, 1)
   }
   tc_fence_before();
   __syncthreads();
+  // the other CTA of the pair arrives on this CTA's barriers: both have
+  // initialised theirs before either goes on
+  if (PAIR) cluster_barrier();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t tS = tmem, tdP = tmem + 64, tdV = tmem + C::DV_COL, tdK = tmem + C::DK_COL,
@@ -1892,11 +2026,20 @@ __global__ void __launch_bounds__(kBwdQ64Threads, 1)
       bool ok = true;
       for (int i = 0; i < nq; ++i) {
         const int st = i % ST;
-        if (!mbar_wait(&dqs_bar[st], (i / ST) & 1, err, 282)) ok = false;
+        const uint32_t ph = (i / ST) & 1;
+        if (PAIR && crank == 1) {
+          // CTA 0 adds this CTA's staged partial into its own and reduces the sum
+          if (!mbar_wait_cluster(&peer_read[st], ph, err, 283)) ok = false;
+          mbar_arrive(&qdo_empty[st]);
+          continue;
+        }
+        if (!mbar_wait(&dqs_bar[st], ph, err, 282)) ok = false;
         if (ok) {
           tma_reduce_add_4d(&tmdQ, reinterpret_cast<float*>(sQD + 2 * st * C::QTILE), 0, h, i * 64, b);
           bulk_wait_read_all();
         }
+        // the dQ warps read the pair's partial before they arrived on dqs_bar
+        if (PAIR) mbar_arrive_remote(cluster_map(smem_u32(&peer_read[st]), 1));
         mbar_arrive(&qdo_empty[st]);
       }
       bulk_wait_all();
@@ -2007,14 +2150,31 @@ __global__ void __launch_bounds__(kBwdQ64Threads, 1)
       tc_fence_after();
       const int st = i % ST;
       float* stage = reinterpret_cast<float*>(sQD + 2 * st * C::QTILE);  // [64 queries][Dh] fp32
+      // CTA 0 of a pair adds CTA 1's staged partial (same stage index, same
+      // layout) while staging its own
+      bool add_peer = false;
+      uint32_t peer_stage = 0;
+      if (PAIR && crank == 0) {
+        add_peer = mbar_wait_cluster(&peer_staged[st], (i / ST) & 1, err, 284);
+        if (!add_peer) ok = false;
+        peer_stage = cluster_map(smem_u32(stage), 1);
+      }
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
         uint32_t v[32];
         tmem_ld32(tdQ + slot * 64 + lane_off + half * 32, v);
         tmem_wait_ld();
         if (dd < a.Dh) {
+          if (add_peer) {
 #pragma unroll
-          for (int qq = 0; qq < 32; ++qq) stage[(half * 32 + qq) * a.Dh + dd] = __uint_as_float(v[qq]);
+            for (int qq = 0; qq < 32; ++qq) {
+              const int e = (half * 32 + qq) * a.Dh + dd;
+              stage[e] = __uint_as_float(v[qq]) + ld_cluster_f32(peer_stage + 4u * (uint32_t)e);
+            }
+          } else {
+#pragma unroll
+            for (int qq = 0; qq < 32; ++qq) stage[(half * 32 + qq) * a.Dh + dd] = __uint_as_float(v[qq]);
+          }
         }
       }
       tc_fence_before();
@@ -2022,7 +2182,8 @@ __global__ void __launch_bounds__(kBwdQ64Threads, 1)
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(&dq_free[slot]);
-        mbar_arrive(&dqs_bar[st]);  // warp 2 reduce-adds the staged tile
+        if (PAIR && crank == 1) mbar_arrive_remote(cluster_map(smem_u32(&peer_staged[st]), 0));
+        else mbar_arrive(&dqs_bar[st]);  // warp 2 reduce-adds the staged tile
       }
     }
     if (ok) ok = mbar_wait(fin, 0, err, 281);
@@ -2054,6 +2215,9 @@ __global__ void __launch_bounds__(kBwdQ64Threads, 1)
 
   tc_fence_before();
   __syncthreads();
+  // neither CTA of a pair leaves while the other may still read its shared
+  // memory or arrive on its barriers
+  if (PAIR) cluster_barrier();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
@@ -2166,6 +2330,19 @@ int bwd_q64_mode() {
 }
 
 // mq / mdo / mdq here are the 64-row maps
+// HARP_ATTN_BWD_PAIR=1: the backward kernels in CTA pairs that combine their
+// dQ partials through distributed shared memory before one reduce-add.  Off
+// by default: measured slower (head dim 72: 3.08 vs 1.53 ms; 128: 13.6 vs
+// 3.22 ms), because the first CTA's distributed-shared-memory loads of the
+// partner's partial sit on the dQ warps' critical path.
+bool bwd_pair_mode() {
+  static const bool m = [] {
+    const char* e = std::getenv("HARP_ATTN_BWD_PAIR");
+    return e && std::string(e) == "1";
+  }();
+  return m;
+}
+
 template <int NCH>
 void launch_bwd_q64(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mdo,
                     const CUtensorMap& mdq, const BwdArgs& args, cudaStream_t stream) {
@@ -2173,12 +2350,31 @@ void launch_bwd_q64(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensor
   static bool configured = false;
   if (!configured) {
     C10_CUDA_CHECK(
-        cudaFuncSetAttribute(attn_bwd_q64_kernel<NCH>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+        cudaFuncSetAttribute(attn_bwd_q64_kernel<NCH, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    C10_CUDA_CHECK(
+        cudaFuncSetAttribute(attn_bwd_q64_kernel<NCH, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     configured = true;
   }
-  const int grid = args.B * args.H * ((args.Skv + 127) / 128);
-  attn_bwd_q64_kernel<NCH><<<grid, kBwdQ64Threads, C::SMEM, stream>>>(mq, mk, mv, mdo, mdq, args);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  const int nkt = (args.Skv + 127) / 128;
+  if (bwd_pair_mode()) {
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(args.B * args.H * 2 * ((nkt + 1) / 2));
+    cfg.blockDim = dim3(kBwdQ64Threads);
+    cfg.dynamicSmemBytes = C::SMEM;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, attn_bwd_q64_kernel<NCH, true>, mq, mk, mv, mdo, mdq, args));
+  } else {
+    attn_bwd_q64_kernel<NCH, false><<<args.B * args.H * nkt, kBwdQ64Threads, C::SMEM, stream>>>(mq, mk, mv, mdo, mdq,
+                                                                                                 args);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
   count_launch();
 }
 
@@ -2203,7 +2399,8 @@ void launch_bwd(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap&
     };
     static const bool pipe_ok = setup(attn_bwd_pipe_kernel<NCH, false, false>) &&
                                 setup(attn_bwd_pipe_kernel<NCH, true, false>) &&
-                                setup(attn_bwd_pipe_kernel<NCH, true, true>);
+                                setup(attn_bwd_pipe_kernel<NCH, true, true>) &&
+                                setup(attn_bwd_pipe_kernel<NCH, true, true, true>);
     // HARP_ATTN_BWD_TM=0 keeps P^T / dS^T in shared memory (comparisons)
     static const bool tm_on = [] {
       const char* e = std::getenv("HARP_ATTN_BWD_TM");
@@ -2215,6 +2412,24 @@ void launch_bwd(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap&
       return !(e && e[0] == '0');
     }();
     const bool fold = fold_on && args.Dh + 2 <= P::DPAD;
+    if (bwd_pipe_enabled() && pipe_ok && fold && tm_on && bwd_pair_mode()) {
+      const int nkt = (args.Skv + 127) / 128;
+      cudaLaunchConfig_t cfg = {};
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 2;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.gridDim = dim3(args.B * args.H * 2 * ((nkt + 1) / 2));
+      cfg.blockDim = dim3(kBwdPipeThreads);
+      cfg.dynamicSmemBytes = P::SMEM;
+      cfg.stream = stream;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, attn_bwd_pipe_kernel<NCH, true, true, true>, mq, mk, mv, mdo, mdq, args));
+      count_launch();
+      return;
+    }
     if (bwd_pipe_enabled() && pipe_ok) {
       const int grid = args.B * args.H * ((args.Skv + 127) / 128);
       auto* kern = fold ? (tm_on ? attn_bwd_pipe_kernel<NCH, true, true> : attn_bwd_pipe_kernel<NCH, true, false>)

@@ -182,11 +182,14 @@ def test_attn_fwd_poly_exp(npoly):
     assert r.returncode == 0 and "ok" in r.stdout, r.stdout + r.stderr
 
 
-@pytest.mark.parametrize("env", [{"HARP_ATTN_BWD_Q64": "all"}, {"HARP_ATTN_FWD": "split"}])
+@pytest.mark.parametrize("env", [{"HARP_ATTN_BWD_Q64": "all"}, {"HARP_ATTN_FWD": "split"},
+                                 {"HARP_ATTN_BWD_PAIR": "1"}])
 def test_attention_alternative_schedules(env):
     """The schedules chosen by environment variables (read once per process):
-    the 64-query-tile backward for head dims 64-80 and the two-warps-per-row
-    forward, run through the same checks in a child process."""
+    the 64-query-tile backward for head dims 64-80, the two-warps-per-row
+    forward, and the backward kernels in CTA pairs that combine dQ partials
+    through distributed shared memory, run through the same checks in a child
+    process."""
     import os
     import subprocess
     import sys
