@@ -236,8 +236,10 @@ class BaselineMMDiTTrainer:
         if self.shard:
             from torch.distributed.fsdp import CPUOffloadPolicy, MixedPrecisionPolicy, fully_shard
 
-            with torch.device("meta"):
+            # the same fp32 initial weights as the replicated path, then sharded
+            with torch.device("cpu" if offload else device):
                 model = BaselineMMDiT(cfg)
+            model.init_weights()
             mp = MixedPrecisionPolicy(param_dtype=torch.bfloat16, reduce_dtype=torch.float32)
             kw = {"mp_policy": mp}
             if offload:
@@ -245,8 +247,6 @@ class BaselineMMDiTTrainer:
             for blk in list(model.double_blocks) + list(model.single_blocks):
                 fully_shard(blk, **kw)
             fully_shard(model, **kw)
-            model.to_empty(device="cpu" if offload else device)
-            model.init_weights()
             self.model = model
             self.params = list(model.parameters())
             self.opt = torch.optim.AdamW(self.params, lr=1e-4, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.0,

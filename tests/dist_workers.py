@@ -198,3 +198,14 @@ def groups(rank, world, out, args):
     par = ParallelState.build(args["sp"], args["rs"])
     get = lambda g: dist.get_process_group_ranks(g) if g is not None else None  # noqa: E731
     return {"sp": get(par.sp_group), "dp": get(par.dp_group), "rs": get(par.rs_group), "rs_size": par.rs_size}
+
+
+def baseline_mmdit(rank, world, out, args):
+    """The NCCL + cuBLAS/SDPA comparison arm's MMDiT trainer (replicated weights
+    under DDP, or FSDP2 per-block sharding) on gloo: losses of a few steps."""
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "baseline"))
+    from mmdit_baseline import BaselineMMDiTTrainer
+
+    tr = BaselineMMDiTTrainer(args["model"], torch.device("cpu"), world, shard=args.get("shard", False))
+    b = torch.load(args["batch"])
+    return {"losses": [float(tr.train_step(b["latent"], b["noise"], b["text"], b["sigmas"])) for _ in range(3)]}

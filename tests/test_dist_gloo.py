@@ -168,3 +168,28 @@ def test_group_topology_four_ranks(tmp_path):
     assert [res[r]["dp"] for r in range(4)] == [[0, 2], [1, 3], [0, 2], [1, 3]]
     assert [res[r]["rs"] for r in range(4)] == [[0, 2], [1, 3], [0, 2], [1, 3]]
     assert res[0]["rs_size"] == 2
+
+
+@pytest.mark.parametrize("shard", [False, True])
+def test_baseline_mmdit_two_ranks_matches_one(tmp_path, shard):
+    """The comparison arm's MMDiT step, sequence-parallel over two gloo ranks
+    (K/V all-gathered, DDP or FSDP2 gradients), follows the one-process run:
+    the ranks' gradients are averaged instead of summed, which AdamW's update
+    does not see beyond its epsilon."""
+    import sys
+
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "baseline"))
+    from mmdit_baseline import BaselineMMDiTTrainer
+
+    g = torch.Generator().manual_seed(5)
+    b = {"latent": torch.randn(1, 16, 16, 16, generator=g).bfloat16(),
+         "noise": torch.randn(1, 16, 16, 16, generator=g).bfloat16(),
+         "text": torch.randn(1, 32, 128, generator=g).bfloat16(), "sigmas": torch.rand(1, generator=g)}
+    path = str(tmp_path / "batch.pt")
+    torch.save(b, path)
+    torch.manual_seed(0)
+    one = BaselineMMDiTTrainer("flux-tiny", torch.device("cpu"), 1)
+    ref = [float(one.train_step(b["latent"], b["noise"], b["text"], b["sigmas"])) for _ in range(3)]
+    res, _ = _run("baseline_mmdit", 2, tmp_path, {"model": "flux-tiny", "batch": path, "shard": shard})
+    for r in (0, 1):
+        assert res[r]["losses"] == pytest.approx(ref, rel=2e-2), (res[r]["losses"], ref)
