@@ -61,7 +61,7 @@ from . import collectives as C
 _KV, _DKV, _DKV_ACK0, _DKV_ACK1, _GRAD, _PARAM, _BARRIER = 0, 8, 16, 24, 32, 40, 48
 _UQKV, _UO, _UDO, _UDQ = 56, 64, 72, 80
 _GRADB = 96  # per-bucket gradient-ready slots: _GRADB + 8 * bucket + rank
-_MAX_BUCKETS = 32
+_MAX_BUCKETS = 128  # flux-12b: 57 blocks, one bucket each with sharded weights
 _GATH = _GRADB + 8 * _MAX_BUCKETS  # sharded parameters: slice landed in staging slot s (_GATH + 8 * s + rank)
 _GACK = _GATH + 16                 # sharded parameters: uses of staging slot s completed (_GACK + 8 * s + rank)
 _NFLAGS = _GACK + 16
@@ -511,7 +511,8 @@ class NVLinkComm:
     # fixed order as gradients complete, then end_grad_sync
     def begin_grad_sync(self, opt):
         assert self._flat is not None, "flat buffers must come from allocate_flat()"
-        assert len(opt.segments) <= _MAX_BUCKETS, "too many gradient buckets"
+        assert len(opt.segments) <= _MAX_BUCKETS, \
+            f"{len(opt.segments)} gradient buckets; the flag layout has room for {_MAX_BUCKETS}"
         self.epoch["grad"] += 1
         opt.step_count += 1
 
