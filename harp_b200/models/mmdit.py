@@ -83,6 +83,17 @@ def _lin(x, m: _Linear):
     return LinearFunction.apply(x, m.weight, m.bias)
 
 
+def _report_unused(module: nn.Module):
+    """This rank holds none of the tokens `module` acts on in this step, so its
+    parameters get no gradient: their (zeroed) gradient slots are complete now.
+    Tells the trainer's overlapped gradient sync (a no-op without one), so the
+    bucket that holds them is not left waiting for gradients that never come."""
+    for p in module.parameters():
+        cb = getattr(p, "_harp_grad_ready", None)
+        if cb is not None:
+            cb(p)
+
+
 def _rms(x, eps, w=None):
     return RMSNormFunction.apply(x, w, eps)
 
@@ -151,6 +162,7 @@ class DoubleStreamBlock(nn.Module):
         splits = [(self.img, x[:, :n_img], freqs[:n_img]), (self.txt, x[:, n_img:], freqs[n_img:])]
         for stream, xs, fs in splits:
             if xs.shape[1] == 0:
+                _report_unused(stream)
                 continue
             q, k, v, md = stream.pre_attn(xs, c_silu, fs.repeat(B, 1, 1), cfg)
             parts.append((stream, xs, md))
@@ -231,8 +243,12 @@ class MMDiT(nn.Module):
         parts = []
         if ih > il:
             parts.append(_lin(x_img[:, il:ih], self.img_in))
+        else:
+            _report_unused(self.img_in)
         if th > tl:
             parts.append(_lin(text[:, tl:th], self.txt_in))
+        else:
+            _report_unused(self.txt_in)
         h = torch.cat(parts, 1) if len(parts) > 1 else parts[0]
         c_silu = MySiLU.apply(self.time_in(t * 1000.0))
         key = (h_tok, w_tok, L, lo, hi, str(h.device))

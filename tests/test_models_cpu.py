@@ -344,3 +344,32 @@ def test_zimage_compat_residuals_single_vs_joint():
         h = zb.feed_forward(zb.ffn_norm1(a))
     torch.testing.assert_close(ys, a + zb.ffn_norm2(h))
     torch.testing.assert_close(yj, h + zb.ffn_norm2(h))
+
+
+def test_mmdit_reports_parameters_a_rank_does_not_use():
+    """A sequence-parallel rank that holds no text tokens reports the text
+    stream's and the text embedder's parameters as gradient-complete during the
+    forward (their zeroed slots get nothing), so an overlapped bucketed gradient
+    sync does not wait for them; the parameters it uses are not reported."""
+    torch.manual_seed(0)
+    cfg = M.PRESETS["flux-tiny"]
+    model = M.MMDiT(cfg)
+    model.initialize_weights(0)
+    seen = []
+    for p in model.parameters():
+        p._harp_grad_ready = seen.append
+    B, n = 1, 48
+    blk = model.double_blocks[0]
+    with torch.no_grad():  # this rank's 48 tokens are all image tokens
+        blk(torch.zeros(B, n, cfg.hidden), n, torch.zeros(B, cfg.hidden), torch.zeros(n, cfg.head_dim // 2, 2),
+            SPContext())
+    ids = {id(p) for p in seen}
+    assert {id(p) for p in blk.txt.parameters()} <= ids
+    assert not ({id(p) for p in blk.img.parameters()} & ids)
+    seen.clear()
+    with torch.no_grad():  # no text tokens at all: the text embedder gets no gradient
+        model.forward_local(torch.randn(B, 64, cfg.patch_dim), torch.randn(B, 0, cfg.text_dim), torch.rand(B), 8, 8,
+                            SPContext())
+    ids = {id(p) for p in seen}
+    assert {id(p) for p in model.txt_in.parameters()} <= ids
+    assert not ({id(p) for p in model.img_in.parameters()} & ids)
