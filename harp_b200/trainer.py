@@ -411,7 +411,7 @@ class Trainer:
         # multi-GPU steps are captured when every exchange is an NVLink kernel
         # (their flag values then come from the device: NVLinkComm.begin_capture)
         multi_ok = (self.grad_comm is not None and (par.sp_size == 1 or self.sp_comm is not None)
-                    and os.environ.get("HARP_GRAPH_MULTI", "0") == "1")
+                    and os.environ.get("HARP_GRAPH_MULTI", "1") != "0")
         self.graph_enabled = bool(cfg.cuda_graph) and on_gpu and (par.world_size == 1 or multi_ok)
 
     # -- device-resident step (inputs already on the GPU) -------------------
