@@ -84,7 +84,8 @@ def parse():
                          "gradient sync, each sequence-parallel exchange and wait) and print their per-step device "
                          "time, max over ranks, as a second JSON line (implies --cuda-graph 0)")
     ap.add_argument("--cuda-graph", type=int, default=1, choices=[0, 1],
-                    help="harp on one GPU: capture the whole step in a CUDA graph after the warm-up steps")
+                    help="harp: capture the whole step (on every GPU) in a CUDA graph after two eager warm-up "
+                         "steps; the capture itself happens inside the warm-up when --warmup >= 3")
     ap.add_argument("--depth", type=int, default=0, help="override depth (debug only; not a valid bench)")
     ap.add_argument("--op", default="train", choices=["train", "ring-attn"],
                     help="ring-attn: sequence-parallel attention fwd+bwd of Q/K/V [1, 24, seq, 128]")

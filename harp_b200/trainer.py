@@ -57,7 +57,8 @@ class TrainConfig:
     comm: str = "auto"  # "auto" | "torch" | "nvl"
     align: int = 256  # elements; every parameter starts on a 512-byte boundary
     # Capture the whole step (zero-grad, forward, backward, AdamW) in one CUDA
-    # graph after `graph_warmup` eager steps and replay it (single-GPU runs).
+    # graph after `graph_warmup` eager steps and replay it (1 GPU, or N GPUs
+    # whose exchanges all run on the NVLink communicator).
     cuda_graph: bool = False
     graph_warmup: int = 2
     # multi-GPU NVLink gradient sync: send each bucket (about this many
@@ -515,7 +516,7 @@ class Trainer:
         for (lo, hi), p in zip(self.flat.buckets, self.opt.param_segments()):
             C.all_gather_flat(p, self.flat.flat[lo:hi], self.par.world_group)
 
-    # -- CUDA-graph replay of the whole step (single GPU) ---------------------------
+    # -- CUDA-graph replay of the whole step ----------------------------------------
     def run(self, batch: Dict[str, torch.Tensor]) -> torch.Tensor:
         """One step from a batch of device or (pinned) host tensors, returning
         the loss as a device tensor.  With `cuda_graph`, the first
