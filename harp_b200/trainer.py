@@ -401,7 +401,7 @@ class Trainer:
         self.sp = SPContext.from_group(par.sp_group, backend=backend, comm=comm, mode=mode) \
             if par.sp_size > 1 else SPContext()
         self.global_step = 0
-        # CUDA-graph state (single GPU): static inputs, the captured step, its loss
+        # CUDA-graph state: static inputs, the captured step, its loss
         self._graph = None
         self._graph_inputs: Optional[Dict[str, torch.Tensor]] = None
         self._graph_loss: Optional[torch.Tensor] = None
