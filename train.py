@@ -80,7 +80,8 @@ def parse_args(argv=None):
                    help="sequence-parallel attention: K/V gather (the reference's ring) or head all-to-all")
     p.add_argument("--enable_profiler", action="store_true")
     p.add_argument("--cuda_graph", action="store_true",
-                   help="single GPU: capture the whole training step in one CUDA graph after two eager steps")
+                   help="capture the whole training step in one CUDA graph after two eager steps "
+                        "(1 GPU, or N GPUs on the NVLink communicator)")
     p.add_argument("--harp_block_compat", action="store_true", help="Z-Image: reproduce HARP's block residual")
     # accepted for command-line compatibility, unused (as in the reference)
     for flag, typ in (("--use_8bit_adam", bool), ("--rank", int), ("--resolution", int), ("--cache_dir", str),
