@@ -312,6 +312,9 @@ def main(args):
         if is_main:
             print(profiler.key_averages().table(sort_by="self_cuda_time_total" if use_cuda else "self_cpu_time_total",
                                                 row_limit=40))
+    if use_cuda:
+        torch.cuda.synchronize()
+    trainer.close()  # a captured step (it may hold NCCL work) goes before the process group
     if world > 1:
         dist.barrier()
         from harp_b200.parallel.nvlink import NVLinkComm
