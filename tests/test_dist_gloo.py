@@ -193,3 +193,19 @@ def test_baseline_mmdit_two_ranks_matches_one(tmp_path, shard):
     res, _ = _run("baseline_mmdit", 2, tmp_path, {"model": "flux-tiny", "batch": path, "shard": shard})
     for r in (0, 1):
         assert res[r]["losses"] == pytest.approx(ref, rel=2e-2), (res[r]["losses"], ref)
+
+
+@pytest.mark.parametrize("sp,mode", [(4, "ring"), (2, "ring"), (2, "ulysses")])
+def test_trainer_four_ranks_matches_single_process(tmp_path, sp, mode):
+    """Parity above two ranks: sequence parallel over 4 ranks (K/V gather; the
+    tiny model's 6 heads do not split 4 ways), and 2-way SP (K/V gather or head
+    all-to-all) x 2-way DP, against the one-process run."""
+    bpath = str(tmp_path / "batch.pt")
+    batch = _batch(bpath)
+    ref_losses, ref_flat = _single_run(batch, 3)
+    res, _ = _run("trainer_run", 4, tmp_path, {"sp": sp, "batch": bpath, "steps": 3, "mode": mode})
+    for r in range(4):
+        assert res[r]["losses"] == pytest.approx(ref_losses, rel=2e-3), (r, res[r]["losses"], ref_losses)
+        torch.testing.assert_close(res[r]["flat"].float(), ref_flat.float(), rtol=2 ** -7, atol=2 * 3 * 1e-3)
+    for r in range(1, 4):
+        assert torch.equal(res[0]["flat"], res[r]["flat"])
