@@ -115,3 +115,54 @@ def c10d_backend(rank, world, out, args):
     res["async"] = True
     dist.destroy_process_group(g)
     return res
+
+
+def nvl_world1(rank, world, out, args):
+    """The NVLink exchange kernels on a one-rank group (every peer pointer is
+    this GPU's own buffer): fused Ulysses dispatch / remaps and the ring K/V
+    dispatch + dK/dV push, through attention forward and backward, against
+    fp32 SDPA.  Returns max errors relative to each reference's largest value."""
+    import torch.nn.functional as F
+
+    from harp_b200.parallel.nvlink import NVLinkComm
+    from harp_b200.runtime import errors
+
+    dev = torch.device("cuda", rank)
+    comm = NVLinkComm.get(dist.group.WORLD, dev)
+    B, S, H, Dh = 2, 384, 2, 64
+    g = torch.Generator(device=dev).manual_seed(11)
+    qkv = torch.randn(B * S, 3 * H * Dh, device=dev, generator=g).bfloat16()
+    do = torch.randn(B * S, H * Dh, device=dev, generator=g).bfloat16()
+
+    def heads(x):
+        return x.float().reshape(B, S, H, Dh).transpose(1, 2)
+
+    def rows(x):
+        return x.transpose(1, 2).reshape(B * S, H * Dh)
+
+    q, k, v = (heads(t).requires_grad_(True) for t in qkv.split(H * Dh, 1))
+    ref = F.scaled_dot_product_attention(q, k, v)
+    ref.backward(heads(do))
+    ref_o = rows(ref.detach())
+    ref_d = [rows(t.grad) for t in (q, k, v)]
+
+    def rel(a, b):
+        return ((a.float() - b).abs().max() / b.abs().max()).item()
+
+    res = {}
+    comm.begin_step()
+    o, _, _, saved = comm.uly_forward(qkv, B, S, H, Dh, None, None, None, 0.0, False)
+    dqkv = comm.uly_backward(saved, do, B, S, H, Dh)
+    torch.cuda.synchronize()
+    res["uly_o"] = rel(o, ref_o)
+    res["uly_dq"], res["uly_dk"], res["uly_dv"] = (rel(t, r) for t, r in zip(dqkv.split(H * Dh, 1), ref_d))
+    comm.begin_step()
+    qs, ks, vs = (t.contiguous() for t in qkv.split(H * Dh, 1))
+    o2, q2, _, _, saved2 = comm.ring_forward(qs, ks, vs, B, S, H, Dh, q_ready=True)
+    dq2, dkv2 = comm.ring_backward(saved2, q2, o2, do, B, S, H, Dh)
+    torch.cuda.synchronize()
+    res["ring_o"] = rel(o2, ref_o)
+    res["ring_dq"] = rel(dq2, ref_d[0])
+    res["ring_dk"], res["ring_dv"] = (rel(t, r) for t, r in zip(dkv2.split(H * Dh, 1), ref_d[1:]))
+    errors.check(dev)
+    return res

@@ -113,6 +113,16 @@ def test_sp2_cuda_graph_step_matches_eager(tmp_path, monkeypatch, mode, shard):
     assert torch.equal(res[True][0]["flat"], res[True][1]["flat"])
 
 
+def test_nvlink_exchange_kernels_on_one_rank(tmp_path):
+    """The fused Ulysses and ring exchange kernels on a one-GPU group (the peer
+    tables hold this GPU's own buffers), so they also run where only one GPU
+    is present: attention forward and backward through them match fp32 SDPA."""
+    _need(1)
+    res = _run("nvl_world1", 1, tmp_path, {})[0]
+    for key, err in res.items():
+        assert err < 2e-2, (key, err, res)
+
+
 def test_never_signalled_flag_times_out_cleanly(tmp_path):
     _need(2)
     res = _run("flag_timeout", 2, tmp_path, {})
