@@ -11,23 +11,34 @@ publishes "my buffer for epoch e is ready" by storing e into its slot of every
 peer's flag array (release, system scope); consumers wait until the slot is
 >= e (acquire, bounded by a timeout that raises HarpDeviceError instead of
 hanging).  Because epochs only grow, flags are never reset.  No kernel waits
-for another kernel of the same GPU: every wait is for a flag that a peer GPU
-writes.
+for another kernel of the same GPU that may still be running: every wait is
+for a flag that a peer GPU writes, or (own slot, or a one-rank group) that an
+earlier kernel of the same stream has already written.
+
+Inside a captured CUDA graph every flag value is step-relative: a kernel
+computes it on the device as the value seen at capture plus the counter's
+per-step increment times step_delta[0], which the host bumps before each
+replay (begin_capture / _sd; step_value in common.cuh).
 
 Purposes and buffers:
-  KV      per-layer symmetric K|V buffers; a layer's gather waits for each
-          peer's KV flag and pulls its chunk into the local gathered buffer.
-  DKV     two symmetric dK|dV buffers used alternately by consecutive
-          backward layers; the pull reduce-scatter of layer i waits for the
-          peers' DKV flags; DKV_ACK tells the writer that everyone finished
-          pulling, before the buffer is written again two layers later.
+  KV      per-layer symmetric K|V buffers of the ring path: the QK-norm/RoPE
+          kernel stores this rank's K|V chunk into every rank's buffer and
+          raises KV; the attention forward waits per key tile for the flag
+          of the chunk it reads, starting with its own.
+  DKV     two symmetric dK|dV receive buffers (one slot per sender) used
+          alternately by consecutive backward layers: the attention
+          backward stores each key chunk's dK|dV into its owner's slot and
+          raises DKV; the owner's reduce waits for every peer's DKV, and
+          DKV_ACK tells the senders that it has summed the buffer before it
+          is written again two layers later.
   GRAD / PARAM  the fused gradient reduce-scatter + AdamW + parameter push
           waits for every peer's GRAD flag; PARAM tells peers the new
           parameters have landed, which the next step waits for.
   GATH / GACK  sharded parameters (harp_b200.parallel.param_shard): each rank
           pushes its slice of a block's weights into every rank's staging
           slot s and sets GATH[s] to the slot's gather count; the GEMMs of
-          that block wait for every GATH[s] inside their producer warp.  A
+          that block wait for every GATH[s] (each CTA's thread 0, before its
+          roles start).  A
           rank sets GACK[s] to the number of uses of slot s it has finished;
           a push into slot s first waits until every rank has finished all
           earlier uses.
@@ -149,11 +160,9 @@ class NVLinkComm:
         self._per_step: Optional[Dict[str, int]] = None
         self._uly: List[Dict[str, SymBuffer]] = []
         self._uly_idx = 0
-        self._kv_bufs: List[SymBuffer] = []
         self._kv_idx = 0
         self._ring_bufs: List[SymBuffer] = []
         self._dkv_push: List[SymBuffer] = []
-        self._dkv_bufs: List[SymBuffer] = []
         self._dkv_idx = 0
         self._dkv_last_epoch = [0, 0]
         self._flat: Optional[Dict[str, SymBuffer]] = None
@@ -180,9 +189,6 @@ class NVLinkComm:
             return None, 0
         return self.step_delta, self._per_step.get(counter, 0)
 
-    def _eager_only(self, what: str):
-        assert self._per_step is None, f"{what} cannot be captured in a CUDA graph"
-
     def signal(self, base: int, value: int, counter: Optional[str] = None):
         """Store `value` into slot base+rank of every rank's flag array (self included)."""
         sd, ps = self._sd(counter)
@@ -204,33 +210,7 @@ class NVLinkComm:
         self._dkv_idx = 0
         self._uly_idx = 0
 
-    # -- sequence-parallel K/V exchange (forward) -------------------------------
-    def kv_exchange(self, k: torch.Tensor, v: torch.Tensor, B: int, S: int, HD: int):
-        """k, v: local [B*S, HD] views.  Returns (kv_full [B*W*S, 2HD], None, 0):
-        rows (b*W + c)*S .. +S of kv_full hold rank c's K|V of sample b."""
-        self._eager_only("kv_exchange")
-        i = self._kv_idx
-        self._kv_idx += 1
-        nbytes = B * S * 2 * HD * 2
-        while len(self._kv_bufs) <= i:
-            self._kv_bufs.append(SymBuffer(self.group, nbytes, self.device))
-        buf = self._kv_bufs[i]
-        assert buf.nbytes >= nbytes, "K/V exchange buffer shape changed between steps"
-        kv_out = buf.tensor(B * S * 2 * HD, torch.bfloat16).view(B * S, 2 * HD)
-        kv_out[:, :HD].copy_(k)
-        kv_out[:, HD:].copy_(v)
-        self.epoch["kv"] += 1
-        e = self.epoch["kv"]
-        self.signal(_KV, e)
-        W = self.world
-        kv_full = torch.empty(B * W * S, 2 * HD, device=k.device, dtype=torch.bfloat16)
-        row = 2 * HD * 2  # bytes per token row
-        # each (source c, sample b) is one contiguous segment of S rows
-        torch.ops.harp_comm.gather(buf.bases, 0, S * row, kv_full, 0, S * row, W * S * row, S * row, B, self.rank,
-                                   self.flags, _KV, e, self.timeout_s, self.err)
-        return kv_full, None, 0
-
-    # -- ring (K/V gather) fused with its producer ------------------------------
+    # -- sequence-parallel ring attention: K/V pushed to every rank, dK/dV back --
     def ring_forward(self, q, k, v, B: int, S: int, H: int, Dh: int, wq=None, wk=None, freqs=None, eps: float = 1e-6,
                      do_norm: bool = False, q_ready: bool = False):
         """q, k, v: this rank's pre-norm rows [B*S, >=H*Dh] (views of one q|k|v
@@ -309,38 +289,6 @@ class NVLinkComm:
         self.signal(_DKV_ACK0 if j == 0 else _DKV_ACK1, e, "dkv")
         return dq, out
 
-    # -- sequence-parallel dK/dV reduce-scatter (backward) ----------------------
-    def dkv_buffer(self, rows: int, cols: int, dtype) -> torch.Tensor:
-        slot = self._dkv_idx % 2
-        nbytes = rows * cols * 2
-        while len(self._dkv_bufs) < 2:
-            self._dkv_bufs.append(SymBuffer(self.group, nbytes, self.device))
-        assert self._dkv_bufs[slot].nbytes >= nbytes
-        # everyone must have finished pulling what this buffer held two layers ago
-        last = self._dkv_last_epoch[slot]
-        if last > 0:
-            self.wait_all(_DKV_ACK0 if slot == 0 else _DKV_ACK1, last)
-        return self._dkv_bufs[slot].tensor(rows * cols, torch.bfloat16).view(rows, cols)
-
-    def dkv_reduce_scatter(self, dkv_full: torch.Tensor, B: int, S: int, HD: int) -> torch.Tensor:
-        self._eager_only("dkv_reduce_scatter")
-        slot = self._dkv_idx % 2
-        self._dkv_idx += 1
-        buf = self._dkv_bufs[slot]
-        self.epoch["dkv"] += 1
-        e = self.epoch["dkv"]
-        self.signal(_DKV, e)
-        W = self.world
-        out = torch.empty(B * S, 2 * HD, device=dkv_full.device, dtype=torch.bfloat16)
-        # my chunk of sample b in every peer's dkv_full: rows (b*W + rank)*S .. +S
-        seg = S * 2 * HD
-        torch.ops.harp_comm.reduce_scatter(buf.bases, self.rank * seg, W * seg, out, seg, seg, B, self.rank,
-                                           self.flags, _DKV, e, self.timeout_s, self.err)
-        self._dkv_last_epoch[slot] = e
-        self.signal(_DKV_ACK0 if slot == 0 else _DKV_ACK1, e)
-        return out
-
-    # -- Ulysses: head all-to-all fused with QK-norm/RoPE and attention --------
     def _uly_layer(self, i: int, B: int, S: int, H: int, Dh: int) -> Dict[str, SymBuffer]:
         W = self.world
         HD, HnDh = H * Dh, (H // W) * Dh
@@ -543,9 +491,9 @@ class NVLinkComm:
         torch.cuda.synchronize(self.device)
         uly = [b for layer in self._uly for b in layer.values()]
         slots = [self._slots] if getattr(self, "_slots", None) is not None else []
-        for b in (self._kv_bufs + self._dkv_bufs + self._ring_bufs + self._dkv_push + uly + slots +
+        for b in (self._ring_bufs + self._dkv_push + uly + slots +
                   list((self._flat or {}).values()) + [self.flags_buf]):
             b.release()
-        self._kv_bufs, self._dkv_bufs, self._flat, self._uly = [], [], None, []
+        self._flat, self._uly = None, []
         self._ring_bufs, self._dkv_push = [], []
         self._slots = None
