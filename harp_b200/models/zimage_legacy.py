@@ -26,7 +26,7 @@ state-dict keys as the diffusers class; diffusers is not needed).
 from __future__ import annotations
 
 import copy
-from typing import Dict, List, Optional, Sequence, Tuple
+from typing import Dict, List, Optional, Tuple
 
 import torch
 import torch.nn as nn
@@ -122,14 +122,16 @@ class Z_Transformer(nn.Module, Z_Mixin):
     (a refiner copied from the noise refiner, a 2x2x192 -> dim embedder and a
     pad token)."""
 
-    def __init__(self, z_transformer: ZImageTransformer2DModel, num_metadata: int = 0, in_channels: Optional[int] = None,
-                 use_cond: bool = False, cond_channels: int = 192, harp_block_compat: bool = False):
+    def __init__(self, z_transformer: ZImageTransformer2DModel, num_metadata: int = 0,
+                 in_channels: Optional[int] = None, use_cond: bool = False, cond_channels: int = 192,
+                 harp_block_compat: bool = False):
         super().__init__()
         self.in_channels = self.out_channels = in_channels or z_transformer.in_channels
         c = harp_block_compat
         self.cond_embedder = None
         if use_cond:
-            self.cond_refiner = nn.ModuleList([Z_SingleBlock(b, 1, c) for b in copy.deepcopy(z_transformer.noise_refiner)])
+            self.cond_refiner = nn.ModuleList([Z_SingleBlock(b, 1, c)
+                                               for b in copy.deepcopy(z_transformer.noise_refiner)])
             self.cond_embedder = Linear(2 * 2 * cond_channels, z_transformer.dim)
             self.cond_pad_token = nn.Parameter(z_transformer.x_pad_token.detach().clone())
         self.noise_refiner = nn.ModuleList([Z_SingleBlock(b, 1, c) for b in z_transformer.noise_refiner])

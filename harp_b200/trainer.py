@@ -38,7 +38,7 @@ from typing import Dict, List, Optional
 import torch
 import torch.distributed as dist
 
-from .models.dit import DiT, flow_matching_loss_local
+from .models.dit import flow_matching_loss_local
 from .ops import functional as Fn
 from .parallel import collectives as C
 from .parallel.sequence import SPContext, resolve_mode
