@@ -209,3 +209,58 @@ def baseline_mmdit(rank, world, out, args):
     tr = BaselineMMDiTTrainer(args["model"], torch.device("cpu"), world, shard=args.get("shard", False))
     b = torch.load(args["batch"])
     return {"losses": [float(tr.train_step(b["latent"], b["noise"], b["text"], b["sigmas"])) for _ in range(3)]}
+
+
+class _HostComm:
+    """Stand-in for the NVLink communicator's buffer API on CPU: plain tensors
+    for the flat parameter/gradient buffers and the two staging slots."""
+
+    def __init__(self, rank, world):
+        self.rank, self.world = rank, world
+
+    def allocate_flat(self, numel, param_numel=None):
+        pn = numel if param_numel is None else param_numel
+        return torch.zeros(pn, dtype=torch.bfloat16), torch.zeros(numel, dtype=torch.bfloat16)
+
+    def param_slots(self, numel):
+        self._slots = torch.zeros(2 * numel, dtype=torch.bfloat16)
+        self._slot_numel = numel
+        return self._slots
+
+    def slot_view(self, s):
+        return self._slots[s * self._slot_numel:(s + 1) * self._slot_numel]
+
+
+def sharded_layout(rank, world, out, args):
+    """ShardedFlatParams on gloo ranks with the host stand-in: each rank keeps
+    1/world of every block bucket, the replicated rest sits at the start of the
+    parameter buffer, and the gathered views reproduce the model."""
+    from harp_b200.models.mmdit import MMDiT, PRESETS
+    from harp_b200.parallel.param_shard import ShardedFlatParams, shard_groups
+
+    torch.manual_seed(0)
+    model = MMDiT(PRESETS["flux-tiny"])
+    model.initialize_weights(0)
+    model = model.to(torch.bfloat16)
+    ref = {n: p.detach().clone() for n, p in model.named_parameters()}
+    comm = _HostComm(rank, world)
+    flat = ShardedFlatParams(model, torch.device("cpu"), comm, align=64)
+    res = {"n_groups": len(shard_groups(model)), "rest": flat.rest_bucket, "buckets": len(flat.buckets)}
+    views = flat.state_dict_views(dist.group.WORLD)
+    res["views_match"] = all(torch.equal(views[n], ref[n]) for n in ref)
+    # gather each block bucket by hand into slot 0 and point the block at it
+    name_of = {id(p): n for n, p in zip(flat.names, flat.params)}
+    ok = True
+    for b in flat.bucket_params:
+        lo, hi = flat.buckets[b]
+        full = flat.full_bucket(b, dist.group.WORLD)
+        comm.slot_view(0)[:hi - lo].copy_(full)
+        flat.point(b, 0)
+        for p, rel in flat.bucket_params[b]:
+            ok = ok and torch.equal(p.data, ref[name_of[id(p)]])
+        nb = (hi - lo) // world
+        ok = ok and torch.equal(flat.local_slice(b), full[rank * nb:(rank + 1) * nb])
+        ok = ok and flat.local_out(b) is not None
+    res["points_match"] = ok
+    res["rest_local"] = flat.local_out(flat.rest_bucket) is None
+    return res

@@ -209,3 +209,14 @@ def test_trainer_four_ranks_matches_single_process(tmp_path, sp, mode):
         torch.testing.assert_close(res[r]["flat"].float(), ref_flat.float(), rtol=2 ** -7, atol=2 * 3 * 1e-3)
     for r in range(1, 4):
         assert torch.equal(res[0]["flat"], res[r]["flat"])
+
+
+def test_sharded_weight_layout_two_ranks(tmp_path):
+    """Host-side logic of sharded block weights (parallel/param_shard.py) on
+    two gloo ranks with a CPU stand-in for the symmetric buffers: one bucket
+    per block, each rank's slice, the gathered views and the staging-slot
+    re-pointing all reproduce the model's parameters."""
+    res, _ = _run("sharded_layout", 2, tmp_path)
+    for r in (0, 1):
+        assert res[r]["views_match"] and res[r]["points_match"] and res[r]["rest_local"], res[r]
+        assert res[r]["buckets"] == res[r]["n_groups"] + 1 and res[r]["rest"] == res[r]["n_groups"], res[r]
