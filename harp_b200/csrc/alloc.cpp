@@ -58,7 +58,8 @@ struct HostPool {
   std::map<size_t, std::vector<HostBlock>> free_;  // size class -> cached blocks
   std::unordered_map<void*, size_t> live_;         // ptr -> size class
   Stats st;
-  int64_t cap = env_bytes("HARP_MAX_DDR_MEMORY", "MAX_DDR_MEMORY");
+  // read by allocating threads, changed at run time by harp_alloc_set_cap
+  std::atomic<int64_t> cap{env_bytes("HARP_MAX_DDR_MEMORY", "MAX_DDR_MEMORY")};
 
   static size_t size_class(size_t n) {
     if (n <= 512) return 512;
@@ -102,8 +103,9 @@ struct HostPool {
         return b.ptr;
       }
     }
-    if (cap > 0 && st.in_use.load() + st.cached.load() + (int64_t)c > cap) release_cached_locked();
-    if (cap > 0 && st.in_use.load() + (int64_t)c > cap) {
+    const int64_t limit = cap.load();
+    if (limit > 0 && st.in_use.load() + st.cached.load() + (int64_t)c > limit) release_cached_locked();
+    if (limit > 0 && st.in_use.load() + (int64_t)c > limit) {
       st.fails++;
       return nullptr;
     }
@@ -155,11 +157,12 @@ struct DevicePool {
   std::mutex mu;
   std::unordered_map<void*, size_t> live_;
   Stats st;
-  int64_t cap = env_bytes("HARP_MAX_HBM_MEMORY", "MAX_HBM_MEMORY");
+  std::atomic<int64_t> cap{env_bytes("HARP_MAX_HBM_MEMORY", "MAX_HBM_MEMORY")};
 
   void* alloc(size_t n, int device, cudaStream_t stream) {
     size_t c = (n + 511) / 512 * 512;
-    if (cap > 0 && st.in_use.load() + (int64_t)c > cap) {
+    const int64_t limit = cap.load();
+    if (limit > 0 && st.in_use.load() + (int64_t)c > limit) {
       st.fails++;
       return nullptr;
     }
@@ -252,8 +255,8 @@ void harp_host_empty_cache() {
 // Caps can be changed at run time (bytes; 0 = unlimited).
 void harp_alloc_set_cap(int tier, long long bytes) {
   if (tier == 0)
-    host_pool().cap = bytes;
+    host_pool().cap.store(bytes);
   else
-    device_pool().cap = bytes;
+    device_pool().cap.store(bytes);
 }
 }
