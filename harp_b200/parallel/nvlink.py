@@ -80,6 +80,27 @@ _NFLAGS = _GACK + 16
 # outstanding 16-byte NVLink loads to keep the links busy, few enough SMs that
 # the backward it overlaps keeps most of the GPU
 BUCKET_CTAS = int(os.environ.get("HARP_BUCKET_CTAS", "24"))
+# HARP_ULY_PUSH=1: the Ulysses attention backward stores dK / dV straight into
+# their owners' dq|dk|dv rows from its epilogue (as the ring path does) and
+# only dQ goes through the remap kernel.  Off by default: not yet timed.
+ULY_PUSH = os.environ.get("HARP_ULY_PUSH", "0") == "1"
+
+
+def uly_dkv_push(dqkv_bases: List[int], rank: int, H: int, Dh: int, S: int) -> Dict[str, object]:
+    """Arguments of the attention backward's dK/dV push for the Ulysses layout.
+
+    The backward runs on this rank's Hn = H / W heads over the full sequence
+    (W chunks of S rows per sample); key row c*S + s of local head hn belongs
+    to rank c, at row b*S + s of its [B*S, 3*H*Dh] dq|dk|dv buffer, column
+    H*Dh + (rank*Hn + hn)*Dh (dK) or 2*H*Dh + (rank*Hn + hn)*Dh (dV) -- the
+    places the head-to-sequence remap would write.  The kernel adds
+    (b*chunk + s)*ld + hn*Dh (+ vcol for dV) elements to base[c], so base[c]
+    carries the column offset of this rank's heads in dK."""
+    W = len(dqkv_bases)
+    HD, Hn = H * Dh, H // W
+    col = HD + rank * Hn * Dh  # elements
+    return {"bases": [b + 2 * col for b in dqkv_bases], "chunk": S, "rank": 0, "slot": 0, "ld": 3 * HD,
+            "vcol": HD}
 DEFAULT_TIMEOUT_S = float(os.environ.get("HARP_COMM_TIMEOUT_S", "120"))
 
 
@@ -149,6 +170,7 @@ class NVLinkComm:
         self.world, self.rank = C.world(group), C.rank(group)
         assert self.world <= 8, "harp NVLink comm: one node, at most 8 GPUs"
         self.timeout_s = timeout_s
+        self.uly_push = ULY_PUSH
         self.flags_buf = SymBuffer(group, _NFLAGS * 4, device)
         self.flags = self.flags_buf.tensor(_NFLAGS, torch.int32)
         self.flag_bases = self.flags_buf.bases
@@ -353,13 +375,15 @@ class NVLinkComm:
             self.wait_all(_UDO, e, "udo")
         dof = bufs["dof"].tensor(B * Sf * Hn * Dh, torch.bfloat16).view(B * Sf, Hn * Dh)
         qkvf = saved["qkvf"]
+        push = uly_dkv_push(bufs["dqkv"].bases, r, H, Dh, S) if self.uly_push else None
         with phase("uly.attn_bwd"):
             dq_f, dk_f, dv_f = Fn.attn_bwd(qkvf[0], qkvf[1], qkvf[2], saved["o_f"], dof, saved["lse"], B, Sf, Sf,
-                                           Hn, Dh)
+                                           Hn, Dh, push=push)
         self.epoch["udq"] += 1
         e2 = self.epoch["udq"]
         with phase("uly.dqkv_remap"):
-            torch.ops.harp_comm.uly_remap([dq_f, dk_f, dv_f], 1, B, S, r, H, Dh, bufs["dqkv"].bases, 0, 3 * HD, HD)
+            parts = [dq_f] if push is not None else [dq_f, dk_f, dv_f]
+            torch.ops.harp_comm.uly_remap(parts, 1, B, S, r, H, Dh, bufs["dqkv"].bases, 0, 3 * HD, HD)
             self.signal(_UDQ, e2, "udq")
         with phase("uly.dqkv_wait"):
             self.wait_all(_UDQ, e2, "udq")

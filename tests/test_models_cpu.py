@@ -373,3 +373,29 @@ def test_mmdit_reports_parameters_a_rank_does_not_use():
     ids = {id(p) for p in seen}
     assert {id(p) for p in model.txt_in.parameters()} <= ids
     assert not ({id(p) for p in model.img_in.parameters()} & ids)
+
+
+def test_ulysses_dkv_push_addresses_match_the_remap():
+    """The attention backward's dK/dV push arguments for the Ulysses layout
+    (uly_dkv_push) put every element where the head-to-sequence remap puts it:
+    the kernel's destination (base[c] + (b*chunk + s)*ld + hn*Dh (+vcol), as in
+    dkv_dst_row of attention_sm100.cu) against the remap's (base[c] +
+    (b*S + s)*ld + p*pcol + (rank*Hn + hn)*Dh, uly_remap_kernel in ulysses.cu)."""
+    from harp_b200.parallel.nvlink import uly_dkv_push
+
+    for W, H, Dh, S, B in ((2, 16, 72, 64, 2), (8, 16, 72, 32, 1), (4, 24, 128, 48, 2)):
+        bases = [(c + 1) << 32 for c in range(W)]
+        HD, Hn = H * Dh, H // W
+        for rank in range(W):
+            a = uly_dkv_push(bases, rank, H, Dh, S)
+            assert a["chunk"] * W == W * S and a["ld"] % 8 == 0 and a["vcol"] % 8 == 0
+            for b in range(B):
+                for key in (0, S - 1, S, W * S - 1):
+                    c, s = key // a["chunk"], key % a["chunk"]
+                    for hn in (0, Hn - 1):
+                        for is_v, part in ((False, 1), (True, 2)):
+                            kern = a["bases"][c] + 2 * ((b * a["chunk"] + s) * a["ld"] + (a["vcol"] if is_v else 0)
+                                                        + hn * Dh)
+                            remap = bases[c] + 2 * ((b * S + s) * 3 * HD + part * HD + (rank * Hn + hn) * Dh)
+                            assert kern == remap, (W, rank, b, key, hn, is_v)
+                            assert kern % 16 == 0
