@@ -269,3 +269,38 @@ def test_launch_rankfile_cpu_sets_and_command(tmp_path):
     assert L.cpu_sets(4, affinity=aff) == [[0, 1], [2, 3], [4, 5], [6, 7]]
     cmd = L.torchrun_cmd(["train.py", "--x"], 8)
     assert "--master-addr=127.0.0.1" in cmd and cmd[-2:] == ["train.py", "--x"]
+
+
+def test_train_cli_checkpoint_and_resume_bit_exact(tmp_path):
+    """train.py end to end on CPU (tiny DiT, synthetic data): a 3-step run saves
+    checkpoint-2 and logs metrics; a second run with --resume_from_checkpoint
+    latest continues at step 3 with the same loss, bit for bit."""
+    import json
+    import subprocess
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    work = str(tmp_path / "w")
+    base = [sys.executable, os.path.join(root, "train.py"), "--model", "tiny", "--synthetic", "--latent_size", "16",
+            "--text_len", "16", "--max_train_steps", "3", "--train_batch_size", "2", "--sp_size", "1",
+            "--work_dir", work, "--checkpointing_steps", "2", "--lr_warmup_steps", "1"]
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="")
+
+    def losses(out_dir):
+        rows = [json.loads(l) for l in open(os.path.join(out_dir, "metrics.jsonl")) if l.strip()]
+        return {r["global_step"]: r["step_loss"] for r in rows if "step_loss" in r}
+
+    r1 = subprocess.run(base, capture_output=True, text=True, timeout=600, env=env, cwd=str(tmp_path))
+    assert r1.returncode == 0, r1.stderr[-3000:]
+    runs = sorted(os.listdir(work))
+    assert len(runs) == 1 and os.path.isdir(os.path.join(work, runs[0], "checkpoint-2"))
+    first = losses(os.path.join(work, runs[0]))
+    assert sorted(first) == [1, 2, 3]
+    r2 = subprocess.run(base + ["--resume_from_checkpoint", "latest"], capture_output=True, text=True, timeout=600,
+                        env=env, cwd=str(tmp_path))
+    assert r2.returncode == 0, r2.stderr[-3000:]
+    metrics = [os.path.join(d, "metrics.jsonl") for d, _, files in os.walk(work) if "metrics.jsonl" in files]
+    second_runs = [m for m in metrics if os.path.dirname(m) != os.path.join(work, runs[0])]
+    assert len(second_runs) == 1, metrics
+    second = losses(os.path.dirname(second_runs[0]))
+    assert sorted(second) == [3] and second[3] == first[3], (first, second)
