@@ -473,12 +473,36 @@ def _local(x: torch.Tensor, sp: SPContext) -> torch.Tensor:
     return x[:, lo:hi]
 
 
+class _GatherSeq(torch.autograd.Function):
+    """All-gather of a stream's chunks along dim 1 whose backward sums the
+    gradient over the ranks before taking this rank's chunk.  After the
+    gather every rank keeps a different chunk of the unified sequence (not a
+    replicated copy), so a stream token's gradient can come from another rank;
+    the reference's SequenceAllGather backward (own chunk only) assumes the
+    replicated case."""
+
+    @staticmethod
+    def forward(ctx, x, group):
+        from ..managers.shard_manager import _gather_dim1
+
+        ctx.group = group
+        return _gather_dim1(x, group)
+
+    @staticmethod
+    def backward(ctx, g):
+        import torch.distributed as dist
+
+        from ..managers.shard_manager import _chunk
+
+        g = g.contiguous().clone()
+        dist.all_reduce(g, op=dist.ReduceOp.SUM, group=ctx.group)
+        return _chunk(g, ctx.group).contiguous(), None
+
+
 def _gather_seq(x: torch.Tensor, sp: SPContext) -> torch.Tensor:
     if sp.size == 1:
         return x
-    from ..managers.shard_manager import SequenceAllGather
-
-    return SequenceAllGather.apply(x.contiguous(), sp.group)
+    return _GatherSeq.apply(x.contiguous(), sp.group)
 
 
 def zimage_loss_local(model: Z_Transformer, latent, noise, text, sigmas, sp: SPContext, metadata=None, cond=None,

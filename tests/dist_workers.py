@@ -264,3 +264,42 @@ def sharded_layout(rank, world, out, args):
     res["points_match"] = ok
     res["rest_local"] = flat.local_out(flat.rest_bucket) is None
     return res
+
+
+def _zimage_model():
+    from harp_b200.models import zimage as Z
+
+    torch.manual_seed(0)
+    base = Z.ZImageTransformer2DModel(**Z.PRESETS["zimage-tiny"])
+    model = Z.Z_Transformer(base, num_metadata=2, use_cond=True)
+    with torch.no_grad():
+        for p in model.parameters():
+            p.normal_(0, 0.05)
+    return model.bfloat16()
+
+
+def _zimage_batch():
+    g = torch.Generator().manual_seed(8)
+    return {"lat": torch.randn(2, 16, 16, 16, generator=g).bfloat16(),
+            "noise": torch.randn(2, 16, 16, 16, generator=g).bfloat16(),
+            "text": torch.randn(2, 32, 64, generator=g).bfloat16(), "sig": torch.rand(2, generator=g),
+            "meta": torch.rand(2, 2, generator=g).bfloat16(),
+            "cond": [torch.randn(2, 192, 16, 16, generator=g).bfloat16()]}
+
+
+def zimage_sp(rank, world, out, args):
+    """Z-Image SP wrapper (refiners, condition branch, metadata, joint layers)
+    sequence-parallel over the gloo ranks: this rank's loss share and the
+    gradients, summed over ranks by the caller."""
+    from harp_b200.models import zimage as Z
+    from harp_b200.parallel.sequence import SPContext
+
+    model = _zimage_model()
+    b = _zimage_batch()
+    sp = SPContext.from_group(dist.group.WORLD, backend="torch", mode=args.get("mode", "ring"))
+    loss = Z.zimage_loss_local(model, b["lat"], b["noise"], b["text"], b["sig"], sp, metadata=b["meta"],
+                               cond=b["cond"])
+    loss.backward()
+    grads = torch.cat([(p.grad if p.grad is not None else torch.zeros_like(p)).float().reshape(-1)
+                       for p in model.parameters()])
+    return {"loss": float(loss), "grads": grads}

@@ -220,3 +220,28 @@ def test_sharded_weight_layout_two_ranks(tmp_path):
     for r in (0, 1):
         assert res[r]["views_match"] and res[r]["points_match"] and res[r]["rest_local"], res[r]
         assert res[r]["buckets"] == res[r]["n_groups"] + 1 and res[r]["rest"] == res[r]["n_groups"], res[r]
+
+
+def test_zimage_two_ranks_match_one():
+    """The Z-Image SP wrapper over two gloo ranks: the ranks' loss shares and
+    gradients sum to the one-process loss and gradients (the reference never
+    checks its SP model against a single-rank run)."""
+    import tempfile
+
+    from harp_b200.models import zimage as Z
+    from harp_b200.parallel.sequence import SPContext
+
+    model = W._zimage_model()
+    b = W._zimage_batch()
+    loss = Z.zimage_loss_local(model, b["lat"], b["noise"], b["text"], b["sig"], SPContext(), metadata=b["meta"],
+                               cond=b["cond"])
+    loss.backward()
+    ref_g = torch.cat([(p.grad if p.grad is not None else torch.zeros_like(p)).float().reshape(-1)
+                       for p in model.parameters()])
+    with tempfile.TemporaryDirectory() as d:
+        res, _ = _run("zimage_sp", 2, d)
+    tot = res[0]["loss"] + res[1]["loss"]
+    assert tot == pytest.approx(float(loss), rel=2e-2), (tot, float(loss))
+    g = res[0]["grads"] + res[1]["grads"]
+    rel = ((g - ref_g).norm() / ref_g.norm()).item()
+    assert rel < 2e-2, rel

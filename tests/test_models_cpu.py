@@ -399,3 +399,29 @@ def test_ulysses_dkv_push_addresses_match_the_remap():
                             remap = bases[c] + 2 * ((b * S + s) * 3 * HD + part * HD + (rank * Hn + hn) * Dh)
                             assert kern == remap, (W, rank, b, key, hn, is_v)
                             assert kern % 16 == 0
+
+
+def test_zimage_sp_wrapper_matches_base_model():
+    """The reference never compares its SP wrapper with the base model; here the
+    wrapper's forward (one rank, no condition branch or metadata) gives the base
+    ZImageTransformer2DModel's prediction on the same weights."""
+    import copy
+
+    torch.manual_seed(0)
+    pre = Z.PRESETS["zimage-tiny"]
+    base = Z.ZImageTransformer2DModel(**pre)
+    with torch.no_grad():
+        for p in base.parameters():
+            p.normal_(0, 0.05)
+    base = base.bfloat16()
+    ref_base = copy.deepcopy(base)
+    model = Z.Z_Transformer(base, num_metadata=0, use_cond=False)
+    x = [torch.randn(16, 1, 16, 16).bfloat16() for _ in range(2)]
+    t = torch.rand(2)
+    caps = [torch.randn(32, pre["cap_feat_dim"]).bfloat16() for _ in range(2)]
+    with torch.no_grad():
+        want = ref_base(x, t, caps)["sample"]
+        pred, lo, hi = model.forward_local(x, t, caps, sp=SPContext())
+    assert (lo, hi) == (0, 64)
+    want_tok = torch.stack(ref_base.patchify([w.float() for w in want], 2, 1)[0])
+    torch.testing.assert_close(pred.float(), want_tok, rtol=0, atol=0)
