@@ -303,3 +303,37 @@ def zimage_sp(rank, world, out, args):
     grads = torch.cat([(p.grad if p.grad is not None else torch.zeros_like(p)).float().reshape(-1)
                        for p in model.parameters()])
     return {"loss": float(loss), "grads": grads}
+
+
+def _mmdit_setup(name):
+    from harp_b200.models import mmdit as M
+
+    torch.manual_seed(0)
+    model = M.MMDiT(M.PRESETS[name])
+    model.initialize_weights(0)
+    with torch.no_grad():  # give the zero-initialised modulation and final layers some signal
+        for n, p in model.named_parameters():
+            if ".mod." in n or "adaLN" in n or "final_layer" in n:
+                p.normal_(0, 0.02)
+    model = model.bfloat16()
+    cfg = M.PRESETS[name]
+    g = torch.Generator().manual_seed(4)
+    b = {"lat": torch.randn(1, cfg.in_channels, 16, 16, generator=g).bfloat16(),
+         "noise": torch.randn(1, cfg.in_channels, 16, 16, generator=g).bfloat16(),
+         "text": torch.randn(1, 32, cfg.text_dim, generator=g).bfloat16(), "sig": torch.rand(1, generator=g)}
+    return model, b
+
+
+def mmdit_sp(rank, world, out, args):
+    """MMDiT / Flux sequence-parallel over the gloo ranks (the text stream
+    lives on the last rank only): this rank's loss share and gradients."""
+    from harp_b200.models import mmdit as M
+    from harp_b200.parallel.sequence import SPContext
+
+    model, b = _mmdit_setup(args["model"])
+    sp = SPContext.from_group(dist.group.WORLD, backend="torch", mode=args.get("mode", "ring"))
+    loss = M.mmdit_loss_local(model, b["lat"], b["noise"], b["text"], b["sig"], sp)
+    loss.backward()
+    grads = torch.cat([(p.grad if p.grad is not None else torch.zeros_like(p)).float().reshape(-1)
+                       for p in model.parameters()])
+    return {"loss": float(loss), "grads": grads}

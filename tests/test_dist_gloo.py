@@ -245,3 +245,27 @@ def test_zimage_two_ranks_match_one():
     g = res[0]["grads"] + res[1]["grads"]
     rel = ((g - ref_g).norm() / ref_g.norm()).item()
     assert rel < 2e-2, rel
+
+
+@pytest.mark.parametrize("name,mode", [("flux-tiny", "ring"), ("mmdit-tiny", "ulysses")])
+def test_mmdit_two_ranks_match_one(name, mode):
+    """MMDiT / Flux (double- and single-stream blocks) over two gloo ranks: the
+    loss shares and gradients sum to the one-process ones, including the text
+    stream's weights, which only the rank holding text tokens uses."""
+    import tempfile
+
+    from harp_b200.models import mmdit as M
+    from harp_b200.parallel.sequence import SPContext
+
+    model, b = W._mmdit_setup(name)
+    loss = M.mmdit_loss_local(model, b["lat"], b["noise"], b["text"], b["sig"], SPContext())
+    loss.backward()
+    ref_g = torch.cat([(p.grad if p.grad is not None else torch.zeros_like(p)).float().reshape(-1)
+                       for p in model.parameters()])
+    with tempfile.TemporaryDirectory() as d:
+        res, _ = _run("mmdit_sp", 2, d, {"model": name, "mode": mode})
+    tot = res[0]["loss"] + res[1]["loss"]
+    assert tot == pytest.approx(float(loss), rel=2e-2), (tot, float(loss))
+    g = res[0]["grads"] + res[1]["grads"]
+    rel = ((g - ref_g).norm() / ref_g.norm()).item()
+    assert rel < 2e-2, rel
