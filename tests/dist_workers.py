@@ -337,3 +337,23 @@ def mmdit_sp(rank, world, out, args):
     grads = torch.cat([(p.grad if p.grad is not None else torch.zeros_like(p)).float().reshape(-1)
                        for p in model.parameters()])
     return {"loss": float(loss), "grads": grads}
+
+
+def ring_ops_sp(rank, world, out, args):
+    """The reference's ring_attention_ops (through CPURingAttention) over the
+    gloo ranks: each rank's chunk of the output and of dQ/dK/dV."""
+    from harp_b200.ops import ring_ops
+    from harp_b200.parallel.sequence import SPContext
+
+    g = torch.Generator().manual_seed(21)
+    B, H, T, D = 1, 2, 24 * world, 32
+    q, k, v, do = (torch.randn(B, H, T, D, generator=g).bfloat16() for _ in range(4))
+    t = T // world
+    sl = slice(rank * t, (rank + 1) * t)
+    # token-major storage viewed as [B, H, T_local, D], as the reference passes it
+    ql, kl, vl = (x[:, :, sl].transpose(1, 2).contiguous().transpose(1, 2).requires_grad_(True) for x in (q, k, v))
+    ring_ops.set_sp_context(SPContext.from_group(dist.group.WORLD, backend="torch", mode="ring"))
+    o = ring_ops.CPURingAttention.apply(ql, kl, vl, world)
+    o.backward(do[:, :, sl])
+    ring_ops.set_sp_context(None)
+    return {"o": o.detach().float(), "dq": ql.grad.float(), "dk": kl.grad.float(), "dv": vl.grad.float()}
