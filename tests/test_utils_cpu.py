@@ -304,3 +304,40 @@ def test_train_cli_checkpoint_and_resume_bit_exact(tmp_path):
     assert len(second_runs) == 1, metrics
     second = losses(os.path.dirname(second_runs[0]))
     assert sorted(second) == [3] and second[3] == first[3], (first, second)
+
+
+def test_train_cli_two_ranks_checkpoint_resume(tmp_path):
+    """train.py under torchrun with two gloo ranks (2-way sequence parallel):
+    every rank's optimizer shard is saved, and the resumed run's next step has
+    the loss of the uninterrupted run, bit for bit."""
+    import socket
+    import subprocess
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    work = str(tmp_path / "w")
+
+    def cmd(extra):
+        with socket.socket() as s:
+            s.bind(("127.0.0.1", 0))
+            port = s.getsockname()[1]
+        return [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+                "--master-addr", "127.0.0.1", "--master-port", str(port), os.path.join(root, "train.py"),
+                "--model", "tiny", "--synthetic", "--latent_size", "16", "--text_len", "16", "--max_train_steps", "3",
+                "--train_batch_size", "2", "--sp_size", "2", "--work_dir", work, "--checkpointing_steps", "2",
+                "--lr_warmup_steps", "1"] + extra
+
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="")
+    r1 = subprocess.run(cmd([]), capture_output=True, text=True, timeout=900, env=env, cwd=str(tmp_path))
+    assert r1.returncode == 0, r1.stderr[-3000:]
+    (run,) = os.listdir(work)
+    ck = os.path.join(work, run, "checkpoint-2")
+    assert {"optimizer.rank0.bin", "optimizer.rank1.bin", "pytorch_model.bin"} <= set(os.listdir(ck))
+    first = {r["global_step"]: r["step_loss"] for r in map(json.loads, open(os.path.join(work, run, "metrics.jsonl")))
+             if "step_loss" in r}
+    r2 = subprocess.run(cmd(["--resume_from_checkpoint", "latest"]), capture_output=True, text=True, timeout=900,
+                        env=env, cwd=str(tmp_path))
+    assert r2.returncode == 0, r2.stderr[-3000:]
+    second = {r["global_step"]: r["step_loss"] for r in map(json.loads, open(os.path.join(work, "metrics.jsonl")))
+              if "step_loss" in r}
+    assert sorted(second) == [3] and second[3] == first[3], (first, second)
