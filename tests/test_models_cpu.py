@@ -425,3 +425,25 @@ def test_zimage_sp_wrapper_matches_base_model():
     assert (lo, hi) == (0, 64)
     want_tok = torch.stack(ref_base.patchify([w.float() for w in want], 2, 1)[0])
     torch.testing.assert_close(pred.float(), want_tok, rtol=0, atol=0)
+
+
+@pytest.mark.parametrize("name", ["dit-xl-2", "mmdit-2b", "flux-12b"])
+def test_comparison_arm_models_have_the_same_parameters(name):
+    """The NCCL + cuBLAS/SDPA comparison arm (baseline/) builds the same models:
+    equal parameter counts for the benchmark configurations (built on the meta
+    device, no memory)."""
+    import os
+    import sys
+
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "baseline"))
+    if name.startswith("dit"):
+        import dit_baseline as B
+
+        with torch.device("meta"):
+            ours, theirs = D.DiT(D.PRESETS[name]), B.BaselineDiT(D.PRESETS[name])
+    else:
+        import mmdit_baseline as B
+
+        with torch.device("meta"):
+            ours, theirs = M.MMDiT(M.PRESETS[name]), B.BaselineMMDiT(M.PRESETS[name])
+    assert sum(p.numel() for p in ours.parameters()) == sum(p.numel() for p in theirs.parameters())
