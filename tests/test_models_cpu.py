@@ -447,3 +447,61 @@ def test_comparison_arm_models_have_the_same_parameters(name):
         with torch.device("meta"):
             ours, theirs = M.MMDiT(M.PRESETS[name]), B.BaselineMMDiT(M.PRESETS[name])
     assert sum(p.numel() for p in ours.parameters()) == sum(p.numel() for p in theirs.parameters())
+
+
+def _baseline_module(name):
+    import os
+    import sys
+
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "baseline"))
+    import importlib
+
+    return importlib.import_module(name)
+
+
+def _baseline_name(n):
+    """harp parameter name -> the comparison arm's name for the same weight."""
+    for a, b in (("final_layer.adaLN_modulation.1", "final_ada"), ("final_layer.linear", "final"),
+                 ("t_embedder.mlp.0", "t1"), ("t_embedder.mlp.2", "t2"), ("time_in.mlp.0", "t1"),
+                 ("time_in.mlp.2", "t2"), ("adaLN_modulation.1", "ada"), (".mod.1.", ".mod."),
+                 ("norm.query_norm", "q_norm.weight"), ("norm.key_norm", "k_norm.weight"), ("attn.", ""),
+                 ("mlp.", "")):
+        n = n.replace(a, b)
+    return n
+
+
+@pytest.mark.parametrize("name", ["tiny", "flux-tiny", "mmdit-tiny"])
+def test_comparison_arm_computes_the_same_function(name):
+    """Loaded with harp's weights, the comparison arm's model (stock PyTorch)
+    predicts what harp's model predicts, to bf16 rounding: the benchmarks
+    compare two implementations of one model, not two models."""
+    torch.manual_seed(0)
+    if name == "tiny":
+        B_ = _baseline_module("dit_baseline")
+        cfg = D.PRESETS[name]
+        ours, theirs = D.DiT(cfg), B_.BaselineDiT(cfg)
+    else:
+        B_ = _baseline_module("mmdit_baseline")
+        cfg = M.PRESETS[name]
+        ours, theirs = M.MMDiT(cfg), B_.BaselineMMDiT(cfg)
+    ours.initialize_weights(0)
+    with torch.no_grad():  # the zero-initialised modulation and output layers get some signal
+        for n, p in ours.named_parameters():
+            if ".mod." in n or "adaLN" in n or "final" in n:
+                p.normal_(0, 0.02)
+    ours, theirs = ours.bfloat16(), theirs.bfloat16()
+    dst = dict(theirs.named_parameters())
+    with torch.no_grad():
+        for n, p in ours.named_parameters():
+            dst[_baseline_name(n)].copy_(p)
+    g = torch.Generator().manual_seed(1)
+    lat = torch.randn(2, cfg.in_channels, 16, 16, generator=g).bfloat16()
+    text = torch.randn(2, 16, cfg.text_dim, generator=g).bfloat16()
+    t = torch.rand(2, generator=g)
+    x = ours.patchify(lat)
+    with torch.no_grad():
+        a, _, _ = ours.forward_local(x, text, t, 8, 8, SPContext())
+        b, _, _ = theirs.forward_local(x, text, t, 8, 8, None, 1, 0) if name == "tiny" else \
+            theirs(x, text, t, 8, 8, None, 1, 0)
+    err = ((a.float() - b.float()).abs().max() / b.float().abs().max()).item()
+    assert err < 2e-2, err
