@@ -279,31 +279,54 @@ class ZImageTransformer2DModel(nn.Module, ConfigMixin):
 
     def forward(self, x: List[torch.Tensor], t, cap_feats: List[torch.Tensor], patch_size=2, f_patch_size=1,
                 return_dict=True, sp: Optional[SPContext] = None):
-        """Single-rank reference forward (standalone_transformer.py:673-755) on
-        equal-size samples whose caption length is a multiple of 32."""
+        """Single-rank forward (standalone_transformer.py:658-755) on samples of
+        any image size and caption length.
+
+        As in the reference, each sample's image and caption token runs are
+        padded to a multiple of 32 (SEQ_MULTI_OF) with the learned pad tokens at
+        position id (0, 0, 0), and the pad tokens are attended to; only the
+        padding that batches samples of different lengths is masked there.
+        Here samples with the same image size and caption length run together
+        as one dense batch instead, so no mask is needed and the attention
+        sees real rows only: the same result for every real token."""
+        from .zimage_legacy import Z_Mixin  # that module imports this one
+
         sp = sp or SPContext()
-        B = len(x)
-        dev = x[0].device
+        key = f"{patch_size}-{f_patch_size}"
         c = self.t_embedder(t * self.t_scale)
-        imgs, sizes = self.patchify(x, patch_size, f_patch_size)
-        xs = self.all_x_embedder[f"{patch_size}-{f_patch_size}"](torch.stack(imgs))
-        caps = self.cap_embedder(torch.stack(list(cap_feats)).to(xs.dtype))
-        F_, H, W = sizes[0]
-        grid = (F_ // f_patch_size, H // patch_size, W // patch_size)
-        img_ids, cap_ids = self.positions(caps.shape[1], grid, dev)
-        f_img = self.rope_embedder(img_ids).repeat(B, 1, 1)
-        f_cap = self.rope_embedder(cap_ids).repeat(B, 1, 1)
-        adaln = c.to(xs.dtype)
-        for layer in self.noise_refiner:
-            xs = layer(xs, f_img, adaln, sp)
-        for layer in self.context_refiner:
-            caps = layer(caps, f_cap)
-        uni = torch.cat([xs, caps], 1)
-        f_uni = torch.cat([self.rope_embedder(img_ids), self.rope_embedder(cap_ids)], 0).repeat(B, 1, 1)
-        for layer in self.layers:
-            uni = layer(uni, f_uni, adaln, sp)
-        out = self.all_final_layer[f"{patch_size}-{f_patch_size}"](uni, adaln)
-        res = [self.unpatchify(out[i], sizes[i], patch_size, f_patch_size) for i in range(B)]
+        imgs, caps, sizes, img_ids, cap_ids, _, _, _ = Z_Mixin().patchify_and_embed(x, cap_feats, patch_size,
+                                                                                   f_patch_size, None)
+        groups: Dict[tuple, List[int]] = {}
+        for i in range(len(x)):
+            groups.setdefault((sizes[i], cap_feats[i].shape[0]), []).append(i)
+        res: List[Optional[torch.Tensor]] = [None] * len(x)
+        for ((F_, H, W), L), idx in groups.items():
+            n = len(idx)
+            xs = self.all_x_embedder[key](torch.stack([imgs[i] for i in idx]))
+            adaln = c.index_select(0, torch.tensor(idx, device=c.device)).to(xs.dtype)
+            n_img = (F_ // f_patch_size) * (H // patch_size) * (W // patch_size)
+            if xs.shape[1] > n_img:
+                pad = self.x_pad_token.to(xs.dtype).expand(n, xs.shape[1] - n_img, -1)
+                xs = torch.cat([xs[:, :n_img], pad], 1)
+            cs = self.cap_embedder(torch.stack([caps[i] for i in idx]).to(xs.dtype))
+            if cs.shape[1] > L:
+                pad = self.cap_pad_token.to(cs.dtype).expand(n, cs.shape[1] - L, -1)
+                cs = torch.cat([cs[:, :L], pad], 1)
+            f_img = self.rope_embedder(img_ids[idx[0]])
+            f_cap = self.rope_embedder(cap_ids[idx[0]])
+            rep_img = f_img.repeat(n, 1, 1)
+            for layer in self.noise_refiner:
+                xs = layer(xs, rep_img, adaln, sp)
+            rep_cap = f_cap.repeat(n, 1, 1)
+            for layer in self.context_refiner:
+                cs = layer(cs, rep_cap)
+            uni = torch.cat([xs, cs], 1)
+            f_uni = torch.cat([f_img, f_cap], 0).repeat(n, 1, 1)
+            for layer in self.layers:
+                uni = layer(uni, f_uni, adaln, sp)
+            out = self.all_final_layer[key](uni, adaln)
+            for j, i in enumerate(idx):
+                res[i] = self.unpatchify(out[j], sizes[i], patch_size, f_patch_size)
         return (res,) if not return_dict else {"sample": res}
 
 
