@@ -172,7 +172,10 @@ class FinalLayer(nn.Module):
 
 class RopeEmbedder:
     """3-axis rotary tables: axis a of head_dim slice axes_dims[a] uses
-    frequencies theta^(-2i/d_a) at integer positions; returns fp32 (cos, sin)."""
+    frequencies theta^(-2i/d_a) at integer positions; returns fp32 (cos, sin).
+    The angle is formed in fp64 and rounded to fp32 before its cosine and sine,
+    as the reference's precomputed tables are (standalone_transformer.py:388-398),
+    so the rotations agree with a model trained there to fp32 rounding."""
 
     def __init__(self, theta=256.0, axes_dims=(16, 56, 56), axes_lens=(64, 128, 128)):
         self.theta, self.axes_dims, self.axes_lens = theta, tuple(axes_dims), tuple(axes_lens)
@@ -181,9 +184,9 @@ class RopeEmbedder:
         parts = []
         for a, d in enumerate(self.axes_dims):
             inv = 1.0 / (self.theta ** (torch.arange(0, d, 2, dtype=torch.float64, device=ids.device) / d))
-            parts.append(ids[:, a].double()[:, None] * inv[None])
+            parts.append((ids[:, a].double()[:, None] * inv[None]).float())
         ang = torch.cat(parts, -1)
-        return torch.stack([ang.cos(), ang.sin()], -1).float()
+        return torch.stack([ang.cos(), ang.sin()], -1)
 
     def complex(self, ids):
         f = self(ids)

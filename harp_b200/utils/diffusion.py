@@ -150,6 +150,8 @@ def get_scheduler(name: str, optimizer: Optimizer, step_rules: Optional[str] = N
                   num_cycles: Union[int, float] = 1, power: float = 1.0, lr_end: float = 1e-7,
                   last_epoch: int = -1) -> LambdaLR:
     name = name.lower()
+    if name not in ("constant", "piecewise_constant") and num_warmup_steps is None:
+        raise ValueError(f"{name} requires num_warmup_steps")
     W = num_warmup_steps or 0
     T = num_training_steps
 

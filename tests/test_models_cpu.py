@@ -530,42 +530,3 @@ def test_zimage_variable_sizes_and_caption_lengths():
     sum(o.float().pow(2).mean() for o in out).backward()
     assert model.x_pad_token.grad.abs().max() > 0 and model.cap_pad_token.grad.abs().max() > 0
 
-
-@pytest.mark.skipif(not os.environ.get("HARP_REFERENCE_DIR"),
-                    reason="HARP_REFERENCE_DIR (the reference project's root) not set")
-def test_zimage_matches_the_reference_models_own_forward_and_backward():
-    """Oracle test against the reference's own model: its standalone
-    ZImageTransformer2DModel (src/models/z_image/standalone_transformer.py,
-    plain PyTorch, fp32) loads into harp's model with every key matching, and
-    on shared weights the two predict the same images and give the same
-    parameter gradients, to the bf16 rounding of harp's GEMM outputs.  The
-    batch mixes image sizes and caption lengths that need padding."""
-    import importlib.util
-
-    path = os.path.join(os.environ["HARP_REFERENCE_DIR"], "src", "models", "z_image", "standalone_transformer.py")
-    spec = importlib.util.spec_from_file_location("_reference_zimage", path)
-    R = importlib.util.module_from_spec(spec)
-    spec.loader.exec_module(R)
-    pre = dict(Z.PRESETS["zimage-tiny"])
-    torch.manual_seed(0)
-    ref = R.ZImageTransformer2DModel(**{k: (list(v) if isinstance(v, tuple) else v) for k, v in pre.items()})
-    with torch.no_grad():
-        for p in ref.parameters():
-            p.normal_(0, 0.05)
-    ours = Z.ZImageTransformer2DModel(**pre)
-    ours.load_state_dict(ref.state_dict(), strict=True)
-    x = [torch.randn(16, 1, 18, 18), torch.randn(16, 1, 16, 12)]
-    caps = [torch.randn(20, pre["cap_feat_dim"]), torch.randn(32, pre["cap_feat_dim"])]
-    t = torch.rand(2)
-    a = ref(x, t, caps).sample
-    b = ours(x, t, caps)["sample"]
-    w = [torch.randn_like(u) for u in a]
-    sum((u * v).sum() for u, v in zip(a, w)).backward()
-    sum((u.float() * v).sum() for u, v in zip(b, w)).backward()
-    for u, v in zip(a, b):
-        assert ((u - v.float()).abs().max() / u.abs().max()).item() < 2e-2
-    theirs = dict(ref.named_parameters())
-    for n, p in ours.named_parameters():
-        g = theirs[n].grad
-        err = ((p.grad.float() - g).abs().max() / g.abs().max().clamp_min(1e-12)).item()
-        assert err < 5e-2, (n, err)
