@@ -84,9 +84,9 @@ def parse_args(argv=None):
                         "(1 GPU, or N GPUs on the NVLink communicator)")
     p.add_argument("--harp_block_compat", action="store_true", help="Z-Image: reproduce HARP's block residual")
     # accepted for command-line compatibility, unused (as in the reference)
-    for flag, typ in (("--use_8bit_adam", bool), ("--rank", int), ("--resolution", int), ("--cache_dir", str),
-                      ("--comp_ckpt", str)):
-        p.add_argument(flag, type=typ, default=None)
+    for flag, typ, default in (("--use_8bit_adam", bool, False), ("--rank", int, 8), ("--resolution", int, 512),
+                               ("--cache_dir", str, "cache"), ("--comp_ckpt", str, None)):
+        p.add_argument(flag, type=typ, default=default)
     args = p.parse_args(argv)
     if args.sub_work_dir:
         args.work_dir = os.path.join(args.work_dir, args.sub_work_dir)
@@ -196,6 +196,11 @@ def main(args):
         backend = "nccl" if use_cuda else "gloo"
         kw = {"device_id": device} if use_cuda else {}
         dist.init_process_group(backend, timeout=datetime.timedelta(minutes=10), **kw)
+        # one run directory for all ranks: rank 0's start time (the ranks parse
+        # their arguments at different moments, possibly in different seconds)
+        stamp = [args.run_timestamp]
+        dist.broadcast_object_list(stamp, src=0)
+        args.run_timestamp = stamp[0]
     sp_size = min(args.sp_size, world) if world > 1 else 1
     par = ParallelState.build(sp_size, args.rs_size)
     is_main = rank == 0
