@@ -23,8 +23,10 @@ Differences from the reference, on purpose:
   * residual math of the blocks follows the base model (x + gate*norm2(f(...)));
     HARP's block.py drops the MLP residual (block.py:44-49) - set
     `harp_block_compat=True` to reproduce that.
-  * samples in a batch must have the same token count (the reference ignores
-    attention masks in its ring attention too, attn.py:91-99).
+  * in the sequence-parallel wrapper, samples in a batch must have the same
+    image size and caption length (the reference ignores attention masks in
+    its ring attention too, attn.py:91-99); the base model's forward takes
+    mixed sizes.
   * under sequence parallelism every embedder and the final layer run on the
     tokens a rank holds (never replicated), so summing parameter gradients
     over all ranks is exact; the reference instead replicates them and keeps
@@ -418,7 +420,14 @@ class Z_Transformer(nn.Module):
 
     def forward_local(self, x: List[torch.Tensor], t, text_embedding: List[torch.Tensor], patch_size=2,
                       f_patch_size=1, metadata=None, cond_list=None, sp: Optional[SPContext] = None):
-        """Returns (pred [B, n_local_img, p*p*C], img_lo, img_hi)."""
+        """Returns (pred [B, n_local_img, p*p*C], img_lo, img_hi): this rank's
+        predictions for the real image tokens img_lo..img_hi-1.
+
+        As in the reference (hl_base.py:41-203, hl_model.py:114-330) the
+        caption, image and condition-image token runs are each padded to a
+        multiple of 32 (the last row repeated, then replaced by the learned pad
+        token after embedding, position id (0, 0, 0)), and the pad tokens are
+        part of the unified sequence that every layer attends over."""
         sp = sp or SPContext()
         zt = self.z_transformer
         B = len(x)
@@ -434,38 +443,41 @@ class Z_Transformer(nn.Module):
         grid = (F_ // f_patch_size, H // patch_size, W // patch_size)
         N, L = img.shape[1], cap.shape[1]
         img_ids, cap_ids = zt.positions(L, grid, dev)
+        img, img_ids, N_pad = _pad_run(img, img_ids)
         L_pad = cap_ids.shape[0]
         if L_pad != L:
             cap = torch.cat([cap, cap[:, -1:].expand(B, L_pad - L, cap.shape[2])], 1)
         adaln = c.to(torch.bfloat16 if img.dtype == torch.bfloat16 else img.dtype)
         xs = _local(img, sp)
         xs = zt.all_x_embedder[f"{patch_size}-{f_patch_size}"](xs)
-        lo_i, hi_i = _range(N, sp)
+        lo_i, hi_i = _range(N_pad, sp)
+        xs = _fill_pad(xs, lo_i, hi_i, N, N_pad, zt.x_pad_token)
         f_img = zt.rope_embedder(img_ids[lo_i:hi_i]).repeat(B, 1, 1)
         for layer in self.noise_refiner:
             xs = layer(xs, None, f_img, adaln, sp)
         caps = zt.cap_embedder(_local(cap, sp).to(xs.dtype))
         lo_c, hi_c = _range(L_pad, sp)
         f_cap = zt.rope_embedder(cap_ids[lo_c:hi_c]).repeat(B, 1, 1)
-        if L_pad != L:
-            padm = torch.arange(lo_c, hi_c, device=dev) >= L
-            caps = torch.where(padm[None, :, None], zt.cap_pad_token.to(caps.dtype), caps)
+        caps = _fill_pad(caps, lo_c, hi_c, L, L_pad, zt.cap_pad_token)
         for layer in self.context_refiner:
             caps = layer(caps, None, f_cap, None, sp)
-        streams = [(xs, N), (caps, L_pad)]
+        streams = [(xs, N_pad), (caps, L_pad)]
         ids = [img_ids, cap_ids]
         if self.use_cond and cond_list is not None:
             for j, cl in enumerate(cond_list):
                 ctoks = torch.stack([self._cond_tokens(cc, patch_size) for cc in cl])
                 Nc = ctoks.shape[1]
-                cids = _grid((1, H // patch_size, W // patch_size), (L_pad + 2 + j, 0, 0), dev).flatten(0, 2)
+                Hc, Wc = cl[0].shape[1:]
+                cids = _grid((1, Hc // patch_size, Wc // patch_size), (L_pad + 2 + j, 0, 0), dev).flatten(0, 2)
+                ctoks, cids, Nc_pad = _pad_run(ctoks, cids)
                 emb = getattr(self, f"cond_embedder_{j + 1}")
                 cs = emb(_local(ctoks.to(xs.dtype), sp))
-                lo_k, hi_k = _range(Nc, sp)
+                lo_k, hi_k = _range(Nc_pad, sp)
+                cs = _fill_pad(cs, lo_k, hi_k, Nc, Nc_pad, self.cond_pad_token)
                 f_c = zt.rope_embedder(cids[lo_k:hi_k]).repeat(B, 1, 1)
                 for layer in getattr(self, f"cond_refiner_{j + 1}"):
                     cs = layer(cs, None, f_c, adaln, sp)
-                streams.append((cs, Nc))
+                streams.append((cs, Nc_pad))
                 ids.append(cids)
         # unified sequence [img ; text ; cond...]: gather each stream, concatenate, take this rank's chunk
         full = [_gather_seq(s, sp) for s, _ in streams]
@@ -484,6 +496,30 @@ class Z_Transformer(nn.Module):
                 cond_list=None, sp: Optional[SPContext] = None):
         pred, lo, hi = self.forward_local(x, t, text_embedding, patch_size, f_patch_size, metadata, cond_list, sp)
         return (pred, lo, hi) if not return_dict else {"sample": pred, "range": (lo, hi)}
+
+
+def _pad_run(tok: torch.Tensor, ids: torch.Tensor):
+    """Pad a [B, n, d] token run to a multiple of SEQ_MULTI_OF by repeating its
+    last row, with position id (0, 0, 0) for the padding.  Returns (tokens,
+    ids, padded length)."""
+    n = tok.shape[1]
+    k = (-n) % SEQ_MULTI_OF
+    if k:
+        tok = torch.cat([tok, tok[:, -1:].expand(tok.shape[0], k, tok.shape[2])], 1)
+        ids = torch.cat([ids, ids.new_zeros(k, ids.shape[1])], 0)
+    return tok, ids, n + k
+
+
+def _fill_pad(x: torch.Tensor, lo: int, hi: int, n_real: int, n_pad: int, pad_token: torch.Tensor) -> torch.Tensor:
+    """Replace the rows of positions >= n_real in the chunk lo..hi-1 of an
+    embedded run (padded length n_pad) by the learned pad token.  Whenever the
+    run has padding every rank uses the pad token, even with no pad row in its
+    chunk (a zero gradient), so its gradient is reported on all ranks at the
+    same point of the backward."""
+    if n_real == n_pad:
+        return x
+    padm = torch.arange(lo, hi, device=x.device) >= n_real
+    return torch.where(padm[None, :, None], pad_token.to(x.dtype), x)
 
 
 def _range(n: int, sp: SPContext) -> Tuple[int, int]:

@@ -278,13 +278,17 @@ def _zimage_model():
     return model.bfloat16()
 
 
-def _zimage_batch():
+def _zimage_batch(padded=False):
+    """padded: an 18 x 18 latent (81 image tokens, padded to 96), a 20-token
+    caption (padded to 32) and an 18 x 18 condition image, so pad tokens sit in
+    the last rank's chunk of every run."""
     g = torch.Generator().manual_seed(8)
-    return {"lat": torch.randn(2, 16, 16, 16, generator=g).bfloat16(),
-            "noise": torch.randn(2, 16, 16, 16, generator=g).bfloat16(),
-            "text": torch.randn(2, 32, 64, generator=g).bfloat16(), "sig": torch.rand(2, generator=g),
+    hw, L = (18, 20) if padded else (16, 32)
+    return {"lat": torch.randn(2, 16, hw, hw, generator=g).bfloat16(),
+            "noise": torch.randn(2, 16, hw, hw, generator=g).bfloat16(),
+            "text": torch.randn(2, L, 64, generator=g).bfloat16(), "sig": torch.rand(2, generator=g),
             "meta": torch.rand(2, 2, generator=g).bfloat16(),
-            "cond": [torch.randn(2, 192, 16, 16, generator=g).bfloat16()]}
+            "cond": [torch.randn(2, 192, hw, hw, generator=g).bfloat16()]}
 
 
 def zimage_sp(rank, world, out, args):
@@ -295,7 +299,7 @@ def zimage_sp(rank, world, out, args):
     from harp_b200.parallel.sequence import SPContext
 
     model = _zimage_model()
-    b = _zimage_batch()
+    b = _zimage_batch(args.get("padded", False))
     sp = SPContext.from_group(dist.group.WORLD, backend="torch", mode=args.get("mode", "ring"))
     loss = Z.zimage_loss_local(model, b["lat"], b["noise"], b["text"], b["sig"], sp, metadata=b["meta"],
                                cond=b["cond"])

@@ -222,24 +222,26 @@ def test_sharded_weight_layout_two_ranks(tmp_path):
         assert res[r]["buckets"] == res[r]["n_groups"] + 1 and res[r]["rest"] == res[r]["n_groups"], res[r]
 
 
-def test_zimage_two_ranks_match_one():
+@pytest.mark.parametrize("padded", [False, True])
+def test_zimage_two_ranks_match_one(padded):
     """The Z-Image SP wrapper over two gloo ranks: the ranks' loss shares and
     gradients sum to the one-process loss and gradients (the reference never
-    checks its SP model against a single-rank run)."""
+    checks its SP model against a single-rank run); also with image, caption
+    and condition runs that need pad tokens."""
     import tempfile
 
     from harp_b200.models import zimage as Z
     from harp_b200.parallel.sequence import SPContext
 
     model = W._zimage_model()
-    b = W._zimage_batch()
+    b = W._zimage_batch(padded)
     loss = Z.zimage_loss_local(model, b["lat"], b["noise"], b["text"], b["sig"], SPContext(), metadata=b["meta"],
                                cond=b["cond"])
     loss.backward()
     ref_g = torch.cat([(p.grad if p.grad is not None else torch.zeros_like(p)).float().reshape(-1)
                        for p in model.parameters()])
     with tempfile.TemporaryDirectory() as d:
-        res, _ = _run("zimage_sp", 2, d)
+        res, _ = _run("zimage_sp", 2, d, {"padded": padded})
     tot = res[0]["loss"] + res[1]["loss"]
     assert tot == pytest.approx(float(loss), rel=2e-2), (tot, float(loss))
     g = res[0]["grads"] + res[1]["grads"]

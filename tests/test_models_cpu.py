@@ -402,10 +402,12 @@ def test_ulysses_dkv_push_addresses_match_the_remap():
                             assert kern % 16 == 0
 
 
-def test_zimage_sp_wrapper_matches_base_model():
+@pytest.mark.parametrize("hw,L", [(16, 32), (18, 20)])
+def test_zimage_sp_wrapper_matches_base_model(hw, L):
     """The reference never compares its SP wrapper with the base model; here the
     wrapper's forward (one rank, no condition branch or metadata) gives the base
-    ZImageTransformer2DModel's prediction on the same weights."""
+    ZImageTransformer2DModel's prediction on the same weights, also when the
+    image and caption runs need pad tokens (18 x 18: 81 image tokens)."""
     import copy
 
     torch.manual_seed(0)
@@ -417,13 +419,13 @@ def test_zimage_sp_wrapper_matches_base_model():
     base = base.bfloat16()
     ref_base = copy.deepcopy(base)
     model = Z.Z_Transformer(base, num_metadata=0, use_cond=False)
-    x = [torch.randn(16, 1, 16, 16).bfloat16() for _ in range(2)]
+    x = [torch.randn(16, 1, hw, hw).bfloat16() for _ in range(2)]
     t = torch.rand(2)
-    caps = [torch.randn(32, pre["cap_feat_dim"]).bfloat16() for _ in range(2)]
+    caps = [torch.randn(L, pre["cap_feat_dim"]).bfloat16() for _ in range(2)]
     with torch.no_grad():
         want = ref_base(x, t, caps)["sample"]
         pred, lo, hi = model.forward_local(x, t, caps, sp=SPContext())
-    assert (lo, hi) == (0, 64)
+    assert (lo, hi) == (0, (hw // 2) ** 2)
     want_tok = torch.stack(ref_base.patchify([w.float() for w in want], 2, 1)[0])
     torch.testing.assert_close(pred.float(), want_tok, rtol=0, atol=0)
 
