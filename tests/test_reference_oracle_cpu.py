@@ -234,3 +234,165 @@ def test_zimage_matches_the_reference_models_own_forward_and_backward():
         g = theirs[n].grad
         err = ((p.grad.float() - g).abs().max() / g.abs().max().clamp_min(1e-12)).item()
         assert err < 5e-2, (n, err)
+
+
+@pytest.mark.parametrize("with_cond", [False, True])
+def test_legacy_token_layout(with_cond):
+    """src/models/z_image/base.py (the legacy model's Z_Mixin) against
+    harp_b200.models.zimage_legacy.Z_Mixin: padded token runs, position ids and
+    pad masks of captions, images and condition images, and unpatchify."""
+    from harp_b200.models.zimage_legacy import Z_Mixin
+
+    R = _load("src/models/z_image/base.py")
+    ref, ours = R.Z_Mixin(), Z_Mixin()
+    torch.manual_seed(0)
+    imgs = [torch.randn(16, 1, 18, 18), torch.randn(16, 2, 16, 12)]
+    caps = [torch.randn(20, 8), torch.randn(32, 8)]
+    conds = [torch.randn(12, 18, 18), torch.randn(12, 16, 12)] if with_cond else None
+    a = ref.patchify_and_embed(imgs, caps, 2, 1, conds)
+    b = ours.patchify_and_embed(imgs, caps, 2, 1, conds)
+    for part_a, part_b in zip(a[:7], b[:7]):
+        assert len(part_a) == len(part_b)
+        for u, v in zip(part_a, part_b):
+            if isinstance(u, torch.Tensor):
+                torch.testing.assert_close(v, u, rtol=0, atol=0)
+            else:
+                assert tuple(u) == tuple(v)
+    if with_cond:
+        for part_a, part_b in zip(a[7], b[7]):
+            for u, v in zip(part_a, part_b):
+                torch.testing.assert_close(v, u, rtol=0, atol=0)
+    else:
+        assert a[7] is None and b[7] is None
+    toks = [torch.randn(t.shape[0], 2 * 2 * 1 * 16) for t in a[0]]
+    want = ref.unpatchify([t.clone() for t in toks], a[2], 2, 1, 16)
+    got = ours.unpatchify([t.clone() for t in toks], b[2], 2, 1, 16)
+    for u, v in zip(want, got):
+        torch.testing.assert_close(v, u, rtol=0, atol=0)
+
+
+def _cli_flags(path):
+    """{flag: {type, default, action, choices}} of every literal add_argument
+    call in a script, read from its syntax tree (the script is not run)."""
+    import ast
+
+    flags = {}
+    for node in ast.walk(ast.parse(open(path).read())):
+        if isinstance(node, ast.Call) and getattr(node.func, "attr", None) == "add_argument":
+            names = [a.value for a in node.args if isinstance(a, ast.Constant)]
+            if not names:
+                continue
+            kw = {}
+            for k in node.keywords:
+                if k.arg in ("type", "default", "action", "choices"):
+                    v = k.value
+                    kw[k.arg] = ast.literal_eval(v) if isinstance(v, (ast.Constant, ast.List)) else ast.unparse(v)
+            flags[names[0]] = kw
+    return flags
+
+
+def test_train_cli_accepts_every_reference_flag():
+    """train.py (the reference's, read as text) against harp's train.py: every
+    reference flag parses, with the reference's type, default and choices."""
+    import sys
+
+    here = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    ref_flags = _cli_flags(os.path.join(REF, "train.py"))
+    assert len(ref_flags) >= 25
+    sys.path.insert(0, here)
+    try:
+        import train as T
+    finally:
+        sys.path.remove(here)
+    args = vars(T.parse_args([]))
+    types = {"str": str, "int": int, "float": float, "bool": bool}
+    for flag, kw in ref_flags.items():
+        dest = flag.lstrip("-").replace("-", "_")
+        assert dest in args, flag
+        if "default" in kw:
+            assert args[dest] == kw["default"], (flag, args[dest], kw["default"])
+        elif kw.get("action") == "store_true":
+            assert args[dest] is False, flag
+        if kw.get("type") in types and args[dest] is not None:
+            assert isinstance(args[dest], types[kw["type"]]), flag
+        if "choices" in kw:
+            for c in kw["choices"]:
+                assert vars(T.parse_args([flag, c]))[dest] == c, (flag, c)
+
+
+class _FakeAccelerator:
+    is_main_process = True
+
+    @staticmethod
+    def unwrap_model(m):
+        return m
+
+
+class _LoraModel(torch.nn.Module):
+    def __init__(self):
+        super().__init__()
+        self.base = torch.nn.Linear(4, 3)
+        self.lora_A = torch.nn.Linear(4, 2, bias=False)
+        self.frozen = torch.nn.Linear(3, 3)
+        self.frozen.requires_grad_(False)
+        self.saved = []
+
+    def save_lora_adapter(self, save_directory, adapter_name):
+        self.saved.append((os.path.basename(save_directory), adapter_name))
+
+
+def test_checkpoint_hooks_and_helpers(tmp_path):
+    """src/utils/hook.py and src/utils/utils.py: the accelerate save hooks write
+    the same model.safetensors (trainable, non-LoRA tensors) and call the same
+    adapter saves; preserve_requires_grad restores the flags; encode_images
+    applies the VAE's shift and scale."""
+    from safetensors.torch import load_file
+
+    from harp_b200.utils import misc as M
+
+    H = _load("src/utils/hook.py")
+    U = _load("src/utils/utils.py")
+    torch.manual_seed(0)
+    model = _LoraModel()
+    for hook_ref, hook_ours, extra in ((H.save_trainable_param_hook, M.save_trainable_param_hook, {}),
+                                       (H.save_lora_adapter_hook, M.save_lora_adapter_hook,
+                                        {"target_adapters": ["a", "b"]})):
+        outs = []
+        for i, hook in enumerate((hook_ref, hook_ours)):
+            d = tmp_path / f"{hook.__name__}{i}"
+            d.mkdir()
+            weights = [object()]
+            model.saved = []
+            hook([model], weights, str(d), _FakeAccelerator(), **extra)
+            assert weights == []
+            outs.append((load_file(str(d / "model.safetensors")), list(model.saved)))
+        (sa, la), (sb, lb) = outs
+        assert sorted(sa) == sorted(sb) == ["base.bias", "base.weight"]
+        for k in sa:
+            assert torch.equal(sa[k], sb[k])
+        assert la == lb
+    for ctx in (U.preserve_requires_grad, M.preserve_requires_grad):
+        with ctx(model):
+            model.requires_grad_(False)
+            model.frozen.requires_grad_(True)
+        assert model.base.weight.requires_grad and not model.frozen.weight.requires_grad
+
+    class _Dist:
+        def __init__(self, z):
+            self.z = z
+
+        def sample(self):
+            return self.z
+
+    class _VAE:
+        dtype = torch.float32
+
+        class config:
+            shift_factor, scaling_factor = 0.1159, 0.3611
+
+        def encode(self, x):
+            return type("Out", (), {"latent_dist": _Dist(x * 2.0)})()
+
+    px = torch.randn(2, 3, 8, 8)
+    torch.testing.assert_close(M.encode_images(_VAE(), px, torch.bfloat16),
+                               U.encode_images(_VAE(), px, torch.bfloat16), rtol=0, atol=0)
