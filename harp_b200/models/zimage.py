@@ -38,13 +38,12 @@ import copy
 import json
 import math
 import os
-from typing import Dict, List, Optional, Sequence, Tuple
+from typing import Dict, List, Optional, Tuple
 
 import torch
 import torch.nn as nn
 
-from ..ops import functional as Fn
-from ..ops.modules import (LinearFunction, MySiLU, MyTanh, QKNormRopeFunction, kpLinear, kpRMSNorm, sp_attention)
+from ..ops.modules import MySiLU, MyTanh, QKNormRopeFunction, kpLinear, kpRMSNorm, sp_attention
 from ..parallel.sequence import SPContext
 
 ADALN_EMBED_DIM = 256
@@ -226,6 +225,151 @@ def _grid(size, start, device):
     return torch.stack(torch.meshgrid(axes, indexing="ij"), -1)
 
 
+def _pad_len(n: int) -> int:
+    return (-n) % SEQ_MULTI_OF
+
+
+class Z_Mixin:
+    """Token layout of the legacy model (base.py:7-203): per sample, padded
+    caption and image token runs, their position ids and pad masks, and one
+    optional condition image."""
+
+    @staticmethod
+    def create_coordinate_grid(size, start=None, device=None) -> torch.Tensor:
+        """int32 [*size, len(size)] grid of coordinates start[a] .. start[a] + size[a] - 1."""
+        start = tuple(start) if start is not None else (0,) * len(size)
+        axes = [torch.arange(s0, s0 + n, dtype=torch.int32, device=device) for s0, n in zip(start, size)]
+        return torch.stack(torch.meshgrid(axes, indexing="ij"), -1)
+
+    def unpatchify(self, x: List[torch.Tensor], size: List[Tuple], patch_size, f_patch_size,
+                   out_channels) -> List[torch.Tensor]:
+        """Token rows (padding at the end ignored) back to [C, F, H, W] per sample."""
+        p, pf = patch_size, f_patch_size
+        out = []
+        for xi, (F_, H, W) in zip(x, size):
+            n = (F_ // pf) * (H // p) * (W // p)
+            out.append(xi[:n].view(F_ // pf, H // p, W // p, pf, p, p, out_channels)
+                       .permute(6, 0, 3, 1, 4, 2, 5).reshape(out_channels, F_, H, W))
+        return out
+
+    def _pad_run(self, tokens: torch.Tensor, ids: torch.Tensor):
+        """Pad a token run to a multiple of 32 by repeating its last row; pad
+        ids are (0, 0, 0).  Returns (tokens, pad_mask, ids)."""
+        n = tokens.shape[0]
+        k = _pad_len(n)
+        dev = tokens.device
+        mask = torch.zeros(n + k, dtype=torch.bool, device=dev)
+        if k:
+            mask[n:] = True
+            tokens = torch.cat([tokens, tokens[-1:].expand(k, tokens.shape[1])], 0)
+            ids = torch.cat([ids, torch.zeros(k, ids.shape[1], dtype=ids.dtype, device=dev)], 0)
+        return tokens, mask, ids
+
+    def cond_patchify_and_embed(self, cond: torch.Tensor, patch_size: int, start: int, device):
+        """cond [C, H, W] -> (tokens [(n+pad), p*p*C], pad_mask, ids) with ids on
+        the plane (start, h, w)."""
+        p = patch_size
+        C, H, W = cond.shape
+        toks = cond.view(C, H // p, p, W // p, p).permute(1, 3, 2, 4, 0).reshape((H // p) * (W // p), p * p * C)
+        ids = self.create_coordinate_grid((1, H // p, W // p), (start, 0, 0), device).flatten(0, 2)
+        return self._pad_run(toks, ids)
+
+    def patchify_and_embed(self, all_image: List[torch.Tensor], all_cap_feats: List[torch.Tensor], patch_size: int,
+                           f_patch_size: int, cond_list: Optional[List[torch.Tensor]]):
+        """Per sample: padded caption and image token runs with their position
+        ids and pad masks (base.py:85-203).  Returns (images, captions,
+        image_sizes, image_ids, caption_ids, image_pad_masks, caption_pad_masks,
+        cond_out) where cond_out is None or (tokens, pad_masks, ids) lists."""
+        p, pf = patch_size, f_patch_size
+        dev = all_image[0].device
+        imgs, caps, sizes, img_ids, cap_ids, img_masks, cap_masks = [], [], [], [], [], [], []
+        cond_out = ([], [], []) if cond_list is not None else None
+        for i, (image, cap) in enumerate(zip(all_image, all_cap_feats)):
+            L = cap.shape[0]
+            Lp = L + _pad_len(L)
+            c_ids = self.create_coordinate_grid((Lp, 1, 1), (1, 0, 0), dev).flatten(0, 2)
+            c_tok = torch.cat([cap, cap[-1:].expand(Lp - L, cap.shape[1])], 0) if Lp > L else cap
+            c_mask = torch.arange(Lp, device=dev) >= L
+            caps.append(c_tok), cap_ids.append(c_ids), cap_masks.append(c_mask)
+            C, F_, H, W = image.shape
+            sizes.append((F_, H, W))
+            t = image.view(C, F_ // pf, pf, H // p, p, W // p, p).permute(1, 3, 5, 2, 4, 6, 0)
+            toks = t.reshape((F_ // pf) * (H // p) * (W // p), pf * p * p * C)
+            ids = self.create_coordinate_grid((F_ // pf, H // p, W // p), (Lp + 1, 0, 0), dev).flatten(0, 2)
+            toks, mask, ids = self._pad_run(toks, ids)
+            imgs.append(toks), img_ids.append(ids), img_masks.append(mask)
+            if cond_out is not None:
+                ct, cm, ci = self.cond_patchify_and_embed(cond_list[i], p, Lp + 2, dev)
+                cond_out[0].append(ct), cond_out[1].append(cm), cond_out[2].append(ci)
+        return imgs, caps, sizes, img_ids, cap_ids, img_masks, cap_masks, cond_out
+
+
+class Z_HLMixin(Z_Mixin):
+    """Token layout of the sequence-parallel model (hl_base.py:7-212): as
+    Z_Mixin, but cond_list holds one list of per-sample condition images per
+    condition branch, and branch j's ids sit on the plane padded caption
+    length + 2 + j.  The condition runs come back as a dict {"c_p", "c_p_m",
+    "c_p_p_id"} of per-branch lists (tokens, pad masks, ids), with at least
+    two branches as in the reference."""
+
+    def patchify_and_embed(self, all_image: List[torch.Tensor], all_cap_feats: List[torch.Tensor], patch_size: int,
+                           f_patch_size: int, cond_list: Optional[List[List[torch.Tensor]]]):
+        out = Z_Mixin.patchify_and_embed(self, all_image, all_cap_feats, patch_size, f_patch_size, None)
+        if cond_list is None:
+            return out
+        dev = all_image[0].device
+        nb = max(2, len(cond_list))
+        cond = {"c_p": [[] for _ in range(nb)], "c_p_m": [[] for _ in range(nb)], "c_p_p_id": [[] for _ in range(nb)]}
+        for i, cap in enumerate(all_cap_feats):
+            base = cap.shape[0] + _pad_len(cap.shape[0]) + 2
+            for j, branch in enumerate(cond_list):
+                tok, mask, ids = self.cond_patchify_and_embed(branch[i], patch_size, base + j, dev)
+                cond["c_p"][j].append(tok), cond["c_p_m"][j].append(mask), cond["c_p_p_id"][j].append(ids)
+        return out[:7] + (cond,)
+
+
+class Z_LoraBranches:
+    """Parameter-group helpers shared by both wrappers (hl_model.py:339-394,
+    model.py:284-336): meta-embedding grad switch and the LoRA target names of
+    each branch."""
+
+    def switch_meta_embedding_grad(self, grad_stat: bool = True) -> int:
+        n = 0
+        if self.meta_embeddings is not None:
+            for p in self.meta_embeddings.parameters():
+                p.requires_grad_(grad_stat)
+                n += p.numel()
+        return n
+
+    def get_branch_lora_modules(self, branch_name: str) -> List[str]:
+        """Names of the LoRA target linears of every block of a branch.  The
+        names resolve in this module tree (attention.attn.*); the reference
+        lists attention.* and stops after the first block."""
+        names: List[str] = []
+        for i, block in enumerate(getattr(self, branch_name)):
+            pre = f"{branch_name}.{i}"
+            names += [f"{pre}.attention.attn.to_q", f"{pre}.attention.attn.to_k", f"{pre}.attention.attn.to_v",
+                      f"{pre}.attention.attn.to_out.0", f"{pre}.z_block.feed_forward.w1",
+                      f"{pre}.z_block.feed_forward.w2", f"{pre}.z_block.feed_forward.w3"]
+            if block.z_block.modulation:
+                names.append(f"{pre}.z_block.adaLN_modulation.0")
+        return names
+
+    def get_noise_lora_branch(self, patch_size: int = 2, f_patch_size: int = 1) -> List[str]:
+        key = f"{patch_size}-{f_patch_size}"
+        return self.get_branch_lora_modules("noise_refiner") + [
+            f"z_transformer.all_x_embedder.{key}", f"z_transformer.all_final_layer.{key}.linear",
+            f"z_transformer.all_final_layer.{key}.adaLN_modulation.1"]
+
+    def get_context_lora_branch(self) -> List[str]:
+        return ["z_transformer.cap_embedder.1"] + self.get_branch_lora_modules("context_refiner")
+
+    def get_main_lora_branch(self) -> List[str]:
+        return self.get_branch_lora_modules("layers") + ["z_transformer.t_embedder.mlp.0",
+                                                         "z_transformer.t_embedder.mlp.2"]
+
+
+
 class ZImageTransformer2DModel(nn.Module, ConfigMixin):
     def __init__(self, all_patch_size=(2,), all_f_patch_size=(1,), in_channels=16, dim=3840, n_layers=30,
                  n_refiner_layers=2, n_heads=30, n_kv_heads=30, norm_eps=1e-5, qk_norm=True, cap_feat_dim=2560,
@@ -294,8 +438,6 @@ class ZImageTransformer2DModel(nn.Module, ConfigMixin):
         Here samples with the same image size and caption length run together
         as one dense batch instead, so no mask is needed and the attention
         sees real rows only: the same result for every real token."""
-        from .zimage_legacy import Z_Mixin  # that module imports this one
-
         sp = sp or SPContext()
         key = f"{patch_size}-{f_patch_size}"
         c = self.t_embedder(t * self.t_scale)
@@ -374,7 +516,7 @@ class Z_JointBlock(Z_SingleBlock):
                             compat="joint" if self.compat else False)
 
 
-class Z_Transformer(nn.Module):
+class Z_Transformer(nn.Module, Z_HLMixin, Z_LoraBranches):
     """Sequence-parallel Z-Image with HARP's condition-image branch and metadata
     embedders (hl_model.py:37-109).  forward() takes the reference's arguments
     and returns the prediction for the image tokens this rank holds, plus the
@@ -412,6 +554,19 @@ class Z_Transformer(nn.Module):
     @property
     def config(self):
         return self.z_transformer.config
+
+    def switch_cond_branch_grad(self, grad_stat: bool = True) -> int:
+        """requires_grad of both condition branches (embedders and refiners);
+        returns the number of parameters switched (0 without the branches)."""
+        n = 0
+        for j in (1, 2):
+            for name in (f"cond_embedder_{j}", f"cond_refiner_{j}"):
+                mod = getattr(self, name, None)
+                if mod is not None:
+                    for p in mod.parameters():
+                        p.requires_grad_(grad_stat)
+                        n += p.numel()
+        return n
 
     def _cond_tokens(self, cond: torch.Tensor, patch_size: int):
         C, H, W = cond.shape

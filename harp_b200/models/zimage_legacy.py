@@ -26,94 +26,17 @@ state-dict keys as the diffusers class; diffusers is not needed).
 from __future__ import annotations
 
 import copy
-from typing import Dict, List, Optional, Tuple
+from typing import Dict, List, Optional
 
 import torch
 import torch.nn as nn
 
 from ..parallel.sequence import SPContext
-from .zimage import (ADALN_EMBED_DIM, SEQ_MULTI_OF, Linear, TimestepEmbedder, Z_JointBlock, Z_SingleBlock,
-                     ZImageTransformer2DModel)
+from .zimage import (ADALN_EMBED_DIM, Linear, TimestepEmbedder, Z_JointBlock, Z_LoraBranches, Z_Mixin,
+                     Z_SingleBlock, ZImageTransformer2DModel)
 
 
-def _pad_len(n: int) -> int:
-    return (-n) % SEQ_MULTI_OF
-
-
-class Z_Mixin:
-    """Token layout helpers (base.py:7-203)."""
-
-    @staticmethod
-    def create_coordinate_grid(size, start=None, device=None) -> torch.Tensor:
-        """int32 [*size, len(size)] grid of coordinates start[a] .. start[a] + size[a] - 1."""
-        start = tuple(start) if start is not None else (0,) * len(size)
-        axes = [torch.arange(s0, s0 + n, dtype=torch.int32, device=device) for s0, n in zip(start, size)]
-        return torch.stack(torch.meshgrid(axes, indexing="ij"), -1)
-
-    def unpatchify(self, x: List[torch.Tensor], size: List[Tuple], patch_size, f_patch_size,
-                   out_channels) -> List[torch.Tensor]:
-        """Token rows (padding at the end ignored) back to [C, F, H, W] per sample."""
-        p, pf = patch_size, f_patch_size
-        out = []
-        for xi, (F_, H, W) in zip(x, size):
-            n = (F_ // pf) * (H // p) * (W // p)
-            out.append(xi[:n].view(F_ // pf, H // p, W // p, pf, p, p, out_channels)
-                       .permute(6, 0, 3, 1, 4, 2, 5).reshape(out_channels, F_, H, W))
-        return out
-
-    def _pad_run(self, tokens: torch.Tensor, ids: torch.Tensor):
-        """Pad a token run to a multiple of 32 by repeating its last row; pad
-        ids are (0, 0, 0).  Returns (tokens, pad_mask, ids)."""
-        n = tokens.shape[0]
-        k = _pad_len(n)
-        dev = tokens.device
-        mask = torch.zeros(n + k, dtype=torch.bool, device=dev)
-        if k:
-            mask[n:] = True
-            tokens = torch.cat([tokens, tokens[-1:].expand(k, tokens.shape[1])], 0)
-            ids = torch.cat([ids, torch.zeros(k, ids.shape[1], dtype=ids.dtype, device=dev)], 0)
-        return tokens, mask, ids
-
-    def cond_patchify_and_embed(self, cond: torch.Tensor, patch_size: int, start: int, device):
-        """cond [C, H, W] -> (tokens [(n+pad), p*p*C], pad_mask, ids) with ids on
-        the plane (start, h, w)."""
-        p = patch_size
-        C, H, W = cond.shape
-        toks = cond.view(C, H // p, p, W // p, p).permute(1, 3, 2, 4, 0).reshape((H // p) * (W // p), p * p * C)
-        ids = self.create_coordinate_grid((1, H // p, W // p), (start, 0, 0), device).flatten(0, 2)
-        return self._pad_run(toks, ids)
-
-    def patchify_and_embed(self, all_image: List[torch.Tensor], all_cap_feats: List[torch.Tensor], patch_size: int,
-                           f_patch_size: int, cond_list: Optional[List[torch.Tensor]]):
-        """Per sample: padded caption and image token runs with their position
-        ids and pad masks (base.py:85-203).  Returns (images, captions,
-        image_sizes, image_ids, caption_ids, image_pad_masks, caption_pad_masks,
-        cond_out) where cond_out is None or (tokens, pad_masks, ids) lists."""
-        p, pf = patch_size, f_patch_size
-        dev = all_image[0].device
-        imgs, caps, sizes, img_ids, cap_ids, img_masks, cap_masks = [], [], [], [], [], [], []
-        cond_out = ([], [], []) if cond_list is not None else None
-        for i, (image, cap) in enumerate(zip(all_image, all_cap_feats)):
-            L = cap.shape[0]
-            Lp = L + _pad_len(L)
-            c_ids = self.create_coordinate_grid((Lp, 1, 1), (1, 0, 0), dev).flatten(0, 2)
-            c_tok = torch.cat([cap, cap[-1:].expand(Lp - L, cap.shape[1])], 0) if Lp > L else cap
-            c_mask = torch.arange(Lp, device=dev) >= L
-            caps.append(c_tok), cap_ids.append(c_ids), cap_masks.append(c_mask)
-            C, F_, H, W = image.shape
-            sizes.append((F_, H, W))
-            t = image.view(C, F_ // pf, pf, H // p, p, W // p, p).permute(1, 3, 5, 2, 4, 6, 0)
-            toks = t.reshape((F_ // pf) * (H // p) * (W // p), pf * p * p * C)
-            ids = self.create_coordinate_grid((F_ // pf, H // p, W // p), (Lp + 1, 0, 0), dev).flatten(0, 2)
-            toks, mask, ids = self._pad_run(toks, ids)
-            imgs.append(toks), img_ids.append(ids), img_masks.append(mask)
-            if cond_out is not None:
-                ct, cm, ci = self.cond_patchify_and_embed(cond_list[i], p, Lp + 2, dev)
-                cond_out[0].append(ct), cond_out[1].append(cm), cond_out[2].append(ci)
-        return imgs, caps, sizes, img_ids, cap_ids, img_masks, cap_masks, cond_out
-
-
-class Z_Transformer(nn.Module, Z_Mixin):
+class Z_Transformer(nn.Module, Z_Mixin, Z_LoraBranches):
     """Legacy (non-SP) Z-Image wrapper: noise/context/condition refiners and the
     joint layers over variable-size samples (model.py:20-349).
 
@@ -216,42 +139,7 @@ class Z_Transformer(nn.Module, Z_Mixin):
         res = self.unpatchify(out, sizes, patch_size, f_patch_size, self.out_channels)
         return {"sample": res} if return_dict else (res,)
 
-    # -- parameter-group helpers (model.py:284-349) ------------------------------
-    def switch_meta_embedding_grad(self, grad_stat: bool = True) -> int:
-        n = 0
-        if self.meta_embeddings is not None:
-            for p in self.meta_embeddings.parameters():
-                p.requires_grad_(grad_stat)
-                n += p.numel()
-        return n
-
-    def get_branch_lora_modules(self, branch_name: str) -> List[str]:
-        """Names of the LoRA target linears of every block of a branch.  The
-        names resolve in this module tree (attention.attn.*); the reference
-        lists attention.* and stops after the first block."""
-        names: List[str] = []
-        for i, block in enumerate(getattr(self, branch_name)):
-            pre = f"{branch_name}.{i}"
-            names += [f"{pre}.attention.attn.to_q", f"{pre}.attention.attn.to_k", f"{pre}.attention.attn.to_v",
-                      f"{pre}.attention.attn.to_out.0", f"{pre}.z_block.feed_forward.w1",
-                      f"{pre}.z_block.feed_forward.w2", f"{pre}.z_block.feed_forward.w3"]
-            if block.z_block.modulation:
-                names.append(f"{pre}.z_block.adaLN_modulation.0")
-        return names
-
-    def get_noise_lora_branch(self, patch_size: int = 2, f_patch_size: int = 1) -> List[str]:
-        key = f"{patch_size}-{f_patch_size}"
-        return self.get_branch_lora_modules("noise_refiner") + [
-            f"z_transformer.all_x_embedder.{key}", f"z_transformer.all_final_layer.{key}.linear",
-            f"z_transformer.all_final_layer.{key}.adaLN_modulation.1"]
-
-    def get_context_lora_branch(self) -> List[str]:
-        return ["z_transformer.cap_embedder.1"] + self.get_branch_lora_modules("context_refiner")
-
-    def get_main_lora_branch(self) -> List[str]:
-        return self.get_branch_lora_modules("layers") + ["z_transformer.t_embedder.mlp.0",
-                                                         "z_transformer.t_embedder.mlp.2"]
-
+    # -- parameter-group helpers (model.py:284-349; the others in Z_LoraBranches) --
     def switch_cond_branch_grad(self, grad_stat: bool = True) -> int:
         n = 0
         if self.cond_embedder is not None:

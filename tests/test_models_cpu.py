@@ -532,3 +532,21 @@ def test_zimage_variable_sizes_and_caption_lengths():
     sum(o.float().pow(2).mean() for o in out).backward()
     assert model.x_pad_token.grad.abs().max() > 0 and model.cap_pad_token.grad.abs().max() > 0
 
+
+
+def test_zimage_sp_wrapper_parameter_groups():
+    """The SP wrapper's parameter-group helpers (hl_model.py:339-394): every
+    LoRA target name resolves to a Linear of the module tree, and the grad
+    switches return the number of parameters they set."""
+    model = Z.Z_Transformer(Z.ZImageTransformer2DModel(**Z.PRESETS["zimage-tiny"]), num_metadata=2, use_cond=True)
+    mods = dict(model.named_modules())
+    names = model.get_noise_lora_branch() + model.get_context_lora_branch() + model.get_main_lora_branch()
+    assert len(names) == len(set(names)) > 10
+    for n in names:
+        assert hasattr(mods[n], "weight"), n
+    n_meta = sum(p.numel() for p in model.meta_embeddings.parameters())
+    assert model.switch_meta_embedding_grad(False) == n_meta
+    assert not any(p.requires_grad for p in model.meta_embeddings.parameters())
+    n_cond = sum(p.numel() for n, p in model.named_parameters() if n.startswith(("cond_embedder_", "cond_refiner_")))
+    assert model.switch_cond_branch_grad(False) == n_cond > 0
+    assert model.switch_cond_branch_grad(True) == n_cond

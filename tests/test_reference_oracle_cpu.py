@@ -396,3 +396,35 @@ def test_checkpoint_hooks_and_helpers(tmp_path):
     px = torch.randn(2, 3, 8, 8)
     torch.testing.assert_close(M.encode_images(_VAE(), px, torch.bfloat16),
                                U.encode_images(_VAE(), px, torch.bfloat16), rtol=0, atol=0)
+
+
+@pytest.mark.parametrize("branches", [0, 1, 2])
+def test_sp_token_layout(branches):
+    """src/models/z_image/hl_base.py (the SP model's Z_Mixin: one list of
+    condition images per branch, branch j on the plane caption + 2 + j)
+    against harp's Z_HLMixin, which the SP Z_Transformer inherits."""
+    from harp_b200.models.zimage import Z_HLMixin
+
+    R = _load("src/models/z_image/hl_base.py")
+    ref, ours = R.Z_Mixin(), Z_HLMixin()
+    torch.manual_seed(0)
+    imgs = [torch.randn(16, 1, 18, 18), torch.randn(16, 1, 16, 12)]
+    caps = [torch.randn(20, 8), torch.randn(32, 8)]
+    conds = [[torch.randn(12, 18, 18), torch.randn(12, 16, 12)] for _ in range(branches)] or None
+    a = ref.patchify_and_embed(imgs, caps, 2, 1, conds)
+    b = ours.patchify_and_embed(imgs, caps, 2, 1, conds)
+    for part_a, part_b in zip(a[:7], b[:7]):
+        for u, v in zip(part_a, part_b):
+            if isinstance(u, torch.Tensor):
+                torch.testing.assert_close(v, u, rtol=0, atol=0)
+            else:
+                assert tuple(u) == tuple(v)
+    if conds is None:
+        assert a[7] is None and b[7] is None
+        return
+    assert sorted(a[7]) == sorted(b[7])
+    for key in a[7]:
+        assert [len(x) for x in a[7][key]] == [len(x) for x in b[7][key]]
+        for la, lb in zip(a[7][key], b[7][key]):
+            for u, v in zip(la, lb):
+                torch.testing.assert_close(v, u, rtol=0, atol=0)
