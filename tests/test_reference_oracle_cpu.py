@@ -428,3 +428,40 @@ def test_sp_token_layout(branches):
         for la, lb in zip(a[7][key], b[7][key]):
             for u, v in zip(la, lb):
                 torch.testing.assert_close(v, u, rtol=0, atol=0)
+
+
+def test_npz_dataset_and_collate(tmp_path):
+    """src/datatsets/TiffDataset.py (NpzDataset, custom_collate_fn) against
+    harp_b200.utils.data on .npz samples of the reference's format.  That file
+    uses json, numpy and torch without importing them; the test supplies the
+    three modules to it."""
+    import numpy as np
+
+    from harp_b200.utils import data as D
+
+    R = _load("src/datatsets/TiffDataset.py")
+    R.json, R.np, R.torch = json, np, torch
+    rng = np.random.default_rng(0)
+    files = []
+    for i, L in enumerate((20, 32, 7)):
+        f = tmp_path / f"s{i}.npz"
+        np.savez(f, norm_metadata=rng.random(4).astype(np.float32),
+                 prompt_embeds=rng.random((L, 16)).astype(np.float32),
+                 latent_image=rng.random((16, 8, 8)).astype(np.float32),
+                 cond=rng.random((12, 8, 8)).astype(np.float32))
+        files.append(str(f))
+    index = tmp_path / "index.json"
+    index.write_text(json.dumps(files))
+    a, b = R.NpzDataset(str(index)), D.NpzDataset(str(index))
+    assert len(a) == len(b) == 3
+    for i in range(3):
+        for k, v in a[i].items():
+            assert np.array_equal(v, b[i][k]), k
+    ca, cb = R.custom_collate_fn([a[i] for i in range(3)]), D.custom_collate_fn([b[i] for i in range(3)])
+    assert sorted(ca) == sorted(cb)
+    torch.testing.assert_close(ca["norm_metadata"], cb["norm_metadata"], rtol=0, atol=0)
+    torch.testing.assert_close(ca["latent_image"], cb["latent_image"], rtol=0, atol=0)
+    for u, v in zip(ca["prompt_embeds"], cb["prompt_embeds"]):
+        torch.testing.assert_close(u, v, rtol=0, atol=0)
+    assert len(ca["cond"]) == len(cb["cond"]) == 1
+    torch.testing.assert_close(ca["cond"][0], cb["cond"][0], rtol=0, atol=0)
