@@ -148,7 +148,10 @@ def build_balanced_param_groups(model, sp_size: int, local_rank: int, block_size
 def build_chunk_param(my_params, model, rs_size: int, rs_rank: int) -> List[torch.Tensor]:
     """Row-chunk each owned parameter over the RS group: the optimizer steps
     `p.chunk_part` (rows [chunk_begin, chunk_end)), whose `.grad` is a view of
-    `p.shared_grad`.  Parameters that do not split evenly stay whole."""
+    `p.shared_grad`.  Parameters that do not split evenly stay whole.
+    Membership in `my_params` is by identity (the reference's `p in my_params`
+    compares tensors by value, which raises once two parameters of different
+    shapes are compared)."""
     mine = {id(p) for p in my_params}
     out = []
     for name, p in model.named_parameters():

@@ -361,3 +361,101 @@ def ring_ops_sp(rank, world, out, args):
     o.backward(do[:, :, sl])
     ring_ops.set_sp_context(None)
     return {"o": o.detach().float(), "dq": ql.grad.float(), "dk": kl.grad.float(), "dv": vl.grad.float()}
+
+
+def _load_reference(ref_dir, rel):
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location("_reference_" + rel.replace("/", "_")[:-3],
+                                                  os.path.join(ref_dir, rel))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+class _IdentityList(list):
+    def __contains__(self, x):
+        return any(x is y for y in self)
+
+
+class _GlooAllGatherShape:
+    """torch.distributed, except that all_gather_into_tensor passes its output
+    to the backend as the inputs concatenated along dim 0 (the same memory as
+    the [world, *input] stacked form the reference allocates).  NCCL takes
+    either shape; gloo takes only the concatenated one."""
+
+    def __getattr__(self, name):
+        return getattr(dist, name)
+
+    @staticmethod
+    def all_gather_into_tensor(output, inp, group=None, async_op=False):
+        return dist.all_gather_into_tensor(output.view(-1, *inp.shape[1:]), inp, group=group, async_op=async_op)
+
+
+def managers_oracle(rank, world, out, args):
+    """The reference's managers/shard_manager.py and the pure-PyTorch parts of
+    managers/weight_manager.py, run beside harp's on the same inputs over the
+    gloo ranks: sequence scatter / all-gather / broadcast (forward and
+    backward), byte-balanced ownership, row chunks and the background
+    all-gather of updated chunks."""
+    from harp_b200.managers import shard_manager as HS
+    from harp_b200.managers import weight_manager as HW
+
+    RS = _load_reference(args["ref"], "managers/shard_manager.py")
+    RW = _load_reference(args["ref"], "managers/weight_manager.py")
+    RS.dist = _GlooAllGatherShape()
+    grp = dist.group.WORLD
+    res = {}
+    for B in (1, 3):
+        g = torch.Generator().manual_seed(11 + B)
+        full = torch.randn(B, 4 * world, 5, generator=g)
+        loc = torch.randn(B, 4, 5, generator=g) + rank
+        w_full = torch.randn(B, 4 * world, 5, generator=g)
+        w_loc = torch.randn(B, 4, 5, generator=g)
+        for tag, mod in (("ref", RS), ("ours", HS)):
+            x = full.clone().requires_grad_(True)
+            y = mod.SequenceScatter.apply(x, grp)
+            (y * w_loc * (rank + 1)).sum().backward()
+            res[f"scatter{B}_{tag}"] = (y.detach(), x.grad)
+            x = loc.clone().requires_grad_(True)
+            y = mod.SequenceAllGather.apply(x, grp)
+            (y * w_full).sum().backward()
+            res[f"gather{B}_{tag}"] = (y.detach(), x.grad)
+            x = loc.clone().requires_grad_(True)
+            (mod.SPBroadcast.apply(x, grp) * (rank + 2)).sum().backward()
+            res[f"bcast{B}_{tag}"] = x.grad
+
+    def make_model():
+        torch.manual_seed(5)
+        return torch.nn.Sequential(torch.nn.Linear(8, 16), torch.nn.LayerNorm(16), torch.nn.Linear(16, 8),
+                                   torch.nn.RMSNorm(8), torch.nn.Linear(8, 4))
+
+    for tag, mod in (("ref", RW), ("ours", HW)):
+        model = make_model()
+        params = list(model.parameters())
+        idx = {id(p): i for i, p in enumerate(params)}
+        mine, prank = mod.build_balanced_param_groups(model, world, rank, block_size=200)
+        res[f"owners_{tag}"] = [prank.get(id(p)) for p in params]
+        res[f"mine_{tag}"] = [idx[id(p)] for p in mine]
+        for p in params:
+            p.shared_grad = torch.arange(p.numel(), dtype=p.dtype).view(p.shape) + idx[id(p)]
+            p.state = torch.zeros((), dtype=torch.uint8)
+        # row chunks over an RS group of both ranks: its members optimize the
+        # same parameters (an owner's), here all of them.  The reference tests
+        # `p in my_params`, which compares tensors by value and raises once two
+        # parameters of different shapes meet; it means identity, which is
+        # what this list's membership test does
+        owned = _IdentityList(p for p in params if p.requires_grad)
+        chunks = mod.build_chunk_param(owned, model, world, rank)
+        res[f"chunks_{tag}"] = [(getattr(c, "chunk_begin", None), getattr(c, "chunk_end", None), c.detach().clone(),
+                                 None if c.grad is None else c.grad.clone()) for c in chunks]
+        mgr = mod.AsyncParamAllGatherManager(grp, world)
+        for p in params:
+            if hasattr(p, "chunk_part"):
+                p.chunk_part.data.mul_(float(rank + 2))  # this rank's "optimizer step" on its rows
+                mgr.push(p)
+        mgr.wait_all()
+        mgr.shutdown()
+        res[f"params_{tag}"] = [p.detach().clone() for p in params]
+        res[f"state_{tag}"] = [int(p.state) for p in params]
+    return res

@@ -297,3 +297,32 @@ def test_ring_attention_ops_two_ranks_match_sdpa():
             got = res[r][key]
             err = ((got - want[:, :, sl]).abs().max() / want[:, :, sl].abs().max()).item()
             assert err < 3e-2, (r, key, err)
+
+
+@pytest.mark.skipif(not os.environ.get("HARP_REFERENCE_DIR"),
+                    reason="HARP_REFERENCE_DIR (the reference project's root) not set")
+def test_managers_match_the_reference_two_ranks(tmp_path):
+    """Oracle: the reference's own shard_manager.py and weight_manager.py
+    (pure PyTorch + torch.distributed) and harp's managers give the same
+    results on two gloo ranks (forward values, input gradients, owners, row
+    chunks with their gradient views, gathered parameters and ready flags)."""
+    res, _ = _run("managers_oracle", 2, tmp_path, {"ref": os.environ["HARP_REFERENCE_DIR"]})
+    for r in (0, 1):
+        d = res[r]
+        keys = sorted({k.rsplit("_", 1)[0] for k in d})
+        for k in keys:
+            a, b = d[k + "_ref"], d[k + "_ours"]
+            if k.startswith("chunks"):
+                assert len(a) == len(b), k
+                for (b0, e0, v0, g0), (b1, e1, v1, g1) in zip(a, b):
+                    assert (b0, e0) == (b1, e1), k
+                    assert torch.equal(v0, v1), k
+                    assert (g0 is None) == (g1 is None) and (g0 is None or torch.equal(g0, g1)), k
+            elif isinstance(a, (list, tuple)) and a and isinstance(a[0], torch.Tensor):
+                assert len(a) == len(b), k
+                for u, v in zip(a, b):
+                    torch.testing.assert_close(v, u, rtol=0, atol=0, msg=k)
+            elif isinstance(a, torch.Tensor):
+                torch.testing.assert_close(b, a, rtol=0, atol=0, msg=k)
+            else:
+                assert a == b, (k, a, b)
