@@ -21,7 +21,7 @@ setup(
     name="harp_b200",
     version="0.1.0",
     description="Sequence-parallel DiT training on B200 (sm_100a): tcgen05 kernels, NVLink collectives",
-    packages=find_packages(include=["harp_b200", "harp_b200.*", "managers"]),
+    packages=find_packages(include=["harp_b200", "harp_b200.*", "managers", "async_rt"]),
     package_data={"harp_b200": ["csrc/*.cu", "csrc/*.cuh", "csrc/*.cpp", "csrc/*.h"]},
     python_requires=">=3.10",
     cmdclass={"build_ext": HarpBuild},

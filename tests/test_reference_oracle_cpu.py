@@ -465,3 +465,31 @@ def test_npz_dataset_and_collate(tmp_path):
         torch.testing.assert_close(u, v, rtol=0, atol=0)
     assert len(ca["cond"]) == len(cb["cond"]) == 1
     torch.testing.assert_close(ca["cond"][0], cb["cond"][0], rtol=0, atol=0)
+
+
+def test_broadcasting_autograd_ops():
+    """async_rt/async_ops.py:55-122 (MyMul, MyAdd; the file's other ops call
+    the reference's compiled library) against harp's, with broadcasting and a
+    Python-number operand."""
+    from async_rt import async_ops as O
+
+    R = _load("async_rt/async_ops.py")
+    torch.manual_seed(0)
+    a0, b0 = torch.randn(4, 1, 5), torch.randn(3, 5)
+    for fn in ("MyMul", "MyAdd"):
+        outs = []
+        for mod in (R, O):
+            a, b = a0.clone().requires_grad_(True), b0.clone().requires_grad_(True)
+            y = getattr(mod, fn).apply(a, b)
+            y.pow(2).sum().backward()
+            outs.append((y.detach(), a.grad, b.grad))
+        for u, v in zip(*outs):
+            torch.testing.assert_close(v, u, rtol=0, atol=0)
+    outs = []
+    for mod in (R, O):
+        b = b0.clone().requires_grad_(True)
+        y = mod.MyAdd.apply(1.5, b)
+        (y * b0).sum().backward()
+        outs.append((y.detach(), b.grad))
+    for u, v in zip(*outs):
+        torch.testing.assert_close(v, u, rtol=0, atol=0)

@@ -341,3 +341,73 @@ def test_train_cli_two_ranks_checkpoint_resume(tmp_path):
     second = {r["global_step"]: r["step_loss"] for r in map(json.loads, open(os.path.join(work, "metrics.jsonl")))
               if "step_loss" in r}
     assert sorted(second) == [3] and second[3] == first[3], (first, second)
+
+
+def test_async_runtime_api_on_streams():
+    """The reference's async-runtime API (async_rt/): the mode switches and
+    syncs are identities on values and gradients and set the mode flag as the
+    reference's do; MyMul / MyAdd broadcast and sum gradients back to each
+    input's shape; the kernel helpers write the linear and SiLU results into
+    the caller's tensors (CPU restatements here, to bf16 rounding)."""
+    import async_rt
+    from async_rt import async_ops as O
+    from async_rt import runtime as R
+
+    assert async_rt.is_asyncrt_enabled() is False
+    x = torch.randn(2, 3, requires_grad=True)
+    y = R.AsyncModeStart.apply(x)
+    assert R.AsyncRunMode.mode_enable is True
+    y = R.AsyncSync.apply(y, True, True)
+    y = R.AsyncModeEnd.apply(y)
+    assert R.AsyncRunMode.mode_enable is False
+    (y * 3).sum().backward()
+    torch.testing.assert_close(x.grad, torch.full_like(x, 3.0))
+    R.RUNTIME.sync()
+    with R.AsyncRunMode():
+        torch.testing.assert_close(torch.ones(2) + 1, torch.full((2,), 2.0))
+
+    a = torch.randn(4, 1, 5, requires_grad=True)
+    b = torch.randn(3, 5, requires_grad=True)
+    O.MyMul.apply(a, b).pow(2).sum().backward()
+    ga, gb = a.grad.clone(), b.grad.clone()
+    a.grad = b.grad = None
+    (a * b).pow(2).sum().backward()
+    torch.testing.assert_close(ga, a.grad)
+    torch.testing.assert_close(gb, b.grad)
+    a.grad = b.grad = None
+    O.MyAdd.apply(a, b).pow(2).sum().backward()
+    ga, gb = a.grad.clone(), b.grad.clone()
+    a.grad = b.grad = None
+    (a + b).pow(2).sum().backward()
+    torch.testing.assert_close(ga, a.grad)
+    torch.testing.assert_close(gb, b.grad)
+    b.grad = None
+    O.MyAdd.apply(2.5, b).sum().backward()
+    torch.testing.assert_close(b.grad, torch.ones_like(b))
+
+    torch.manual_seed(0)
+    xin = torch.randn(6, 16).bfloat16()
+    w = torch.randn(8, 16).bfloat16()
+    bias = torch.randn(8).bfloat16()
+    out = torch.empty(6, 8, dtype=torch.bfloat16)
+    O.mm_kernel(out, xin, w, bias)
+    ref = xin.float() @ w.float().t() + bias.float()
+    torch.testing.assert_close(out.float(), ref, rtol=2e-2, atol=2e-2)
+    dy = torch.randn(6, 8).bfloat16()
+    gi, gw, gbias = torch.empty_like(xin), torch.empty_like(w), torch.empty_like(bias)
+    O.mm_backward_kernel(gi, dy, xin, w, gw, gbias)
+    torch.testing.assert_close(gi.float(), dy.float() @ w.float(), rtol=2e-2, atol=5e-2)
+    torch.testing.assert_close(gw.float(), dy.float().t() @ xin.float(), rtol=2e-2, atol=5e-2)
+    torch.testing.assert_close(gbias.float(), dy.float().sum(0), rtol=2e-2, atol=5e-2)
+    s = torch.empty_like(xin)
+    O.silu_kernel(s, xin)
+    torch.testing.assert_close(s.float(), torch.nn.functional.silu(xin.float()), rtol=1e-2, atol=1e-2)
+    O.silu_backward_kernel(s, dy[:, :1].expand(6, 16).contiguous(), xin)
+    xf = xin.float().requires_grad_(True)
+    torch.nn.functional.silu(xf).backward(dy[:, :1].expand(6, 16).float())
+    torch.testing.assert_close(s.float(), xf.grad, rtol=1e-2, atol=1e-2)
+    o2 = torch.empty(6, 16)
+    O.mul_fast(o2, xin.float(), xin.float())
+    torch.testing.assert_close(o2, xin.float() ** 2)
+    O.add_kernel(o2, xin.float(), xin.float())
+    torch.testing.assert_close(o2, 2 * xin.float())
