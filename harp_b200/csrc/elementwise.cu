@@ -15,6 +15,7 @@
 #include "common.cuh"
 #include "norm_rope.cuh"
 #include "gemm_sm100.h"
+#include "staging.h"
 
 #include <ATen/ATen.h>
 #include <ATen/cuda/CUDAContext.h>
@@ -1568,16 +1569,27 @@ void layernorm_mod_bwd(const at::Tensor& x, const at::Tensor& mean, const at::Te
   count_launch();
 }
 
-void elementwise(int64_t op, const at::Tensor& a, const c10::optional<at::Tensor>& b, double s, at::Tensor& out) {
-  TORCH_CHECK(a.is_contiguous() && out.is_contiguous(), "elementwise: contiguous");
-  if (b.has_value()) TORCH_CHECK(b->is_contiguous() && b->numel() == a.numel(), "elementwise: b");
-  const long n = a.numel();
+// Operands are taken in flat element order; any that is not a contiguous,
+// 16-byte aligned block is staged (staging.h).
+void elementwise(int64_t op, const at::Tensor& a_in, const c10::optional<at::Tensor>& b_in, double s,
+                 at::Tensor& out) {
+  TORCH_CHECK(a_in.scalar_type() == at::kBFloat16 && out.scalar_type() == at::kBFloat16 &&
+                  (!b_in.has_value() || b_in->scalar_type() == at::kBFloat16),
+              "elementwise: bf16 tensors");
+  TORCH_CHECK(out.numel() == a_in.numel(), "elementwise: out has ", out.numel(), " elements, a has ", a_in.numel());
+  if (b_in.has_value()) TORCH_CHECK(b_in->numel() == a_in.numel(), "elementwise: b size");
+  const long n = a_in.numel();
   if (n == 0) return;
-  const at::cuda::CUDAGuard g(a.device());
+  const at::cuda::CUDAGuard g(a_in.device());
+  const at::Tensor a = block16(a_in);
+  c10::optional<at::Tensor> b;
+  if (b_in.has_value()) b = block16(*b_in);
+  StagedOut o(out);
   const long grid = ((n + 7) / 8 + 255) / 256;
-  ew_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>((int)op, bp(a), bp(b), (float)s, n, bpm(out));
+  ew_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>((int)op, bp(a), bp(b), (float)s, n, bpm(o.work));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   count_launch();
+  o.finish();
 }
 
 // `hyper` (optional fp32 device tensor [lr, 1 - beta1^t, sqrt(1 - beta2^t)])

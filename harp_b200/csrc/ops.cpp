@@ -14,6 +14,7 @@
 #include <torch/library.h>
 
 #include "gemm_sm100.h"
+#include "staging.h"
 
 namespace harp {
 
@@ -113,24 +114,40 @@ void add_scalar_out(const at::Tensor& a, double s, at::Tensor out) { elementwise
 
 // rmsnorm_forward_out saves rms (not its inverse), as the reference does
 // (rms_norm.cc:21-101).
+// The caller's tensors may be views at any offset: operands that are not
+// contiguous 16-byte aligned blocks are staged (staging.h).
 void rmsnorm_forward_out(const at::Tensor& input, const at::Tensor& weight, at::Tensor output, at::Tensor rms,
                          double eps) {
-  auto x = input.contiguous().view({-1, input.size(-1)});
-  auto y = output.view({-1, output.size(-1)});
-  rmsnorm_mod_fwd(x, weight, c10::nullopt, c10::nullopt, x.size(0), eps, y, rms, true);
+  TORCH_CHECK(input.scalar_type() == at::kBFloat16 && weight.scalar_type() == at::kBFloat16 &&
+                  output.scalar_type() == at::kBFloat16 && rms.scalar_type() == at::kFloat,
+              "rmsnorm_forward_out: bf16 input, weight and output, fp32 rms");
+  auto x = block16(input).view({-1, input.size(-1)});
+  StagedOut out(output), r(rms);
+  auto y = out.work.view({-1, output.size(-1)});
+  rmsnorm_mod_fwd(x, block16(weight), c10::nullopt, c10::nullopt, x.size(0), eps, y, r.work, true);
+  out.finish();
+  r.finish();
 }
 void rmsnorm_backward_out(const at::Tensor& input, const at::Tensor& grad_out, const at::Tensor& weight,
                           const at::Tensor& rms, at::Tensor grad_input, at::Tensor grad_weight) {
-  auto x = input.contiguous().view({-1, input.size(-1)});
-  auto g = grad_out.contiguous().view({-1, grad_out.size(-1)});
-  auto gi = grad_input.view({-1, grad_input.size(-1)});
+  TORCH_CHECK(input.scalar_type() == at::kBFloat16 && grad_out.scalar_type() == at::kBFloat16 &&
+                  weight.scalar_type() == at::kBFloat16 && grad_input.scalar_type() == at::kBFloat16 &&
+                  grad_weight.scalar_type() == at::kBFloat16,
+              "rmsnorm_backward_out: bf16 tensors (rms fp32)");
+  auto x = block16(input).view({-1, input.size(-1)});
+  auto g = block16(grad_out).view({-1, grad_out.size(-1)});
+  StagedOut gi_out(grad_input), gw_out(grad_weight);
+  auto gi = gi_out.work.view({-1, grad_input.size(-1)});
   const int R = x.size(0), D = x.size(1);
-  auto rstd = rms.reciprocal();
+  auto rstd = rms.reciprocal().contiguous();
   const int rpb = 32;
   auto pw = at::empty({(R + rpb - 1) / rpb, D}, x.options().dtype(at::kFloat));
-  rmsnorm_mod_bwd(x, rstd, g, weight, c10::nullopt, R, c10::nullopt, gi, pw, c10::nullopt, c10::nullopt, rpb);
-  auto gw = grad_weight.view({1, D});
+  rmsnorm_mod_bwd(x, rstd, g, block16(weight), c10::nullopt, R, c10::nullopt, gi, pw, c10::nullopt, c10::nullopt,
+                  rpb);
+  auto gw = gw_out.work.view({1, D});
   reduce_partials(pw, pw.size(0), gw, false);
+  gi_out.finish();
+  gw_out.finish();
 }
 // x: [..., D] (interleaved complex pairs); freqs_cis: complex64 [..., D/2]
 // broadcastable over the leading dims of x except the last two.

@@ -416,7 +416,7 @@ def rowdot(a: torch.Tensor, b: torch.Tensor, H: int, Dh: int, S: int) -> torch.T
 
 def silu(x: torch.Tensor) -> torch.Tensor:
     out = torch.empty_like(x)
-    if _cuda(x) and x.is_contiguous():
+    if _cuda(x) and x.dtype == torch.bfloat16 and x.is_contiguous():
         torch.ops.harp.elementwise(0, x, None, 0.0, out)
         return out
     return torch.nn.functional.silu(x.float()).to(x.dtype)
@@ -424,7 +424,7 @@ def silu(x: torch.Tensor) -> torch.Tensor:
 
 def silu_bwd(dy: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
     out = torch.empty_like(x)
-    if _cuda(x) and x.is_contiguous() and dy.is_contiguous():
+    if _cuda(x) and x.dtype == dy.dtype == torch.bfloat16 and x.is_contiguous() and dy.is_contiguous():
         torch.ops.harp.elementwise(1, dy, x, 0.0, out)
         return out
     s = torch.sigmoid(x.float())

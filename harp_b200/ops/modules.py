@@ -186,7 +186,7 @@ class MyTanh(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x):
         x = x.contiguous()
-        if x.is_cuda:
+        if x.is_cuda and x.dtype == torch.bfloat16:
             y = torch.empty_like(x)
             torch.ops.async_op.tanh_out(x, y)
         else:
@@ -197,7 +197,7 @@ class MyTanh(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dy):
         (y,) = ctx.saved_tensors
-        if y.is_cuda:
+        if y.is_cuda and y.dtype == torch.bfloat16:
             dx = torch.empty_like(y)
             torch.ops.async_op.tanh_backward_out(dy.contiguous(), y, dx)
             return dx
