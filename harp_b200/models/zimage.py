@@ -194,6 +194,44 @@ class RopeEmbedder:
         return torch.complex(f[..., 0], f[..., 1])
 
 
+class RopeTableEmbedder(RopeEmbedder):
+    """RopeEmbedder that computes each axis's (cos, sin) table once per device
+    (axes_lens[a] positions) and then only gathers rows by id, as the
+    reference's table-lookup embedder does (kp_rope_embedder.py:46-67).  Same
+    values as RopeEmbedder for ids inside the tables."""
+
+    def __init__(self, theta=256.0, axes_dims=(16, 56, 56), axes_lens=(64, 128, 128)):
+        super().__init__(theta, axes_dims, axes_lens)
+        self._tables: Dict[torch.device, List[torch.Tensor]] = {}
+
+    def tables(self, device) -> List[torch.Tensor]:
+        device = torch.device(device)
+        if device not in self._tables:
+            tabs = []
+            for a, (d, n) in enumerate(zip(self.axes_dims, self.axes_lens)):
+                ids = torch.zeros(n, len(self.axes_dims), dtype=torch.int64, device=device)
+                ids[:, a] = torch.arange(n, device=device)
+                full = RopeEmbedder.__call__(self, ids)
+                lo = sum(self.axes_dims[:a]) // 2
+                tabs.append(full[:, lo:lo + d // 2].contiguous())
+            self._tables[device] = tabs
+        return self._tables[device]
+
+    def __call__(self, ids: torch.Tensor) -> torch.Tensor:
+        tabs = self.tables(ids.device)
+        return torch.cat([t[ids[:, a].long()] for a, t in enumerate(tabs)], 1)
+
+
+def replace_ropeembedder_with_sverope(model: nn.Module, rope_class=RopeTableEmbedder) -> nn.Module:
+    """Swap every `rope_embedder` attribute in the module tree for a
+    `rope_class` with the same theta and axes (kp_rope_embedder.py:70-84)."""
+    for mod in model.modules():
+        emb = getattr(mod, "rope_embedder", None)
+        if emb is not None and not isinstance(emb, rope_class):
+            mod.rope_embedder = rope_class(theta=emb.theta, axes_dims=emb.axes_dims, axes_lens=emb.axes_lens)
+    return model
+
+
 class ConfigMixin:
     config_name = "config.json"
 

@@ -550,3 +550,23 @@ def test_zimage_sp_wrapper_parameter_groups():
     n_cond = sum(p.numel() for n, p in model.named_parameters() if n.startswith(("cond_embedder_", "cond_refiner_")))
     assert model.switch_cond_branch_grad(False) == n_cond > 0
     assert model.switch_cond_branch_grad(True) == n_cond
+
+
+def test_rope_table_embedder_swap_keeps_predictions():
+    """replace_ropeembedder_with_sverope swaps the Z-Image model's rotary
+    embedder for the table-lookup one: bitwise the same predictions."""
+    torch.manual_seed(0)
+    pre = Z.PRESETS["zimage-tiny"]
+    model = Z.ZImageTransformer2DModel(**pre)
+    with torch.no_grad():
+        for p in model.parameters():
+            p.normal_(0, 0.05)
+    x = [torch.randn(16, 1, 18, 18)]
+    caps = [torch.randn(20, pre["cap_feat_dim"])]
+    t = torch.rand(1)
+    with torch.no_grad():
+        a = model(x, t, caps)["sample"][0]
+        Z.replace_ropeembedder_with_sverope(model)
+        assert isinstance(model.rope_embedder, Z.RopeTableEmbedder)
+        b = model(x, t, caps)["sample"][0]
+    torch.testing.assert_close(a, b, rtol=0, atol=0)

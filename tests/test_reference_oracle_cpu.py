@@ -177,9 +177,27 @@ def test_rope_embedder_tables():
     R = _load("kp_rope_embedder.py")
     dims, lens = (32, 48, 48), (1024, 512, 512)
     ref = R.RopeEmbedderReference(256.0, dims, lens)
-    ours = RopeEmbedder(256.0, dims, lens)
     ids = torch.stack([torch.randint(0, n, (300,)) for n in lens], -1).int()
-    torch.testing.assert_close(ours.complex(ids), ref(ids), rtol=0, atol=2e-6)
+    import kp_rope_embedder as K
+
+    for cls in (RopeEmbedder, K.RopeEmbedderReference, K.RopeEmbedderSVE):
+        torch.testing.assert_close(cls(256.0, dims, lens).complex(ids), ref(ids), rtol=0, atol=2e-6)
+
+
+def test_kp_rope_complex_form():
+    """kp_rope.kp_apply_rotary_emb (complex form) against the reference's
+    src/utils/rope.py apply_rotary_emb(use_real=False); the real form is
+    refused in both."""
+    import kp_rope
+
+    R = _load("src/utils/rope.py")
+    x = torch.randn(2, 3, 10, 16)
+    ang = torch.rand(2, 10, 8) * 6
+    f = torch.polar(torch.ones_like(ang), ang)
+    torch.testing.assert_close(kp_rope.kp_apply_rotary_emb(x, f, use_real=False),
+                               R.apply_rotary_emb(x, f, use_real=False), rtol=0, atol=1e-5)
+    with pytest.raises(NotImplementedError):
+        kp_rope.kp_apply_rotary_emb(x, f)
 
 
 def test_metadata():

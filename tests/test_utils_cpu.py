@@ -411,3 +411,36 @@ def test_async_runtime_api_on_streams():
     torch.testing.assert_close(o2, xin.float() ** 2)
     O.add_kernel(o2, xin.float(), xin.float())
     torch.testing.assert_close(o2, 2 * xin.float())
+
+
+def test_reference_import_paths():
+    """The reference's top-level import paths resolve to harp's implementations
+    (managers.*, async_rt.*, unigemm_linear, kp_normalization,
+    kp_multi_tensor_adamw, kp_rope, kp_rope_embedder)."""
+    import importlib
+
+    from harp_b200.models import zimage as Z
+    from harp_b200.ops import modules as M
+
+    want = {
+        "unigemm_linear": {"kpLinear": M.kpLinear, "replace_linear_with_kplinear": M.replace_linear_with_kplinear,
+                           "CustomLinearFunction": M.LinearFunction},
+        "kp_normalization": {"kpRMSNorm": M.kpRMSNorm, "CustomNormFunction": M.RMSNormFunction,
+                             "replace_rmsNorm_with_kpRMSNorm": M.replace_rmsNorm_with_kpRMSNorm},
+        "kp_multi_tensor_adamw": {"kp_multi_tensor_adamw": M.kp_multi_tensor_adamw},
+        "kp_rope_embedder": {"RopeEmbedderSVE": Z.RopeTableEmbedder,
+                             "replace_ropeembedder_with_sverope": Z.replace_ropeembedder_with_sverope},
+        "async_rt.async_ops": {"MySiLU": M.MySiLU, "MyTanh": M.MyTanh, "ApplyRotaryComplexFn": M.ApplyRotaryComplexFn},
+        "managers.shard_manager": {},
+        "managers.weight_manager": {},
+        "managers.grad_manager": {},
+        "managers.mem_manager": {},
+        "managers.ring_attn_manager": {},
+    }
+    for mod_name, names in want.items():
+        mod = importlib.import_module(mod_name)
+        for n, obj in names.items():
+            assert getattr(mod, n) is obj, (mod_name, n)
+    import kp_rope
+
+    assert callable(kp_rope.kp_apply_rotary_emb)
