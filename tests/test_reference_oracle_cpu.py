@@ -511,3 +511,35 @@ def test_broadcasting_autograd_ops():
         outs.append((y.detach(), b.grad))
     for u, v in zip(*outs):
         torch.testing.assert_close(v, u, rtol=0, atol=0)
+
+
+def test_train_cli_on_the_reference_sample_data(tmp_path):
+    """harp's train.py reads the reference's shipped samples (data/index.json,
+    whose entries are "HARP/data/..." paths) and trains a small Z-Image with
+    their shapes (caption features 2560 wide, 16 x 64 x 64 latents, 192-channel
+    condition images, 4 metadata values) for two steps, with finite losses."""
+    import subprocess
+    import sys
+
+    from harp_b200.utils.data import NpzDataset
+
+    index = os.path.join(REF, "data", "index.json")
+    assert len(NpzDataset(index)) == len(json.load(open(index)))
+    cfg_dir = tmp_path / "cfg" / "transformer"
+    cfg_dir.mkdir(parents=True)
+    (cfg_dir / "config.json").write_text(json.dumps({
+        "all_patch_size": [2], "all_f_patch_size": [1], "in_channels": 16, "dim": 64, "n_layers": 1,
+        "n_refiner_layers": 1, "n_heads": 2, "n_kv_heads": 2, "cap_feat_dim": 2560, "axes_dims": [8, 12, 12],
+        "axes_lens": [2048, 64, 64]}))
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    work = tmp_path / "w"
+    cmd = [sys.executable, os.path.join(root, "train.py"), "--model", "zimage-tiny", "--pretrained_model_name_or_path",
+           str(tmp_path / "cfg"), "--data_root", index, "--max_train_steps", "2", "--train_batch_size", "1",
+           "--sp_size", "1", "--work_dir", str(work), "--lr_warmup_steps", "1", "--checkpointing_steps", "100"]
+    r = subprocess.run(cmd, capture_output=True, text=True, timeout=900, cwd=str(tmp_path),
+                       env=dict(os.environ, CUDA_VISIBLE_DEVICES=""))
+    assert r.returncode == 0, r.stderr[-3000:]
+    (run,) = os.listdir(work)
+    rows = [json.loads(line) for line in open(work / run / "metrics.jsonl") if line.strip()]
+    losses = [row["step_loss"] for row in rows if "step_loss" in row]
+    assert len(losses) == 2 and all(math.isfinite(v) for v in losses)
