@@ -30,7 +30,12 @@ Differences from the reference, on purpose:
   * under sequence parallelism every embedder and the final layer run on the
     tokens a rank holds (never replicated), so summing parameter gradients
     over all ranks is exact; the reference instead replicates them and keeps
-    only the owner's gradient (grad_manager.py:53-61).
+    only the owner's gradient (grad_manager.py:53-61).  There, the adaLN input
+    passes through SPBroadcast (an all-reduce of its gradient) once per
+    section (hl_model.py:174, 312, 439), so the sections' already summed
+    gradients are summed again: with its own hl_model.py on two CPU ranks,
+    the t_embedder and metadata-embedder gradients come out 1.97x the
+    one-rank values.  The blocks' gradients agree with the one-rank run.
 """
 from __future__ import annotations
 

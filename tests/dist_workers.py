@@ -459,3 +459,87 @@ def managers_oracle(rank, world, out, args):
         res[f"params_{tag}"] = [p.detach().clone() for p in params]
         res[f"state_{tag}"] = [int(p.state) for p in params]
     return res
+
+
+def zimage_reference_sp(rank, world, out, args):
+    """The reference's own sequence-parallel Z-Image (src/models/z_image/
+    hl_model.py with its module/block.py and module/attn.py, on its
+    standalone base model) beside harp's Z_Transformer(harp_block_compat=True)
+    with the same weights.  The reference's imports of managers.*, async_rt.*
+    and its ring-attention ops resolve to this repository's implementations of
+    those APIs (the repository root precedes the reference on sys.path).
+
+    The reference runs on a one-rank group, in fp32 and in bf16, so its
+    gradients are the exact ones: over several ranks its SPBroadcast of the
+    adaLN input sums the final layer's (replicated) adaLN gradient over the
+    ranks, so t_embedder and the metadata embedders would get that term
+    sp_size times.  Over the whole group it runs the forward only, in bf16.
+    harp runs sequence-parallel over the whole group in bf16.  Returns the
+    image predictions (the reference's in full, harp's for this rank's tokens)
+    and the parameter gradients of a fixed weighted sum of the predictions."""
+    import sys
+
+    sys.path.append(args["ref"])
+    from src.models.z_image import hl_model as RH
+    from src.models.z_image import standalone_transformer as RS
+
+    from harp_b200.models import zimage as Z
+    from harp_b200.ops import ring_ops
+    from harp_b200.parallel.sequence import SPContext
+
+    grp = dist.group.WORLD
+    solo = [dist.new_group([r]) for r in range(world)][rank]
+    sp = SPContext.from_group(grp, backend="torch") if world > 1 else SPContext()
+    pre = dict(Z.PRESETS["zimage-tiny"])
+
+    def reference_model(group, size):
+        torch.manual_seed(0)
+        base = RS.ZImageTransformer2DModel(**{k: (list(v) if isinstance(v, tuple) else v) for k, v in pre.items()})
+        return RH.Z_Transformer(base, num_metadata=2, use_cond=True, sp_group_model=group, sp_size=size)
+
+    ref32 = reference_model(solo, 1)
+    with torch.no_grad():
+        for p in ref32.parameters():
+            p.normal_(0, 0.05)
+    ref16 = reference_model(solo, 1)
+    ref16.load_state_dict(ref32.state_dict(), strict=True)
+    obase = Z.ZImageTransformer2DModel(**pre)
+    ours = Z.Z_Transformer(obase, num_metadata=2, use_cond=True, sp_size=world, harp_block_compat=True)
+    ours.load_state_dict(ref32.state_dict(), strict=True)
+    ref32, ref16, ours = ref32.float(), ref16.bfloat16(), ours.bfloat16()
+
+    g = torch.Generator().manual_seed(3)
+    B, hw = 2, args.get("hw", 16)
+    x = [torch.randn(16, 1, hw, hw, generator=g).bfloat16() for _ in range(B)]
+    t = torch.rand(B, generator=g)
+    caps = [torch.randn(args.get("cap", 32), pre["cap_feat_dim"], generator=g).bfloat16() for _ in range(B)]
+    meta = torch.rand(B, 2, generator=g).bfloat16()
+    cond = [[torch.randn(192, hw, hw, generator=g).bfloat16() for _ in range(B)]]
+    n_img = (hw // 2) ** 2
+    w = torch.randn(B, n_img, 4 * 16, generator=g)
+
+    def grads(m):
+        return {n: (p.grad.float().clone() if p.grad is not None else torch.zeros(p.shape)) for n, p in
+                m.named_parameters()}
+
+    def run_reference(m, dt):
+        pred = m([v.to(dt) for v in x], t, [c.to(dt) for c in caps], metadata=meta.to(dt),
+                 cond_list=[[c.to(dt) for c in branch] for branch in cond]).sample
+        return torch.stack(obase.patchify([p.float() for p in pred], 2, 1)[0])  # [B, n_img, p*p*C]
+
+    res = {}
+    ring_ops.set_sp_context(None)
+    for tag, m, dt in (("ref32", ref32, torch.float32), ("ref16", ref16, torch.bfloat16)):
+        tok = run_reference(m, dt)
+        (tok * w).sum().backward()
+        res["pred_" + tag], res["grads_" + tag] = tok.detach(), grads(m)
+    if world > 1:
+        refw = reference_model(grp, world)
+        refw.load_state_dict(ref32.state_dict(), strict=True)
+        ring_ops.set_sp_context(sp)
+        with torch.no_grad():
+            res["pred_refw"] = run_reference(refw.bfloat16(), torch.bfloat16)
+    pred_o, lo, hi = ours.forward_local(x, t, caps, metadata=meta, cond_list=cond, sp=sp)
+    (pred_o.float() * w[:, lo:hi]).sum().backward()
+    res.update(pred_ours=pred_o.detach().float(), range=(lo, hi), grads_ours=grads(ours))
+    return res
