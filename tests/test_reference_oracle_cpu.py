@@ -543,3 +543,72 @@ def test_train_cli_on_the_reference_sample_data(tmp_path):
     rows = [json.loads(line) for line in open(work / run / "metrics.jsonl") if line.strip()]
     losses = [row["step_loss"] for row in rows if "step_loss" in row]
     assert len(losses) == 2 and all(math.isfinite(v) for v in losses)
+
+
+def _load_reference_inference(monkeypatch):
+    """src/utils/inference.py imports diffusers (not needed for latent output);
+    stand-ins for the names it imports let the module load."""
+    import sys
+    import types
+
+    def randn_tensor(shape, generator=None, device=None, dtype=None):
+        return torch.randn(shape, generator=generator, dtype=dtype).to(device)
+
+    mods = {n: types.ModuleType(n) for n in ("diffusers", "diffusers.utils", "diffusers.utils.torch_utils",
+                                             "diffusers.image_processor", "diffusers.pipelines",
+                                             "diffusers.pipelines.z_image",
+                                             "diffusers.pipelines.z_image.pipeline_output")}
+    mods["diffusers.utils.torch_utils"].randn_tensor = randn_tensor
+    mods["diffusers.image_processor"].VaeImageProcessor = object
+    for n in ("ZImageTransformer2DModel", "AutoencoderKL", "FlowMatchEulerDiscreteScheduler"):
+        setattr(mods["diffusers"], n, object)
+    mods["diffusers.pipelines.z_image.pipeline_output"].ZImagePipelineOutput = dict
+    for n, m in mods.items():
+        monkeypatch.setitem(sys.modules, n, m)
+    return _load("src/utils/inference.py")
+
+
+@pytest.mark.parametrize("cfg", [None, dict(guidance_scale=4.0, cfg_truncation=0.6, cfg_normalization=1.2)])
+def test_sampling_loop_matches_the_reference(monkeypatch, cfg):
+    """src/utils/inference.py batch_image_inference (the reference's sampling
+    loop: shifted flow-match grid, classifier-free guidance with truncation
+    and renormalisation, Euler steps) against harp_b200.inference's, with the
+    same model (harp's Z-Image, called through the reference loop's
+    convention) and harp's scheduler in both: the same final latents."""
+    from harp_b200 import inference as HI
+    from harp_b200.models import zimage as Z
+    from harp_b200.parallel.sequence import SPContext
+    from harp_b200.utils.diffusion import FlowMatchEulerDiscreteScheduler
+
+    R = _load_reference_inference(monkeypatch)
+    torch.manual_seed(0)
+    pre = Z.PRESETS["zimage-tiny"]
+    model = Z.Z_Transformer(Z.ZImageTransformer2DModel(**pre))
+    with torch.no_grad():
+        for p in model.parameters():
+            p.normal_(0, 0.05)
+    model = model.bfloat16()
+
+    class ReferenceConvention:
+        """transformer(x=[C, 1, H, W] list, t, text_embedding, return_dict=False)[0] -> list of [C, 1, H, W]."""
+        device = torch.device("cpu")
+        in_channels = 16
+
+        def __call__(self, x, t, text_embedding, return_dict=False):
+            pred, _, _ = model.forward_local(x, t, text_embedding, sp=SPContext())
+            return ([model.z_transformer.unpatchify(pred[b], tuple(x[b].shape[1:]), 2, 1) for b in range(len(x))],)
+
+    g = torch.Generator().manual_seed(1)
+    lat = torch.randn(2, 16, 16, 16, generator=g).bfloat16()
+    pos = [torch.randn(32, pre["cap_feat_dim"], generator=g).bfloat16() for _ in range(2)]
+    neg = [torch.randn(32, pre["cap_feat_dim"], generator=g).bfloat16() for _ in range(2)] if cfg else None
+    kw = dict(prompt_embeds=pos, negative_prompt_embeds=neg, num_inference_steps=6, output_type="latent",
+              return_dict=False, initial_latents=lat.clone(), vae_scale_factor=8, **(cfg or {}))
+
+    def scheduler():
+        return FlowMatchEulerDiscreteScheduler(shift=3.0, use_dynamic_shifting=True)
+
+    want = R.batch_image_inference(ReferenceConvention(), None, scheduler(), None, **kw)[0]
+    got = HI.batch_image_inference(model, None, scheduler(), None, **kw)[0]
+    assert got.dtype == want.dtype == torch.bfloat16
+    assert ((got.float() - want.float()).norm() / want.float().norm()).item() < 5e-3
