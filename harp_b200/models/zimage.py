@@ -227,6 +227,11 @@ class RopeTableEmbedder(RopeEmbedder):
         return torch.cat([t[ids[:, a].long()] for a, t in enumerate(tabs)], 1)
 
 
+# the reference's names (kp_rope_embedder.py:6, 46)
+RopeEmbedderReference = RopeEmbedder
+RopeEmbedderSVE = RopeTableEmbedder
+
+
 def replace_ropeembedder_with_sverope(model: nn.Module, rope_class=RopeTableEmbedder) -> nn.Module:
     """Swap every `rope_embedder` attribute in the module tree for a
     `rope_class` with the same theta and axes (kp_rope_embedder.py:70-84)."""

@@ -140,6 +140,7 @@ class kpRMSNorm(nn.Module):
 
 
 RMSNorm = kpRMSNorm
+CustomNormFunction = RMSNormFunction  # the reference's name (kp_normalization.py:8)
 
 
 def _is_rmsnorm(m: nn.Module) -> bool:
@@ -257,6 +258,14 @@ class ApplyRotaryComplexFn(torch.autograd.Function):
     def backward(ctx, g):
         (freqs_cis,) = ctx.saved_tensors
         return _rope_apply(g, freqs_cis, inverse=True), None
+
+
+def kp_apply_rotary_emb(x, freqs_cis, use_real: bool = True, use_real_unbind_dim: int = -1):
+    """Rotary embedding of x [B, H, S, D] by complex freqs_cis (kp_rope.py:4-14);
+    as in the reference only the complex form (use_real=False) exists."""
+    if use_real:
+        raise NotImplementedError("kp_apply_rotary_emb: only the complex form (use_real=False)")
+    return ApplyRotaryComplexFn.apply(x, freqs_cis)
 
 
 def _rope_apply(x, freqs_cis, inverse):

@@ -21,8 +21,7 @@ setup(
     name="harp_b200",
     version="0.1.0",
     description="Sequence-parallel DiT training on B200 (sm_100a): tcgen05 kernels, NVLink collectives",
-    packages=find_packages(include=["harp_b200", "harp_b200.*", "managers", "async_rt"]),
-    py_modules=["unigemm_linear", "kp_normalization", "kp_multi_tensor_adamw", "kp_rope", "kp_rope_embedder"],
+    packages=find_packages(include=["harp_b200", "harp_b200.*"]),
     package_data={"harp_b200": ["csrc/*.cu", "csrc/*.cuh", "csrc/*.cpp", "csrc/*.h"]},
     python_requires=">=3.10",
     cmdclass={"build_ext": HarpBuild},

@@ -467,18 +467,22 @@ def zimage_reference_sp(rank, world, out, args):
     standalone base model) beside harp's Z_Transformer(harp_block_compat=True)
     with the same weights.  The reference's imports of managers.*, async_rt.*
     and its ring-attention ops resolve to this repository's implementations of
-    those APIs (the repository root precedes the reference on sys.path).
+    those APIs (harp_b200.compat registers the module names before the
+    reference's directory joins sys.path).
 
     The reference runs on a one-rank group, in fp32 and in bf16, so its
-    gradients are the exact ones: over several ranks its SPBroadcast of the
-    adaLN input sums the final layer's (replicated) adaLN gradient over the
-    ranks, so t_embedder and the metadata embedders would get that term
-    sp_size times.  Over the whole group it runs the forward only, in bf16.
+    gradients are the exact ones: over several ranks it all-reduces the adaLN
+    input's gradient once per section (SPBroadcast), summing gradients that are
+    already sums, so t_embedder and the metadata embedders come out inflated.
+    Over the whole group it runs the forward only, in bf16.
     harp runs sequence-parallel over the whole group in bf16.  Returns the
     image predictions (the reference's in full, harp's for this rank's tokens)
     and the parameter gradients of a fixed weighted sum of the predictions."""
     import sys
 
+    from harp_b200.compat import install_reference_import_paths
+
+    install_reference_import_paths()
     sys.path.append(args["ref"])
     from src.models.z_image import hl_model as RH
     from src.models.z_image import standalone_transformer as RS

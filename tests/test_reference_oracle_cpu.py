@@ -178,17 +178,17 @@ def test_rope_embedder_tables():
     dims, lens = (32, 48, 48), (1024, 512, 512)
     ref = R.RopeEmbedderReference(256.0, dims, lens)
     ids = torch.stack([torch.randint(0, n, (300,)) for n in lens], -1).int()
-    import kp_rope_embedder as K
+    from harp_b200.models.zimage import RopeTableEmbedder
 
-    for cls in (RopeEmbedder, K.RopeEmbedderReference, K.RopeEmbedderSVE):
+    for cls in (RopeEmbedder, RopeTableEmbedder):
         torch.testing.assert_close(cls(256.0, dims, lens).complex(ids), ref(ids), rtol=0, atol=2e-6)
 
 
 def test_kp_rope_complex_form():
-    """kp_rope.kp_apply_rotary_emb (complex form) against the reference's
-    src/utils/rope.py apply_rotary_emb(use_real=False); the real form is
-    refused in both."""
-    import kp_rope
+    """kp_apply_rotary_emb (the reference's kp_rope.py; complex form) against
+    the reference's src/utils/rope.py apply_rotary_emb(use_real=False); the
+    real form is refused."""
+    from harp_b200.ops import modules as kp_rope
 
     R = _load("src/utils/rope.py")
     x = torch.randn(2, 3, 10, 16)
@@ -489,7 +489,7 @@ def test_broadcasting_autograd_ops():
     """async_rt/async_ops.py:55-122 (MyMul, MyAdd; the file's other ops call
     the reference's compiled library) against harp's, with broadcasting and a
     Python-number operand."""
-    from async_rt import async_ops as O
+    from harp_b200.runtime import async_compat as O
 
     R = _load("async_rt/async_ops.py")
     torch.manual_seed(0)

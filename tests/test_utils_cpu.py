@@ -349,6 +349,9 @@ def test_async_runtime_api_on_streams():
     reference's do; MyMul / MyAdd broadcast and sum gradients back to each
     input's shape; the kernel helpers write the linear and SiLU results into
     the caller's tensors (CPU restatements here, to bf16 rounding)."""
+    from harp_b200.compat import install_reference_import_paths
+
+    install_reference_import_paths()
     import async_rt
     from async_rt import async_ops as O
     from async_rt import runtime as R
@@ -414,33 +417,41 @@ def test_async_runtime_api_on_streams():
 
 
 def test_reference_import_paths():
-    """The reference's top-level import paths resolve to harp's implementations
+    """harp_b200.compat registers the reference's top-level import paths
     (managers.*, async_rt.*, unigemm_linear, kp_normalization,
-    kp_multi_tensor_adamw, kp_rope, kp_rope_embedder)."""
+    kp_multi_tensor_adamw, kp_rope, kp_rope_embedder) as harp's modules, and
+    every name the reference imports from them resolves."""
     import importlib
 
+    from harp_b200.compat import REFERENCE_MODULES, install_reference_import_paths
     from harp_b200.models import zimage as Z
     from harp_b200.ops import modules as M
 
+    install_reference_import_paths()
+    for name, target in REFERENCE_MODULES.items():
+        assert importlib.import_module(name) is importlib.import_module(target), name
     want = {
         "unigemm_linear": {"kpLinear": M.kpLinear, "replace_linear_with_kplinear": M.replace_linear_with_kplinear,
                            "CustomLinearFunction": M.LinearFunction},
         "kp_normalization": {"kpRMSNorm": M.kpRMSNorm, "CustomNormFunction": M.RMSNormFunction,
                              "replace_rmsNorm_with_kpRMSNorm": M.replace_rmsNorm_with_kpRMSNorm},
         "kp_multi_tensor_adamw": {"kp_multi_tensor_adamw": M.kp_multi_tensor_adamw},
-        "kp_rope_embedder": {"RopeEmbedderSVE": Z.RopeTableEmbedder,
+        "kp_rope": {"kp_apply_rotary_emb": M.kp_apply_rotary_emb},
+        "kp_rope_embedder": {"RopeEmbedderSVE": Z.RopeTableEmbedder, "RopeEmbedderReference": Z.RopeEmbedder,
                              "replace_ropeembedder_with_sverope": Z.replace_ropeembedder_with_sverope},
         "async_rt.async_ops": {"MySiLU": M.MySiLU, "MyTanh": M.MyTanh, "ApplyRotaryComplexFn": M.ApplyRotaryComplexFn},
-        "managers.shard_manager": {},
-        "managers.weight_manager": {},
-        "managers.grad_manager": {},
-        "managers.mem_manager": {},
-        "managers.ring_attn_manager": {},
     }
     for mod_name, names in want.items():
         mod = importlib.import_module(mod_name)
         for n, obj in names.items():
             assert getattr(mod, n) is obj, (mod_name, n)
-    import kp_rope
-
-    assert callable(kp_rope.kp_apply_rotary_emb)
+    # every `from X import a, b` of the reference's train.py and Z-Image SP model
+    from async_rt import is_asyncrt_enabled  # noqa: F401
+    from async_rt.async_ops import MySiLU  # noqa: F401
+    from async_rt.runtime import RUNTIME, AsyncModeEnd, AsyncModeStart, AsyncRunMode, AsyncSync  # noqa: F401
+    from managers.grad_manager import AsyncGradSyncManager  # noqa: F401
+    from managers.mem_manager import use_hbm_allocator  # noqa: F401
+    from managers.ring_attn_manager import CPUWaitEngine  # noqa: F401
+    from managers.shard_manager import SequenceAllGather, SequenceScatter, SPBroadcast  # noqa: F401
+    from managers.weight_manager import (AsyncParamAllGatherManager, build_balanced_param_groups,  # noqa: F401
+                                         build_chunk_param, set_opt_hook, setup_shared_model)
