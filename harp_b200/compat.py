@@ -14,8 +14,8 @@ unchanged afterwards:
     from managers.weight_manager import build_chunk_param   # harp_b200.managers.weight_manager
 
 A name that already resolves to a module of another origin (for example the
-reference's own package on sys.path, already imported) is left alone unless
-`replace=True`.  `python -m harp_b200.compat` prints the table.
+reference's own package on sys.path, already imported) is left alone, with
+its submodules, unless `replace=True`.  `python -m harp_b200.compat` prints the table.
 """
 from __future__ import annotations
 
@@ -44,11 +44,13 @@ REFERENCE_MODULES: Dict[str, str] = {
 
 def install_reference_import_paths(replace: bool = False) -> List[str]:
     """Register the reference's module names; returns the names registered."""
-    done = []
+    done, kept = [], set()
     for name, target in REFERENCE_MODULES.items():
         mod = importlib.import_module(target)
         cur = sys.modules.get(name)
-        if cur is not None and cur is not mod and not replace:
+        parent = name.rpartition(".")[0]
+        if not replace and (parent in kept or (cur is not None and cur is not mod)):
+            kept.add(name)  # another package of this name is in use: leave its subtree alone
             continue
         sys.modules[name] = mod
         parent, _, child = name.rpartition(".")
