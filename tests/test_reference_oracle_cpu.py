@@ -1,10 +1,11 @@
 """Oracle tests against the reference's own pure-PyTorch modules.
 
 The reference project's root is read from HARP_REFERENCE_DIR; every test here
-is skipped when it is unset.  Only files that import nothing but torch (and the
-standard library) are loaded, one at a time with importlib, so none of the
-reference's compiled extensions are needed.  Each test runs the reference's
-function and harp's on the same inputs.
+is skipped when it is unset.  Files are loaded one at a time with importlib
+and none of the reference's compiled extensions are needed: most import
+nothing but torch and the standard library; src/utils/inference.py gets
+stand-ins for the diffusers names it imports.  Each test runs the reference's
+code and harp's on the same inputs (train.py and data/ are read, not run).
 """
 import importlib.util
 import json
