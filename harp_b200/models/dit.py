@@ -29,7 +29,7 @@ used by the tests).
 from __future__ import annotations
 
 import math
-from dataclasses import asdict, dataclass, field
+from dataclasses import asdict, dataclass
 from typing import List, Optional, Sequence, Tuple
 
 import torch

@@ -17,9 +17,8 @@ from __future__ import annotations
 
 import argparse
 import json
-import math
 import os
-from typing import Callable, Dict, Optional
+from typing import Callable, Dict
 
 import torch
 

@@ -5,7 +5,6 @@ path; these serve the gloo (CPU) tests, the NCCL fallback and cold paths.
 """
 from __future__ import annotations
 
-from typing import Optional
 
 import torch
 import torch.distributed as dist

@@ -5,7 +5,6 @@ against closed-form values)."""
 import json
 import math
 import os
-import threading
 import time
 
 import numpy as np
