@@ -90,19 +90,32 @@ def _natural_key(s: str):
 
 
 def generate_rankfile(hosts: Sequence[str], ranks_per_node: int = 8, max_nodes: Optional[int] = None,
-                      cores_per_node: Optional[int] = None) -> List[str]:
-    """Lines "rank <r>=<host> gpu=<g> cpus=<a>-<b>": hosts in natural order,
-    `ranks_per_node` ranks per host, each owning GPU g = r % ranks_per_node and
-    an equal contiguous core block."""
+                      cores_per_node: Optional[int] = None, fmt: str = "gpu", sockets: int = 2) -> List[str]:
+    """One line per rank: hosts in natural order (node2 before node10), at most
+    `max_nodes` of them, `ranks_per_node` ranks per host, rank i of a host
+    owning the i-th equal contiguous block of its cores.
+
+    fmt="gpu": "rank <r>=<host> gpu=<i> cpus=<a>-<b>" (GPU i, node-wide core ids).
+    fmt="mpi": the OpenMPI rankfile line "rank <r>=<host> slot=<s>:<a>-<b>",
+    with socket s and core ids counted within the socket (the cores split
+    evenly over `sockets`), the format the reference's launcher writes for
+    mpirun (gen_rankfile/gen_rankfile.py:4-60)."""
     nodes = sorted(dict.fromkeys(h for h in hosts if h), key=_natural_key)
     if max_nodes is not None:
         nodes = nodes[:max_nodes]
     cores = cores_per_node or (os.cpu_count() or ranks_per_node)
     per = max(1, cores // ranks_per_node)
+    per_socket = max(1, cores // max(1, sockets))
     lines, r = [], 0
     for host in nodes:
         for i in range(ranks_per_node):
-            lines.append(f"rank {r}={host} gpu={i} cpus={i * per}-{(i + 1) * per - 1}")
+            a, b = i * per, (i + 1) * per - 1
+            if fmt == "mpi":
+                lines.append(f"rank {r}={host} slot={a // per_socket}:{a % per_socket}-{b % per_socket}")
+            elif fmt == "gpu":
+                lines.append(f"rank {r}={host} gpu={i} cpus={a}-{b}")
+            else:
+                raise ValueError(f"unknown rankfile format {fmt!r} (gpu | mpi)")
             r += 1
     return lines
 
@@ -122,10 +135,14 @@ def main(argv=None):
         ap.add_argument("--ranks-per-node", type=int, default=8)
         ap.add_argument("--max-nodes", type=int, default=None)
         ap.add_argument("--cores-per-node", type=int, default=None)
+        ap.add_argument("--format", choices=["gpu", "mpi"], default="gpu",
+                        help="gpu: GPU index and node-wide cores; mpi: OpenMPI rankfile slots (socket:cores)")
+        ap.add_argument("--sockets", type=int, default=2)
         a = ap.parse_args(argv[1:])
         with open(a.hostfile) as fh:
             hosts = [ln.split()[0] for ln in fh if ln.strip()]
-        print("\n".join(generate_rankfile(hosts, a.ranks_per_node, a.max_nodes, a.cores_per_node)))
+        print("\n".join(generate_rankfile(hosts, a.ranks_per_node, a.max_nodes, a.cores_per_node, a.format,
+                                           a.sockets)))
         return 0
     ap = argparse.ArgumentParser(prog="harp_b200.launch")
     ap.add_argument("--nproc-per-node", type=int, default=8)

@@ -613,3 +613,22 @@ def test_sampling_loop_matches_the_reference(monkeypatch, cfg):
     got = HI.batch_image_inference(model, None, scheduler(), None, **kw)[0]
     assert got.dtype == want.dtype == torch.bfloat16
     assert ((got.float() - want.float()).norm() / want.float().norm()).item() < 5e-3
+
+
+@pytest.mark.parametrize("max_nodes", [None, 2])
+def test_mpi_rankfile_matches_the_reference(tmp_path, capsys, max_nodes):
+    """gen_rankfile/gen_rankfile.py (the reference's OpenMPI rankfile for its
+    16-rank, 608-core, two-socket nodes) against harp_b200.launch's
+    generate_rankfile(fmt="mpi") with those parameters: the same lines, nodes
+    in natural order, truncated to max_nodes."""
+    from harp_b200.launch import generate_rankfile
+
+    R = _load("gen_rankfile/gen_rankfile.py")
+    hosts = ["node10", "node2", "node1", "gpu-a3"]
+    hostfile = tmp_path / "nodes.txt"
+    hostfile.write_text("\n".join(f"{h} slots=16" for h in hosts) + "\n")
+    R.generate_cpuset_rankfile(str(hostfile), max_nodes=max_nodes)
+    want = capsys.readouterr().out.split("\n")
+    want = [line for line in want if line]
+    got = generate_rankfile(hosts, ranks_per_node=16, max_nodes=max_nodes, cores_per_node=608, fmt="mpi", sockets=2)
+    assert got == want
