@@ -454,3 +454,37 @@ def test_reference_import_paths():
     from managers.shard_manager import SequenceAllGather, SequenceScatter, SPBroadcast  # noqa: F401
     from managers.weight_manager import (AsyncParamAllGatherManager, build_balanced_param_groups,  # noqa: F401
                                          build_chunk_param, set_opt_hook, setup_shared_model)
+
+
+def test_train_cli_under_mpirun_style_environment(tmp_path):
+    """train.py started the way mpirun starts it (OMPI_COMM_WORLD_RANK / _SIZE /
+    _LOCAL_RANK in the environment, no torchrun variables): two processes
+    find each other, train two sequence-parallel steps over gloo and write one
+    metrics file."""
+    import json
+    import socket
+    import subprocess
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    work = tmp_path / "w"
+    cmd = [sys.executable, os.path.join(root, "train.py"), "--model", "tiny", "--synthetic", "--latent_size", "16",
+           "--text_len", "16", "--max_train_steps", "2", "--train_batch_size", "2", "--sp_size", "2",
+           "--work_dir", str(work), "--checkpointing_steps", "100", "--lr_warmup_steps", "1"]
+    base = {k: v for k, v in os.environ.items() if k not in ("RANK", "WORLD_SIZE", "LOCAL_RANK", "MASTER_ADDR",
+                                                             "MASTER_PORT")}
+    procs = []
+    for r in range(2):
+        env = dict(base, CUDA_VISIBLE_DEVICES="", OMPI_COMM_WORLD_RANK=str(r), OMPI_COMM_WORLD_SIZE="2",
+                   OMPI_COMM_WORLD_LOCAL_RANK=str(r), MASTER_PORT=str(port))
+        procs.append(subprocess.Popen(cmd, env=env, cwd=str(tmp_path), stdout=subprocess.PIPE,
+                                      stderr=subprocess.PIPE, text=True))
+    outs = [p.communicate(timeout=600) for p in procs]
+    for p, (_, err) in zip(procs, outs):
+        assert p.returncode == 0, err[-3000:]
+    (run,) = os.listdir(work)
+    rows = [json.loads(line) for line in open(work / run / "metrics.jsonl") if line.strip()]
+    assert [row["global_step"] for row in rows if "step_loss" in row] == [1, 2]
