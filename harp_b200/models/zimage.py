@@ -450,7 +450,8 @@ class ZImageTransformer2DModel(nn.Module, ConfigMixin):
         assert dim // n_heads == sum(axes_dims)
         self.rope_embedder = RopeEmbedder(rope_theta, axes_dims, axes_lens)
 
-    # -- patchify (standalone_transformer.py:535-640), equal-size samples --
+    # -- token layout helpers (standalone_transformer.py:533-644): patchify without padding (the SP
+    #    wrapper pads its runs itself), unpatchify of one sample, position ids --
     def patchify(self, images: List[torch.Tensor], patch_size: int, f_patch_size: int):
         out, sizes = [], []
         for img in images:
@@ -476,7 +477,7 @@ class ZImageTransformer2DModel(nn.Module, ConfigMixin):
 
     def forward(self, x: List[torch.Tensor], t, cap_feats: List[torch.Tensor], patch_size=2, f_patch_size=1,
                 return_dict=True, sp: Optional[SPContext] = None):
-        """Single-rank forward (standalone_transformer.py:658-755) on samples of
+        """Single-rank forward (standalone_transformer.py:557-755) on samples of
         any image size and caption length.
 
         As in the reference, each sample's image and caption token runs are
