@@ -488,3 +488,24 @@ def test_train_cli_under_mpirun_style_environment(tmp_path):
     (run,) = os.listdir(work)
     rows = [json.loads(line) for line in open(work / run / "metrics.jsonl") if line.strip()]
     assert [row["global_step"] for row in rows if "step_loss" in row] == [1, 2]
+
+
+def test_reference_import_paths_leave_a_foreign_package_alone(monkeypatch):
+    """A package already imported under a reference name (for example the
+    reference's own `managers`) keeps that name and its submodules unless
+    replace=True."""
+    import sys
+    import types
+
+    from harp_b200.compat import REFERENCE_MODULES, install_reference_import_paths
+    from harp_b200.managers import shard_manager
+
+    for name in REFERENCE_MODULES:
+        monkeypatch.delitem(sys.modules, name, raising=False)
+    foreign = types.ModuleType("managers")
+    monkeypatch.setitem(sys.modules, "managers", foreign)
+    done = install_reference_import_paths()
+    assert sys.modules["managers"] is foreign and "managers.shard_manager" not in sys.modules
+    assert not any(n.startswith("managers") for n in done) and "async_rt" in done
+    done = install_reference_import_paths(replace=True)
+    assert sys.modules["managers.shard_manager"] is shard_manager and "managers" in done
