@@ -65,10 +65,8 @@ def velocity(model, latents: torch.Tensor, prompts: List[torch.Tensor], sigma: t
     sp = SPContext.single()
     if _is_zimage(model):
         imgs = list(latents.unsqueeze(2).unbind(0))
-        tokens = model(x=imgs, t=1.0 - sigma, text_embedding=list(prompts), return_dict=False,
-                       metadata=metadata, cond_list=cond, sp=sp)[0]
-        zt = model.z_transformer
-        out = [zt.unpatchify(tokens[b], tuple(imgs[b].shape[1:]), 2, 1) for b in range(len(imgs))]
+        out = model(x=imgs, t=1.0 - sigma, text_embedding=list(prompts), return_dict=False,
+                    metadata=metadata, cond_list=cond, sp=sp)[0]
         return -torch.stack(out, 0).squeeze(2)
     text = torch.stack(list(prompts), 0) if isinstance(prompts, (list, tuple)) else prompts
     return model(latents, text, sigma.float(), sp)

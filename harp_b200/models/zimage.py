@@ -622,10 +622,15 @@ class Z_Transformer(nn.Module, Z_HLMixin, Z_LoraBranches):
         t = cond.view(C, H // patch_size, patch_size, W // patch_size, patch_size).permute(1, 3, 2, 4, 0)
         return t.reshape((H // patch_size) * (W // patch_size), patch_size * patch_size * C)
 
+    @property
+    def device(self) -> torch.device:
+        return next(self.parameters()).device
+
     def forward_local(self, x: List[torch.Tensor], t, text_embedding: List[torch.Tensor], patch_size=2,
                       f_patch_size=1, metadata=None, cond_list=None, sp: Optional[SPContext] = None):
         """Returns (pred [B, n_local_img, p*p*C], img_lo, img_hi): this rank's
-        predictions for the real image tokens img_lo..img_hi-1.
+        predictions for the real image tokens img_lo..img_hi-1 (the training
+        path: no gather of the predictions).
 
         As in the reference (hl_base.py:41-203, hl_model.py:114-330) the
         caption, image and condition-image token runs are each padded to a
@@ -694,12 +699,32 @@ class Z_Transformer(nn.Module, Z_HLMixin, Z_LoraBranches):
             uni = layer(uni, None, f_uni, adaln, sp)
         out = zt.all_final_layer[f"{patch_size}-{f_patch_size}"](uni, adaln)
         img_lo, img_hi = min(lo_u, N), min(hi_u, N)
+        self._chunk_len = hi_u - lo_u  # this rank's share of the unified sequence (read by forward)
         return out[:, : max(0, img_hi - img_lo)], img_lo, img_hi
 
     def forward(self, x, t, text_embedding, patch_size=2, f_patch_size=1, return_dict=True, metadata=None,
                 cond_list=None, sp: Optional[SPContext] = None):
+        """The reference's contract (hl_model.py:114-337): every rank gets the
+        full predictions, one [C, F, H, W] per sample ({"sample": list}, or a
+        1-tuple when return_dict is False).  Under sequence parallelism the
+        ranks' image-token predictions are all-gathered; as in the reference,
+        the gather's backward keeps this rank's part of the gradient, so a loss
+        computed in full on every rank yields per-rank partial parameter
+        gradients whose sum over the ranks is the gradient (harp's trainer
+        sums them).  forward_local is the training path without the gather."""
+        sp = sp or SPContext()
         pred, lo, hi = self.forward_local(x, t, text_embedding, patch_size, f_patch_size, metadata, cond_list, sp)
-        return (pred, lo, hi) if not return_dict else {"sample": pred, "range": (lo, hi)}
+        C, F_, H, W = x[0].shape
+        n_img = (F_ // f_patch_size) * (H // patch_size) * (W // patch_size)
+        if sp.size > 1:
+            from ..managers.shard_manager import SequenceAllGather
+
+            c = self._chunk_len  # image tokens lead the unified sequence, so a rank's lie at its chunk's start
+            pad = pred.new_zeros(pred.shape[0], c - pred.shape[1], pred.shape[2])
+            pred = SequenceAllGather.apply(torch.cat([pred, pad], 1).contiguous(), sp.group)[:, :n_img]
+        zt = self.z_transformer
+        res = [zt.unpatchify(pred[b], tuple(x[b].shape[1:]), patch_size, f_patch_size) for b in range(len(x))]
+        return {"sample": res} if return_dict else (res,)
 
 
 def _pad_run(tok: torch.Tensor, ids: torch.Tensor):

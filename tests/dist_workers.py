@@ -309,6 +309,27 @@ def zimage_sp(rank, world, out, args):
     return {"loss": float(loss), "grads": grads}
 
 
+def zimage_forward_full(rank, world, out, args):
+    """The SP wrapper's forward (the reference's output contract: the full
+    predictions on every rank) over the gloo ranks, with a loss computed in
+    full on every rank as the reference's trainer does: the predictions and
+    this rank's parameter gradients."""
+    from harp_b200.models import zimage as Z
+    from harp_b200.parallel.sequence import SPContext
+
+    model = _zimage_model()
+    b = _zimage_batch(args.get("padded", False))
+    sp = SPContext.from_group(dist.group.WORLD, backend="torch") if world > 1 else SPContext()
+    x = list(b["lat"].unsqueeze(2).unbind(0))
+    pred = model(x, b["sig"], list(b["text"].unbind(0)), return_dict=False, metadata=b["meta"],
+                 cond_list=b["cond"], sp=sp)[0]
+    loss = sum((p.float() * (i + 1)).pow(2).mean() for i, p in enumerate(pred))
+    loss.backward()
+    grads = torch.cat([(p.grad if p.grad is not None else torch.zeros_like(p)).float().reshape(-1)
+                       for p in model.parameters()])
+    return {"pred": [p.detach().float() for p in pred], "grads": grads}
+
+
 def _mmdit_setup(name):
     from harp_b200.models import mmdit as M
 

@@ -426,6 +426,10 @@ def test_zimage_sp_wrapper_matches_base_model(hw, L):
         want = ref_base(x, t, caps)["sample"]
         pred, lo, hi = model.forward_local(x, t, caps, sp=SPContext())
     assert (lo, hi) == (0, (hw // 2) ** 2)
+    with torch.no_grad():  # the reference's output contract: one [C, F, H, W] per sample
+        full = model(x, t, caps, return_dict=False)[0]
+    for u, v in zip(full, want):
+        torch.testing.assert_close(u, v, rtol=0, atol=0)
     want_tok = torch.stack(ref_base.patchify([w.float() for w in want], 2, 1)[0])
     torch.testing.assert_close(pred.float(), want_tok, rtol=0, atol=0)
 

@@ -574,11 +574,12 @@ def test_sampling_loop_matches_the_reference(monkeypatch, cfg):
     """src/utils/inference.py batch_image_inference (the reference's sampling
     loop: shifted flow-match grid, classifier-free guidance with truncation
     and renormalisation, Euler steps) against harp_b200.inference's, with the
-    same model (harp's Z-Image, called through the reference loop's
-    convention) and harp's scheduler in both: the same final latents."""
+    same model (harp's SP Z-Image, which the reference loop calls with its own
+    convention: transformer(x=..., t=..., text_embedding=..., return_dict=False)[0]
+    gives one [C, 1, H, W] per sample) and harp's scheduler in both: the same
+    final latents."""
     from harp_b200 import inference as HI
     from harp_b200.models import zimage as Z
-    from harp_b200.parallel.sequence import SPContext
     from harp_b200.utils.diffusion import FlowMatchEulerDiscreteScheduler
 
     R = _load_reference_inference(monkeypatch)
@@ -590,15 +591,6 @@ def test_sampling_loop_matches_the_reference(monkeypatch, cfg):
             p.normal_(0, 0.05)
     model = model.bfloat16()
 
-    class ReferenceConvention:
-        """transformer(x=[C, 1, H, W] list, t, text_embedding, return_dict=False)[0] -> list of [C, 1, H, W]."""
-        device = torch.device("cpu")
-        in_channels = 16
-
-        def __call__(self, x, t, text_embedding, return_dict=False):
-            pred, _, _ = model.forward_local(x, t, text_embedding, sp=SPContext())
-            return ([model.z_transformer.unpatchify(pred[b], tuple(x[b].shape[1:]), 2, 1) for b in range(len(x))],)
-
     g = torch.Generator().manual_seed(1)
     lat = torch.randn(2, 16, 16, 16, generator=g).bfloat16()
     pos = [torch.randn(32, pre["cap_feat_dim"], generator=g).bfloat16() for _ in range(2)]
@@ -609,7 +601,7 @@ def test_sampling_loop_matches_the_reference(monkeypatch, cfg):
     def scheduler():
         return FlowMatchEulerDiscreteScheduler(shift=3.0, use_dynamic_shifting=True)
 
-    want = R.batch_image_inference(ReferenceConvention(), None, scheduler(), None, **kw)[0]
+    want = R.batch_image_inference(model, None, scheduler(), None, **kw)[0]
     got = HI.batch_image_inference(model, None, scheduler(), None, **kw)[0]
     assert got.dtype == want.dtype == torch.bfloat16
     assert ((got.float() - want.float()).norm() / want.float().norm()).item() < 5e-3
