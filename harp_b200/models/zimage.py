@@ -568,8 +568,9 @@ class Z_JointBlock(Z_SingleBlock):
 class Z_Transformer(nn.Module, Z_HLMixin, Z_LoraBranches):
     """Sequence-parallel Z-Image with HARP's condition-image branch and metadata
     embedders (hl_model.py:37-109).  forward() takes the reference's arguments
-    and returns the prediction for the image tokens this rank holds, plus the
-    range of image positions they cover (use loss_local for training)."""
+    and returns its output (the full per-sample predictions on every rank);
+    forward_local() returns this rank's image-token predictions and their
+    range, the training path (zimage_loss_local)."""
 
     def __init__(self, z_transformer: ZImageTransformer2DModel, num_metadata: int = 0, in_channels=None,
                  use_cond: bool = False, sp_group_model=None, sp_size=None, cond_channels: int = 192,
