@@ -418,7 +418,50 @@ class Z_LoraBranches:
 
 
 
-class ZImageTransformer2DModel(nn.Module, ConfigMixin):
+class ModelMixin:
+    """The reference's model conveniences (standalone_transformer.py:91-121):
+    device / dtype properties, no-op xformers switches, and gradient
+    checkpointing, which here is real: with it enabled every transformer
+    block's activations are recomputed in the backward
+    (torch.utils.checkpoint, non-reentrant) instead of being kept.  Under
+    sequence parallelism the recomputation repeats the block's exchanges in
+    the backward, in the same order on every rank."""
+
+    gradient_checkpointing = False
+
+    @property
+    def device(self) -> torch.device:
+        for t in list(self.parameters()) + list(self.buffers()):
+            return t.device
+        return torch.device("cpu")
+
+    @property
+    def dtype(self) -> torch.dtype:
+        for t in list(self.parameters()) + list(self.buffers()):
+            return t.dtype
+        return torch.float32
+
+    def enable_xformers_memory_efficient_attention(self, *args, **kwargs):
+        return self
+
+    def disable_xformers_memory_efficient_attention(self):
+        return self
+
+    def gradient_checkpointing_enable(self):
+        self.gradient_checkpointing = True
+
+    def gradient_checkpointing_disable(self):
+        self.gradient_checkpointing = False
+
+    def _run_block(self, block, *args):
+        if self.gradient_checkpointing and torch.is_grad_enabled():
+            import torch.utils.checkpoint as ckpt
+
+            return ckpt.checkpoint(block, *args, use_reentrant=False)
+        return block(*args)
+
+
+class ZImageTransformer2DModel(nn.Module, ModelMixin, ConfigMixin):
     def __init__(self, all_patch_size=(2,), all_f_patch_size=(1,), in_channels=16, dim=3840, n_layers=30,
                  n_refiner_layers=2, n_heads=30, n_kv_heads=30, norm_eps=1e-5, qk_norm=True, cap_feat_dim=2560,
                  rope_theta=256.0, t_scale=1000.0, axes_dims=(32, 48, 48), axes_lens=(1024, 512, 512)):
@@ -512,14 +555,14 @@ class ZImageTransformer2DModel(nn.Module, ConfigMixin):
             f_cap = self.rope_embedder(cap_ids[idx[0]])
             rep_img = f_img.repeat(n, 1, 1)
             for layer in self.noise_refiner:
-                xs = layer(xs, rep_img, adaln, sp)
+                xs = self._run_block(layer, xs, rep_img, adaln, sp)
             rep_cap = f_cap.repeat(n, 1, 1)
             for layer in self.context_refiner:
-                cs = layer(cs, rep_cap)
+                cs = self._run_block(layer, cs, rep_cap)
             uni = torch.cat([xs, cs], 1)
             f_uni = torch.cat([f_img, f_cap], 0).repeat(n, 1, 1)
             for layer in self.layers:
-                uni = layer(uni, f_uni, adaln, sp)
+                uni = self._run_block(layer, uni, f_uni, adaln, sp)
             out = self.all_final_layer[key](uni, adaln)
             for j, i in enumerate(idx):
                 res[i] = self.unpatchify(out[j], sizes[i], patch_size, f_patch_size)
@@ -565,7 +608,7 @@ class Z_JointBlock(Z_SingleBlock):
                             compat="joint" if self.compat else False)
 
 
-class Z_Transformer(nn.Module, Z_HLMixin, Z_LoraBranches):
+class Z_Transformer(nn.Module, ModelMixin, Z_HLMixin, Z_LoraBranches):
     """Sequence-parallel Z-Image with HARP's condition-image branch and metadata
     embedders (hl_model.py:37-109).  forward() takes the reference's arguments
     and returns its output (the full per-sample predictions on every rank);
@@ -623,10 +666,6 @@ class Z_Transformer(nn.Module, Z_HLMixin, Z_LoraBranches):
         t = cond.view(C, H // patch_size, patch_size, W // patch_size, patch_size).permute(1, 3, 2, 4, 0)
         return t.reshape((H // patch_size) * (W // patch_size), patch_size * patch_size * C)
 
-    @property
-    def device(self) -> torch.device:
-        return next(self.parameters()).device
-
     def forward_local(self, x: List[torch.Tensor], t, text_embedding: List[torch.Tensor], patch_size=2,
                       f_patch_size=1, metadata=None, cond_list=None, sp: Optional[SPContext] = None):
         """Returns (pred [B, n_local_img, p*p*C], img_lo, img_hi): this rank's
@@ -664,13 +703,13 @@ class Z_Transformer(nn.Module, Z_HLMixin, Z_LoraBranches):
         xs = _fill_pad(xs, lo_i, hi_i, N, N_pad, zt.x_pad_token)
         f_img = zt.rope_embedder(img_ids[lo_i:hi_i]).repeat(B, 1, 1)
         for layer in self.noise_refiner:
-            xs = layer(xs, None, f_img, adaln, sp)
+            xs = self._run_block(layer, xs, None, f_img, adaln, sp)
         caps = zt.cap_embedder(_local(cap, sp).to(xs.dtype))
         lo_c, hi_c = _range(L_pad, sp)
         f_cap = zt.rope_embedder(cap_ids[lo_c:hi_c]).repeat(B, 1, 1)
         caps = _fill_pad(caps, lo_c, hi_c, L, L_pad, zt.cap_pad_token)
         for layer in self.context_refiner:
-            caps = layer(caps, None, f_cap, None, sp)
+            caps = self._run_block(layer, caps, None, f_cap, None, sp)
         streams = [(xs, N_pad), (caps, L_pad)]
         ids = [img_ids, cap_ids]
         if self.use_cond and cond_list is not None:
@@ -686,7 +725,7 @@ class Z_Transformer(nn.Module, Z_HLMixin, Z_LoraBranches):
                 cs = _fill_pad(cs, lo_k, hi_k, Nc, Nc_pad, self.cond_pad_token)
                 f_c = zt.rope_embedder(cids[lo_k:hi_k]).repeat(B, 1, 1)
                 for layer in getattr(self, f"cond_refiner_{j + 1}"):
-                    cs = layer(cs, None, f_c, adaln, sp)
+                    cs = self._run_block(layer, cs, None, f_c, adaln, sp)
                 streams.append((cs, Nc_pad))
                 ids.append(cids)
         # unified sequence [img ; text ; cond...]: gather each stream, concatenate, take this rank's chunk
@@ -697,7 +736,7 @@ class Z_Transformer(nn.Module, Z_HLMixin, Z_LoraBranches):
         lo_u, hi_u = _range(all_ids.shape[0], sp)
         f_uni = zt.rope_embedder(all_ids[lo_u:hi_u]).repeat(B, 1, 1)
         for layer in self.layers:
-            uni = layer(uni, None, f_uni, adaln, sp)
+            uni = self._run_block(layer, uni, None, f_uni, adaln, sp)
         out = zt.all_final_layer[f"{patch_size}-{f_patch_size}"](uni, adaln)
         img_lo, img_hi = min(lo_u, N), min(hi_u, N)
         self._chunk_len = hi_u - lo_u  # this rank's share of the unified sequence (read by forward)

@@ -32,11 +32,11 @@ import torch
 import torch.nn as nn
 
 from ..parallel.sequence import SPContext
-from .zimage import (ADALN_EMBED_DIM, Linear, TimestepEmbedder, Z_JointBlock, Z_LoraBranches, Z_Mixin,
-                     Z_SingleBlock, ZImageTransformer2DModel)
+from .zimage import (ADALN_EMBED_DIM, Linear, ModelMixin, TimestepEmbedder, Z_JointBlock, Z_LoraBranches,
+                     Z_Mixin, Z_SingleBlock, ZImageTransformer2DModel)
 
 
-class Z_Transformer(nn.Module, Z_Mixin, Z_LoraBranches):
+class Z_Transformer(nn.Module, ModelMixin, Z_Mixin, Z_LoraBranches):
     """Legacy (non-SP) Z-Image wrapper: noise/context/condition refiners and the
     joint layers over variable-size samples (model.py:20-349).
 
@@ -112,13 +112,13 @@ class Z_Transformer(nn.Module, Z_Mixin, Z_LoraBranches):
             xs = torch.where(m, zt.x_pad_token.to(dt), emb_x)
             f_x = zt.rope_embedder(img_ids[idx[0]])
             for layer in self.noise_refiner:
-                xs = layer(xs, None, f_x.repeat(n, 1, 1), adaln, sp)
+                xs = self._run_block(layer, xs, None, f_x.repeat(n, 1, 1), adaln, sp)
             caps_b = zt.cap_embedder(torch.stack([caps[i] for i in idx]).to(dt))
             m = torch.stack([cap_masks[i] for i in idx])[..., None]
             caps_b = torch.where(m, zt.cap_pad_token.to(dt), caps_b)
             f_c = zt.rope_embedder(cap_ids[idx[0]])
             for layer in self.context_refiner:
-                caps_b = layer(caps_b, None, f_c.repeat(n, 1, 1), None, sp)
+                caps_b = self._run_block(layer, caps_b, None, f_c.repeat(n, 1, 1), None, sp)
             seqs, fr = [xs, caps_b], [f_x, f_c]
             if use_cond:
                 cs = self.cond_embedder(torch.stack([cond_out[0][i] for i in idx]).to(dt))
@@ -126,13 +126,13 @@ class Z_Transformer(nn.Module, Z_Mixin, Z_LoraBranches):
                 cs = torch.where(m, self.cond_pad_token.to(dt), cs)
                 f_k = zt.rope_embedder(cond_out[2][idx[0]])
                 for layer in self.cond_refiner:
-                    cs = layer(cs, None, f_k.repeat(n, 1, 1), adaln, sp)
+                    cs = self._run_block(layer, cs, None, f_k.repeat(n, 1, 1), adaln, sp)
                 seqs.append(cs)
                 fr.append(f_k)
             uni = torch.cat(seqs, 1)
             f_u = torch.cat(fr, 0).repeat(n, 1, 1)
             for layer in self.layers:
-                uni = layer(uni, None, f_u, adaln, sp)
+                uni = self._run_block(layer, uni, None, f_u, adaln, sp)
             pred = zt.all_final_layer[key](uni, adaln)
             for j, i in enumerate(idx):
                 out[i] = pred[j, : imgs[i].shape[0]]

@@ -299,6 +299,8 @@ def zimage_sp(rank, world, out, args):
     from harp_b200.parallel.sequence import SPContext
 
     model = _zimage_model()
+    if args.get("ckpt"):
+        model.gradient_checkpointing_enable()
     b = _zimage_batch(args.get("padded", False))
     sp = SPContext.from_group(dist.group.WORLD, backend="torch", mode=args.get("mode", "ring"))
     loss = Z.zimage_loss_local(model, b["lat"], b["noise"], b["text"], b["sig"], sp, metadata=b["meta"],

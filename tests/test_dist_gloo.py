@@ -382,3 +382,17 @@ def test_zimage_forward_gathers_full_predictions_two_ranks(tmp_path, padded):
     g = two[0]["grads"] + two[1]["grads"]
     ref = one[0]["grads"]
     assert ((g - ref).norm() / ref.norm()).item() < 2e-2
+
+
+@pytest.mark.parametrize("mode", ["ring", "ulysses"])
+def test_zimage_gradient_checkpointing_two_ranks(tmp_path, mode):
+    """With gradient checkpointing the blocks (and their sequence-parallel
+    exchanges) run again in the backward on both gloo ranks: the same loss
+    shares and gradients as without it."""
+    (tmp_path / "a").mkdir()
+    (tmp_path / "b").mkdir()
+    plain, _ = _run("zimage_sp", 2, tmp_path / "a", {"mode": mode, "padded": True})
+    ckpt, _ = _run("zimage_sp", 2, tmp_path / "b", {"mode": mode, "padded": True, "ckpt": True})
+    for r in (0, 1):
+        assert ckpt[r]["loss"] == plain[r]["loss"]
+        torch.testing.assert_close(ckpt[r]["grads"], plain[r]["grads"], rtol=0, atol=0)

@@ -574,3 +574,43 @@ def test_rope_table_embedder_swap_keeps_predictions():
         assert isinstance(model.rope_embedder, Z.RopeTableEmbedder)
         b = model(x, t, caps)["sample"][0]
     torch.testing.assert_close(a, b, rtol=0, atol=0)
+
+
+def test_zimage_gradient_checkpointing_gives_the_same_gradients():
+    """gradient_checkpointing_enable() (the reference's ModelMixin switch, a
+    no-op there) recomputes each block in the backward here: the same loss and
+    bitwise the same gradients for the base model and the SP wrapper, with
+    padded runs and a condition branch."""
+    pre = Z.PRESETS["zimage-tiny"]
+
+    def run(ckpt, wrapper):
+        torch.manual_seed(0)
+        base = Z.ZImageTransformer2DModel(**pre)
+        model = Z.Z_Transformer(base, num_metadata=2, use_cond=True) if wrapper else base
+        with torch.no_grad():
+            for p in model.parameters():
+                p.normal_(0, 0.05)
+        model = model.bfloat16()
+        if ckpt:
+            model.gradient_checkpointing_enable()
+        g = torch.Generator().manual_seed(1)
+        x = [torch.randn(16, 1, 18, 18, generator=g).bfloat16() for _ in range(2)]
+        caps = [torch.randn(20, pre["cap_feat_dim"], generator=g).bfloat16() for _ in range(2)]
+        t = torch.rand(2, generator=g)
+        if wrapper:
+            meta = torch.rand(2, 2, generator=g).bfloat16()
+            cond = [torch.randn(2, 192, 18, 18, generator=g).bfloat16()]
+            pred, _, _ = model.forward_local(x, t, caps, metadata=meta, cond_list=cond, sp=SPContext())
+            loss = pred.float().pow(2).mean()
+        else:
+            loss = sum(o.float().pow(2).mean() for o in model(x, t, caps)["sample"])
+        loss.backward()
+        return loss.detach(), [p.grad.clone() if p.grad is not None else None for p in model.parameters()]
+
+    for wrapper in (False, True):
+        (l0, g0), (l1, g1) = run(False, wrapper), run(True, wrapper)
+        torch.testing.assert_close(l1, l0, rtol=0, atol=0)
+        for a, b in zip(g0, g1):
+            assert (a is None) == (b is None)
+            if a is not None:
+                torch.testing.assert_close(b, a, rtol=0, atol=0)

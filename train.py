@@ -83,6 +83,8 @@ def parse_args(argv=None):
                    help="capture the whole training step in one CUDA graph after two eager steps "
                         "(1 GPU, or N GPUs on the NVLink communicator)")
     p.add_argument("--harp_block_compat", action="store_true", help="Z-Image: reproduce HARP's block residual")
+    p.add_argument("--gradient_checkpointing", action="store_true",
+                   help="Z-Image: recompute each block's activations in the backward instead of keeping them")
     # accepted for command-line compatibility, unused (as in the reference)
     for flag, typ, default in (("--use_8bit_adam", bool, False), ("--rank", int, 8), ("--resolution", int, 512),
                                ("--cache_dir", str, "cache"), ("--comp_ckpt", str, None)):
@@ -122,6 +124,8 @@ def build_model(args, device, sp_group, dtype=torch.bfloat16):
                                     harp_block_compat=args.harp_block_compat)
         model = model.to(dtype)
         _init_fixed(model, args.seed)
+        if getattr(args, "gradient_checkpointing", False):
+            model.gradient_checkpointing_enable()
         shapes = dict(C=base.in_channels, cap_dim=cfg.get("cap_feat_dim", 2560), kind="zimage")
 
         def loss_fn(m, latent, noise, text, sigmas, sp, weighting=None, metadata=None, cond=None):
