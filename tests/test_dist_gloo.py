@@ -222,12 +222,14 @@ def test_sharded_weight_layout_two_ranks(tmp_path):
         assert res[r]["buckets"] == res[r]["n_groups"] + 1 and res[r]["rest"] == res[r]["n_groups"], res[r]
 
 
-@pytest.mark.parametrize("padded", [False, True])
-def test_zimage_two_ranks_match_one(padded):
-    """The Z-Image SP wrapper over two gloo ranks: the ranks' loss shares and
-    gradients sum to the one-process loss and gradients (the reference never
-    checks its SP model against a single-rank run); also with image, caption
-    and condition runs that need pad tokens."""
+@pytest.mark.parametrize("padded,world,mode", [(False, 2, "ring"), (True, 2, "ring"), (True, 4, "ring"),
+                                               (True, 4, "ulysses")])
+def test_zimage_two_ranks_match_one(padded, world, mode):
+    """The Z-Image SP wrapper over two or four gloo ranks: the ranks' loss
+    shares and gradients sum to the one-process loss and gradients (the
+    reference never checks its SP model against a single-rank run); also with
+    image, caption and condition runs that need pad tokens, whose padding then
+    lands in the last ranks' chunks."""
     import tempfile
 
     from harp_b200.models import zimage as Z
@@ -241,10 +243,10 @@ def test_zimage_two_ranks_match_one(padded):
     ref_g = torch.cat([(p.grad if p.grad is not None else torch.zeros_like(p)).float().reshape(-1)
                        for p in model.parameters()])
     with tempfile.TemporaryDirectory() as d:
-        res, _ = _run("zimage_sp", 2, d, {"padded": padded})
-    tot = res[0]["loss"] + res[1]["loss"]
+        res, _ = _run("zimage_sp", world, d, {"padded": padded, "mode": mode})
+    tot = sum(res[r]["loss"] for r in range(world))
     assert tot == pytest.approx(float(loss), rel=2e-2), (tot, float(loss))
-    g = res[0]["grads"] + res[1]["grads"]
+    g = sum(res[r]["grads"] for r in range(world))
     rel = ((g - ref_g).norm() / ref_g.norm()).item()
     assert rel < 2e-2, rel
 
