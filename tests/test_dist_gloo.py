@@ -368,20 +368,21 @@ def test_zimage_sp_matches_the_reference_sp_model(tmp_path, world, hw, cap):
         assert rel(ours, g32) <= 2 * rel(g16, g32) + 1e-2, (n, rel(ours, g32), rel(g16, g32))
 
 
-@pytest.mark.parametrize("padded", [False, True])
-def test_zimage_forward_gathers_full_predictions_two_ranks(tmp_path, padded):
+@pytest.mark.parametrize("padded,world", [(False, 2), (True, 2), (True, 4)])
+def test_zimage_forward_gathers_full_predictions_two_ranks(tmp_path, padded, world):
     """Z_Transformer.forward keeps the reference's contract under sequence
-    parallelism: on two gloo ranks every rank gets the one-process predictions,
+    parallelism: on two or four gloo ranks every rank gets the one-process
+    predictions,
     and with the loss computed in full on every rank the ranks' parameter
     gradients sum to the one-process gradients."""
     (tmp_path / "one").mkdir()
     (tmp_path / "two").mkdir()
     one, _ = _run("zimage_forward_full", 1, tmp_path / "one", {"padded": padded})
-    two, _ = _run("zimage_forward_full", 2, tmp_path / "two", {"padded": padded})
-    for r in (0, 1):
+    two, _ = _run("zimage_forward_full", world, tmp_path / "two", {"padded": padded})
+    for r in range(world):
         for u, v in zip(two[r]["pred"], one[0]["pred"]):
             assert ((u - v).norm() / v.norm()).item() < 2e-2
-    g = two[0]["grads"] + two[1]["grads"]
+    g = sum(two[r]["grads"] for r in range(world))
     ref = one[0]["grads"]
     assert ((g - ref).norm() / ref.norm()).item() < 2e-2
 
