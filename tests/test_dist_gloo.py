@@ -1,7 +1,9 @@
-"""Multi-process tests on CPU (gloo, 2 ranks): sequence-parallel attention,
-trainer parity (SP=2 and DP=2 against one process), the managers API, sharded
-checkpoints, and detection of a rank that leaves (reference test strategy:
-multi-rank paths checked against a single-rank run of the same math)."""
+"""Multi-process tests on CPU (gloo, 2 and 4 ranks): sequence-parallel
+attention, trainer parity (SP and DP against one process), the managers API,
+the model families under sequence parallelism, sharded checkpoints, detection
+of a rank that leaves, and (with HARP_REFERENCE_DIR) the reference's own
+managers and SP Z-Image beside harp's.  Multi-rank paths are checked against
+a single-rank run of the same math."""
 import multiprocessing as mp
 import os
 import socket
